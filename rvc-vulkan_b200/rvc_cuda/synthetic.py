@@ -1,0 +1,237 @@
+"""Seeded synthetic checkpoints and inputs for the RVC inference hot path.
+
+No checkpoints can be downloaded on the machines this library is measured on,
+so every test and benchmark builds random-init weights of the real
+architectures with the reference's own state-dict key names, and synthetic
+inputs with the shapes and value distributions of the measured configs.
+
+Everything is drawn from ``numpy.random.RandomState`` (the frozen legacy
+stream), so a seed gives the same arrays on every numpy version and every
+machine: golden fixtures store only seeds, outputs and checksums.
+
+Weight distribution: plain weights and biases are N(0, 0.02), LayerNorm
+gamma=1 / beta=0 (BASELINE config text "random-init fp32 weights N(0,0.02)").
+The checkpoints of the reference use ``torch.nn.utils.weight_norm`` for the
+flow and decoder convolutions (``runtime/models/vits.py:416-442``).  For those
+``weight_v`` is N(0, 0.02) and ``weight_g`` is set so that the folded weight
+W = g * v / ||v|| keeps activations of order one through the stack (a gain per
+layer, jittered by 10 %); with g also N(0, 0.02) the decoder would shrink its
+signal by ~1e-6 and the waveform test would be vacuous.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+__all__ = [
+    "VITS_V2_40K", "VITS_V2_48K", "vits_config_array", "make_vits_weights",
+    "make_vits_inputs", "make_vits_noise", "make_hubert_weights",
+    "make_hubert_input", "coarse_pitch",
+]
+
+# (sr, upsample_rates, upsample_kernels) of the two measured v2 generators.
+# 40k uses the v1/40k decoder (configs/v1/40k.json); 48k is configs/v2/48k.json.
+VITS_V2_40K = (40000, [10, 10, 2, 2], [16, 16, 4, 4])
+VITS_V2_48K = (48000, [12, 10, 2, 2], [24, 20, 4, 4])
+
+_HIDDEN = 192
+_FILTER = 768
+_PHONE = 768
+_HEADS = 2
+_LAYERS = 6
+_WINDOW = 10
+_GIN = 256
+_UP0 = 512
+
+
+def vits_config_array(sr: int = 40000) -> list:
+    """Config array in the checkpoint layout of ``runtime/models/vits.py:174-177``."""
+    sr_, rates, kernels = VITS_V2_48K if sr == 48000 else VITS_V2_40K
+    return [1025, 32, _HIDDEN, _HIDDEN, _FILTER, _HEADS, _LAYERS, 3, 0, "1",
+            [3, 7, 11], [[1, 3, 5], [1, 3, 5], [1, 3, 5]], list(rates), _UP0,
+            list(kernels), 1, _GIN, sr_]
+
+
+class _Gen:
+    def __init__(self, seed: int):
+        self.rs = np.random.RandomState(seed)
+
+    def n(self, *shape, std=0.02):
+        return (self.rs.standard_normal(shape) * std).astype(np.float32)
+
+    def wn(self, d: dict, key: str, shape, gain: float):
+        """weight_norm pair: v ~ N(0,0.02), g = gain * (1 + 0.1 N) per dim-0 row."""
+        d[key + ".weight_v"] = self.n(*shape)
+        g = gain * (1.0 + 0.1 * self.rs.standard_normal((shape[0], 1, 1)))
+        d[key + ".weight_g"] = g.astype(np.float32)
+
+
+def make_vits_weights(sr: int = 40000, seed: int = 0) -> dict:
+    """Random-init ``SynthesizerTrnMs768NSFsid`` state dict (v2, 1 speaker).
+
+    Key names and shapes follow the reference loader
+    (``runtime/models/vits.py:166-249``, ``:499-538``, ``:962-1059``,
+    ``:1086-1145``, ``:1285-1311``, ``:1390-1501``, ``:2133-2231``).
+    """
+    _, rates, kernels = VITS_V2_48K if sr == 48000 else VITS_V2_40K
+    G = _Gen(seed)
+    w: dict = {}
+    h, f = _HIDDEN, _FILTER
+    kc = h // _HEADS
+    w["emb_g.weight"] = G.n(1, _GIN, std=0.5)
+    w["enc_p.emb_phone.weight"] = G.n(h, _PHONE)
+    w["enc_p.emb_phone.bias"] = G.n(h)
+    w["enc_p.emb_pitch.weight"] = G.n(256, h)
+    for i in range(_LAYERS):
+        p = f"enc_p.encoder.attn_layers.{i}"
+        for nm in ("conv_q", "conv_k", "conv_v", "conv_o"):
+            w[f"{p}.{nm}.weight"] = G.n(h, h, 1, std=1.0 / math.sqrt(h))
+            w[f"{p}.{nm}.bias"] = G.n(h)
+        w[f"{p}.emb_rel_k"] = G.n(1, 2 * _WINDOW + 1, kc, std=kc ** -0.5)
+        w[f"{p}.emb_rel_v"] = G.n(1, 2 * _WINDOW + 1, kc, std=kc ** -0.5)
+        for nm in ("norm_layers_1", "norm_layers_2"):
+            w[f"enc_p.encoder.{nm}.{i}.gamma"] = np.ones(h, np.float32)
+            w[f"enc_p.encoder.{nm}.{i}.beta"] = np.zeros(h, np.float32)
+        q = f"enc_p.encoder.ffn_layers.{i}"
+        w[f"{q}.conv_1.weight"] = G.n(f, h, 3, std=1.0 / math.sqrt(3 * h))
+        w[f"{q}.conv_1.bias"] = G.n(f)
+        w[f"{q}.conv_2.weight"] = G.n(h, f, 3, std=1.0 / math.sqrt(3 * f))
+        w[f"{q}.conv_2.bias"] = G.n(h)
+    w["enc_p.proj.weight"] = G.n(2 * h, h, 1, std=0.5 / math.sqrt(h))
+    w["enc_p.proj.bias"] = G.n(2 * h)
+    half = h // 2
+    for idx in (0, 2, 4, 6):
+        p = f"flow.flows.{idx}"
+        w[f"{p}.pre.weight"] = G.n(h, half, 1, std=1.0 / math.sqrt(half))
+        w[f"{p}.pre.bias"] = G.n(h)
+        G.wn(w, f"{p}.enc.cond_layer", (2 * h * 3, _GIN, 1), gain=1.0)
+        w[f"{p}.enc.cond_layer.bias"] = G.n(2 * h * 3)
+        for i in range(3):
+            G.wn(w, f"{p}.enc.in_layers.{i}", (2 * h, h, 5), gain=1.0)
+            w[f"{p}.enc.in_layers.{i}.bias"] = G.n(2 * h)
+            out = 2 * h if i < 2 else h
+            G.wn(w, f"{p}.enc.res_skip_layers.{i}", (out, h, 1), gain=0.5)
+            w[f"{p}.enc.res_skip_layers.{i}.bias"] = G.n(out)
+        w[f"{p}.post.weight"] = G.n(half, h, 1, std=0.3 / math.sqrt(h))
+        w[f"{p}.post.bias"] = G.n(half)
+    # ---- GeneratorNSF ----
+    w["dec.conv_pre.weight"] = G.n(_UP0, h, 7, std=1.0 / math.sqrt(7 * h))
+    w["dec.conv_pre.bias"] = G.n(_UP0)
+    w["dec.cond.weight"] = G.n(_UP0, _GIN, 1, std=1.0 / math.sqrt(_GIN))
+    w["dec.cond.bias"] = G.n(_UP0)
+    w["dec.m_source.l_linear.weight"] = np.array([[0.9]], np.float32) + G.n(1, 1)
+    w["dec.m_source.l_linear.bias"] = G.n(1)
+    n_ups = len(rates)
+    for i in range(n_ups):
+        cin = _UP0 // (2 ** i)
+        cout = cin // 2
+        # convT weight [Cin, Cout, K]; norm is per input channel (dim 0).
+        # Variance gain of a stride-r transposed conv ~ g^2 * Cin / (Cout * r).
+        gain = math.sqrt(rates[i] * cout / cin) * 1.2
+        G.wn(w, f"dec.ups.{i}", (cin, cout, kernels[i]), gain=gain)
+        w[f"dec.ups.{i}.bias"] = G.n(cout)
+        stride_f0 = int(np.prod(rates[i + 1:])) if i + 1 < n_ups else 1
+        kn = stride_f0 * 2 if i + 1 < n_ups else 1
+        w[f"dec.noise_convs.{i}.weight"] = G.n(cout, 1, kn, std=1.0 / math.sqrt(kn))
+        w[f"dec.noise_convs.{i}.bias"] = G.n(cout)
+        for j, k in enumerate((3, 7, 11)):
+            base = f"dec.resblocks.{i * 3 + j}"
+            for conv in ("convs1", "convs2"):
+                for m in range(3):
+                    G.wn(w, f"{base}.{conv}.{m}", (cout, cout, k), gain=0.8)
+                    w[f"{base}.{conv}.{m}.bias"] = G.n(cout)
+    w["dec.conv_post.weight"] = G.n(1, _UP0 // (2 ** n_ups), 7,
+                                    std=0.6 / math.sqrt(7 * _UP0 // (2 ** n_ups)))
+    return w
+
+
+def coarse_pitch(f0: np.ndarray) -> np.ndarray:
+    """Mel quantisation of f0 to the 1..255 coarse bins (``runtime/pipeline.py:424-483``)."""
+    f0_min, f0_max = 50.0, 1100.0
+    mel_min = 1127 * np.log(1 + f0_min / 700)
+    mel_max = 1127 * np.log(1 + f0_max / 700)
+    f0 = np.asarray(f0, dtype=np.float64)
+    mel = 1127 * np.log(1 + f0 / 700)
+    pos = mel > 0
+    mel[pos] = (mel[pos] - mel_min) * 254 / (mel_max - mel_min) + 1
+    mel = np.clip(mel, 1, 255)
+    return np.rint(mel).astype(np.int64)
+
+
+def make_vits_inputs(P: int, seed: int = 0, phone_dim: int = _PHONE):
+    """One chunk of synthesizer inputs (BASELINE config 0 distribution).
+
+    Returns ``phone [1,P,768] f32 ~N(0,1)``, ``pitch [1,P] int64`` (coarse bins of
+    nsff0), ``nsff0 [1,P] f32 ~U(100,400) Hz`` with 10 % of frames zeroed
+    (unvoiced), ``sid [1] int64 = 0``.
+    """
+    rs = np.random.RandomState(10_000 + seed)
+    phone = rs.standard_normal((1, P, phone_dim)).astype(np.float32)
+    f0 = rs.uniform(100.0, 400.0, size=P)
+    f0[rs.uniform(size=P) < 0.1] = 0.0
+    nsff0 = f0.astype(np.float32)[None, :]
+    pitch = coarse_pitch(f0)[None, :]
+    sid = np.zeros(1, np.int64)
+    return phone, pitch, nsff0, sid
+
+
+def make_vits_noise(P: int, upp: int, seed: int, hidden: int = _HIDDEN):
+    """``nz [1,192,P]`` then ``ns [1,P*upp,1]`` from ``RandomState(seed)``.
+
+    Same draw order as ``SynthesizerTrn._make_noise`` (``runtime/models/vits.py:2337-2350``).
+    """
+    rng = np.random.RandomState(seed)
+    nz = rng.standard_normal((1, hidden, P)).astype(np.float32)
+    ns = rng.standard_normal((1, P * upp, 1)).astype(np.float32)
+    return nz, ns
+
+
+def make_hubert_weights(seed: int = 0) -> dict:
+    """Random-init HuBERT-base state dict with transformers key names.
+
+    Keys follow the reference loader ``runtime/models/hubert.py:499-559``.
+    """
+    G = _Gen(20_000 + seed)
+    sd: dict = {}
+    ks = [10, 3, 3, 3, 3, 2, 2]
+    cin = 1
+    for i, k in enumerate(ks):
+        sd[f"feature_extractor.conv_layers.{i}.conv.weight"] = G.n(
+            512, cin, k, std=1.0 / math.sqrt(cin * k))
+        cin = 512
+    sd["feature_extractor.conv_layers.0.layer_norm.weight"] = np.ones(512, np.float32)
+    sd["feature_extractor.conv_layers.0.layer_norm.bias"] = np.zeros(512, np.float32)
+    sd["feature_projection.layer_norm.weight"] = np.ones(512, np.float32)
+    sd["feature_projection.layer_norm.bias"] = np.zeros(512, np.float32)
+    sd["feature_projection.projection.weight"] = G.n(768, 512)
+    sd["feature_projection.projection.bias"] = G.n(768)
+    sd["encoder.pos_conv_embed.conv.weight_g"] = (
+        1.0 + 0.1 * G.rs.standard_normal((1, 1, 128))).astype(np.float32)
+    sd["encoder.pos_conv_embed.conv.weight_v"] = G.n(768, 48, 128)
+    sd["encoder.pos_conv_embed.conv.bias"] = G.n(768)
+    sd["encoder.layer_norm.weight"] = np.ones(768, np.float32)
+    sd["encoder.layer_norm.bias"] = np.zeros(768, np.float32)
+    for i in range(12):
+        p = f"encoder.layers.{i}."
+        for nm in ("q_proj", "k_proj", "v_proj", "out_proj"):
+            sd[p + f"attention.{nm}.weight"] = G.n(768, 768)
+            sd[p + f"attention.{nm}.bias"] = G.n(768)
+        sd[p + "layer_norm.weight"] = np.ones(768, np.float32)
+        sd[p + "layer_norm.bias"] = np.zeros(768, np.float32)
+        sd[p + "feed_forward.intermediate_dense.weight"] = G.n(3072, 768)
+        sd[p + "feed_forward.intermediate_dense.bias"] = G.n(3072)
+        sd[p + "feed_forward.output_dense.weight"] = G.n(768, 3072)
+        sd[p + "feed_forward.output_dense.bias"] = G.n(768)
+        sd[p + "final_layer_norm.weight"] = np.ones(768, np.float32)
+        sd[p + "final_layer_norm.bias"] = np.zeros(768, np.float32)
+    sd["final_proj.weight"] = G.n(256, 768)
+    sd["final_proj.bias"] = G.n(256)
+    return sd
+
+
+def make_hubert_input(T: int = 160000, seed: int = 0) -> np.ndarray:
+    """16 kHz waveform ``[1,T] f32 ~U(-0.5,0.5)``."""
+    rs = np.random.RandomState(30_000 + seed)
+    return rs.uniform(-0.5, 0.5, size=(1, T)).astype(np.float32)

@@ -1,0 +1,186 @@
+"""Generate golden vectors by running the reference's own numpy CPU path.
+
+Run in a container where the reference checkout is present::
+
+    python tests/golden/make_golden.py [--ref /path/to/rvc-vulkan]
+
+It imports ``runtime`` from the reference (read-only, ``RVC_BACKEND=numpy``),
+replaces the checkpoint loaders with the seeded synthetic checkpoints of
+``rvc_cuda.synthetic`` (the loaders read files; no checkpoints exist here),
+runs ``SynthesizerTrn.infer_controlled`` / ``HubertEncoder.encode`` and the
+per-op numpy kernels, and writes ``tests/golden/*.npz``.  Weights and inputs
+are not stored: they are regenerated from the recorded seeds (legacy
+``RandomState`` streams are frozen) and checked against recorded SHA-256
+digests, so a drift in generation is detected rather than silently compared.
+"""
+
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import os
+import sys
+import tempfile
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(ROOT, "rvc-vulkan_b200"))
+
+from rvc_cuda import synthetic as syn  # noqa: E402
+
+
+def digest(arrays) -> str:
+    h = hashlib.sha256()
+    for a in arrays:
+        a = np.ascontiguousarray(a)
+        h.update(str(a.dtype).encode())
+        h.update(str(a.shape).encode())
+        h.update(a.tobytes())
+    return h.hexdigest()
+
+
+def weights_digest(w: dict) -> str:
+    return digest([w[k] for k in sorted(w)])
+
+
+# (name, sr, P frames, weight seed, input seed, noise seed)
+VITS_CASES = [
+    ("vits40k_p32", 40000, 32, 0, 1, 11),
+    ("vits48k_p24", 48000, 24, 1, 2, 12),
+    ("vits40k_p7", 40000, 7, 0, 3, 13),     # P < window+1: sliced rel-embeddings
+]
+# (name, T samples, weight seed, input seed)
+HUBERT_CASES = [
+    ("hubert_t8000", 8000, 0, 1),
+    ("hubert_t3201", 3201, 0, 2),           # odd length: ragged conv strides
+]
+
+
+def run_vits(runtime_vits, name, sr, P, wseed, iseed, nseed, meta):
+    w = syn.make_vits_weights(sr, wseed)
+    cfg = syn.vits_config_array(sr)
+    runtime_vits._load_ckpt = lambda path: {"weight": w, "config": cfg}
+    net = runtime_vits.SynthesizerTrn("synthetic.pth")
+    phone, pitch, nsff0, sid = syn.make_vits_inputs(P, iseed)
+    nz, ns = syn.make_vits_noise(P, net.cfg.upp, nseed)
+    rec = {}
+    enc_cls = runtime_vits._TextEncoder
+    flow_cls = runtime_vits._FlowBlock
+    orig_stats, orig_rev = enc_cls.stats, flow_cls.reverse
+
+    def stats(self, x):
+        rec["enc_h"] = np.array(x[0])
+        m, logs = orig_stats(self, x)
+        rec["enc_m"], rec["enc_logs"] = np.array(m[0].T), np.array(logs[0].T)
+        return m, logs
+
+    def reverse(self, z, x_mask, g):
+        out = orig_rev(self, z, x_mask, g)
+        rec["flow_z"] = np.array(out[0].T)
+        return out
+
+    enc_cls.stats, flow_cls.reverse = stats, reverse
+    try:
+        wav = net.infer_controlled(phone, pitch, nsff0, sid, nz, ns)
+    finally:
+        enc_cls.stats, flow_cls.reverse = orig_stats, orig_rev
+    rec["wave"] = np.asarray(wav, np.float32).reshape(-1)
+    np.savez_compressed(os.path.join(HERE, name + ".npz"), **rec)
+    meta[name] = {
+        "kind": "vits", "sr": sr, "P": P, "weight_seed": wseed, "input_seed": iseed,
+        "noise_seed": nseed, "upp": int(net.cfg.upp),
+        "weights_sha256": weights_digest(w),
+        "inputs_sha256": digest([phone, pitch, nsff0, sid, nz, ns]),
+    }
+
+
+def run_hubert(runtime_hubert, name, T, wseed, iseed, meta):
+    sd = syn.make_hubert_weights(wseed)
+    x = syn.make_hubert_input(T, iseed)
+    with tempfile.TemporaryDirectory() as d:
+        open(os.path.join(d, "pytorch_model.bin"), "wb").close()
+        runtime_hubert.load_pth = lambda path: sd
+        enc = runtime_hubert.HubertEncoder(d)
+        feats = enc._feature_extractor(x)
+        out = enc.encode(x, version=2)
+    np.savez_compressed(os.path.join(HERE, name + ".npz"),
+                        conv=np.asarray(feats[0], np.float32),
+                        out=np.asarray(out[0], np.float32))
+    meta[name] = {"kind": "hubert", "T": T, "weight_seed": wseed, "input_seed": iseed,
+                  "weights_sha256": weights_digest(sd), "inputs_sha256": digest([x])}
+
+
+def run_ops(nn, meta):
+    """Per-op vectors from ``runtime.nn``'s numpy kernels (``_conv1d_numpy`` etc.)."""
+    rs = np.random.RandomState(4242)
+    rec = {}
+    cases = []
+    conv_cases = [  # (B, C, T, O, K, stride, pad, dil)
+        (1, 5, 37, 7, 3, 1, 1, 1), (2, 16, 64, 8, 7, 1, (3, 3), 2),
+        (1, 3, 50, 4, 10, 5, 0, 1), (1, 8, 33, 8, 11, 1, (25, 25), 5),
+        (1, 4, 9, 6, 5, 2, (2, 1), 1), (1, 2, 3, 3, 5, 1, 0, 1),
+    ]
+    for i, (B, C, T, O, K, s, p, d) in enumerate(conv_cases):
+        x = rs.standard_normal((B, C, T)).astype(np.float32)
+        w = rs.standard_normal((O, C, K)).astype(np.float32)
+        b = rs.standard_normal(O).astype(np.float32)
+        rec[f"conv1d_{i}_x"], rec[f"conv1d_{i}_w"], rec[f"conv1d_{i}_b"] = x, w, b
+        rec[f"conv1d_{i}_y"] = nn._conv1d_numpy(x, w, b, s, p, d)
+        cases.append({"op": "conv1d", "i": i, "stride": s,
+                      "padding": list(p) if isinstance(p, tuple) else p, "dilation": d})
+    convt_cases = [(1, 6, 11, 4, 16, 10, 3), (2, 8, 7, 5, 4, 2, 1), (1, 3, 5, 2, 24, 12, 6)]
+    for i, (B, Ci, T, Co, K, s, p) in enumerate(convt_cases):
+        x = rs.standard_normal((B, Ci, T)).astype(np.float32)
+        w = rs.standard_normal((Ci, Co, K)).astype(np.float32)
+        b = rs.standard_normal(Co).astype(np.float32)
+        rec[f"convt_{i}_x"], rec[f"convt_{i}_w"], rec[f"convt_{i}_b"] = x, w, b
+        rec[f"convt_{i}_y"] = nn._conv_transpose1d_numpy(x, w, b, s, p, 0, 1)
+        cases.append({"op": "conv_transpose1d", "i": i, "stride": s, "padding": p})
+    x = (rs.standard_normal((3, 17, 192)) * 3 + 1).astype(np.float32)
+    g = rs.standard_normal(192).astype(np.float32)
+    bt = rs.standard_normal(192).astype(np.float32)
+    rec["ln_x"], rec["ln_g"], rec["ln_b"] = x, g, bt
+    from runtime import backend  # numpy backend: the reference formula
+    rec["ln_y"] = backend.layer_norm(x, g, bt, 1e-5)
+    sx = (rs.standard_normal((4, 33)) * 10).astype(np.float32)
+    sx[0, :] += 1000.0
+    rec["sm_x"], rec["sm_y"] = sx, backend.softmax(sx)
+    gx = (rs.standard_normal(4096) * 3).astype(np.float32)
+    rec["gelu_x"] = gx
+    from runtime.models import hubert as rh
+    rec["gelu_y"] = rh.gelu_erf(gx)
+    rec["leaky_x"] = gx
+    rec["leaky_y"] = nn.leaky_relu(gx, 0.1)
+    np.savez_compressed(os.path.join(HERE, "ops.npz"), **rec)
+    meta["ops"] = {"kind": "ops", "cases": cases}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default=os.environ.get("RVC_REFERENCE", "/root/reference"))
+    args = ap.parse_args()
+    os.environ["RVC_BACKEND"] = "numpy"
+    sys.path.insert(0, args.ref)
+    from runtime import nn  # noqa: PLC0415
+    from runtime.models import hubert as runtime_hubert  # noqa: PLC0415
+    from runtime.models import vits as runtime_vits  # noqa: PLC0415
+    import numba  # noqa: PLC0415
+    import threadpoolctl  # noqa: PLC0415
+
+    meta = {"numpy": np.__version__, "numba": numba.__version__,
+            "blas": [i.get("internal_api") for i in threadpoolctl.threadpool_info()]}
+    for c in VITS_CASES:
+        run_vits(runtime_vits, *c, meta)
+    for c in HUBERT_CASES:
+        run_hubert(runtime_hubert, *c, meta)
+    run_ops(nn, meta)
+    with open(os.path.join(HERE, "golden.json"), "w") as f:
+        json.dump(meta, f, indent=1, sort_keys=True)
+    print("wrote", sorted(k for k in meta if k not in ("numpy", "numba", "blas")))
+
+
+if __name__ == "__main__":
+    main()

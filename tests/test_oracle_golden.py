@@ -1,0 +1,73 @@
+"""Pin the oracle: it must reproduce the reference's own outputs.
+
+The golden vectors were produced by running the reference's numpy CPU path
+(``tests/golden/make_golden.py``).  Oracle and reference are both float32
+numpy; they differ only in BLAS summation order, so the bar here is far
+tighter than the CUDA parity bar.
+"""
+
+import numpy as np
+import pytest
+
+from tests.conftest import load_golden, rel_l2
+from oracle import hubert as OH
+from oracle import ops as O
+from oracle import vits as OV
+from rvc_cuda import synthetic as syn
+from tests.golden.make_golden import digest, weights_digest
+
+VITS = ["vits40k_p32", "vits48k_p24", "vits40k_p7"]
+HUB = ["hubert_t8000", "hubert_t3201"]
+
+
+@pytest.mark.parametrize("name", VITS)
+def test_vits_oracle_matches_reference(name, golden_meta):
+    m = golden_meta[name]
+    w = syn.make_vits_weights(m["sr"], m["weight_seed"])
+    assert weights_digest(w) == m["weights_sha256"], "synthetic weight stream drifted"
+    phone, pitch, nsff0, sid = syn.make_vits_inputs(m["P"], m["input_seed"])
+    nz, ns = syn.make_vits_noise(m["P"], m["upp"], m["noise_seed"])
+    assert digest([phone, pitch, nsff0, sid, nz, ns]) == m["inputs_sha256"]
+    g = load_golden(name)
+    taps = {}
+    wav = OV.synth(w, syn.vits_config_array(m["sr"]), phone, pitch, nsff0, sid, nz, ns, taps)
+    assert rel_l2(taps["enc.l5"], g["enc_h"]) < 1e-5
+    assert rel_l2(taps["enc.m"], g["enc_m"]) < 1e-5
+    assert rel_l2(taps["enc.logs"], g["enc_logs"]) < 1e-5
+    assert rel_l2(taps["flow.z"], g["flow_z"]) < 1e-5
+    assert wav.size == g["wave"].size
+    assert np.abs(wav.reshape(-1) - g["wave"]).max() < 1e-5
+
+
+@pytest.mark.parametrize("name", HUB)
+def test_hubert_oracle_matches_reference(name, golden_meta):
+    m = golden_meta[name]
+    sd = syn.make_hubert_weights(m["weight_seed"])
+    assert weights_digest(sd) == m["weights_sha256"]
+    x = syn.make_hubert_input(m["T"], m["input_seed"])
+    g = load_golden(name)
+    taps = {}
+    out = OH.encode(OH.prepare(sd), x, taps)
+    assert rel_l2(taps["conv6"], g["conv"]) < 1e-5
+    assert out.shape[1:] == g["out"].shape
+    assert rel_l2(out[0], g["out"]) < 1e-5
+
+
+def test_ops_oracle_matches_reference(golden_meta):
+    g = load_golden("ops")
+    for c in golden_meta["ops"]["cases"]:
+        i = c["i"]
+        if c["op"] == "conv1d":
+            pad = tuple(c["padding"]) if isinstance(c["padding"], list) else c["padding"]
+            y = O.conv1d(g[f"conv1d_{i}_x"], g[f"conv1d_{i}_w"], g[f"conv1d_{i}_b"],
+                         c["stride"], pad, c["dilation"])
+            np.testing.assert_allclose(y, g[f"conv1d_{i}_y"], rtol=1e-5, atol=1e-5)
+        else:
+            y = O.conv_transpose1d(g[f"convt_{i}_x"], g[f"convt_{i}_w"], g[f"convt_{i}_b"],
+                                   c["stride"], c["padding"])
+            np.testing.assert_allclose(y, g[f"convt_{i}_y"], rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(O.layer_norm(g["ln_x"], g["ln_g"], g["ln_b"]), g["ln_y"],
+                               rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(O.softmax(g["sm_x"]), g["sm_y"], rtol=1e-6, atol=1e-7)
+    np.testing.assert_allclose(O.gelu_erf(g["gelu_x"]), g["gelu_y"], rtol=1e-6, atol=1e-6)
+    np.testing.assert_array_equal(O.leaky_relu(g["leaky_x"], 0.1), g["leaky_y"])
