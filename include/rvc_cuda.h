@@ -1,0 +1,157 @@
+/* librvc_cuda: B200 (sm_100a) CUDA backend for the RVC inference hot path.
+ *
+ * C ABI reached from Python through ctypes, the same way the reference reaches
+ * its Vulkan engine rvc_core.dll (runtime/_vulkan.py:127-279).  Conventions
+ * follow the reference engine's FFI (engine/src/ffi.zig):
+ *   - every call returns int32: 0 = ok, < 0 = error code (RVC_E_*);
+ *   - the message of the last error of the calling thread is read with
+ *     rvc_cuda_last_error (ffi.zig:1110 rvc_last_error; the reference turns
+ *     rc != 0 into RuntimeError at runtime/_vulkan.py:320-324);
+ *   - objects are opaque int64 handles (ffi.zig:50 rvc_engine_create);
+ *   - host pointers are borrowed for the duration of the call only; device
+ *     memory belongs to the context that allocated it;
+ *   - one context per device; calls on a context are serialised by a mutex
+ *     (the reference serialises on _BATCH_LIFECYCLE_LOCK,
+ *     runtime/vulkan_ops.py:160); different devices may be driven from
+ *     different host threads.
+ * No C++ exception crosses this boundary.  All float tensors are float32,
+ * C-contiguous, in the reference's layouts unless a function says otherwise.
+ */
+#ifndef RVC_CUDA_H
+#define RVC_CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RVC_OK 0
+#define RVC_E_ARG (-1)     /* bad argument or shape (Python raises ValueError) */
+#define RVC_E_CUDA (-2)    /* CUDA runtime error */
+#define RVC_E_TIMEOUT (-3) /* a bounded device wait gave up */
+#define RVC_E_STATE (-4)   /* missing weight, freed handle, not finalised */
+#define RVC_E_OOM (-5)     /* device allocation failed or over the context cap */
+
+/* ---------------------------------------------------------------- library */
+/* Library ABI version (major*100 + minor). */
+int32_t rvc_cuda_version(void);
+/* Copies the calling thread's last error message (NUL-terminated, truncated to
+ * n bytes); returns its full length.  Replaces rvc_last_error (ffi.zig:1110). */
+int32_t rvc_cuda_last_error(char* buf, int64_t n);
+/* Kernel launches issued by this library so far (process-wide). */
+int32_t rvc_cuda_launch_count(int64_t* n);
+/* Number of visible CUDA devices. */
+int32_t rvc_cuda_device_count(int32_t* n);
+
+/* ---------------------------------------------------------------- context */
+/* Creates a context (stream, error flag, workspace) on `device`.
+ * Replaces rvc_engine_create / rvc_engine_destroy (ffi.zig:50-74). */
+int32_t rvc_cuda_create(int32_t device, int64_t* ctx);
+int32_t rvc_cuda_destroy(int64_t ctx);
+/* Waits for all work on the context's stream, polling at most timeout_ms
+ * (<= 0: 60 s); returns RVC_E_TIMEOUT instead of blocking forever.  Also
+ * reports a device-side wait that gave up inside a kernel (RVC_E_TIMEOUT). */
+int32_t rvc_cuda_sync(int64_t ctx, int32_t timeout_ms);
+/* The context's cudaStream_t, for callers that time work with CUDA events. */
+int32_t rvc_cuda_stream(int64_t ctx, void** stream);
+/* Caps the bytes the context may hold on the device (0 = no cap); a request
+ * over the cap fails with RVC_E_OOM (host-side fault injection for tests). */
+int32_t rvc_cuda_set_mem_cap(int64_t ctx, int64_t bytes);
+/* Device buffers owned by the context (for device-resident inputs). */
+int32_t rvc_cuda_alloc(int64_t ctx, int64_t bytes, void** dptr);
+int32_t rvc_cuda_free(int64_t ctx, void* dptr);
+int32_t rvc_cuda_h2d(int64_t ctx, void* dst, const void* src, int64_t bytes);
+int32_t rvc_cuda_d2h(int64_t ctx, void* dst, const void* src, int64_t bytes);
+/* Per-kernel timing of the tensor-core convolutions: enable, then read the
+ * accumulated launch count, device milliseconds and algorithmic FLOPs. */
+int32_t rvc_cuda_profile(int64_t ctx, int32_t enable);
+int32_t rvc_cuda_profile_read(int64_t ctx, int64_t* launches, double* ms, double* flops);
+
+/* ------------------------------------------------- tier 1: operator module
+ * Numpy-semantics operators behind runtime.backend's RVC_BACKEND dispatch
+ * (runtime/backend.py:205-319).  Host in, host out. */
+
+/* conv1d, torch semantics: x[B,C,T], w[O,C,K], b[O] or NULL, asymmetric pad.
+ * y[B,O,oL], oL = (T+pad_l+pad_r-dil*(K-1)-1)/stride+1.
+ * Replaces backend.conv1d (runtime/backend.py:233) / rvc_conv1d (ffi.zig:294). */
+int32_t rvc_cuda_conv1d(int64_t ctx, const float* x, int32_t B, int32_t C, int32_t T, const float* w,
+                        int32_t O, int32_t K, const float* b, int32_t stride, int32_t pad_l, int32_t pad_r,
+                        int32_t dilation, float* y, int32_t oL);
+/* conv_transpose1d: x[B,Ci,T], w[Ci,Co,K], b[Co] or NULL,
+ * oL = (T-1)*stride - 2*padding + dilation*(K-1) + output_padding + 1.
+ * Replaces backend.conv_transpose1d (runtime/backend.py:242) / rvc_conv_t1d (ffi.zig:336). */
+int32_t rvc_cuda_conv_transpose1d(int64_t ctx, const float* x, int32_t B, int32_t Ci, int32_t T,
+                                  const float* w, int32_t Co, int32_t K, const float* b, int32_t stride,
+                                  int32_t padding, int32_t output_padding, int32_t dilation, float* y,
+                                  int32_t oL);
+/* c[M,N] = a[M,K] @ b[K,N].  Replaces backend.matmul (runtime/backend.py:205) / rvc_matmul (ffi.zig:233). */
+int32_t rvc_cuda_matmul(int64_t ctx, const float* a, const float* b, int32_t M, int32_t K, int32_t N,
+                        float* c);
+/* Row LayerNorm over the last axis (biased variance).  Replaces
+ * backend.layer_norm (runtime/backend.py:286) / rvc_layernorm (ffi.zig:575). */
+int32_t rvc_cuda_layer_norm(int64_t ctx, const float* x, int64_t rows, int32_t C, const float* gamma,
+                            const float* beta, float eps, float* y);
+/* Row softmax over the last axis.  Replaces backend.softmax (runtime/backend.py:298) / rvc_softmax (ffi.zig:604). */
+int32_t rvc_cuda_softmax(int64_t ctx, const float* x, int64_t rows, int32_t C, float* y);
+/* Elementwise: op 0 add(a,b), 1 mul(a,b), 2 relu(a), 3 leaky_relu(a, alpha),
+ * 4 gelu_erf(a), 5 tanh(a), 6 sigmoid(a).  b may be NULL for unary ops.
+ * Replaces backend.add/mul/relu/add_inplace/mul_inplace (runtime/backend.py:212-284). */
+int32_t rvc_cuda_elementwise(int64_t ctx, int32_t op, const float* a, const float* b, int64_t n,
+                             float alpha, float* y);
+/* Row gather y[n,E] = table[ids[n]] (negative ids count from the end).
+ * Replaces backend.embedding (runtime/backend.py:263). */
+int32_t rvc_cuda_embedding(int64_t ctx, const int64_t* ids, int64_t n, const float* table, int32_t V,
+                           int32_t E, float* y);
+/* WaveNet gate: x[B,2H,T] (+ g[B,2H,1] or NULL) -> tanh(x[:H]+g[:H]) * sigmoid(x[H:]+g[H:]) -> y[B,H,T]
+ * (runtime/models/vits.py:1131-1132; engine/shaders/gating.comp). */
+int32_t rvc_cuda_gating(int64_t ctx, const float* x, const float* g, int32_t B, int32_t H, int32_t T,
+                        float* y);
+/* T5 relative-position self-attention of the text encoder for one layer:
+ * q,k,v[B,heads*kc,P] (projected, NCT) + emb_rel_k/v[2*window+1,kc] -> y[B,heads*kc,P]
+ * (runtime/models/vits.py:993-1014; engine/shaders/banded_attn_qk/sv.comp). */
+int32_t rvc_cuda_rel_attention(int64_t ctx, const float* q, const float* k, const float* v,
+                               const float* emb_k, const float* emb_v, int32_t B, int32_t heads,
+                               int32_t kc, int32_t P, int32_t window, float* y);
+/* im2col of a 1-D conv: x[B,C,T] -> cols[B,oL,C*K] (column index c*K+k).
+ * Replaces BatchRunner.im2col_1d (runtime/vulkan_ops.py:2727). */
+int32_t rvc_cuda_im2col1d(int64_t ctx, const float* x, int32_t B, int32_t C, int32_t T, int32_t K,
+                          int32_t stride, int32_t pad_l, int32_t dilation, int32_t oL, float* cols);
+
+/* ------------------------------------------------ tier 2: synthesizer model
+ * Device-resident SynthesizerTrnMs768NSFsid (runtime/models/vits.py:2237-2598):
+ * weights uploaded once under their checkpoint keys, weight norm folded on the
+ * device, one call runs enc_p + flow + GeneratorNSF for B equal-length chunks. */
+
+/* cfg: {sr, hidden, filter, heads, layers, kc, window, gin, up0, n_ups,
+ *       rates[n_ups]..., kernels[n_ups]..., phone_dim, n_spk, precision}
+ * precision: 0 = BF16x3 split (parity), 1 = SIMT fp32 (in-library check). */
+int32_t rvc_cuda_synth_create(int64_t ctx, const int32_t* cfg, int32_t ncfg, int64_t* model);
+int32_t rvc_cuda_synth_destroy(int64_t model);
+/* Uploads one checkpoint tensor (key as in the reference state dict). */
+int32_t rvc_cuda_synth_set_weight(int64_t model, const char* key, const float* data, const int64_t* shape,
+                                  int32_t ndim);
+/* Folds weight norm, packs tensor-core operands; required before infer. */
+int32_t rvc_cuda_synth_finalize(int64_t model);
+/* B chunks of P frames: phone[B,P,phone_dim], pitch[B,P] int64, nsff0[B,P],
+ * sid[B] int64, nz[B,hidden,P], ns[B,P*upp] -> wave[B,P*upp].
+ * Host buffers; same math as SynthesizerTrn.infer_controlled (vits.py:2551). */
+int32_t rvc_cuda_synth_infer(int64_t model, int32_t B, int32_t P, const float* phone, const int64_t* pitch,
+                             const float* nsff0, const int64_t* sid, const float* nz, const float* ns,
+                             float* wave);
+/* Same with device pointers (allocated by rvc_cuda_alloc); asynchronous on
+ * the context stream (call rvc_cuda_sync before reading `wave`). */
+int32_t rvc_cuda_synth_infer_device(int64_t model, int32_t B, int32_t P, const float* phone,
+                                    const int64_t* pitch, const float* nsff0, const int64_t* sid,
+                                    const float* nz, const float* ns, float* wave);
+/* Debug taps: copies the named intermediate of the last infer (e.g.
+ * "enc.l5", "flow.z", "dec.s2.out") into out (n floats); RVC_E_ARG if unknown. */
+int32_t rvc_cuda_synth_tap(int64_t model, const char* name, float* out, int64_t n);
+/* Enables recording of debug taps (off by default: taps cost a copy). */
+int32_t rvc_cuda_synth_keep_taps(int64_t model, int32_t enable);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RVC_CUDA_H */

@@ -1,0 +1,522 @@
+// extern "C" boundary of librvc_cuda (declared in include/rvc_cuda.h).
+// Every entry point: look up handles, take the context lock, set the device,
+// run, and turn any exception into an int32 status + thread-local message.
+#include "../../include/rvc_cuda.h"
+#include "synth.cuh"
+
+#include <cstring>
+#include <memory>
+#include <unordered_map>
+
+using namespace rvc;
+
+namespace {
+
+std::mutex g_reg_mu;
+std::unordered_map<int64_t, std::unique_ptr<Context>> g_ctx;
+std::unordered_map<int64_t, std::unique_ptr<SynthModel>> g_synth;
+int64_t g_next = 1;
+
+Context* get_ctx(int64_t h) {
+  std::lock_guard<std::mutex> lk(g_reg_mu);
+  auto it = g_ctx.find(h);
+  if (it == g_ctx.end()) throw Error{kErrState, "invalid context handle " + std::to_string(h)};
+  return it->second.get();
+}
+
+SynthModel* get_synth(int64_t h) {
+  std::lock_guard<std::mutex> lk(g_reg_mu);
+  auto it = g_synth.find(h);
+  if (it == g_synth.end()) throw Error{kErrState, "invalid synthesizer handle " + std::to_string(h)};
+  return it->second.get();
+}
+
+template <typename F>
+int32_t guarded(F&& f) {
+  try {
+    f();
+    return kOk;
+  } catch (const Error& e) {
+    set_error(e.msg);
+    return e.code;
+  } catch (const std::exception& e) {
+    set_error(std::string("internal error: ") + e.what());
+    return kErrState;
+  } catch (...) {
+    set_error("internal error");
+    return kErrState;
+  }
+}
+
+// Runs `f` on the context's device under its lock.
+template <typename F>
+int32_t on_ctx(int64_t h, F&& f) {
+  return guarded([&] {
+    Context* c = get_ctx(h);
+    std::lock_guard<std::mutex> lk(c->mu);
+    DeviceGuard dg(c->device);
+    f(c);
+  });
+}
+
+int32_t finish(Context* c) {
+  int32_t rc = c->sync(0);
+  if (rc != kOk) throw Error{rc, get_error()};
+  return rc;
+}
+
+void h2d(Context* c, void* d, const void* h, size_t n) {
+  if (n) RVC_CUDA_TRY(cudaMemcpyAsync(d, h, n, cudaMemcpyHostToDevice, c->stream));
+}
+void d2h(Context* c, void* h, const void* d, size_t n) {
+  if (n) RVC_CUDA_TRY(cudaMemcpyAsync(h, d, n, cudaMemcpyDeviceToHost, c->stream));
+}
+
+template <typename F>
+int32_t on_synth(int64_t model, F&& f) {
+  return guarded([&] {
+    SynthModel* m = get_synth(model);
+    std::lock_guard<std::mutex> lk(m->ctx->mu);
+    DeviceGuard dg(m->ctx->device);
+    f(m);
+  });
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t rvc_cuda_version(void) { return 100; }
+
+int32_t rvc_cuda_launch_count(int64_t* n) {
+  *n = launch_count();
+  return kOk;
+}
+
+int32_t rvc_cuda_last_error(char* buf, int64_t n) {
+  const std::string& m = get_error();
+  if (buf && n > 0) {
+    size_t k = std::min<size_t>((size_t)n - 1, m.size());
+    std::memcpy(buf, m.data(), k);
+    buf[k] = 0;
+  }
+  return (int32_t)m.size();
+}
+
+int32_t rvc_cuda_device_count(int32_t* n) {
+  return guarded([&] {
+    int c = 0;
+    cudaError_t e = cudaGetDeviceCount(&c);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      c = 0;
+    }
+    *n = c;
+  });
+}
+
+int32_t rvc_cuda_create(int32_t device, int64_t* ctx) {
+  return guarded([&] {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+      cudaGetLastError();
+      throw Error{kErrArg, "no CUDA device " + std::to_string(device) + " (" + std::to_string(n) + " visible)"};
+    }
+    cudaDeviceProp prop;
+    RVC_CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10)
+      throw Error{kErrArg, std::string("librvc_cuda is built for sm_100a (B200); device is ") + prop.name};
+    auto c = std::make_unique<Context>(device);
+    std::lock_guard<std::mutex> lk(g_reg_mu);
+    *ctx = g_next++;
+    g_ctx[*ctx] = std::move(c);
+  });
+}
+
+int32_t rvc_cuda_destroy(int64_t ctx) {
+  return guarded([&] {
+    std::unique_ptr<Context> c;
+    {
+      std::lock_guard<std::mutex> lk(g_reg_mu);
+      auto it = g_ctx.find(ctx);
+      if (it == g_ctx.end()) throw Error{kErrState, "invalid context handle " + std::to_string(ctx)};
+      for (auto s = g_synth.begin(); s != g_synth.end();) {
+        if (s->second->ctx == it->second.get())
+          s = g_synth.erase(s);
+        else
+          ++s;
+      }
+      c = std::move(it->second);
+      g_ctx.erase(it);
+    }
+    std::lock_guard<std::mutex> lk(c->mu);
+    c.reset();
+  });
+}
+
+int32_t rvc_cuda_sync(int64_t ctx, int32_t timeout_ms) {
+  return on_ctx(ctx, [&](Context* c) {
+    int32_t rc = c->sync(timeout_ms);
+    if (rc != kOk) throw Error{rc, get_error()};
+  });
+}
+
+int32_t rvc_cuda_stream(int64_t ctx, void** stream) {
+  return on_ctx(ctx, [&](Context* c) { *stream = (void*)c->stream; });
+}
+
+int32_t rvc_cuda_set_mem_cap(int64_t ctx, int64_t bytes) {
+  return on_ctx(ctx, [&](Context* c) { c->mem_cap = bytes; });
+}
+
+int32_t rvc_cuda_alloc(int64_t ctx, int64_t bytes, void** dptr) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(bytes >= 0, "alloc: negative size");
+    *dptr = c->alloc((size_t)bytes);
+  });
+}
+
+int32_t rvc_cuda_free(int64_t ctx, void* dptr) {
+  return on_ctx(ctx, [&](Context* c) { c->free(dptr); });
+}
+
+int32_t rvc_cuda_h2d(int64_t ctx, void* dst, const void* src, int64_t bytes) {
+  return on_ctx(ctx, [&](Context* c) {
+    h2d(c, dst, src, (size_t)bytes);
+    finish(c);
+  });
+}
+
+int32_t rvc_cuda_d2h(int64_t ctx, void* dst, const void* src, int64_t bytes) {
+  return on_ctx(ctx, [&](Context* c) {
+    d2h(c, dst, src, (size_t)bytes);
+    finish(c);
+  });
+}
+
+int32_t rvc_cuda_profile(int64_t ctx, int32_t enable) {
+  return on_ctx(ctx, [&](Context* c) {
+    c->prof_collect();
+    c->prof = enable != 0;
+    c->prof_launches = 0;
+    c->prof_ms = 0.0;
+    c->prof_flops = 0.0;
+  });
+}
+
+int32_t rvc_cuda_profile_read(int64_t ctx, int64_t* launches, double* ms, double* flops) {
+  return on_ctx(ctx, [&](Context* c) {
+    c->prof_collect();
+    *launches = c->prof_launches;
+    *ms = c->prof_ms;
+    *flops = c->prof_flops;
+  });
+}
+
+// ----------------------------------------------------------------- tier 1
+int32_t rvc_cuda_conv1d(int64_t ctx, const float* x, int32_t B, int32_t C, int32_t T, const float* w, int32_t O,
+                        int32_t K, const float* b, int32_t stride, int32_t pad_l, int32_t pad_r, int32_t dilation,
+                        float* y, int32_t oL) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(B >= 0 && C > 0 && T >= 0 && O > 0 && K > 0 && stride > 0 && dilation > 0 && pad_l >= 0 &&
+                      pad_r >= 0,
+                  "conv1d: bad arguments");
+    RVC_CHECK_ARG(oL == (T + pad_l + pad_r - dilation * (K - 1) - 1) / stride + 1 || (oL == 0),
+                  "conv1d: output length mismatch");
+    if (B == 0 || oL <= 0) return;
+    DevBuf dx(c, sizeof(float) * (size_t)B * C * T), dxt(c, sizeof(float) * (size_t)B * C * T);
+    DevBuf dw(c, sizeof(float) * (size_t)O * C * K), dy(c, sizeof(float) * (size_t)B * O * oL),
+        dyt(c, sizeof(float) * (size_t)B * O * oL);
+    DevBuf db;
+    h2d(c, dx.p, x, dx.bytes);
+    h2d(c, dw.p, w, dw.bytes);
+    if (b) {
+      db = DevBuf(c, sizeof(float) * O);
+      h2d(c, db.p, b, db.bytes);
+    }
+    k_nct_to_ntc(dx.f(), dxt.f(), B, C, T, C, c->stream);
+    ConvLayer L;
+    L.dil = dilation;
+    L.pad_l = pad_l;
+    L.pad_r = pad_r;
+    L.stride = stride;
+    L.build(c, LayerKind::kConv, dw.f(), db.p ? db.f() : nullptr, O, C, K, true);
+    ConvIO io;
+    io.x = dxt.f(); io.x_ld = C; io.x_bs = (long long)T * C; io.T_in = T;
+    io.y = dy.f(); io.y_ld = O; io.y_bs = (long long)oL * O;
+    io.B = B;
+    L.run(c, io);
+    k_ntc_to_nct(dy.f(), O, dyt.f(), B, O, oL, c->stream);
+    d2h(c, y, dyt.p, dyt.bytes);
+    finish(c);
+  });
+}
+
+int32_t rvc_cuda_conv_transpose1d(int64_t ctx, const float* x, int32_t B, int32_t Ci, int32_t T, const float* w,
+                                  int32_t Co, int32_t K, const float* b, int32_t stride, int32_t padding,
+                                  int32_t output_padding, int32_t dilation, float* y, int32_t oL) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(B >= 0 && Ci > 0 && T >= 0 && Co > 0 && K > 0 && stride > 0 && padding >= 0,
+                  "conv_transpose1d: bad arguments");
+    RVC_CHECK_ARG(dilation == 1 && output_padding == 0,
+                  "conv_transpose1d: only dilation=1, output_padding=0 are supported");
+    RVC_CHECK_ARG(stride <= kMaxSlices, "conv_transpose1d: stride > 16 unsupported");
+    RVC_CHECK_ARG(oL == (T - 1) * stride - 2 * padding + K, "conv_transpose1d: output length mismatch");
+    if (B == 0 || oL <= 0) return;
+    DevBuf dx(c, sizeof(float) * (size_t)B * Ci * T), dxt(c, sizeof(float) * (size_t)B * Ci * T);
+    DevBuf dw(c, sizeof(float) * (size_t)Ci * Co * K), dy(c, sizeof(float) * (size_t)B * Co * oL),
+        dyt(c, sizeof(float) * (size_t)B * Co * oL);
+    DevBuf db;
+    h2d(c, dx.p, x, dx.bytes);
+    h2d(c, dw.p, w, dw.bytes);
+    if (b) {
+      db = DevBuf(c, sizeof(float) * Co);
+      h2d(c, db.p, b, db.bytes);
+    }
+    k_nct_to_ntc(dx.f(), dxt.f(), B, Ci, T, Ci, c->stream);
+    ConvLayer L;
+    L.up = stride;
+    L.up_pad = padding;
+    L.build(c, LayerKind::kConvT, dw.f(), db.p ? db.f() : nullptr, Co, Ci, K, true);
+    ConvIO io;
+    io.x = dxt.f(); io.x_ld = Ci; io.x_bs = (long long)T * Ci; io.T_in = T;
+    io.y = dy.f(); io.y_ld = Co; io.y_bs = (long long)oL * Co;
+    io.B = B;
+    L.run(c, io);
+    k_ntc_to_nct(dy.f(), Co, dyt.f(), B, Co, oL, c->stream);
+    d2h(c, y, dyt.p, dyt.bytes);
+    finish(c);
+  });
+}
+
+int32_t rvc_cuda_matmul(int64_t ctx, const float* a, const float* b, int32_t M, int32_t K, int32_t N, float* cc) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(M >= 0 && K > 0 && N > 0, "matmul: bad shape");
+    if (M == 0) return;
+    DevBuf da(c, sizeof(float) * (size_t)M * K), dw(c, sizeof(float) * (size_t)K * N),
+        dc(c, sizeof(float) * (size_t)M * N);
+    h2d(c, da.p, a, da.bytes);
+    // b[K,N] row-major is exactly the [tap=1][C_in=K][C_out=N] weight layout;
+    // build() expects [O,I,K]: upload as conv weight via an explicit transpose.
+    DevBuf dbt(c, sizeof(float) * (size_t)K * N), dbn(c, sizeof(float) * (size_t)K * N);
+    h2d(c, dbt.p, b, dbt.bytes);
+    k_ntc_to_nct(dbt.f(), N, dbn.f(), 1, N, K, c->stream);  // [K][N] -> [N][K]
+    ConvLayer L;
+    L.build(c, LayerKind::kConv, dbn.f(), nullptr, N, K, 1, true);
+    ConvIO io;
+    io.x = da.f(); io.x_ld = K; io.x_bs = (long long)M * K; io.T_in = M;
+    io.y = dc.f(); io.y_ld = N; io.y_bs = (long long)M * N;
+    io.B = 1;
+    L.run(c, io);
+    d2h(c, cc, dc.p, dc.bytes);
+    finish(c);
+  });
+}
+
+int32_t rvc_cuda_layer_norm(int64_t ctx, const float* x, int64_t rows, int32_t C, const float* gamma,
+                            const float* beta, float eps, float* y) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(rows >= 0 && C > 0 && C <= 1024, "layer_norm: bad shape (C <= 1024)");
+    if (rows == 0) return;
+    DevBuf dx(c, sizeof(float) * (size_t)rows * C), dg(c, sizeof(float) * C), dbb(c, sizeof(float) * C);
+    h2d(c, dx.p, x, dx.bytes);
+    h2d(c, dg.p, gamma, dg.bytes);
+    h2d(c, dbb.p, beta, dbb.bytes);
+    k_layernorm(dx.f(), C, nullptr, 0, rows, C, dg.f(), dbb.f(), eps, dx.f(), C, c->stream);
+    d2h(c, y, dx.p, dx.bytes);
+    finish(c);
+  });
+}
+
+int32_t rvc_cuda_softmax(int64_t ctx, const float* x, int64_t rows, int32_t C, float* y) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(rows >= 0 && C > 0, "softmax: bad shape");
+    if (rows == 0) return;
+    DevBuf dx(c, sizeof(float) * (size_t)rows * C);
+    h2d(c, dx.p, x, dx.bytes);
+    k_softmax_rows(dx.f(), dx.f(), rows, C, c->stream);
+    d2h(c, y, dx.p, dx.bytes);
+    finish(c);
+  });
+}
+
+int32_t rvc_cuda_elementwise(int64_t ctx, int32_t op, const float* a, const float* b, int64_t n, float alpha,
+                             float* y) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(op >= 0 && op <= 6 && n >= 0, "elementwise: bad op or size");
+    RVC_CHECK_ARG(op > 1 || b != nullptr, "elementwise: binary op needs b");
+    if (n == 0) return;
+    DevBuf da(c, sizeof(float) * (size_t)n), dbb;
+    h2d(c, da.p, a, da.bytes);
+    if (op <= 1) {
+      dbb = DevBuf(c, sizeof(float) * (size_t)n);
+      h2d(c, dbb.p, b, dbb.bytes);
+    }
+    k_elementwise(op, da.f(), dbb.p ? dbb.f() : nullptr, n, alpha, da.f(), c->stream);
+    d2h(c, y, da.p, da.bytes);
+    finish(c);
+  });
+}
+
+int32_t rvc_cuda_embedding(int64_t ctx, const int64_t* ids, int64_t n, const float* table, int32_t V, int32_t E,
+                           float* y) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(n >= 0 && V > 0 && E > 0, "embedding: bad shape");
+    for (int64_t i = 0; i < n; ++i)
+      RVC_CHECK_ARG(ids[i] >= -V && ids[i] < V, "embedding: id out of range");
+    if (n == 0) return;
+    DevBuf di(c, sizeof(int64_t) * (size_t)n), dt(c, sizeof(float) * (size_t)V * E), dy(c, sizeof(float) * (size_t)n * E);
+    h2d(c, di.p, ids, di.bytes);
+    h2d(c, dt.p, table, dt.bytes);
+    k_embedding(di.as<long long>(), n, dt.f(), V, E, dy.f(), c->stream);
+    d2h(c, y, dy.p, dy.bytes);
+    finish(c);
+  });
+}
+
+int32_t rvc_cuda_gating(int64_t ctx, const float* x, const float* g, int32_t B, int32_t H, int32_t T, float* y) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(B >= 0 && H > 0 && T >= 0, "gating: bad shape");
+    if (B * T == 0) return;
+    DevBuf dx(c, sizeof(float) * (size_t)B * 2 * H * T), dg, dy(c, sizeof(float) * (size_t)B * H * T);
+    h2d(c, dx.p, x, dx.bytes);
+    if (g) {
+      dg = DevBuf(c, sizeof(float) * (size_t)B * 2 * H);
+      h2d(c, dg.p, g, dg.bytes);
+    }
+    k_gating_nct(dx.f(), dg.p ? dg.f() : nullptr, B, H, T, dy.f(), c->stream);
+    d2h(c, y, dy.p, dy.bytes);
+    finish(c);
+  });
+}
+
+int32_t rvc_cuda_rel_attention(int64_t ctx, const float* q, const float* k, const float* v, const float* emb_k,
+                               const float* emb_v, int32_t B, int32_t heads, int32_t kc, int32_t P, int32_t window,
+                               float* y) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(B >= 0 && heads > 0 && kc > 0 && P >= 0 && window >= 0, "rel_attention: bad shape");
+    if (B * P == 0) return;
+    const int H = heads * kc;
+    const size_t n = (size_t)B * H * P;
+    DevBuf dq(c, sizeof(float) * n), dk(c, sizeof(float) * n), dv(c, sizeof(float) * n);
+    DevBuf qkv(c, sizeof(float) * 3 * n), ek(c, sizeof(float) * (2 * window + 1) * kc),
+        ev(c, sizeof(float) * (2 * window + 1) * kc);
+    DevBuf S(c, sizeof(float) * (size_t)B * heads * P * P), yt(c, sizeof(float) * n), yo(c, sizeof(float) * n);
+    h2d(c, dq.p, q, dq.bytes);
+    h2d(c, dk.p, k, dk.bytes);
+    h2d(c, dv.p, v, dv.bytes);
+    h2d(c, ek.p, emb_k, ek.bytes);
+    h2d(c, ev.p, emb_v, ev.bytes);
+    // pack [B, P, 3H] channels-last
+    for (int bb = 0; bb < B; ++bb) {
+      k_nct_to_ntc(dq.f() + (size_t)bb * H * P, qkv.f() + (size_t)bb * P * 3 * H, 1, H, P, 3 * H, c->stream);
+      k_nct_to_ntc(dk.f() + (size_t)bb * H * P, qkv.f() + (size_t)bb * P * 3 * H + H, 1, H, P, 3 * H, c->stream);
+      k_nct_to_ntc(dv.f() + (size_t)bb * H * P, qkv.f() + (size_t)bb * P * 3 * H + 2 * H, 1, H, P, 3 * H, c->stream);
+    }
+    k_rel_attention(qkv.f(), 3 * H, 0, H, 2 * H, ek.f(), ev.f(), B, heads, kc, P, window, S.f(), yt.f(), H,
+                    c->stream);
+    k_ntc_to_nct(yt.f(), H, yo.f(), B, H, P, c->stream);
+    d2h(c, y, yo.p, yo.bytes);
+    finish(c);
+  });
+}
+
+int32_t rvc_cuda_im2col1d(int64_t ctx, const float* x, int32_t B, int32_t C, int32_t T, int32_t K, int32_t stride,
+                          int32_t pad_l, int32_t dilation, int32_t oL, float* cols) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(B >= 0 && C > 0 && T >= 0 && K > 0 && stride > 0 && dilation > 0 && oL >= 0,
+                  "im2col1d: bad shape");
+    if (B * oL == 0) return;
+    DevBuf dx(c, sizeof(float) * (size_t)B * C * T), dc(c, sizeof(float) * (size_t)B * oL * C * K);
+    h2d(c, dx.p, x, dx.bytes);
+    k_im2col1d(dx.f(), B, C, T, K, stride, pad_l, dilation, oL, dc.f(), c->stream);
+    d2h(c, cols, dc.p, dc.bytes);
+    finish(c);
+  });
+}
+
+// ----------------------------------------------------------------- tier 2
+int32_t rvc_cuda_synth_create(int64_t ctx, const int32_t* cfg, int32_t ncfg, int64_t* model) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(ncfg >= 10, "synth_create: config too short");
+    SynthConfig s;
+    int i = 0;
+    s.sr = cfg[i++]; s.hidden = cfg[i++]; s.filter = cfg[i++]; s.heads = cfg[i++]; s.layers = cfg[i++];
+    s.kc = cfg[i++]; s.window = cfg[i++]; s.gin = cfg[i++]; s.up0 = cfg[i++]; s.n_ups = cfg[i++];
+    RVC_CHECK_ARG(s.n_ups >= 1 && s.n_ups <= 8 && ncfg >= 10 + 2 * s.n_ups + 3, "synth_create: config too short");
+    for (int u = 0; u < s.n_ups; ++u) s.rates.push_back(cfg[i++]);
+    for (int u = 0; u < s.n_ups; ++u) s.kernels.push_back(cfg[i++]);
+    s.phone_dim = cfg[i++]; s.n_spk = cfg[i++]; s.precision = cfg[i++];
+    RVC_CHECK_ARG(s.precision == 0 || s.precision == 1, "synth_create: precision must be 0 or 1");
+    auto m = std::make_unique<SynthModel>(c, s);
+    std::lock_guard<std::mutex> lk(g_reg_mu);
+    *model = g_next++;
+    g_synth[*model] = std::move(m);
+  });
+}
+
+int32_t rvc_cuda_synth_destroy(int64_t model) {
+  return guarded([&] {
+    std::unique_ptr<SynthModel> m;
+    {
+      std::lock_guard<std::mutex> lk(g_reg_mu);
+      auto it = g_synth.find(model);
+      if (it == g_synth.end()) throw Error{kErrState, "invalid synthesizer handle " + std::to_string(model)};
+      m = std::move(it->second);
+      g_synth.erase(it);
+    }
+    std::lock_guard<std::mutex> lk(m->ctx->mu);
+    DeviceGuard dg(m->ctx->device);
+    m.reset();
+  });
+}
+
+int32_t rvc_cuda_synth_set_weight(int64_t model, const char* key, const float* data, const int64_t* shape,
+                                  int32_t ndim) {
+  return on_synth(model, [&](SynthModel* m) {
+    RVC_CHECK_ARG(key && data && ndim >= 0 && ndim <= 8, "synth_set_weight: bad arguments");
+    std::vector<int64_t> s(shape, shape + ndim);
+    m->set_weight(key, data, s);
+  });
+}
+
+int32_t rvc_cuda_synth_finalize(int64_t model) {
+  return on_synth(model, [&](SynthModel* m) {
+    m->finalize();
+    finish(m->ctx);
+  });
+}
+
+int32_t rvc_cuda_synth_infer(int64_t model, int32_t B, int32_t P, const float* phone, const int64_t* pitch,
+                             const float* nsff0, const int64_t* sid, const float* nz, const float* ns, float* wave) {
+  return on_synth(model, [&](SynthModel* m) {
+    RVC_CHECK_ARG(B >= 1 && P >= 1, "synth_infer: B and P must be positive");
+    const int V = 256;
+    for (int64_t i = 0; i < (int64_t)B * P; ++i)
+      RVC_CHECK_ARG(pitch[i] >= -V && pitch[i] < V, "synth_infer: pitch id out of [0,256)");
+    for (int i = 0; i < B; ++i)
+      RVC_CHECK_ARG(sid[i] >= -m->cfg.n_spk && sid[i] < m->cfg.n_spk, "synth_infer: speaker id out of range");
+    m->infer_host(B, P, phone, (const long long*)pitch, nsff0, (const long long*)sid, nz, ns, wave);
+    finish(m->ctx);
+  });
+}
+
+int32_t rvc_cuda_synth_infer_device(int64_t model, int32_t B, int32_t P, const float* phone, const int64_t* pitch,
+                                    const float* nsff0, const int64_t* sid, const float* nz, const float* ns,
+                                    float* wave) {
+  return on_synth(model, [&](SynthModel* m) {
+    m->infer_device(B, P, phone, (const long long*)pitch, nsff0, (const long long*)sid, nz, ns, wave);
+  });
+}
+
+int32_t rvc_cuda_synth_tap(int64_t model, const char* name, float* out, int64_t n) {
+  return on_synth(model, [&](SynthModel* m) {
+    if (!m->tap(name, out, n)) throw Error{kErrArg, std::string("synth_tap: no tap '") + name + "' of that size"};
+  });
+}
+
+int32_t rvc_cuda_synth_keep_taps(int64_t model, int32_t enable) {
+  return on_synth(model, [&](SynthModel* m) { m->keep_taps = enable != 0; });
+}
+
+}  // extern "C"

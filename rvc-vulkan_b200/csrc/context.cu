@@ -1,0 +1,132 @@
+#include "context.cuh"
+
+#include <atomic>
+#include <chrono>
+#include <thread>
+
+namespace rvc {
+
+static thread_local std::string g_last_error;
+static std::atomic<long long> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+long long launch_count() { return g_launches.load(); }
+void set_error(const std::string& msg) { g_last_error = msg; }
+const std::string& get_error() { return g_last_error; }
+
+Context::Context(int dev) : device(dev) {
+  DeviceGuard g(dev);
+  RVC_CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+  RVC_CUDA_TRY(cudaMalloc(&d_err, sizeof(int) * 4));
+  RVC_CUDA_TRY(cudaMemset(d_err, 0, sizeof(int) * 4));
+}
+
+Context::~Context() {
+  DeviceGuard g(device);
+  cudaStreamSynchronize(stream);
+  for (auto& kv : allocs) cudaFree(kv.first);
+  allocs.clear();
+  for (auto& e : prof_ev) {
+    cudaEventDestroy(e.first);
+    cudaEventDestroy(e.second);
+  }
+  for (auto e : ev_pool) cudaEventDestroy(e);
+  if (d_err) cudaFree(d_err);
+  if (stream) cudaStreamDestroy(stream);
+}
+
+void* Context::alloc(size_t bytes) {
+  if (bytes == 0) bytes = 16;
+  if (mem_cap > 0 && mem_used + (int64_t)bytes > mem_cap)
+    throw Error{kErrOom, "device memory cap exceeded: need " + std::to_string(bytes) + " B, used " +
+                             std::to_string(mem_used) + " of " + std::to_string(mem_cap)};
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    throw Error{kErrOom, std::string("cudaMalloc failed: ") + cudaGetErrorString(e)};
+  }
+  // Zero-filled: padding rows of activation buffers must read as zeros.
+  RVC_CUDA_TRY(cudaMemsetAsync(p, 0, bytes, stream));
+  allocs[p] = bytes;
+  mem_used += (int64_t)bytes;
+  return p;
+}
+
+void Context::free(void* p) {
+  auto it = allocs.find(p);
+  if (it == allocs.end()) return;
+  // Work queued on the stream may still read the buffer.
+  cudaStreamSynchronize(stream);
+  cudaFree(p);
+  mem_used -= (int64_t)it->second;
+  allocs.erase(it);
+}
+
+void Context::prof_begin(cudaEvent_t* a, cudaEvent_t* b) {
+  auto get = [&]() {
+    cudaEvent_t e;
+    if (!ev_pool.empty()) {
+      e = ev_pool.back();
+      ev_pool.pop_back();
+    } else {
+      RVC_CUDA_TRY(cudaEventCreate(&e));
+    }
+    return e;
+  };
+  *a = get();
+  *b = get();
+  RVC_CUDA_TRY(cudaEventRecord(*a, stream));
+}
+
+void Context::prof_end(cudaEvent_t a, cudaEvent_t b, double flops) {
+  RVC_CUDA_TRY(cudaEventRecord(b, stream));
+  prof_ev.emplace_back(a, b);
+  prof_launches += 1;
+  prof_flops += flops;
+  if (prof_ev.size() > 4096) prof_collect();
+}
+
+void Context::prof_collect() {
+  RVC_CUDA_TRY(cudaStreamSynchronize(stream));
+  for (auto& e : prof_ev) {
+    float ms = 0.f;
+    RVC_CUDA_TRY(cudaEventElapsedTime(&ms, e.first, e.second));
+    prof_ms += ms;
+    ev_pool.push_back(e.first);
+    ev_pool.push_back(e.second);
+  }
+  prof_ev.clear();
+}
+
+int32_t Context::sync(int timeout_ms) {
+  if (timeout_ms <= 0) timeout_ms = 60000;
+  auto t0 = std::chrono::steady_clock::now();
+  while (true) {
+    cudaError_t e = cudaStreamQuery(stream);
+    if (e == cudaSuccess) break;
+    if (e != cudaErrorNotReady) {
+      set_error(std::string("stream error: ") + cudaGetErrorString(e));
+      return kErrCuda;
+    }
+    auto el = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
+    if (el.count() > timeout_ms) {
+      set_error("rvc_cuda_sync: stream did not drain within " + std::to_string(timeout_ms) + " ms");
+      return kErrTimeout;
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+  int herr[4] = {0, 0, 0, 0};
+  cudaError_t e = cudaMemcpy(herr, d_err, sizeof(herr), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) {
+    set_error(std::string("error-flag read: ") + cudaGetErrorString(e));
+    return kErrCuda;
+  }
+  if (herr[0] != 0) {
+    cudaMemset(d_err, 0, sizeof(int) * 4);
+    set_error("device wait gave up inside a kernel (code " + std::to_string(herr[0]) + ")");
+    return kErrTimeout;
+  }
+  return kOk;
+}
+
+}  // namespace rvc

@@ -1,0 +1,81 @@
+// Per-device context: stream, device error flag, accounted device memory,
+// optional per-launch profiling of the tensor-core convolutions.
+#pragma once
+
+#include "common.cuh"
+
+#include <mutex>
+#include <unordered_map>
+#include <utility>
+#include <vector>
+
+namespace rvc {
+
+struct Context {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  int* d_err = nullptr;
+  std::mutex mu;
+  int64_t mem_cap = 0;   // 0 = unlimited
+  int64_t mem_used = 0;
+  std::unordered_map<void*, size_t> allocs;
+  // profiling of tensor-core conv launches
+  bool prof = false;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> prof_ev;
+  std::vector<cudaEvent_t> ev_pool;
+  int64_t prof_launches = 0;
+  double prof_ms = 0.0, prof_flops = 0.0;
+
+  explicit Context(int dev);
+  ~Context();
+  void* alloc(size_t bytes);  // zero-filled
+  void free(void* p);
+  void prof_begin(cudaEvent_t* a, cudaEvent_t* b);
+  void prof_end(cudaEvent_t a, cudaEvent_t b, double flops);
+  void prof_collect();
+  // Polls the stream (bounded) and the device error flag.
+  int32_t sync(int timeout_ms);
+};
+
+// RAII device buffer owned by a context.
+struct DevBuf {
+  Context* ctx = nullptr;
+  void* p = nullptr;
+  size_t bytes = 0;
+  DevBuf() = default;
+  DevBuf(Context* c, size_t n) : ctx(c), p(c->alloc(n)), bytes(n) {}
+  DevBuf(const DevBuf&) = delete;
+  DevBuf& operator=(const DevBuf&) = delete;
+  DevBuf(DevBuf&& o) noexcept : ctx(o.ctx), p(o.p), bytes(o.bytes) { o.p = nullptr; }
+  DevBuf& operator=(DevBuf&& o) noexcept {
+    if (this != &o) {
+      reset();
+      ctx = o.ctx; p = o.p; bytes = o.bytes; o.p = nullptr;
+    }
+    return *this;
+  }
+  ~DevBuf() { reset(); }
+  void reset() {
+    if (p && ctx) ctx->free(p);
+    p = nullptr;
+    bytes = 0;
+  }
+  template <typename T> T* as() const { return static_cast<T*>(p); }
+  float* f() const { return static_cast<float*>(p); }
+};
+
+// Sets the calling thread's current device for the duration of a call.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+}  // namespace rvc

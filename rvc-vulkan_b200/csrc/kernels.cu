@@ -1,0 +1,583 @@
+// SIMT kernels for the non-GEMM parts of the hot path (see kernels.cuh).
+#include "kernels.cuh"
+
+#include <algorithm>
+#include <cmath>
+
+namespace rvc {
+
+static inline int grid_for(long long n, int block, int cap = 148 * 32) {
+  long long g = (n + block - 1) / block;
+  return (int)std::max<long long>(1, std::min<long long>(g, cap));
+}
+
+#define RVC_LAUNCH_CHECK() \
+  do {                      \
+    note_launch();          \
+    RVC_CUDA_TRY(cudaGetLastError()); \
+  } while (0)
+
+// ------------------------------------------------------------------ layout
+__global__ void nct_to_ntc_kernel(const float* __restrict__ x, float* __restrict__ y, int C, int T, int y_ld) {
+  __shared__ float tile[32][33];
+  const int b = blockIdx.z;
+  const int t0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+  const float* xb = x + (long long)b * C * T;
+  float* yb = y + (long long)b * T * y_ld;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    int c = c0 + i, t = t0 + threadIdx.x;
+    tile[i][threadIdx.x] = (c < C && t < T) ? xb[(long long)c * T + t] : 0.f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    int t = t0 + i, c = c0 + threadIdx.x;
+    if (c < C && t < T) yb[(long long)t * y_ld + c] = tile[threadIdx.x][i];
+  }
+}
+void k_nct_to_ntc(const float* x, float* y, int B, int C, int T, int y_ld, cudaStream_t st) {
+  if (B * C * T == 0) return;
+  dim3 g(cdiv(T, 32), cdiv(C, 32), B);
+  nct_to_ntc_kernel<<<g, dim3(32, 8), 0, st>>>(x, y, C, T, y_ld);
+  RVC_LAUNCH_CHECK();
+}
+
+__global__ void ntc_to_nct_kernel(const float* __restrict__ x, int x_ld, float* __restrict__ y, int C, int T) {
+  __shared__ float tile[32][33];
+  const int b = blockIdx.z;
+  const int t0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+  const float* xb = x + (long long)b * T * x_ld;
+  float* yb = y + (long long)b * C * T;
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    int t = t0 + i, c = c0 + threadIdx.x;
+    tile[i][threadIdx.x] = (c < C && t < T) ? xb[(long long)t * x_ld + c] : 0.f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += 8) {
+    int c = c0 + i, t = t0 + threadIdx.x;
+    if (c < C && t < T) yb[(long long)c * T + t] = tile[threadIdx.x][i];
+  }
+}
+void k_ntc_to_nct(const float* x, int x_ld, float* y, int B, int C, int T, cudaStream_t st) {
+  if (B * C * T == 0) return;
+  dim3 g(cdiv(T, 32), cdiv(C, 32), B);
+  ntc_to_nct_kernel<<<g, dim3(32, 8), 0, st>>>(x, x_ld, y, C, T);
+  RVC_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------ norms
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// One warp per row, two passes over registers (mean, then centred variance),
+// the same two-pass formula as numpy's x.mean()/x.var() (runtime/backend.py:292-296).
+template <int MAXV>
+__global__ void layernorm_kernel(const float* __restrict__ x, int x_ld, const float* __restrict__ res, int res_ld,
+                                 long long rows, int C, const float* __restrict__ gamma,
+                                 const float* __restrict__ beta, float eps, float* __restrict__ y, int y_ld) {
+  const long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  float v[MAXV];
+  const float* xr = x + r * x_ld;
+  const float* rr = res ? res + r * res_ld : nullptr;
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    int c = lane + 32 * i;
+    float a = 0.f;
+    if (c < C) {
+      a = xr[c];
+      if (rr) a = a + rr[c];
+    }
+    v[i] = a;
+    s += a;
+  }
+  const float mean = warp_sum(s) / (float)C;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    int c = lane + 32 * i;
+    if (c < C) {
+      float d = v[i] - mean;
+      q += d * d;
+    }
+  }
+  const float var = warp_sum(q) / (float)C;
+  const float den = sqrtf(var + eps);
+  float* yr = y + r * y_ld;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    int c = lane + 32 * i;
+    if (c < C) yr[c] = (v[i] - mean) / den * gamma[c] + beta[c];
+  }
+}
+void k_layernorm(const float* x, int x_ld, const float* res, int res_ld, long long rows, int C, const float* gamma,
+                 const float* beta, float eps, float* y, int y_ld, cudaStream_t st) {
+  if (rows == 0) return;
+  RVC_CHECK_ARG(C <= 1024, "layer_norm: C > 1024 unsupported");
+  int grid = (int)((rows + 7) / 8);
+  if (C <= 256)
+    layernorm_kernel<8><<<grid, 256, 0, st>>>(x, x_ld, res, res_ld, rows, C, gamma, beta, eps, y, y_ld);
+  else
+    layernorm_kernel<32><<<grid, 256, 0, st>>>(x, x_ld, res, res_ld, rows, C, gamma, beta, eps, y, y_ld);
+  RVC_LAUNCH_CHECK();
+}
+
+// exp(x - max) / sum, one warp per row (runtime/backend.py:298-306).
+__global__ void softmax_kernel(const float* __restrict__ x, float* __restrict__ y, long long rows, int C) {
+  const long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const float* xr = x + r * C;
+  float* yr = y + r * C;
+  float m = -INFINITY;
+  for (int c = lane; c < C; c += 32) m = fmaxf(m, xr[c]);
+  m = warp_max(m);
+  float s = 0.f;
+  for (int c = lane; c < C; c += 32) {
+    float e = expf(xr[c] - m);
+    yr[c] = e;
+    s += e;
+  }
+  s = warp_sum(s);
+  for (int c = lane; c < C; c += 32) yr[c] = yr[c] / s;
+}
+void k_softmax_rows(const float* x, float* y, long long rows, int C, cudaStream_t st) {
+  if (rows == 0) return;
+  softmax_kernel<<<(int)((rows + 7) / 8), 256, 0, st>>>(x, y, rows, C);
+  RVC_LAUNCH_CHECK();
+}
+
+__device__ __forceinline__ float sigmoid_np(float x) {
+  // two-sided form of runtime/nn.py:520-523
+  if (x >= 0.f) return 1.f / (1.f + expf(-x));
+  float e = expf(x);
+  return e / (1.f + e);
+}
+
+__global__ void elementwise_kernel(int op, const float* __restrict__ a, const float* __restrict__ b, long long n,
+                                   float alpha, float* __restrict__ y) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    float v = a[i], r;
+    switch (op) {
+      case 0: r = v + b[i]; break;
+      case 1: r = v * b[i]; break;
+      case 2: r = v > 0.f ? v : 0.f; break;
+      case 3: r = v >= 0.f ? v : alpha * v; break;
+      case 4: r = 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); break;
+      case 5: r = tanhf(v); break;
+      default: r = sigmoid_np(v); break;
+    }
+    y[i] = r;
+  }
+}
+void k_elementwise(int op, const float* a, const float* b, long long n, float alpha, float* y, cudaStream_t st) {
+  if (n == 0) return;
+  elementwise_kernel<<<grid_for(n, 256), 256, 0, st>>>(op, a, b, n, alpha, y);
+  RVC_LAUNCH_CHECK();
+}
+
+__global__ void embedding_kernel(const long long* __restrict__ ids, long long n, const float* __restrict__ table,
+                                 int V, int E, float* __restrict__ y) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n * E; i += (long long)gridDim.x * blockDim.x) {
+    long long r = i / E;
+    int c = (int)(i % E);
+    long long id = ids[r];
+    if (id < 0) id += V;
+    y[i] = table[id * E + c];
+  }
+}
+void k_embedding(const long long* ids, long long n, const float* table, int V, int E, float* y, cudaStream_t st) {
+  if (n == 0) return;
+  embedding_kernel<<<grid_for(n * E, 256), 256, 0, st>>>(ids, n, table, V, E, y);
+  RVC_LAUNCH_CHECK();
+}
+
+__global__ void gating_nct_kernel(const float* __restrict__ x, const float* __restrict__ g, int B, int H, int T,
+                                  float* __restrict__ y) {
+  long long n = (long long)B * H * T;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    int t = (int)(i % T);
+    long long r = i / T;
+    int c = (int)(r % H);
+    int b = (int)(r / H);
+    const float* xb = x + (long long)b * 2 * H * T;
+    float a = xb[(long long)c * T + t], s = xb[(long long)(H + c) * T + t];
+    if (g) {
+      a = a + g[(long long)b * 2 * H + c];
+      s = s + g[(long long)b * 2 * H + H + c];
+    }
+    y[i] = tanhf(a) * sigmoid_np(s);
+  }
+}
+void k_gating_nct(const float* x, const float* g, int B, int H, int T, float* y, cudaStream_t st) {
+  long long n = (long long)B * H * T;
+  if (n == 0) return;
+  gating_nct_kernel<<<grid_for(n, 256), 256, 0, st>>>(x, g, B, H, T, y);
+  RVC_LAUNCH_CHECK();
+}
+
+__global__ void im2col1d_kernel(const float* __restrict__ x, int B, int C, int T, int K, int stride, int pad_l,
+                                int dil, int oL, float* __restrict__ cols) {
+  long long n = (long long)B * oL * C * K;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    int k = (int)(i % K);
+    long long r = i / K;
+    int c = (int)(r % C);
+    r /= C;
+    int t = (int)(r % oL);
+    int b = (int)(r / oL);
+    int src = t * stride + k * dil - pad_l;
+    cols[i] = (src >= 0 && src < T) ? x[((long long)b * C + c) * T + src] : 0.f;
+  }
+}
+void k_im2col1d(const float* x, int B, int C, int T, int K, int stride, int pad_l, int dil, int oL, float* cols,
+                cudaStream_t st) {
+  long long n = (long long)B * oL * C * K;
+  if (n == 0) return;
+  im2col1d_kernel<<<grid_for(n, 256), 256, 0, st>>>(x, B, C, T, K, stride, pad_l, dil, oL, cols);
+  RVC_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------ weight prep
+__global__ void fold_wn_kernel(const float* __restrict__ v, const float* __restrict__ g, float* __restrict__ out,
+                               int inner) {
+  const int r = blockIdx.x;
+  const float* vr = v + (long long)r * inner;
+  float s = 0.f;
+  for (int i = threadIdx.x; i < inner; i += blockDim.x) s += vr[i] * vr[i];
+  __shared__ float red[32];
+  s = warp_sum(s);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float norm = fmaxf(sqrtf(red[0]), 1e-12f);
+  const float sc = g[r] / norm;   // w_g / ||w_v|| first, then times w_v (vits.py:440-441)
+  for (int i = threadIdx.x; i < inner; i += blockDim.x) out[(long long)r * inner + i] = vr[i] * sc;
+}
+void k_fold_weight_norm(const float* v, const float* g, float* out, int rows, int inner, cudaStream_t st) {
+  if (rows == 0) return;
+  fold_wn_kernel<<<rows, 256, 0, st>>>(v, g, out, inner);
+  RVC_LAUNCH_CHECK();
+}
+
+__global__ void gather_taps_kernel(const float* __restrict__ W, float* __restrict__ Wg, int O, int I, int K,
+                                   int layout, const int* __restrict__ tap_k, int ntaps) {
+  long long n = (long long)ntaps * I * O;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    int o = (int)(i % O);
+    long long r = i / O;
+    int ci = (int)(r % I);
+    int j = (int)(r / I);
+    int k = tap_k[j];
+    Wg[i] = layout == 0 ? W[((long long)o * I + ci) * K + k] : W[((long long)ci * O + o) * K + k];
+  }
+}
+void k_gather_taps(const float* W, float* Wg, int O, int I, int K, int layout, const int* tap_k_dev, int ntaps,
+                   cudaStream_t st) {
+  long long n = (long long)ntaps * I * O;
+  if (n == 0) return;
+  gather_taps_kernel<<<grid_for(n, 256), 256, 0, st>>>(W, Wg, O, I, K, layout, tap_k_dev, ntaps);
+  RVC_LAUNCH_CHECK();
+}
+
+__global__ void gemv_rows_kernel(const float* __restrict__ W, const float* __restrict__ bias,
+                                 const float* __restrict__ x, int B, int O, int I, float* __restrict__ y) {
+  long long n = (long long)B * O;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    int o = (int)(i % O), b = (int)(i / O);
+    float s = 0.f;
+    for (int k = 0; k < I; ++k) s = fmaf(W[(long long)o * I + k], x[(long long)b * I + k], s);
+    y[i] = s + (bias ? bias[o] : 0.f);
+  }
+}
+void k_gemv_rows(const float* W, const float* bias, const float* x, int B, int O, int I, float* y, cudaStream_t st) {
+  if (B * O == 0) return;
+  gemv_rows_kernel<<<grid_for((long long)B * O, 128), 128, 0, st>>>(W, bias, x, B, O, I, y);
+  RVC_LAUNCH_CHECK();
+}
+
+// --------------------------------------------------------- synthesizer
+__global__ void enc_embed_finish_kernel(float* __restrict__ lin, const long long* __restrict__ pitch,
+                                        const float* __restrict__ E, long long rows, int H, float scale) {
+  long long n = rows * H;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    long long r = i / H;
+    int c = (int)(i % H);
+    long long p = pitch[r];
+    if (p < 0) p += 256;
+    float v = (lin[i] + E[p * H + c]) * scale;
+    lin[i] = v >= 0.f ? v : 0.1f * v;
+  }
+}
+void k_enc_embed_finish(float* lin, const long long* pitch, const float* E, long long rows, int H, float scale,
+                        cudaStream_t st) {
+  if (rows == 0) return;
+  enc_embed_finish_kernel<<<grid_for(rows * H, 256), 256, 0, st>>>(lin, pitch, E, rows, H, scale);
+  RVC_LAUNCH_CHECK();
+}
+
+// Relative attention, pass 1: S[b,h,i,j] = qs_i.k_j + (|j-i|<=W ? qs_i.ek[j-i+W] : 0),
+// qs = q / sqrt(kc)   (runtime/models/vits.py:998-1005).
+constexpr int kAttT = 32;
+__global__ void rel_scores_kernel(const float* __restrict__ qkv, int ld, int q_off, int k_off,
+                                  const float* __restrict__ emb_k, int heads, int kc, int P, int window,
+                                  float inv_div, float* __restrict__ S) {
+  extern __shared__ float sm[];
+  float* qs = sm;                    // [32][kc+1]
+  float* ks = sm + kAttT * (kc + 1);  // [32][kc+1]
+  const int bh = blockIdx.z;
+  const int b = bh / heads, h = bh % heads;
+  const int i0 = blockIdx.y * kAttT, j0 = blockIdx.x * kAttT;
+  const float* base = qkv + (long long)b * P * ld;
+  for (int e = threadIdx.x; e < kAttT * kc; e += blockDim.x) {
+    int r = e / kc, d = e % kc;
+    int i = i0 + r, j = j0 + r;
+    qs[r * (kc + 1) + d] = i < P ? base[(long long)i * ld + q_off + h * kc + d] / inv_div : 0.f;
+    ks[r * (kc + 1) + d] = j < P ? base[(long long)j * ld + k_off + h * kc + d] : 0.f;
+  }
+  __syncthreads();
+  const int tj = threadIdx.x & 31, ti0 = (threadIdx.x >> 5) * 4;
+  for (int u = 0; u < 4; ++u) {
+    int ri = ti0 + u;
+    int i = i0 + ri, j = j0 + tj;
+    if (i >= P || j >= P) continue;
+    float s = 0.f;
+    for (int d = 0; d < kc; ++d) s = fmaf(qs[ri * (kc + 1) + d], ks[tj * (kc + 1) + d], s);
+    int rel = j - i;
+    if (rel >= -window && rel <= window) {
+      const float* e = emb_k + (long long)(h * 0 + rel + window) * kc;  // emb_rel shared by heads
+      float r2 = 0.f;
+      for (int d = 0; d < kc; ++d) r2 = fmaf(qs[ri * (kc + 1) + d], e[d], r2);
+      s = s + r2;
+    }
+    S[((long long)bh * P + i) * P + j] = s;
+  }
+}
+
+// Pass 3: y[b,i,h*kc+d] = sum_j p[i,j] v_j[d] + sum_{|j-i|<=W} p[i,j] ev[j-i+W][d]
+__global__ void rel_pv_kernel(const float* __restrict__ Pm, const float* __restrict__ qkv, int ld, int v_off,
+                              const float* __restrict__ emb_v, int heads, int kc, int P, int window,
+                              float* __restrict__ y, int y_ld) {
+  extern __shared__ float sm[];
+  float* ps = sm;                          // [32][33]
+  float* vs = sm + kAttT * (kAttT + 1);    // [32][kc]
+  const int bh = blockIdx.z;
+  const int b = bh / heads, h = bh % heads;
+  const int i0 = blockIdx.x * kAttT;
+  const float* vb = qkv + (long long)b * P * ld + v_off + h * kc;
+  const float* prow = Pm + (long long)bh * P * P;
+  // each thread: row i = i0 + threadIdx.x / 8 ... use (32 rows) x (kc cols) outputs over 256 threads
+  const int nout = kAttT * kc;
+  float acc[12];
+  for (int u = 0; u < 12; ++u) acc[u] = 0.f;
+  for (int j0 = 0; j0 < P; j0 += kAttT) {
+    for (int e = threadIdx.x; e < kAttT * kAttT; e += blockDim.x) {
+      int r = e / kAttT, c = e % kAttT;
+      int i = i0 + r, j = j0 + c;
+      ps[r * (kAttT + 1) + c] = (i < P && j < P) ? prow[(long long)i * P + j] : 0.f;
+    }
+    for (int e = threadIdx.x; e < kAttT * kc; e += blockDim.x) {
+      int r = e / kc, d = e % kc;
+      int j = j0 + r;
+      vs[r * kc + d] = j < P ? vb[(long long)j * ld + d] : 0.f;
+    }
+    __syncthreads();
+    for (int u = 0; u < 12; ++u) {
+      int o = threadIdx.x + u * blockDim.x;
+      if (o >= nout) break;
+      int r = o / kc, d = o % kc;
+      float s = acc[u];
+      for (int c = 0; c < kAttT; ++c) s = fmaf(ps[r * (kAttT + 1) + c], vs[c * kc + d], s);
+      acc[u] = s;
+    }
+    __syncthreads();
+  }
+  for (int u = 0; u < 12; ++u) {
+    int o = threadIdx.x + u * blockDim.x;
+    if (o >= nout) break;
+    int r = o / kc, d = o % kc;
+    int i = i0 + r;
+    if (i >= P) continue;
+    float rel = 0.f;
+    for (int rr = -window; rr <= window; ++rr) {
+      int j = i + rr;
+      if (j < 0 || j >= P) continue;
+      rel = fmaf(prow[(long long)i * P + j], emb_v[(long long)(rr + window) * kc + d], rel);
+    }
+    y[((long long)b * P + i) * y_ld + h * kc + d] = acc[u] + rel;
+  }
+}
+
+void k_rel_attention(const float* qkv, int qkv_ld, int q_off, int k_off, int v_off, const float* emb_k,
+                     const float* emb_v, int B, int heads, int kc, int P, int window, float* scratch, float* y,
+                     int y_ld, cudaStream_t st) {
+  if (B * P == 0) return;
+  RVC_CHECK_ARG(kc <= 128 && kAttT * kc <= 12 * 256, "rel_attention: head dim too large");
+  const float div = (float)std::sqrt((double)kc);
+  dim3 g1(cdiv(P, kAttT), cdiv(P, kAttT), B * heads);
+  size_t sm1 = 2 * kAttT * (kc + 1) * sizeof(float);
+  rel_scores_kernel<<<g1, 256, sm1, st>>>(qkv, qkv_ld, q_off, k_off, emb_k, heads, kc, P, window, div, scratch);
+  RVC_LAUNCH_CHECK();
+  k_softmax_rows(scratch, scratch, (long long)B * heads * P, P, st);
+  dim3 g3(cdiv(P, kAttT), 1, B * heads);
+  size_t sm3 = (kAttT * (kAttT + 1) + kAttT * kc) * sizeof(float);
+  rel_pv_kernel<<<g3, 256, sm3, st>>>(scratch, qkv, qkv_ld, v_off, emb_v, heads, kc, P, window, y, y_ld);
+  RVC_LAUNCH_CHECK();
+}
+
+__global__ void zp_kernel(const float* __restrict__ stats, const float* __restrict__ nz, int P, int H,
+                          float* __restrict__ z, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    int c = (int)(i % H);
+    long long r = i / H;
+    int t = (int)(r % P);
+    int b = (int)(r / P);
+    const float* s = stats + r * 2 * H;
+    float nzv = nz[((long long)b * H + c) * P + t];
+    z[i] = s[c] + expf(s[H + c]) * nzv * 0.66666f;
+  }
+}
+void k_zp(const float* stats, const float* nz, int B, int P, int H, float* z, cudaStream_t st) {
+  long long n = (long long)B * P * H;
+  if (n == 0) return;
+  zp_kernel<<<grid_for(n, 256), 256, 0, st>>>(stats, nz, P, H, z, n);
+  RVC_LAUNCH_CHECK();
+}
+
+__global__ void flip_kernel(const float* __restrict__ x, float* __restrict__ y, long long n, int C) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    long long r = i / C;
+    int c = (int)(i % C);
+    y[i] = x[r * C + (C - 1 - c)];
+  }
+}
+void k_flip_channels(const float* x, float* y, long long rows, int C, cudaStream_t st) {
+  if (rows == 0) return;
+  flip_kernel<<<grid_for(rows * C, 256), 256, 0, st>>>(x, y, rows * C, C);
+  RVC_LAUNCH_CHECK();
+}
+
+__global__ void gate_rows_kernel(const float* __restrict__ xin, long long n, int H, float* __restrict__ acts) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    long long r = i / H;
+    int c = (int)(i % H);
+    const float* xr = xin + r * 2 * H;
+    acts[i] = tanhf(xr[c]) * sigmoid_np(xr[H + c]);
+  }
+}
+void k_gate_rows(const float* xin, long long rows, int H, float* acts, cudaStream_t st) {
+  if (rows == 0) return;
+  gate_rows_kernel<<<grid_for(rows * H, 256), 256, 0, st>>>(xin, rows * H, H, acts);
+  RVC_LAUNCH_CHECK();
+}
+
+__global__ void wn_update_kernel(float* __restrict__ h, float* __restrict__ skip, const float* __restrict__ rs,
+                                 long long n, int H, int first, int last) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    long long r = i / H;
+    int c = (int)(i % H);
+    if (last) {
+      skip[i] = skip[i] + rs[r * H + c];
+    } else {
+      const float* rr = rs + r * 2 * H;
+      h[i] = h[i] + rr[c];
+      skip[i] = (first ? 0.f : skip[i]) + rr[H + c];
+    }
+  }
+}
+void k_wn_update(float* h, float* skip, const float* rs, long long rows, int H, int first, int last,
+                 cudaStream_t st) {
+  if (rows == 0) return;
+  wn_update_kernel<<<grid_for(rows * H, 256), 256, 0, st>>>(h, skip, rs, rows * H, H, first, last);
+  RVC_LAUNCH_CHECK();
+}
+
+// NSF source (runtime/models/vits.py:1468-1501).  Phase carry: a float32
+// running sum over frames of fmod(rad_last + 0.5, 1) - 0.5, then fmod(., 1),
+// sequential like numpy's cumsum.
+__global__ void sine_phase_kernel(const float* __restrict__ f0, int B, int P, int upp, float srf,
+                                  float* __restrict__ phase) {
+  int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  float acc = 0.f;
+  const float last = (float)upp;
+  for (int t = 0; t < P; ++t) {
+    float rl = (f0[(long long)b * P + t] / srf) * last;
+    float r2 = fmodf(rl + 0.5f, 1.0f) - 0.5f;
+    acc = acc + r2;
+    phase[(long long)b * P + t] = fmodf(acc, 1.0f);
+  }
+}
+__global__ void sine_source_kernel(const float* __restrict__ f0, const float* __restrict__ ns,
+                                   const float* __restrict__ phase, int B, int P, int upp, float srf, float lw,
+                                   float lb, float* __restrict__ har) {
+  const long long N = (long long)P * upp;
+  const long long n = (long long)B * N;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int b = (int)(i / N);
+    const long long s = i % N;
+    const int t = (int)(s / upp), j = (int)(s % upp);
+    const float f = f0[(long long)b * P + t];
+    float rad = (f / srf) * (float)(j + 1);
+    if (t > 0) rad = rad + phase[(long long)b * P + t - 1];
+    float sine = sinf(6.2831855f * rad) * 0.1f;
+    const float uv = f > 0.f ? 1.f : 0.f;
+    const float amp = uv * 0.003f + ((1.f - uv) * 0.1f) / 3.f;
+    sine = sine * uv + amp * ns[i];
+    har[i] = tanhf(sine * lw + lb);
+  }
+}
+void k_sine_source(const float* f0, const float* ns, int B, int P, int upp, int sr, float lin_w, float lin_b,
+                   float* phase_scratch, float* har, cudaStream_t st) {
+  if (B * P == 0) return;
+  sine_phase_kernel<<<cdiv(B, 32), 32, 0, st>>>(f0, B, P, upp, (float)sr, phase_scratch);
+  RVC_LAUNCH_CHECK();
+  long long n = (long long)B * P * upp;
+  sine_source_kernel<<<grid_for(n, 256), 256, 0, st>>>(f0, ns, phase_scratch, B, P, upp, (float)sr, lin_w, lin_b,
+                                                       har);
+  RVC_LAUNCH_CHECK();
+}
+
+__global__ void conv_post_kernel(const float* __restrict__ x, long long x_bs, int B, int T, int C, const float* __restrict__ w,
+                                 int K, int pad, float slope, float* __restrict__ y) {
+  const long long n = (long long)B * T;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int b = (int)(i / T), t = (int)(i % T);
+    const float* xb = x + (long long)b * x_bs;
+    float s = 0.f;
+    for (int k = 0; k < K; ++k) {
+      int r = t + k - pad;
+      if (r < 0 || r >= T) continue;
+      const float* xr = xb + (long long)r * C;
+      for (int c = 0; c < C; ++c) {
+        float v = xr[c];
+        v = v >= 0.f ? v : slope * v;
+        s = fmaf(v, w[c * K + k], s);
+      }
+    }
+    y[i] = tanhf(s);
+  }
+}
+void k_conv_post_tanh(const float* x, long long x_bs, int B, int T, int C, const float* w, int K, int pad,
+                      float slope, float* y, cudaStream_t st) {
+  long long n = (long long)B * T;
+  if (n == 0) return;
+  conv_post_kernel<<<grid_for(n, 128, 148 * 64), 128, 0, st>>>(x, x_bs, B, T, C, w, K, pad, slope, y);
+  RVC_LAUNCH_CHECK();
+}
+
+}  // namespace rvc

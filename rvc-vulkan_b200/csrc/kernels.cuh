@@ -1,0 +1,58 @@
+// SIMT kernels for the non-GEMM parts of the hot path (norms, attention,
+// gates, the NSF source, weight preparation).  Host launchers; all run on the
+// given stream.  Activations are channels-last [B][T][C] unless noted.
+#pragma once
+
+#include "common.cuh"
+
+namespace rvc {
+
+// ---- layout
+void k_nct_to_ntc(const float* x, float* y, int B, int C, int T, int y_ld, cudaStream_t st);
+void k_ntc_to_nct(const float* x, int x_ld, float* y, int B, int C, int T, cudaStream_t st);
+
+// ---- norms / softmax / elementwise
+// y[r] = LN(x[r] (+ res[r])) ; rows of C with lds.
+void k_layernorm(const float* x, int x_ld, const float* res, int res_ld, long long rows, int C,
+                 const float* gamma, const float* beta, float eps, float* y, int y_ld, cudaStream_t st);
+void k_softmax_rows(const float* x, float* y, long long rows, int C, cudaStream_t st);
+void k_elementwise(int op, const float* a, const float* b, long long n, float alpha, float* y, cudaStream_t st);
+void k_embedding(const long long* ids, long long n, const float* table, int V, int E, float* y, cudaStream_t st);
+void k_gating_nct(const float* x, const float* g, int B, int H, int T, float* y, cudaStream_t st);
+void k_im2col1d(const float* x, int B, int C, int T, int K, int stride, int pad_l, int dil, int oL, float* cols,
+                cudaStream_t st);
+
+// ---- weight preparation
+// out[r, :] = v[r, :] * (g[r] / max(||v[r, :]||, 1e-12)), rows of `inner` (weight_norm dim 0).
+void k_fold_weight_norm(const float* v, const float* g, float* out, int rows, int inner, cudaStream_t st);
+// Wg[j][i][o] = layout==0 ? W[o][i][tap_k[j]] : W[i][o][tap_k[j]]   (conv [O,I,K] / convT [I,O,K])
+void k_gather_taps(const float* W, float* Wg, int O, int I, int K, int layout, const int* tap_k_dev, int ntaps,
+                   cudaStream_t st);
+// y[b][o] = sum_i W[o][i] x[b][i] + bias[o]  (1x1 conv on one frame)
+void k_gemv_rows(const float* W, const float* bias, const float* x, int B, int O, int I, float* y,
+                 cudaStream_t st);
+
+// ---- synthesizer pieces
+// x = leaky(((lin + E[pitch]) * scale), 0.1), in place on lin [B*P, H]
+void k_enc_embed_finish(float* lin, const long long* pitch, const float* E, long long rows, int H, float scale,
+                        cudaStream_t st);
+// T5 relative attention, head-interleaved channels-last qkv [B,P,3*H*kc] -> y [B,P,H*kc]
+void k_rel_attention(const float* qkv, int qkv_ld, int q_off, int k_off, int v_off, const float* emb_k,
+                     const float* emb_v, int B, int heads, int kc, int P, int window, float* scratch, float* y,
+                     int y_ld, cudaStream_t st);
+// z[b,t,c] = m + exp(logs) * nz[b,c,t] * 0.66666   (stats [B,P,2H])
+void k_zp(const float* stats, const float* nz, int B, int P, int H, float* z, cudaStream_t st);
+void k_flip_channels(const float* x, float* y, long long rows, int C, cudaStream_t st);
+// acts = tanh(xin[:, :H]) * sigmoid(xin[:, H:])   (g already added by the conv epilogue)
+void k_gate_rows(const float* xin, long long rows, int H, float* acts, cudaStream_t st);
+// i<last: h += rs[:, :H]; skip = (first ? 0 : skip) + rs[:, H:] ; last: skip += rs
+void k_wn_update(float* h, float* skip, const float* rs, long long rows, int H, int first, int last,
+                 cudaStream_t st);
+// NSF sine source: har[b, n], n < P*upp
+void k_sine_source(const float* f0, const float* ns, int B, int P, int upp, int sr, float lin_w, float lin_b,
+                   float* phase_scratch, float* har, cudaStream_t st);
+// y[b,t] = tanh(sum_k sum_c leaky(x[b,t+k-pad,c],slope) * w[c][k])   (conv_post, C_out = 1, no bias)
+void k_conv_post_tanh(const float* x, long long x_bs, int B, int T, int C, const float* w, int K, int pad, float slope,
+                      float* y, cudaStream_t st);
+
+}  // namespace rvc

@@ -1,0 +1,127 @@
+#include "layer.cuh"
+
+#include <algorithm>
+
+namespace rvc {
+
+void ConvLayer::build(Context* ctx, LayerKind k, const float* W, const float* b, int O, int I, int Kk,
+                      bool use_tc) {
+  kind = k;
+  K = Kk;
+  cudaStream_t st = ctx->stream;
+  std::vector<int> tap_k;
+  slices.clear();
+  if (k == LayerKind::kConv) {
+    C_in = I;
+    C_out = O;
+    for (int j = 0; j < K; ++j) tap_k.push_back(j);
+    ConvSlice s{};
+    s.ntaps = K;
+    s.tap_base = -pad_l;
+    s.tap_step = dil;
+    s.out_r0 = 0;
+    s.ci_off = 0;
+    s.co_off = 0;
+    s.wtap0 = 0;
+    slices.push_back(s);
+  } else {
+    // Transposed conv as `up` phase GEMMs: output row q*up + p takes taps
+    // k = k0 + j*up with k0 = (p + pad) mod up, reading input row
+    // q + (p + pad - k0)/up - j  (runtime/nn.py:294-346 scatter, gathered).
+    C_in = I;
+    C_out = O;
+    RVC_CHECK_ARG(up >= 1 && up <= kMaxSlices, "conv_transpose1d: stride must be in [1,16]");
+    for (int p = 0; p < up; ++p) {
+      int k0 = (p + up_pad) % up;
+      ConvSlice s{};
+      s.wtap0 = (int)tap_k.size();
+      int n = 0;
+      for (int kk = k0; kk < K; kk += up) {
+        tap_k.push_back(kk);
+        ++n;
+      }
+      s.ntaps = n;
+      s.tap_base = (p + up_pad - k0) / up;
+      s.tap_step = -1;
+      s.out_r0 = p;
+      s.ci_off = 0;
+      s.co_off = 0;
+      slices.push_back(s);
+    }
+  }
+  taps_total = (int)tap_k.size();
+  DevBuf taps(ctx, sizeof(int) * std::max(1, taps_total));
+  RVC_CUDA_TRY(cudaMemcpyAsync(taps.p, tap_k.data(), sizeof(int) * taps_total, cudaMemcpyHostToDevice, st));
+  Wg = DevBuf(ctx, sizeof(float) * (size_t)std::max(1, taps_total) * C_in * C_out);
+  k_gather_taps(W, Wg.f(), O, I, K, k == LayerKind::kConv ? 0 : 1, taps.as<int>(), taps_total, st);
+  if (b) {
+    bias = DevBuf(ctx, sizeof(float) * C_out);
+    RVC_CUDA_TRY(cudaMemcpyAsync(bias.p, b, sizeof(float) * C_out, cudaMemcpyDeviceToDevice, st));
+  }
+  tc = use_tc && tc_shape_ok(C_in, C_out) && stride == 1;
+  if (tc) {
+    bn = tc_pick_bn(C_out);
+    cb = tc_pick_cb(C_in);
+    wpk = DevBuf(ctx, sizeof(uint16_t) * tc_packed_elems(taps_total, C_in, C_out, bn, cb));
+    launch_tc_pack(Wg.f(), wpk.as<uint16_t>(), taps_total, C_in, C_out, bn, cb, st);
+  }
+  RVC_CUDA_TRY(cudaStreamSynchronize(st));  // `taps` is freed on return
+}
+
+int ConvLayer::out_len(int T_in) const {
+  if (kind == LayerKind::kConv) return (T_in + pad_l + pad_r - dil * (K - 1) - 1) / stride + 1;
+  return (T_in - 1) * up - 2 * up_pad + (K - 1) + 1;
+}
+
+double ConvLayer::flops(int B, int T_in) const {
+  return 2.0 * B * (double)out_len(T_in) * C_in * C_out * (kind == LayerKind::kConv ? K : (double)K / up);
+}
+
+void ConvLayer::run(Context* ctx, const ConvIO& io, bool force_simt) const {
+  ConvArgs a{};
+  a.x = io.x; a.x_bs = io.x_bs; a.x_ld = io.x_ld; a.T_in = io.T_in; a.C_in = C_in;
+  a.in_act = io.in_act; a.in_slope = io.in_slope;
+  a.stride = stride;
+  a.out_rs = kind == LayerKind::kConv ? 1 : up;
+  a.C_out = C_out;
+  a.B = io.B;
+  const int oL = out_len(io.T_in);
+  RVC_CHECK_ARG(oL >= 0, "conv: negative output length");
+  a.nslices = (int)slices.size();
+  for (int s = 0; s < a.nslices; ++s) {
+    a.sl[s] = slices[s];
+    if (kind == LayerKind::kConv) {
+      a.sl[s].rows = oL;
+    } else {
+      const int p = slices[s].out_r0;
+      a.sl[s].rows = oL > p ? cdiv(oL - p, up) : 0;
+    }
+  }
+  a.w = Wg.f();
+  a.wpk = wpk.as<uint16_t>();
+  a.bn = bn; a.cb = cb;
+  a.bias = bias.p ? bias.f() : nullptr;
+  a.bias2 = io.bias2; a.bias2_bs = io.bias2_bs;
+  a.res = io.res; a.res_bs = io.res_bs; a.res_ld = io.res_ld; a.res_sub = io.res_sub;
+  a.accin = io.accin; a.acc_bs = io.acc_bs; a.acc_ld = io.acc_ld;
+  a.out_div = io.out_div;
+  a.out_act = io.out_act; a.out_slope = io.out_slope;
+  a.y = io.y; a.y_bs = io.y_bs; a.y_ld = io.y_ld; a.y_raw = io.y_raw;
+  a.har = io.har; a.har_bs = io.har_bs; a.har_len = io.har_len;
+  a.wn = io.wn; a.bn_ = io.bn; a.nk = io.nk; a.nstr = io.nstr; a.npad = io.npad;
+  a.err = ctx->d_err;
+  if (oL == 0 || io.B == 0) return;
+  bool any_empty = false;  // a transposed-conv phase with no taps: output = epilogue(0)
+  for (int s = 0; s < a.nslices; ++s) any_empty |= a.sl[s].ntaps == 0;
+  const bool use_tc = tc && !force_simt && !any_empty && (io.x_ld % 4 == 0) && (io.x_bs % 4 == 0);
+  if (use_tc) {
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (ctx->prof) ctx->prof_begin(&e0, &e1);
+    launch_tc_conv(a, ctx->stream);
+    if (ctx->prof) ctx->prof_end(e0, e1, flops(io.B, io.T_in));
+  } else {
+    launch_simt_conv(a, ctx->stream);
+  }
+}
+
+}  // namespace rvc

@@ -1,0 +1,52 @@
+// ConvLayer: device-resident weights of one GEMM-shaped op in both operand
+// forms (fp32 [taps][C_in][C_out] and the packed bf16 hi/lo tensor-core form),
+// plus the slice geometry; run() binds activations and an epilogue.
+#pragma once
+
+#include "context.cuh"
+#include "conv.cuh"
+#include "kernels.cuh"
+
+#include <string>
+#include <vector>
+
+namespace rvc {
+
+// Epilogue/IO binding for one launch (everything ConvArgs needs besides weights).
+struct ConvIO {
+  const float* x = nullptr; long long x_bs = 0; int x_ld = 0; int T_in = 0;
+  int in_act = kActNone; float in_slope = 0.f;
+  float* y = nullptr; long long y_bs = 0; int y_ld = 0;
+  float* y_raw = nullptr;
+  const float* bias2 = nullptr; long long bias2_bs = 0;
+  const float* res = nullptr; long long res_bs = 0; int res_ld = 0; int res_sub = 0;
+  const float* accin = nullptr; long long acc_bs = 0; int acc_ld = 0;
+  float out_div = 0.f;
+  int out_act = kActNone; float out_slope = 0.f;
+  const float* har = nullptr; long long har_bs = 0; int har_len = 0;
+  const float* wn = nullptr; const float* bn = nullptr; int nk = 0, nstr = 0, npad = 0;
+  int B = 1;
+};
+
+enum class LayerKind { kConv, kConvT };
+
+struct ConvLayer {
+  LayerKind kind = LayerKind::kConv;
+  int C_in = 0, C_out = 0, K = 0;
+  int dil = 1, pad_l = 0, pad_r = 0, stride = 1;  // conv
+  int up = 1, up_pad = 0;                          // convT: stride, padding
+  int taps_total = 0;
+  std::vector<ConvSlice> slices;  // rows filled per launch
+  DevBuf Wg, wpk, bias;
+  bool tc = false;
+  int bn = 0, cb = 0;
+
+  // W: conv [O,I,K] or convT [I,O,K], device fp32 (already weight-norm folded).
+  void build(Context* ctx, LayerKind k, const float* W, const float* b, int O, int I, int Kk, bool use_tc);
+  int out_len(int T_in) const;
+  // Launch on ctx->stream.  force_simt: run the fp32 SIMT kernel.
+  void run(Context* ctx, const ConvIO& io, bool force_simt = false) const;
+  double flops(int B, int T_in) const;
+};
+
+}  // namespace rvc

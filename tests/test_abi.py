@@ -1,0 +1,65 @@
+"""C-ABI checks that need no GPU: the library loads, exports every function
+that include/rvc_cuda.h declares, and reports errors through the
+status + last-error convention instead of crashing."""
+
+import ctypes as C
+import os
+import re
+
+import numpy as np
+import pytest
+
+from tests.conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "rvc_cuda.h")
+
+
+def declared():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"^int32_t\s+(rvc_cuda_\w+)\(", src, flags=re.M)))
+
+
+def test_header_declares_entry_points():
+    names = declared()
+    assert "rvc_cuda_synth_infer" in names and "rvc_cuda_conv1d" in names
+    assert len(names) >= 30
+
+
+def test_library_exports_every_declared_symbol():
+    from rvc_cuda import _lib
+    missing = [n for n in declared() if not hasattr(_lib.lib, n)]
+    assert not missing, missing
+    assert set(declared()) == set(_lib.EXPORTED)
+
+
+def test_version_and_device_count():
+    from rvc_cuda import _lib
+    assert _lib.lib.rvc_cuda_version() >= 100
+    assert _lib.device_count() >= 0
+
+
+def test_bad_device_is_an_error_not_a_crash():
+    from rvc_cuda import _lib
+    h = C.c_int64(0)
+    rc = _lib.lib.rvc_cuda_create(9999, C.byref(h))
+    assert rc == _lib.RVC_E_ARG
+    assert "9999" in _lib.last_error()
+    with pytest.raises(ValueError):
+        _lib.check(rc)
+
+
+def test_invalid_handles_report_state_errors():
+    from rvc_cuda import _lib
+    assert _lib.lib.rvc_cuda_sync(123456, 10) == -4
+    assert "invalid context handle" in _lib.last_error()
+    assert _lib.lib.rvc_cuda_synth_finalize(987654) == -4
+    out = np.zeros(4, np.float32)
+    assert _lib.lib.rvc_cuda_synth_tap(987654, b"x", _lib.fptr(out), 4) == -4
+
+
+def test_last_error_truncates_safely():
+    from rvc_cuda import _lib
+    _lib.lib.rvc_cuda_sync(123456, 10)
+    buf = C.create_string_buffer(8)
+    n = _lib.lib.rvc_cuda_last_error(buf, 8)
+    assert n > 8 and len(buf.value) == 7

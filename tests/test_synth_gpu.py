@@ -1,0 +1,124 @@
+"""Synthesizer parity: CudaSynthesizer (GPU, whole model through the C ABI)
+against the oracle and the reference's golden vectors.
+
+Bars: waveform max-abs error <= 1e-3 and per-layer
+relative L2 <= 1e-3, on identical seeded weights, inputs and noise.
+"""
+
+import numpy as np
+import pytest
+
+from oracle import vits as OV
+from rvc_cuda import synthetic as syn
+from tests.conftest import load_golden, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+synth = pytest.importorskip("rvc_cuda.synth")
+
+WAVE_TOL = 1e-3
+LAYER_TOL = 1e-3
+_models = {}
+
+
+def model(sr, seed, precision="bf16x3"):
+    key = (sr, seed, precision)
+    if key not in _models:
+        w = syn.make_vits_weights(sr, seed)
+        _models[key] = (w, synth.CudaSynthesizer(w, syn.vits_config_array(sr), precision=precision))
+    return _models[key]
+
+
+def run_case(sr, P, wseed, iseed, nseed, precision="bf16x3"):
+    w, m = model(sr, wseed, precision)
+    phone, pitch, nsff0, sid = syn.make_vits_inputs(P, iseed)
+    nz, ns = syn.make_vits_noise(P, m.upp, nseed)
+    m.keep_taps(True)
+    wav = m.infer_controlled(phone, pitch, nsff0, sid, nz, ns)
+    taps = {}
+    ref = OV.synth(w, syn.vits_config_array(sr), phone, pitch, nsff0, sid, nz, ns, taps)
+    return m, wav, ref, taps
+
+
+
+@pytest.mark.parametrize("name", ["vits40k_p32", "vits48k_p24", "vits40k_p7"])
+def test_synth_matches_golden(name, golden_meta):
+    g = golden_meta[name]
+    w, m = model(g["sr"], g["weight_seed"])
+    phone, pitch, nsff0, sid = syn.make_vits_inputs(g["P"], g["input_seed"])
+    nz, ns = syn.make_vits_noise(g["P"], g["upp"], g["noise_seed"])
+    wav = m.infer_controlled(phone, pitch, nsff0, sid, nz, ns)
+    gold = load_golden(name)
+    assert wav.shape == (1, 1, g["P"] * g["upp"])
+    err = np.abs(wav.reshape(-1) - gold["wave"]).max()
+    assert err <= WAVE_TOL, err
+
+
+@pytest.mark.parametrize("sr,P", [(40000, 64), (48000, 40)])
+def test_synth_per_layer(sr, P):
+    m, wav, ref, taps = run_case(sr, P, 0, 5, 55)
+    H = m.hidden
+    checks = {"enc.embed": (P, H), "enc.l0": (P, H), "enc.l5": (P, H), "enc.zp": (P, H), "flow.z": (P, H),
+              "dec.har": (P * m.upp,), "dec.pre": (P, 512)}
+    L = P
+    for i, r in enumerate(m.arch["rates"]):
+        L *= r
+        checks[f"dec.s{i}.ups"] = (L, 512 >> (i + 1))
+        checks[f"dec.s{i}.out"] = (L, 512 >> (i + 1))
+    worst = {}
+    for k, shp in checks.items():
+        got = m.tap(k, shp)
+        worst[k] = rel_l2(got, taps[k])
+    bad = {k: v for k, v in worst.items() if not v <= LAYER_TOL}
+    assert not bad, (bad, worst)
+    assert np.abs(wav - ref).max() <= WAVE_TOL
+
+
+def test_synth_simt_precision_agrees():
+    _, wav, ref, _ = run_case(40000, 20, 0, 6, 66, precision="simt")
+    assert np.abs(wav - ref).max() <= WAVE_TOL
+
+
+def test_synth_batch_equals_single():
+    w, m = model(40000, 0)
+    P, B = 24, 3
+    ins = [syn.make_vits_inputs(P, 100 + i) for i in range(B)]
+    noise = [syn.make_vits_noise(P, m.upp, 200 + i) for i in range(B)]
+    batch = m.infer_batch(np.concatenate([i[0] for i in ins]), np.concatenate([i[1] for i in ins]),
+                          np.concatenate([i[2] for i in ins]), np.concatenate([i[3] for i in ins]),
+                          np.concatenate([n[0] for n in noise]), np.stack([n[1].reshape(-1) for n in noise]))
+    for i in range(B):
+        one = m.infer_controlled(*ins[i], *noise[i]).reshape(-1)
+        np.testing.assert_allclose(batch[i], one, rtol=0, atol=1e-6)
+
+
+def test_synth_long_chunk_properties():
+    """Full 10 s chunk (P=1000): output shape, finite, bounded, deterministic."""
+    w, m = model(40000, 0)
+    phone, pitch, nsff0, sid = syn.make_vits_inputs(1000, 9)
+    nz, ns = syn.make_vits_noise(1000, m.upp, 99)
+    a = m.infer_controlled(phone, pitch, nsff0, sid, nz, ns)
+    b = m.infer_controlled(phone, pitch, nsff0, sid, nz, ns)
+    assert a.shape == (1, 1, 400000)
+    assert np.isfinite(a).all() and np.abs(a).max() <= 1.0
+    np.testing.assert_array_equal(a, b)
+    assert 0.05 < a.std() < 0.8
+
+
+def test_seeded_infer_matches_infer_controlled():
+    w, m = model(40000, 0)
+    phone, pitch, nsff0, sid = syn.make_vits_inputs(16, 3)
+    a = m.infer(phone, pitch, nsff0, sid, seed=1234)
+    nz, ns = syn.make_vits_noise(16, m.upp, 1234)
+    b = m.infer_controlled(phone, pitch, nsff0, sid, nz, ns)
+    np.testing.assert_array_equal(a, b)
+
+
+def test_bad_inputs_raise():
+    w, m = model(40000, 0)
+    phone, pitch, nsff0, sid = syn.make_vits_inputs(8, 3)
+    nz, ns = syn.make_vits_noise(8, m.upp, 1)
+    with pytest.raises(ValueError):
+        m.infer_controlled(phone, pitch + 300, nsff0, sid, nz, ns)
+    with pytest.raises(ValueError):
+        m.infer_controlled(phone, pitch, nsff0, np.array([5]), nz, ns)
