@@ -89,7 +89,7 @@ class ClockSampler:
         sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4) if "Active" in r[4 + i]})
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[4 + i].strip() == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": reasons, "samples": len(self.rows)}
 
@@ -252,6 +252,9 @@ def run_ours(args, world, rank, local):
     with ClockSampler(local) as clk:
         t = timed(step_device, args.steps)
     prof_n, prof_ms, prof_flops = ctx.profile_read()
+    if args.profile_out and rank == 0:
+        with open(args.profile_out, "w") as f:
+            f.write(ctx.profile_dump())
     ctx.profile(False)
     launches = _lib.launch_count() - n0
     t = max_over_ranks(t)
@@ -315,6 +318,7 @@ def main():
     ap.add_argument("--precision", default="bf16x3", choices=["bf16x3", "simt"])
     ap.add_argument("--ref-frames", type=int, default=100)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--profile-out", default="", help="write the per-layer conv profile (CSV) here")
     args = ap.parse_args()
     world, rank, local = dist_setup()
     if args.impl == "reference":

@@ -67,6 +67,9 @@ int32_t rvc_cuda_d2h(int64_t ctx, void* dst, const void* src, int64_t bytes);
  * accumulated launch count, device milliseconds and algorithmic FLOPs. */
 int32_t rvc_cuda_profile(int64_t ctx, int32_t enable);
 int32_t rvc_cuda_profile_read(int64_t ctx, int64_t* launches, double* ms, double* flops);
+/* Per-layer breakdown as CSV text (label,launches,ms,flops); returns the full
+ * length (>= 0) or an error status. */
+int32_t rvc_cuda_profile_dump(int64_t ctx, char* buf, int64_t n);
 
 /* ------------------------------------------------- tier 1: operator module
  * Numpy-semantics operators behind runtime.backend's RVC_BACKEND dispatch

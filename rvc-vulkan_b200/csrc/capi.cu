@@ -198,10 +198,32 @@ int32_t rvc_cuda_profile(int64_t ctx, int32_t enable) {
   return on_ctx(ctx, [&](Context* c) {
     c->prof_collect();
     c->prof = enable != 0;
+    c->prof_by_label.clear();
     c->prof_launches = 0;
     c->prof_ms = 0.0;
     c->prof_flops = 0.0;
   });
+}
+
+int32_t rvc_cuda_profile_dump(int64_t ctx, char* buf, int64_t n) {
+  int32_t len = 0;
+  int32_t rc = on_ctx(ctx, [&](Context* c) {
+    c->prof_collect();
+    std::string out = "label,launches,ms,flops\n";
+    for (auto& kv : c->prof_by_label) {
+      char line[256];
+      snprintf(line, sizeof(line), "\"%s\",%lld,%.6f,%.6e\n", kv.first.c_str(), kv.second.n, kv.second.ms,
+               kv.second.flops);
+      out += line;
+    }
+    len = (int32_t)out.size();
+    if (buf && n > 0) {
+      size_t k = std::min<size_t>((size_t)n - 1, out.size());
+      std::memcpy(buf, out.data(), k);
+      buf[k] = 0;
+    }
+  });
+  return rc == kOk ? len : rc;
 }
 
 int32_t rvc_cuda_profile_read(int64_t ctx, int64_t* launches, double* ms, double* flops) {

@@ -26,8 +26,8 @@ Context::~Context() {
   for (auto& kv : allocs) cudaFree(kv.first);
   allocs.clear();
   for (auto& e : prof_ev) {
-    cudaEventDestroy(e.first);
-    cudaEventDestroy(e.second);
+    cudaEventDestroy(e.a);
+    cudaEventDestroy(e.b);
   }
   for (auto e : ev_pool) cudaEventDestroy(e);
   if (d_err) cudaFree(d_err);
@@ -78,9 +78,9 @@ void Context::prof_begin(cudaEvent_t* a, cudaEvent_t* b) {
   RVC_CUDA_TRY(cudaEventRecord(*a, stream));
 }
 
-void Context::prof_end(cudaEvent_t a, cudaEvent_t b, double flops) {
+void Context::prof_end(cudaEvent_t a, cudaEvent_t b, double flops, const std::string& label) {
   RVC_CUDA_TRY(cudaEventRecord(b, stream));
-  prof_ev.emplace_back(a, b);
+  prof_ev.push_back(ProfRec{a, b, flops, label});
   prof_launches += 1;
   prof_flops += flops;
   if (prof_ev.size() > 4096) prof_collect();
@@ -90,10 +90,14 @@ void Context::prof_collect() {
   RVC_CUDA_TRY(cudaStreamSynchronize(stream));
   for (auto& e : prof_ev) {
     float ms = 0.f;
-    RVC_CUDA_TRY(cudaEventElapsedTime(&ms, e.first, e.second));
+    RVC_CUDA_TRY(cudaEventElapsedTime(&ms, e.a, e.b));
     prof_ms += ms;
-    ev_pool.push_back(e.first);
-    ev_pool.push_back(e.second);
+    auto& g = prof_by_label[e.label];
+    g.n += 1;
+    g.ms += ms;
+    g.flops += e.flops;
+    ev_pool.push_back(e.a);
+    ev_pool.push_back(e.b);
   }
   prof_ev.clear();
 }

@@ -4,7 +4,9 @@
 
 #include "common.cuh"
 
+#include <map>
 #include <mutex>
+#include <string>
 #include <unordered_map>
 #include <utility>
 #include <vector>
@@ -21,7 +23,10 @@ struct Context {
   std::unordered_map<void*, size_t> allocs;
   // profiling of tensor-core conv launches
   bool prof = false;
-  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> prof_ev;
+  struct ProfRec { cudaEvent_t a, b; double flops; std::string label; };
+  std::vector<ProfRec> prof_ev;
+  struct ProfAgg { long long n = 0; double ms = 0, flops = 0; };
+  std::map<std::string, ProfAgg> prof_by_label;
   std::vector<cudaEvent_t> ev_pool;
   int64_t prof_launches = 0;
   double prof_ms = 0.0, prof_flops = 0.0;
@@ -31,7 +36,7 @@ struct Context {
   void* alloc(size_t bytes);  // zero-filled
   void free(void* p);
   void prof_begin(cudaEvent_t* a, cudaEvent_t* b);
-  void prof_end(cudaEvent_t a, cudaEvent_t b, double flops);
+  void prof_end(cudaEvent_t a, cudaEvent_t b, double flops, const std::string& label);
   void prof_collect();
   // Polls the stream (bounded) and the device error flag.
   int32_t sync(int timeout_ms);

@@ -53,7 +53,7 @@ struct ConvArgs {
   const uint16_t* wpk;
   int bn;          // tcgen05 N tile
   int cb;          // tcgen05 channel block (K per stage)
-  // epilogue: v = acc + bias[c] + bias2[b][c] (+ noise) (+ res) ; v = accin + v ; v /= div ;
+  // epilogue: v = acc + bias[c] + bias2[b][c] (+ res) ; v = accin + v ; v /= div ;
   //           y = act(v)   (optionally also y_raw = v before act)
   const float* bias;
   const float* bias2; long long bias2_bs;
@@ -64,9 +64,6 @@ struct ConvArgs {
   int out_act; float out_slope;
   float* y; long long y_bs; int y_ld;
   float* y_raw;    // optional pre-activation copy (same strides as y)
-  // fused NSF noise conv (conv1d over the 1-channel source): stride nstr, pad npad
-  const float* har; long long har_bs; int har_len;
-  const float* wn; const float* bn_; int nk, nstr, npad;
   int* err;        // device error flag (bounded waits)
 };
 
@@ -76,18 +73,6 @@ __device__ __forceinline__ void conv_epilogue(const ConvArgs& a, int b, int prow
   float v = acc;
   if (a.bias) v += a.bias[cg];
   if (a.bias2) v += a.bias2[(long long)b * a.bias2_bs + cg];
-  if (a.har) {
-    // numpy order: x = convT(x)+b_up ; x = x + (noise_conv(har)+b_n)
-    const float* h = a.har + (long long)b * a.har_bs;
-    float s = 0.f;
-    int base = prow * a.nstr - a.npad;
-    for (int k = 0; k < a.nk; ++k) {
-      int idx = base + k;
-      float hv = (idx >= 0 && idx < a.har_len) ? h[idx] : 0.f;
-      s = fmaf(hv, a.wn[cg * a.nk + k], s);
-    }
-    v = v + (s + a.bn_[cg]);
-  }
   if (a.res) {
     const float r = a.res[(long long)b * a.res_bs + (long long)prow * a.res_ld + cg];
     v = a.res_sub ? (r - v) : (v + r);

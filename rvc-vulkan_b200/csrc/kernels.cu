@@ -2,6 +2,7 @@
 #include "kernels.cuh"
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 
 namespace rvc {
@@ -549,6 +550,73 @@ void k_sine_source(const float* f0, const float* ns, int B, int P, int upp, int 
   long long n = (long long)B * P * upp;
   sine_source_kernel<<<grid_for(n, 256), 256, 0, st>>>(f0, ns, phase_scratch, B, P, upp, (float)sr, lin_w, lin_b,
                                                        har);
+  RVC_LAUNCH_CHECK();
+}
+
+// NSF noise conv (runtime/models/vits.py:1616-1636 noise_convs): a tile of 32
+// output rows x 64 channels per CTA, the source window and the weights staged
+// in shared memory (weights transposed to [k][co] for conflict-free reads).
+constexpr int kNzRows = 32, kNzCols = 64, kNzMaxK = 128;
+__global__ void __launch_bounds__(256) noise_conv_kernel(const float* __restrict__ har, long long har_bs, int har_len,
+                                                         const float* __restrict__ w, const float* __restrict__ bias,
+                                                         int C, int nk, int str, int pad, int T_out,
+                                                         float* __restrict__ y, long long y_bs) {
+  extern __shared__ float sm[];
+  const int span = (kNzRows - 1) * str + nk;
+  float* hs = sm;                       // [span]
+  float* ws = sm + ((span + 3) & ~3);   // [nk][kNzCols], 16-byte aligned for float4 reads
+  const int b = blockIdx.z;
+  const int t0 = blockIdx.x * kNzRows, c0 = blockIdx.y * kNzCols;
+  const float* hb = har + (long long)b * har_bs;
+  const int base = t0 * str - pad;
+  for (int i = threadIdx.x; i < span; i += blockDim.x) {
+    int idx = base + i;
+    hs[i] = (idx >= 0 && idx < har_len) ? hb[idx] : 0.f;
+  }
+  for (int i = threadIdx.x; i < nk * kNzCols; i += blockDim.x) {
+    int k = i / kNzCols, c = i % kNzCols;
+    ws[i] = (c0 + c < C) ? w[(long long)(c0 + c) * nk + k] : 0.f;
+  }
+  __syncthreads();
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // 2 rows x 4 cols per thread
+  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  for (int k = 0; k < nk; ++k) {
+    const float h0 = hs[(ty * 2) * str + k], h1 = hs[(ty * 2 + 1) * str + k];
+    const float4 wv = *reinterpret_cast<const float4*>(ws + k * kNzCols + tx * 4);
+    const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      acc[0][j] = fmaf(h0, wa[j], acc[0][j]);
+      acc[1][j] = fmaf(h1, wa[j], acc[1][j]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int t = t0 + ty * 2 + i;
+    if (t >= T_out) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = c0 + tx * 4 + j;
+      if (c < C) y[(long long)b * y_bs + (long long)t * C + c] = acc[i][j] + bias[c];
+    }
+  }
+}
+void k_noise_conv(const float* har, long long har_bs, int har_len, const float* w, const float* bias, int C, int nk,
+                  int str, int pad, int B, int T_out, float* y, long long y_bs, cudaStream_t st) {
+  if (B * T_out == 0) return;
+  RVC_CHECK_ARG(nk <= kNzMaxK * 4, "noise_conv: kernel too long");
+  const int span = (kNzRows - 1) * str + nk;
+  size_t smem = sizeof(float) * ((size_t)((span + 3) & ~3) + (size_t)nk * kNzCols);
+  RVC_CHECK_ARG(smem <= 200 * 1024, "noise_conv: tile does not fit in shared memory");
+  static std::atomic<uint64_t> attr_done{0};
+  int dev = 0;
+  RVC_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 64 && !(attr_done.load() & (1ull << dev))) {
+    RVC_CUDA_TRY(cudaFuncSetAttribute(noise_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    attr_done.fetch_or(1ull << dev);
+  }
+  dim3 g(cdiv(T_out, kNzRows), cdiv(C, kNzCols), B);
+  noise_conv_kernel<<<g, 256, smem, st>>>(har, har_bs, har_len, w, bias, C, nk, str, pad, T_out, y, y_bs);
   RVC_LAUNCH_CHECK();
 }
 

@@ -51,6 +51,10 @@ void k_wn_update(float* h, float* skip, const float* rs, long long rows, int H, 
 // NSF sine source: har[b, n], n < P*upp
 void k_sine_source(const float* f0, const float* ns, int B, int P, int upp, int sr, float lin_w, float lin_b,
                    float* phase_scratch, float* har, cudaStream_t st);
+// NSF noise conv (conv1d with one input channel): y[b,t,co] = sum_k har[b, t*str - pad + k] * w[co][k] + bias[co]
+// for t < T_out, written to y with batch stride y_bs and row stride C.
+void k_noise_conv(const float* har, long long har_bs, int har_len, const float* w, const float* bias, int C, int nk,
+                  int str, int pad, int B, int T_out, float* y, long long y_bs, cudaStream_t st);
 // y[b,t] = tanh(sum_k sum_c leaky(x[b,t+k-pad,c],slope) * w[c][k])   (conv_post, C_out = 1, no bias)
 void k_conv_post_tanh(const float* x, long long x_bs, int B, int T, int C, const float* w, int K, int pad, float slope,
                       float* y, cudaStream_t st);

@@ -1,6 +1,7 @@
 #include "layer.cuh"
 
 #include <algorithm>
+#include <cstdio>
 
 namespace rvc {
 
@@ -107,8 +108,6 @@ void ConvLayer::run(Context* ctx, const ConvIO& io, bool force_simt) const {
   a.out_div = io.out_div;
   a.out_act = io.out_act; a.out_slope = io.out_slope;
   a.y = io.y; a.y_bs = io.y_bs; a.y_ld = io.y_ld; a.y_raw = io.y_raw;
-  a.har = io.har; a.har_bs = io.har_bs; a.har_len = io.har_len;
-  a.wn = io.wn; a.bn_ = io.bn; a.nk = io.nk; a.nstr = io.nstr; a.npad = io.npad;
   a.err = ctx->d_err;
   if (oL == 0 || io.B == 0) return;
   bool any_empty = false;  // a transposed-conv phase with no taps: output = epilogue(0)
@@ -118,7 +117,12 @@ void ConvLayer::run(Context* ctx, const ConvIO& io, bool force_simt) const {
     cudaEvent_t e0 = nullptr, e1 = nullptr;
     if (ctx->prof) ctx->prof_begin(&e0, &e1);
     launch_tc_conv(a, ctx->stream);
-    if (ctx->prof) ctx->prof_end(e0, e1, flops(io.B, io.T_in));
+    if (ctx->prof) {
+      char lab[160];
+      snprintf(lab, sizeof(lab), "%s Cin=%d Cout=%d K=%d dil=%d up=%d T=%d B=%d bn=%d cb=%d",
+               kind == LayerKind::kConv ? "conv" : "convT", C_in, C_out, K, dil, up, io.T_in, io.B, bn, cb);
+      ctx->prof_end(e0, e1, flops(io.B, io.T_in), lab);
+    }
   } else {
     launch_simt_conv(a, ctx->stream);
   }

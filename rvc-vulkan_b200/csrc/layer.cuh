@@ -23,8 +23,6 @@ struct ConvIO {
   const float* accin = nullptr; long long acc_bs = 0; int acc_ld = 0;
   float out_div = 0.f;
   int out_act = kActNone; float out_slope = 0.f;
-  const float* har = nullptr; long long har_bs = 0; int har_len = 0;
-  const float* wn = nullptr; const float* bn = nullptr; int nk = 0, nstr = 0, npad = 0;
   int B = 1;
 };
 

@@ -187,7 +187,7 @@ void SynthModel::ensure_ws(int B, int P) {
   add("rs", (long long)P * 2 * H);
   add("har", (long long)P * upp);
   add("phase", P);
-  for (const char* n : {"xo", "x0", "r", "t", "s"}) add(n, dmax);
+  for (const char* n : {"xo", "x0", "r", "t", "s", "noise"}) add(n, dmax);
   ws_B = B;
   ws_P = P;
 }
@@ -309,14 +309,14 @@ void SynthModel::infer_device(int B, int P, const float* phone, const long long*
       ConvIO a = io_rows(xo, cfg.up0 >> i, Lc, x0, C, B, dmax, dmax);
       a.in_act = kActLeaky;
       a.in_slope = 0.1f;
-      a.har = buf("har");
-      a.har_bs = N;
-      a.har_len = (int)N;
-      a.wn = W("dec.noise_convs." + std::to_string(i) + ".weight").buf.f();
-      a.bn = W("dec.noise_convs." + std::to_string(i) + ".bias").buf.f();
-      a.nk = noise_k_[i];
-      a.nstr = noise_s_[i];
-      a.npad = noise_s_[i] / 2;
+      // x = ups(x) + noise_conv(har): the noise conv (bias included) runs first
+      // and enters the transposed conv's epilogue as its residual term.
+      k_noise_conv(buf("har"), N, (int)N, W("dec.noise_convs." + std::to_string(i) + ".weight").buf.f(),
+                   W("dec.noise_convs." + std::to_string(i) + ".bias").buf.f(), C, noise_k_[i], noise_s_[i],
+                   noise_s_[i] / 2, B, Ln, buf("noise"), dmax, st);
+      a.res = buf("noise");
+      a.res_bs = dmax;
+      a.res_ld = C;
       run_conv(ups_[i], a);
       save_tap("dec.s" + std::to_string(i) + ".ups", x0, (long long)B * dmax);
     }

@@ -65,6 +65,7 @@ _SIGS = {
     "rvc_cuda_h2d": ([_i64, _p, _p, _i64], _i32),
     "rvc_cuda_d2h": ([_i64, _p, _p, _i64], _i32),
     "rvc_cuda_profile": ([_i64, _i32], _i32),
+    "rvc_cuda_profile_dump": ([_i64, C.c_char_p, _i64], _i32),
     "rvc_cuda_profile_read": ([_i64, C.POINTER(_i64), C.POINTER(_f64), C.POINTER(_f64)], _i32),
     "rvc_cuda_conv1d": ([_i64, _fp, _i32, _i32, _i32, _fp, _i32, _i32, _fp, _i32, _i32, _i32, _i32, _fp, _i32], _i32),
     "rvc_cuda_conv_transpose1d": ([_i64, _fp, _i32, _i32, _i32, _fp, _i32, _i32, _fp, _i32, _i32, _i32, _i32, _fp,
@@ -178,6 +179,13 @@ class Context:
         n, ms, fl = _i64(0), _f64(0), _f64(0)
         check(lib.rvc_cuda_profile_read(self.handle, C.byref(n), C.byref(ms), C.byref(fl)))
         return int(n.value), float(ms.value), float(fl.value)
+
+    def profile_dump(self) -> str:
+        buf = C.create_string_buffer(1 << 20)
+        n = lib.rvc_cuda_profile_dump(self.handle, buf, len(buf))
+        if n < 0:
+            check(n)
+        return buf.value.decode()
 
     def __del__(self):
         try:
