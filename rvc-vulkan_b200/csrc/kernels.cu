@@ -331,114 +331,7 @@ void k_enc_embed_finish(float* lin, const long long* pitch, const float* E, long
   RVC_LAUNCH_CHECK();
 }
 
-// Relative attention, pass 1: S[b,h,i,j] = qs_i.k_j + (|j-i|<=W ? qs_i.ek[j-i+W] : 0),
-// qs = q / sqrt(kc)   (runtime/models/vits.py:998-1005).
-constexpr int kAttT = 32;
-__global__ void rel_scores_kernel(const float* __restrict__ qkv, int ld, int q_off, int k_off,
-                                  const float* __restrict__ emb_k, int heads, int kc, int P, int window,
-                                  float inv_div, float* __restrict__ S) {
-  extern __shared__ float sm[];
-  float* qs = sm;                    // [32][kc+1]
-  float* ks = sm + kAttT * (kc + 1);  // [32][kc+1]
-  const int bh = blockIdx.z;
-  const int b = bh / heads, h = bh % heads;
-  const int i0 = blockIdx.y * kAttT, j0 = blockIdx.x * kAttT;
-  const float* base = qkv + (long long)b * P * ld;
-  for (int e = threadIdx.x; e < kAttT * kc; e += blockDim.x) {
-    int r = e / kc, d = e % kc;
-    int i = i0 + r, j = j0 + r;
-    qs[r * (kc + 1) + d] = i < P ? base[(long long)i * ld + q_off + h * kc + d] / inv_div : 0.f;
-    ks[r * (kc + 1) + d] = j < P ? base[(long long)j * ld + k_off + h * kc + d] : 0.f;
-  }
-  __syncthreads();
-  const int tj = threadIdx.x & 31, ti0 = (threadIdx.x >> 5) * 4;
-  for (int u = 0; u < 4; ++u) {
-    int ri = ti0 + u;
-    int i = i0 + ri, j = j0 + tj;
-    if (i >= P || j >= P) continue;
-    float s = 0.f;
-    for (int d = 0; d < kc; ++d) s = fmaf(qs[ri * (kc + 1) + d], ks[tj * (kc + 1) + d], s);
-    int rel = j - i;
-    if (rel >= -window && rel <= window) {
-      const float* e = emb_k + (long long)(h * 0 + rel + window) * kc;  // emb_rel shared by heads
-      float r2 = 0.f;
-      for (int d = 0; d < kc; ++d) r2 = fmaf(qs[ri * (kc + 1) + d], e[d], r2);
-      s = s + r2;
-    }
-    S[((long long)bh * P + i) * P + j] = s;
-  }
-}
-
-// Pass 3: y[b,i,h*kc+d] = sum_j p[i,j] v_j[d] + sum_{|j-i|<=W} p[i,j] ev[j-i+W][d]
-__global__ void rel_pv_kernel(const float* __restrict__ Pm, const float* __restrict__ qkv, int ld, int v_off,
-                              const float* __restrict__ emb_v, int heads, int kc, int P, int window,
-                              float* __restrict__ y, int y_ld) {
-  extern __shared__ float sm[];
-  float* ps = sm;                          // [32][33]
-  float* vs = sm + kAttT * (kAttT + 1);    // [32][kc]
-  const int bh = blockIdx.z;
-  const int b = bh / heads, h = bh % heads;
-  const int i0 = blockIdx.x * kAttT;
-  const float* vb = qkv + (long long)b * P * ld + v_off + h * kc;
-  const float* prow = Pm + (long long)bh * P * P;
-  // each thread: row i = i0 + threadIdx.x / 8 ... use (32 rows) x (kc cols) outputs over 256 threads
-  const int nout = kAttT * kc;
-  float acc[12];
-  for (int u = 0; u < 12; ++u) acc[u] = 0.f;
-  for (int j0 = 0; j0 < P; j0 += kAttT) {
-    for (int e = threadIdx.x; e < kAttT * kAttT; e += blockDim.x) {
-      int r = e / kAttT, c = e % kAttT;
-      int i = i0 + r, j = j0 + c;
-      ps[r * (kAttT + 1) + c] = (i < P && j < P) ? prow[(long long)i * P + j] : 0.f;
-    }
-    for (int e = threadIdx.x; e < kAttT * kc; e += blockDim.x) {
-      int r = e / kc, d = e % kc;
-      int j = j0 + r;
-      vs[r * kc + d] = j < P ? vb[(long long)j * ld + d] : 0.f;
-    }
-    __syncthreads();
-    for (int u = 0; u < 12; ++u) {
-      int o = threadIdx.x + u * blockDim.x;
-      if (o >= nout) break;
-      int r = o / kc, d = o % kc;
-      float s = acc[u];
-      for (int c = 0; c < kAttT; ++c) s = fmaf(ps[r * (kAttT + 1) + c], vs[c * kc + d], s);
-      acc[u] = s;
-    }
-    __syncthreads();
-  }
-  for (int u = 0; u < 12; ++u) {
-    int o = threadIdx.x + u * blockDim.x;
-    if (o >= nout) break;
-    int r = o / kc, d = o % kc;
-    int i = i0 + r;
-    if (i >= P) continue;
-    float rel = 0.f;
-    for (int rr = -window; rr <= window; ++rr) {
-      int j = i + rr;
-      if (j < 0 || j >= P) continue;
-      rel = fmaf(prow[(long long)i * P + j], emb_v[(long long)(rr + window) * kc + d], rel);
-    }
-    y[((long long)b * P + i) * y_ld + h * kc + d] = acc[u] + rel;
-  }
-}
-
-void k_rel_attention(const float* qkv, int qkv_ld, int q_off, int k_off, int v_off, const float* emb_k,
-                     const float* emb_v, int B, int heads, int kc, int P, int window, float* scratch, float* y,
-                     int y_ld, cudaStream_t st) {
-  if (B * P == 0) return;
-  RVC_CHECK_ARG(kc <= 128 && kAttT * kc <= 12 * 256, "rel_attention: head dim too large");
-  const float div = (float)std::sqrt((double)kc);
-  dim3 g1(cdiv(P, kAttT), cdiv(P, kAttT), B * heads);
-  size_t sm1 = 2 * kAttT * (kc + 1) * sizeof(float);
-  rel_scores_kernel<<<g1, 256, sm1, st>>>(qkv, qkv_ld, q_off, k_off, emb_k, heads, kc, P, window, div, scratch);
-  RVC_LAUNCH_CHECK();
-  k_softmax_rows(scratch, scratch, (long long)B * heads * P, P, st);
-  dim3 g3(cdiv(P, kAttT), 1, B * heads);
-  size_t sm3 = (kAttT * (kAttT + 1) + kAttT * kc) * sizeof(float);
-  rel_pv_kernel<<<g3, 256, sm3, st>>>(scratch, qkv, qkv_ld, v_off, emb_v, heads, kc, P, window, y, y_ld);
-  RVC_LAUNCH_CHECK();
-}
+// k_rel_attention lives in attention.cu.
 
 __global__ void zp_kernel(const float* __restrict__ stats, const float* __restrict__ nz, int P, int H,
                           float* __restrict__ z, long long n) {
@@ -507,51 +400,7 @@ void k_wn_update(float* h, float* skip, const float* rs, long long rows, int H, 
   RVC_LAUNCH_CHECK();
 }
 
-// NSF source (runtime/models/vits.py:1468-1501).  Phase carry: a float32
-// running sum over frames of fmod(rad_last + 0.5, 1) - 0.5, then fmod(., 1),
-// sequential like numpy's cumsum.
-__global__ void sine_phase_kernel(const float* __restrict__ f0, int B, int P, int upp, float srf,
-                                  float* __restrict__ phase) {
-  int b = blockIdx.x * blockDim.x + threadIdx.x;
-  if (b >= B) return;
-  float acc = 0.f;
-  const float last = (float)upp;
-  for (int t = 0; t < P; ++t) {
-    float rl = (f0[(long long)b * P + t] / srf) * last;
-    float r2 = fmodf(rl + 0.5f, 1.0f) - 0.5f;
-    acc = acc + r2;
-    phase[(long long)b * P + t] = fmodf(acc, 1.0f);
-  }
-}
-__global__ void sine_source_kernel(const float* __restrict__ f0, const float* __restrict__ ns,
-                                   const float* __restrict__ phase, int B, int P, int upp, float srf, float lw,
-                                   float lb, float* __restrict__ har) {
-  const long long N = (long long)P * upp;
-  const long long n = (long long)B * N;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const int b = (int)(i / N);
-    const long long s = i % N;
-    const int t = (int)(s / upp), j = (int)(s % upp);
-    const float f = f0[(long long)b * P + t];
-    float rad = (f / srf) * (float)(j + 1);
-    if (t > 0) rad = rad + phase[(long long)b * P + t - 1];
-    float sine = sinf(6.2831855f * rad) * 0.1f;
-    const float uv = f > 0.f ? 1.f : 0.f;
-    const float amp = uv * 0.003f + ((1.f - uv) * 0.1f) / 3.f;
-    sine = sine * uv + amp * ns[i];
-    har[i] = tanhf(sine * lw + lb);
-  }
-}
-void k_sine_source(const float* f0, const float* ns, int B, int P, int upp, int sr, float lin_w, float lin_b,
-                   float* phase_scratch, float* har, cudaStream_t st) {
-  if (B * P == 0) return;
-  sine_phase_kernel<<<cdiv(B, 32), 32, 0, st>>>(f0, B, P, upp, (float)sr, phase_scratch);
-  RVC_LAUNCH_CHECK();
-  long long n = (long long)B * P * upp;
-  sine_source_kernel<<<grid_for(n, 256), 256, 0, st>>>(f0, ns, phase_scratch, B, P, upp, (float)sr, lin_w, lin_b,
-                                                       har);
-  RVC_LAUNCH_CHECK();
-}
+// k_sine_source, k_conv_post_tanh live in dec_kernels.cu.
 
 // NSF noise conv (runtime/models/vits.py:1616-1636 noise_convs): a tile of 32
 // output rows x 64 channels per CTA, the source window and the weights staged
@@ -617,34 +466,6 @@ void k_noise_conv(const float* har, long long har_bs, int har_len, const float* 
   }
   dim3 g(cdiv(T_out, kNzRows), cdiv(C, kNzCols), B);
   noise_conv_kernel<<<g, 256, smem, st>>>(har, har_bs, har_len, w, bias, C, nk, str, pad, T_out, y, y_bs);
-  RVC_LAUNCH_CHECK();
-}
-
-__global__ void conv_post_kernel(const float* __restrict__ x, long long x_bs, int B, int T, int C, const float* __restrict__ w,
-                                 int K, int pad, float slope, float* __restrict__ y) {
-  const long long n = (long long)B * T;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    const int b = (int)(i / T), t = (int)(i % T);
-    const float* xb = x + (long long)b * x_bs;
-    float s = 0.f;
-    for (int k = 0; k < K; ++k) {
-      int r = t + k - pad;
-      if (r < 0 || r >= T) continue;
-      const float* xr = xb + (long long)r * C;
-      for (int c = 0; c < C; ++c) {
-        float v = xr[c];
-        v = v >= 0.f ? v : slope * v;
-        s = fmaf(v, w[c * K + k], s);
-      }
-    }
-    y[i] = tanhf(s);
-  }
-}
-void k_conv_post_tanh(const float* x, long long x_bs, int B, int T, int C, const float* w, int K, int pad,
-                      float slope, float* y, cudaStream_t st) {
-  long long n = (long long)B * T;
-  if (n == 0) return;
-  conv_post_kernel<<<grid_for(n, 128, 148 * 64), 128, 0, st>>>(x, x_bs, B, T, C, w, K, pad, slope, y);
   RVC_LAUNCH_CHECK();
 }
 

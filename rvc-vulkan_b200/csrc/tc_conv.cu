@@ -1,0 +1,764 @@
+// tcgen05 implicit-GEMM convolution: persistent, TMA-fed, BF16x3 split
+// precision with fp32 accumulation in TMEM.  Operator contract in conv.cuh.
+//
+// A CTA loops over tiles of msub*128 output rows x bn output channels.  Each
+// weight stage (one tap x one cb-channel block, bf16 hi and lo planes) feeds
+// msub MMAs, one per 128-row subtile, so weights stream through shared memory
+// once per msub*128 rows.  Accumulators live in TMEM: nacc sets of msub*bn
+// columns, so the epilogue of one tile overlaps the main loop of the next.
+//
+//   warp 0       weight producer: cp.async.bulk of packed hi/lo planes into a
+//                `stages`-deep ring
+//   warp 1       TMEM owner + single-thread tcgen05.mma issuer
+//   warp 2       activation loader: TMA (cp.async.bulk.tensor) of the fp32 halo
+//                tile (out-of-range rows zero-filled = conv padding) into a
+//                staging buffer
+//   warps 3..6   converters: staging fp32 -> prologue activation -> bf16 hi/lo
+//                MMA planes (the halo tile serves every tap of the block)
+//   warps 7..10  epilogue: TMEM -> registers; residual / accumulator tiles
+//                arrive by TMA into 128B-swizzled slots (prefetched one step
+//                ahead), the result is written in place and stored by TMA.
+//                Transposed-conv phases (strided output rows) and unaligned
+//                cases use direct vector stores instead.
+#include "conv.cuh"
+#include "tc_ptx.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <atomic>
+#include <mutex>
+
+namespace rvc {
+
+constexpr int kTM = 128;
+constexpr int kWarps = 11;
+constexpr int kThreads = kWarps * 32;
+constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s per barrier wait
+constexpr int kEpiCols = 32;
+constexpr uint32_t kSlotBytes = kTM * kEpiCols * 4;  // one 128 x 32 fp32 tile
+
+struct TcMaps {
+  CUtensorMap a, res, acc, y;
+};
+
+struct TcPlan {
+  int msub, nacc, arows_pad, stages;
+  int nstg, box_rows, nbox;
+  int nslot, acc_slot, tma_epi;
+  uint32_t a_plane, b_plane, stg_bytes;
+  uint32_t off_a, off_stg, off_b, off_epi, off_bar, smem_bytes;
+  uint32_t off_bias;  // bias staged in shared memory (0: read from global)
+  int bias_n;
+  int w_res;          // whole packed weight tensor resident in shared memory
+  uint32_t off_w, w_bytes;
+  int ephase;         // epilogue maps are 4-D {ch, phase, q, b} (transposed conv)
+  uint32_t tmem_cols;
+  int tiles_m, ntiles, total_tiles;
+  int vec;
+};
+
+// Direct epilogue for N (16 or 32) consecutive output channels of one row;
+// every global load of the step is issued before any is used.
+template <int N>
+__device__ __forceinline__ void epi_direct(const ConvArgs& a, int b, int prow, int cg0, float (&v)[N], int vec) {
+  if (!vec) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) conv_epilogue(a, b, prow, cg0 + i, v[i]);
+    return;
+  }
+  constexpr int Q = N / 4;
+  float4 rb[Q], ra[Q];
+  if (a.res) {
+    const float4* p =
+        reinterpret_cast<const float4*>(a.res + (long long)b * a.res_bs + (long long)prow * a.res_ld + cg0);
+#pragma unroll
+    for (int q = 0; q < Q; ++q) rb[q] = p[q];
+  }
+  if (a.accin) {
+    const float4* p =
+        reinterpret_cast<const float4*>(a.accin + (long long)b * a.acc_bs + (long long)prow * a.acc_ld + cg0);
+#pragma unroll
+    for (int q = 0; q < Q; ++q) ra[q] = p[q];
+  }
+  float out[N];
+#pragma unroll
+  for (int q = 0; q < Q; ++q) {
+    float x[4] = {v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]};
+    const float4 bi = a.bias ? __ldg(reinterpret_cast<const float4*>(a.bias + cg0) + q) : make_float4(0, 0, 0, 0);
+    const float4 b2 = a.bias2 ? __ldg(reinterpret_cast<const float4*>(a.bias2 + (long long)b * a.bias2_bs + cg0) + q)
+                              : make_float4(0, 0, 0, 0);
+    const float bb[4] = {bi.x, bi.y, bi.z, bi.w}, b22[4] = {b2.x, b2.y, b2.z, b2.w};
+    const float rr[4] = {rb[q].x, rb[q].y, rb[q].z, rb[q].w}, aa[4] = {ra[q].x, ra[q].y, ra[q].z, ra[q].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float t = x[e];
+      if (a.bias) t += bb[e];
+      if (a.bias2) t += b22[e];
+      if (a.res) t = a.res_sub ? (rr[e] - t) : (t + rr[e]);
+      if (a.accin) t = aa[e] + t;
+      if (a.out_div != 0.f) t = t / a.out_div;
+      out[4 * q + e] = t;
+    }
+  }
+  const long long o = (long long)b * a.y_bs + (long long)prow * a.y_ld + cg0;
+  if (a.y_raw) {
+    float4* p = reinterpret_cast<float4*>(a.y_raw + o);
+#pragma unroll
+    for (int q = 0; q < Q; ++q) p[q] = make_float4(out[4 * q], out[4 * q + 1], out[4 * q + 2], out[4 * q + 3]);
+  }
+  float4* p = reinterpret_cast<float4*>(a.y + o);
+#pragma unroll
+  for (int q = 0; q < Q; ++q)
+    p[q] = make_float4(act_apply(out[4 * q], a.out_act, a.out_slope), act_apply(out[4 * q + 1], a.out_act, a.out_slope),
+                       act_apply(out[4 * q + 2], a.out_act, a.out_slope),
+                       act_apply(out[4 * q + 3], a.out_act, a.out_slope));
+}
+
+struct TileCoord {
+  int b, s, nt, mt;
+};
+__device__ __forceinline__ TileCoord tile_coord(int tile, int nslices, int ntiles, int tiles_m) {
+  TileCoord c;
+  c.mt = tile % tiles_m;
+  int r = tile / tiles_m;
+  c.nt = r % ntiles;
+  r /= ntiles;
+  c.s = r % nslices;
+  c.b = r / nslices;
+  return c;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_conv_kernel(const __grid_constant__ ConvArgs a, const __grid_constant__ TcMaps maps, TcPlan g) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const int BN = a.bn, CB = a.cb;
+  const int nblk = a.C_in / CB;
+  const int MT = g.msub * kTM;
+  const uint32_t LBO_A = (uint32_t)g.arows_pad * 16u;
+  const uint32_t LBO_B = (uint32_t)BN * 16u;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t sbase = ptx::smem_u32(smem);
+  const uint32_t bar0 = sbase + g.off_bar;
+  // barriers: A_FULL[2] A_EMPTY[2] STG_FULL[4] STG_EMPTY[4] ACC_FULL[2] ACC_EMPTY[2] EPI_FULL[4] DRAIN
+  //           B_FULL[stages] B_EMPTY[stages], then the TMEM address slot
+  const uint32_t A_FULL = bar0, A_EMPTY = bar0 + 16, STG_FULL = bar0 + 32, STG_EMPTY = bar0 + 64;
+  const uint32_t ACC_FULL = bar0 + 96, ACC_EMPTY = bar0 + 112, EPI_FULL = bar0 + 128, DRAIN = bar0 + 160;
+  const uint32_t W_FULL = bar0 + 168;
+  const uint32_t B_FULL = bar0 + 176, B_EMPTY = B_FULL + 8u * g.stages;
+  uint32_t* tmem_slot = (uint32_t*)(smem + g.off_bar + 8 * (22 + 2 * g.stages));
+  auto a_plane = [&](int buf, int lo) { return sbase + g.off_a + (uint32_t)(2 * buf + lo) * g.a_plane; };
+  auto b_plane = [&](int st, int lo) { return sbase + g.off_b + (uint32_t)(2 * st + lo) * g.b_plane; };
+  auto stg = [&](int sb) { return g.off_stg + (uint32_t)sb * g.stg_bytes; };  // offset from smem
+  const uint32_t slot_span = kSlotBytes * (g.acc_slot ? 2u : 1u);
+  auto slot_main = [&](int s) { return g.off_epi + (uint32_t)s * slot_span; };
+  auto slot_aux = [&](int s) { return g.off_epi + (uint32_t)s * slot_span + kSlotBytes; };
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(A_FULL + 8 * i, 128);
+      ptx::mbar_init(A_EMPTY + 8 * i, 1);
+      ptx::mbar_init(ACC_FULL + 8 * i, 1);
+      ptx::mbar_init(ACC_EMPTY + 8 * i, 128);
+    }
+    for (int i = 0; i < 4; ++i) {
+      ptx::mbar_init(STG_FULL + 8 * i, 1);
+      ptx::mbar_init(STG_EMPTY + 8 * i, 128);
+      ptx::mbar_init(EPI_FULL + 8 * i, 1);
+    }
+    ptx::mbar_init(DRAIN, 1);
+    ptx::mbar_init(W_FULL, 1);
+    for (int i = 0; i < g.stages; ++i) {
+      ptx::mbar_init(B_FULL + 8 * i, 1);
+      ptx::mbar_init(B_EMPTY + 8 * i, 1);
+    }
+    ptx::fence_mbar_init();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(ptx::smem_u32(tmem_slot), g.tmem_cols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------ weight producer
+    if (lane == 0 && g.w_res) {
+      // whole packed tensor once per CTA (n-tile 0 is the only n-tile)
+      ptx::mbar_expect_tx(W_FULL, g.w_bytes);
+      const uint8_t* src = reinterpret_cast<const uint8_t*>(a.wpk);
+      for (uint32_t o = 0; o < g.w_bytes; o += 32768u)
+        ptx::bulk_g2s(sbase + g.off_w + o, src + o, min(32768u, g.w_bytes - o), W_FULL);
+      ptx::mbar_wait(W_FULL, 0, kWaitNs);  // never exit with the copy in flight
+    } else if (lane == 0) {
+      const size_t blk_elems = 2u * (size_t)CB * BN;
+      int ks = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < g.total_tiles && ok; tile += gridDim.x) {
+        const TileCoord c = tile_coord(tile, a.nslices, g.ntiles, g.tiles_m);
+        const ConvSlice& S = a.sl[c.s];
+        if (c.mt * MT >= S.rows) continue;
+        for (int kb = 0; kb < nblk && ok; ++kb)
+          for (int j = 0; j < S.ntaps; ++j, ++ks) {
+            const int st = ks % g.stages, round = ks / g.stages;
+            if (!ptx::mbar_wait(B_EMPTY + 8 * st, (round & 1) ^ 1, kWaitNs)) {
+              ok = false;
+              atomicExch(a.err, 1);
+              break;
+            }
+            const uint16_t* src = a.wpk + ((size_t)((S.wtap0 + j) * g.ntiles + c.nt) * nblk + kb) * blk_elems;
+            ptx::mbar_expect_tx(B_FULL + 8 * st, 2u * g.b_plane);
+            ptx::bulk_g2s(b_plane(st, 0), src, g.b_plane, B_FULL + 8 * st);
+            ptx::bulk_g2s(b_plane(st, 1), src + (size_t)CB * BN, g.b_plane, B_FULL + 8 * st);
+          }
+      }
+      for (int k = (ks > g.stages ? ks - g.stages : 0); k < ks; ++k)  // no copy left in flight
+        ptx::mbar_wait(B_FULL + 8 * (k % g.stages), (k / g.stages) & 1, kWaitNs);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = ptx::idesc_bf16_f32(kTM, BN);
+      int ks = 0, ab = 0, it = 0;
+      bool ok = true;
+      if (g.w_res && !ptx::mbar_wait(W_FULL, 0, kWaitNs)) {
+        ok = false;
+        atomicExch(a.err, 10);
+      }
+      for (int tile = blockIdx.x; tile < g.total_tiles && ok; tile += gridDim.x) {
+        const TileCoord c = tile_coord(tile, a.nslices, g.ntiles, g.tiles_m);
+        const ConvSlice& S = a.sl[c.s];
+        if (c.mt * MT >= S.rows) continue;
+        const int set = it % g.nacc;
+        if (!ptx::mbar_wait(ACC_EMPTY + 8 * set, ((it / g.nacc) & 1) ^ 1, kWaitNs)) {
+          ok = false;
+          atomicExch(a.err, 2);
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t dbase = tmem + (uint32_t)(set * g.msub * BN);
+        const int span = (S.ntaps - 1) * S.tap_step;
+        const int shift = span < 0 ? -span : 0;
+        bool first = true;
+        for (int kb = 0; kb < nblk && ok; ++kb, ++ab) {
+          const int buf = ab & 1;
+          if (!ptx::mbar_wait(A_FULL + 8 * buf, (ab >> 1) & 1, kWaitNs)) {
+            ok = false;
+            atomicExch(a.err, 3);
+            break;
+          }
+          for (int j = 0; j < S.ntaps; ++j, ++ks) {
+            const int st = ks % g.stages, round = ks / g.stages;
+            uint32_t bhi, blo;
+            if (g.w_res) {
+              bhi = sbase + g.off_w + (uint32_t)((S.wtap0 + j) * nblk + kb) * 2u * g.b_plane;
+              blo = bhi + g.b_plane;
+            } else {
+              if (!ptx::mbar_wait(B_FULL + 8 * st, round & 1, kWaitNs)) {
+                ok = false;
+                atomicExch(a.err, 4);
+                break;
+              }
+              ptx::tc_fence_after();
+              bhi = b_plane(st, 0);
+              blo = b_plane(st, 1);
+            }
+            const uint32_t rowoff = (uint32_t)(j * S.tap_step + shift);
+            for (int kk = 0; kk < CB / 16; ++kk) {
+              const uint32_t ko_b = (uint32_t)(2 * kk) * LBO_B;
+              const uint64_t dbh = ptx::smem_desc(bhi + ko_b, LBO_B, 128);
+              const uint64_t dbl = ptx::smem_desc(blo + ko_b, LBO_B, 128);
+              for (int sub = 0; sub < g.msub; ++sub) {
+                const uint32_t ao = (uint32_t)(2 * kk) * LBO_A + (rowoff + (uint32_t)(sub * kTM)) * 16u;
+                const uint64_t dah = ptx::smem_desc(a_plane(buf, 0) + ao, LBO_A, 128);
+                const uint64_t dal = ptx::smem_desc(a_plane(buf, 1) + ao, LBO_A, 128);
+                const uint32_t d = dbase + (uint32_t)(sub * BN);
+                ptx::mma_bf16(d, dah, dbh, idesc, first ? 0u : 1u);
+                ptx::mma_bf16(d, dah, dbl, idesc, 1u);
+                ptx::mma_bf16(d, dal, dbh, idesc, 1u);
+              }
+              first = false;
+            }
+            if (!g.w_res) ptx::mma_commit(B_EMPTY + 8 * st);
+          }
+          if (ok) ptx::mma_commit(A_EMPTY + 8 * buf);
+        }
+        if (ok) ptx::mma_commit(ACC_FULL + 8 * set);
+        ++it;
+      }
+      ptx::mma_commit(DRAIN);
+      ptx::mbar_wait(DRAIN, 0, kWaitNs);
+    }
+    __syncwarp();
+  } else if (warp == 2) {
+    // ------------------------------------------------ activation loader (TMA)
+    if (lane == 0) {
+      const uint32_t bytes = (uint32_t)g.nbox * g.box_rows * CB * 4u;
+      int ab = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < g.total_tiles && ok; tile += gridDim.x) {
+        const TileCoord c = tile_coord(tile, a.nslices, g.ntiles, g.tiles_m);
+        const ConvSlice& S = a.sl[c.s];
+        const int t0 = c.mt * MT;
+        if (t0 >= S.rows) continue;
+        const int span = (S.ntaps - 1) * S.tap_step;
+        const int r_start = t0 + S.tap_base + (span < 0 ? span : 0);
+        for (int kb = 0; kb < nblk; ++kb, ++ab) {
+          const int sb = ab % g.nstg;
+          if (!ptx::mbar_wait(STG_EMPTY + 8 * sb, ((ab / g.nstg) & 1) ^ 1, kWaitNs)) {
+            ok = false;
+            atomicExch(a.err, 5);
+            break;
+          }
+          ptx::mbar_expect_tx(STG_FULL + 8 * sb, bytes);
+          for (int i = 0; i < g.nbox; ++i)
+            ptx::tma_load_3d(sbase + stg(sb) + (uint32_t)i * g.box_rows * CB * 4u, &maps.a, S.ci_off + kb * CB,
+                             r_start + i * g.box_rows, c.b, STG_FULL + 8 * sb);
+        }
+      }
+      for (int k = (ab > g.nstg ? ab - g.nstg : 0); k < ab; ++k)  // no copy left in flight
+        ptx::mbar_wait(STG_FULL + 8 * (k % g.nstg), (k / g.nstg) & 1, kWaitNs);
+    }
+  } else if (warp < 7) {
+    // ------------------------------------------------ converters
+    const int tp = threadIdx.x - 96;
+    const int c4n = CB / 4;
+    int ab = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < g.total_tiles && ok; tile += gridDim.x) {
+      const TileCoord c = tile_coord(tile, a.nslices, g.ntiles, g.tiles_m);
+      const ConvSlice& S = a.sl[c.s];
+      if (c.mt * MT >= S.rows) continue;
+      const int span = (S.ntaps - 1) * S.tap_step;
+      const int arows = MT + (span < 0 ? -span : span);
+      const int total = arows * c4n;
+      for (int kb = 0; kb < nblk; ++kb, ++ab) {
+        const int sb = ab % g.nstg, buf = ab & 1;
+        if (!ptx::mbar_wait(STG_FULL + 8 * sb, (ab / g.nstg) & 1, kWaitNs) ||
+            !ptx::mbar_wait(A_EMPTY + 8 * buf, ((ab >> 1) & 1) ^ 1, kWaitNs)) {
+          ok = false;
+          atomicExch(a.err, 6);
+          break;
+        }
+        const uint32_t src = sbase + stg(sb);
+        const uint32_t phi = a_plane(buf, 0), plo = a_plane(buf, 1);
+#pragma unroll 4
+        for (int e = tp; e < total; e += 128) {
+          const int r = e / c4n, c4 = e - r * c4n;
+          float4 v = ptx::lds128(src + (uint32_t)e * 16u);
+          if (a.in_act) {
+            v.x = act_apply(v.x, a.in_act, a.in_slope);
+            v.y = act_apply(v.y, a.in_act, a.in_slope);
+            v.z = act_apply(v.z, a.in_act, a.in_slope);
+            v.w = act_apply(v.w, a.in_act, a.in_slope);
+          }
+          __nv_bfloat16 h0, h1, h2, h3, l0, l1, l2, l3;
+          split_bf16(v.x, h0, l0);
+          split_bf16(v.y, h1, l1);
+          split_bf16(v.z, h2, l2);
+          split_bf16(v.w, h3, l3);
+          const uint32_t off = (uint32_t)(c4 >> 1) * LBO_A + (uint32_t)r * 16u + (uint32_t)(c4 & 1) * 8u;
+          ptx::sts64(phi + off, pack_bf16x2(h0, h1), pack_bf16x2(h2, h3));
+          ptx::sts64(plo + off, pack_bf16x2(l0, l1), pack_bf16x2(l2, l3));
+        }
+        ptx::fence_proxy_async_smem();
+        ptx::mbar_arrive(A_FULL + 8 * buf);
+        ptx::mbar_arrive(STG_EMPTY + 8 * sb);
+      }
+    }
+  } else {
+    // ------------------------------------------------ epilogue
+    const int wq = warp & 3;
+    const int r_in = wq * 32 + lane;  // row within a 128-row subtile
+    int it = 0;
+    if (g.tma_epi) {
+      const bool leader = (warp == 7 && lane == 0);
+      const int nch = BN / kEpiCols;
+      const int spt = g.msub * nch;
+      const int ntile_cta = (g.total_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+      const int total_steps = ntile_cta * spt;
+      int issued = 0;
+      auto issue = [&](int f) {
+        if (f >= total_steps) return;
+        issued = f + 1;
+        const int sl = f % g.nslot;
+        const TileCoord c = tile_coord(blockIdx.x + (f / spt) * gridDim.x, a.nslices, g.ntiles, g.tiles_m);
+        const ConvSlice& S = a.sl[c.s];
+        const int q = f % spt, sub = q / nch, ch = q % nch;
+        const int row0 = c.mt * MT + sub * kTM, col0 = S.co_off + c.nt * BN + ch * kEpiCols;
+        ptx::bulk_wait_read0();  // earlier stores have finished reading their slots
+        const uint32_t bytes = (a.res ? kSlotBytes : 0u) + (a.accin ? kSlotBytes : 0u);
+        ptx::mbar_expect_tx(EPI_FULL + 8 * sl, bytes);
+        if (g.ephase) {  // transposed-conv phase p: rows q*up + p through the 4-D view
+          if (a.res) ptx::tma_load_4d(sbase + slot_main(sl), &maps.res, col0, S.out_r0, row0, c.b, EPI_FULL + 8 * sl);
+          if (a.accin)
+            ptx::tma_load_4d(sbase + slot_aux(sl), &maps.acc, col0, S.out_r0, row0, c.b, EPI_FULL + 8 * sl);
+        } else {
+          if (a.res) ptx::tma_load_3d(sbase + slot_main(sl), &maps.res, col0, row0, c.b, EPI_FULL + 8 * sl);
+          if (a.accin) ptx::tma_load_3d(sbase + slot_aux(sl), &maps.acc, col0, row0, c.b, EPI_FULL + 8 * sl);
+        }
+      };
+      if (g.off_bias) {  // stage the bias vector once per CTA
+        for (int i = r_in; i < g.bias_n; i += 128) {
+          const float bv = a.bias[i];
+          asm volatile("st.shared.f32 [%0], %1;" ::"r"(sbase + g.off_bias + 4u * (uint32_t)i), "f"(bv) : "memory");
+        }
+        ptx::named_bar(3, 128);
+      }
+      if (leader)
+        for (int f = 0; f < g.nslot - 1; ++f) issue(f);
+      int e = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < g.total_tiles && ok; tile += gridDim.x) {
+        const TileCoord c = tile_coord(tile, a.nslices, g.ntiles, g.tiles_m);
+        const ConvSlice& S = a.sl[c.s];
+        const int set = it % g.nacc;
+        // all four epilogue warps agree on the outcome (bar.red.and)
+        const bool got = ptx::named_bar_and(1, 128, ptx::mbar_wait(ACC_FULL + 8 * set, (it / g.nacc) & 1, kWaitNs));
+        if (!got) {
+          if (lane == 0) atomicExch(a.err, 7);
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t dbase = tmem + (uint32_t)(set * g.msub * BN) + ((uint32_t)(wq * 32) << 16);
+        for (int q = 0; q < spt; ++q, ++e) {
+          if (leader) issue(e + g.nslot - 1);
+          const int sl = e % g.nslot;
+          const int sub = q / nch, ch = q % nch;
+          const bool in = ptx::named_bar_and(1, 128, ptx::mbar_wait(EPI_FULL + 8 * sl, (e / g.nslot) & 1, kWaitNs));
+          float v[32];
+          ptx::tmem_ld32(dbase + (uint32_t)(sub * BN + ch * kEpiCols), v);
+          if (q == spt - 1) {
+            ptx::tc_fence_before();
+            ptx::mbar_arrive(ACC_EMPTY + 8 * set);
+          }
+          if (!in) {
+            if (lane == 0) atomicExch(a.err, 8);
+            ok = false;
+            break;
+          }
+          const int col0 = S.co_off + c.nt * BN + ch * kEpiCols;
+          const uint32_t mainp = sbase + slot_main(sl) + (uint32_t)r_in * 128u;
+          const uint32_t auxp = sbase + slot_aux(sl) + (uint32_t)r_in * 128u;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t off = (uint32_t)((j ^ (r_in & 7)) << 4);  // 128B swizzle of the TMA box
+            float x[4] = {v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]};
+            if (a.bias) {
+              const float4 t = g.off_bias ? ptx::lds128(sbase + g.off_bias + (uint32_t)(col0 + 4 * j) * 4u)
+                                          : __ldg(reinterpret_cast<const float4*>(a.bias + col0) + j);
+              x[0] += t.x; x[1] += t.y; x[2] += t.z; x[3] += t.w;
+            }
+            if (a.bias2) {
+              const float4 t = __ldg(reinterpret_cast<const float4*>(a.bias2 + (long long)c.b * a.bias2_bs + col0) + j);
+              x[0] += t.x; x[1] += t.y; x[2] += t.z; x[3] += t.w;
+            }
+            if (a.res) {
+              const float4 t = ptx::lds128(mainp + off);
+              const float r4[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+              for (int k = 0; k < 4; ++k) x[k] = a.res_sub ? (r4[k] - x[k]) : (x[k] + r4[k]);
+            }
+            if (a.accin) {
+              const float4 t = ptx::lds128(auxp + off);
+              x[0] = t.x + x[0]; x[1] = t.y + x[1]; x[2] = t.z + x[2]; x[3] = t.w + x[3];
+            }
+            if (a.out_div != 0.f) {
+#pragma unroll
+              for (int k = 0; k < 4; ++k) x[k] = x[k] / a.out_div;
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) x[k] = act_apply(x[k], a.out_act, a.out_slope);
+            ptx::sts128(mainp + off, make_float4(x[0], x[1], x[2], x[3]));
+          }
+          ptx::fence_proxy_async_smem();
+          ptx::named_bar(2, 128);
+          if (leader) {
+            if (g.ephase)
+              ptx::tma_store_4d(&maps.y, col0, S.out_r0, c.mt * MT + sub * kTM, c.b, sbase + slot_main(sl));
+            else
+              ptx::tma_store_3d(&maps.y, col0, c.mt * MT + sub * kTM, c.b, sbase + slot_main(sl));
+            ptx::bulk_commit();
+          }
+        }
+        ++it;
+      }
+      if (leader) {
+        // no TMA load left in flight into a slot, no store still reading one
+        for (int f = (issued > g.nslot ? issued - g.nslot : 0); f < issued; ++f)
+          ptx::mbar_wait(EPI_FULL + 8 * (f % g.nslot), (f / g.nslot) & 1, kWaitNs);
+        ptx::bulk_wait0();
+      }
+    } else {
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < g.total_tiles && ok; tile += gridDim.x) {
+        const TileCoord c = tile_coord(tile, a.nslices, g.ntiles, g.tiles_m);
+        const ConvSlice& S = a.sl[c.s];
+        const int t0 = c.mt * MT;
+        if (t0 >= S.rows) continue;
+        const int set = it % g.nacc;
+        bool got = ptx::mbar_wait(ACC_FULL + 8 * set, (it / g.nacc) & 1, kWaitNs);
+        got = __all_sync(0xffffffffu, got);
+        if (!got) {
+          if (lane == 0) atomicExch(a.err, 9);
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t dbase = tmem + (uint32_t)(set * g.msub * BN) + ((uint32_t)(wq * 32) << 16);
+        for (int sub = 0; sub < g.msub; ++sub) {
+          const int row = t0 + sub * kTM + r_in;
+          const bool valid = row < S.rows;
+          const int prow = row * a.out_rs + S.out_r0;
+          int col = 0;
+          for (; col + 32 <= BN; col += 32) {
+            float v[32];
+            ptx::tmem_ld32(dbase + (uint32_t)(sub * BN + col), v);
+            if (valid) epi_direct<32>(a, c.b, prow, S.co_off + c.nt * BN + col, v, g.vec);
+          }
+          if (col < BN) {
+            float v[16];
+            ptx::tmem_ld16(dbase + (uint32_t)(sub * BN + col), v);
+            if (valid) epi_direct<16>(a, c.b, prow, S.co_off + c.nt * BN + col, v, g.vec);
+          }
+        }
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(ACC_EMPTY + 8 * set);
+        ++it;
+      }
+    }
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  if (warp == 1) ptx::tmem_dealloc(tmem, g.tmem_cols);
+}
+
+// ----------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  if (!fn) throw Error{kErrCuda, "cuTensorMapEncodeTiled is not available from the driver"};
+  return fn;
+}
+
+// fp32 3-D map [B][rows][width] with row stride `ld` and batch stride `bs` (elements).
+static void make_map(CUtensorMap* m, const float* base, int width, int rows, int B, long long ld, long long bs,
+                     int box_w, int box_r, bool swz128) {
+  cuuint64_t dims[3] = {(cuuint64_t)width, (cuuint64_t)rows, (cuuint64_t)B};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * 4, (cuuint64_t)bs * 4};
+  cuuint32_t box[3] = {(cuuint32_t)box_w, (cuuint32_t)box_r, 1};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)base, dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           swz128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw Error{kErrCuda, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")"};
+}
+
+// fp32 4-D epilogue view of a transposed conv output: element (c, p, q, b) is
+// row q*up + p, channel c of batch item b.  Box: 32 channels x 1 phase x 128 q.
+static void make_phase_map(CUtensorMap* m, const float* base, int width, int up, int q_rows, int B, long long ld,
+                           long long bs) {
+  cuuint64_t dims[4] = {(cuuint64_t)width, (cuuint64_t)up, (cuuint64_t)q_rows, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)ld * 4, (cuuint64_t)ld * 4 * up, (cuuint64_t)bs * 4};
+  cuuint32_t box[4] = {(cuuint32_t)kEpiCols, 1, (cuuint32_t)kTM, 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  CUresult r = encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void*)base, dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw Error{kErrCuda, "cuTensorMapEncodeTiled (phase view) failed (" + std::to_string((int)r) + ")"};
+}
+
+static int g_num_sms = 0;
+
+static TcPlan tc_plan(const ConvArgs& a) {
+  TcPlan g{};
+  int halo = 0, maxrows = 0, minrows = 1 << 30;
+  for (int s = 0; s < a.nslices; ++s) {
+    int span = (a.sl[s].ntaps - 1) * a.sl[s].tap_step;
+    halo = std::max(halo, span < 0 ? -span : span);
+    maxrows = std::max(maxrows, a.sl[s].rows);
+    minrows = std::min(minrows, a.sl[s].rows);
+  }
+  auto al16 = [](const void* p) { return ((uintptr_t)p & 15) == 0; };
+  bool v = (a.y_ld % 4 == 0) && (a.y_bs % 4 == 0) && al16(a.y) && (!a.y_raw || al16(a.y_raw));
+  v = v && (!a.res || (a.res_ld % 4 == 0 && a.res_bs % 4 == 0 && al16(a.res)));
+  v = v && (!a.accin || (a.acc_ld % 4 == 0 && a.acc_bs % 4 == 0 && al16(a.accin)));
+  v = v && (!a.bias || al16(a.bias)) && (!a.bias2 || (a.bias2_bs % 4 == 0 && al16(a.bias2)));
+  for (int s = 0; s < a.nslices; ++s) v = v && (a.sl[s].co_off % 4 == 0);
+  g.vec = v ? 1 : 0;
+  // TMA epilogue: plain row mapping, whole 32-column steps, every tile valid.
+  // Transposed convs qualify when every phase has the same row count (output
+  // length a multiple of the stride): phase p's rows q*up+p are then a box of
+  // the 4-D view {channel, phase, q, batch}.
+  g.tma_epi = v && a.bn % kEpiCols == 0 && !a.y_raw && minrows == maxrows &&
+              (a.out_rs == 1 || a.nslices == a.out_rs);
+  g.ephase = a.out_rs > 1 ? 1 : 0;
+  for (int s = 0; s < a.nslices; ++s) g.tma_epi = g.tma_epi && a.sl[s].out_r0 == (a.out_rs > 1 ? s : 0);
+
+  const uint32_t limit = 227u * 1024u;
+  g.b_plane = (uint32_t)a.cb * a.bn * 2u;
+  const int acc_slot = (g.tma_epi && a.accin) ? 1 : 0;
+  const uint32_t slot_span = kSlotBytes * (acc_slot ? 2u : 1u);
+  int width = 0, ntaps_max = 1;
+  for (int s = 0; s < a.nslices; ++s) {
+    width = std::max(width, a.sl[s].co_off + a.C_out);
+    ntaps_max = std::max(ntaps_max, a.sl[s].ntaps);
+  }
+  const uint32_t bias_bytes = (g.tma_epi && a.bias && width <= 2048) ? (uint32_t)((width * 4 + 127) & ~127) : 0u;
+  // Candidate pipelines, best first.  Narrow convs (bn <= 64) are HBM-bound:
+  // short tiles with deep activation/epilogue pipelines keep ~100 KB in
+  // flight per SM.  Wide convs are tensor-bound: tall tiles reuse each
+  // weight stage, and when one K block already keeps the MMA busy for
+  // thousands of cycles a single staging buffer leaves room for more
+  // weight stages.
+  int taps_total = 0;
+  for (int s = 0; s < a.nslices; ++s) taps_total = std::max(taps_total, a.sl[s].wtap0 + a.sl[s].ntaps);
+  const uint32_t w_all = (uint32_t)taps_total * a.C_in * a.C_out * 4u;  // packed hi + lo
+  const bool can_res = (a.C_out == a.bn) && w_all <= 120u * 1024u;
+  // Candidate pipelines, best first.  Narrow convs (bn <= 64) are HBM-bound
+  // and their weights are small: keep the whole packed weight tensor resident
+  // (one bulk copy per CTA, no per-stage round trips), 256-row tiles, double
+  // activation staging and epilogue slots.  Wide convs are tensor-bound: tall
+  // tiles reuse each streamed weight stage, and when one K block already keeps
+  // the MMA busy for thousands of cycles a single staging buffer leaves room
+  // for more weight stages.
+  struct Cand {
+    int msub, nacc, nstg, nslot, min_stages, res;
+  };
+  Cand cands[12];
+  int ncand = 0;
+  if (a.bn <= 64) {
+    const Cand c[] = {{2, 2, 2, 2, 0, 1}, {2, 2, 1, 2, 0, 1}, {2, 2, 1, 1, 0, 1}, {1, 2, 2, 2, 0, 1},
+                      {2, 2, 2, 2, 6, 0}, {2, 2, 1, 2, 6, 0}, {2, 2, 1, 1, 4, 0}, {1, 2, 2, 2, 2, 0},
+                      {1, 1, 1, 1, 2, 0}};
+    for (const Cand& x : c)
+      if (!x.res || can_res) cands[ncand++] = x;
+  } else {
+    const long long blk_clk = (long long)ntaps_max * (a.cb / 16) * 2 * 3 * (a.bn / 2);
+    const int ns = blk_clk >= 6000 ? 1 : 2;
+    const Cand c[] = {{4, 2, ns, 2, 4, 0}, {2, 2, ns, 2, 4, 0}, {2, 1, ns, 2, 4, 0}, {2, 2, 1, 1, 3, 0},
+                      {2, 1, 1, 1, 3, 0},  {1, 2, 2, 2, 2, 0},  {1, 1, 1, 1, 2, 0}};
+    for (const Cand& x : c) cands[ncand++] = x;
+  }
+  auto try_cand = [&](const Cand& cd, int need_stages) -> bool {
+    int cols = 32;
+    while (cols < cd.nacc * cd.msub * a.bn) cols <<= 1;
+    if (cols > 512) return false;
+    const int arows = cd.msub * kTM + halo;
+    const int pad = arows + ((1 - arows % 8) + 8) % 8;  // == 1 (mod 8): spreads chunk planes over banks
+    const uint32_t a_plane = (uint32_t)a.cb * pad * 2u;
+    const int nbox = (arows + 255) / 256;
+    // rows per TMA box: <= 256, multiple of 8 so every box lands 128B-aligned
+    const int box_rows = std::min(256, ((arows + nbox - 1) / nbox + 7) / 8 * 8);
+    const uint32_t stg_bytes = (uint32_t)nbox * box_rows * a.cb * 4u;
+    const int nslot = g.tma_epi ? cd.nslot : 0;
+    uint32_t off = 0;
+    const uint32_t off_epi = off;
+    off += (uint32_t)nslot * slot_span;  // slots first: 1024-aligned for the 128B swizzle
+    const uint32_t off_bias = bias_bytes ? off : 0u;
+    off += bias_bytes;
+    off = (off + 1023u) & ~1023u;
+    const uint32_t off_a = off;
+    off += 4u * a_plane;
+    off = (off + 1023u) & ~1023u;
+    const uint32_t off_stg = off;
+    off += (uint32_t)cd.nstg * stg_bytes;
+    off = (off + 127u) & ~127u;
+    const uint32_t off_w = off;
+    if (cd.res) off += w_all;  // resident weights replace the streaming ring
+    off = (off + 127u) & ~127u;
+    const uint32_t off_b = off;
+    int stages = cd.res ? 1 : 8;
+    const uint32_t ring = cd.res ? 0u : 2u * g.b_plane;
+    auto total = [&](int st) { return 1024u + off_b + (uint32_t)st * ring + 8u * (22 + 2 * st) + 16u; };
+    while (stages > 2 && total(stages) > limit) --stages;
+    if (total(stages) > limit || (!cd.res && stages < need_stages)) return false;
+    g.w_res = cd.res;
+    g.off_w = off_w;
+    g.w_bytes = cd.res ? w_all : 0u;
+    g.msub = cd.msub;
+    g.nacc = cd.nacc;
+    g.arows_pad = pad;
+    g.a_plane = a_plane;
+    g.tmem_cols = (uint32_t)cols;
+    g.nbox = nbox;
+    g.box_rows = box_rows;
+    g.stg_bytes = stg_bytes;
+    g.nstg = cd.nstg;
+    g.nslot = nslot;
+    g.acc_slot = acc_slot;
+    g.off_epi = off_epi;
+    g.off_bias = off_bias;
+    g.bias_n = bias_bytes ? width : 0;
+    g.off_a = off_a;
+    g.off_stg = off_stg;
+    g.off_b = off_b;
+    g.stages = stages;
+    g.off_bar = off_b + (uint32_t)stages * ring;
+    g.smem_bytes = total(stages);
+    return true;
+  };
+  bool found = false;
+  for (int i = 0; i < ncand && !found; ++i) found = try_cand(cands[i], cands[i].min_stages);
+  for (int i = 0; i < ncand && !found; ++i) found = try_cand(cands[i], 2);
+  RVC_CHECK_ARG(found, "tc_conv: tile does not fit in shared memory");
+  g.tiles_m = cdiv(maxrows, g.msub * kTM);
+  g.ntiles = a.C_out / a.bn;
+  g.total_tiles = a.B * a.nslices * g.ntiles * g.tiles_m;
+  return g;
+}
+
+void launch_tc_conv(const ConvArgs& a, cudaStream_t st) {
+  RVC_CHECK_ARG(a.stride == 1, "tc_conv: stride must be 1 (use the strided view)");
+  RVC_CHECK_ARG(a.C_in % a.cb == 0 && a.C_out % a.bn == 0 && a.cb % 16 == 0 && a.bn % 16 == 0 && a.bn <= 256,
+                "tc_conv: channel tiling");
+  RVC_CHECK_ARG(a.x_ld % 4 == 0 && a.x_bs % 4 == 0 && ((uintptr_t)a.x & 15) == 0,
+                "tc_conv: input rows must be 16-byte aligned");
+  TcPlan g = tc_plan(a);
+  if (g.total_tiles == 0) return;
+  TcMaps maps;
+  memset(&maps, 0, sizeof(maps));
+  make_map(&maps.a, a.x, a.x_ld, a.T_in, a.B, a.x_ld, a.x_bs, a.cb, g.box_rows, false);
+  if (g.tma_epi) {
+    int width = 0;
+    for (int s = 0; s < a.nslices; ++s) width = std::max(width, a.sl[s].co_off + a.C_out);
+    const int rows = a.sl[0].rows;
+    if (g.ephase) {
+      make_phase_map(&maps.y, a.y, width, a.out_rs, rows, a.B, a.y_ld, a.y_bs);
+      if (a.res) make_phase_map(&maps.res, a.res, width, a.out_rs, rows, a.B, a.res_ld, a.res_bs);
+      if (a.accin) make_phase_map(&maps.acc, a.accin, width, a.out_rs, rows, a.B, a.acc_ld, a.acc_bs);
+    } else {
+      make_map(&maps.y, a.y, width, rows, a.B, a.y_ld, a.y_bs, kEpiCols, kTM, true);
+      if (a.res) make_map(&maps.res, a.res, width, rows, a.B, a.res_ld, a.res_bs, kEpiCols, kTM, true);
+      if (a.accin) make_map(&maps.acc, a.accin, width, rows, a.B, a.acc_ld, a.acc_bs, kEpiCols, kTM, true);
+    }
+  }
+  int dev = 0;
+  RVC_CUDA_TRY(cudaGetDevice(&dev));
+  static std::atomic<uint64_t> attr_done{0};  // the attribute is per device
+  if (dev < 64 && !(attr_done.load() & (1ull << dev))) {
+    RVC_CUDA_TRY(cudaFuncSetAttribute(tc_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    attr_done.fetch_or(1ull << dev);
+  }
+  if (g_num_sms == 0) RVC_CUDA_TRY(cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev));
+  const int grid = std::min(g.total_tiles, g_num_sms);
+  tc_conv_kernel<<<grid, kThreads, g.smem_bytes, st>>>(a, maps, g);
+  note_launch();
+  RVC_CUDA_TRY(cudaGetLastError());
+}
+
+}  // namespace rvc
