@@ -116,6 +116,45 @@ __device__ __forceinline__ void epi_direct(const ConvArgs& a, int b, int prow, i
                        act_apply(out[4 * q + 3], a.out_act, a.out_slope));
 }
 
+// Issues the BF16x3 MMAs of one weight stage: for each 16-wide k step and each
+// 128-row subtile, D += Ahi*Bhi + Ahi*Blo + Alo*Bhi.  Descriptors are built once
+// and advanced by adding encoded offsets (the start-address field holds
+// addr >> 4; shared addresses stay below 256 KB, so an add never carries out of
+// the 14-bit field), which keeps the single issuing thread at a few
+// instructions per MMA.
+template <int MSUB, int KK>
+__device__ __forceinline__ void issue_stage(uint32_t dbase, uint64_t dah0, uint64_t dal0, uint64_t dbh0,
+                                            uint64_t dbl0, uint32_t lbo_a, uint32_t lbo_b, int bn, uint32_t idesc,
+                                            bool first) {
+#pragma unroll
+  for (int kk = 0; kk < KK; ++kk) {
+    const uint64_t ka = (uint64_t)((2u * (uint32_t)kk * lbo_a) >> 4);
+    const uint64_t kb = (uint64_t)((2u * (uint32_t)kk * lbo_b) >> 4);
+#pragma unroll
+    for (int sub = 0; sub < MSUB; ++sub) {
+      const uint64_t sa = (uint64_t)(sub * kTM);  // 128 rows x 16 B, >> 4
+      const uint32_t d = dbase + (uint32_t)(sub * bn);
+      ptx::mma_bf16(d, dah0 + ka + sa, dbh0 + kb, idesc, (first && kk == 0) ? 0u : 1u);
+      ptx::mma_bf16(d, dah0 + ka + sa, dbl0 + kb, idesc, 1u);
+      ptx::mma_bf16(d, dal0 + ka + sa, dbh0 + kb, idesc, 1u);
+    }
+  }
+}
+
+__device__ __forceinline__ void issue_any(int msub, int kk, uint32_t dbase, uint64_t dah0, uint64_t dal0,
+                                          uint64_t dbh0, uint64_t dbl0, uint32_t lbo_a, uint32_t lbo_b, int bn,
+                                          uint32_t idesc, bool first) {
+#define RVC_ISSUE(M, K)                                                                    \
+  if (msub == M && kk == K) {                                                              \
+    issue_stage<M, K>(dbase, dah0, dal0, dbh0, dbl0, lbo_a, lbo_b, bn, idesc, first);      \
+    return;                                                                                \
+  }
+  RVC_ISSUE(1, 1) RVC_ISSUE(1, 2) RVC_ISSUE(1, 3) RVC_ISSUE(1, 4)
+  RVC_ISSUE(2, 1) RVC_ISSUE(2, 2) RVC_ISSUE(2, 3) RVC_ISSUE(2, 4)
+  RVC_ISSUE(4, 1) RVC_ISSUE(4, 2) RVC_ISSUE(4, 3) RVC_ISSUE(4, 4)
+#undef RVC_ISSUE
+}
+
 struct TileCoord {
   int b, s, nt, mt;
 };
@@ -268,21 +307,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               blo = b_plane(st, 1);
             }
             const uint32_t rowoff = (uint32_t)(j * S.tap_step + shift);
-            for (int kk = 0; kk < CB / 16; ++kk) {
-              const uint32_t ko_b = (uint32_t)(2 * kk) * LBO_B;
-              const uint64_t dbh = ptx::smem_desc(bhi + ko_b, LBO_B, 128);
-              const uint64_t dbl = ptx::smem_desc(blo + ko_b, LBO_B, 128);
-              for (int sub = 0; sub < g.msub; ++sub) {
-                const uint32_t ao = (uint32_t)(2 * kk) * LBO_A + (rowoff + (uint32_t)(sub * kTM)) * 16u;
-                const uint64_t dah = ptx::smem_desc(a_plane(buf, 0) + ao, LBO_A, 128);
-                const uint64_t dal = ptx::smem_desc(a_plane(buf, 1) + ao, LBO_A, 128);
-                const uint32_t d = dbase + (uint32_t)(sub * BN);
-                ptx::mma_bf16(d, dah, dbh, idesc, first ? 0u : 1u);
-                ptx::mma_bf16(d, dah, dbl, idesc, 1u);
-                ptx::mma_bf16(d, dal, dbh, idesc, 1u);
-              }
-              first = false;
-            }
+            const uint64_t dah0 = ptx::smem_desc(a_plane(buf, 0) + rowoff * 16u, LBO_A, 128);
+            const uint64_t dal0 = ptx::smem_desc(a_plane(buf, 1) + rowoff * 16u, LBO_A, 128);
+            const uint64_t dbh0 = ptx::smem_desc(bhi, LBO_B, 128);
+            const uint64_t dbl0 = ptx::smem_desc(blo, LBO_B, 128);
+            issue_any(g.msub, CB / 16, dbase, dah0, dal0, dbh0, dbl0, LBO_A, LBO_B, BN, idesc, first);
+            first = false;
             if (!g.w_res) ptx::mma_commit(B_EMPTY + 8 * st);
           }
           if (ok) ptx::mma_commit(A_EMPTY + 8 * buf);
@@ -381,6 +411,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int spt = g.msub * nch;
       const int ntile_cta = (g.total_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
       const int total_steps = ntile_cta * spt;
+      // prefetch distance: loads for step e + pdist are issued at step e; with
+      // nslot >= 3 that slot's last store is not the one just committed
+      const int pdist = g.nslot >= 3 ? g.nslot - 2 : g.nslot - 1;
       int issued = 0;
       auto issue = [&](int f) {
         if (f >= total_steps) return;
@@ -390,7 +423,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const ConvSlice& S = a.sl[c.s];
         const int q = f % spt, sub = q / nch, ch = q % nch;
         const int row0 = c.mt * MT + sub * kTM, col0 = S.co_off + c.nt * BN + ch * kEpiCols;
-        ptx::bulk_wait_read0();  // earlier stores have finished reading their slots
+        // the slot's previous store (step f - nslot) has finished reading it; the
+        // nslot - pdist - 1 newer stores may still be in flight
+        ptx::bulk_wait_read(g.nslot - pdist - 1);
         const uint32_t bytes = (a.res ? kSlotBytes : 0u) + (a.accin ? kSlotBytes : 0u);
         ptx::mbar_expect_tx(EPI_FULL + 8 * sl, bytes);
         if (g.ephase) {  // transposed-conv phase p: rows q*up + p through the 4-D view
@@ -410,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::named_bar(3, 128);
       }
       if (leader)
-        for (int f = 0; f < g.nslot - 1; ++f) issue(f);
+        for (int f = 0; f < pdist; ++f) issue(f);
       int e = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < g.total_tiles && ok; tile += gridDim.x) {
@@ -427,7 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tc_fence_after();
         const uint32_t dbase = tmem + (uint32_t)(set * g.msub * BN) + ((uint32_t)(wq * 32) << 16);
         for (int q = 0; q < spt; ++q, ++e) {
-          if (leader) issue(e + g.nslot - 1);
+          if (leader) issue(e + pdist);
           const int sl = e % g.nslot;
           const int sub = q / nch, ch = q % nch;
           const bool in = ptx::named_bar_and(1, 128, ptx::mbar_wait(EPI_FULL + 8 * sl, (e / g.nslot) & 1, kWaitNs));
@@ -642,16 +677,17 @@ static TcPlan tc_plan(const ConvArgs& a) {
   Cand cands[12];
   int ncand = 0;
   if (a.bn <= 64) {
-    const Cand c[] = {{2, 2, 2, 2, 0, 1}, {2, 2, 1, 2, 0, 1}, {2, 2, 1, 1, 0, 1}, {1, 2, 2, 2, 0, 1},
-                      {2, 2, 2, 2, 6, 0}, {2, 2, 1, 2, 6, 0}, {2, 2, 1, 1, 4, 0}, {1, 2, 2, 2, 2, 0},
-                      {1, 1, 1, 1, 2, 0}};
+    const Cand c[] = {{2, 2, 2, 4, 0, 1}, {2, 2, 2, 3, 0, 1}, {2, 2, 1, 3, 0, 1}, {2, 2, 1, 2, 0, 1},
+                      {1, 2, 2, 3, 0, 1}, {2, 2, 2, 3, 6, 0}, {2, 2, 1, 3, 6, 0}, {2, 2, 1, 2, 4, 0},
+                      {1, 2, 2, 2, 2, 0}, {1, 1, 1, 1, 2, 0}};
     for (const Cand& x : c)
       if (!x.res || can_res) cands[ncand++] = x;
   } else {
     const long long blk_clk = (long long)ntaps_max * (a.cb / 16) * 2 * 3 * (a.bn / 2);
     const int ns = blk_clk >= 6000 ? 1 : 2;
-    const Cand c[] = {{4, 2, ns, 2, 4, 0}, {2, 2, ns, 2, 4, 0}, {2, 1, ns, 2, 4, 0}, {2, 2, 1, 1, 3, 0},
-                      {2, 1, 1, 1, 3, 0},  {1, 2, 2, 2, 2, 0},  {1, 1, 1, 1, 2, 0}};
+    const Cand c[] = {{4, 2, ns, 3, 4, 0}, {2, 2, ns, 3, 4, 0}, {2, 1, ns, 3, 4, 0}, {2, 2, 1, 3, 3, 0},
+                      {2, 2, 1, 2, 3, 0},  {2, 1, 1, 2, 3, 0},  {2, 1, 1, 1, 3, 0}, {1, 2, 2, 2, 2, 0},
+                      {1, 1, 1, 1, 2, 0}};
     for (const Cand& x : c) cands[ncand++] = x;
   }
   auto try_cand = [&](const Cand& cd, int need_stages) -> bool {
