@@ -116,6 +116,19 @@ int32_t rvc_cuda_gating(int64_t ctx, const float* x, const float* g, int32_t B, 
 int32_t rvc_cuda_rel_attention(int64_t ctx, const float* q, const float* k, const float* v,
                                const float* emb_k, const float* emb_v, int32_t B, int32_t heads,
                                int32_t kc, int32_t P, int32_t window, float* y);
+/* rvc_cuda_rel_attention for callers that cannot allocate device memory: no
+ * counterpart in the reference.  Same math and layouts, but q, k, v, emb_k,
+ * emb_v and y are DEVICE pointers the caller owns, and the intermediates live in
+ * one fixed 8 MiB array in device global memory (held by every GPU that loads
+ * the library until exit), so the call makes no cudaMalloc/cudaFree.  Requires
+ * 4*B*heads*kc*P <= 2^21, else RVC_E_ARG.  Asynchronous on the context stream
+ * (rvc_cuda_sync waits).  All calls on a device share the array: calls on
+ * different streams of one device race; calls on one context run in order.
+ * The first call on a device resolves the array's address (with that device
+ * current) and should come before any stream capture on it. */
+int32_t rvc_cuda_rel_attention_noalloc(int64_t ctx, const float* q, const float* k, const float* v,
+                                       const float* emb_k, const float* emb_v, int32_t B, int32_t heads,
+                                       int32_t kc, int32_t P, int32_t window, float* y);
 /* im2col of a 1-D conv: x[B,C,T] -> cols[B,oL,C*K] (column index c*K+k).
  * Replaces BatchRunner.im2col_1d (runtime/vulkan_ops.py:2727). */
 int32_t rvc_cuda_im2col1d(int64_t ctx, const float* x, int32_t B, int32_t C, int32_t T, int32_t K,

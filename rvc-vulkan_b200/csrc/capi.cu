@@ -84,6 +84,9 @@ int32_t on_synth(int64_t model, F&& f) {
 
 }  // namespace
 
+// Handle lookup for entry points defined in other translation units.
+rvc::Context* rvc_capi_context(int64_t h) { return get_ctx(h); }
+
 extern "C" {
 
 int32_t rvc_cuda_version(void) { return 100; }

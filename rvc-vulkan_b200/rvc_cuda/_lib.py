@@ -77,6 +77,7 @@ _SIGS = {
     "rvc_cuda_embedding": ([_i64, _ip64, _i64, _fp, _i32, _i32, _fp], _i32),
     "rvc_cuda_gating": ([_i64, _fp, _fp, _i32, _i32, _i32, _fp], _i32),
     "rvc_cuda_rel_attention": ([_i64, _fp, _fp, _fp, _fp, _fp, _i32, _i32, _i32, _i32, _i32, _fp], _i32),
+    "rvc_cuda_rel_attention_noalloc": ([_i64, _p, _p, _p, _p, _p, _i32, _i32, _i32, _i32, _i32, _p], _i32),
     "rvc_cuda_im2col1d": ([_i64, _fp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _fp], _i32),
     "rvc_cuda_synth_create": ([_i64, C.POINTER(_i32), _i32, C.POINTER(_i64)], _i32),
     "rvc_cuda_synth_destroy": ([_i64], _i32),
