@@ -166,6 +166,35 @@ int32_t rvc_cuda_synth_tap(int64_t model, const char* name, float* out, int64_t 
 /* Enables recording of debug taps (off by default: taps cost a copy). */
 int32_t rvc_cuda_synth_keep_taps(int64_t model, int32_t enable);
 
+/* ---------------------------------------------------------------- HuBERT
+ * Device-resident HuBERT-base encoder; replaces HubertEncoder.encode /
+ * encode_batch (runtime/models/hubert.py:564-589, :593-628) and its pieces
+ * _feature_extractor (:658), _feature_projection (:775), _pos_conv_embed
+ * (:838), _encoder (:928), _encoder_layer (:1262).
+ * precision: 0 = BF16x3 tensor cores (default), 1 = fp32 SIMT check path. */
+int32_t rvc_cuda_hubert_create(int64_t ctx, int32_t precision, int64_t* model);
+int32_t rvc_cuda_hubert_destroy(int64_t model);
+/* Weights by the reference's state-dict key (prefix-stripped transformers
+ * names, runtime/models/hubert.py:499-559); the positional conv is given as
+ * weight_g/weight_v (or parametrizations.weight.original0/1) and folded on the
+ * device, or pre-folded as "_pos_conv_weight" [768,48,128]. */
+int32_t rvc_cuda_hubert_set_weight(int64_t model, const char* key, const float* data, const int64_t* shape,
+                                   int32_t ndim);
+int32_t rvc_cuda_hubert_finalize(int64_t model);
+/* Frames L produced for T samples (0 when T is too short for the conv stack). */
+int32_t rvc_cuda_hubert_out_len(int64_t T, int64_t* L);
+/* B equal-length chunks x [B,T] (host) -> out [B,L,768] (version 2,
+ * last_hidden_state) or [B,L,256] (version 1, layer 9 through final_proj);
+ * runtime/models/hubert.py:564-589.  Synchronous. */
+int32_t rvc_cuda_hubert_encode(int64_t model, int32_t B, int64_t T, const float* x, int32_t version, float* out);
+/* Same with device pointers, asynchronous on the context's stream. */
+int32_t rvc_cuda_hubert_encode_device(int64_t model, int32_t B, int64_t T, const float* x, int32_t version,
+                                      float* out);
+/* Debug taps after an encode with taps enabled: "conv0".."conv6" [B,Ti,512],
+ * "proj" and "pos" [B*L,768], "layer0".."layer11" [B*L,768]. */
+int32_t rvc_cuda_hubert_tap(int64_t model, const char* name, float* out, int64_t n);
+int32_t rvc_cuda_hubert_keep_taps(int64_t model, int32_t enable);
+
 #ifdef __cplusplus
 }
 #endif

@@ -43,8 +43,10 @@ def grouped_conv1d(x, w, b, groups, padding):
     return np.concatenate(parts, axis=1)
 
 
-def encode(sd: dict, x: np.ndarray, taps=None) -> np.ndarray:
-    """``[1,T]`` 16 kHz waveform -> ``[1,L,768]`` last hidden state."""
+def encode(sd: dict, x: np.ndarray, taps=None, version: int = 2) -> np.ndarray:
+    """``[1,T]`` 16 kHz waveform -> ``[1,L,768]`` last hidden state (version 2),
+    or layer 9's output through ``final_proj`` ``[1,L,256]`` (version 1,
+    ``runtime/models/hubert.py:580-586``)."""
     x = np.asarray(x, dtype=F32)
     h = x[:, None, :]
     for i in range(7):
@@ -68,7 +70,7 @@ def encode(sd: dict, x: np.ndarray, taps=None) -> np.ndarray:
     _tap(taps, "pos", pos[0])
     h = ops.layer_norm(h + pos, sd["encoder.layer_norm.weight"], sd["encoder.layer_norm.bias"])
     scale = 64.0 ** -0.5
-    for i in range(12):                                              # :1262-1287
+    for i in range(9 if version == 1 else 12):                       # :1262-1287
         p = f"encoder.layers.{i}."
         q = ops.linear(h, sd[p + "attention.q_proj.weight"], sd[p + "attention.q_proj.bias"]) * scale
         k = ops.linear(h, sd[p + "attention.k_proj.weight"], sd[p + "attention.k_proj.bias"])
@@ -87,4 +89,6 @@ def encode(sd: dict, x: np.ndarray, taps=None) -> np.ndarray:
                        sd[p + "feed_forward.output_dense.bias"])
         h = ops.layer_norm(h + f, sd[p + "final_layer_norm.weight"], sd[p + "final_layer_norm.bias"])
         _tap(taps, f"layer{i}", h[0])
+    if version == 1:
+        return ops.linear(h, sd["final_proj.weight"], sd["final_proj.bias"])
     return h

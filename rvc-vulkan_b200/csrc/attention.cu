@@ -213,13 +213,12 @@ __global__ void __launch_bounds__(256) flash_rel_attn_kernel(const float* __rest
   }
 }
 
-void k_rel_attention(const float* qkv, int qkv_ld, int q_off, int k_off, int v_off, const float* emb_k,
-                     const float* emb_v, int B, int heads, int kc, int P, int window, float* scratch, float* y,
-                     int y_ld, cudaStream_t st) {
-  (void)scratch;
+static void launch_attn(const float* qkv, int ld, int q_off, int k_off, int v_off, const float* emb_k,
+                        const float* emb_v, int B, int heads, int D, int P, int window, float q_div, float* y, int y_ld,
+                        cudaStream_t st) {
   if (B * P == 0) return;
-  RVC_CHECK_ARG(kc <= kMaxD && window <= kMaxW, "attention: head dim <= 128 and window <= 16 supported");
-  const size_t smem = sizeof(float) * AttnSmem::floats(kc, window);
+  RVC_CHECK_ARG(D <= kMaxD && window <= kMaxW, "attention: head dim <= 128 and window <= 16 supported");
+  const size_t smem = sizeof(float) * AttnSmem::floats(D, window);
   static std::atomic<uint64_t> attr_done{0};  // the attribute is per device
   int dev = 0;
   RVC_CUDA_TRY(cudaGetDevice(&dev));
@@ -228,11 +227,23 @@ void k_rel_attention(const float* qkv, int qkv_ld, int q_off, int k_off, int v_o
     attr_done.fetch_or(1ull << dev);
   }
   dim3 g(cdiv(P, kQB), B * heads);
-  const float qdiv = window >= 0 ? (float)std::sqrt((double)kc) : 1.f;
-  flash_rel_attn_kernel<<<g, 256, smem, st>>>(qkv, qkv_ld, q_off, k_off, v_off, emb_k, emb_v, heads, kc, P, window,
-                                               qdiv, y, y_ld);
+  flash_rel_attn_kernel<<<g, 256, smem, st>>>(qkv, ld, q_off, k_off, v_off, emb_k, emb_v, heads, D, P, window, q_div,
+                                               y, y_ld);
   note_launch();
   RVC_CUDA_TRY(cudaGetLastError());
+}
+
+void k_rel_attention(const float* qkv, int qkv_ld, int q_off, int k_off, int v_off, const float* emb_k,
+                     const float* emb_v, int B, int heads, int kc, int P, int window, float* scratch, float* y,
+                     int y_ld, cudaStream_t st) {
+  (void)scratch;
+  const float qdiv = window >= 0 ? (float)std::sqrt((double)kc) : 1.f;
+  launch_attn(qkv, qkv_ld, q_off, k_off, v_off, emb_k, emb_v, B, heads, kc, P, window, qdiv, y, y_ld, st);
+}
+
+void k_attention(const float* qkv, int qkv_ld, int q_off, int k_off, int v_off, int B, int heads, int D, int P,
+                 float q_div, float* y, int y_ld, cudaStream_t st) {
+  launch_attn(qkv, qkv_ld, q_off, k_off, v_off, nullptr, nullptr, B, heads, D, P, -1, q_div, y, y_ld, st);
 }
 
 }  // namespace rvc

@@ -2,6 +2,7 @@
 // Every entry point: look up handles, take the context lock, set the device,
 // run, and turn any exception into an int32 status + thread-local message.
 #include "../../include/rvc_cuda.h"
+#include "hubert.cuh"
 #include "synth.cuh"
 
 #include <cstring>
@@ -15,6 +16,7 @@ namespace {
 std::mutex g_reg_mu;
 std::unordered_map<int64_t, std::unique_ptr<Context>> g_ctx;
 std::unordered_map<int64_t, std::unique_ptr<SynthModel>> g_synth;
+std::unordered_map<int64_t, std::unique_ptr<HubertModel>> g_hubert;
 int64_t g_next = 1;
 
 Context* get_ctx(int64_t h) {
@@ -28,6 +30,13 @@ SynthModel* get_synth(int64_t h) {
   std::lock_guard<std::mutex> lk(g_reg_mu);
   auto it = g_synth.find(h);
   if (it == g_synth.end()) throw Error{kErrState, "invalid synthesizer handle " + std::to_string(h)};
+  return it->second.get();
+}
+
+HubertModel* get_hubert(int64_t h) {
+  std::lock_guard<std::mutex> lk(g_reg_mu);
+  auto it = g_hubert.find(h);
+  if (it == g_hubert.end()) throw Error{kErrState, "invalid HuBERT handle " + std::to_string(h)};
   return it->second.get();
 }
 
@@ -76,6 +85,16 @@ template <typename F>
 int32_t on_synth(int64_t model, F&& f) {
   return guarded([&] {
     SynthModel* m = get_synth(model);
+    std::lock_guard<std::mutex> lk(m->ctx->mu);
+    DeviceGuard dg(m->ctx->device);
+    f(m);
+  });
+}
+
+template <typename F>
+int32_t on_hubert(int64_t model, F&& f) {
+  return guarded([&] {
+    HubertModel* m = get_hubert(model);
     std::lock_guard<std::mutex> lk(m->ctx->mu);
     DeviceGuard dg(m->ctx->device);
     f(m);
@@ -542,6 +561,78 @@ int32_t rvc_cuda_synth_tap(int64_t model, const char* name, float* out, int64_t 
 
 int32_t rvc_cuda_synth_keep_taps(int64_t model, int32_t enable) {
   return on_synth(model, [&](SynthModel* m) { m->keep_taps = enable != 0; });
+}
+
+// ----------------------------------------------------------------- HuBERT
+int32_t rvc_cuda_hubert_create(int64_t ctx, int32_t precision, int64_t* model) {
+  return on_ctx(ctx, [&](Context* c) {
+    auto m = std::make_unique<HubertModel>(c, precision);
+    std::lock_guard<std::mutex> lk(g_reg_mu);
+    *model = g_next++;
+    g_hubert[*model] = std::move(m);
+  });
+}
+
+int32_t rvc_cuda_hubert_destroy(int64_t model) {
+  return guarded([&] {
+    std::unique_ptr<HubertModel> m;
+    {
+      std::lock_guard<std::mutex> lk(g_reg_mu);
+      auto it = g_hubert.find(model);
+      if (it == g_hubert.end()) throw Error{kErrState, "invalid HuBERT handle " + std::to_string(model)};
+      m = std::move(it->second);
+      g_hubert.erase(it);
+    }
+    std::lock_guard<std::mutex> lk(m->ctx->mu);
+    DeviceGuard dg(m->ctx->device);
+    m.reset();
+  });
+}
+
+int32_t rvc_cuda_hubert_set_weight(int64_t model, const char* key, const float* data, const int64_t* shape,
+                                   int32_t ndim) {
+  return on_hubert(model, [&](HubertModel* m) {
+    RVC_CHECK_ARG(key && data && ndim >= 0 && ndim <= 8, "hubert_set_weight: bad arguments");
+    std::vector<int64_t> s(shape, shape + ndim);
+    m->set_weight(key, data, s);
+  });
+}
+
+int32_t rvc_cuda_hubert_finalize(int64_t model) {
+  return on_hubert(model, [&](HubertModel* m) {
+    m->finalize();
+    finish(m->ctx);
+  });
+}
+
+int32_t rvc_cuda_hubert_out_len(int64_t T, int64_t* L) {
+  return guarded([&] {
+    RVC_CHECK_ARG(T >= 0 && L, "hubert_out_len: bad arguments");
+    *L = HubertModel::out_len(T);
+  });
+}
+
+int32_t rvc_cuda_hubert_encode(int64_t model, int32_t B, int64_t T, const float* x, int32_t version, float* out) {
+  return on_hubert(model, [&](HubertModel* m) {
+    RVC_CHECK_ARG(B >= 1 && T >= 1 && x && out, "hubert_encode: bad arguments");
+    m->encode_host(B, T, x, version, out);
+    finish(m->ctx);
+  });
+}
+
+int32_t rvc_cuda_hubert_encode_device(int64_t model, int32_t B, int64_t T, const float* x, int32_t version,
+                                      float* out) {
+  return on_hubert(model, [&](HubertModel* m) { m->encode_device(B, T, x, version, out); });
+}
+
+int32_t rvc_cuda_hubert_tap(int64_t model, const char* name, float* out, int64_t n) {
+  return on_hubert(model, [&](HubertModel* m) {
+    if (!m->tap(name, out, n)) throw Error{kErrArg, std::string("hubert_tap: no tap '") + name + "' of that size"};
+  });
+}
+
+int32_t rvc_cuda_hubert_keep_taps(int64_t model, int32_t enable) {
+  return on_hubert(model, [&](HubertModel* m) { m->keep_taps = enable != 0; });
 }
 
 }  // extern "C"

@@ -50,12 +50,27 @@ struct Error {
 // Activation codes shared by kernel prologues/epilogues.
 enum Act : int32_t { kActNone = 0, kActLeaky = 1, kActRelu = 2, kActTanh = 3, kActGelu = 4 };
 
+// GELU 0.5 x (1 + erf(x / sqrt 2)) with erf from Abramowitz & Stegun 7.1.26
+// (|error| <= 1.5e-7), the formula the reference's HuBERT uses
+// (runtime/models/hubert.py:168-176, :194-210): t = 1 / (1 + p|u|),
+// erf(|u|) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-u^2), odd in u.
+__device__ __forceinline__ float gelu_as(float x) {
+  const float u = x * 0.70710678118654752f;
+  const float au = fabsf(u);
+  const float t = 1.f / (1.f + 0.3275911f * au);
+  const float poly = ((((1.061405429f * t - 1.453152027f) * t + 1.421413741f) * t - 0.284496736f) * t +
+                      0.254829592f) * t;
+  float e = 1.f - poly * expf(-au * au);
+  e = u < 0.f ? -e : e;
+  return 0.5f * x * (1.f + e);
+}
+
 __device__ __forceinline__ float act_apply(float v, int act, float slope) {
   switch (act) {
     case kActLeaky: return v >= 0.f ? v : slope * v;
     case kActRelu: return v > 0.f ? v : 0.f;
     case kActTanh: return tanhf(v);
-    case kActGelu: return 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
+    case kActGelu: return gelu_as(v);
     default: return v;
   }
 }

@@ -173,7 +173,7 @@ __global__ void elementwise_kernel(int op, const float* __restrict__ a, const fl
       case 1: r = v * b[i]; break;
       case 2: r = v > 0.f ? v : 0.f; break;
       case 3: r = v >= 0.f ? v : alpha * v; break;
-      case 4: r = 0.5f * v * (1.f + erff(v * 0.70710678118654752f)); break;
+      case 4: r = gelu_as(v); break;
       case 5: r = tanhf(v); break;
       default: r = sigmoid_np(v); break;
     }
@@ -446,7 +446,7 @@ __global__ void __launch_bounds__(256) noise_conv_kernel(const float* __restrict
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int c = c0 + tx * 4 + j;
-      if (c < C) y[(long long)b * y_bs + (long long)t * C + c] = acc[i][j] + bias[c];
+      if (c < C) y[(long long)b * y_bs + (long long)t * C + c] = bias ? acc[i][j] + bias[c] : acc[i][j];
     }
   }
 }
@@ -466,6 +466,142 @@ void k_noise_conv(const float* har, long long har_bs, int har_len, const float* 
   }
   dim3 g(cdiv(T_out, kNzRows), cdiv(C, kNzCols), B);
   noise_conv_kernel<<<g, 256, smem, st>>>(har, har_bs, har_len, w, bias, C, nk, str, pad, T_out, y, y_bs);
+  RVC_LAUNCH_CHECK();
+}
+
+
+// ------------------------------------------------------------------ HuBERT pieces
+// GroupNorm with one group per channel over time (runtime/models/hubert.py:689-695,
+// runtime/nn.py:415-440), channels-last x[b][t][c].  Stage 1: each block takes
+// kGnSplit-th of the rows of one chunk, one thread per channel, and computes the
+// slice mean and the centred sum of squares (two passes over its rows).
+// Stage 2 merges the slices with Chan's pairwise update in double and stores
+// mean and sqrt(var + eps), var = M2 / T (biased, as numpy's var).
+constexpr int kGnSplit = 64;
+
+__global__ void gn_partial_kernel(const float* __restrict__ x, long long x_bs, int T, int C, float* __restrict__ part) {
+  const int b = blockIdx.y, sp = blockIdx.x;
+  const int r0 = (int)((long long)T * sp / kGnSplit), r1 = (int)((long long)T * (sp + 1) / kGnSplit);
+  const float* xb = x + (long long)b * x_bs;
+  float* pb = part + ((long long)b * kGnSplit + sp) * 2 * C;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    float s = 0.f;
+    for (int r = r0; r < r1; ++r) s += xb[(long long)r * C + c];
+    const int n = r1 - r0;
+    const float m = n > 0 ? s / (float)n : 0.f;
+    float q = 0.f;
+    for (int r = r0; r < r1; ++r) {
+      const float d = xb[(long long)r * C + c] - m;
+      q = fmaf(d, d, q);
+    }
+    pb[c] = m;
+    pb[C + c] = q;
+  }
+}
+
+__global__ void gn_finalize_kernel(const float* __restrict__ part, int T, int C, float eps, float* __restrict__ mean,
+                                   float* __restrict__ den) {
+  const int b = blockIdx.y;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  double n = 0.0, m = 0.0, q = 0.0;
+  for (int sp = 0; sp < kGnSplit; ++sp) {
+    const int r0 = (int)((long long)T * sp / kGnSplit), r1 = (int)((long long)T * (sp + 1) / kGnSplit);
+    const double nb = r1 - r0;
+    if (nb == 0.0) continue;
+    const float* pb = part + ((long long)b * kGnSplit + sp) * 2 * C;
+    const double mb = pb[c], qb = pb[C + c];
+    const double nt = n + nb, d = mb - m;
+    m += d * nb / nt;
+    q += qb + d * d * n * nb / nt;
+    n = nt;
+  }
+  const float var = (float)(q / (n > 0.0 ? n : 1.0));
+  mean[(long long)b * C + c] = (float)m;
+  den[(long long)b * C + c] = sqrtf(var + eps);
+}
+
+__global__ void gn_apply_gelu_kernel(float* __restrict__ x, long long x_bs, int T, int C, int B,
+                                     const float* __restrict__ mean, const float* __restrict__ den,
+                                     const float* __restrict__ gamma, const float* __restrict__ beta) {
+  const long long per = (long long)T * C / 4, n = per * B;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const int b = (int)(i / per);
+    const long long e = (i % per) * 4;
+    const int c = (int)(e % C);
+    float4* p = reinterpret_cast<float4*>(x + (long long)b * x_bs + e);
+    float4 v = *p;
+    float o[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const long long bc = (long long)b * C + c + j;
+      o[j] = gelu_as((o[j] - mean[bc]) / den[bc] * gamma[c + j] + beta[c + j]);
+    }
+    *p = make_float4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+void k_groupnorm_chan_gelu(float* x, long long x_bs, int T, int C, int B, const float* gamma, const float* beta,
+                           float eps, float* scratch, cudaStream_t st) {
+  if (B * T == 0) return;
+  RVC_CHECK_ARG(C % 4 == 0 && x_bs % 4 == 0 && ((uintptr_t)x & 15) == 0, "group_norm: C and strides must be x4");
+  float* part = scratch;
+  float* mean = part + (size_t)B * kGnSplit * 2 * C;
+  float* den = mean + (size_t)B * C;
+  gn_partial_kernel<<<dim3(kGnSplit, B), 512, 0, st>>>(x, x_bs, T, C, part);
+  RVC_LAUNCH_CHECK();
+  gn_finalize_kernel<<<dim3(cdiv(C, 128), B), 128, 0, st>>>(part, T, C, eps, mean, den);
+  RVC_LAUNCH_CHECK();
+  gn_apply_gelu_kernel<<<grid_for((long long)B * T * C / 4, 256), 256, 0, st>>>(x, x_bs, T, C, B, mean, den, gamma,
+                                                                             beta);
+  RVC_LAUNCH_CHECK();
+}
+
+size_t groupnorm_chan_scratch_floats(int B, int C) { return (size_t)B * kGnSplit * 2 * C + 2 * (size_t)B * C; }
+
+// Weight norm over dims (0, 1) for each tap k (weight_norm dim=2):
+// W[o][i][k] = g[k] * (v[o][i][k] / ||v[:, :, k]||), the norm summed in double
+// and cast to float first (runtime/models/hubert.py:521-522).
+__global__ void fold_wn_dim2_kernel(const float* __restrict__ v, const float* __restrict__ g, float* __restrict__ out,
+                                    long long rows, int K) {
+  const int k = blockIdx.x;
+  double s = 0.0;
+  for (long long r = threadIdx.x; r < rows; r += blockDim.x) {
+    const double a = v[r * K + k];
+    s += a * a;
+  }
+  __shared__ double red[256];
+  red[threadIdx.x] = s;
+  __syncthreads();
+  for (int o = blockDim.x / 2; o > 0; o >>= 1) {
+    if ((int)threadIdx.x < o) red[threadIdx.x] += red[threadIdx.x + o];
+    __syncthreads();
+  }
+  const float norm = (float)sqrt(red[0]);
+  const float gk = g[k];
+  for (long long r = threadIdx.x; r < rows; r += blockDim.x) out[r * K + k] = gk * (v[r * K + k] / norm);
+}
+void k_fold_weight_norm_dim2(const float* v, const float* g, float* out, long long rows, int K, cudaStream_t st) {
+  if (rows * K == 0) return;
+  fold_wn_dim2_kernel<<<K, 256, 0, st>>>(v, g, out, rows, K);
+  RVC_LAUNCH_CHECK();
+}
+
+// y[o][t*I + i] = W[o][i][j0 + t] for t < nt: taps j0..j0+nt-1 of a conv
+// [O][I][K] become one 1-tap conv over nt*I channels (the stride-2 view).
+__global__ void taps_to_channels_kernel(const float* __restrict__ W, int O, int I, int K, int j0, int nt,
+                                        float* __restrict__ y) {
+  const long long n = (long long)O * nt * I;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
+    const int o = (int)(e / ((long long)nt * I));
+    const int r = (int)(e % ((long long)nt * I));
+    const int t = r / I, i = r % I;
+    y[e] = W[((long long)o * I + i) * K + j0 + t];
+  }
+}
+void k_taps_to_channels(const float* W, int O, int I, int K, int j0, int nt, float* y, cudaStream_t st) {
+  if ((long long)O * I * nt == 0) return;
+  taps_to_channels_kernel<<<grid_for((long long)O * I * nt, 256), 256, 0, st>>>(W, O, I, K, j0, nt, y);
   RVC_LAUNCH_CHECK();
 }
 

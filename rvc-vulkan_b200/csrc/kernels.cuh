@@ -59,4 +59,18 @@ void k_noise_conv(const float* har, long long har_bs, int har_len, const float* 
 void k_conv_post_tanh(const float* x, long long x_bs, int B, int T, int C, const float* w, int K, int pad, float slope,
                       float* y, cudaStream_t st);
 
+// ---- HuBERT pieces
+// Per-channel GroupNorm over time of channels-last x [B][T][C] (in place), then
+// GELU; scratch holds groupnorm_chan_scratch_floats(B, C) floats.
+void k_groupnorm_chan_gelu(float* x, long long x_bs, int T, int C, int B, const float* gamma, const float* beta,
+                           float eps, float* scratch, cudaStream_t st);
+size_t groupnorm_chan_scratch_floats(int B, int C);
+// out[r][k] = g[k] * v[r][k] / ||v[:, k]||  for v viewed as [rows][K] (weight_norm dim=2)
+void k_fold_weight_norm_dim2(const float* v, const float* g, float* out, long long rows, int K, cudaStream_t st);
+// y[o][t*I + i] = W[o][i][j0 + t], t < nt  (taps folded into input channels)
+void k_taps_to_channels(const float* W, int O, int I, int K, int j0, int nt, float* y, cudaStream_t st);
+// Plain softmax(q k^T / q_div) v attention over head-interleaved channels-last rows.
+void k_attention(const float* qkv, int qkv_ld, int q_off, int k_off, int v_off, int B, int heads, int D, int P,
+                 float q_div, float* y, int y_ld, cudaStream_t st);
+
 }  // namespace rvc

@@ -13,18 +13,21 @@ void ConvLayer::build(Context* ctx, LayerKind k, const float* W, const float* b,
   std::vector<int> tap_k;
   slices.clear();
   if (k == LayerKind::kConv) {
+    RVC_CHECK_ARG(groups >= 1 && groups <= kMaxSlices && O % groups == 0, "conv1d: groups must divide C_out, <= 16");
     C_in = I;
-    C_out = O;
-    for (int j = 0; j < K; ++j) tap_k.push_back(j);
-    ConvSlice s{};
-    s.ntaps = K;
-    s.tap_base = -pad_l;
-    s.tap_step = dil;
-    s.out_r0 = 0;
-    s.ci_off = 0;
-    s.co_off = 0;
-    s.wtap0 = 0;
-    slices.push_back(s);
+    C_out = O / groups;
+    for (int g = 0; g < groups; ++g) {
+      for (int j = 0; j < K; ++j) tap_k.push_back(j);
+      ConvSlice s{};
+      s.ntaps = K;
+      s.tap_base = -pad_l;
+      s.tap_step = dil;
+      s.out_r0 = 0;
+      s.ci_off = g * I;
+      s.co_off = g * C_out;
+      s.wtap0 = g * K;
+      slices.push_back(s);
+    }
   } else {
     // Transposed conv as `up` phase GEMMs: output row q*up + p takes taps
     // k = k0 + j*up with k0 = (p + pad) mod up, reading input row
@@ -54,10 +57,18 @@ void ConvLayer::build(Context* ctx, LayerKind k, const float* W, const float* b,
   DevBuf taps(ctx, sizeof(int) * std::max(1, taps_total));
   RVC_CUDA_TRY(cudaMemcpyAsync(taps.p, tap_k.data(), sizeof(int) * taps_total, cudaMemcpyHostToDevice, st));
   Wg = DevBuf(ctx, sizeof(float) * (size_t)std::max(1, taps_total) * C_in * C_out);
-  k_gather_taps(W, Wg.f(), O, I, K, k == LayerKind::kConv ? 0 : 1, taps.as<int>(), taps_total, st);
-  if (b) {
-    bias = DevBuf(ctx, sizeof(float) * C_out);
-    RVC_CUDA_TRY(cudaMemcpyAsync(bias.p, b, sizeof(float) * C_out, cudaMemcpyDeviceToDevice, st));
+  if (k == LayerKind::kConv && groups > 1) {
+    // group g: taps [g*K, (g+1)*K) of Wg hold W[g*C_out + o][i][k]
+    for (int g = 0; g < groups; ++g)
+      k_gather_taps(W + (size_t)g * C_out * I * K, Wg.f() + (size_t)g * K * I * C_out, C_out, I, K, 0, taps.as<int>(),
+                    K, st);
+  } else {
+    k_gather_taps(W, Wg.f(), O, I, K, k == LayerKind::kConv ? 0 : 1, taps.as<int>(), taps_total, st);
+  }
+  if (b) {  // the epilogue indexes bias by the global output channel (co_off + co)
+    const int nb = k == LayerKind::kConv ? O : C_out;
+    bias = DevBuf(ctx, sizeof(float) * nb);
+    RVC_CUDA_TRY(cudaMemcpyAsync(bias.p, b, sizeof(float) * nb, cudaMemcpyDeviceToDevice, st));
   }
   tc = use_tc && tc_shape_ok(C_in, C_out) && stride == 1;
   if (tc) {
@@ -75,7 +86,7 @@ int ConvLayer::out_len(int T_in) const {
 }
 
 double ConvLayer::flops(int B, int T_in) const {
-  return 2.0 * B * (double)out_len(T_in) * C_in * C_out * (kind == LayerKind::kConv ? K : (double)K / up);
+  return 2.0 * B * (double)out_len(T_in) * C_in * C_out * (kind == LayerKind::kConv ? (double)K * groups : (double)K / up);
 }
 
 void ConvLayer::run(Context* ctx, const ConvIO& io, bool force_simt) const {
@@ -119,8 +130,8 @@ void ConvLayer::run(Context* ctx, const ConvIO& io, bool force_simt) const {
     launch_tc_conv(a, ctx->stream);
     if (ctx->prof) {
       char lab[160];
-      snprintf(lab, sizeof(lab), "%s Cin=%d Cout=%d K=%d dil=%d up=%d T=%d B=%d bn=%d cb=%d",
-               kind == LayerKind::kConv ? "conv" : "convT", C_in, C_out, K, dil, up, io.T_in, io.B, bn, cb);
+      snprintf(lab, sizeof(lab), "%s Cin=%d Cout=%d K=%d dil=%d up=%d g=%d T=%d B=%d bn=%d cb=%d",
+               kind == LayerKind::kConv ? "conv" : "convT", C_in, C_out, K, dil, up, groups, io.T_in, io.B, bn, cb);
       ctx->prof_end(e0, e1, flops(io.B, io.T_in), lab);
     }
   } else {

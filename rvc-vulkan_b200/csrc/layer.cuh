@@ -33,13 +33,15 @@ struct ConvLayer {
   int C_in = 0, C_out = 0, K = 0;
   int dil = 1, pad_l = 0, pad_r = 0, stride = 1;  // conv
   int up = 1, up_pad = 0;                          // convT: stride, padding
+  int groups = 1;                                  // conv: one slice per group (<= 16)
   int taps_total = 0;
   std::vector<ConvSlice> slices;  // rows filled per launch
   DevBuf Wg, wpk, bias;
   bool tc = false;
   int bn = 0, cb = 0;
 
-  // W: conv [O,I,K] or convT [I,O,K], device fp32 (already weight-norm folded).
+  // W: conv [O,I,K] (I = input channels per group) or convT [I,O,K], device
+  // fp32 (already weight-norm folded).
   void build(Context* ctx, LayerKind k, const float* W, const float* b, int O, int I, int Kk, bool use_tc);
   int out_len(int T_in) const;
   // Launch on ctx->stream.  force_simt: run the fp32 SIMT kernel.

@@ -6,7 +6,8 @@ Drop-in for jiangchengnay/rvc-vulkan's numpy runtime:
   (``runtime/backend.py:57-70``); ``RVC_BACKEND=cuda`` then routes the
   ``runtime.nn`` float32 ops through ``rvc_cuda.ops``.
 * ``patch_reference()`` installs the whole-model fast paths
-  (``rvc_cuda.synth.patch_reference`` for ``SynthesizerTrn``).
+  (``rvc_cuda.synth.patch_reference`` for ``SynthesizerTrn``,
+  ``rvc_cuda.hubert.patch_reference`` for ``HubertEncoder``).
 
 Importing this package does not touch the GPU; the shared library is loaded
 on first use of ``rvc_cuda.ops`` / ``rvc_cuda.synth`` and raises if missing.
@@ -41,6 +42,7 @@ def register(name: str = "cuda") -> None:
 
 def patch_reference(device=None, precision: str = "bf16x3") -> None:
     """Install the model-level CUDA paths on the reference's model classes."""
-    from . import synth  # noqa: PLC0415
+    from . import hubert, synth  # noqa: PLC0415
 
     synth.patch_reference(device=device, precision=precision)
+    hubert.patch_reference(device=device, precision=precision)

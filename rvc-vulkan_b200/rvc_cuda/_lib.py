@@ -87,6 +87,15 @@ _SIGS = {
     "rvc_cuda_synth_infer_device": ([_i64, _i32, _i32, _p, _p, _p, _p, _p, _p, _p], _i32),
     "rvc_cuda_synth_tap": ([_i64, C.c_char_p, _fp, _i64], _i32),
     "rvc_cuda_synth_keep_taps": ([_i64, _i32], _i32),
+    "rvc_cuda_hubert_create": ([_i64, _i32, C.POINTER(_i64)], _i32),
+    "rvc_cuda_hubert_destroy": ([_i64], _i32),
+    "rvc_cuda_hubert_set_weight": ([_i64, C.c_char_p, _fp, _ip64, _i32], _i32),
+    "rvc_cuda_hubert_finalize": ([_i64], _i32),
+    "rvc_cuda_hubert_out_len": ([_i64, C.POINTER(_i64)], _i32),
+    "rvc_cuda_hubert_encode": ([_i64, _i32, _i64, _fp, _i32, _fp], _i32),
+    "rvc_cuda_hubert_encode_device": ([_i64, _i32, _i64, _p, _i32, _p], _i32),
+    "rvc_cuda_hubert_tap": ([_i64, C.c_char_p, _fp, _i64], _i32),
+    "rvc_cuda_hubert_keep_taps": ([_i64, _i32], _i32),
 }
 for _name, (_args, _ret) in _SIGS.items():
     _fn = getattr(lib, _name)

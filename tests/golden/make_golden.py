@@ -106,9 +106,11 @@ def run_hubert(runtime_hubert, name, T, wseed, iseed, meta):
         enc = runtime_hubert.HubertEncoder(d)
         feats = enc._feature_extractor(x)
         out = enc.encode(x, version=2)
+        out1 = enc.encode(x, version=1)
     np.savez_compressed(os.path.join(HERE, name + ".npz"),
                         conv=np.asarray(feats[0], np.float32),
-                        out=np.asarray(out[0], np.float32))
+                        out=np.asarray(out[0], np.float32),
+                        out_v1=np.asarray(out1[0], np.float32))
     meta[name] = {"kind": "hubert", "T": T, "weight_seed": wseed, "input_seed": iseed,
                   "weights_sha256": weights_digest(sd), "inputs_sha256": digest([x])}
 
@@ -161,6 +163,8 @@ def run_ops(nn, meta):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("RVC_REFERENCE", "/root/reference"))
+    ap.add_argument("--only", choices=["vits", "hubert", "ops"], default=None,
+                    help="regenerate one family and keep the other fixtures")
     args = ap.parse_args()
     os.environ["RVC_BACKEND"] = "numpy"
     sys.path.insert(0, args.ref)
@@ -172,11 +176,17 @@ def main():
 
     meta = {"numpy": np.__version__, "numba": numba.__version__,
             "blas": [i.get("internal_api") for i in threadpoolctl.threadpool_info()]}
-    for c in VITS_CASES:
-        run_vits(runtime_vits, *c, meta)
-    for c in HUBERT_CASES:
-        run_hubert(runtime_hubert, *c, meta)
-    run_ops(nn, meta)
+    if args.only is not None:
+        with open(os.path.join(HERE, "golden.json")) as f:
+            meta = json.load(f)
+    if args.only in (None, "vits"):
+        for c in VITS_CASES:
+            run_vits(runtime_vits, *c, meta)
+    if args.only in (None, "hubert"):
+        for c in HUBERT_CASES:
+            run_hubert(runtime_hubert, *c, meta)
+    if args.only in (None, "ops"):
+        run_ops(nn, meta)
     with open(os.path.join(HERE, "golden.json"), "w") as f:
         json.dump(meta, f, indent=1, sort_keys=True)
     print("wrote", sorted(k for k in meta if k not in ("numpy", "numba", "blas")))

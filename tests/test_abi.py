@@ -63,3 +63,38 @@ def test_last_error_truncates_safely():
     buf = C.create_string_buffer(8)
     n = _lib.lib.rvc_cuda_last_error(buf, 8)
     assert n > 8 and len(buf.value) == 7
+
+
+def test_hubert_out_len_matches_conv_stack_arithmetic():
+    from rvc_cuda import hubert
+
+    def ref_len(T):
+        for i, k in enumerate((10, 3, 3, 3, 3, 2, 2)):
+            if T < k:
+                return 0
+            T = (T - k) // (5 if i == 0 else 2) + 1
+        return T
+
+    for T in (0, 1, 399, 400, 401, 3201, 8000, 16000, 160000, 160001, 480000):
+        assert hubert.out_len(T) == ref_len(T), T
+    assert hubert.out_len(160000) == 499
+
+
+def test_hubert_patch_reference_replaces_class_methods():
+    from rvc_cuda import hubert
+
+    class FakeEncoder:
+        def encode(self, x, version=2):
+            return "numpy"
+
+        def encode_batch(self, xs, version=2):
+            return ["numpy"]
+
+    class FakeModule:
+        HubertEncoder = FakeEncoder
+
+    cls = hubert.patch_reference(FakeModule)
+    assert cls is FakeEncoder and cls._rvc_cuda_patched
+    assert FakeEncoder.encode is not FakeEncoder._rvc_cuda_orig_encode
+    assert FakeEncoder.encode_batch is not FakeEncoder._rvc_cuda_orig_encode_batch
+    assert hubert.patch_reference(FakeModule) is FakeEncoder  # idempotent

@@ -51,6 +51,9 @@ def test_hubert_oracle_matches_reference(name, golden_meta):
     assert rel_l2(taps["conv6"], g["conv"]) < 1e-5
     assert out.shape[1:] == g["out"].shape
     assert rel_l2(out[0], g["out"]) < 1e-5
+    out1 = OH.encode(OH.prepare(sd), x, version=1)
+    assert out1.shape[1:] == g["out_v1"].shape
+    assert rel_l2(out1[0], g["out_v1"]) < 1e-5
 
 
 def test_ops_oracle_matches_reference(golden_meta):
