@@ -156,6 +156,163 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def hubert_cpu_sample(T, steps=1):
+    """Time the HuBERT oracle (numpy restatement of HubertEncoder.encode) on one chunk."""
+    from oracle import hubert as OH
+    from rvc_cuda import synthetic as syn
+    sd = OH.prepare(syn.make_hubert_weights(0))
+    x = syn.make_hubert_input(T, 1)
+    ts = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        OH.encode(sd, x)
+        ts.append(time.perf_counter() - t0)
+    return T / 16000.0, ts
+
+
+def run_hubert(args, world, rank, local):
+    """HuBERT-base over chunks of --samples 16 kHz samples."""
+    import torch
+
+    from rvc_cuda import _lib, synthetic as syn
+    from rvc_cuda.hubert import CudaHubert, out_len
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    T, G = args.samples, args.group
+    m = CudaHubert(syn.make_hubert_weights(0), device=local, precision=args.precision)
+    ctx = m.ctx
+    L = out_len(T)
+    assert args.chunks % world == 0, "chunks must split evenly across ranks"
+    n_local = args.chunks // world
+    n_unique = min(args.unique, n_local)
+    xs = [syn.make_hubert_input(T, 100 + i)[0] for i in range(n_unique)]
+    h_x = torch.empty((n_local, T), dtype=torch.float32, pin_memory=True).numpy()
+    h_y = torch.empty((n_local, L, 768), dtype=torch.float32, pin_memory=True).numpy()
+    for j in range(n_local):
+        h_x[j] = xs[(rank * n_local + j) % n_unique]
+    d_x = ctx.alloc(h_x.nbytes)
+    ctx.h2d(d_x, h_x)
+    d_y = ctx.alloc(h_y.nbytes)
+    groups = [(s, min(G, n_local - s)) for s in range(0, n_local, G)]
+
+    def step_device():
+        for s, g in groups:
+            _lib.check(_lib.lib.rvc_cuda_hubert_encode_device(m.handle, g, T, _lib._p(d_x + s * T * 4), 2,
+                                                              _lib._p(d_y + s * L * 768 * 4)))
+
+    def step_e2e():
+        for s, g in groups:
+            h_y[s:s + g] = m.encode_equal(h_x[s:s + g])
+
+    stream = torch.cuda.ExternalStream(ctx.stream(), device=local)
+
+    def timed(fn, steps):
+        barrier()
+        ctx.sync()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        ctx.sync()
+        torch.cuda.synchronize()
+        barrier()
+        return e0.elapsed_time(e1) / 1e3
+
+    for _ in range(args.warmup):
+        step_device()
+    ctx.sync()
+    n0 = _lib.launch_count()
+    ctx.profile(True)
+    with ClockSampler(local) as clk:
+        t = timed(step_device, args.steps)
+    prof_n, prof_ms, prof_flops = ctx.profile_read()
+    if args.profile_out and rank == 0:
+        with open(args.profile_out, "w") as f:
+            f.write(ctx.profile_dump())
+    ctx.profile(False)
+    launches = _lib.launch_count() - n0
+    t = max_over_ranks(t)
+    audio_per_step = args.chunks * T / 16000.0
+    value = audio_per_step * args.steps / t
+    step_e2e()
+    te = max_over_ranks(timed(step_e2e, args.steps))
+    e2e = audio_per_step * args.steps / te
+    if rank == 0:
+        pb, ps, hbm, src = peaks()
+        achieved = prof_flops / (prof_ms / 1e3) / 1e12 if prof_ms > 0 else None
+        line = {
+            "metric": "seconds of input audio encoded per wall-second (HuBERT-base)", "value": value,
+            "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * t / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "f32 (BF16x3 split on tcgen05, fp32 accumulate)" if args.precision == "bf16x3" else "f32",
+            "data": f"synthetic: seeded random-init weights, {n_unique} distinct seeded chunks tiled",
+            "config": {"workload": f"config1 HuBERT-base, {args.chunks} chunks x {T} samples -> [{L},768], "
+                                   "sharded by chunk", "chunks": args.chunks, "samples": T, "group": G,
+                       "precision": args.precision, "l2": "inputs larger than L2",
+                       "parallelism": f"chunk-sharded x{world}, no collective"},
+            "roofline": {"bound": "tensor", "kernel": "tc_conv_kernel (GEMMs and convs, all launches)",
+                         "achieved": achieved, "peak": ps, "unit": "TFLOP/s",
+                         "frac": (achieved / ps) if achieved else None, "traffic": None,
+                         "peak_source": f"{src} bf16 dense sustained",
+                         "note": "useful fp32 FLOPs / tensor-core kernel time; BF16x3 => frac <= 1/3",
+                         "launches": prof_n, "kernel_ms_per_step": prof_ms / args.steps},
+            "e2e": {"value": e2e, "unit": UNIT, "h2d_bytes_per_step": h_x.nbytes * world,
+                    "d2h_bytes_per_step": h_y.nbytes * world},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+            "finite": bool(np.isfinite(h_y).all()),
+        }
+        if world == 1 and not args.no_cpu:
+            audio_s, ts = hubert_cpu_sample(T, steps=1)
+            line["cpu_baseline"] = {"value": audio_s / ts[0], "unit": UNIT, "cores": blas_threads(), "kind": "port",
+                                    "sample": f"1 chunk of {T} samples ({audio_s:.1f} s audio), CPU oracle"}
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def run_hubert_reference(args, world, rank):
+    if rank != 0:
+        return
+    T = args.samples
+    hubert_cpu_sample(T, steps=args.warmup)
+    audio_s, ts = hubert_cpu_sample(T, steps=args.steps)
+    t = sum(ts)
+    value = audio_s * len(ts) / t
+    line = {
+        "impl": "reference", "metric": "seconds of input audio encoded per wall-second (HuBERT-base)",
+        "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * t / len(ts), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded)",
+        "config": {"workload": "config1 HuBERT-base, CPU sample", "samples": T},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": blas_threads(), "kind": "port",
+                         "sample": f"1 chunk of {T} samples per step, CPU oracle"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_ours(args, world, rank, local):
     import torch
 
@@ -319,9 +476,17 @@ def main():
     ap.add_argument("--ref-frames", type=int, default=100)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile-out", default="", help="write the per-layer conv profile (CSV) here")
+    ap.add_argument("--workload", default="synth", choices=["synth", "hubert"],
+                    help="synth: config 3 (headline); hubert: config 1 (HuBERT-base encoder)")
+    ap.add_argument("--samples", type=int, default=160000, help="hubert: samples per chunk")
     args = ap.parse_args()
     world, rank, local = dist_setup()
-    if args.impl == "reference":
+    if args.workload == "hubert":
+        if args.impl == "reference":
+            run_hubert_reference(args, world, rank)
+        else:
+            run_hubert(args, world, rank, local)
+    elif args.impl == "reference":
         run_reference(args, world, rank)
     else:
         run_ours(args, world, rank, local)

@@ -78,11 +78,13 @@ void Context::prof_begin(cudaEvent_t* a, cudaEvent_t* b) {
   RVC_CUDA_TRY(cudaEventRecord(*a, stream));
 }
 
-void Context::prof_end(cudaEvent_t a, cudaEvent_t b, double flops, const std::string& label) {
+void Context::prof_end(cudaEvent_t a, cudaEvent_t b, double flops, const std::string& label, bool tc) {
   RVC_CUDA_TRY(cudaEventRecord(b, stream));
-  prof_ev.push_back(ProfRec{a, b, flops, label});
-  prof_launches += 1;
-  prof_flops += flops;
+  prof_ev.push_back(ProfRec{a, b, flops, label, tc});
+  if (tc) {
+    prof_launches += 1;
+    prof_flops += flops;
+  }
   if (prof_ev.size() > 4096) prof_collect();
 }
 
@@ -91,7 +93,7 @@ void Context::prof_collect() {
   for (auto& e : prof_ev) {
     float ms = 0.f;
     RVC_CUDA_TRY(cudaEventElapsedTime(&ms, e.a, e.b));
-    prof_ms += ms;
+    if (e.tc) prof_ms += ms;
     auto& g = prof_by_label[e.label];
     g.n += 1;
     g.ms += ms;

@@ -21,9 +21,10 @@ struct Context {
   int64_t mem_cap = 0;   // 0 = unlimited
   int64_t mem_used = 0;
   std::unordered_map<void*, size_t> allocs;
-  // profiling of tensor-core conv launches
+  // profiling: totals cover the tensor-core conv launches; other labelled
+  // kernels (attention) are kept per label only
   bool prof = false;
-  struct ProfRec { cudaEvent_t a, b; double flops; std::string label; };
+  struct ProfRec { cudaEvent_t a, b; double flops; std::string label; bool tc; };
   std::vector<ProfRec> prof_ev;
   struct ProfAgg { long long n = 0; double ms = 0, flops = 0; };
   std::map<std::string, ProfAgg> prof_by_label;
@@ -36,7 +37,8 @@ struct Context {
   void* alloc(size_t bytes);  // zero-filled
   void free(void* p);
   void prof_begin(cudaEvent_t* a, cudaEvent_t* b);
-  void prof_end(cudaEvent_t a, cudaEvent_t b, double flops, const std::string& label);
+  // tc = false: recorded per label only, outside the tensor-core totals.
+  void prof_end(cudaEvent_t a, cudaEvent_t b, double flops, const std::string& label, bool tc = true);
   void prof_collect();
   // Polls the stream (bounded) and the device error flag.
   int32_t sync(int timeout_ms);

@@ -290,7 +290,14 @@ void HubertModel::encode_device(int B, int64_t T, const float* x, int version, f
     const std::string p = "encoder.layers." + std::to_string(l) + ".";
     run_conv(qkv_[l], gemm_io(h, D, buf("qkv"), 3 * D));
     // q * 64^-0.5 == q / 8 exactly
-    k_attention(buf("qkv"), 3 * D, 0, D, 2 * D, B, kHeads, kHeadD, (int)L, 8.f, buf("att"), D, st);
+    {
+      cudaEvent_t e0 = nullptr, e1 = nullptr;
+      if (ctx->prof) ctx->prof_begin(&e0, &e1);
+      k_attention(buf("qkv"), 3 * D, 0, D, 2 * D, B, kHeads, kHeadD, (int)L, 8.f, buf("att"), D, st);
+      if (ctx->prof)
+        ctx->prof_end(e0, e1, 4.0 * B * kHeads * (double)L * L * kHeadD,
+                      "attn hubert B=" + std::to_string(B) + " L=" + std::to_string(L), false);
+    }
     ConvIO o = gemm_io(buf("att"), D, buf("t1"), D);
     o.res = h; o.res_ld = D; o.res_bs = rows * D;
     run_conv(o_[l], o);

@@ -243,8 +243,15 @@ void SynthModel::infer_device(int B, int P, const float* phone, const long long*
   for (int i = 0; i < cfg.layers; ++i) {
     const std::string p = "enc_p.encoder.attn_layers." + std::to_string(i);
     run_conv(qkv_[i], io_rows(ex, H, P, buf("qkv"), 3 * H, B, PH, 3 * PH));
-    k_rel_attention(buf("qkv"), 3 * H, 0, H, 2 * H, W(p + ".emb_rel_k").buf.f(), W(p + ".emb_rel_v").buf.f(), B,
-                    cfg.heads, cfg.kc, P, cfg.window, buf("S"), buf("att"), H, st);
+    {
+      cudaEvent_t e0 = nullptr, e1 = nullptr;
+      if (ctx->prof) ctx->prof_begin(&e0, &e1);
+      k_rel_attention(buf("qkv"), 3 * H, 0, H, 2 * H, W(p + ".emb_rel_k").buf.f(), W(p + ".emb_rel_v").buf.f(), B,
+                      cfg.heads, cfg.kc, P, cfg.window, buf("S"), buf("att"), H, st);
+      if (ctx->prof)
+        ctx->prof_end(e0, e1, 4.0 * B * cfg.heads * (double)P * P * cfg.kc,
+                      "attn enc_p B=" + std::to_string(B) + " P=" + std::to_string(P), false);
+    }
     run_conv(o_[i], io_rows(buf("att"), H, P, buf("ao"), H, B, PH, PH));
     save_tap("enc.l" + std::to_string(i) + ".attn", buf("ao"), (long long)B * PH);
     const std::string nl = "enc_p.encoder.norm_layers_";
