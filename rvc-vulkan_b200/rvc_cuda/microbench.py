@@ -2,10 +2,12 @@
 
     python -m rvc_cuda.microbench conv --C 32 --K 3 --T 1920000 [--dil 1] [--reps 2]
     python -m rvc_cuda.microbench synth --sr 48000 --B 2 --P 1000 [--reps 2]
+    python -m rvc_cuda.microbench hubert --B 4 --T 160000 [--reps 2]
 
 `conv` runs rvc_cuda.ops.conv1d ([1,C,T] -> [1,C,T], "same" padding) `reps`
-times; `synth` runs CudaSynthesizer.infer_batch on B seeded chunks.  Each
-prints the wall time of the last repetition.
+times; `synth` runs CudaSynthesizer.infer_batch on B seeded chunks; `hubert`
+runs CudaHubert.encode_equal on B seeded chunks of T samples.  Each prints the
+wall time of the last repetition.
 """
 
 from __future__ import annotations
@@ -53,6 +55,20 @@ def _synth(args):
           f"std={out.std():.4f}")
 
 
+def _hubert(args):
+    from rvc_cuda import synthetic as syn
+    from rvc_cuda.hubert import CudaHubert
+
+    m = CudaHubert(syn.make_hubert_weights(0))
+    x = np.concatenate([syn.make_hubert_input(args.T, i) for i in range(args.B)], axis=0)
+    for _ in range(args.reps):
+        t0 = time.perf_counter()
+        y = m.encode_equal(x)
+        dt = time.perf_counter() - t0
+    print(f"hubert B={args.B} T={args.T}: {dt * 1e3:.2f} ms, {args.B * args.T / 16000 / dt:.1f}x realtime, "
+          f"std={y.std():.4f}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -67,8 +83,12 @@ def main():
     s.add_argument("--B", type=int, default=2)
     s.add_argument("--P", type=int, default=1000)
     s.add_argument("--reps", type=int, default=2)
+    h = sub.add_parser("hubert")
+    h.add_argument("--B", type=int, default=4)
+    h.add_argument("--T", type=int, default=160000)
+    h.add_argument("--reps", type=int, default=2)
     args = ap.parse_args()
-    (_conv if args.cmd == "conv" else _synth)(args)
+    {"conv": _conv, "synth": _synth, "hubert": _hubert}[args.cmd](args)
 
 
 if __name__ == "__main__":
