@@ -195,6 +195,32 @@ int32_t rvc_cuda_hubert_encode_device(int64_t model, int32_t B, int64_t T, const
 int32_t rvc_cuda_hubert_tap(int64_t model, const char* name, float* out, int64_t n);
 int32_t rvc_cuda_hubert_keep_taps(int64_t model, int32_t enable);
 
+/* ---------------------------------------------------------------- retrieval
+ * Device-resident feature index for brute-force L2 search; replaces
+ * runtime.retrieval.search_l2 (runtime/retrieval.py:35-82), weighted_blend
+ * (:85-108) and the pipeline's blend + mix (runtime/pipeline.py:545-551,
+ * :563-566).  db [N,D] (host) is copied; precision 0 = tensor-core GEMM with an
+ * exact float64 re-rank of the candidates, 1 = fp32 SIMT GEMM (same re-rank). */
+int32_t rvc_cuda_index_create(int64_t ctx, const float* db, int64_t N, int32_t D, int32_t precision,
+                              int64_t* index);
+int32_t rvc_cuda_index_destroy(int64_t index);
+/* q [F,D] -> scores [F,k'] (ascending squared L2 distance) and inds [F,k']
+ * (int64), k' = min(k, N), 1 <= k <= 16; equal distances keep the lower index
+ * first.  Synchronous, host pointers. */
+int32_t rvc_cuda_index_search(int64_t index, const float* q, int64_t F, int32_t D, int32_t k, float* scores,
+                              int64_t* inds);
+/* Same with device pointers, asynchronous on the context's stream. */
+int32_t rvc_cuda_index_search_device(int64_t index, const float* q, int64_t F, int32_t D, int32_t k,
+                                     float* scores, int64_t* inds);
+/* out [F,D] = sum_j w_j db[inds_j] with w = (1/score)^2 normalised (mode 0,
+ * runtime/pipeline.py:547-551) or w = 1/max(score,1e-6)^2 normalised (mode 1,
+ * weighted_blend); when feats [F,D] is given, out = blend * index_rate +
+ * feats * (1 - index_rate) (runtime/pipeline.py:563-566).  Host pointers. */
+int32_t rvc_cuda_index_blend(int64_t index, const float* q, int64_t F, int32_t D, int32_t k, int32_t mode,
+                             double index_rate, const float* feats, float* out);
+int32_t rvc_cuda_index_blend_device(int64_t index, const float* q, int64_t F, int32_t D, int32_t k, int32_t mode,
+                                    double index_rate, const float* feats, float* out);
+
 #ifdef __cplusplus
 }
 #endif

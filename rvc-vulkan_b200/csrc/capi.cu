@@ -3,6 +3,7 @@
 // run, and turn any exception into an int32 status + thread-local message.
 #include "../../include/rvc_cuda.h"
 #include "hubert.cuh"
+#include "retrieval.cuh"
 #include "synth.cuh"
 
 #include <cstring>
@@ -17,6 +18,7 @@ std::mutex g_reg_mu;
 std::unordered_map<int64_t, std::unique_ptr<Context>> g_ctx;
 std::unordered_map<int64_t, std::unique_ptr<SynthModel>> g_synth;
 std::unordered_map<int64_t, std::unique_ptr<HubertModel>> g_hubert;
+std::unordered_map<int64_t, std::unique_ptr<IndexModel>> g_index;
 int64_t g_next = 1;
 
 Context* get_ctx(int64_t h) {
@@ -37,6 +39,13 @@ HubertModel* get_hubert(int64_t h) {
   std::lock_guard<std::mutex> lk(g_reg_mu);
   auto it = g_hubert.find(h);
   if (it == g_hubert.end()) throw Error{kErrState, "invalid HuBERT handle " + std::to_string(h)};
+  return it->second.get();
+}
+
+IndexModel* get_index(int64_t h) {
+  std::lock_guard<std::mutex> lk(g_reg_mu);
+  auto it = g_index.find(h);
+  if (it == g_index.end()) throw Error{kErrState, "invalid index handle " + std::to_string(h)};
   return it->second.get();
 }
 
@@ -95,6 +104,16 @@ template <typename F>
 int32_t on_hubert(int64_t model, F&& f) {
   return guarded([&] {
     HubertModel* m = get_hubert(model);
+    std::lock_guard<std::mutex> lk(m->ctx->mu);
+    DeviceGuard dg(m->ctx->device);
+    f(m);
+  });
+}
+
+template <typename F>
+int32_t on_index(int64_t index, F&& f) {
+  return guarded([&] {
+    IndexModel* m = get_index(index);
     std::lock_guard<std::mutex> lk(m->ctx->mu);
     DeviceGuard dg(m->ctx->device);
     f(m);
@@ -633,6 +652,72 @@ int32_t rvc_cuda_hubert_tap(int64_t model, const char* name, float* out, int64_t
 
 int32_t rvc_cuda_hubert_keep_taps(int64_t model, int32_t enable) {
   return on_hubert(model, [&](HubertModel* m) { m->keep_taps = enable != 0; });
+}
+
+// ----------------------------------------------------------------- retrieval
+int32_t rvc_cuda_index_create(int64_t ctx, const float* db, int64_t N, int32_t D, int32_t precision,
+                              int64_t* index) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(db && index && N >= 1 && D >= 1, "index_create: need N >= 1 rows of D >= 1 floats");
+    auto m = std::make_unique<IndexModel>(c, db, N, D, precision);
+    std::lock_guard<std::mutex> lk(g_reg_mu);
+    *index = g_next++;
+    g_index[*index] = std::move(m);
+  });
+}
+
+int32_t rvc_cuda_index_destroy(int64_t index) {
+  return guarded([&] {
+    std::unique_ptr<IndexModel> m;
+    {
+      std::lock_guard<std::mutex> lk(g_reg_mu);
+      auto it = g_index.find(index);
+      if (it == g_index.end()) throw Error{kErrState, "invalid index handle " + std::to_string(index)};
+      m = std::move(it->second);
+      g_index.erase(it);
+    }
+    std::lock_guard<std::mutex> lk(m->ctx->mu);
+    DeviceGuard dg(m->ctx->device);
+    m.reset();
+  });
+}
+
+int32_t rvc_cuda_index_search(int64_t index, const float* q, int64_t F, int32_t D, int32_t k, float* scores,
+                              int64_t* inds) {
+  return on_index(index, [&](IndexModel* m) {
+    RVC_CHECK_ARG(D == m->D, "index_search: query width " + std::to_string(D) + " != index width " +
+                                 std::to_string(m->D));
+    RVC_CHECK_ARG(F >= 0 && (F == 0 || (q && scores && inds)), "index_search: bad arguments");
+    m->search_host(q, F, k, scores, inds);
+    finish(m->ctx);
+  });
+}
+
+int32_t rvc_cuda_index_search_device(int64_t index, const float* q, int64_t F, int32_t D, int32_t k,
+                                     float* scores, int64_t* inds) {
+  return on_index(index, [&](IndexModel* m) {
+    RVC_CHECK_ARG(D == m->D, "index_search: query width does not match the index");
+    m->search_device(q, F, k, scores, inds);
+  });
+}
+
+int32_t rvc_cuda_index_blend(int64_t index, const float* q, int64_t F, int32_t D, int32_t k, int32_t mode,
+                             double index_rate, const float* feats, float* out) {
+  return on_index(index, [&](IndexModel* m) {
+    RVC_CHECK_ARG(D == m->D, "index_blend: query width does not match the index");
+    RVC_CHECK_ARG(F >= 0 && (F == 0 || (q && out)), "index_blend: bad arguments");
+    // blend * rate + feats * (1 - rate), each factor rounded to float32 as numpy does
+    m->blend_host(q, F, k, mode, (float)index_rate, (float)(1.0 - index_rate), feats, out);
+    finish(m->ctx);
+  });
+}
+
+int32_t rvc_cuda_index_blend_device(int64_t index, const float* q, int64_t F, int32_t D, int32_t k, int32_t mode,
+                                    double index_rate, const float* feats, float* out) {
+  return on_index(index, [&](IndexModel* m) {
+    RVC_CHECK_ARG(D == m->D, "index_blend: query width does not match the index");
+    m->blend_device(q, F, k, mode, (float)index_rate, (float)(1.0 - index_rate), feats, out);
+  });
 }
 
 }  // extern "C"

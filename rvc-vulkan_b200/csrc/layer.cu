@@ -124,6 +124,7 @@ void ConvLayer::run(Context* ctx, const ConvIO& io, bool force_simt) const {
   bool any_empty = false;  // a transposed-conv phase with no taps: output = epilogue(0)
   for (int s = 0; s < a.nslices; ++s) any_empty |= a.sl[s].ntaps == 0;
   const bool use_tc = tc && !force_simt && !any_empty && (io.x_ld % 4 == 0) && (io.x_bs % 4 == 0);
+  RVC_CHECK_ARG(use_tc || Wg.p, "conv: fp32 weights were released; only the tensor-core path can run this layer");
   if (use_tc) {
     cudaEvent_t e0 = nullptr, e1 = nullptr;
     if (ctx->prof) ctx->prof_begin(&e0, &e1);

@@ -47,6 +47,11 @@ struct ConvLayer {
   // Launch on ctx->stream.  force_simt: run the fp32 SIMT kernel.
   void run(Context* ctx, const ConvIO& io, bool force_simt = false) const;
   double flops(int B, int T_in) const;
+  // Drops the fp32 weight copy when the tensor-core form exists (the SIMT
+  // kernel, which reads it, is then unavailable for this layer).
+  void release_fp32() {
+    if (tc) Wg.reset();
+  }
 };
 
 }  // namespace rvc

@@ -1,0 +1,396 @@
+// Brute-force L2 retrieval on the device.
+//
+// Reference semantics: runtime.retrieval.search_l2 (runtime/retrieval.py:35-82):
+// dist = (||q||^2 + ||d||^2) - 2 q.d, clamped at 0, the k smallest per query in
+// ascending order; the pipeline blend (runtime/pipeline.py:545-551, :563-566)
+// and weighted_blend (runtime/retrieval.py:85-108).
+//
+// Plan per block of query rows:
+//   1. q.d for every index row: one tensor-core GEMM (the implicit-GEMM conv
+//      kernel with K = 1; the index is its resident "weight", packed once) into
+//      a [rows][Npad] fp32 block (Npad = N rounded up to 256, pad rows have
+//      ||d||^2 = +inf so they never win);
+//   2. a warp per query scans its row, forms the reference's fp32 distance and
+//      keeps the k + 8 smallest (value, index) in registers, then merges lanes;
+//   3. a warp per query re-ranks those candidates with the exact distance
+//      sum((q - d)^2) in float64 and writes the k best, ties to the lower index.
+// Step 3 makes the order independent of the GEMM's rounding: the result
+// matches the reference wherever the reference's own fp32 rounding does not
+// reorder two candidates.
+#include "retrieval.cuh"
+
+#include <cfloat>
+#include <cmath>
+
+namespace rvc {
+
+namespace {
+
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// out[r] = sum_d x[r][d]^2 (fp32), +inf for rows in [n_valid, rows).
+__global__ void row_sqnorm_kernel(const float* __restrict__ x, long long rows, long long n_valid, int D,
+                                  float* __restrict__ out) {
+  const long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  if (r >= n_valid) {
+    if (lane == 0) out[r] = INFINITY;
+    return;
+  }
+  float s = 0.f;
+  for (int d = lane; d < D; d += 32) {
+    const float v = x[r * D + d];
+    s = fmaf(v, v, s);
+  }
+  s = warp_sum_f(s);
+  if (lane == 0) out[r] = s;
+}
+
+// Lexicographic (value, index, lane) order; the lane makes it total so every
+// lane of a warp agrees on the winner.
+__device__ __forceinline__ bool before(float d1, int i1, int l1, float d2, int i2, int l2) {
+  if (d1 != d2) return d1 < d2;
+  if (i1 != i2) return (unsigned)i1 < (unsigned)i2;  // -1 (empty) sorts last
+  return l1 < l2;
+}
+
+template <int KC>
+__global__ void topk_approx_kernel(const float* __restrict__ dot, long long ld, const float* __restrict__ q2,
+                                   const float* __restrict__ d2, long long rows, long long npad,
+                                   int* __restrict__ cand) {
+  const long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  float dl[KC];
+  int il[KC];
+#pragma unroll
+  for (int j = 0; j < KC; ++j) {
+    dl[j] = INFINITY;
+    il[j] = -1;
+  }
+  const float qq = q2[r];
+  const float* row = dot + r * ld;
+  auto offer = [&](float dist, int col) {
+    if (dist < dl[KC - 1]) {
+      float cd = dist;
+      int ci = col;
+#pragma unroll
+      for (int j = 0; j < KC; ++j) {
+        if (cd < dl[j]) {  // strict: an equal value stays behind the earlier index
+          const float td = dl[j];
+          const int ti = il[j];
+          dl[j] = cd;
+          il[j] = ci;
+          cd = td;
+          ci = ti;
+        }
+      }
+    }
+  };
+  // four 16-byte loads in flight per lane (2 KB per warp) before any is used
+  for (long long base = 4ll * lane; base < npad; base += 512) {
+    float4 v[4], n2[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long long c0 = base + 128ll * u;
+      if (c0 < npad) {
+        v[u] = *reinterpret_cast<const float4*>(row + c0);
+        n2[u] = *reinterpret_cast<const float4*>(d2 + c0);
+      } else {
+        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        n2[u] = make_float4(INFINITY, INFINITY, INFINITY, INFINITY);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float x[4] = {v[u].x, v[u].y, v[u].z, v[u].w}, nn[4] = {n2[u].x, n2[u].y, n2[u].z, n2[u].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float dist = fmaxf((qq + nn[e]) - 2.f * x[e], 0.f);  // the reference's fp32 order
+        offer(dist, (int)(base + 128ll * u + e));
+      }
+    }
+  }
+  int* out = cand + r * KC;
+  for (int t = 0; t < KC; ++t) {
+    float bd = dl[0];
+    int bi = il[0], bl = lane;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float od = __shfl_xor_sync(0xffffffffu, bd, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      const int ol = __shfl_xor_sync(0xffffffffu, bl, o);
+      if (before(od, oi, ol, bd, bi, bl)) {
+        bd = od;
+        bi = oi;
+        bl = ol;
+      }
+    }
+    if (lane == bl) {
+#pragma unroll
+      for (int j = 0; j < KC - 1; ++j) {
+        dl[j] = dl[j + 1];
+        il[j] = il[j + 1];
+      }
+      dl[KC - 1] = INFINITY;
+      il[KC - 1] = -1;
+    }
+    if (lane == 0) out[t] = bi;
+  }
+}
+
+template <int KC>
+__global__ void rerank_kernel(const float* __restrict__ q, const float* __restrict__ db, int D,
+                              const int* __restrict__ cand, long long rows, int k, float* __restrict__ scores,
+                              long long* __restrict__ inds) {
+  const long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const float* qr = q + r * D;
+  double dd[KC];
+  int ci[KC];
+#pragma unroll
+  for (int j = 0; j < KC; ++j) {
+    ci[j] = cand[r * KC + j];
+    double s = 0.0;
+    if (ci[j] >= 0) {
+      const float* dr = db + (long long)ci[j] * D;
+      for (int d = lane; d < D; d += 32) {
+        const double t = (double)qr[d] - (double)dr[d];
+        s = fma(t, t, s);
+      }
+      s = warp_sum_d(s);
+    } else {
+      s = INFINITY;
+    }
+    dd[j] = s;
+  }
+  if (lane != 0) return;
+  bool used[KC];
+#pragma unroll
+  for (int j = 0; j < KC; ++j) used[j] = false;
+  for (int t = 0; t < k; ++t) {
+    int best = -1, bc = 0;
+    double bd = 0.0;
+#pragma unroll
+    for (int j = 0; j < KC; ++j) {
+      if (used[j] || ci[j] < 0) continue;
+      if (best < 0 || dd[j] < bd || (dd[j] == bd && ci[j] < bc)) {
+        best = j;
+        bd = dd[j];
+        bc = ci[j];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < KC; ++j)
+      if (j == best) used[j] = true;
+    const float sc = best >= 0 ? (float)bd : INFINITY;
+    const long long ix = best >= 0 ? (long long)bc : -1;
+    scores[r * k + t] = sc;
+    inds[r * k + t] = ix;
+  }
+}
+
+// numpy's float32 sum of a short contiguous row (pairwise_sum for n < 128):
+// n < 8 sequential; otherwise eight running sums folded as
+// ((r0 + r1) + (r2 + r3)) + ((r4 + r5) + (r6 + r7)), then the tail in order.
+__device__ __forceinline__ float np_sum(const float* a, int n) {
+  if (n < 8) {
+    float s = 0.f;
+    for (int i = 0; i < n; ++i) s += a[i];
+    return s;
+  }
+  float r[8];
+  for (int j = 0; j < 8; ++j) r[j] = a[j];
+  int i = 8;
+  for (; i < n - (n % 8); i += 8)
+    for (int j = 0; j < 8; ++j) r[j] += a[i + j];
+  float s = ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
+  for (; i < n; ++i) s += a[i];
+  return s;
+}
+
+__global__ void blend_kernel(const float* __restrict__ db, int D, const float* __restrict__ scores,
+                             const long long* __restrict__ inds, long long rows, int k, int mode, float c_blend,
+                             float c_feats, const float* __restrict__ feats, float* __restrict__ out) {
+  const long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  float w[IndexModel::kMaxK];
+  long long ix[IndexModel::kMaxK];
+  for (int j = 0; j < k; ++j) {
+    const float s = scores[r * k + j];
+    ix[j] = inds[r * k + j];
+    if (mode == 0) {
+      const float t = 1.f / s;  // np.square(1.0 / sc)
+      w[j] = t * t;
+    } else {
+      const float m = fmaxf(s, 1e-6f);  // 1.0 / np.maximum(s, 1e-6) ** 2, valid rows only
+      w[j] = ix[j] >= 0 ? 1.f / (m * m) : 0.f;
+    }
+  }
+  const float norm = fmaxf(np_sum(w, k), 1e-12f);
+  for (int j = 0; j < k; ++j) w[j] = w[j] / norm;
+  for (int d = lane; d < D; d += 32) {
+    float acc = 0.f;
+    bool first = true;
+    for (int j = 0; j < k; ++j) {
+      if (ix[j] < 0) continue;
+      const float p = db[ix[j] * D + d] * w[j];
+      acc = first ? p : acc + p;
+      first = false;
+    }
+    float o = acc;
+    if (feats) o = acc * c_blend + feats[r * D + d] * c_feats;
+    out[r * D + d] = o;
+  }
+}
+
+constexpr int kRows = 8;  // warps (query rows) per 256-thread block
+
+}  // namespace
+
+IndexModel::IndexModel(Context* c, const float* db, int64_t n, int d, int prec) : ctx(c), precision(prec) {
+  RVC_CHECK_ARG(n >= 1 && d >= 1, "index: N and D must be positive");
+  RVC_CHECK_ARG(n < (1ll << 31), "index: at most 2^31 - 1 rows");
+  RVC_CHECK_ARG(prec == 0 || prec == 1, "index: precision must be 0 (tensor cores) or 1 (fp32 SIMT)");
+  N = n;
+  D = d;
+  Npad = (n + 255) / 256 * 256;
+  cudaStream_t st = ctx->stream;
+  db_ = DevBuf(ctx, sizeof(float) * (size_t)N * D);
+  RVC_CUDA_TRY(cudaMemcpyAsync(db_.p, db, db_.bytes, cudaMemcpyHostToDevice, st));
+  d2_ = DevBuf(ctx, sizeof(float) * (size_t)Npad);
+  row_sqnorm_kernel<<<(unsigned)((Npad + kRows - 1) / kRows), 32 * kRows, 0, st>>>(db_.f(), Npad, N, D, d2_.f());
+  note_launch();
+  RVC_CUDA_TRY(cudaGetLastError());
+  {
+    // the GEMM's [C_out = Npad][C_in = D] operand: the index rows plus zero pad rows
+    DevBuf padded(ctx, sizeof(float) * (size_t)Npad * D);  // zero-filled
+    RVC_CUDA_TRY(cudaMemcpyAsync(padded.p, db_.p, db_.bytes, cudaMemcpyDeviceToDevice, st));
+    gemm_.build(ctx, LayerKind::kConv, padded.f(), nullptr, (int)Npad, D, 1, precision == 0);
+  }
+  if (precision == 0) gemm_.release_fp32();  // the packed tensor-core copy is all the GEMM reads
+  RVC_CUDA_TRY(cudaStreamSynchronize(st));
+}
+
+void IndexModel::ensure_ws(int64_t rows) {
+  if (rows <= ws_rows_) return;
+  dot_ = DevBuf();
+  dot_ = DevBuf(ctx, sizeof(float) * (size_t)rows * Npad);
+  q2_ = DevBuf(ctx, sizeof(float) * (size_t)rows);
+  cand_ = DevBuf(ctx, sizeof(int) * (size_t)rows * (kMaxK + kExtra));
+  sc_ = DevBuf(ctx, sizeof(float) * (size_t)rows * kMaxK);
+  ix_ = DevBuf(ctx, sizeof(long long) * (size_t)rows * kMaxK);
+  ws_rows_ = rows;
+}
+
+void IndexModel::search_device(const float* q, int64_t F, int k, float* scores, int64_t* inds) {
+  RVC_CHECK_ARG(k >= 1 && k <= kMaxK, "index_search: k must be in [1, 16]");
+  RVC_CHECK_ARG(F >= 0, "index_search: negative query count");
+  if (F == 0) return;
+  const int kk = (int)std::min<int64_t>(k, N);
+  cudaStream_t st = ctx->stream;
+  // query rows per block: the distance block stays within ~2 GiB
+  int64_t chunk = std::max<int64_t>(128, ((int64_t)1 << 29) / Npad);
+  chunk = std::min<int64_t>(chunk, F);
+  ensure_ws(chunk);
+  const int KC = kk + kExtra <= 16 ? 16 : 24;
+  for (int64_t r0 = 0; r0 < F; r0 += chunk) {
+    const int64_t rows = std::min<int64_t>(chunk, F - r0);
+    const float* qb = q + r0 * D;
+    row_sqnorm_kernel<<<(unsigned)((rows + kRows - 1) / kRows), 32 * kRows, 0, st>>>(qb, rows, rows, D, q2_.f());
+    note_launch();
+    RVC_CUDA_TRY(cudaGetLastError());
+    ConvIO io;
+    io.x = qb; io.x_ld = D; io.x_bs = rows * D; io.T_in = (int)rows;
+    io.y = dot_.f(); io.y_ld = (int)Npad; io.y_bs = rows * Npad;
+    io.B = 1;
+    gemm_.run(ctx, io, precision == 1);
+    const unsigned grid = (unsigned)((rows + kRows - 1) / kRows);
+    if (KC == 16) {
+      topk_approx_kernel<16><<<grid, 32 * kRows, 0, st>>>(dot_.f(), Npad, q2_.f(), d2_.f(), rows, Npad, cand_.as<int>());
+      note_launch();
+      rerank_kernel<16><<<grid, 32 * kRows, 0, st>>>(qb, db_.f(), D, cand_.as<int>(), rows, kk, scores + r0 * kk,
+                                                     (long long*)inds + r0 * kk);
+    } else {
+      topk_approx_kernel<24><<<grid, 32 * kRows, 0, st>>>(dot_.f(), Npad, q2_.f(), d2_.f(), rows, Npad, cand_.as<int>());
+      note_launch();
+      rerank_kernel<24><<<grid, 32 * kRows, 0, st>>>(qb, db_.f(), D, cand_.as<int>(), rows, kk, scores + r0 * kk,
+                                                     (long long*)inds + r0 * kk);
+    }
+    note_launch();
+    RVC_CUDA_TRY(cudaGetLastError());
+  }
+}
+
+void IndexModel::blend_device(const float* q, int64_t F, int k, int mode, float c_blend, float c_feats,
+                              const float* feats, float* out) {
+  RVC_CHECK_ARG(mode == 0 || mode == 1, "index_blend: mode must be 0 (pipeline) or 1 (weighted_blend)");
+  RVC_CHECK_ARG(k >= 1 && k <= kMaxK, "index_blend: k must be in [1, 16]");
+  if (F == 0) return;
+  const int kk = (int)std::min<int64_t>(k, N);
+  int64_t chunk = std::max<int64_t>(128, ((int64_t)1 << 29) / Npad);
+  chunk = std::min<int64_t>(chunk, F);
+  ensure_ws(chunk);
+  cudaStream_t st = ctx->stream;
+  for (int64_t r0 = 0; r0 < F; r0 += chunk) {
+    const int64_t rows = std::min<int64_t>(chunk, F - r0);
+    search_device(q + r0 * D, rows, kk, sc_.f(), ix_.as<int64_t>());
+    blend_kernel<<<(unsigned)((rows + kRows - 1) / kRows), 32 * kRows, 0, st>>>(
+        db_.f(), D, sc_.f(), ix_.as<long long>(), rows, kk, mode, c_blend, c_feats, feats ? feats + r0 * D : nullptr,
+        out + r0 * D);
+    note_launch();
+    RVC_CUDA_TRY(cudaGetLastError());
+  }
+}
+
+void IndexModel::stage(DevBuf& b, size_t bytes) {
+  if (b.bytes < bytes) {
+    b = DevBuf();
+    b = DevBuf(ctx, bytes);
+  }
+}
+
+void IndexModel::search_host(const float* q, int64_t F, int k, float* scores, int64_t* inds) {
+  RVC_CHECK_ARG(k >= 1 && k <= kMaxK, "index_search: k must be in [1, 16]");
+  if (F <= 0) return;
+  const int kk = (int)std::min<int64_t>(k, N);
+  cudaStream_t st = ctx->stream;
+  stage(h_q_, sizeof(float) * (size_t)F * D);
+  stage(h_s_, sizeof(float) * (size_t)F * kk);
+  stage(h_i_, sizeof(int64_t) * (size_t)F * kk);
+  RVC_CUDA_TRY(cudaMemcpyAsync(h_q_.p, q, sizeof(float) * (size_t)F * D, cudaMemcpyHostToDevice, st));
+  search_device(h_q_.f(), F, k, h_s_.f(), h_i_.as<int64_t>());
+  RVC_CUDA_TRY(cudaMemcpyAsync(scores, h_s_.p, sizeof(float) * (size_t)F * kk, cudaMemcpyDeviceToHost, st));
+  RVC_CUDA_TRY(cudaMemcpyAsync(inds, h_i_.p, sizeof(int64_t) * (size_t)F * kk, cudaMemcpyDeviceToHost, st));
+}
+
+void IndexModel::blend_host(const float* q, int64_t F, int k, int mode, float c_blend, float c_feats,
+                            const float* feats, float* out) {
+  if (F <= 0) return;
+  cudaStream_t st = ctx->stream;
+  const size_t nb = sizeof(float) * (size_t)F * D;
+  stage(h_q_, nb);
+  stage(h_o_, nb);
+  RVC_CUDA_TRY(cudaMemcpyAsync(h_q_.p, q, nb, cudaMemcpyHostToDevice, st));
+  if (feats) {
+    stage(h_f_, nb);
+    RVC_CUDA_TRY(cudaMemcpyAsync(h_f_.p, feats, nb, cudaMemcpyHostToDevice, st));
+  }
+  blend_device(h_q_.f(), F, k, mode, c_blend, c_feats, feats ? h_f_.f() : nullptr, h_o_.f());
+  RVC_CUDA_TRY(cudaMemcpyAsync(out, h_o_.p, nb, cudaMemcpyDeviceToHost, st));
+}
+
+}  // namespace rvc

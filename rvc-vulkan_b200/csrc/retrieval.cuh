@@ -1,0 +1,42 @@
+// Device-resident feature index: brute-force L2 top-k search and the
+// inverse-squared-distance blend of the retrieved vectors.
+#pragma once
+
+#include "layer.cuh"
+
+namespace rvc {
+
+class IndexModel {
+ public:
+  static constexpr int kMaxK = 16;   // largest k served
+  static constexpr int kExtra = 8;   // extra approximate candidates re-ranked exactly
+
+  // db: host [N][D] float32 (copied to the device).
+  IndexModel(Context* ctx, const float* db, int64_t N, int D, int precision);
+  // Device pointers, asynchronous on ctx->stream: q [F][D] -> scores/inds [F][min(k, N)].
+  void search_device(const float* q, int64_t F, int k, float* scores, int64_t* inds);
+  // Device pointers: out [F][D] = blend (mode 0: w = (1/s)^2, the pipeline's formula;
+  // mode 1: w = 1/max(s,1e-6)^2, weighted_blend), mixed with feats when feats != nullptr:
+  // out = blend * c_blend + feats * c_feats.
+  void blend_device(const float* q, int64_t F, int k, int mode, float c_blend, float c_feats, const float* feats,
+                    float* out);
+  // Host-pointer versions (inputs staged through buffers the model keeps).
+  void search_host(const float* q, int64_t F, int k, float* scores, int64_t* inds);
+  void blend_host(const float* q, int64_t F, int k, int mode, float c_blend, float c_feats, const float* feats,
+                  float* out);
+  int64_t N = 0, Npad = 0;
+  int D = 0;
+  Context* ctx;
+  int precision;
+
+ private:
+  void ensure_ws(int64_t rows);
+  DevBuf db_, d2_;
+  ConvLayer gemm_;
+  int64_t ws_rows_ = 0;
+  DevBuf dot_, q2_, cand_, sc_, ix_;
+  DevBuf h_q_, h_f_, h_o_, h_s_, h_i_;  // staging for the host-pointer calls
+  void stage(DevBuf& b, size_t bytes);
+};
+
+}  // namespace rvc

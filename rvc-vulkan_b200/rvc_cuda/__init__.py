@@ -7,7 +7,8 @@ Drop-in for jiangchengnay/rvc-vulkan's numpy runtime:
   ``runtime.nn`` float32 ops through ``rvc_cuda.ops``.
 * ``patch_reference()`` installs the whole-model fast paths
   (``rvc_cuda.synth.patch_reference`` for ``SynthesizerTrn``,
-  ``rvc_cuda.hubert.patch_reference`` for ``HubertEncoder``).
+  ``rvc_cuda.hubert.patch_reference`` for ``HubertEncoder``,
+  ``rvc_cuda.retrieval.patch_reference`` for the brute-force ``search_l2``).
 
 Importing this package does not touch the GPU; the shared library is loaded
 on first use of ``rvc_cuda.ops`` / ``rvc_cuda.synth`` and raises if missing.
@@ -42,7 +43,8 @@ def register(name: str = "cuda") -> None:
 
 def patch_reference(device=None, precision: str = "bf16x3") -> None:
     """Install the model-level CUDA paths on the reference's model classes."""
-    from . import hubert, synth  # noqa: PLC0415
+    from . import hubert, retrieval, synth  # noqa: PLC0415
 
     synth.patch_reference(device=device, precision=precision)
     hubert.patch_reference(device=device, precision=precision)
+    retrieval.patch_reference()

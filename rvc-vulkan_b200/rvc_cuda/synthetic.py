@@ -28,7 +28,7 @@ import numpy as np
 __all__ = [
     "VITS_V2_40K", "VITS_V2_48K", "vits_config_array", "make_vits_weights",
     "make_vits_inputs", "make_vits_noise", "make_hubert_weights",
-    "make_hubert_input", "coarse_pitch",
+    "make_hubert_input", "coarse_pitch", "make_index", "make_queries",
 ]
 
 # (sr, upsample_rates, upsample_kernels) of the two measured v2 generators.
@@ -235,3 +235,15 @@ def make_hubert_input(T: int = 160000, seed: int = 0) -> np.ndarray:
     """16 kHz waveform ``[1,T] f32 ~U(-0.5,0.5)``."""
     rs = np.random.RandomState(30_000 + seed)
     return rs.uniform(-0.5, 0.5, size=(1, T)).astype(np.float32)
+
+
+def make_index(N: int, D: int = 768, seed: int = 0) -> np.ndarray:
+    """Feature index ``[N,D] f32 ~N(0,1)`` (200000 x 768)."""
+    rs = np.random.RandomState(40_000 + seed)
+    return rs.standard_normal((N, D)).astype(np.float32)
+
+
+def make_queries(F: int, D: int = 768, seed: int = 0) -> np.ndarray:
+    """Retrieval queries ``[F,D] f32 ~N(0,1)`` (one per feature frame)."""
+    rs = np.random.RandomState(50_000 + seed)
+    return rs.standard_normal((F, D)).astype(np.float32)

@@ -7,8 +7,9 @@ Run in a container where the reference checkout is present::
 It imports ``runtime`` from the reference (read-only, ``RVC_BACKEND=numpy``),
 replaces the checkpoint loaders with the seeded synthetic checkpoints of
 ``rvc_cuda.synthetic`` (the loaders read files; no checkpoints exist here),
-runs ``SynthesizerTrn.infer_controlled`` / ``HubertEncoder.encode`` and the
-per-op numpy kernels, and writes ``tests/golden/*.npz``.  Weights and inputs
+runs ``SynthesizerTrn.infer_controlled`` / ``HubertEncoder.encode``, the
+retrieval search (``runtime.retrieval.search_l2``) and the per-op numpy
+kernels, and writes ``tests/golden/*.npz``.  Weights and inputs
 are not stored: they are regenerated from the recorded seeds (legacy
 ``RandomState`` streams are frozen) and checked against recorded SHA-256
 digests, so a drift in generation is detected rather than silently compared.
@@ -56,6 +57,13 @@ VITS_CASES = [
 HUBERT_CASES = [
     ("hubert_t8000", 8000, 0, 1),
     ("hubert_t3201", 3201, 0, 2),           # odd length: ragged conv strides
+]
+# (name, F queries, N index rows, D, k, index seed, query seed)
+RETRIEVAL_CASES = [
+    ("ret_f200_n20000", 200, 20000, 768, 8, 0, 0),   # several 4096-row merge chunks
+    ("ret_f64_n3000_d256", 64, 3000, 256, 8, 1, 1),  # v1 feature width
+    ("ret_f37_n5", 37, 5, 768, 8, 2, 2),             # N < k: k' = N
+    ("ret_f9_n1000_d60", 9, 1000, 60, 3, 3, 3),      # D not a multiple of 16, k = 3
 ]
 
 
@@ -115,6 +123,24 @@ def run_hubert(runtime_hubert, name, T, wseed, iseed, meta):
                   "weights_sha256": weights_digest(sd), "inputs_sha256": digest([x])}
 
 
+def run_retrieval(retrieval, name, F, N, D, k, iseed, qseed, meta):
+    """The reference's ``search_l2`` and ``weighted_blend`` (``runtime/retrieval.py:35-108``)
+    plus the pipeline blend written exactly as ``runtime/pipeline.py:547-551`` does it."""
+    db = syn.make_index(N, D, iseed)
+    q = syn.make_queries(F, D, qseed)
+    sc, ix = retrieval.search_l2(q, db, k=k)
+    blk = db[ix]
+    w = np.square(1.0 / sc)
+    w /= np.maximum(w.sum(axis=1, keepdims=True), 1e-12)
+    pipe = np.sum(blk * w[:, :, None], axis=1)
+    wb = retrieval.weighted_blend(q, db, k=k)
+    # blends of the first 16 queries keep the fixture small; all scores/indices are stored
+    np.savez_compressed(os.path.join(HERE, name + ".npz"), scores=sc, inds=ix, blend=pipe[:16],
+                        weighted=wb[:16])
+    meta[name] = {"kind": "retrieval", "F": F, "N": N, "D": D, "k": k, "index_seed": iseed, "query_seed": qseed,
+                  "inputs_sha256": digest([db, q])}
+
+
 def run_ops(nn, meta):
     """Per-op vectors from ``runtime.nn``'s numpy kernels (``_conv1d_numpy`` etc.)."""
     rs = np.random.RandomState(4242)
@@ -163,7 +189,7 @@ def run_ops(nn, meta):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("RVC_REFERENCE", "/root/reference"))
-    ap.add_argument("--only", choices=["vits", "hubert", "ops"], default=None,
+    ap.add_argument("--only", choices=["vits", "hubert", "ops", "retrieval"], default=None,
                     help="regenerate one family and keep the other fixtures")
     args = ap.parse_args()
     os.environ["RVC_BACKEND"] = "numpy"
@@ -187,6 +213,10 @@ def main():
             run_hubert(runtime_hubert, *c, meta)
     if args.only in (None, "ops"):
         run_ops(nn, meta)
+    if args.only in (None, "retrieval"):
+        from runtime import retrieval  # noqa: PLC0415
+        for c in RETRIEVAL_CASES:
+            run_retrieval(retrieval, *c, meta)
     with open(os.path.join(HERE, "golden.json"), "w") as f:
         json.dump(meta, f, indent=1, sort_keys=True)
     print("wrote", sorted(k for k in meta if k not in ("numpy", "numba", "blas")))

@@ -98,3 +98,16 @@ def test_hubert_patch_reference_replaces_class_methods():
     assert FakeEncoder.encode is not FakeEncoder._rvc_cuda_orig_encode
     assert FakeEncoder.encode_batch is not FakeEncoder._rvc_cuda_orig_encode_batch
     assert hubert.patch_reference(FakeModule) is FakeEncoder  # idempotent
+
+
+def test_retrieval_patch_reference_replaces_module_functions():
+    import types
+
+    from rvc_cuda import retrieval
+
+    ret_mod = types.SimpleNamespace(search_l2=lambda *a, **k: "numpy", weighted_blend=lambda *a, **k: "numpy")
+    pipe_mod = types.SimpleNamespace(search_l2=ret_mod.search_l2)
+    retrieval.patch_reference(ret_mod, pipe_mod)
+    assert ret_mod.search_l2 is retrieval.search_l2 and pipe_mod.search_l2 is retrieval.search_l2
+    assert ret_mod.weighted_blend is retrieval.weighted_blend
+    assert ret_mod._rvc_cuda_orig_search_l2() == "numpy"

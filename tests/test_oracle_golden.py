@@ -12,6 +12,7 @@ import pytest
 from tests.conftest import load_golden, rel_l2
 from oracle import hubert as OH
 from oracle import ops as O
+from oracle import retrieval as OR
 from oracle import vits as OV
 from rvc_cuda import synthetic as syn
 from tests.golden.make_golden import digest, weights_digest
@@ -74,3 +75,20 @@ def test_ops_oracle_matches_reference(golden_meta):
     np.testing.assert_allclose(O.softmax(g["sm_x"]), g["sm_y"], rtol=1e-6, atol=1e-7)
     np.testing.assert_allclose(O.gelu_erf(g["gelu_x"]), g["gelu_y"], rtol=1e-6, atol=1e-6)
     np.testing.assert_array_equal(O.leaky_relu(g["leaky_x"], 0.1), g["leaky_y"])
+
+
+RET = ["ret_f200_n20000", "ret_f64_n3000_d256", "ret_f37_n5", "ret_f9_n1000_d60"]
+
+
+@pytest.mark.parametrize("name", RET)
+def test_retrieval_oracle_matches_reference(name, golden_meta):
+    m = golden_meta[name]
+    db = syn.make_index(m["N"], m["D"], m["index_seed"])
+    q = syn.make_queries(m["F"], m["D"], m["query_seed"])
+    assert digest([db, q]) == m["inputs_sha256"]
+    g = load_golden(name)
+    sc, ix = OR.search_l2(q, db, k=m["k"])
+    np.testing.assert_array_equal(ix, g["inds"])
+    np.testing.assert_allclose(sc, g["scores"], rtol=1e-6, atol=1e-4)
+    n = g["blend"].shape[0]
+    np.testing.assert_allclose(OR.blend(q[:n], db, k=m["k"]), g["blend"], rtol=1e-5, atol=1e-6)

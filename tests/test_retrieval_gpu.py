@@ -1,0 +1,106 @@
+"""Retrieval parity: the device index (C ABI) against the reference's own
+search_l2 / blend outputs (golden fixtures) and the oracle.
+
+Bar: top-k indices bit-exact.  The device re-ranks its
+candidates with the exact float64 distance, so it can only differ from the
+fp32 reference where the reference's own rounding reorders two candidates
+whose distances agree to ~1e-4; the large random case checks that every
+difference is such a tie.  Scores: rel 1e-6 / abs 1e-3; blends: rel 1e-5.
+"""
+
+import numpy as np
+import pytest
+
+from oracle import retrieval as OR
+from rvc_cuda import synthetic as syn
+from tests.conftest import load_golden
+
+pytestmark = pytest.mark.gpu
+
+ret = pytest.importorskip("rvc_cuda.retrieval")
+
+GOLD = ["ret_f200_n20000", "ret_f64_n3000_d256", "ret_f37_n5", "ret_f9_n1000_d60"]
+
+
+@pytest.mark.parametrize("name", GOLD)
+def test_search_matches_reference_golden(name, golden_meta):
+    m = golden_meta[name]
+    db = syn.make_index(m["N"], m["D"], m["index_seed"])
+    q = syn.make_queries(m["F"], m["D"], m["query_seed"])
+    g = load_golden(name)
+    idx = ret.CudaIndex(db)
+    sc, ix = idx.search(q, m["k"])
+    assert ix.shape == g["inds"].shape and ix.dtype == np.int64
+    np.testing.assert_array_equal(ix, g["inds"])
+    np.testing.assert_allclose(sc, g["scores"], rtol=1e-6, atol=1e-3)
+    n = g["blend"].shape[0]
+    np.testing.assert_allclose(idx.blend(q[:n], m["k"]), g["blend"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(idx.blend(q[:n], m["k"], mode="weighted"), g["weighted"], rtol=1e-5, atol=1e-6)
+
+
+def _check_against_oracle(ix, sc, rix, rsc, tie_tol=1e-3):
+    """Exact equality, except positions where the oracle's own distances are a
+    near-tie (the swapped candidates' oracle scores agree within tie_tol)."""
+    diff = np.argwhere(ix != rix)
+    for r, j in diff:
+        a, b = ix[r, j], rix[r, j]
+        row = dict(zip(rix[r].tolist(), rsc[r].tolist()))
+        assert a in row, f"row {r}: index {a} not in the reference top-k"
+        assert abs(row[a] - row[b]) <= tie_tol, f"row {r} pos {j}: {a} vs {b} not a tie"
+    np.testing.assert_allclose(sc, rsc, rtol=1e-6, atol=1e-3)
+    return len(diff)
+
+
+def test_config4_index_size_against_oracle():
+    """BASELINE config 4 index (200000 x 768 ~N(0,1)), 256 queries."""
+    db = syn.make_index(200000, 768, 7)
+    q = syn.make_queries(256, 768, 7)
+    idx = ret.CudaIndex(db)
+    sc, ix = idx.search(q, 8)
+    rsc, rix = OR.search_l2(q, db, 8)
+    ndiff = _check_against_oracle(ix, sc, rix, rsc)
+    assert ndiff <= 2
+    feats = syn.make_queries(256, 768, 8)
+    got = idx.blend(q, 8, feats=feats, index_rate=0.75)
+    blended = OR.blend(q, db, 8)
+    ref = OR.mix(feats, blended, 0.75)
+    if ndiff == 0:
+        np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-5)
+
+
+def test_k_range_simt_path_and_ties():
+    db = syn.make_index(5000, 768, 9)
+    db[4000] = db[17]  # an exact duplicate: equal distances, lower index first
+    q = np.concatenate([db[17:18] + 0.01, syn.make_queries(40, 768, 9)], axis=0)
+    for prec in ("bf16x3", "simt"):
+        idx = ret.CudaIndex(db, precision=prec)
+        for k in (1, 8, 16):
+            sc, ix = idx.search(q, k)
+            rsc, rix = OR.search_l2(q, db, k)
+            assert ix.shape == (41, k)
+            assert ix[0, 0] == 17 and (k == 1 or ix[0, 1] == 4000)
+            _check_against_oracle(ix[1:], sc[1:], rix[1:], rsc[1:])
+
+
+def test_bad_arguments_and_empty_queries():
+    idx = ret.CudaIndex(syn.make_index(300, 64, 1))
+    with pytest.raises(ValueError):
+        idx.search(np.zeros((3, 63), np.float32), 8)
+    with pytest.raises(ValueError):
+        idx.search(np.zeros((3, 64), np.float32), 0)
+    with pytest.raises(ValueError):
+        idx.search(np.zeros((3, 64), np.float32), 17)
+    sc, ix = idx.search(np.zeros((0, 64), np.float32), 8)
+    assert sc.shape == (0, 8) and ix.shape == (0, 8)
+    with pytest.raises(ValueError):
+        ret.CudaIndex(np.zeros((0, 64), np.float32))
+
+
+def test_dropin_search_l2_caches_one_index_per_array():
+    db = syn.make_index(3000, 128, 4)
+    q = syn.make_queries(10, 128, 4)
+    a = ret.search_l2(q, db, k=8)
+    b = ret.search_l2(q, db, k=8)
+    assert ret._index_for(db) is ret._index_for(db)
+    np.testing.assert_array_equal(a[1], b[1])
+    np.testing.assert_array_equal(a[1], OR.search_l2(q, db, 8)[1])
