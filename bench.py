@@ -292,6 +292,158 @@ def run_hubert(args, world, rank, local):
         dist.destroy_process_group()
 
 
+def retrieval_cpu_sample(N, D, F, steps=1):
+    """Time the retrieval oracle (restated search_l2 + pipeline blend) on F queries."""
+    from oracle import retrieval as OR
+    from rvc_cuda import synthetic as syn
+    db = syn.make_index(N, D, 0)
+    q = syn.make_queries(F, D, 1)
+    ts = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        OR.blend(q, db, 8)
+        ts.append(time.perf_counter() - t0)
+    return F / 50.0, ts
+
+
+def run_retrieval(args, world, rank, local):
+    """BASELINE config 4's retrieval stage: F = 50 frames/s x --audio-s queries
+    against a --index-rows x 768 index, top-8 + inverse-squared-distance blend + mix."""
+    import torch
+
+    from rvc_cuda import _lib, synthetic as syn
+    from rvc_cuda.retrieval import CudaIndex
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    N, D = args.index_rows, 768
+    F_total = int(round(args.audio_s * 50))
+    assert F_total % world == 0, "queries must split evenly across ranks"
+    F = F_total // world
+    db = syn.make_index(N, D, 0)
+    idx = CudaIndex(db, device=local, precision=args.precision)
+    ctx = idx.ctx
+    h_q = torch.empty((F, D), dtype=torch.float32, pin_memory=True).numpy()
+    h_f = torch.empty((F, D), dtype=torch.float32, pin_memory=True).numpy()
+    h_o = torch.empty((F, D), dtype=torch.float32, pin_memory=True).numpy()
+    h_q[:] = syn.make_queries(F, D, 1 + rank)
+    h_f[:] = syn.make_queries(F, D, 100 + rank)
+    d_q, d_f, d_o = ctx.alloc(h_q.nbytes), ctx.alloc(h_f.nbytes), ctx.alloc(h_o.nbytes)
+    ctx.h2d(d_q, h_q)
+    ctx.h2d(d_f, h_f)
+
+    def step_device():
+        _lib.check(_lib.lib.rvc_cuda_index_blend_device(idx.handle, _lib._p(d_q), F, D, 8, 0, 0.75, _lib._p(d_f),
+                                                        _lib._p(d_o)))
+
+    def step_e2e():
+        h_o[:] = idx.blend(h_q, 8, feats=h_f, index_rate=0.75)
+
+    stream = torch.cuda.ExternalStream(ctx.stream(), device=local)
+
+    def timed(fn, steps):
+        barrier()
+        ctx.sync()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        ctx.sync()
+        torch.cuda.synchronize()
+        barrier()
+        return e0.elapsed_time(e1) / 1e3
+
+    for _ in range(args.warmup):
+        step_device()
+    ctx.sync()
+    n0 = _lib.launch_count()
+    ctx.profile(True)
+    with ClockSampler(local) as clk:
+        t = timed(step_device, args.steps)
+    prof_n, prof_ms, prof_flops = ctx.profile_read()
+    if args.profile_out and rank == 0:
+        with open(args.profile_out, "w") as f:
+            f.write(ctx.profile_dump())
+    ctx.profile(False)
+    launches = _lib.launch_count() - n0
+    t = max_over_ranks(t)
+    audio_per_step = F_total / 50.0
+    value = audio_per_step * args.steps / t
+    step_e2e()
+    te = max_over_ranks(timed(step_e2e, args.steps))
+    if rank == 0:
+        pb, ps, hbm, src = peaks()
+        achieved = prof_flops / (prof_ms / 1e3) / 1e12 if prof_ms > 0 else None
+        line = {
+            "metric": "seconds of audio retrieved per wall-second (top-8 L2 search + blend)", "value": value,
+            "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * t / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32 (BF16x3 GEMM on tcgen05 + float64 re-rank)",
+            "data": "synthetic: index and queries ~N(0,1), seeded",
+            "config": {"workload": f"config4 retrieval stage: {F_total} queries ({args.audio_s:g} s of frames) "
+                                   f"x {N} x {D} index, top-8, blend, index_rate 0.75",
+                       "queries": F_total, "index_rows": N, "dim": D, "precision": args.precision,
+                       "l2": "index (614 MB) larger than L2",
+                       "parallelism": f"queries sharded x{world}, index replicated, no collective"},
+            "roofline": {"bound": "tensor", "kernel": "tc_conv_kernel (q . d GEMM)", "achieved": achieved,
+                         "peak": ps, "unit": "TFLOP/s", "frac": (achieved / ps) if achieved else None,
+                         "traffic": None, "peak_source": f"{src} bf16 dense sustained",
+                         "note": "useful 2*F*N*D FLOPs / GEMM time; BF16x3 => frac <= 1/3",
+                         "launches": prof_n, "kernel_ms_per_step": prof_ms / args.steps},
+            "e2e": {"value": audio_per_step * args.steps / te, "unit": UNIT,
+                    "h2d_bytes_per_step": 2 * h_q.nbytes * world, "d2h_bytes_per_step": h_o.nbytes * world},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+            "finite": bool(np.isfinite(h_o).all()),
+        }
+        if world == 1 and not args.no_cpu:
+            audio_s, ts = retrieval_cpu_sample(N, D, 500, steps=1)
+            line["cpu_baseline"] = {"value": audio_s / ts[0], "unit": UNIT, "cores": blas_threads(), "kind": "port",
+                                    "sample": f"500 queries ({audio_s:g} s of frames) x {N} x {D}, CPU oracle"}
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def run_retrieval_reference(args, world, rank):
+    if rank != 0:
+        return
+    retrieval_cpu_sample(args.index_rows, 768, 500, steps=max(1, min(args.warmup, 1)))
+    audio_s, ts = retrieval_cpu_sample(args.index_rows, 768, 500, steps=args.steps)
+    t = sum(ts)
+    value = audio_s * len(ts) / t
+    line = {
+        "impl": "reference", "metric": "seconds of audio retrieved per wall-second (top-8 L2 search + blend)",
+        "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * t / len(ts), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded)",
+        "config": {"workload": "config4 retrieval stage, CPU sample", "queries": 500, "index_rows": args.index_rows},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": blas_threads(), "kind": "port",
+                         "sample": f"500 queries per step x {args.index_rows} x 768, CPU oracle"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_hubert_reference(args, world, rank):
     if rank != 0:
         return
@@ -476,12 +628,20 @@ def main():
     ap.add_argument("--ref-frames", type=int, default=100)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile-out", default="", help="write the per-layer conv profile (CSV) here")
-    ap.add_argument("--workload", default="synth", choices=["synth", "hubert"],
-                    help="synth: config 3 (headline); hubert: config 1 (HuBERT-base encoder)")
+    ap.add_argument("--workload", default="synth", choices=["synth", "hubert", "retrieval"],
+                    help="synth: config 3 (headline); hubert: config 1 (HuBERT-base encoder); "
+                         "retrieval: config 4's top-8 search + blend")
     ap.add_argument("--samples", type=int, default=160000, help="hubert: samples per chunk")
+    ap.add_argument("--audio-s", type=float, default=60.0, help="retrieval: seconds of frames (50 per s)")
+    ap.add_argument("--index-rows", type=int, default=200000, help="retrieval: index rows")
     args = ap.parse_args()
     world, rank, local = dist_setup()
-    if args.workload == "hubert":
+    if args.workload == "retrieval":
+        if args.impl == "reference":
+            run_retrieval_reference(args, world, rank)
+        else:
+            run_retrieval(args, world, rank, local)
+    elif args.workload == "hubert":
         if args.impl == "reference":
             run_hubert_reference(args, world, rank)
         else:
