@@ -29,6 +29,7 @@ __all__ = [
     "VITS_V2_40K", "VITS_V2_48K", "vits_config_array", "make_vits_weights",
     "make_vits_inputs", "make_vits_noise", "make_hubert_weights",
     "make_hubert_input", "coarse_pitch", "make_index", "make_queries",
+    "make_rmvpe_weights", "make_rmvpe_input", "RMVPE_ENC", "RMVPE_INTER", "RMVPE_DEC",
 ]
 
 # (sr, upsample_rates, upsample_kernels) of the two measured v2 generators.
@@ -247,3 +248,73 @@ def make_queries(F: int, D: int = 768, seed: int = 0) -> np.ndarray:
     """Retrieval queries ``[F,D] f32 ~N(0,1)`` (one per feature frame)."""
     rs = np.random.RandomState(50_000 + seed)
     return rs.standard_normal((F, D)).astype(np.float32)
+
+
+# RMVPE E2E(4, 1, (2, 2)) channel plan (runtime/models/rmvpe.py:7-22):
+# (in, out) per encoder / intermediate / decoder layer, 4 ConvBlockRes each.
+RMVPE_ENC = [(1, 16), (16, 32), (32, 64), (64, 128), (128, 256)]
+RMVPE_INTER = [(256, 512), (512, 512), (512, 512), (512, 512)]
+RMVPE_DEC = [(512, 256), (256, 128), (128, 64), (64, 32), (32, 16)]
+
+
+def make_rmvpe_weights(seed: int = 0) -> dict:
+    """Random-init RMVPE state dict (He-scaled conv weights,
+    BatchNorm statistics near (0, 1)).  Keys follow the reference's use of the
+    checkpoint (``runtime/models/rmvpe.py:486-547``, ``:643-751``)."""
+    G = _Gen(60_000 + seed)
+
+    def conv(o, i, kh, kw):
+        return G.n(o, i, kh, kw, std=math.sqrt(2.0 / (i * kh * kw)))
+
+    def bn(sd, p, c):
+        sd[p + ".weight"] = (1.0 + 0.1 * G.rs.standard_normal(c)).astype(np.float32)
+        sd[p + ".bias"] = (0.1 * G.rs.standard_normal(c)).astype(np.float32)
+        sd[p + ".running_mean"] = (0.1 * G.rs.standard_normal(c)).astype(np.float32)
+        sd[p + ".running_var"] = G.rs.uniform(0.5, 1.5, c).astype(np.float32)
+        sd[p + ".num_batches_tracked"] = np.zeros((), np.float32)
+
+    def block(sd, p, cin, cout):
+        sd[p + ".conv.0.weight"] = conv(cout, cin, 3, 3)
+        bn(sd, p + ".conv.1", cout)
+        sd[p + ".conv.3.weight"] = conv(cout, cout, 3, 3)
+        bn(sd, p + ".conv.4", cout)
+        if cin != cout:
+            sd[p + ".shortcut.weight"] = conv(cout, cin, 1, 1)
+            sd[p + ".shortcut.bias"] = (0.1 * G.rs.standard_normal(cout)).astype(np.float32)
+
+    sd: dict = {}
+    bn(sd, "unet.encoder.bn", 1)
+    for i, (ci, co) in enumerate(RMVPE_ENC):
+        for j in range(4):
+            block(sd, f"unet.encoder.layers.{i}.conv.{j}", ci if j == 0 else co, co)
+    for i, (ci, co) in enumerate(RMVPE_INTER):
+        for j in range(4):
+            block(sd, f"unet.intermediate.layers.{i}.conv.{j}", ci if j == 0 else co, co)
+    for i, (ci, co) in enumerate(RMVPE_DEC):
+        p = f"unet.decoder.layers.{i}"
+        sd[p + ".conv1.0.weight"] = G.n(ci, co, 3, 3, std=math.sqrt(2.0 / (ci * 9 / 4)))
+        bn(sd, p + ".conv1.1", co)
+        for j in range(4):
+            block(sd, f"{p}.conv2.{j}", 2 * co if j == 0 else co, co)
+    sd["cnn.weight"] = conv(3, 16, 3, 3)
+    sd["cnn.bias"] = (0.1 * G.rs.standard_normal(3)).astype(np.float32)
+    Hh = 256
+    a = 1.0 / math.sqrt(Hh)
+    for suf in ("", "_reverse"):
+        sd[f"fc.0.gru.weight_ih_l0{suf}"] = G.rs.uniform(-a, a, (3 * Hh, 384)).astype(np.float32)
+        sd[f"fc.0.gru.weight_hh_l0{suf}"] = G.rs.uniform(-a, a, (3 * Hh, Hh)).astype(np.float32)
+        sd[f"fc.0.gru.bias_ih_l0{suf}"] = G.rs.uniform(-a, a, 3 * Hh).astype(np.float32)
+        sd[f"fc.0.gru.bias_hh_l0{suf}"] = G.rs.uniform(-a, a, 3 * Hh).astype(np.float32)
+    sd["fc.1.weight"] = G.n(360, 512, std=1.0 / math.sqrt(512))
+    sd["fc.1.bias"] = (-2.0 + 0.1 * G.rs.standard_normal(360)).astype(np.float32)
+    return sd
+
+
+def make_rmvpe_input(T: int = 160000, seed: int = 0) -> np.ndarray:
+    """16 kHz mono ``[T] f32``: a harmonic tone on a random-walk f0 (80-300 Hz)
+    plus white noise, 10 s by default."""
+    rs = np.random.RandomState(70_000 + seed)
+    f0 = np.clip(150.0 + np.cumsum(rs.standard_normal(T)) * 0.05, 80.0, 300.0)
+    ph = 2 * np.pi * np.cumsum(f0) / 16000.0
+    x = 0.3 * np.sin(ph) + 0.1 * np.sin(2 * ph) + 0.05 * np.sin(3 * ph) + 0.02 * rs.standard_normal(T)
+    return x.astype(np.float32)

@@ -7,7 +7,8 @@ Run in a container where the reference checkout is present::
 It imports ``runtime`` from the reference (read-only, ``RVC_BACKEND=numpy``),
 replaces the checkpoint loaders with the seeded synthetic checkpoints of
 ``rvc_cuda.synthetic`` (the loaders read files; no checkpoints exist here),
-runs ``SynthesizerTrn.infer_controlled`` / ``HubertEncoder.encode``, the
+runs ``SynthesizerTrn.infer_controlled`` / ``HubertEncoder.encode`` /
+``RMVPE.infer_from_audio``, the
 retrieval search (``runtime.retrieval.search_l2``) and the per-op numpy
 kernels, and writes ``tests/golden/*.npz``.  Weights and inputs
 are not stored: they are regenerated from the recorded seeds (legacy
@@ -57,6 +58,11 @@ VITS_CASES = [
 HUBERT_CASES = [
     ("hubert_t8000", 8000, 0, 1),
     ("hubert_t3201", 3201, 0, 2),           # odd length: ragged conv strides
+]
+# (name, T samples, weight seed, input seed)
+RMVPE_CASES = [
+    ("rmvpe_t16000", 16000, 0, 1),          # 101 frames -> U-Net on 128
+    ("rmvpe_t6401", 6401, 0, 2),            # 41 frames: padded to 64, odd length
 ]
 # (name, F queries, N index rows, D, k, index seed, query seed)
 RETRIEVAL_CASES = [
@@ -120,6 +126,22 @@ def run_hubert(runtime_hubert, name, T, wseed, iseed, meta):
                         out=np.asarray(out[0], np.float32),
                         out_v1=np.asarray(out1[0], np.float32))
     meta[name] = {"kind": "hubert", "T": T, "weight_seed": wseed, "input_seed": iseed,
+                  "weights_sha256": weights_digest(sd), "inputs_sha256": digest([x])}
+
+
+def run_rmvpe(runtime_rmvpe, name, T, wseed, iseed, meta):
+    """``RMVPE.infer_from_audio`` pieces: log-mel, salience (``mel2hidden``), f0."""
+    sd = syn.make_rmvpe_weights(wseed)
+    x = syn.make_rmvpe_input(T, iseed)
+    with tempfile.TemporaryDirectory() as d:
+        runtime_rmvpe.load_pth = lambda path: sd
+        m = runtime_rmvpe.RMVPE(os.path.join(d, "rmvpe.pt"))
+    mel = m._extract_mel(x)
+    hidden = m.mel2hidden(mel)
+    f0 = m.infer_from_audio(x)
+    np.savez_compressed(os.path.join(HERE, name + ".npz"), mel=mel[0], salience=hidden[0],
+                        argmax=np.argmax(hidden[0], axis=1).astype(np.int64), f0=f0)
+    meta[name] = {"kind": "rmvpe", "T": T, "weight_seed": wseed, "input_seed": iseed,
                   "weights_sha256": weights_digest(sd), "inputs_sha256": digest([x])}
 
 
@@ -189,7 +211,7 @@ def run_ops(nn, meta):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("RVC_REFERENCE", "/root/reference"))
-    ap.add_argument("--only", choices=["vits", "hubert", "ops", "retrieval"], default=None,
+    ap.add_argument("--only", choices=["vits", "hubert", "ops", "retrieval", "rmvpe"], default=None,
                     help="regenerate one family and keep the other fixtures")
     args = ap.parse_args()
     os.environ["RVC_BACKEND"] = "numpy"
@@ -213,6 +235,10 @@ def main():
             run_hubert(runtime_hubert, *c, meta)
     if args.only in (None, "ops"):
         run_ops(nn, meta)
+    if args.only in (None, "rmvpe"):
+        from runtime.models import rmvpe as runtime_rmvpe  # noqa: PLC0415
+        for c in RMVPE_CASES:
+            run_rmvpe(runtime_rmvpe, *c, meta)
     if args.only in (None, "retrieval"):
         from runtime import retrieval  # noqa: PLC0415
         for c in RETRIEVAL_CASES:

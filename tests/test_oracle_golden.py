@@ -92,3 +92,20 @@ def test_retrieval_oracle_matches_reference(name, golden_meta):
     np.testing.assert_allclose(sc, g["scores"], rtol=1e-6, atol=1e-4)
     n = g["blend"].shape[0]
     np.testing.assert_allclose(OR.blend(q[:n], db, k=m["k"]), g["blend"], rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("name", ["rmvpe_t16000", "rmvpe_t6401"])
+def test_rmvpe_oracle_matches_reference(name, golden_meta):
+    from oracle import rmvpe as ORM
+    m = golden_meta[name]
+    sd = syn.make_rmvpe_weights(m["weight_seed"])
+    assert weights_digest(sd) == m["weights_sha256"]
+    x = syn.make_rmvpe_input(m["T"], m["input_seed"])
+    assert digest([x]) == m["inputs_sha256"]
+    g = load_golden(name)
+    mel = ORM.log_mel(x)
+    np.testing.assert_allclose(mel, g["mel"], rtol=1e-5, atol=1e-5)
+    sal = ORM.salience(sd, g["mel"])
+    assert rel_l2(sal, g["salience"]) < 1e-5
+    np.testing.assert_array_equal(np.argmax(sal, axis=1), g["argmax"])
+    np.testing.assert_allclose(ORM.decode(sal), g["f0"], rtol=1e-5, atol=1e-4)
