@@ -195,6 +195,33 @@ int32_t rvc_cuda_hubert_encode_device(int64_t model, int32_t B, int64_t T, const
 int32_t rvc_cuda_hubert_tap(int64_t model, const char* name, float* out, int64_t n);
 int32_t rvc_cuda_hubert_keep_taps(int64_t model, int32_t enable);
 
+/* ---------------------------------------------------------------- RMVPE
+ * Device-resident RMVPE F0 estimator; replaces RMVPE.infer_from_audio
+ * (runtime/models/rmvpe.py:927-952) with its pieces _extract_mel (:632),
+ * mel2hidden (:861), _unet (:727), _conv_block_res (:518), conv_transpose2d
+ * (:319), _bgru (:393), decode / to_local_average_cents (:899-925).
+ * fp32 throughout (float64 STFT) so the salience argmax follows the reference. */
+int32_t rvc_cuda_rmvpe_create(int64_t ctx, int64_t* model);
+int32_t rvc_cuda_rmvpe_destroy(int64_t model);
+/* Checkpoint tensors under the reference's keys (RMVPE.W). */
+int32_t rvc_cuda_rmvpe_set_weight(int64_t model, const char* key, const float* data, const int64_t* shape,
+                                  int32_t ndim);
+int32_t rvc_cuda_rmvpe_finalize(int64_t model);
+/* F = 1 + T / 160 frames for T samples. */
+int32_t rvc_cuda_rmvpe_frames(int64_t T, int64_t* F);
+/* B equal-length clips x [B,T] (host, 16 kHz, T > 512) -> f0 [B,F] Hz and,
+ * when argmax is not NULL, the per-frame salience argmax [B,F].  Synchronous. */
+int32_t rvc_cuda_rmvpe_infer(int64_t model, int32_t B, int64_t T, const float* x, float thred, float* f0,
+                             int32_t* argmax);
+/* Same with device pointers, asynchronous on the context's stream. */
+int32_t rvc_cuda_rmvpe_infer_device(int64_t model, int32_t B, int64_t T, const float* x, float thred, float* f0,
+                                    int32_t* argmax);
+/* Debug taps after an infer with taps enabled: "mel" [B,Fp,128], "enc0".."enc4",
+ * "inter", "dec0".."dec4" (channels-last buffers), "cnn" [B,Fp,384],
+ * "gru" [B,Fp,512], "salience" [B,Fp,360]; Fp = F rounded up to 32. */
+int32_t rvc_cuda_rmvpe_tap(int64_t model, const char* name, float* out, int64_t n);
+int32_t rvc_cuda_rmvpe_keep_taps(int64_t model, int32_t enable);
+
 /* ---------------------------------------------------------------- retrieval
  * Device-resident feature index for brute-force L2 search; replaces
  * runtime.retrieval.search_l2 (runtime/retrieval.py:35-82), weighted_blend

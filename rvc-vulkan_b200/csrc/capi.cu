@@ -4,6 +4,7 @@
 #include "../../include/rvc_cuda.h"
 #include "hubert.cuh"
 #include "retrieval.cuh"
+#include "rmvpe.cuh"
 #include "synth.cuh"
 
 #include <cstring>
@@ -19,6 +20,7 @@ std::unordered_map<int64_t, std::unique_ptr<Context>> g_ctx;
 std::unordered_map<int64_t, std::unique_ptr<SynthModel>> g_synth;
 std::unordered_map<int64_t, std::unique_ptr<HubertModel>> g_hubert;
 std::unordered_map<int64_t, std::unique_ptr<IndexModel>> g_index;
+std::unordered_map<int64_t, std::unique_ptr<RmvpeModel>> g_rmvpe;
 int64_t g_next = 1;
 
 Context* get_ctx(int64_t h) {
@@ -39,6 +41,13 @@ HubertModel* get_hubert(int64_t h) {
   std::lock_guard<std::mutex> lk(g_reg_mu);
   auto it = g_hubert.find(h);
   if (it == g_hubert.end()) throw Error{kErrState, "invalid HuBERT handle " + std::to_string(h)};
+  return it->second.get();
+}
+
+RmvpeModel* get_rmvpe(int64_t h) {
+  std::lock_guard<std::mutex> lk(g_reg_mu);
+  auto it = g_rmvpe.find(h);
+  if (it == g_rmvpe.end()) throw Error{kErrState, "invalid RMVPE handle " + std::to_string(h)};
   return it->second.get();
 }
 
@@ -114,6 +123,16 @@ template <typename F>
 int32_t on_index(int64_t index, F&& f) {
   return guarded([&] {
     IndexModel* m = get_index(index);
+    std::lock_guard<std::mutex> lk(m->ctx->mu);
+    DeviceGuard dg(m->ctx->device);
+    f(m);
+  });
+}
+
+template <typename F>
+int32_t on_rmvpe(int64_t model, F&& f) {
+  return guarded([&] {
+    RmvpeModel* m = get_rmvpe(model);
     std::lock_guard<std::mutex> lk(m->ctx->mu);
     DeviceGuard dg(m->ctx->device);
     f(m);
@@ -718,6 +737,79 @@ int32_t rvc_cuda_index_blend_device(int64_t index, const float* q, int64_t F, in
     RVC_CHECK_ARG(D == m->D, "index_blend: query width does not match the index");
     m->blend_device(q, F, k, mode, (float)index_rate, (float)(1.0 - index_rate), feats, out);
   });
+}
+
+// ----------------------------------------------------------------- RMVPE
+int32_t rvc_cuda_rmvpe_create(int64_t ctx, int64_t* model) {
+  return on_ctx(ctx, [&](Context* c) {
+    auto m = std::make_unique<RmvpeModel>(c);
+    std::lock_guard<std::mutex> lk(g_reg_mu);
+    *model = g_next++;
+    g_rmvpe[*model] = std::move(m);
+  });
+}
+
+int32_t rvc_cuda_rmvpe_destroy(int64_t model) {
+  return guarded([&] {
+    std::unique_ptr<RmvpeModel> m;
+    {
+      std::lock_guard<std::mutex> lk(g_reg_mu);
+      auto it = g_rmvpe.find(model);
+      if (it == g_rmvpe.end()) throw Error{kErrState, "invalid RMVPE handle " + std::to_string(model)};
+      m = std::move(it->second);
+      g_rmvpe.erase(it);
+    }
+    std::lock_guard<std::mutex> lk(m->ctx->mu);
+    DeviceGuard dg(m->ctx->device);
+    m.reset();
+  });
+}
+
+int32_t rvc_cuda_rmvpe_set_weight(int64_t model, const char* key, const float* data, const int64_t* shape,
+                                  int32_t ndim) {
+  return on_rmvpe(model, [&](RmvpeModel* m) {
+    RVC_CHECK_ARG(key && data && ndim >= 0 && ndim <= 8, "rmvpe_set_weight: bad arguments");
+    std::vector<int64_t> s(shape, shape + ndim);
+    m->set_weight(key, data, s);
+  });
+}
+
+int32_t rvc_cuda_rmvpe_finalize(int64_t model) {
+  return on_rmvpe(model, [&](RmvpeModel* m) {
+    m->finalize();
+    finish(m->ctx);
+  });
+}
+
+int32_t rvc_cuda_rmvpe_frames(int64_t T, int64_t* F) {
+  return guarded([&] {
+    RVC_CHECK_ARG(T >= 0 && F, "rmvpe_frames: bad arguments");
+    *F = RmvpeModel::frames(T);
+  });
+}
+
+int32_t rvc_cuda_rmvpe_infer(int64_t model, int32_t B, int64_t T, const float* x, float thred, float* f0,
+                             int32_t* argmax) {
+  return on_rmvpe(model, [&](RmvpeModel* m) {
+    RVC_CHECK_ARG(B >= 1 && x && f0, "rmvpe_infer: bad arguments");
+    m->infer_host(B, T, x, thred, f0, argmax);
+    finish(m->ctx);
+  });
+}
+
+int32_t rvc_cuda_rmvpe_infer_device(int64_t model, int32_t B, int64_t T, const float* x, float thred, float* f0,
+                                    int32_t* argmax) {
+  return on_rmvpe(model, [&](RmvpeModel* m) { m->infer_device(B, T, x, thred, f0, argmax); });
+}
+
+int32_t rvc_cuda_rmvpe_tap(int64_t model, const char* name, float* out, int64_t n) {
+  return on_rmvpe(model, [&](RmvpeModel* m) {
+    if (!m->tap(name, out, n)) throw Error{kErrArg, std::string("rmvpe_tap: no tap '") + name + "' of that size"};
+  });
+}
+
+int32_t rvc_cuda_rmvpe_keep_taps(int64_t model, int32_t enable) {
+  return on_rmvpe(model, [&](RmvpeModel* m) { m->keep_taps = enable != 0; });
 }
 
 }  // extern "C"

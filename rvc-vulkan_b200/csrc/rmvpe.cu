@@ -1,0 +1,869 @@
+// Device-resident RMVPE F0 estimator.
+//
+// Reference semantics: RMVPE.infer_from_audio (runtime/models/rmvpe.py:927-952):
+// log-mel front end (:632-641, runtime/dsp/fft.py:59-113, runtime/dsp/mel.py:97-122),
+// deep U-Net (:643-760) of ConvBlockRes (:518-547), 2x2 average pooling
+// (:387-390), 3x3 stride-2 transposed convs (:319-384), cnn + BiGRU + linear +
+// sigmoid (:878-897, :393-442) and the local-average decode (:899-925).
+//
+// Layout: channels-last images [B][H = frames][W = mel bins][C], fp32.  The
+// argmax over 360 salience bins must reproduce the reference's, so the whole
+// network runs in fp32 on the CUDA cores (no reduced-precision tensor-core
+// split): every conv is an fp32 implicit GEMM (64 pixels x 64 channels per
+// block, split over K when a layer has few pixels), BatchNorm + ReLU +
+// residual in its epilogue, in the reference's operation order.  The STFT is
+// a float64 DFT (the reference transforms in float64).  The BiGRU runs as one
+// 8-CTA thread-block cluster per direction: each CTA keeps 96 rows of the
+// recurrent matrix in shared memory and broadcasts its 32 new hidden units to
+// the other CTAs' shared memory every step.
+#include "rmvpe.cuh"
+
+#include <cooperative_groups.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+
+namespace cg = cooperative_groups;
+
+namespace rvc {
+
+namespace {
+
+__device__ __forceinline__ float sigmoid_two_sided(float x) {
+  // runtime/nn.py:520-523
+  if (x >= 0.f) return __fdiv_rn(1.f, __fadd_rn(1.f, expf(-x)));
+  const float e = expf(x);
+  return __fdiv_rn(e, __fadd_rn(1.f, e));
+}
+
+// numpy float32 sum of a short contiguous row (pairwise_sum, n < 128).
+__device__ __forceinline__ float np_sum_small(const float* a, int n) {
+  if (n < 8) {
+    float s = 0.f;
+    for (int i = 0; i < n; ++i) s = __fadd_rn(s, a[i]);
+    return s;
+  }
+  float r[8];
+  for (int j = 0; j < 8; ++j) r[j] = a[j];
+  int i = 8;
+  for (; i < n - (n % 8); i += 8)
+    for (int j = 0; j < 8; ++j) r[j] = __fadd_rn(r[j], a[i + j]);
+  float s = __fadd_rn(__fadd_rn(__fadd_rn(r[0], r[1]), __fadd_rn(r[2], r[3])),
+                      __fadd_rn(__fadd_rn(r[4], r[5]), __fadd_rn(r[6], r[7])));
+  for (; i < n; ++i) s = __fadd_rn(s, a[i]);
+  return s;
+}
+
+// ------------------------------------------------------------------ front end
+// |rfft(frame * hann)| in float64, cast to float32: mag[b][t][k], k < 513.
+// Frames come from the reflect-padded signal (pad 512 each side).
+__global__ void __launch_bounds__(256) stft_mag_kernel(const float* __restrict__ x, long long T, int F,
+                                                        const double* __restrict__ window,
+                                                        const double* __restrict__ tw, float* __restrict__ mag) {
+  __shared__ double xs[1024];
+  __shared__ double cs[1024], sn[1024];
+  const int t = blockIdx.x, b = blockIdx.y;
+  const float* xb = x + (long long)b * T;
+  for (int n = threadIdx.x; n < 1024; n += blockDim.x) {
+    long long p = (long long)t * 160 + n - 512;
+    if (p < 0) p = -p;
+    if (p >= T) p = 2 * (T - 1) - p;
+    xs[n] = (double)xb[p] * window[n];
+    cs[n] = tw[n];
+    sn[n] = tw[1024 + n];
+  }
+  __syncthreads();
+  for (int k = threadIdx.x; k < 513; k += blockDim.x) {
+    double re = 0.0, im = 0.0;
+    int idx = 0;
+    for (int n = 0; n < 1024; ++n) {
+      re = fma(xs[n], cs[idx], re);
+      im = fma(xs[n], sn[idx], im);
+      idx = (idx + k) & 1023;
+    }
+    mag[((long long)b * F + t) * 513 + k] = (float)sqrt(re * re + im * im);
+  }
+}
+
+// log(clip(basis @ mag, 1e-5)) per (frame, mel bin); frames >= F are the
+// zero padding to a multiple of 32 (mel2hidden, :861-867).  Writes the raw
+// log-mel [B][Fp][128] and the encoder's input BatchNorm of it.
+__global__ void mel_log_kernel(const float* __restrict__ mag, const float* __restrict__ basis, int F, int Fp,
+                               const float* __restrict__ s_in, const float* __restrict__ t_in,
+                               float* __restrict__ mel, float* __restrict__ x0) {
+  const int t = blockIdx.x, b = blockIdx.y, m = threadIdx.x;
+  float v = 0.f;
+  if (t < F) {
+    const float* mr = mag + ((long long)b * F + t) * 513;
+    const float* br = basis + (long long)m * 513;
+    float s = 0.f;
+    for (int k = 0; k < 513; ++k) s = fmaf(br[k], mr[k], s);
+    v = logf(fmaxf(s, 1e-5f));
+  }
+  const long long o = ((long long)b * Fp + t) * 128 + m;
+  mel[o] = v;
+  x0[o] = __fadd_rn(__fmul_rn(v, s_in[0]), t_in[0]);
+}
+
+// ------------------------------------------------------------------ conv
+struct C2Args {
+  const float* x;
+  long long x_bs;
+  int H, W, ldi;
+  int C_in, C_out, taps, transposed;
+  const float* w;  // [taps][C_in][C_out]
+  int OH, OW;
+  float* y;
+  long long y_bs, oh_s;
+  int ow_s, oc_s;
+  const float *bias, *scale, *shift;
+  int relu, sigm;
+  const float* res;
+  long long res_bs;
+  int ldr;
+  int splits, kit;
+  float* part;
+  int B;
+};
+
+__device__ __forceinline__ void c2_store(const C2Args& a, int b, int m, int co, float v) {
+  if (a.bias) v = __fadd_rn(v, a.bias[co]);
+  if (a.scale) v = __fadd_rn(__fmul_rn(v, a.scale[co]), a.shift[co]);
+  if (a.relu) v = v > 0.f ? v : 0.f;
+  if (a.sigm) v = sigmoid_two_sided(v);
+  if (a.res) v = __fadd_rn(v, a.res[(long long)b * a.res_bs + (long long)m * a.ldr + co]);
+  const int oh = m / a.OW, ow = m - oh * a.OW;
+  a.y[(long long)b * a.y_bs + (long long)oh * a.oh_s + (long long)ow * a.ow_s + (long long)co * a.oc_s] = v;
+}
+
+constexpr int kBM = 64, kBN = 64, kBK = 16;
+
+__global__ void __launch_bounds__(256) conv2d_kernel(const C2Args a) {
+  __shared__ __align__(16) float As[2][kBK][kBM + 4];
+  __shared__ __align__(16) float Bs[2][kBK][kBN];
+  const int tid = threadIdx.x;
+  const int M = a.OH * a.OW;
+  const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * kBN;
+  const int b = blockIdx.z / a.splits, sp = blockIdx.z - (blockIdx.z / a.splits) * a.splits;
+  const int nci = (a.C_in + kBK - 1) / kBK;
+  const int it0 = (int)((long long)a.kit * sp / a.splits), it1 = (int)((long long)a.kit * (sp + 1) / a.splits);
+  const float* xb = a.x + (long long)b * a.x_bs;
+  // A-load slots: pixel px = (tid >> 4) + 16 q, channel c = tid & 15
+  const int ac = tid & 15;
+  int aoh[4], aow[4];
+  bool am[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int m = m0 + (tid >> 4) + 16 * q;
+    am[q] = m < M;
+    aoh[q] = am[q] ? m / a.OW : 0;
+    aow[q] = am[q] ? m - aoh[q] * a.OW : 0;
+  }
+  // B-load slots: c = (tid >> 6) + 4 q, column n = tid & 63
+  const int bn = tid & 63, bco = n0 + bn;
+  float ra[4], rb[4];
+  auto load = [&](int it) {
+    const int tap = it / nci, cb = it - (it / nci) * nci;
+    const int ci = cb * kBK + ac;
+    int dy, dx;
+    if (a.taps == 9) {
+      dy = tap / 3;
+      dx = tap - dy * 3;
+    } else {
+      dy = dx = 1;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float v = 0.f;
+      int ih, iw;
+      bool ok = am[q] && ci < a.C_in;
+      if (a.transposed) {  // out (oh, ow) takes in ((oh + 1 - ky) / 2, (ow + 1 - kx) / 2) when even
+        const int h2 = aoh[q] + 1 - dy, w2 = aow[q] + 1 - dx;
+        // the reference computes rows/cols < 2H-1 / 2W-1 and zero-fills the
+        // output-padding row and column (runtime/models/rmvpe.py:378-384)
+        ok = ok && h2 >= 0 && w2 >= 0 && !(h2 & 1) && !(w2 & 1) && aoh[q] < 2 * a.H - 1 && aow[q] < 2 * a.W - 1;
+        ih = h2 >> 1;
+        iw = w2 >> 1;
+      } else {
+        ih = aoh[q] + dy - 1;
+        iw = aow[q] + dx - 1;
+      }
+      ok = ok && ih >= 0 && ih < a.H && iw >= 0 && iw < a.W;
+      if (ok) v = __ldg(xb + ((long long)ih * a.W + iw) * a.ldi + ci);
+      ra[q] = v;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int c = cb * kBK + (tid >> 6) + 4 * q;
+      rb[q] = (c < a.C_in && bco < a.C_out) ? __ldg(a.w + ((long long)tap * a.C_in + c) * a.C_out + bco) : 0.f;
+    }
+  };
+  auto store = [&](int buf) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) As[buf][ac][(tid >> 4) + 16 * q] = ra[q];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) Bs[buf][(tid >> 6) + 4 * q][bn] = rb[q];
+  };
+  const int tx = tid & 15, ty = tid >> 4;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  if (it0 < it1) {
+    load(it0);
+    store(0);
+    __syncthreads();
+    for (int it = it0; it < it1; ++it) {
+      const int cur = (it - it0) & 1;
+      const bool more = it + 1 < it1;
+      if (more) load(it + 1);
+#pragma unroll
+      for (int c = 0; c < kBK; ++c) {
+        const float4 av = *reinterpret_cast<const float4*>(&As[cur][c][ty * 4]);
+        const float4 bv = *reinterpret_cast<const float4*>(&Bs[cur][c][tx * 4]);
+        const float aa[4] = {av.x, av.y, av.z, av.w}, bb[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(aa[i], bb[j], acc[i][j]);
+      }
+      if (more) store(cur ^ 1);
+      __syncthreads();
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int m = m0 + ty * 4 + i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int co = n0 + tx * 4 + j;
+      if (co >= a.C_out) continue;
+      if (a.splits > 1)
+        a.part[(((long long)sp * a.B + b) * M + m) * a.C_out + co] = acc[i][j];
+      else
+        c2_store(a, b, m, co, acc[i][j]);
+    }
+  }
+}
+
+// Split-K: partial sums added in split order, then the epilogue.
+__global__ void conv2d_reduce_kernel(const C2Args a) {
+  const long long M = (long long)a.OH * a.OW, per = M * a.C_out, n = per * a.B;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
+    const int b = (int)(e / per);
+    const long long r = e - (long long)b * per;
+    const int m = (int)(r / a.C_out), co = (int)(r - (long long)m * a.C_out);
+    float v = a.part[e];
+    for (int s = 1; s < a.splits; ++s) v = __fadd_rn(v, a.part[(long long)s * n + e]);
+    c2_store(a, b, m, co, v);
+  }
+}
+
+// 2x2 average pooling: ((x00 + x01) + x10) + x11, times 1/4 (numpy's reduce order
+// over the two pooled axes, then the mean's division by 4).
+__global__ void avgpool_kernel(const float* __restrict__ x, long long x_bs, int H, int W, int C, int ldi,
+                               float* __restrict__ y, long long y_bs, int B) {
+  const int OH = H / 2, OW = W / 2;
+  const long long per = (long long)OH * OW * C, n = per * B;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
+    const int b = (int)(e / per);
+    long long r = e - (long long)b * per;
+    const int c = (int)(r % C);
+    r /= C;
+    const int ow = (int)(r % OW), oh = (int)(r / OW);
+    const float* p = x + (long long)b * x_bs + ((long long)(2 * oh) * W + 2 * ow) * ldi + c;
+    const float s = __fadd_rn(__fadd_rn(__fadd_rn(p[0], p[ldi]), p[(long long)W * ldi]), p[(long long)W * ldi + ldi]);
+    y[(long long)b * y_bs + ((long long)oh * OW + ow) * C + c] = __fmul_rn(s, 0.25f);
+  }
+}
+
+// ------------------------------------------------------------------ BiGRU
+// One 8-CTA cluster per direction (blockIdx.x / 8).  CTA `rank` owns hidden
+// units [32 rank, 32 rank + 32): rows g*256 + unit of the recurrent matrix for
+// the gates g = r, z, n.  Per step: gh = W_hh h + b_hh for its 96 rows, the
+// gate update of its 32 units for every sequence, and a store of the new units
+// into every CTA's next h buffer (distributed shared memory), then one cluster
+// barrier.  gx = x W_ih^T + b_ih is precomputed for both directions.
+constexpr int kGruCta = 8, kGruUnits = 32, kGruRows = 96, kGruThreads = 384, kGruMaxB = 8, kGruLd = 257;
+
+__global__ void __cluster_dims__(kGruCta, 1, 1) __launch_bounds__(kGruThreads)
+    gru_kernel(const float* __restrict__ gx, const float* __restrict__ whh, const float* __restrict__ bhh, int B,
+               int T, float* __restrict__ out) {
+  extern __shared__ float sm[];
+  float* Ws = sm;                                  // [96][257]
+  float* hb = Ws + kGruRows * kGruLd;              // [2][kGruMaxB][256]
+  float* gh = hb + 2 * kGruMaxB * 256;             // [kGruMaxB][96]
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int dir = blockIdx.x / kGruCta;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float* W = whh + (long long)dir * 768 * 256;
+  for (int e = tid; e < kGruRows * 256; e += kGruThreads) {
+    const int rr = e / 256, k = e - rr * 256;
+    const int row = (rr / kGruUnits) * 256 + rank * kGruUnits + (rr % kGruUnits);
+    Ws[rr * kGruLd + k] = W[(long long)row * 256 + k];
+  }
+  for (int e = tid; e < 2 * kGruMaxB * 256; e += kGruThreads) hb[e] = 0.f;
+  float bias_row[kGruRows / 12];
+  // warp w handles rows w*8 .. w*8+7 (12 warps x 8 rows = 96)
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const int rr = warp * 8 + q;
+    bias_row[q] = bhh[dir * 768 + (rr / kGruUnits) * 256 + rank * kGruUnits + (rr % kGruUnits)];
+  }
+  cluster.sync();
+  const int gu = tid % kGruUnits, gb = tid / kGruUnits;  // gate threads: unit, sequence
+  const bool gate = gb < B;
+  const int j = rank * kGruUnits + gu;
+  for (int s = 0; s < T; ++s) {
+    const int tt = dir == 0 ? s : T - 1 - s;
+    const int cur = s & 1, nxt = cur ^ 1;
+    float gxr = 0.f, gxz = 0.f, gxn = 0.f;
+    if (gate) {
+      const float* g = gx + ((long long)gb * T + tt) * 1536 + dir * 768;
+      gxr = g[j];
+      gxz = g[256 + j];
+      gxn = g[512 + j];
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int rr = warp * 8 + q;
+      const float* wr = Ws + rr * kGruLd;
+      for (int bb = 0; bb < B; ++bb) {
+        const float* h = hb + (cur * kGruMaxB + bb) * 256;
+        float acc = 0.f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc = fmaf(wr[lane + 32 * k], h[lane + 32 * k], acc);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (lane == 0) gh[bb * kGruRows + rr] = __fadd_rn(acc, bias_row[q]);
+      }
+    }
+    __syncthreads();
+    if (gate) {
+      const float* g = gh + gb * kGruRows;
+      const float r = sigmoid_two_sided(__fadd_rn(gxr, g[gu]));
+      const float z = sigmoid_two_sided(__fadd_rn(gxz, g[kGruUnits + gu]));
+      const float n = tanhf(__fadd_rn(gxn, __fmul_rn(r, g[2 * kGruUnits + gu])));
+      const float hp = hb[(cur * kGruMaxB + gb) * 256 + j];
+      const float hn = __fadd_rn(__fmul_rn(__fsub_rn(1.f, z), n), __fmul_rn(z, hp));
+      out[((long long)gb * T + tt) * 512 + dir * 256 + j] = hn;
+      float* dst = hb + (nxt * kGruMaxB + gb) * 256 + j;
+      for (int r2 = 0; r2 < kGruCta; ++r2) *cluster.map_shared_rank(dst, r2) = hn;
+    }
+    cluster.sync();
+  }
+}
+
+constexpr size_t kGruSmem = sizeof(float) * (kGruRows * kGruLd + 2 * kGruMaxB * 256 + kGruMaxB * kGruRows);
+
+// ------------------------------------------------------------------ decode
+__global__ void decode_kernel(const float* __restrict__ sal, int Fp, int F, float thred, float* __restrict__ f0,
+                              int* __restrict__ amax, int B) {
+  const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= (long long)B * F) return;
+  const int b = (int)(row / F), t = (int)(row - (long long)b * F);
+  const float* s = sal + ((long long)b * Fp + t) * 360;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int c = lane; c < 360; c += 32) {
+    const float v = s[c];
+    if (v > best || (v == best && c < bi)) {
+      best = v;
+      bi = c;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  if (lane != 0) return;
+  float ts[9], pr[9];
+  for (int q = 0; q < 9; ++q) {
+    const int c = bi + q - 4;  // window in unpadded bins; the 4-bin zero pads read 0
+    const int p = bi + q;      // padded cents index
+    const float v = (c >= 0 && c < 360) ? s[c] : 0.f;
+    const float cents = (p >= 4 && p < 364) ? (float)(20.0 * (p - 4) + 1997.3794084376191) : 0.f;
+    ts[q] = v;
+    pr[q] = __fmul_rn(v, cents);
+  }
+  float cents = __fdiv_rn(np_sum_small(pr, 9), np_sum_small(ts, 9));
+  const float maxx = best > 0.f ? best : 0.f;  // the max of the zero-padded row
+  if (maxx <= thred) cents = 0.f;
+  float f = __fmul_rn(10.f, powf(2.f, __fdiv_rn(cents, 1200.f)));
+  if (f == 10.f) f = 0.f;
+  f0[(long long)b * F + t] = f;
+  if (amax) amax[(long long)b * F + t] = bi;
+}
+
+template <typename K>
+void set_smem_once(K kernel, size_t bytes) {
+  static std::atomic<uint64_t> done{0};
+  int dev = 0;
+  RVC_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 64 && !(done.load() & (1ull << dev))) {
+    RVC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+    done.fetch_or(1ull << dev);
+  }
+}
+
+int grid_for(long long n, int block) {
+  return (int)std::max<long long>(1, std::min<long long>((n + block - 1) / block, 148ll * 16));
+}
+
+}  // namespace
+
+// ================================================================== model
+RmvpeModel::RmvpeModel(Context* c) : ctx(c) {}
+
+void RmvpeModel::set_weight(const std::string& key, const float* host, const std::vector<int64_t>& shape) {
+  RmvpeTensor t;
+  t.shape = shape;
+  t.buf = DevBuf(ctx, sizeof(float) * (size_t)std::max<int64_t>(1, t.numel()));
+  RVC_CUDA_TRY(cudaMemcpyAsync(t.buf.p, host, sizeof(float) * t.numel(), cudaMemcpyHostToDevice, ctx->stream));
+  RVC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  raw_[key] = std::move(t);
+  finalized_ = false;
+}
+
+const RmvpeTensor& RmvpeModel::W(const std::string& key) const {
+  auto it = raw_.find(key);
+  if (it == raw_.end()) throw Error{kErrState, "rmvpe: missing weight '" + key + "'"};
+  return it->second;
+}
+
+namespace {
+// scale = gamma / sqrt(var + 1e-5), shift = beta - mean * scale (float32, :507-515)
+__global__ void bn_fold_kernel(const float* g, const float* bt, const float* rm, const float* rv, int C, float* s,
+                               float* t) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  const float sc = __fdiv_rn(g[c], __fsqrt_rn(__fadd_rn(rv[c], 1e-5f)));
+  s[c] = sc;
+  t[c] = __fsub_rn(bt[c], __fmul_rn(rm[c], sc));
+}
+// w [O][I][kh][kw] (conv) or [I][O][kh][kw] (transposed) -> [kh*kw][I][O]
+__global__ void conv_w_kernel(const float* w, int O, int I, int taps, int transposed, float* out) {
+  const long long n = (long long)taps * I * O;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
+    const int o = (int)(e % O);
+    const long long r = e / O;
+    const int i = (int)(r % I), tap = (int)(r / I);
+    out[e] = transposed ? w[((long long)i * O + o) * taps + tap] : w[((long long)o * I + i) * taps + tap];
+  }
+}
+}  // namespace
+
+void RmvpeModel::bn_fold(const std::string& p, DevBuf& scale, DevBuf& shift, int C) {
+  for (const char* s : {".weight", ".bias", ".running_mean", ".running_var"})
+    RVC_CHECK_ARG(W(p + s).numel() == C, "rmvpe: BatchNorm '" + p + "' does not have " + std::to_string(C) + " channels");
+  scale = DevBuf(ctx, sizeof(float) * C);
+  shift = DevBuf(ctx, sizeof(float) * C);
+  bn_fold_kernel<<<(C + 127) / 128, 128, 0, ctx->stream>>>(W(p + ".weight").buf.f(), W(p + ".bias").buf.f(),
+                                                            W(p + ".running_mean").buf.f(),
+                                                            W(p + ".running_var").buf.f(), C, scale.f(), shift.f());
+  note_launch();
+  RVC_CUDA_TRY(cudaGetLastError());
+}
+
+static Conv2dW make_conv(Context* ctx, const RmvpeTensor& w, bool transposed, const std::string& key) {
+  RVC_CHECK_ARG(w.shape.size() == 4 && w.shape[2] == w.shape[3] && (w.shape[2] == 3 || w.shape[2] == 1),
+                "rmvpe: conv weight '" + key + "' must be [*, *, 3, 3] or [*, *, 1, 1]");
+  Conv2dW L;
+  L.transposed = transposed;
+  L.taps = (int)(w.shape[2] * w.shape[3]);
+  L.C_out = (int)(transposed ? w.shape[1] : w.shape[0]);
+  L.C_in = (int)(transposed ? w.shape[0] : w.shape[1]);
+  L.w = DevBuf(ctx, sizeof(float) * (size_t)L.taps * L.C_in * L.C_out);
+  conv_w_kernel<<<grid_for(w.numel(), 256), 256, 0, ctx->stream>>>(w.buf.f(), L.C_out, L.C_in, L.taps, transposed,
+                                                                   L.w.f());
+  note_launch();
+  RVC_CUDA_TRY(cudaGetLastError());
+  return L;
+}
+
+void RmvpeModel::build_block(const std::string& p, int cin, int cout) {
+  Conv2dW c0 = make_conv(ctx, W(p + ".conv.0.weight"), false, p + ".conv.0.weight");
+  RVC_CHECK_ARG(c0.C_in == cin && c0.C_out == cout && c0.taps == 9, "rmvpe: unexpected shape of " + p + ".conv.0");
+  bn_fold(p + ".conv.1", c0.scale, c0.shift, cout);
+  Conv2dW c3 = make_conv(ctx, W(p + ".conv.3.weight"), false, p + ".conv.3.weight");
+  RVC_CHECK_ARG(c3.C_in == cout && c3.C_out == cout && c3.taps == 9, "rmvpe: unexpected shape of " + p + ".conv.3");
+  bn_fold(p + ".conv.4", c3.scale, c3.shift, cout);
+  convs_[p + ".conv.0"] = std::move(c0);
+  convs_[p + ".conv.3"] = std::move(c3);
+  if (cin != cout) {
+    Conv2dW sc = make_conv(ctx, W(p + ".shortcut.weight"), false, p + ".shortcut.weight");
+    RVC_CHECK_ARG(sc.taps == 1 && sc.C_in == cin && sc.C_out == cout, "rmvpe: unexpected shortcut shape in " + p);
+    if (raw_.count(p + ".shortcut.bias")) {
+      sc.bias = DevBuf(ctx, sizeof(float) * cout);
+      RVC_CUDA_TRY(cudaMemcpyAsync(sc.bias.p, W(p + ".shortcut.bias").buf.p, sizeof(float) * cout,
+                                   cudaMemcpyDeviceToDevice, ctx->stream));
+    }
+    convs_[p + ".shortcut"] = std::move(sc);
+  } else {
+    RVC_CHECK_ARG(!raw_.count(p + ".shortcut.weight"), "rmvpe: shortcut in an equal-width block " + p);
+  }
+}
+
+static const int kEnc[5][2] = {{1, 16}, {16, 32}, {32, 64}, {64, 128}, {128, 256}};
+static const int kInter[4][2] = {{256, 512}, {512, 512}, {512, 512}, {512, 512}};
+static const int kDec[5][2] = {{512, 256}, {256, 128}, {128, 64}, {64, 32}, {32, 16}};
+
+void RmvpeModel::finalize() {
+  cudaStream_t st = ctx->stream;
+  convs_.clear();
+  bn_fold("unet.encoder.bn", in_scale_, in_shift_, 1);
+  for (int i = 0; i < 5; ++i)
+    for (int j = 0; j < 4; ++j)
+      build_block("unet.encoder.layers." + std::to_string(i) + ".conv." + std::to_string(j), j == 0 ? kEnc[i][0] : kEnc[i][1],
+                  kEnc[i][1]);
+  for (int i = 0; i < 4; ++i)
+    for (int j = 0; j < 4; ++j)
+      build_block("unet.intermediate.layers." + std::to_string(i) + ".conv." + std::to_string(j),
+                  j == 0 ? kInter[i][0] : kInter[i][1], kInter[i][1]);
+  for (int i = 0; i < 5; ++i) {
+    const std::string p = "unet.decoder.layers." + std::to_string(i);
+    Conv2dW ct = make_conv(ctx, W(p + ".conv1.0.weight"), true, p + ".conv1.0.weight");
+    RVC_CHECK_ARG(ct.taps == 9 && ct.C_in == kDec[i][0] && ct.C_out == kDec[i][1], "rmvpe: unexpected " + p + ".conv1.0");
+    bn_fold(p + ".conv1.1", ct.scale, ct.shift, kDec[i][1]);
+    convs_[p + ".conv1"] = std::move(ct);
+    for (int j = 0; j < 4; ++j)
+      build_block(p + ".conv2." + std::to_string(j), j == 0 ? 2 * kDec[i][1] : kDec[i][1], kDec[i][1]);
+  }
+  {
+    Conv2dW cnn = make_conv(ctx, W("cnn.weight"), false, "cnn.weight");
+    RVC_CHECK_ARG(cnn.C_in == 16 && cnn.C_out == 3 && cnn.taps == 9, "rmvpe: cnn.weight must be [3,16,3,3]");
+    cnn.bias = DevBuf(ctx, sizeof(float) * 3);
+    RVC_CUDA_TRY(cudaMemcpyAsync(cnn.bias.p, W("cnn.bias").buf.p, sizeof(float) * 3, cudaMemcpyDeviceToDevice, st));
+    convs_["cnn"] = std::move(cnn);
+  }
+  {
+    // GRU input projection of both directions as one [384 -> 1536] 1x1 conv
+    Conv2dW gi;
+    gi.C_in = 384;
+    gi.C_out = 1536;
+    gi.taps = 1;
+    std::vector<float> w((size_t)384 * 1536), bsum(1536);
+    std::vector<float> wf((size_t)768 * 384), bf(768);
+    for (int d = 0; d < 2; ++d) {
+      const std::string sfx = d ? "_reverse" : "";
+      const auto& wi = W("fc.0.gru.weight_ih_l0" + sfx);
+      RVC_CHECK_ARG(wi.numel() == 768 * 384, "rmvpe: fc.0.gru.weight_ih_l0" + sfx + " must be [768, 384]");
+      RVC_CUDA_TRY(cudaMemcpy(wf.data(), wi.buf.p, sizeof(float) * wf.size(), cudaMemcpyDeviceToHost));
+      RVC_CUDA_TRY(cudaMemcpy(bf.data(), W("fc.0.gru.bias_ih_l0" + sfx).buf.p, sizeof(float) * 768,
+                              cudaMemcpyDeviceToHost));
+      for (int o = 0; o < 768; ++o) {
+        for (int i = 0; i < 384; ++i) w[(size_t)i * 1536 + d * 768 + o] = wf[(size_t)o * 384 + i];
+        bsum[d * 768 + o] = bf[o];
+      }
+    }
+    gi.w = DevBuf(ctx, sizeof(float) * w.size());
+    gi.bias = DevBuf(ctx, sizeof(float) * 1536);
+    RVC_CUDA_TRY(cudaMemcpy(gi.w.p, w.data(), sizeof(float) * w.size(), cudaMemcpyHostToDevice));
+    RVC_CUDA_TRY(cudaMemcpy(gi.bias.p, bsum.data(), sizeof(float) * 1536, cudaMemcpyHostToDevice));
+    convs_["gru_in"] = std::move(gi);
+    w_hh_ = DevBuf(ctx, sizeof(float) * 2 * 768 * 256);
+    b_hh_ = DevBuf(ctx, sizeof(float) * 2 * 768);
+    for (int d = 0; d < 2; ++d) {
+      const std::string sfx = d ? "_reverse" : "";
+      RVC_CHECK_ARG(W("fc.0.gru.weight_hh_l0" + sfx).numel() == 768 * 256, "rmvpe: GRU hidden size must be 256");
+      RVC_CUDA_TRY(cudaMemcpyAsync(w_hh_.f() + (size_t)d * 768 * 256, W("fc.0.gru.weight_hh_l0" + sfx).buf.p,
+                                   sizeof(float) * 768 * 256, cudaMemcpyDeviceToDevice, st));
+      RVC_CUDA_TRY(cudaMemcpyAsync(b_hh_.f() + (size_t)d * 768, W("fc.0.gru.bias_hh_l0" + sfx).buf.p,
+                                   sizeof(float) * 768, cudaMemcpyDeviceToDevice, st));
+    }
+  }
+  {
+    // fc.1: Linear(512 -> 360) as a 1x1 conv ([O][I] == [O][I][1][1])
+    const auto& wf = W("fc.1.weight");
+    RVC_CHECK_ARG(wf.numel() == 360 * 512, "rmvpe: fc.1.weight must be [360, 512]");
+    RmvpeTensor t4;
+    t4.shape = {360, 512, 1, 1};
+    t4.buf = DevBuf(ctx, sizeof(float) * 360 * 512);
+    RVC_CUDA_TRY(cudaMemcpyAsync(t4.buf.p, wf.buf.p, t4.buf.bytes, cudaMemcpyDeviceToDevice, st));
+    Conv2dW fc = make_conv(ctx, t4, false, "fc.1.weight");
+    fc.bias = DevBuf(ctx, sizeof(float) * 360);
+    RVC_CUDA_TRY(cudaMemcpyAsync(fc.bias.p, W("fc.1.bias").buf.p, sizeof(float) * 360, cudaMemcpyDeviceToDevice, st));
+    RVC_CUDA_TRY(cudaStreamSynchronize(st));  // t4 is freed on return
+    convs_["fc"] = std::move(fc);
+  }
+  // front-end tables: HTK mel filters (rows normalised to sum 1), numpy's
+  // symmetric Hann window, DFT twiddles (runtime/dsp/mel.py:97-122,
+  // runtime/dsp/fft.py:16-56)
+  {
+    const int nb = kBins;
+    std::vector<double> fftf(nb);
+    for (int k = 0; k < nb; ++k) fftf[k] = (nb == 1) ? 0.0 : 8000.0 * k / (nb - 1);
+    const double mlo = 1127.0 * std::log1p(30.0 / 700.0), mhi = 1127.0 * std::log1p(8000.0 / 700.0);
+    std::vector<double> fpts(kMels + 2);
+    const double step = (mhi - mlo) / (kMels + 1);  // numpy.linspace: i * step + start, exact end point
+    for (int i = 0; i < kMels + 2; ++i) {
+      const double m = i == kMels + 1 ? mhi : i * step + mlo;
+      fpts[i] = 700.0 * std::expm1(m / 1127.0);
+    }
+    std::vector<float> basis((size_t)kMels * nb);
+    for (int i = 0; i < kMels; ++i) {
+      const double lo = fpts[i], c = fpts[i + 1], hi = fpts[i + 2];
+      std::vector<double> tri(nb);
+      double s = 0.0;
+      for (int k = 0; k < nb; ++k) {
+        const double up = c - lo > 0 ? (fftf[k] - lo) / (c - lo) : 0.0;
+        const double dn = hi - c > 0 ? (hi - fftf[k]) / (hi - c) : 0.0;
+        tri[k] = std::max(0.0, std::min(up, dn));
+        s += tri[k];
+      }
+      for (int k = 0; k < nb; ++k) basis[(size_t)i * nb + k] = (float)(s > 0 ? tri[k] / s : tri[k]);
+    }
+    std::vector<double> win(kNFFT), tw(2 * kNFFT);
+    const double pi = 3.14159265358979323846;
+    for (int k = 0; k < kNFFT; ++k) {
+      const double n = 1.0 - kNFFT + 2.0 * k;  // numpy.hanning: 0.5 + 0.5 cos(pi n / (M - 1))
+      win[k] = 0.5 + 0.5 * std::cos(pi * n / (kNFFT - 1));
+      tw[k] = std::cos(2.0 * pi * k / kNFFT);
+      tw[kNFFT + k] = -std::sin(2.0 * pi * k / kNFFT);
+    }
+    mel_basis_ = DevBuf(ctx, sizeof(float) * basis.size());
+    window_ = DevBuf(ctx, sizeof(double) * win.size());
+    twiddle_ = DevBuf(ctx, sizeof(double) * tw.size());
+    RVC_CUDA_TRY(cudaMemcpy(mel_basis_.p, basis.data(), mel_basis_.bytes, cudaMemcpyHostToDevice));
+    RVC_CUDA_TRY(cudaMemcpy(window_.p, win.data(), window_.bytes, cudaMemcpyHostToDevice));
+    RVC_CUDA_TRY(cudaMemcpy(twiddle_.p, tw.data(), twiddle_.bytes, cudaMemcpyHostToDevice));
+  }
+  RVC_CUDA_TRY(cudaStreamSynchronize(st));
+  finalized_ = true;
+}
+
+void RmvpeModel::ensure_ws(int B, int64_t T) {
+  if (B <= ws_B && T <= ws_T) return;
+  B = std::max(B, ws_B);
+  T = std::max(T, ws_T);
+  ws_.clear();
+  const int64_t F = frames(T), Fp = 32 * ((F - 1) / 32 + 1);
+  const int64_t big = Fp * 128 * 16;  // widest activation: level 0, 16 channels
+  auto add = [&](const std::string& n, long long per_chunk) {
+    ws_.emplace(n, DevBuf(ctx, sizeof(float) * (size_t)B * std::max<long long>(1, per_chunk)));
+  };
+  add("x", T);
+  add("mag", F * kBins);
+  add("mel", Fp * 128);
+  add("x0", Fp * 128);
+  add("A", big);
+  add("Bb", big);
+  add("Tt", big);
+  add("P", big / 2);
+  for (int l = 0; l < 5; ++l) add("cat" + std::to_string(l), (Fp >> l) * (128 >> l) * 2 * kEnc[l][1]);
+  add("feat", Fp * 384);
+  add("gx", Fp * 1536);
+  add("hg", Fp * 512);
+  add("sal", Fp * 360);
+  add("f0", F);
+  ws_.emplace("amax", DevBuf(ctx, sizeof(int32_t) * (size_t)B * F));
+  ws_.emplace("part", DevBuf(ctx, sizeof(float) * (size_t)(4 * 148 + 64) * kBM * kBN));
+  ws_B = B;
+  ws_T = T;
+}
+
+void RmvpeModel::save_tap(const std::string& name, const float* d, int64_t n) {
+  if (!keep_taps) return;
+  std::vector<float> h((size_t)n);
+  RVC_CUDA_TRY(cudaMemcpyAsync(h.data(), d, sizeof(float) * n, cudaMemcpyDeviceToHost, ctx->stream));
+  RVC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  taps_[name] = std::move(h);
+}
+
+bool RmvpeModel::tap(const std::string& name, float* host, int64_t n) {
+  auto it = taps_.find(name);
+  if (it == taps_.end() || (int64_t)it->second.size() < n) return false;
+  std::copy(it->second.begin(), it->second.begin() + n, host);
+  return true;
+}
+
+void RmvpeModel::conv(const Conv2dW& L, int B, const float* x, long long x_bs, int H, int Wd, int ldi, float* y,
+                      long long y_bs, long long oh_s, int ow_s, int oc_s, bool relu, const float* res,
+                      long long res_bs, int ldr, bool sigmoid) {
+  C2Args a{};
+  a.x = x; a.x_bs = x_bs; a.H = H; a.W = Wd; a.ldi = ldi;
+  a.C_in = L.C_in; a.C_out = L.C_out; a.taps = L.taps; a.transposed = L.transposed ? 1 : 0;
+  a.w = L.w.f();
+  a.OH = L.transposed ? 2 * H : H;
+  a.OW = L.transposed ? 2 * Wd : Wd;
+  a.y = y; a.y_bs = y_bs; a.oh_s = oh_s; a.ow_s = ow_s; a.oc_s = oc_s;
+  a.bias = L.bias.p ? L.bias.f() : nullptr;
+  a.scale = L.scale.p ? L.scale.f() : nullptr;
+  a.shift = L.shift.p ? L.shift.f() : nullptr;
+  a.relu = relu ? 1 : 0;
+  a.sigm = sigmoid ? 1 : 0;
+  a.res = res; a.res_bs = res_bs; a.ldr = ldr;
+  a.B = B;
+  a.kit = L.taps * ((L.C_in + kBK - 1) / kBK);
+  const long long M = (long long)a.OH * a.OW;
+  const int mt = (int)((M + kBM - 1) / kBM), nt = (L.C_out + kBN - 1) / kBN;
+  const long long tiles = (long long)mt * nt * B;
+  int splits = 1;
+  // few output tiles and a long K loop: split K so ~2 waves of blocks run
+  while (tiles * splits < 2 * 148 && a.kit / (splits * 2) >= 8 && splits < 16) splits *= 2;
+  if (splits > 1) {
+    const size_t need = (size_t)splits * B * M * L.C_out;
+    if (need * sizeof(float) > ws_.at("part").bytes) splits = 1;
+  }
+  a.splits = splits;
+  a.part = ws_.at("part").f();
+  dim3 g(mt, nt, B * splits);
+  conv2d_kernel<<<g, 256, 0, ctx->stream>>>(a);
+  note_launch();
+  RVC_CUDA_TRY(cudaGetLastError());
+  if (splits > 1) {
+    conv2d_reduce_kernel<<<grid_for(B * M * L.C_out, 256), 256, 0, ctx->stream>>>(a);
+    note_launch();
+    RVC_CUDA_TRY(cudaGetLastError());
+  }
+}
+
+void RmvpeModel::block(const std::string& p, int B, const float* x, long long x_bs, int H, int Wd, int ldi,
+                       float* out, long long out_bs, int ldo, float* tmp, long long tmp_bs) {
+  const Conv2dW& c0 = convs_.at(p + ".conv.0");
+  const Conv2dW& c3 = convs_.at(p + ".conv.3");
+  const int co = c0.C_out;
+  const long long ohs_o = (long long)Wd * ldo, ohs_t = (long long)Wd * co;
+  auto sc = convs_.find(p + ".shortcut");
+  if (sc != convs_.end())  // shortcut = conv1x1(x) + b, written first, then added to the main branch
+    conv(sc->second, B, x, x_bs, H, Wd, ldi, out, out_bs, ohs_o, ldo, 1, false, nullptr, 0, 0);
+  conv(c0, B, x, x_bs, H, Wd, ldi, tmp, tmp_bs, ohs_t, co, 1, true, nullptr, 0, 0);
+  if (sc != convs_.end())
+    conv(c3, B, tmp, tmp_bs, H, Wd, co, out, out_bs, ohs_o, ldo, 1, true, out, out_bs, ldo);
+  else
+    conv(c3, B, tmp, tmp_bs, H, Wd, co, out, out_bs, ohs_o, ldo, 1, true, x, x_bs, ldi);
+}
+
+void RmvpeModel::infer_device(int B, int64_t T, const float* x, float thred, float* f0, int32_t* argmax) {
+  if (!finalized_) throw Error{kErrState, "rmvpe: finalize() not called after the last weight upload"};
+  RVC_CHECK_ARG(B >= 1, "rmvpe: B must be positive");
+  RVC_CHECK_ARG(T > kNFFT / 2, "rmvpe: audio must be longer than 512 samples (reflect padding)");
+  RVC_CHECK_ARG(T <= (1ll << 31), "rmvpe: audio too long");
+  ensure_ws(B, T);
+  taps_.clear();
+  cudaStream_t st = ctx->stream;
+  const int F = (int)frames(T), Fp = 32 * ((F - 1) / 32 + 1);
+  const long long bs_big = (long long)(ws_.at("A").bytes / sizeof(float) / ws_B);
+  // ---------------- front end
+  stft_mag_kernel<<<dim3(F, B), 256, 0, st>>>(x, T, F, (const double*)window_.p, (const double*)twiddle_.p,
+                                              buf("mag"));
+  note_launch();
+  mel_log_kernel<<<dim3(Fp, B), 128, 0, st>>>(buf("mag"), mel_basis_.f(), F, Fp, in_scale_.f(), in_shift_.f(),
+                                              buf("mel"), buf("x0"));
+  note_launch();
+  RVC_CUDA_TRY(cudaGetLastError());
+  save_tap("mel", buf("mel"), (long long)B * Fp * 128);
+  // ---------------- encoder
+  float *A = buf("A"), *Bb = buf("Bb"), *Tt = buf("Tt"), *P = buf("P");
+  const float* lin = buf("x0");
+  long long lin_bs = (long long)Fp * 128;
+  int ldin = 1;
+  for (int l = 0; l < 5; ++l) {
+    const int H = Fp >> l, Wd = 128 >> l, co = kEnc[l][1];
+    float* cat = buf(("cat" + std::to_string(l)).c_str());
+    const long long cat_bs = (long long)(ws_.at("cat" + std::to_string(l)).bytes / sizeof(float) / ws_B);
+    const std::string p = "unet.encoder.layers." + std::to_string(l) + ".conv.";
+    block(p + "0", B, lin, lin_bs, H, Wd, ldin, A, bs_big, co, Tt, bs_big);
+    block(p + "1", B, A, bs_big, H, Wd, co, Bb, bs_big, co, Tt, bs_big);
+    block(p + "2", B, Bb, bs_big, H, Wd, co, A, bs_big, co, Tt, bs_big);
+    block(p + "3", B, A, bs_big, H, Wd, co, cat + co, cat_bs, 2 * co, Tt, bs_big);  // skip half of the concat
+    save_tap("enc" + std::to_string(l), cat, (long long)B * cat_bs);  // skip = channels [co, 2co)
+    const long long pn = (long long)(H / 2) * (Wd / 2) * co;
+    avgpool_kernel<<<grid_for(pn * B, 256), 256, 0, st>>>(cat + co, cat_bs, H, Wd, co, 2 * co, P, bs_big / 2, B);
+    note_launch();
+    RVC_CUDA_TRY(cudaGetLastError());
+    lin = P;
+    lin_bs = bs_big / 2;
+    ldin = co;
+  }
+  // ---------------- intermediate: [Fp/32][4]
+  {
+    const int H = Fp >> 5, Wd = 4;
+    float* bufs[2] = {A, Bb};
+    const float* cur = P;
+    long long cur_bs = bs_big / 2;
+    int ldc = 256, k = 0;
+    for (int i = 0; i < 4; ++i)
+      for (int j = 0; j < 4; ++j, ++k) {
+        float* o = bufs[k & 1];
+        block("unet.intermediate.layers." + std::to_string(i) + ".conv." + std::to_string(j), B, cur, cur_bs, H, Wd,
+              ldc, o, bs_big, 512, Tt, bs_big);
+        cur = o;
+        cur_bs = bs_big;
+        ldc = 512;
+      }
+    lin = cur;  // == bufs[1] after 16 blocks
+    lin_bs = bs_big;
+    ldin = 512;
+    save_tap("inter", lin, (long long)B * bs_big);
+  }
+  // ---------------- decoder
+  for (int i = 0; i < 5; ++i) {
+    const int l = 4 - i, H = Fp >> l, Wd = 128 >> l, co = kDec[i][1];
+    float* cat = buf(("cat" + std::to_string(l)).c_str());
+    const long long cat_bs = (long long)(ws_.at("cat" + std::to_string(l)).bytes / sizeof(float) / ws_B);
+    const std::string p = "unet.decoder.layers." + std::to_string(i);
+    // convT + BN + ReLU into the first half of the concat buffer
+    conv(convs_.at(p + ".conv1"), B, lin, lin_bs, H / 2, Wd / 2, ldin, cat, cat_bs, (long long)Wd * 2 * co, 2 * co, 1,
+         true, nullptr, 0, 0);
+    float* outb = (lin == A) ? Bb : A;
+    float* other = (outb == A) ? Bb : A;
+    block(p + ".conv2.0", B, cat, cat_bs, H, Wd, 2 * co, outb, bs_big, co, Tt, bs_big);
+    block(p + ".conv2.1", B, outb, bs_big, H, Wd, co, other, bs_big, co, Tt, bs_big);
+    block(p + ".conv2.2", B, other, bs_big, H, Wd, co, outb, bs_big, co, Tt, bs_big);
+    block(p + ".conv2.3", B, outb, bs_big, H, Wd, co, other, bs_big, co, Tt, bs_big);
+    lin = other;
+    lin_bs = bs_big;
+    ldin = co;
+    save_tap("dec" + std::to_string(i), lin, (long long)B * bs_big);
+  }
+  // ---------------- cnn (16 -> 3, bias) written as [Fp][3 * 128] (channel-major within a frame)
+  conv(convs_.at("cnn"), B, lin, lin_bs, Fp, 128, 16, buf("feat"), (long long)Fp * 384, 384, 1, 128, false, nullptr,
+       0, 0);
+  save_tap("cnn", buf("feat"), (long long)B * Fp * 384);
+  // ---------------- BiGRU: gx for both directions, then the recurrence
+  conv(convs_.at("gru_in"), B, buf("feat"), (long long)Fp * 384, Fp, 1, 384, buf("gx"), (long long)Fp * 1536, 1536,
+       1536, 1, false, nullptr, 0, 0);
+  set_smem_once(gru_kernel, kGruSmem);
+  for (int b0 = 0; b0 < B; b0 += kGruMaxB) {
+    const int nb = std::min(kGruMaxB, B - b0);
+    gru_kernel<<<2 * kGruCta, kGruThreads, kGruSmem, st>>>(buf("gx") + (size_t)b0 * Fp * 1536, w_hh_.f(), b_hh_.f(),
+                                                            nb, Fp, buf("hg") + (size_t)b0 * Fp * 512);
+    note_launch();
+    RVC_CUDA_TRY(cudaGetLastError());
+  }
+  save_tap("gru", buf("hg"), (long long)B * Fp * 512);
+  // ---------------- fc: Linear(512 -> 360) + sigmoid
+  conv(convs_.at("fc"), B, buf("hg"), (long long)Fp * 512, Fp, 1, 512, buf("sal"), (long long)Fp * 360, 360, 360, 1,
+       false, nullptr, 0, 0, true);
+  save_tap("salience", buf("sal"), (long long)B * Fp * 360);
+  // ---------------- decode
+  decode_kernel<<<(unsigned)(((long long)B * F + 7) / 8), 256, 0, st>>>(buf("sal"), Fp, F, thred, f0, argmax, B);
+  note_launch();
+  RVC_CUDA_TRY(cudaGetLastError());
+}
+
+void RmvpeModel::infer_host(int B, int64_t T, const float* x, float thred, float* f0, int32_t* argmax) {
+  RVC_CHECK_ARG(T > kNFFT / 2, "rmvpe: audio must be longer than 512 samples (reflect padding)");
+  ensure_ws(B, T);
+  cudaStream_t st = ctx->stream;
+  const int64_t F = frames(T);
+  RVC_CUDA_TRY(cudaMemcpyAsync(buf("x"), x, sizeof(float) * (size_t)B * T, cudaMemcpyHostToDevice, st));
+  infer_device(B, T, buf("x"), thred, buf("f0"), ws_.at("amax").as<int32_t>());
+  RVC_CUDA_TRY(cudaMemcpyAsync(f0, buf("f0"), sizeof(float) * (size_t)B * F, cudaMemcpyDeviceToHost, st));
+  if (argmax)
+    RVC_CUDA_TRY(cudaMemcpyAsync(argmax, ws_.at("amax").p, sizeof(int32_t) * (size_t)B * F, cudaMemcpyDeviceToHost,
+                                 st));
+}
+
+}  // namespace rvc

@@ -8,7 +8,8 @@ Drop-in for jiangchengnay/rvc-vulkan's numpy runtime:
 * ``patch_reference()`` installs the whole-model fast paths
   (``rvc_cuda.synth.patch_reference`` for ``SynthesizerTrn``,
   ``rvc_cuda.hubert.patch_reference`` for ``HubertEncoder``,
-  ``rvc_cuda.retrieval.patch_reference`` for the brute-force ``search_l2``).
+  ``rvc_cuda.retrieval.patch_reference`` for the brute-force ``search_l2``,
+  ``rvc_cuda.rmvpe.patch_reference`` for ``RMVPE.infer_from_audio``).
 
 Importing this package does not touch the GPU; the shared library is loaded
 on first use of ``rvc_cuda.ops`` / ``rvc_cuda.synth`` and raises if missing.
@@ -43,8 +44,9 @@ def register(name: str = "cuda") -> None:
 
 def patch_reference(device=None, precision: str = "bf16x3") -> None:
     """Install the model-level CUDA paths on the reference's model classes."""
-    from . import hubert, retrieval, synth  # noqa: PLC0415
+    from . import hubert, retrieval, rmvpe, synth  # noqa: PLC0415
 
     synth.patch_reference(device=device, precision=precision)
     hubert.patch_reference(device=device, precision=precision)
     retrieval.patch_reference()
+    rmvpe.patch_reference(device=device)

@@ -111,3 +111,19 @@ def test_retrieval_patch_reference_replaces_module_functions():
     assert ret_mod.search_l2 is retrieval.search_l2 and pipe_mod.search_l2 is retrieval.search_l2
     assert ret_mod.weighted_blend is retrieval.weighted_blend
     assert ret_mod._rvc_cuda_orig_search_l2() == "numpy"
+
+
+def test_rmvpe_frames_and_patch_reference():
+    from rvc_cuda import rmvpe
+
+    assert rmvpe.frames(160000) == 1001 and rmvpe.frames(16000) == 101
+
+    class FakeRmvpe:
+        def infer_from_audio(self, x, thred=0.03):
+            return "numpy"
+
+    class FakeModule:
+        RMVPE = FakeRmvpe
+
+    cls = rmvpe.patch_reference(FakeModule)
+    assert cls is FakeRmvpe and FakeRmvpe.infer_from_audio is not FakeRmvpe._rvc_cuda_orig_infer_from_audio
