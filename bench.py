@@ -444,6 +444,187 @@ def run_retrieval_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def rmvpe_cpu_sample(T, steps=1):
+    """Time the RMVPE oracle (numpy restatement of RMVPE.infer_from_audio) on one clip."""
+    from oracle import rmvpe as ORM
+    from rvc_cuda import synthetic as syn
+    sd = syn.make_rmvpe_weights(0)
+    x = syn.make_rmvpe_input(T, 1)
+    ts = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        ORM.infer(sd, x)
+        ts.append(time.perf_counter() - t0)
+    return T / 16000.0, ts
+
+
+def run_rmvpe(args, world, rank, local):
+    """RMVPE over clips of --samples 16 kHz samples."""
+    import torch
+
+    from rvc_cuda import _lib, synthetic as syn
+    from rvc_cuda.rmvpe import CudaRmvpe, frames
+
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    T, G = args.samples, args.group
+    m = CudaRmvpe(syn.make_rmvpe_weights(0), device=local)
+    ctx = m.ctx
+    F = frames(T)
+    assert args.chunks % world == 0, "chunks must split evenly across ranks"
+    n_local = args.chunks // world
+    n_unique = min(args.unique, n_local)
+    xs = [syn.make_rmvpe_input(T, 100 + i) for i in range(n_unique)]
+    h_x = torch.empty((n_local, T), dtype=torch.float32, pin_memory=True).numpy()
+    h_f = torch.empty((n_local, F), dtype=torch.float32, pin_memory=True).numpy()
+    for j in range(n_local):
+        h_x[j] = xs[(rank * n_local + j) % n_unique]
+    d_x, d_f = ctx.alloc(h_x.nbytes), ctx.alloc(h_f.nbytes)
+    ctx.h2d(d_x, h_x)
+    groups = [(s, min(G, n_local - s)) for s in range(0, n_local, G)]
+
+    def step_device():
+        for s, g in groups:
+            _lib.check(_lib.lib.rvc_cuda_rmvpe_infer_device(m.handle, g, T, _lib._p(d_x + s * T * 4), 0.03,
+                                                            _lib._p(d_f + s * F * 4), None))
+
+    def step_e2e():
+        for s, g in groups:
+            h_f[s:s + g] = m.infer_batch(h_x[s:s + g])
+
+    stream = torch.cuda.ExternalStream(ctx.stream(), device=local)
+
+    def timed(fn, steps):
+        barrier()
+        ctx.sync()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        ctx.sync()
+        torch.cuda.synchronize()
+        barrier()
+        return e0.elapsed_time(e1) / 1e3
+
+    for _ in range(args.warmup):
+        step_device()
+    ctx.sync()
+    n0 = _lib.launch_count()
+    if args.profile_out:
+        ctx.profile(True)
+    with ClockSampler(local) as clk:
+        t = timed(step_device, args.steps)
+    if args.profile_out and rank == 0:
+        with open(args.profile_out, "w") as f:
+            f.write(ctx.profile_dump())
+    ctx.profile(False)
+    launches = _lib.launch_count() - n0
+    t = max_over_ranks(t)
+    audio_per_step = args.chunks * T / 16000.0
+    value = audio_per_step * args.steps / t
+    step_e2e()
+    te = max_over_ranks(timed(step_e2e, args.steps))
+    if rank == 0:
+        pb, ps, hbm, src = peaks()
+        # fp32 SIMT network: roofline against the fp32 CUDA-core peak (148 SMs x 128 FMA/clk x 2 x max clock)
+        fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+        gflop_chunk = rmvpe_gflop(T)
+        achieved = gflop_chunk * args.chunks * args.steps / t / 1e3
+        line = {
+            "metric": "seconds of input audio pitch-tracked per wall-second (RMVPE)", "value": value,
+            "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * t / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32 (float64 STFT)",
+            "data": f"synthetic: seeded random-init weights, {n_unique} distinct seeded clips tiled",
+            "config": {"workload": f"config2 RMVPE, {args.chunks} clips x {T} samples -> {F} frames, sharded by clip",
+                       "chunks": args.chunks, "samples": T, "group": G, "l2": "inputs larger than L2",
+                       "parallelism": f"clip-sharded x{world}, no collective"},
+            "roofline": {"bound": "fp32 SIMT", "kernel": "whole step (U-Net convs dominate)", "achieved": achieved,
+                         "peak": fp32_peak, "unit": "TFLOP/s", "frac": achieved / fp32_peak, "traffic": None,
+                         "peak_source": "nominal fp32 FMA peak at max clock (no measured fp32 figure)",
+                         "note": f"{gflop_chunk:.1f} GFLOP of convs/GEMMs per clip over the step time"},
+            "e2e": {"value": audio_per_step * args.steps / te, "unit": UNIT,
+                    "h2d_bytes_per_step": h_x.nbytes * world, "d2h_bytes_per_step": h_f.nbytes * world},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+            "finite": bool(np.isfinite(h_f).all()),
+        }
+        if world == 1 and not args.no_cpu:
+            audio_s, ts = rmvpe_cpu_sample(T, steps=1)
+            line["cpu_baseline"] = {"value": audio_s / ts[0], "unit": UNIT, "cores": blas_threads(), "kind": "port",
+                                    "sample": f"1 clip of {T} samples ({audio_s:.1f} s audio), CPU oracle"}
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def rmvpe_gflop(T):
+    """Algorithmic GFLOP of one RMVPE clip: every conv / convT (useful taps) / GEMM."""
+    from rvc_cuda import synthetic as syn
+    F = 1 + T // 160
+    Fp = 32 * ((F - 1) // 32 + 1)
+    fl = 0.0
+    for l, (ci, co) in enumerate(syn.RMVPE_ENC):
+        px = (Fp >> l) * (128 >> l)
+        for j in range(4):
+            cin = ci if j == 0 else co
+            fl += 2 * px * 9 * (cin * co + co * co) + (2 * px * cin * co if cin != co else 0)
+    px = (Fp >> 5) * 4
+    for i, (ci, co) in enumerate(syn.RMVPE_INTER):
+        for j in range(4):
+            cin = ci if j == 0 else co
+            fl += 2 * px * 9 * (cin * co + co * co) + (2 * px * cin * co if cin != co else 0)
+    for i, (ci, co) in enumerate(syn.RMVPE_DEC):
+        l = 4 - i
+        px = (Fp >> l) * (128 >> l)
+        fl += 2 * px * ci * co * 2.25
+        for j in range(4):
+            cin = 2 * co if j == 0 else co
+            fl += 2 * px * 9 * (cin * co + co * co) + (2 * px * cin * co if cin != co else 0)
+    fl += 2 * Fp * 128 * 9 * 16 * 3 + 2 * Fp * 384 * 1536 + 2 * 2 * Fp * 768 * 256 + 2 * Fp * 512 * 360
+    return fl / 1e9
+
+
+def run_rmvpe_reference(args, world, rank):
+    if rank != 0:
+        return
+    T = args.samples
+    rmvpe_cpu_sample(T, steps=1)
+    audio_s, ts = rmvpe_cpu_sample(T, steps=args.steps)
+    t = sum(ts)
+    value = audio_s * len(ts) / t
+    line = {
+        "impl": "reference", "metric": "seconds of input audio pitch-tracked per wall-second (RMVPE)",
+        "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * t / len(ts), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic (seeded)",
+        "config": {"workload": "config2 RMVPE, CPU sample", "samples": T},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": blas_threads(), "kind": "port",
+                         "sample": f"1 clip of {T} samples per step, CPU oracle"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_hubert_reference(args, world, rank):
     if rank != 0:
         return
@@ -628,15 +809,20 @@ def main():
     ap.add_argument("--ref-frames", type=int, default=100)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile-out", default="", help="write the per-layer conv profile (CSV) here")
-    ap.add_argument("--workload", default="synth", choices=["synth", "hubert", "retrieval"],
+    ap.add_argument("--workload", default="synth", choices=["synth", "hubert", "retrieval", "rmvpe"],
                     help="synth: config 3 (headline); hubert: config 1 (HuBERT-base encoder); "
-                         "retrieval: config 4's top-8 search + blend")
-    ap.add_argument("--samples", type=int, default=160000, help="hubert: samples per chunk")
+                         "retrieval: config 4's top-8 search + blend; rmvpe: config 2")
+    ap.add_argument("--samples", type=int, default=160000, help="hubert / rmvpe: samples per chunk")
     ap.add_argument("--audio-s", type=float, default=60.0, help="retrieval: seconds of frames (50 per s)")
     ap.add_argument("--index-rows", type=int, default=200000, help="retrieval: index rows")
     args = ap.parse_args()
     world, rank, local = dist_setup()
-    if args.workload == "retrieval":
+    if args.workload == "rmvpe":
+        if args.impl == "reference":
+            run_rmvpe_reference(args, world, rank)
+        else:
+            run_rmvpe(args, world, rank, local)
+    elif args.workload == "retrieval":
         if args.impl == "reference":
             run_retrieval_reference(args, world, rank)
         else:

@@ -21,8 +21,8 @@
 #include <cooperative_groups.h>
 
 #include <algorithm>
-#include <atomic>
 #include <cmath>
+#include <cstdio>
 
 namespace cg = cooperative_groups;
 
@@ -137,32 +137,36 @@ __device__ __forceinline__ void c2_store(const C2Args& a, int b, int m, int co, 
   a.y[(long long)b * a.y_bs + (long long)oh * a.oh_s + (long long)ow * a.ow_s + (long long)co * a.oc_s] = v;
 }
 
-constexpr int kBM = 64, kBN = 64, kBK = 16;
+constexpr int kBK = 16, kTileElems = 4096;  // BM x BN output tile, 4 x 4 per thread, 256 threads
 
+// BM x BN in {64 x 64, 128 x 32, 256 x 16}: narrow layers (16 / 32 output
+// channels) take taller pixel tiles instead of idle columns.
+template <int BM, int BN>
 __global__ void __launch_bounds__(256) conv2d_kernel(const C2Args a) {
-  __shared__ __align__(16) float As[2][kBK][kBM + 4];
-  __shared__ __align__(16) float Bs[2][kBK][kBN];
+  constexpr int QA = BM / 16, QB = BN / 16, BS = 256 / BN;
+  __shared__ __align__(16) float As[2][kBK][BM + 4];
+  __shared__ __align__(16) float Bs[2][kBK][BN];
   const int tid = threadIdx.x;
   const int M = a.OH * a.OW;
-  const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * kBN;
+  const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
   const int b = blockIdx.z / a.splits, sp = blockIdx.z - (blockIdx.z / a.splits) * a.splits;
   const int nci = (a.C_in + kBK - 1) / kBK;
   const int it0 = (int)((long long)a.kit * sp / a.splits), it1 = (int)((long long)a.kit * (sp + 1) / a.splits);
   const float* xb = a.x + (long long)b * a.x_bs;
   // A-load slots: pixel px = (tid >> 4) + 16 q, channel c = tid & 15
   const int ac = tid & 15;
-  int aoh[4], aow[4];
-  bool am[4];
+  int aoh[QA], aow[QA];
+  bool am[QA];
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
+  for (int q = 0; q < QA; ++q) {
     const int m = m0 + (tid >> 4) + 16 * q;
     am[q] = m < M;
     aoh[q] = am[q] ? m / a.OW : 0;
     aow[q] = am[q] ? m - aoh[q] * a.OW : 0;
   }
-  // B-load slots: c = (tid >> 6) + 4 q, column n = tid & 63
-  const int bn = tid & 63, bco = n0 + bn;
-  float ra[4], rb[4];
+  // B-load slots: c = tid / BN + BS q, column n = tid % BN
+  const int bn = tid % BN, bco = n0 + bn;
+  float ra[QA], rb[QB];
   auto load = [&](int it) {
     const int tap = it / nci, cb = it - (it / nci) * nci;
     const int ci = cb * kBK + ac;
@@ -174,7 +178,7 @@ __global__ void __launch_bounds__(256) conv2d_kernel(const C2Args a) {
       dy = dx = 1;
     }
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < QA; ++q) {
       float v = 0.f;
       int ih, iw;
       bool ok = am[q] && ci < a.C_in;
@@ -194,18 +198,18 @@ __global__ void __launch_bounds__(256) conv2d_kernel(const C2Args a) {
       ra[q] = v;
     }
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int c = cb * kBK + (tid >> 6) + 4 * q;
+    for (int q = 0; q < QB; ++q) {
+      const int c = cb * kBK + tid / BN + BS * q;
       rb[q] = (c < a.C_in && bco < a.C_out) ? __ldg(a.w + ((long long)tap * a.C_in + c) * a.C_out + bco) : 0.f;
     }
   };
   auto store = [&](int buf) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) As[buf][ac][(tid >> 4) + 16 * q] = ra[q];
+    for (int q = 0; q < QA; ++q) As[buf][ac][(tid >> 4) + 16 * q] = ra[q];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) Bs[buf][(tid >> 6) + 4 * q][bn] = rb[q];
+    for (int q = 0; q < QB; ++q) Bs[buf][tid / BN + BS * q][bn] = rb[q];
   };
-  const int tx = tid & 15, ty = tid >> 4;
+  const int tx = tid % (BN / 4), ty = tid / (BN / 4);
   float acc[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
@@ -281,84 +285,80 @@ __global__ void avgpool_kernel(const float* __restrict__ x, long long x_bs, int 
 }
 
 // ------------------------------------------------------------------ BiGRU
-// One 8-CTA cluster per direction (blockIdx.x / 8).  CTA `rank` owns hidden
-// units [32 rank, 32 rank + 32): rows g*256 + unit of the recurrent matrix for
-// the gates g = r, z, n.  Per step: gh = W_hh h + b_hh for its 96 rows, the
-// gate update of its 32 units for every sequence, and a store of the new units
-// into every CTA's next h buffer (distributed shared memory), then one cluster
-// barrier.  gx = x W_ih^T + b_ih is precomputed for both directions.
-constexpr int kGruCta = 8, kGruUnits = 32, kGruRows = 96, kGruThreads = 384, kGruMaxB = 8, kGruLd = 257;
+// One 8-CTA cluster per (direction, group of kGruBg sequences).  CTA `rank`
+// owns hidden units [32 rank, 32 rank + 32): the 96 rows g*256 + unit of the
+// recurrent matrix for the gates g = r, z, n, held in registers (warp w: rows
+// 8w..8w+7, lane l: columns l + 32k).  Per step: gh = W_hh h + b_hh for those
+// rows, the gate update of its 32 units, a store of the new units into every
+// CTA's next h buffer (distributed shared memory), then one cluster barrier.
+// gx = x W_ih^T + b_ih is precomputed for both directions.
+constexpr int kGruCta = 8, kGruUnits = 32, kGruRows = 96, kGruThreads = 384, kGruBg = 2;
 
 __global__ void __cluster_dims__(kGruCta, 1, 1) __launch_bounds__(kGruThreads)
     gru_kernel(const float* __restrict__ gx, const float* __restrict__ whh, const float* __restrict__ bhh, int B,
                int T, float* __restrict__ out) {
-  extern __shared__ float sm[];
-  float* Ws = sm;                                  // [96][257]
-  float* hb = Ws + kGruRows * kGruLd;              // [2][kGruMaxB][256]
-  float* gh = hb + 2 * kGruMaxB * 256;             // [kGruMaxB][96]
+  __shared__ float hb[2][kGruBg][256];
+  __shared__ float gh[kGruBg][kGruRows];
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
-  const int dir = blockIdx.x / kGruCta;
+  const int cid = blockIdx.x / kGruCta;
+  const int dir = cid & 1, b0 = (cid >> 1) * kGruBg;
+  const int nb = min(kGruBg, B - b0);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float* W = whh + (long long)dir * 768 * 256;
-  for (int e = tid; e < kGruRows * 256; e += kGruThreads) {
-    const int rr = e / 256, k = e - rr * 256;
-    const int row = (rr / kGruUnits) * 256 + rank * kGruUnits + (rr % kGruUnits);
-    Ws[rr * kGruLd + k] = W[(long long)row * 256 + k];
-  }
-  for (int e = tid; e < 2 * kGruMaxB * 256; e += kGruThreads) hb[e] = 0.f;
-  float bias_row[kGruRows / 12];
-  // warp w handles rows w*8 .. w*8+7 (12 warps x 8 rows = 96)
+  float w[8][8], bias_row[8];
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
     const int rr = warp * 8 + q;
-    bias_row[q] = bhh[dir * 768 + (rr / kGruUnits) * 256 + rank * kGruUnits + (rr % kGruUnits)];
+    const int row = (rr / kGruUnits) * 256 + rank * kGruUnits + (rr % kGruUnits);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) w[q][k] = W[(long long)row * 256 + lane + 32 * k];
+    bias_row[q] = bhh[dir * 768 + row];
   }
+  for (int e = tid; e < 2 * kGruBg * 256; e += kGruThreads) (&hb[0][0][0])[e] = 0.f;
   cluster.sync();
   const int gu = tid % kGruUnits, gb = tid / kGruUnits;  // gate threads: unit, sequence
-  const bool gate = gb < B;
+  const bool gate = gb < nb;
   const int j = rank * kGruUnits + gu;
   for (int s = 0; s < T; ++s) {
     const int tt = dir == 0 ? s : T - 1 - s;
     const int cur = s & 1, nxt = cur ^ 1;
     float gxr = 0.f, gxz = 0.f, gxn = 0.f;
     if (gate) {
-      const float* g = gx + ((long long)gb * T + tt) * 1536 + dir * 768;
+      const float* g = gx + ((long long)(b0 + gb) * T + tt) * 1536 + dir * 768;
       gxr = g[j];
       gxz = g[256 + j];
       gxn = g[512 + j];
     }
+    for (int bb = 0; bb < nb; ++bb) {
+      float hv[8];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const int rr = warp * 8 + q;
-      const float* wr = Ws + rr * kGruLd;
-      for (int bb = 0; bb < B; ++bb) {
-        const float* h = hb + (cur * kGruMaxB + bb) * 256;
+      for (int k = 0; k < 8; ++k) hv[k] = hb[cur][bb][lane + 32 * k];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
         float acc = 0.f;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) acc = fmaf(wr[lane + 32 * k], h[lane + 32 * k], acc);
+        for (int k = 0; k < 8; ++k) acc = fmaf(w[q][k], hv[k], acc);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (lane == 0) gh[bb * kGruRows + rr] = __fadd_rn(acc, bias_row[q]);
+        if (lane == 0) gh[bb][warp * 8 + q] = __fadd_rn(acc, bias_row[q]);
       }
     }
     __syncthreads();
     if (gate) {
-      const float* g = gh + gb * kGruRows;
-      const float r = sigmoid_two_sided(__fadd_rn(gxr, g[gu]));
-      const float z = sigmoid_two_sided(__fadd_rn(gxz, g[kGruUnits + gu]));
-      const float n = tanhf(__fadd_rn(gxn, __fmul_rn(r, g[2 * kGruUnits + gu])));
-      const float hp = hb[(cur * kGruMaxB + gb) * 256 + j];
+      const float r = sigmoid_two_sided(__fadd_rn(gxr, gh[gb][gu]));
+      const float z = sigmoid_two_sided(__fadd_rn(gxz, gh[gb][kGruUnits + gu]));
+      const float n = tanhf(__fadd_rn(gxn, __fmul_rn(r, gh[gb][2 * kGruUnits + gu])));
+      const float hp = hb[cur][gb][j];
       const float hn = __fadd_rn(__fmul_rn(__fsub_rn(1.f, z), n), __fmul_rn(z, hp));
-      out[((long long)gb * T + tt) * 512 + dir * 256 + j] = hn;
-      float* dst = hb + (nxt * kGruMaxB + gb) * 256 + j;
+      out[((long long)(b0 + gb) * T + tt) * 512 + dir * 256 + j] = hn;
+      float* dst = &hb[nxt][gb][j];
+#pragma unroll
       for (int r2 = 0; r2 < kGruCta; ++r2) *cluster.map_shared_rank(dst, r2) = hn;
     }
     cluster.sync();
   }
 }
-
-constexpr size_t kGruSmem = sizeof(float) * (kGruRows * kGruLd + 2 * kGruMaxB * 256 + kGruMaxB * kGruRows);
 
 // ------------------------------------------------------------------ decode
 __global__ void decode_kernel(const float* __restrict__ sal, int Fp, int F, float thred, float* __restrict__ f0,
@@ -403,17 +403,6 @@ __global__ void decode_kernel(const float* __restrict__ sal, int Fp, int F, floa
   if (f == 10.f) f = 0.f;
   f0[(long long)b * F + t] = f;
   if (amax) amax[(long long)b * F + t] = bi;
-}
-
-template <typename K>
-void set_smem_once(K kernel, size_t bytes) {
-  static std::atomic<uint64_t> done{0};
-  int dev = 0;
-  RVC_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev < 64 && !(done.load() & (1ull << dev))) {
-    RVC_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
-    done.fetch_or(1ull << dev);
-  }
 }
 
 int grid_for(long long n, int block) {
@@ -667,7 +656,7 @@ void RmvpeModel::ensure_ws(int B, int64_t T) {
   add("sal", Fp * 360);
   add("f0", F);
   ws_.emplace("amax", DevBuf(ctx, sizeof(int32_t) * (size_t)B * F));
-  ws_.emplace("part", DevBuf(ctx, sizeof(float) * (size_t)(4 * 148 + 64) * kBM * kBN));
+  ws_.emplace("part", DevBuf(ctx, sizeof(float) * (size_t)(4 * 148 + 64) * kTileElems));
   ws_B = B;
   ws_T = T;
 }
@@ -706,7 +695,8 @@ void RmvpeModel::conv(const Conv2dW& L, int B, const float* x, long long x_bs, i
   a.B = B;
   a.kit = L.taps * ((L.C_in + kBK - 1) / kBK);
   const long long M = (long long)a.OH * a.OW;
-  const int mt = (int)((M + kBM - 1) / kBM), nt = (L.C_out + kBN - 1) / kBN;
+  const int BN = L.C_out <= 16 ? 16 : (L.C_out <= 32 ? 32 : 64), BM = kTileElems / BN;
+  const int mt = (int)((M + BM - 1) / BM), nt = (L.C_out + BN - 1) / BN;
   const long long tiles = (long long)mt * nt * B;
   int splits = 1;
   // few output tiles and a long K loop: split K so ~2 waves of blocks run
@@ -718,13 +708,26 @@ void RmvpeModel::conv(const Conv2dW& L, int B, const float* x, long long x_bs, i
   a.splits = splits;
   a.part = ws_.at("part").f();
   dim3 g(mt, nt, B * splits);
-  conv2d_kernel<<<g, 256, 0, ctx->stream>>>(a);
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  if (ctx->prof) ctx->prof_begin(&e0, &e1);
+  if (BN == 16)
+    conv2d_kernel<256, 16><<<g, 256, 0, ctx->stream>>>(a);
+  else if (BN == 32)
+    conv2d_kernel<128, 32><<<g, 256, 0, ctx->stream>>>(a);
+  else
+    conv2d_kernel<64, 64><<<g, 256, 0, ctx->stream>>>(a);
   note_launch();
   RVC_CUDA_TRY(cudaGetLastError());
   if (splits > 1) {
     conv2d_reduce_kernel<<<grid_for(B * M * L.C_out, 256), 256, 0, ctx->stream>>>(a);
     note_launch();
     RVC_CUDA_TRY(cudaGetLastError());
+  }
+  if (ctx->prof) {
+    char lab[160];
+    snprintf(lab, sizeof(lab), "rmvpe %s Cin=%d Cout=%d taps=%d %dx%d B=%d split=%d", L.transposed ? "convT" : "conv",
+             L.C_in, L.C_out, L.taps, a.OH, a.OW, B, splits);
+    ctx->prof_end(e0, e1, 2.0 * B * M * L.C_out * L.C_in * (L.transposed ? 2.25 : (double)L.taps), lab, false);
   }
 }
 
@@ -834,11 +837,9 @@ void RmvpeModel::infer_device(int B, int64_t T, const float* x, float thred, flo
   // ---------------- BiGRU: gx for both directions, then the recurrence
   conv(convs_.at("gru_in"), B, buf("feat"), (long long)Fp * 384, Fp, 1, 384, buf("gx"), (long long)Fp * 1536, 1536,
        1536, 1, false, nullptr, 0, 0);
-  set_smem_once(gru_kernel, kGruSmem);
-  for (int b0 = 0; b0 < B; b0 += kGruMaxB) {
-    const int nb = std::min(kGruMaxB, B - b0);
-    gru_kernel<<<2 * kGruCta, kGruThreads, kGruSmem, st>>>(buf("gx") + (size_t)b0 * Fp * 1536, w_hh_.f(), b_hh_.f(),
-                                                            nb, Fp, buf("hg") + (size_t)b0 * Fp * 512);
+  {
+    const int groups = (B + kGruBg - 1) / kGruBg;  // every (direction, sequence group) cluster runs at once
+    gru_kernel<<<2 * groups * kGruCta, kGruThreads, 0, st>>>(buf("gx"), w_hh_.f(), b_hh_.f(), B, Fp, buf("hg"));
     note_launch();
     RVC_CUDA_TRY(cudaGetLastError());
   }
