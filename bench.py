@@ -183,7 +183,8 @@ def run_hubert(args, world, rank, local):
         import datetime
 
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
 
     def barrier():
         if dist is not None:
@@ -320,7 +321,8 @@ def run_retrieval(args, world, rank, local):
         import datetime
 
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
 
     def barrier():
         if dist is not None:
@@ -471,7 +473,8 @@ def run_rmvpe(args, world, rank, local):
         import datetime
 
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
 
     def barrier():
         if dist is not None:
@@ -658,7 +661,8 @@ def run_ours(args, world, rank, local):
         import datetime
 
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
 
     def barrier():
         if dist is not None:
