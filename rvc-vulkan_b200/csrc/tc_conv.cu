@@ -38,6 +38,9 @@ constexpr int kThreads = kWarps * 32;
 constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s per barrier wait
 constexpr int kEpiCols = 32;
 constexpr uint32_t kSlotBytes = kTM * kEpiCols * 4;  // one 128 x 32 fp32 tile
+constexpr int kEpiRows = 32;                           // rows per epilogue warp (its TMEM lane quarter)
+constexpr uint32_t kWarpSlotBytes = kEpiRows * kEpiCols * 4;  // a warp's 32 x 32 part of a slot
+constexpr int kBarriers = 22 + 16;                     // fixed barriers + EPI_W[4 slots][4 warps]
 
 struct TcMaps {
   CUtensorMap a, res, acc, y;
@@ -181,13 +184,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t sbase = ptx::smem_u32(smem);
   const uint32_t bar0 = sbase + g.off_bar;
-  // barriers: A_FULL[2] A_EMPTY[2] STG_FULL[4] STG_EMPTY[4] ACC_FULL[2] ACC_EMPTY[2] EPI_FULL[4] DRAIN
-  //           B_FULL[stages] B_EMPTY[stages], then the TMEM address slot
+  // barriers: A_FULL[2] A_EMPTY[2] STG_FULL[4] STG_EMPTY[4] ACC_FULL[2] ACC_EMPTY[2] (4 unused) DRAIN
+  //           W_FULL EPI_W[4 slots][4 epilogue warps] B_FULL[stages] B_EMPTY[stages], then the TMEM
+  //           address slot
   const uint32_t A_FULL = bar0, A_EMPTY = bar0 + 16, STG_FULL = bar0 + 32, STG_EMPTY = bar0 + 64;
-  const uint32_t ACC_FULL = bar0 + 96, ACC_EMPTY = bar0 + 112, EPI_FULL = bar0 + 128, DRAIN = bar0 + 160;
-  const uint32_t W_FULL = bar0 + 168;
-  const uint32_t B_FULL = bar0 + 176, B_EMPTY = B_FULL + 8u * g.stages;
-  uint32_t* tmem_slot = (uint32_t*)(smem + g.off_bar + 8 * (22 + 2 * g.stages));
+  const uint32_t ACC_FULL = bar0 + 96, ACC_EMPTY = bar0 + 112, DRAIN = bar0 + 160;
+  const uint32_t W_FULL = bar0 + 168, EPI_W = bar0 + 176;
+  const uint32_t B_FULL = EPI_W + 8u * 16, B_EMPTY = B_FULL + 8u * g.stages;
+  uint32_t* tmem_slot = (uint32_t*)(smem + g.off_bar + 8 * (kBarriers + 2 * g.stages));
   auto a_plane = [&](int buf, int lo) { return sbase + g.off_a + (uint32_t)(2 * buf + lo) * g.a_plane; };
   auto b_plane = [&](int st, int lo) { return sbase + g.off_b + (uint32_t)(2 * st + lo) * g.b_plane; };
   auto stg = [&](int sb) { return g.off_stg + (uint32_t)sb * g.stg_bytes; };  // offset from smem
@@ -205,8 +209,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 4; ++i) {
       ptx::mbar_init(STG_FULL + 8 * i, 1);
       ptx::mbar_init(STG_EMPTY + 8 * i, 128);
-      ptx::mbar_init(EPI_FULL + 8 * i, 1);
     }
+    for (int i = 0; i < 16; ++i) ptx::mbar_init(EPI_W + 8 * i, 1);
     ptx::mbar_init(DRAIN, 1);
     ptx::mbar_init(W_FULL, 1);
     for (int i = 0; i < g.stages; ++i) {
@@ -406,7 +410,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int r_in = wq * 32 + lane;  // row within a 128-row subtile
     int it = 0;
     if (g.tma_epi) {
-      const bool leader = (warp == 7 && lane == 0);
+      // Each epilogue warp runs its own pipeline over its 32 TMEM lanes: its
+      // residual / accumulator boxes (32 rows x 32 columns) arrive by TMA into its
+      // 4 KB part of a slot, it writes the result there in place and its lane 0
+      // stores the box.  No barrier across the four warps per step.
+      const bool wlead = lane == 0;
       const int nch = BN / kEpiCols;
       const int spt = g.msub * nch;
       const int ntile_cta = (g.total_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
@@ -414,6 +422,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // prefetch distance: loads for step e + pdist are issued at step e; with
       // nslot >= 3 that slot's last store is not the one just committed
       const int pdist = g.nslot >= 3 ? g.nslot - 2 : g.nslot - 1;
+      const uint32_t wslot = (uint32_t)wq * kWarpSlotBytes;
+      auto epi_bar = [&](int sl) { return EPI_W + 8u * (uint32_t)(sl * 4 + wq); };
       int issued = 0;
       auto issue = [&](int f) {
         if (f >= total_steps) return;
@@ -422,19 +432,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const TileCoord c = tile_coord(blockIdx.x + (f / spt) * gridDim.x, a.nslices, g.ntiles, g.tiles_m);
         const ConvSlice& S = a.sl[c.s];
         const int q = f % spt, sub = q / nch, ch = q % nch;
-        const int row0 = c.mt * MT + sub * kTM, col0 = S.co_off + c.nt * BN + ch * kEpiCols;
-        // the slot's previous store (step f - nslot) has finished reading it; the
-        // nslot - pdist - 1 newer stores may still be in flight
+        const int row0 = c.mt * MT + sub * kTM + wq * kEpiRows, col0 = S.co_off + c.nt * BN + ch * kEpiCols;
+        // this warp's previous store from the slot (step f - nslot) has finished
+        // reading it; the nslot - pdist - 1 newer stores may still be in flight
         ptx::bulk_wait_read(g.nslot - pdist - 1);
-        const uint32_t bytes = (a.res ? kSlotBytes : 0u) + (a.accin ? kSlotBytes : 0u);
-        ptx::mbar_expect_tx(EPI_FULL + 8 * sl, bytes);
+        const uint32_t bytes = (a.res ? kWarpSlotBytes : 0u) + (a.accin ? kWarpSlotBytes : 0u);
+        ptx::mbar_expect_tx(epi_bar(sl), bytes);
         if (g.ephase) {  // transposed-conv phase p: rows q*up + p through the 4-D view
-          if (a.res) ptx::tma_load_4d(sbase + slot_main(sl), &maps.res, col0, S.out_r0, row0, c.b, EPI_FULL + 8 * sl);
+          if (a.res)
+            ptx::tma_load_4d(sbase + slot_main(sl) + wslot, &maps.res, col0, S.out_r0, row0, c.b, epi_bar(sl));
           if (a.accin)
-            ptx::tma_load_4d(sbase + slot_aux(sl), &maps.acc, col0, S.out_r0, row0, c.b, EPI_FULL + 8 * sl);
+            ptx::tma_load_4d(sbase + slot_aux(sl) + wslot, &maps.acc, col0, S.out_r0, row0, c.b, epi_bar(sl));
         } else {
-          if (a.res) ptx::tma_load_3d(sbase + slot_main(sl), &maps.res, col0, row0, c.b, EPI_FULL + 8 * sl);
-          if (a.accin) ptx::tma_load_3d(sbase + slot_aux(sl), &maps.acc, col0, row0, c.b, EPI_FULL + 8 * sl);
+          if (a.res) ptx::tma_load_3d(sbase + slot_main(sl) + wslot, &maps.res, col0, row0, c.b, epi_bar(sl));
+          if (a.accin) ptx::tma_load_3d(sbase + slot_aux(sl) + wslot, &maps.acc, col0, row0, c.b, epi_bar(sl));
         }
       };
       if (g.off_bias) {  // stage the bias vector once per CTA
@@ -444,7 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ptx::named_bar(3, 128);
       }
-      if (leader)
+      if (wlead)
         for (int f = 0; f < pdist; ++f) issue(f);
       int e = 0;
       bool ok = true;
@@ -452,8 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const TileCoord c = tile_coord(tile, a.nslices, g.ntiles, g.tiles_m);
         const ConvSlice& S = a.sl[c.s];
         const int set = it % g.nacc;
-        // all four epilogue warps agree on the outcome (bar.red.and)
-        const bool got = ptx::named_bar_and(1, 128, ptx::mbar_wait(ACC_FULL + 8 * set, (it / g.nacc) & 1, kWaitNs));
+        const bool got = __all_sync(0xffffffffu, ptx::mbar_wait(ACC_FULL + 8 * set, (it / g.nacc) & 1, kWaitNs));
         if (!got) {
           if (lane == 0) atomicExch(a.err, 7);
           ok = false;
@@ -462,10 +472,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         ptx::tc_fence_after();
         const uint32_t dbase = tmem + (uint32_t)(set * g.msub * BN) + ((uint32_t)(wq * 32) << 16);
         for (int q = 0; q < spt; ++q, ++e) {
-          if (leader) issue(e + pdist);
+          if (wlead) issue(e + pdist);
           const int sl = e % g.nslot;
           const int sub = q / nch, ch = q % nch;
-          const bool in = ptx::named_bar_and(1, 128, ptx::mbar_wait(EPI_FULL + 8 * sl, (e / g.nslot) & 1, kWaitNs));
+          const bool in = __all_sync(0xffffffffu, ptx::mbar_wait(epi_bar(sl), (e / g.nslot) & 1, kWaitNs));
           float v[32];
           ptx::tmem_ld32(dbase + (uint32_t)(sub * BN + ch * kEpiCols), v);
           if (q == spt - 1) {
@@ -478,11 +488,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const int col0 = S.co_off + c.nt * BN + ch * kEpiCols;
-          const uint32_t mainp = sbase + slot_main(sl) + (uint32_t)r_in * 128u;
-          const uint32_t auxp = sbase + slot_aux(sl) + (uint32_t)r_in * 128u;
+          const uint32_t mainp = sbase + slot_main(sl) + wslot + (uint32_t)lane * 128u;
+          const uint32_t auxp = sbase + slot_aux(sl) + wslot + (uint32_t)lane * 128u;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const uint32_t off = (uint32_t)((j ^ (r_in & 7)) << 4);  // 128B swizzle of the TMA box
+            const uint32_t off = (uint32_t)((j ^ (lane & 7)) << 4);  // 128B swizzle of the TMA box
             float x[4] = {v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]};
             if (a.bias) {
               const float4 t = g.off_bias ? ptx::lds128(sbase + g.off_bias + (uint32_t)(col0 + 4 * j) * 4u)
@@ -512,23 +522,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             ptx::sts128(mainp + off, make_float4(x[0], x[1], x[2], x[3]));
           }
           ptx::fence_proxy_async_smem();
-          ptx::named_bar(2, 128);
-          if (leader) {
+          __syncwarp();
+          if (wlead) {
+            const int row0 = c.mt * MT + sub * kTM + wq * kEpiRows;
             if (g.ephase)
-              ptx::tma_store_4d(&maps.y, col0, S.out_r0, c.mt * MT + sub * kTM, c.b, sbase + slot_main(sl));
+              ptx::tma_store_4d(&maps.y, col0, S.out_r0, row0, c.b, sbase + slot_main(sl) + wslot);
             else
-              ptx::tma_store_3d(&maps.y, col0, c.mt * MT + sub * kTM, c.b, sbase + slot_main(sl));
+              ptx::tma_store_3d(&maps.y, col0, row0, c.b, sbase + slot_main(sl) + wslot);
             ptx::bulk_commit();
           }
         }
         ++it;
       }
-      if (leader) {
-        // no TMA load left in flight into a slot, no store still reading one
+      if (wlead) {
+        // no TMA load left in flight into this warp's slots, no store still reading one
         for (int f = (issued > g.nslot ? issued - g.nslot : 0); f < issued; ++f)
-          ptx::mbar_wait(EPI_FULL + 8 * (f % g.nslot), (f / g.nslot) & 1, kWaitNs);
+          ptx::mbar_wait(epi_bar(f % g.nslot), (f / g.nslot) & 1, kWaitNs);
         ptx::bulk_wait0();
       }
+      __syncwarp();
     } else {
       bool ok = true;
       for (int tile = blockIdx.x; tile < g.total_tiles && ok; tile += gridDim.x) {
@@ -609,7 +621,7 @@ static void make_phase_map(CUtensorMap* m, const float* base, int width, int up,
                            long long bs) {
   cuuint64_t dims[4] = {(cuuint64_t)width, (cuuint64_t)up, (cuuint64_t)q_rows, (cuuint64_t)B};
   cuuint64_t strides[3] = {(cuuint64_t)ld * 4, (cuuint64_t)ld * 4 * up, (cuuint64_t)bs * 4};
-  cuuint32_t box[4] = {(cuuint32_t)kEpiCols, 1, (cuuint32_t)kTM, 1};
+  cuuint32_t box[4] = {(cuuint32_t)kEpiCols, 1, (cuuint32_t)kEpiRows, 1};
   cuuint32_t es[4] = {1, 1, 1, 1};
   CUresult r = encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (void*)base, dims, strides, box, es,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -720,7 +732,7 @@ static TcPlan tc_plan(const ConvArgs& a) {
     const uint32_t off_b = off;
     int stages = cd.res ? 1 : 8;
     const uint32_t ring = cd.res ? 0u : 2u * g.b_plane;
-    auto total = [&](int st) { return 1024u + off_b + (uint32_t)st * ring + 8u * (22 + 2 * st) + 16u; };
+    auto total = [&](int st) { return 1024u + off_b + (uint32_t)st * ring + 8u * (kBarriers + 2 * st) + 16u; };
     while (stages > 2 && total(stages) > limit) --stages;
     if (total(stages) > limit || (!cd.res && stages < need_stages)) return false;
     g.w_res = cd.res;
@@ -778,9 +790,9 @@ void launch_tc_conv(const ConvArgs& a, cudaStream_t st) {
       if (a.res) make_phase_map(&maps.res, a.res, width, a.out_rs, rows, a.B, a.res_ld, a.res_bs);
       if (a.accin) make_phase_map(&maps.acc, a.accin, width, a.out_rs, rows, a.B, a.acc_ld, a.acc_bs);
     } else {
-      make_map(&maps.y, a.y, width, rows, a.B, a.y_ld, a.y_bs, kEpiCols, kTM, true);
-      if (a.res) make_map(&maps.res, a.res, width, rows, a.B, a.res_ld, a.res_bs, kEpiCols, kTM, true);
-      if (a.accin) make_map(&maps.acc, a.accin, width, rows, a.B, a.acc_ld, a.acc_bs, kEpiCols, kTM, true);
+      make_map(&maps.y, a.y, width, rows, a.B, a.y_ld, a.y_bs, kEpiCols, kEpiRows, true);
+      if (a.res) make_map(&maps.res, a.res, width, rows, a.B, a.res_ld, a.res_bs, kEpiCols, kEpiRows, true);
+      if (a.accin) make_map(&maps.acc, a.accin, width, rows, a.B, a.acc_ld, a.acc_bs, kEpiCols, kEpiRows, true);
     }
   }
   int dev = 0;
