@@ -172,6 +172,36 @@ __device__ __forceinline__ TileCoord tile_coord(int tile, int nslices, int ntile
   return c;
 }
 
+// Two fp32 values -> (hi, lo) bf16x2 words with hi = RN(x), lo = RN(x - hi),
+// one paired conversion per word (same values as split_bf16 element by element).
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  const float2 hf = __bfloat1622float2(h);
+  const __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// Activation of a whole 32-value epilogue row segment, the act chosen once.
+// leaky_relu as max(x, s*x) when 0 <= s <= 1 (equal to x >= 0 ? x : s*x there).
+__device__ __forceinline__ void act_row(float (&x)[32], int act, float slope) {
+  switch (act) {
+    case kActNone: return;
+    case kActLeaky:
+      if (slope >= 0.f && slope <= 1.f) {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) x[k] = fmaxf(x[k], slope * x[k]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) x[k] = x[k] >= 0.f ? x[k] : slope * x[k];
+      }
+      return;
+    default:
+#pragma unroll
+      for (int k = 0; k < 32; ++k) x[k] = act_apply(x[k], act, slope);
+  }
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     tc_conv_kernel(const __grid_constant__ ConvArgs a, const __grid_constant__ TcMaps maps, TcPlan g) {
   extern __shared__ uint8_t smem_raw[];
@@ -380,24 +410,49 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const uint32_t src = sbase + stg(sb);
         const uint32_t phi = a_plane(buf, 0), plo = a_plane(buf, 1);
+        const bool leaky_max = a.in_act == kActLeaky && a.in_slope >= 0.f && a.in_slope <= 1.f;
+        if ((128 % c4n) == 0 && (a.in_act == kActNone || leaky_max)) {
+          // each thread keeps one 4-channel column c4 and walks rows 128/c4n apart
+          const int c4 = tp % c4n, rstep = 128 / c4n;
+          const int niter = total > tp ? (total - tp + 127) / 128 : 0;
+          uint32_t s_addr = src + (uint32_t)tp * 16u;
+          uint32_t off = (uint32_t)(c4 >> 1) * LBO_A + (uint32_t)(tp / c4n) * 16u + (uint32_t)(c4 & 1) * 8u;
+          const float sl = leaky_max ? a.in_slope : 1.f;
 #pragma unroll 4
-        for (int e = tp; e < total; e += 128) {
-          const int r = e / c4n, c4 = e - r * c4n;
-          float4 v = ptx::lds128(src + (uint32_t)e * 16u);
-          if (a.in_act) {
-            v.x = act_apply(v.x, a.in_act, a.in_slope);
-            v.y = act_apply(v.y, a.in_act, a.in_slope);
-            v.z = act_apply(v.z, a.in_act, a.in_slope);
-            v.w = act_apply(v.w, a.in_act, a.in_slope);
+          for (int i = 0; i < niter; ++i) {
+            float4 v = ptx::lds128(s_addr);
+            if (leaky_max) {
+              v.x = fmaxf(v.x, sl * v.x);
+              v.y = fmaxf(v.y, sl * v.y);
+              v.z = fmaxf(v.z, sl * v.z);
+              v.w = fmaxf(v.w, sl * v.w);
+            }
+            uint32_t h01, l01, h23, l23;
+            split_pair(v.x, v.y, h01, l01);
+            split_pair(v.z, v.w, h23, l23);
+            ptx::sts64(phi + off, h01, h23);
+            ptx::sts64(plo + off, l01, l23);
+            s_addr += 2048u;
+            off += (uint32_t)rstep * 16u;
           }
-          __nv_bfloat16 h0, h1, h2, h3, l0, l1, l2, l3;
-          split_bf16(v.x, h0, l0);
-          split_bf16(v.y, h1, l1);
-          split_bf16(v.z, h2, l2);
-          split_bf16(v.w, h3, l3);
-          const uint32_t off = (uint32_t)(c4 >> 1) * LBO_A + (uint32_t)r * 16u + (uint32_t)(c4 & 1) * 8u;
-          ptx::sts64(phi + off, pack_bf16x2(h0, h1), pack_bf16x2(h2, h3));
-          ptx::sts64(plo + off, pack_bf16x2(l0, l1), pack_bf16x2(l2, l3));
+        } else {
+#pragma unroll 4
+          for (int e = tp; e < total; e += 128) {
+            const int r = e / c4n, c4 = e - r * c4n;
+            float4 v = ptx::lds128(src + (uint32_t)e * 16u);
+            if (a.in_act) {
+              v.x = act_apply(v.x, a.in_act, a.in_slope);
+              v.y = act_apply(v.y, a.in_act, a.in_slope);
+              v.z = act_apply(v.z, a.in_act, a.in_slope);
+              v.w = act_apply(v.w, a.in_act, a.in_slope);
+            }
+            uint32_t h01, l01, h23, l23;
+            split_pair(v.x, v.y, h01, l01);
+            split_pair(v.z, v.w, h23, l23);
+            const uint32_t off = (uint32_t)(c4 >> 1) * LBO_A + (uint32_t)r * 16u + (uint32_t)(c4 & 1) * 8u;
+            ptx::sts64(phi + off, h01, h23);
+            ptx::sts64(plo + off, l01, l23);
+          }
         }
         ptx::fence_proxy_async_smem();
         ptx::mbar_arrive(A_FULL + 8 * buf);
@@ -490,37 +545,55 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int col0 = S.co_off + c.nt * BN + ch * kEpiCols;
           const uint32_t mainp = sbase + slot_main(sl) + wslot + (uint32_t)lane * 128u;
           const uint32_t auxp = sbase + slot_aux(sl) + wslot + (uint32_t)lane * 128u;
+          // each optional term is one uniform branch per 32 values
+          if (a.bias) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const uint32_t off = (uint32_t)((j ^ (lane & 7)) << 4);  // 128B swizzle of the TMA box
-            float x[4] = {v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]};
-            if (a.bias) {
+            for (int j = 0; j < 8; ++j) {
               const float4 t = g.off_bias ? ptx::lds128(sbase + g.off_bias + (uint32_t)(col0 + 4 * j) * 4u)
                                           : __ldg(reinterpret_cast<const float4*>(a.bias + col0) + j);
-              x[0] += t.x; x[1] += t.y; x[2] += t.z; x[3] += t.w;
+              v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
             }
-            if (a.bias2) {
-              const float4 t = __ldg(reinterpret_cast<const float4*>(a.bias2 + (long long)c.b * a.bias2_bs + col0) + j);
-              x[0] += t.x; x[1] += t.y; x[2] += t.z; x[3] += t.w;
-            }
-            if (a.res) {
-              const float4 t = ptx::lds128(mainp + off);
-              const float r4[4] = {t.x, t.y, t.z, t.w};
-#pragma unroll
-              for (int k = 0; k < 4; ++k) x[k] = a.res_sub ? (r4[k] - x[k]) : (x[k] + r4[k]);
-            }
-            if (a.accin) {
-              const float4 t = ptx::lds128(auxp + off);
-              x[0] = t.x + x[0]; x[1] = t.y + x[1]; x[2] = t.z + x[2]; x[3] = t.w + x[3];
-            }
-            if (a.out_div != 0.f) {
-#pragma unroll
-              for (int k = 0; k < 4; ++k) x[k] = x[k] / a.out_div;
-            }
-#pragma unroll
-            for (int k = 0; k < 4; ++k) x[k] = act_apply(x[k], a.out_act, a.out_slope);
-            ptx::sts128(mainp + off, make_float4(x[0], x[1], x[2], x[3]));
           }
+          if (a.bias2) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 t = __ldg(reinterpret_cast<const float4*>(a.bias2 + (long long)c.b * a.bias2_bs + col0) + j);
+              v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
+            }
+          }
+          if (a.res) {
+            if (a.res_sub) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 t = ptx::lds128(mainp + (uint32_t)((j ^ (lane & 7)) << 4));
+                v[4 * j] = t.x - v[4 * j]; v[4 * j + 1] = t.y - v[4 * j + 1];
+                v[4 * j + 2] = t.z - v[4 * j + 2]; v[4 * j + 3] = t.w - v[4 * j + 3];
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 t = ptx::lds128(mainp + (uint32_t)((j ^ (lane & 7)) << 4));
+                v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
+              }
+            }
+          }
+          if (a.accin) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 t = ptx::lds128(auxp + (uint32_t)((j ^ (lane & 7)) << 4));
+              v[4 * j] = t.x + v[4 * j]; v[4 * j + 1] = t.y + v[4 * j + 1];
+              v[4 * j + 2] = t.z + v[4 * j + 2]; v[4 * j + 3] = t.w + v[4 * j + 3];
+            }
+          }
+          if (a.out_div != 0.f) {
+#pragma unroll
+            for (int k = 0; k < 32; ++k) v[k] = v[k] / a.out_div;
+          }
+          act_row(v, a.out_act, a.out_slope);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            ptx::sts128(mainp + (uint32_t)((j ^ (lane & 7)) << 4),
+                        make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]));
           ptx::fence_proxy_async_smem();
           __syncwarp();
           if (wlead) {
