@@ -88,10 +88,13 @@ void launch_simt_conv(const ConvArgs& a, cudaStream_t st) {
 
 // =====================================================================
 // Weight packing for the tensor path.
-// Layout per (tap, n-tile, k-block): [hi plane | lo plane], each plane
-// [chunk c (cb/8)][row n (bn)][8 bf16]  == the K-major no-swizzle canonical
-// layout with SBO = 128 B and LBO = bn*16 B, so one bulk copy per plane lands
-// an MMA-ready B tile in shared memory.
+// Layout per (tap, n-tile, k-block), 2*cb*bn bf16:
+//  * bn > 64: [hi plane | lo plane], each plane [chunk c (cb/8)][row n (bn)][8 bf16]
+//    == the K-major no-swizzle canonical layout with SBO = 128 B, LBO = bn*16 B;
+//  * bn <= 64 (stacked): [chunk c][row: hi rows 0..bn-1, lo rows bn..2bn-1][8 bf16]
+//    with LBO = 2*bn*16 B, so [B_hi | B_lo] is one N = 2*bn operand and B_hi alone
+//    the first bn rows of it.
+// One bulk copy per block lands an MMA-ready B tile in shared memory.
 // =====================================================================
 bool tc_shape_ok(int C_in, int C_out) { return C_in % 16 == 0 && C_out % 16 == 0; }
 
@@ -129,11 +132,17 @@ __global__ void tc_pack_kernel(const float* __restrict__ w, uint16_t* __restrict
     const int kb = ci / cb, cc = ci % cb;
     const int chunk = cc >> 3, e = cc & 7;
     const long long blk = ((long long)(tap * ntiles + nt) * nblk + kb) * (2LL * cb * bn);
-    const long long off = ((long long)chunk * bn + n) * 8 + e;
     __nv_bfloat16 hi, lo;
     split_bf16(w[i], hi, lo);
-    wpk[blk + off] = __bfloat16_as_ushort(hi);
-    wpk[blk + (long long)cb * bn + off] = __bfloat16_as_ushort(lo);
+    if (tc_stacked(bn)) {
+      const long long off = ((long long)chunk * 2 * bn + n) * 8 + e;
+      wpk[blk + off] = __bfloat16_as_ushort(hi);
+      wpk[blk + off + (long long)bn * 8] = __bfloat16_as_ushort(lo);
+    } else {
+      const long long off = ((long long)chunk * bn + n) * 8 + e;
+      wpk[blk + off] = __bfloat16_as_ushort(hi);
+      wpk[blk + (long long)cb * bn + off] = __bfloat16_as_ushort(lo);
+    }
   }
 }
 

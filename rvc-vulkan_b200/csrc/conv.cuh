@@ -92,6 +92,9 @@ size_t tc_packed_elems(int taps, int C_in, int C_out, int bn, int cb);
 void launch_tc_pack(const float* w, uint16_t* wpk, int taps, int C_in, int C_out, int bn, int cb,
                     cudaStream_t st);
 bool tc_shape_ok(int C_in, int C_out);
+// Narrow N tiles issue A_hi.[B_hi | B_lo] as one N = 2*bn MMA plus A_lo.B_hi
+// (two MMAs per k step instead of three); the packed weight layout follows.
+__host__ __device__ __forceinline__ bool tc_stacked(int bn) { return bn <= 64; }
 int tc_pick_bn(int C_out);
 int tc_pick_cb(int C_in);
 

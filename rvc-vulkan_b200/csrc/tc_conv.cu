@@ -133,15 +133,56 @@ __device__ __forceinline__ void issue_stage(uint32_t dbase, uint64_t dah0, uint6
   for (int kk = 0; kk < KK; ++kk) {
     const uint64_t ka = (uint64_t)((2u * (uint32_t)kk * lbo_a) >> 4);
     const uint64_t kb = (uint64_t)((2u * (uint32_t)kk * lbo_b) >> 4);
+    // products grouped across subtiles: an MMA's accumulator was last written
+    // MSUB instructions earlier (sa: 128 rows x 16 B, >> 4)
 #pragma unroll
-    for (int sub = 0; sub < MSUB; ++sub) {
-      const uint64_t sa = (uint64_t)(sub * kTM);  // 128 rows x 16 B, >> 4
-      const uint32_t d = dbase + (uint32_t)(sub * bn);
-      ptx::mma_bf16(d, dah0 + ka + sa, dbh0 + kb, idesc, (first && kk == 0) ? 0u : 1u);
-      ptx::mma_bf16(d, dah0 + ka + sa, dbl0 + kb, idesc, 1u);
-      ptx::mma_bf16(d, dal0 + ka + sa, dbh0 + kb, idesc, 1u);
-    }
+    for (int sub = 0; sub < MSUB; ++sub)
+      ptx::mma_bf16(dbase + (uint32_t)(sub * bn), dah0 + ka + (uint64_t)(sub * kTM), dbh0 + kb, idesc,
+                    (first && kk == 0) ? 0u : 1u);
+#pragma unroll
+    for (int sub = 0; sub < MSUB; ++sub)
+      ptx::mma_bf16(dbase + (uint32_t)(sub * bn), dah0 + ka + (uint64_t)(sub * kTM), dbl0 + kb, idesc, 1u);
+#pragma unroll
+    for (int sub = 0; sub < MSUB; ++sub)
+      ptx::mma_bf16(dbase + (uint32_t)(sub * bn), dal0 + ka + (uint64_t)(sub * kTM), dbh0 + kb, idesc, 1u);
   }
+}
+
+// Stacked form: per 16-wide k step and subtile, D[0:2bn) += Ahi.[Bhi|Blo] (one
+// N = 2bn MMA) and D[0:bn) += Alo.Bhi; the epilogue adds D[bn:2bn) to D[0:bn).
+template <int MSUB, int KK>
+__device__ __forceinline__ void issue_stacked(uint32_t dbase, uint64_t dah0, uint64_t dal0, uint64_t db0,
+                                              uint32_t lbo_a, uint32_t lbo_b, int bn, uint32_t idesc2,
+                                              uint32_t idesc1, bool first) {
+#pragma unroll
+  for (int kk = 0; kk < KK; ++kk) {
+    const uint64_t ka = (uint64_t)((2u * (uint32_t)kk * lbo_a) >> 4);
+    const uint64_t kb = (uint64_t)((2u * (uint32_t)kk * lbo_b) >> 4);
+    // the subtiles' MMAs interleave, so consecutive MMAs never accumulate into
+    // the same TMEM columns (the accumulation chain of one subtile advances
+    // every MSUB instructions)
+#pragma unroll
+    for (int sub = 0; sub < MSUB; ++sub)
+      ptx::mma_bf16(dbase + (uint32_t)(sub * 2 * bn), dah0 + ka + (uint64_t)(sub * kTM), db0 + kb, idesc2,
+                    (first && kk == 0) ? 0u : 1u);
+#pragma unroll
+    for (int sub = 0; sub < MSUB; ++sub)
+      ptx::mma_bf16(dbase + (uint32_t)(sub * 2 * bn), dal0 + ka + (uint64_t)(sub * kTM), db0 + kb, idesc1, 1u);
+  }
+}
+
+__device__ __forceinline__ void issue_stacked_any(int msub, int kk, uint32_t dbase, uint64_t dah0, uint64_t dal0,
+                                                  uint64_t db0, uint32_t lbo_a, uint32_t lbo_b, int bn,
+                                                  uint32_t idesc2, uint32_t idesc1, bool first) {
+#define RVC_ISSUE_S(M, K)                                                                  \
+  if (msub == M && kk == K) {                                                              \
+    issue_stacked<M, K>(dbase, dah0, dal0, db0, lbo_a, lbo_b, bn, idesc2, idesc1, first); \
+    return;                                                                                \
+  }
+  RVC_ISSUE_S(1, 1) RVC_ISSUE_S(1, 2) RVC_ISSUE_S(1, 3) RVC_ISSUE_S(1, 4)
+  RVC_ISSUE_S(2, 1) RVC_ISSUE_S(2, 2) RVC_ISSUE_S(2, 3) RVC_ISSUE_S(2, 4)
+  RVC_ISSUE_S(4, 1) RVC_ISSUE_S(4, 2) RVC_ISSUE_S(4, 3) RVC_ISSUE_S(4, 4)
+#undef RVC_ISSUE_S
 }
 
 __device__ __forceinline__ void issue_any(int msub, int kk, uint32_t dbase, uint64_t dah0, uint64_t dal0,
@@ -210,7 +251,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nblk = a.C_in / CB;
   const int MT = g.msub * kTM;
   const uint32_t LBO_A = (uint32_t)g.arows_pad * 16u;
-  const uint32_t LBO_B = (uint32_t)BN * 16u;
+  const bool STK = tc_stacked(BN);
+  const int ACW = STK ? 2 * BN : BN;  // TMEM columns per 128-row subtile
+  const uint32_t LBO_B = (uint32_t)(STK ? 2 * BN : BN) * 16u;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t sbase = ptx::smem_u32(smem);
   const uint32_t bar0 = sbase + g.off_bar;
@@ -296,6 +339,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
       const uint32_t idesc = ptx::idesc_bf16_f32(kTM, BN);
+      const uint32_t idesc2 = ptx::idesc_bf16_f32(kTM, 2 * BN);
       int ks = 0, ab = 0, it = 0;
       bool ok = true;
       if (g.w_res && !ptx::mbar_wait(W_FULL, 0, kWaitNs)) {
@@ -313,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         ptx::tc_fence_after();
-        const uint32_t dbase = tmem + (uint32_t)(set * g.msub * BN);
+        const uint32_t dbase = tmem + (uint32_t)(set * g.msub * ACW);
         const int span = (S.ntaps - 1) * S.tap_step;
         const int shift = span < 0 ? -span : 0;
         bool first = true;
@@ -344,8 +388,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t dah0 = ptx::smem_desc(a_plane(buf, 0) + rowoff * 16u, LBO_A, 128);
             const uint64_t dal0 = ptx::smem_desc(a_plane(buf, 1) + rowoff * 16u, LBO_A, 128);
             const uint64_t dbh0 = ptx::smem_desc(bhi, LBO_B, 128);
-            const uint64_t dbl0 = ptx::smem_desc(blo, LBO_B, 128);
-            issue_any(g.msub, CB / 16, dbase, dah0, dal0, dbh0, dbl0, LBO_A, LBO_B, BN, idesc, first);
+            if (STK) {
+              issue_stacked_any(g.msub, CB / 16, dbase, dah0, dal0, dbh0, LBO_A, LBO_B, BN, idesc2, idesc, first);
+            } else {
+              const uint64_t dbl0 = ptx::smem_desc(blo, LBO_B, 128);
+              issue_any(g.msub, CB / 16, dbase, dah0, dal0, dbh0, dbl0, LBO_A, LBO_B, BN, idesc, first);
+            }
             first = false;
             if (!g.w_res) ptx::mma_commit(B_EMPTY + 8 * st);
           }
@@ -525,14 +573,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         ptx::tc_fence_after();
-        const uint32_t dbase = tmem + (uint32_t)(set * g.msub * BN) + ((uint32_t)(wq * 32) << 16);
+        const uint32_t dbase = tmem + (uint32_t)(set * g.msub * ACW) + ((uint32_t)(wq * 32) << 16);
         for (int q = 0; q < spt; ++q, ++e) {
           if (wlead) issue(e + pdist);
           const int sl = e % g.nslot;
           const int sub = q / nch, ch = q % nch;
           const bool in = __all_sync(0xffffffffu, ptx::mbar_wait(epi_bar(sl), (e / g.nslot) & 1, kWaitNs));
           float v[32];
-          ptx::tmem_ld32(dbase + (uint32_t)(sub * BN + ch * kEpiCols), v);
+          ptx::tmem_ld32(dbase + (uint32_t)(sub * ACW + ch * kEpiCols), v);
+          if (STK) {  // add the Ahi.Blo half, 16 columns at a time
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              float w2[16];
+              ptx::tmem_ld16(dbase + (uint32_t)(sub * ACW + BN + ch * kEpiCols + 16 * h), w2);
+#pragma unroll
+              for (int k = 0; k < 16; ++k) v[16 * h + k] += w2[k];
+            }
+          }
           if (q == spt - 1) {
             ptx::tc_fence_before();
             ptx::mbar_arrive(ACC_EMPTY + 8 * set);
@@ -630,7 +687,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         ptx::tc_fence_after();
-        const uint32_t dbase = tmem + (uint32_t)(set * g.msub * BN) + ((uint32_t)(wq * 32) << 16);
+        const uint32_t dbase = tmem + (uint32_t)(set * g.msub * ACW) + ((uint32_t)(wq * 32) << 16);
         for (int sub = 0; sub < g.msub; ++sub) {
           const int row = t0 + sub * kTM + r_in;
           const bool valid = row < S.rows;
@@ -638,12 +695,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           int col = 0;
           for (; col + 32 <= BN; col += 32) {
             float v[32];
-            ptx::tmem_ld32(dbase + (uint32_t)(sub * BN + col), v);
+            ptx::tmem_ld32(dbase + (uint32_t)(sub * ACW + col), v);
+            if (STK) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                float w2[16];
+                ptx::tmem_ld16(dbase + (uint32_t)(sub * ACW + BN + col + 16 * h), w2);
+#pragma unroll
+                for (int k = 0; k < 16; ++k) v[16 * h + k] += w2[k];
+              }
+            }
             if (valid) epi_direct<32>(a, c.b, prow, S.co_off + c.nt * BN + col, v, g.vec);
           }
           if (col < BN) {
             float v[16];
-            ptx::tmem_ld16(dbase + (uint32_t)(sub * BN + col), v);
+            ptx::tmem_ld16(dbase + (uint32_t)(sub * ACW + col), v);
+            if (STK) {
+              float w2[16];
+              ptx::tmem_ld16(dbase + (uint32_t)(sub * ACW + BN + col), w2);
+#pragma unroll
+              for (int k = 0; k < 16; ++k) v[k] += w2[k];
+            }
             if (valid) epi_direct<16>(a, c.b, prow, S.co_off + c.nt * BN + col, v, g.vec);
           }
         }
@@ -777,7 +849,8 @@ static TcPlan tc_plan(const ConvArgs& a) {
   }
   auto try_cand = [&](const Cand& cd, int need_stages) -> bool {
     int cols = 32;
-    while (cols < cd.nacc * cd.msub * a.bn) cols <<= 1;
+    const int acw = tc_stacked(a.bn) ? 2 * a.bn : a.bn;
+    while (cols < cd.nacc * cd.msub * acw) cols <<= 1;
     if (cols > 512) return false;
     const int arows = cd.msub * kTM + halo;
     const int pad = arows + ((1 - arows % 8) + 8) % 8;  // == 1 (mod 8): spreads chunk planes over banks
