@@ -160,6 +160,13 @@ int32_t rvc_cuda_synth_infer(int64_t model, int32_t B, int32_t P, const float* p
 int32_t rvc_cuda_synth_infer_device(int64_t model, int32_t B, int32_t P, const float* phone,
                                     const int64_t* pitch, const float* nsff0, const int64_t* sid,
                                     const float* nz, const float* ns, float* wave);
+/* Partial synthesis of one chunk (SynthesizerTrn.infer with skip_head /
+ * return_length, runtime/models/vits.py:2404-2420, :2422-2476, :2539-2548):
+ * inputs as rvc_cuda_synth_infer with B = 1 -> wave[return_length*upp], the
+ * samples of frames [skip_head, skip_head + return_length).  Host buffers. */
+int32_t rvc_cuda_synth_infer_partial(int64_t model, int32_t P, int32_t skip_head, int32_t return_length,
+                                     const float* phone, const int64_t* pitch, const float* nsff0, const int64_t* sid,
+                                     const float* nz, const float* ns, float* wave);
 /* Debug taps: copies the named intermediate of the last infer (e.g.
  * "enc.l5", "flow.z", "dec.s2.out") into out (n floats); RVC_E_ARG if unknown. */
 int32_t rvc_cuda_synth_tap(int64_t model, const char* name, float* out, int64_t n);

@@ -163,7 +163,15 @@ def flow_reverse(w, S: VitsShape, z, g):
     return z
 
 
-def sine_source(w, S: VitsShape, f0, ns):
+def phase_offsets(S: VitsShape, f0):
+    """Full-length per-frame phase carry ``fmod(cumsum(...))`` (``runtime/models/vits.py:2396-2407``)."""
+    f0r = f0[:, None].transpose(0, 2, 1)
+    rad = f0r / S.sr * np.arange(1, S.upp + 1, dtype=F32)[None, None, :]
+    rad2 = np.fmod(rad[..., -1:] + 0.5, 1.0) - 0.5
+    return np.fmod(np.cumsum(rad2, axis=1), 1.0)
+
+
+def sine_source(w, S: VitsShape, f0, ns, off=None):
     """SineGen (harmonic_num 0) + SourceModuleHnNSF, full-length phase path.
 
     ``_GeneratorNSF._sine_gen`` (:1468-1501): per-frame phase ramp
@@ -174,10 +182,13 @@ def sine_source(w, S: VitsShape, f0, ns):
     upp, sr = S.upp, S.sr
     f0r = f0[:, None].transpose(0, 2, 1)                     # [1,P,1]
     rad = f0r / sr * np.arange(1, upp + 1, dtype=F32)[None, None, :]
-    rad2 = np.fmod(rad[..., -1:] + 0.5, 1.0) - 0.5
-    acc = np.fmod(np.cumsum(rad2, axis=1), 1.0)
-    rad = rad.copy()
-    rad[:, 1:, :] += acc[:, :-1, :]
+    if off is None:
+        rad2 = np.fmod(rad[..., -1:] + 0.5, 1.0) - 0.5
+        acc = np.fmod(np.cumsum(rad2, axis=1), 1.0)
+        rad = rad.copy()
+        rad[:, 1:, :] += acc[:, :-1, :]
+    else:  # segment with per-frame total phase offsets (:1490-1491)
+        rad = rad + np.asarray(off, dtype=F32)
     rad = rad.reshape(1, -1, 1)
     sine = np.sin(2 * np.pi * rad) * 0.1
     uv = np.repeat((f0r > 0).astype(F32), upp, axis=1)
@@ -202,10 +213,10 @@ def _resblock(w, base, x, k):
     return x
 
 
-def generator(w, S: VitsShape, z, f0, g, ns, taps=None):
+def generator(w, S: VitsShape, z, f0, g, ns, taps=None, off=None):
     """``_GeneratorNSF.forward`` numpy branch (:2133-2231) and the per-stage
     ``_dec_ups_single`` (:1616-1636).  Returns the waveform ``[1,1,P*upp]``."""
-    har = sine_source(w, S, f0, ns)
+    har = sine_source(w, S, f0, ns, off)
     _tap(taps, "dec.har", har[0, 0])
     x = ops.conv1d(z, w["dec.conv_pre.weight"], w["dec.conv_pre.bias"], padding=3)
     x = x + ops.conv1d(g, w["dec.cond.weight"], w["dec.cond.bias"])
@@ -241,3 +252,34 @@ def synth(w, cfg, phone, pitch, nsff0, sid, nz, ns, taps=None):
     z = flow_reverse(w, S, z_p, g)
     _tap(taps, "flow.z", z[0].T)
     return generator(w, S, z, nsff0, g, ns, taps)
+
+
+FLOW_PAD, DEC_PAD = 24, 16  # runtime/models/vits.py:148-152
+
+
+def synth_partial(w, cfg, phone, pitch, nsff0, sid, nz, ns, head, length):
+    """``SynthesizerTrn._infer_partial`` (:2539-2548) with ``_partial_prep``
+    (:2422-2476): full text encoder, flow from ``max(head-24-16, 0)``, generator
+    on frames ``[max(head-16,0), min(P, head+length+16))`` with phase offsets,
+    output samples of frames ``[head, head+length)``."""
+    S = VitsShape(w, cfg)
+    P = phone.shape[1]
+    upp = S.upp
+    g = ops.embedding(sid, w["emb_g.weight"])[0].reshape(1, -1, 1)
+    m, logs = text_encoder(w, S, phone, pitch)
+    fh = max(head - FLOW_PAD - DEC_PAD, 0)
+    z_p = m[:, :, fh:] + np.exp(logs[:, :, fh:]) * nz[:, :, fh:] * 0.66666
+    z = flow_reverse(w, S, z_p, g)
+    zs, ze = max(head - DEC_PAD, 0), min(P, head + length + DEC_PAD)
+    z_seg = z[:, :, zs - fh:ze - fh]
+    acc = phase_offsets(S, nsff0)
+    n = ze - zs
+    if zs == 0:
+        off = np.zeros((1, n, 1), dtype=F32)
+        if n > 1:
+            off[:, 1:, :] = acc[:, :n - 1, :]
+    else:
+        off = acc[:, zs - 1:zs - 1 + n, :]
+    o = generator(w, S, z_seg, nsff0[:, zs:ze], g, ns[:, zs * upp:ze * upp, :], off=off)
+    s0 = (head - zs) * upp
+    return o[:, :, s0:s0 + length * upp]

@@ -591,6 +591,33 @@ int32_t rvc_cuda_synth_infer_device(int64_t model, int32_t B, int32_t P, const f
   });
 }
 
+int32_t rvc_cuda_synth_infer_partial(int64_t model, int32_t P, int32_t skip_head, int32_t return_length,
+                                     const float* phone, const int64_t* pitch, const float* nsff0, const int64_t* sid,
+                                     const float* nz, const float* ns, float* wave) {
+  return on_synth(model, [&](SynthModel* m) {
+    RVC_CHECK_ARG(P >= 1 && skip_head >= 0 && skip_head < P && return_length >= 1 && skip_head + return_length <= P,
+                  "synth_infer_partial: skip_head/return_length out of range");
+    for (int64_t i = 0; i < P; ++i)
+      RVC_CHECK_ARG(pitch[i] >= -256 && pitch[i] < 256, "synth_infer_partial: pitch id out of [0,256)");
+    RVC_CHECK_ARG(sid[0] >= -m->cfg.n_spk && sid[0] < m->cfg.n_spk, "synth_infer_partial: speaker id out of range");
+    const int H = m->cfg.hidden, upp = m->cfg.upp();
+    const int Dp = m->cfg.phone_dim;
+    DevBuf dph(m->ctx, sizeof(float) * (size_t)P * Dp), dpi(m->ctx, sizeof(int64_t) * P), df0(m->ctx, sizeof(float) * P),
+        dsid(m->ctx, sizeof(int64_t)), dnz(m->ctx, sizeof(float) * (size_t)H * P),
+        dns(m->ctx, sizeof(float) * (size_t)P * upp), dw(m->ctx, sizeof(float) * (size_t)return_length * upp);
+    h2d(m->ctx, dph.p, phone, dph.bytes);
+    h2d(m->ctx, dpi.p, pitch, dpi.bytes);
+    h2d(m->ctx, df0.p, nsff0, df0.bytes);
+    h2d(m->ctx, dsid.p, sid, dsid.bytes);
+    h2d(m->ctx, dnz.p, nz, dnz.bytes);
+    h2d(m->ctx, dns.p, ns, dns.bytes);
+    m->infer_partial_device(P, skip_head, return_length, dph.f(), dpi.as<long long>(), df0.f(),
+                            dsid.as<long long>(), dnz.f(), dns.f(), dw.f());
+    d2h(m->ctx, wave, dw.p, dw.bytes);
+    finish(m->ctx);
+  });
+}
+
 int32_t rvc_cuda_synth_tap(int64_t model, const char* name, float* out, int64_t n) {
   return on_synth(model, [&](SynthModel* m) {
     if (!m->tap(name, out, n)) throw Error{kErrArg, std::string("synth_tap: no tap '") + name + "' of that size"};

@@ -217,20 +217,17 @@ static ConvIO io_rows(const float* x, int ld, int T, float* y, int y_ld, int B, 
   return io;
 }
 
-void SynthModel::infer_device(int B, int P, const float* phone, const long long* pitch, const float* nsff0,
-                              const long long* sid, const float* nz, const float* ns, float* wave) {
-  if (!finalized_) throw Error{kErrState, "synth: finalize() not called after the last weight upload"};
-  RVC_CHECK_ARG(B >= 1 && P >= 1, "synth: B and P must be positive");
-  ensure_ws(B, P);
+// enc_p + speaker conditioning + z_p = m + exp(logs) * nz * 0.66666 into buf("z").
+void SynthModel::enc_stage(int B, int P, const float* phone, const long long* pitch, const long long* sid,
+                           const float* nz) {
   cudaStream_t st = ctx->stream;
-  const int H = cfg.hidden, F = cfg.filter, upp = cfg.upp();
+  const int H = cfg.hidden, F = cfg.filter;
   const long long PH = (long long)P * H;
-  taps_.clear();
   // speaker conditioning g = emb_g(sid); dec.cond(g); flow cond layers
   k_embedding(sid, B, W("emb_g.weight").buf.f(), (int)W("emb_g.weight").shape[0], cfg.gin, buf("gvec"), st);
   k_gemv_rows(W("dec.cond.weight").buf.f(), W("dec.cond.bias").buf.f(), buf("gvec"), B, cfg.up0, cfg.gin,
               buf("dcond"), st);
-  const char* fc[4] = {"fcond0", "fcond1", "fcond2", "fcond3"};
+  static const char* fc[4] = {"fcond0", "fcond1", "fcond2", "fcond3"};
   for (int fi = 0; fi < 4; ++fi)
     k_gemv_rows(flow_cond_w_[fi].f(), flow_cond_b_[fi].f(), buf("gvec"), B, 6 * H, cfg.gin, buf(fc[fi]), st);
 
@@ -266,11 +263,18 @@ void SynthModel::infer_device(int B, int P, const float* phone, const long long*
     save_tap("enc.l" + std::to_string(i), ex, (long long)B * PH);
   }
   run_conv(proj_, io_rows(ex, H, P, buf("stats"), 2 * H, B, PH, 2 * PH));
-  float* z = buf("z");
-  float* zf = buf("zf");
-  k_zp(buf("stats"), nz, B, P, H, z, st);
-  save_tap("enc.zp", z, (long long)B * PH);
+  k_zp(buf("stats"), nz, B, P, H, buf("z"), st);
+  save_tap("enc.zp", buf("z"), (long long)B * PH);
 
+}
+
+// Flow reverse over P frames of z (rows of H channels, batch stride P*H); zf is
+// scratch of the same size.  Returns the buffer holding the result.
+float* SynthModel::flow_stage(int B, int P, float* z, float* zf) {
+  cudaStream_t st = ctx->stream;
+  const int H = cfg.hidden;
+  const long long PH = (long long)P * H;
+  static const char* fc[4] = {"fcond0", "fcond1", "fcond2", "fcond3"};
   // ---------------- flow reverse: Flip, RC(6), Flip, RC(4), Flip, RC(2), Flip, RC(0)
   for (int fi = 3; fi >= 0; --fi) {
     k_flip_channels(z, zf, (long long)B * P, H, st);
@@ -293,12 +297,18 @@ void SynthModel::infer_device(int B, int P, const float* phone, const long long*
     run_conv(post_[fi], pm);
     std::swap(z, zf);
   }
-  save_tap("flow.z", z, (long long)B * PH);
+  return z;
+}
 
+// GeneratorNSF over P frames of z (batch stride z_bs) with the harmonic source
+// har (har_len samples per chunk, batch stride har_bs) -> wave [B][P*upp].
+void SynthModel::dec_stage(int B, int P, const float* z, long long z_bs, const float* har, long long har_bs,
+                           int har_len, float* wave) {
+  cudaStream_t st = ctx->stream;
+  const int H = cfg.hidden, upp = cfg.upp();
+  const long long PH = z_bs;
   // ---------------- GeneratorNSF
   const long long N = (long long)P * upp;
-  k_sine_source(nsff0, ns, B, P, upp, cfg.sr, lin_w_, lin_b_, buf("phase"), buf("har"), st);
-  save_tap("dec.har", buf("har"), (long long)B * N);
   long long dmax = ws_.at("xo").bytes / sizeof(float) / ws_B;
   float *xo = buf("xo"), *x0 = buf("x0"), *r = buf("r"), *t = buf("t"), *s = buf("s");
   {
@@ -318,7 +328,7 @@ void SynthModel::infer_device(int B, int P, const float* phone, const long long*
       a.in_slope = 0.1f;
       // x = ups(x) + noise_conv(har): the noise conv (bias included) runs first
       // and enters the transposed conv's epilogue as its residual term.
-      k_noise_conv(buf("har"), N, (int)N, W("dec.noise_convs." + std::to_string(i) + ".weight").buf.f(),
+      k_noise_conv(har, har_bs, har_len, W("dec.noise_convs." + std::to_string(i) + ".weight").buf.f(),
                    W("dec.noise_convs." + std::to_string(i) + ".bias").buf.f(), C, noise_k_[i], noise_s_[i],
                    noise_s_[i] / 2, B, Ln, buf("noise"), dmax, st);
       a.res = buf("noise");
@@ -361,6 +371,59 @@ void SynthModel::infer_device(int B, int P, const float* phone, const long long*
   const int Cl = cfg.up0 >> cfg.n_ups;
   k_conv_post_tanh(xo, dmax, B, Lc, Cl, W("dec.conv_post.weight").buf.f(), 7, 3, 0.01f, wave, st);
   save_tap("dec.wave", wave, (long long)B * N);
+}
+
+void SynthModel::infer_device(int B, int P, const float* phone, const long long* pitch, const float* nsff0,
+                              const long long* sid, const float* nz, const float* ns, float* wave) {
+  if (!finalized_) throw Error{kErrState, "synth: finalize() not called after the last weight upload"};
+  RVC_CHECK_ARG(B >= 1 && P >= 1, "synth: B and P must be positive");
+  ensure_ws(B, P);
+  cudaStream_t st = ctx->stream;
+  const int H = cfg.hidden, upp = cfg.upp();
+  const long long PH = (long long)P * H, N = (long long)P * upp;
+  taps_.clear();
+  enc_stage(B, P, phone, pitch, sid, nz);
+  float* z = flow_stage(B, P, buf("z"), buf("zf"));
+  save_tap("flow.z", z, (long long)B * PH);
+  k_sine_source(nsff0, ns, B, P, upp, cfg.sr, lin_w_, lin_b_, buf("phase"), buf("har"), st);
+  save_tap("dec.har", buf("har"), (long long)B * N);
+  dec_stage(B, P, z, PH, buf("har"), N, (int)N, wave);
+}
+
+// Partial synthesis of one chunk (runtime/models/vits.py:2404-2420, :2422-2476,
+// :2539-2548): the text encoder over all P frames; the flow from
+// flow_head = max(head - 24 - 16, 0); the generator over frames
+// [zs, ze) = [max(head - 16, 0), min(P, head + length + 16)) with the harmonic
+// source of those frames taken from the full-length source (its phase is the
+// full-length phase at each absolute frame, which is what the reference's
+// per-segment phase offsets reproduce); output samples [(head - zs) * upp,
+// + length * upp) of that segment.
+void SynthModel::infer_partial_device(int P, int head, int length, const float* phone, const long long* pitch,
+                                      const float* nsff0, const long long* sid, const float* nz, const float* ns,
+                                      float* wave) {
+  if (!finalized_) throw Error{kErrState, "synth: finalize() not called after the last weight upload"};
+  RVC_CHECK_ARG(P >= 1 && head >= 0 && head < P && length >= 1 && head + length <= P,
+                "synth: skip_head/return_length out of range");
+  ensure_ws(1, P);
+  cudaStream_t st = ctx->stream;
+  const int H = cfg.hidden, upp = cfg.upp();
+  const long long N = (long long)P * upp;
+  constexpr int kFlowPad = 24, kDecPad = 16;
+  taps_.clear();
+  enc_stage(1, P, phone, pitch, sid, nz);
+  const int flow_head = std::max(head - kFlowPad - kDecPad, 0);
+  float* z = flow_stage(1, P - flow_head, buf("z") + (size_t)flow_head * H, buf("zf") + (size_t)flow_head * H);
+  k_sine_source(nsff0, ns, 1, P, upp, cfg.sr, lin_w_, lin_b_, buf("phase"), buf("har"), st);
+  const int zs = std::max(head - kDecPad, 0), ze = std::min(P, head + length + kDecPad);
+  const int nseg = ze - zs;
+  // z rows are absolute frames offset by flow_head; the segment starts at frame zs
+  const float* zseg = z + (size_t)(zs - flow_head) * H;
+  float* wseg = buf("out_wave");
+  dec_stage(1, nseg, zseg, (long long)nseg * H, buf("har") + (size_t)zs * upp, (long long)nseg * upp, nseg * upp,
+            wseg);
+  RVC_CUDA_TRY(cudaMemcpyAsync(wave, wseg + (size_t)(head - zs) * upp, sizeof(float) * (size_t)length * upp,
+                               cudaMemcpyDeviceToDevice, st));
+  (void)N;
 }
 
 void SynthModel::infer_host(int B, int P, const float* phone, const long long* pitch, const float* nsff0,

@@ -44,6 +44,10 @@ class SynthModel {
                     const long long* sid, const float* nz, const float* ns, float* wave);
   void infer_host(int B, int P, const float* phone, const long long* pitch, const float* nsff0,
                   const long long* sid, const float* nz, const float* ns, float* wave);
+  // Partial synthesis of one chunk: wave [length * upp] for frames [head, head + length).
+  void infer_partial_device(int P, int head, int length, const float* phone, const long long* pitch,
+                            const float* nsff0, const long long* sid, const float* nz, const float* ns,
+                            float* wave);
   bool tap(const std::string& name, float* host, int64_t n);
   bool keep_taps = false;
   Context* ctx;
@@ -55,6 +59,10 @@ class SynthModel {
   void ensure_ws(int B, int P);
   void save_tap(const std::string& name, const float* d, int64_t n);
   void run_conv(const ConvLayer& L, const ConvIO& io);
+  void enc_stage(int B, int P, const float* phone, const long long* pitch, const long long* sid, const float* nz);
+  float* flow_stage(int B, int P, float* z, float* zf);
+  void dec_stage(int B, int P, const float* z, long long z_bs, const float* har, long long har_bs, int har_len,
+                 float* wave);
   bool finalized_ = false;
   std::unordered_map<std::string, RawTensor> raw_;
   // enc

@@ -161,11 +161,30 @@ class CudaSynthesizer:
     def infer(self, phone, pitch, nsff0, sid, seed=None, skip_head=None, return_length=None, phone_gpu=None,
               _defer: bool = False):
         """``SynthesizerTrn.infer`` (full synthesis; ``runtime/models/vits.py:2352``)."""
-        if skip_head is not None and return_length is not None:
-            raise NotImplementedError("partial synthesis (skip_head/return_length) is not on the CUDA path yet")
         P = np.asarray(phone).shape[1]
         nz, ns = self.make_noise(P, seed)
+        if skip_head is not None and return_length is not None:
+            return self.infer_partial(phone, pitch, nsff0, sid, nz, ns, int(skip_head), int(return_length))
         return self.infer_controlled(phone, pitch, nsff0, sid, nz, ns, _defer=_defer)
+
+    def infer_partial(self, phone, pitch, nsff0, sid, nz, ns, skip_head: int, return_length: int) -> np.ndarray:
+        """Partial synthesis (``SynthesizerTrn._infer_partial``, ``runtime/models/vits.py:2539-2548``):
+        ``[1,1,upp*return_length]``, the samples of frames ``[skip_head, skip_head+return_length)``."""
+        phone = np.ascontiguousarray(np.asarray(phone, dtype=np.float32))
+        if phone.ndim != 3 or phone.shape[0] != 1:
+            raise ValueError(f"phone must be [1,P,D], got {phone.shape}")
+        P = phone.shape[1]
+        if skip_head < 0 or skip_head >= P or return_length <= 0 or skip_head + return_length > P:
+            raise ValueError(f"skip_head/return_length out of range: P={P}, head={skip_head}, length={return_length}")
+        pitch = np.ascontiguousarray(np.asarray(pitch).reshape(P), dtype=np.int64)
+        nsff0 = np.ascontiguousarray(np.asarray(nsff0).reshape(P), dtype=np.float32)
+        sid = np.ascontiguousarray(np.asarray(sid).reshape(1), dtype=np.int64)
+        nz = np.ascontiguousarray(np.asarray(nz, dtype=np.float32).reshape(self.hidden, P))
+        ns = np.ascontiguousarray(np.asarray(ns, dtype=np.float32).reshape(P * self.upp))
+        out = np.empty(return_length * self.upp, np.float32)
+        check(lib.rvc_cuda_synth_infer_partial(self.handle, P, skip_head, return_length, fptr(phone), iptr(pitch),
+                                               fptr(nsff0), iptr(sid), fptr(nz), fptr(ns), fptr(out)))
+        return out.reshape(1, 1, -1)
 
     # ---------------------------------------------------------------- debug
     def keep_taps(self, on: bool = True):
@@ -179,7 +198,8 @@ class CudaSynthesizer:
 
 def patch_reference(vits_module=None, device: Optional[int] = None, precision: str = "bf16x3"):
     """Route ``SynthesizerTrn.infer_controlled`` (and thus ``infer`` for full
-    synthesis) of the reference through ``CudaSynthesizer``.
+    synthesis) and ``_infer_partial`` (``infer`` with skip_head/return_length)
+    of the reference through ``CudaSynthesizer``.
 
     The class methods are replaced, not the loader, because ``runtime/vc.py``
     imports the loaders by name.  A device model is built once per
@@ -199,7 +219,17 @@ def patch_reference(vits_module=None, device: Optional[int] = None, precision: s
             self.__dict__["_rvc_cuda_model"] = m
         return m.infer_controlled(phone, pitch, nsff0, sid, nz, ns, _defer=_defer)
 
+    def _infer_partial(self, phone, pitch, nsff0, sid, nz, ns, head, length, phone_gpu=None):
+        m = self.__dict__.get("_rvc_cuda_model")
+        if m is None:
+            m = CudaSynthesizer.from_reference(self, device=device, precision=precision)
+            self.__dict__["_rvc_cuda_model"] = m
+        return m.infer_partial(phone, pitch, nsff0, sid, nz, ns, int(head), int(length))
+
     cls._rvc_cuda_orig_infer_controlled = cls.infer_controlled
     cls.infer_controlled = infer_controlled
+    if hasattr(cls, "_infer_partial"):  # SynthesizerTrn.infer's skip_head path (vits.py:2416-2420)
+        cls._rvc_cuda_orig_infer_partial = cls._infer_partial
+        cls._infer_partial = _infer_partial
     cls._rvc_cuda_patched = True
     return cls

@@ -59,6 +59,12 @@ HUBERT_CASES = [
     ("hubert_t8000", 8000, 0, 1),
     ("hubert_t3201", 3201, 0, 2),           # odd length: ragged conv strides
 ]
+# partial synthesis (infer with skip_head / return_length):
+# (name, sr, P, weight seed, input seed, noise seed, head, length)
+PARTIAL_CASES = [
+    ("vits40k_p96_part", 40000, 96, 0, 4, 14, 50, 20),   # interior segment, flow from frame 10
+    ("vits48k_p40_part", 48000, 40, 1, 5, 15, 5, 30),    # head < pads: segment starts at 0
+]
 # (name, T samples, weight seed, input seed)
 RMVPE_CASES = [
     ("rmvpe_t16000", 16000, 0, 1),          # 101 frames -> U-Net on 128
@@ -127,6 +133,22 @@ def run_hubert(runtime_hubert, name, T, wseed, iseed, meta):
                         out_v1=np.asarray(out1[0], np.float32))
     meta[name] = {"kind": "hubert", "T": T, "weight_seed": wseed, "input_seed": iseed,
                   "weights_sha256": weights_digest(sd), "inputs_sha256": digest([x])}
+
+
+def run_partial(runtime_vits, name, sr, P, wseed, iseed, nseed, head, length, meta):
+    """``SynthesizerTrn._infer_partial`` (the skip_head path of ``infer``) on seeded inputs."""
+    w = syn.make_vits_weights(sr, wseed)
+    cfg = syn.vits_config_array(sr)
+    phone, pitch, nsff0, sid = syn.make_vits_inputs(P, iseed)
+    upp = int(np.prod(cfg[12]))
+    nz, ns = syn.make_vits_noise(P, upp, nseed)
+    runtime_vits._load_ckpt = lambda path: {"weight": w, "config": cfg}
+    m = runtime_vits.SynthesizerTrn("synthetic.pth")
+    wav = m._infer_partial(phone, pitch, nsff0, sid, nz, ns, head, length)
+    np.savez_compressed(os.path.join(HERE, name + ".npz"), wave=np.asarray(wav, np.float32).reshape(-1))
+    meta[name] = {"kind": "vits_partial", "sr": sr, "P": P, "upp": upp, "weight_seed": wseed, "input_seed": iseed,
+                  "noise_seed": nseed, "head": head, "length": length, "weights_sha256": weights_digest(w),
+                  "inputs_sha256": digest([phone, pitch, nsff0, sid, nz, ns])}
 
 
 def run_rmvpe(runtime_rmvpe, name, T, wseed, iseed, meta):
@@ -211,7 +233,7 @@ def run_ops(nn, meta):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("RVC_REFERENCE", "/root/reference"))
-    ap.add_argument("--only", choices=["vits", "hubert", "ops", "retrieval", "rmvpe"], default=None,
+    ap.add_argument("--only", choices=["vits", "hubert", "ops", "retrieval", "rmvpe", "partial"], default=None,
                     help="regenerate one family and keep the other fixtures")
     args = ap.parse_args()
     os.environ["RVC_BACKEND"] = "numpy"
@@ -235,6 +257,9 @@ def main():
             run_hubert(runtime_hubert, *c, meta)
     if args.only in (None, "ops"):
         run_ops(nn, meta)
+    if args.only in (None, "partial"):
+        for c in PARTIAL_CASES:
+            run_partial(runtime_vits, *c, meta)
     if args.only in (None, "rmvpe"):
         from runtime.models import rmvpe as runtime_rmvpe  # noqa: PLC0415
         for c in RMVPE_CASES:

@@ -109,3 +109,18 @@ def test_rmvpe_oracle_matches_reference(name, golden_meta):
     assert rel_l2(sal, g["salience"]) < 1e-5
     np.testing.assert_array_equal(np.argmax(sal, axis=1), g["argmax"])
     np.testing.assert_allclose(ORM.decode(sal), g["f0"], rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.parametrize("name", ["vits40k_p96_part", "vits48k_p40_part"])
+def test_partial_synthesis_oracle_matches_reference(name, golden_meta):
+    m = golden_meta[name]
+    w = syn.make_vits_weights(m["sr"], m["weight_seed"])
+    assert weights_digest(w) == m["weights_sha256"]
+    phone, pitch, nsff0, sid = syn.make_vits_inputs(m["P"], m["input_seed"])
+    nz, ns = syn.make_vits_noise(m["P"], m["upp"], m["noise_seed"])
+    assert digest([phone, pitch, nsff0, sid, nz, ns]) == m["inputs_sha256"]
+    wav = OV.synth_partial(w, syn.vits_config_array(m["sr"]), phone, pitch, nsff0, sid, nz, ns, m["head"],
+                           m["length"])
+    g = load_golden(name)
+    assert wav.size == g["wave"].size == m["length"] * m["upp"]
+    assert np.abs(wav.reshape(-1) - g["wave"]).max() < 1e-5

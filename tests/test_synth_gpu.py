@@ -122,3 +122,31 @@ def test_bad_inputs_raise():
         m.infer_controlled(phone, pitch + 300, nsff0, sid, nz, ns)
     with pytest.raises(ValueError):
         m.infer_controlled(phone, pitch, nsff0, np.array([5]), nz, ns)
+
+
+@pytest.mark.parametrize("name", ["vits40k_p96_part", "vits48k_p40_part"])
+def test_partial_synthesis_matches_golden(name, golden_meta):
+    """infer with skip_head / return_length (SynthesizerTrn._infer_partial)."""
+    g = golden_meta[name]
+    w, m = model(g["sr"], g["weight_seed"])
+    phone, pitch, nsff0, sid = syn.make_vits_inputs(g["P"], g["input_seed"])
+    nz, ns = syn.make_vits_noise(g["P"], g["upp"], g["noise_seed"])
+    wav = m.infer_partial(phone, pitch, nsff0, sid, nz, ns, g["head"], g["length"])
+    gold = load_golden(name)
+    assert wav.shape == (1, 1, g["length"] * g["upp"])
+    assert np.abs(wav.reshape(-1) - gold["wave"]).max() <= WAVE_TOL
+
+
+def test_partial_equals_slice_of_full_interior():
+    """Away from the segment edges, partial synthesis equals the full synthesis'
+    samples (the reference's stated property, runtime/models/vits.py:2381-2388)."""
+    w, m = model(40000, 0)
+    P, head, length = 120, 60, 24
+    phone, pitch, nsff0, sid = syn.make_vits_inputs(P, 21)
+    nz, ns = syn.make_vits_noise(P, m.upp, 22)
+    full = m.infer_controlled(phone, pitch, nsff0, sid, nz, ns).reshape(-1)
+    part = m.infer_partial(phone, pitch, nsff0, sid, nz, ns, head, length).reshape(-1)
+    seg = full[head * m.upp:(head + length) * m.upp]
+    assert np.abs(part - seg).max() <= WAVE_TOL
+    with pytest.raises(ValueError):
+        m.infer_partial(phone, pitch, nsff0, sid, nz, ns, P - 4, 8)
