@@ -127,3 +127,22 @@ def test_rmvpe_frames_and_patch_reference():
 
     cls = rmvpe.patch_reference(FakeModule)
     assert cls is FakeRmvpe and FakeRmvpe.infer_from_audio is not FakeRmvpe._rvc_cuda_orig_infer_from_audio
+
+
+def test_synth_patch_reference_replaces_full_and_partial_paths():
+    from rvc_cuda import synth
+
+    class FakeSynth:
+        def infer_controlled(self, *a, **k):
+            return "numpy"
+
+        def _infer_partial(self, *a, **k):
+            return "numpy"
+
+    class FakeModule:
+        SynthesizerTrn = FakeSynth
+
+    cls = synth.patch_reference(FakeModule)
+    assert cls is FakeSynth
+    assert FakeSynth.infer_controlled is not FakeSynth._rvc_cuda_orig_infer_controlled
+    assert FakeSynth._infer_partial is not FakeSynth._rvc_cuda_orig_infer_partial
