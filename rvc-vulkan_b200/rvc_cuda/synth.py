@@ -186,6 +186,47 @@ class CudaSynthesizer:
                                                fptr(nsff0), iptr(sid), fptr(nz), fptr(ns), fptr(out)))
         return out.reshape(1, 1, -1)
 
+    # ---------------------------------------------------------------- batched decode
+    def prep_dec(self, phone, pitch, nsff0, sid, seed=None, skip_head=None, return_length=None, phone_gpu=None):
+        """``SynthesizerTrn.prep_dec`` (``runtime/models/vits.py:2478-2500``): draws the
+        chunk's noise in the reference's order and keeps the inputs for
+        ``decode_batch`` (the whole model runs there, batched on the device)."""
+        phone = np.asarray(phone, dtype=np.float32)
+        P = phone.shape[1]
+        if skip_head is not None and return_length is not None:
+            head, length = int(skip_head), int(return_length)
+            if head < 0 or head >= P or length <= 0 or head + length > P:
+                raise ValueError(f"skip_head/return_length out of range: P={P}, head={head}, length={length}")
+        else:
+            head = length = None
+        nz, ns = self.make_noise(P, seed)
+        return {"phone": phone, "pitch": np.asarray(pitch), "nsff0": np.asarray(nsff0, dtype=np.float32),
+                "sid": np.asarray(sid), "nz": nz, "ns": ns, "head": head, "length": length}
+
+    def decode_batch(self, preps) -> list:
+        """``SynthesizerTrn.decode_batch`` (``runtime/models/vits.py:2502-2536``): one
+        waveform per prep (``[1,1,upp*P]``, or the target segment for partial
+        preps); full-length chunks of equal length share one batched call."""
+        out: list = [None] * len(preps)
+        groups: dict = {}
+        for i, p in enumerate(preps):
+            if p["head"] is not None:
+                out[i] = self.infer_partial(p["phone"], p["pitch"], p["nsff0"], p["sid"], p["nz"], p["ns"],
+                                            p["head"], p["length"])
+            else:
+                groups.setdefault(p["phone"].shape[1], []).append(i)
+        for P, idx in groups.items():
+            ps = [preps[i] for i in idx]
+            waves = self.infer_batch(np.concatenate([p["phone"] for p in ps], axis=0),
+                                     np.stack([p["pitch"].reshape(P) for p in ps]),
+                                     np.stack([p["nsff0"].reshape(P) for p in ps]),
+                                     np.concatenate([p["sid"].reshape(1) for p in ps]),
+                                     np.concatenate([p["nz"].reshape(1, self.hidden, P) for p in ps]),
+                                     np.stack([p["ns"].reshape(-1) for p in ps]))
+            for j, i in enumerate(idx):
+                out[i] = waves[j:j + 1].reshape(1, 1, -1)
+        return out
+
     # ---------------------------------------------------------------- debug
     def keep_taps(self, on: bool = True):
         check(lib.rvc_cuda_synth_keep_taps(self.handle, 1 if on else 0))
@@ -198,8 +239,9 @@ class CudaSynthesizer:
 
 def patch_reference(vits_module=None, device: Optional[int] = None, precision: str = "bf16x3"):
     """Route ``SynthesizerTrn.infer_controlled`` (and thus ``infer`` for full
-    synthesis) and ``_infer_partial`` (``infer`` with skip_head/return_length)
-    of the reference through ``CudaSynthesizer``.
+    synthesis), ``_infer_partial`` (``infer`` with skip_head/return_length) and
+    the pipeline's batched ``prep_dec`` / ``decode_batch`` of the reference
+    through ``CudaSynthesizer``.
 
     The class methods are replaced, not the loader, because ``runtime/vc.py``
     imports the loaders by name.  A device model is built once per
@@ -226,8 +268,26 @@ def patch_reference(vits_module=None, device: Optional[int] = None, precision: s
             self.__dict__["_rvc_cuda_model"] = m
         return m.infer_partial(phone, pitch, nsff0, sid, nz, ns, int(head), int(length))
 
+    def _model(self):
+        m = self.__dict__.get("_rvc_cuda_model")
+        if m is None:
+            m = CudaSynthesizer.from_reference(self, device=device, precision=precision)
+            self.__dict__["_rvc_cuda_model"] = m
+        return m
+
+    def prep_dec(self, phone, pitch, nsff0, sid, seed=None, skip_head=None, return_length=None, phone_gpu=None):
+        return _model(self).prep_dec(phone, pitch, nsff0, sid, seed, skip_head, return_length)
+
+    def decode_batch(self, preps):
+        return _model(self).decode_batch(preps)
+
     cls._rvc_cuda_orig_infer_controlled = cls.infer_controlled
     cls.infer_controlled = infer_controlled
+    if hasattr(cls, "prep_dec") and hasattr(cls, "decode_batch"):  # the pipeline's batched decode path
+        cls._rvc_cuda_orig_prep_dec = cls.prep_dec
+        cls._rvc_cuda_orig_decode_batch = cls.decode_batch
+        cls.prep_dec = prep_dec
+        cls.decode_batch = decode_batch
     if hasattr(cls, "_infer_partial"):  # SynthesizerTrn.infer's skip_head path (vits.py:2416-2420)
         cls._rvc_cuda_orig_infer_partial = cls._infer_partial
         cls._infer_partial = _infer_partial

@@ -139,6 +139,12 @@ def test_synth_patch_reference_replaces_full_and_partial_paths():
         def _infer_partial(self, *a, **k):
             return "numpy"
 
+        def prep_dec(self, *a, **k):
+            return "numpy"
+
+        def decode_batch(self, *a, **k):
+            return "numpy"
+
     class FakeModule:
         SynthesizerTrn = FakeSynth
 
@@ -146,3 +152,5 @@ def test_synth_patch_reference_replaces_full_and_partial_paths():
     assert cls is FakeSynth
     assert FakeSynth.infer_controlled is not FakeSynth._rvc_cuda_orig_infer_controlled
     assert FakeSynth._infer_partial is not FakeSynth._rvc_cuda_orig_infer_partial
+    assert FakeSynth.decode_batch is not FakeSynth._rvc_cuda_orig_decode_batch
+    assert FakeSynth.prep_dec is not FakeSynth._rvc_cuda_orig_prep_dec
