@@ -255,6 +255,35 @@ int32_t rvc_cuda_index_blend(int64_t index, const float* q, int64_t F, int32_t D
 int32_t rvc_cuda_index_blend_device(int64_t index, const float* q, int64_t F, int32_t D, int32_t k, int32_t mode,
                                     double index_rate, const float* feats, float* out);
 
+/* ---------------------------------------------------------------- pipeline DSP
+ * The signal-processing steps of Pipeline.pipeline / _vc_prepare run on the
+ * device (host pointers, synchronous). */
+/* scipy.signal.filtfilt(b, a, x) with padtype 'odd' (padlen 3*max(na, nb)),
+ * float64 out; the 48 Hz high-pass of runtime/pipeline.py:49, :765.  x holds
+ * float32 samples when x_f32 != 0 (the odd extension is then formed in
+ * float32, as scipy does for a float32 signal), else float64. */
+int32_t rvc_cuda_filtfilt(int64_t ctx, const double* b, int32_t nb, const double* a, int32_t na, const void* x,
+                          int32_t x_f32, int64_t n, double* y);
+/* Silence split (runtime/pipeline.py:767-790): for t = step, 2*step, ... < n,
+ * the first argmin of the 160-sample absolute sums of the reflect-padded audio
+ * over [max(0, t - t_query), min(n, t + t_query)); -1 for an empty window.
+ * count = number of t values (<= cap). */
+int32_t rvc_cuda_split_points(int64_t ctx, const double* audio, int64_t n, int32_t window, int64_t t_query,
+                              int64_t step, int64_t* out, int64_t cap, int64_t* count);
+/* runtime.nn.interpolate_linear along time (runtime/nn.py:734-758) of x [L, D]
+ * (time-major) -> y [Lo, D], Lo = int(L * scale), float32. */
+int32_t rvc_cuda_interp_linear(int64_t ctx, const float* x, int64_t L, int32_t D, double scale, float* y,
+                               int64_t Lo);
+/* Protect blend (runtime/pipeline.py:594-608): feats * w + feats0 * (1 - w),
+ * w = protect where pitchf < 1 else 1; feats, feats0, out [P, D], pitchf [P]. */
+int32_t rvc_cuda_protect(int64_t ctx, const float* feats, const float* feats0, const float* pitchf, int64_t P,
+                         int32_t D, float protect, float* out);
+/* change_rms(data1, data2, sr1, sr2, rate) (runtime/pipeline.py:164-235). */
+int32_t rvc_cuda_change_rms(int64_t ctx, const float* d1, int64_t n1, int32_t sr1, const float* d2, int64_t n2,
+                            int32_t sr2, double rate, float* out);
+/* Peak-normalised int16 conversion (runtime/pipeline.py:1208-1213). */
+int32_t rvc_cuda_to_int16(int64_t ctx, const float* x, int64_t n, int16_t* y);
+
 #ifdef __cplusplus
 }
 #endif

@@ -839,4 +839,94 @@ int32_t rvc_cuda_rmvpe_keep_taps(int64_t model, int32_t enable) {
   return on_rmvpe(model, [&](RmvpeModel* m) { m->keep_taps = enable != 0; });
 }
 
+// ----------------------------------------------------------------- pipeline DSP
+int32_t rvc_cuda_filtfilt(int64_t ctx, const double* b, int32_t nb, const double* a, int32_t na, const void* x,
+                          int32_t x_f32, int64_t n, double* y) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(b && a && x && y && nb >= 1 && na >= 1 && n >= 0, "filtfilt: bad arguments");
+    DevBuf dx(c, sizeof(double) * (size_t)std::max<int64_t>(1, n)), dy(c, sizeof(double) * (size_t)std::max<int64_t>(1, n));
+    if (x_f32) {
+      DevBuf xf(c, sizeof(float) * (size_t)std::max<int64_t>(1, n));
+      h2d(c, xf.p, x, sizeof(float) * n);
+      dsp_f32_to_f64(c, xf.f(), n, (double*)dx.p);
+      RVC_CUDA_TRY(cudaStreamSynchronize(c->stream));
+    } else {
+      h2d(c, dx.p, x, sizeof(double) * n);
+    }
+    dsp_filtfilt(c, b, nb, a, na, (const double*)dx.p, n, x_f32 != 0, (double*)dy.p);
+    d2h(c, y, dy.p, sizeof(double) * n);
+    finish(c);
+  });
+}
+
+int32_t rvc_cuda_split_points(int64_t ctx, const double* audio, int64_t n, int32_t window, int64_t t_query,
+                              int64_t step, int64_t* out, int64_t cap, int64_t* count) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(audio && out && count && n >= 1 && cap >= 0, "split_points: bad arguments");
+    const int64_t nq = n > step ? (n - 1) / step : 0;
+    RVC_CHECK_ARG(nq <= cap, "split_points: output holds " + std::to_string(cap) + " points, " +
+                                 std::to_string(nq) + " needed");
+    DevBuf dx(c, sizeof(double) * (size_t)n), dout(c, sizeof(int64_t) * (size_t)std::max<int64_t>(1, nq));
+    h2d(c, dx.p, audio, sizeof(double) * n);
+    *count = dsp_split_points(c, (const double*)dx.p, n, window, t_query, step, (long long*)dout.p);
+    d2h(c, out, dout.p, sizeof(int64_t) * (size_t)nq);
+    finish(c);
+  });
+}
+
+int32_t rvc_cuda_interp_linear(int64_t ctx, const float* x, int64_t L, int32_t D, double scale, float* y,
+                               int64_t Lo) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(x && y && L >= 1 && D >= 1 && scale > 0.0 && Lo == (int64_t)((double)L * scale),
+                  "interp_linear: bad arguments (Lo must be int(L * scale))");
+    DevBuf dx(c, sizeof(float) * (size_t)L * D), dy(c, sizeof(float) * (size_t)std::max<int64_t>(1, Lo) * D);
+    h2d(c, dx.p, x, dx.bytes);
+    dsp_interp_time(c, dx.f(), L, D, scale, dy.f(), Lo);
+    d2h(c, y, dy.p, sizeof(float) * (size_t)Lo * D);
+    finish(c);
+  });
+}
+
+int32_t rvc_cuda_protect(int64_t ctx, const float* feats, const float* feats0, const float* pitchf, int64_t P,
+                         int32_t D, float protect, float* out) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(feats && feats0 && pitchf && out && P >= 0 && D >= 1, "protect: bad arguments");
+    if (P == 0) return;
+    const size_t nb = sizeof(float) * (size_t)P * D;
+    DevBuf df(c, nb), df0(c, nb), dp(c, sizeof(float) * P), dout(c, nb);
+    h2d(c, df.p, feats, nb);
+    h2d(c, df0.p, feats0, nb);
+    h2d(c, dp.p, pitchf, sizeof(float) * P);
+    dsp_protect(c, df.f(), df0.f(), dp.f(), P, D, protect, dout.f());
+    d2h(c, out, dout.p, nb);
+    finish(c);
+  });
+}
+
+int32_t rvc_cuda_change_rms(int64_t ctx, const float* d1, int64_t n1, int32_t sr1, const float* d2, int64_t n2,
+                            int32_t sr2, double rate, float* out) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(d1 && d2 && out && n1 >= 0 && n2 >= 0, "change_rms: bad arguments");
+    if (n2 == 0) return;
+    DevBuf a(c, sizeof(float) * (size_t)std::max<int64_t>(1, n1)), b(c, sizeof(float) * (size_t)n2),
+        o(c, sizeof(float) * (size_t)n2);
+    h2d(c, a.p, d1, sizeof(float) * n1);
+    h2d(c, b.p, d2, sizeof(float) * n2);
+    dsp_change_rms(c, a.f(), n1, sr1, b.f(), n2, sr2, rate, o.f());
+    d2h(c, out, o.p, sizeof(float) * n2);
+    finish(c);
+  });
+}
+
+int32_t rvc_cuda_to_int16(int64_t ctx, const float* x, int64_t n, int16_t* y) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(x && y && n >= 1, "to_int16: bad arguments");
+    DevBuf dx(c, sizeof(float) * (size_t)n), dy(c, sizeof(int16_t) * (size_t)n);
+    h2d(c, dx.p, x, dx.bytes);
+    dsp_to_int16(c, dx.f(), n, (short*)dy.p);
+    d2h(c, y, dy.p, dy.bytes);
+    finish(c);
+  });
+}
+
 }  // extern "C"

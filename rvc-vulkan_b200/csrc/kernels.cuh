@@ -73,4 +73,20 @@ void k_taps_to_channels(const float* W, int O, int I, int K, int j0, int nt, flo
 void k_attention(const float* qkv, int qkv_ld, int q_off, int k_off, int v_off, int B, int heads, int D, int P,
                  float q_div, float* y, int y_ld, cudaStream_t st);
 
+// ---- pipeline signal processing (dsp.cu); device pointers unless noted
+struct Context;
+// scipy.signal.filtfilt(b, a, x) with padtype 'odd' (b, a host arrays), float64
+void dsp_filtfilt(Context* ctx, const double* b, int nb, const double* a, int na, const double* x_dev, long long n,
+                  bool ext_f32, double* y_dev);
+void dsp_f32_to_f64(Context* ctx, const float* x, long long n, double* y);
+// first argmin of the 160-sample absolute sums around t = step, 2 step, ... (< n); -1 = empty window
+long long dsp_split_points(Context* ctx, const double* audio, long long n, int window, long long t_query,
+                           long long step, long long* out_dev);
+void dsp_interp_time(Context* ctx, const float* x, long long L, int D, double scale, float* y, long long Lo);
+void dsp_protect(Context* ctx, const float* feats, const float* feats0, const float* pitchf, long long P, int D,
+                 float protect, float* out);
+void dsp_change_rms(Context* ctx, const float* d1, long long n1, int sr1, const float* d2, long long n2, int sr2,
+                    double rate, float* out);
+void dsp_to_int16(Context* ctx, const float* x, long long n, short* y);
+
 }  // namespace rvc

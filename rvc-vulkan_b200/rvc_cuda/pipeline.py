@@ -1,0 +1,267 @@
+"""The offline conversion pipeline with its signal processing on the device.
+
+``Pipeline`` mirrors the reference's ``runtime.pipeline.Pipeline``
+(``runtime/pipeline.py:368``): the same constructor ``(tgt_sr, config)``, the
+same ``get_f0`` and ``pipeline(...)`` signatures and return value
+``(tgt_sr, int16 audio)``, the same chunking.  The models are the duck-typed
+objects the reference's pipeline takes (``runtime/pipeline.py:15-25``):
+``model.encode`` / ``encode_batch`` (``CudaHubert``), ``net_g.infer`` /
+``prep_dec`` + ``decode_batch`` (``CudaSynthesizer``) and
+``self.model_rmvpe.infer_from_audio`` (``CudaRmvpe``).  The steps between the
+models run on the device through ``rvc_cuda.dsp``: the 48 Hz high-pass, the
+silence split, the retrieval blend (``CudaIndex``), the x2 interpolation and
+the protect blend, ``change_rms`` and the int16 conversion.
+
+Host-side glue that stays in numpy: the reflect padding and slicing of the
+chunks, the frame alignment of pitch arrays (``:572-603``) and the f0
+post-processing of ``get_f0`` (``:468-482``, a few thousand values per call).
+
+Not offered here: the ``pm`` / ``fcpe`` f0 methods, output resampling
+(``resample_sr``), the IVF retrieval mode and ``brute_mix != 0``; asking for
+one raises ``NotImplementedError``.
+"""
+
+from __future__ import annotations
+
+import time
+from typing import Optional
+
+import numpy as np
+
+from . import dsp
+
+__all__ = ["Pipeline"]
+
+_WINDOW = 160
+_K_SEARCH = 8
+
+
+def _as_version(version):
+    """1 / 2 from 1, 2, "v1", "v2" (``runtime/pipeline.py:1281-1288``)."""
+    if version in ("v1", "v2"):
+        return 1 if version == "v1" else 2
+    v = int(version)
+    if v not in (1, 2):
+        raise ValueError(f"version must be 1 or 2, got {version!r}")
+    return v
+
+
+def _align(arr, n):
+    """Repeat the last frame or cut to ``n`` frames (``runtime/pipeline.py:582-603``)."""
+    m = arr.shape[1]
+    if m == n:
+        return arr
+    if m < n:
+        return np.concatenate([arr, np.repeat(arr[:, -1:], n - m, axis=1)], axis=1)
+    return arr[:, :n]
+
+
+class Pipeline:
+    """Device pipeline with the reference ``Pipeline``'s interface."""
+
+    def __init__(self, tgt_sr, config):
+        self.x_pad, self.x_query, self.x_center, self.x_max = (config.x_pad, config.x_query, config.x_center,
+                                                               config.x_max)
+        self.is_half = False
+        self.sr = 16000
+        self.window = _WINDOW
+        self.t_pad = self.sr * self.x_pad
+        self.t_pad_tgt = tgt_sr * self.x_pad
+        self.t_pad2 = self.t_pad * 2
+        self.t_query = self.sr * self.x_query
+        self.t_center = self.sr * self.x_center
+        self.t_max = self.sr * self.x_max
+        self.device = getattr(config, "device", None)
+
+    # ------------------------------------------------------------------ f0
+    def get_f0(self, x, p_len, f0_up_key, f0_method):
+        """f0 of a segment through ``self.model_rmvpe`` and the reference's
+        post-processing (``runtime/pipeline.py:408-483``): unvoiced frames
+        linearly interpolated, transposed by ``f0_up_key`` semitones, then the
+        mel quantisation to 1..255.  Returns ``(f0_coarse int32, f0 float32)``."""
+        if f0_method not in ("pm", "rmvpe", "fcpe"):
+            raise ValueError(f"Unsupported F0 method: {f0_method}")
+        if f0_method != "rmvpe":
+            raise NotImplementedError(f"f0 method {f0_method!r} is not on the device path (rmvpe is)")
+        if not hasattr(self, "model_rmvpe"):
+            raise RuntimeError("Pipeline.model_rmvpe must be set (a CudaRmvpe, or any object with "
+                               "infer_from_audio(x, thred))")
+        f0_min, f0_max = 50, 1100
+        f0_mel_min = 1127 * np.log(1 + f0_min / 700)
+        f0_mel_max = 1127 * np.log(1 + f0_max / 700)
+        f0 = np.asarray(self.model_rmvpe.infer_from_audio(np.asarray(x, dtype=np.float32), thred=0.03),
+                        dtype=np.float64)
+        uv = f0 == 0
+        if uv.any():
+            voiced = np.where(~uv)[0]
+            if voiced.size:
+                f0[uv] = np.interp(np.where(uv)[0], voiced, f0[voiced])
+        f0 *= pow(2, f0_up_key / 12)
+        f0bak = f0.astype(np.float32).copy()
+        f0_mel = 1127 * np.log(1 + f0 / 700)
+        f0_mel[f0_mel > 0] = (f0_mel[f0_mel > 0] - f0_mel_min) * 254 / (f0_mel_max - f0_mel_min) + 1
+        f0_mel = np.clip(f0_mel, 1, 255)
+        return np.rint(f0_mel).astype(np.int32), f0bak
+
+    # ------------------------------------------------------------------ index
+    @staticmethod
+    def _resolve_index(file_index, index_rate):
+        """A ``CudaIndex`` for ``file_index`` (a ``CudaIndex``, an ``[N, D]``
+        array, or an object with ``ntotal`` / ``reconstruct_n`` such as the
+        reference's ``FeatureIndex``), or None (``runtime/pipeline.py:1227-1256``)."""
+        from . import retrieval  # noqa: PLC0415
+        if index_rate == 0 or file_index is None or (isinstance(file_index, str) and file_index == ""):
+            return None
+        if isinstance(file_index, retrieval.CudaIndex):
+            return file_index if file_index.N > 0 else None
+        if isinstance(file_index, str):
+            raise NotImplementedError("index files are loaded by the caller: pass the index vectors or a CudaIndex")
+        if getattr(file_index, "vectors_by_rows", None) is not None:
+            raise NotImplementedError("the IVF retrieval mode is not on the device path")
+        if isinstance(file_index, np.ndarray):
+            vecs = file_index
+        elif hasattr(file_index, "reconstruct_n") and hasattr(file_index, "ntotal"):
+            if file_index.ntotal <= 0:
+                return None
+            vecs = file_index.reconstruct_n(0, file_index.ntotal)
+        else:
+            return None
+        return retrieval._index_for(vecs)
+
+    # ------------------------------------------------------------------ chunk
+    def _vc_prepare(self, sid, audio_len, pitch, pitchf, feats, index, index_rate, protect, times,
+                    retrieval_mode="ivf", brute_mix=0.0):
+        """Per-chunk preparation (``runtime/pipeline.py:488-614``) on the device:
+        retrieval blend, x2 interpolation of ``feats`` (and of the unblended
+        ``feats0`` when protecting), frame alignment, protect blend."""
+        t0 = time.perf_counter()
+        feats = np.asarray(feats, dtype=np.float32)
+        protecting = protect < 0.5 and pitch is not None and pitchf is not None
+        feats0 = feats if protecting else None
+        if index is not None and index_rate != 0:
+            if brute_mix != 0:
+                raise NotImplementedError("brute_mix != 0 is not on the device path")
+            feats = index.blend(feats[0], k=_K_SEARCH, mode="pipeline", feats=feats[0],
+                                index_rate=index_rate)[None]
+        feats = dsp.interpolate_linear(feats, scale_factor=2, axis=1)
+        if protecting:
+            feats0 = dsp.interpolate_linear(feats0, scale_factor=2, axis=1)
+        t1 = time.perf_counter()
+        if pitch is not None and pitchf is not None:
+            n = feats.shape[1]
+            pitch = _align(pitch, n)
+            pitchf = _align(pitchf, n)
+        if protecting:
+            pitchf = _align(pitchf, feats.shape[1])
+            feats = dsp.protect_blend(feats, feats0, pitchf, protect)
+        times[0] += t1 - t0
+        return {"feats": feats, "pitch": pitch, "pitchf": pitchf, "sid_arr": np.asarray([sid], dtype=np.int64)}
+
+    # ------------------------------------------------------------------ whole
+    def pipeline(self, model, net_g, sid, audio, times, f0_up_key, f0_method, file_index, index_rate, if_f0,
+                 tgt_sr, resample_sr, rms_mix_rate, version, protect, progress_cb=None, slice_length=0,
+                 retrieval_mode="ivf", brute_mix=0.0):
+        """Offline conversion of 16 kHz ``audio`` (``runtime/pipeline.py:697-1213``).
+        Returns ``(tgt_sr, int16 audio)``."""
+        if not if_f0:
+            raise NotImplementedError("only f0-guided models are supported (as in the reference)")
+        if tgt_sr != resample_sr >= 16000:
+            raise NotImplementedError("output resampling is not on the device path")
+        index = self._resolve_index(file_index, index_rate)
+        version = _as_version(version)
+        t_max = self.t_max
+        try:
+            slice_length = float(slice_length or 0)
+        except (TypeError, ValueError):
+            slice_length = 0
+        if slice_length > 0:
+            t_max = int(slice_length * self.sr)
+
+        audio = np.asarray(audio, dtype=np.float32)
+        audio = dsp.highpass(audio)                                   # float64, :765
+
+        opt_ts = []
+        if audio.shape[0] + 2 * (self.window // 2) > t_max:           # :769-790
+            step = min(self.t_center, t_max)
+            opt_ts = dsp.split_points(audio, self.t_query, step, self.window)
+
+        t1 = time.perf_counter()
+        audio_pad_f0 = np.pad(audio, (self.t_pad, self.t_pad), mode="reflect")
+        seg_pts = [0] + [o + self.t_pad for o in opt_ts] + [audio_pad_f0.shape[0]]
+        pitch_parts, pitchf_parts = [], []
+        for si in range(len(seg_pts) - 1):                            # :800-813
+            ap, bp = seg_pts[si], seg_pts[si + 1]
+            b = min(bp + self.t_pad2 + self.window, audio_pad_f0.shape[0])
+            seg = audio_pad_f0[ap:b]
+            pi, pfi = self.get_f0(seg, seg.shape[0] // self.window, f0_up_key, f0_method)
+            core_n = max(1, (bp - ap) // self.window)
+            pitch_parts.append(pi[:core_n])
+            pitchf_parts.append(pfi[:core_n])
+        pitch = np.concatenate(pitch_parts)[None, :]
+        pitchf = np.concatenate(pitchf_parts).astype(np.float32)[None, :]
+        times[1] += time.perf_counter() - t1
+        audio_pad = audio_pad_f0                                      # same reflect pad, :819
+
+        total = len(opt_ts) + 1
+        if progress_cb is not None:
+            progress_cb(0, total, "split into %d chunks" % total)
+        bounds, s = [], 0
+        for t in opt_ts:                                              # :840-846
+            t = t // self.window * self.window
+            bounds.append((s, t))
+            s = t
+        bounds.append((s, None))
+
+        blocks = []                                                   # (idx, audio, pitch, pitchf)
+        for idx, (s0, e0) in enumerate(bounds):
+            if e0 is None:
+                blk = audio_pad[s0:]
+                p, pf = pitch[:, s0 // self.window:], pitchf[:, s0 // self.window:]
+            else:
+                blk = audio_pad[s0:e0 + self.t_pad2 + self.window]
+                p = pitch[:, s0 // self.window:(e0 + self.t_pad2) // self.window]
+                pf = pitchf[:, s0 // self.window:(e0 + self.t_pad2) // self.window]
+            if blk.shape[0] < self.window * 10:
+                continue
+            blocks.append((idx, np.asarray(blk, dtype=np.float32), p, pf))
+
+        feats_all = self._encode(model, [b[1] for b in blocks], version)
+        preps = [self._vc_prepare(sid, b[1].shape[0], b[2], b[3], f, index, index_rate, protect, times,
+                                  retrieval_mode, brute_mix) for b, f in zip(blocks, feats_all)]
+        t2 = time.perf_counter()
+        waves = self._decode(net_g, preps)
+        times[2] += time.perf_counter() - t2
+
+        results = [None] * len(bounds)
+        for done, ((idx, *_), w) in enumerate(zip(blocks, waves), 1):
+            w = np.asarray(w, dtype=np.float32).reshape(-1)
+            results[idx] = w[self.t_pad_tgt:-self.t_pad_tgt]
+            if progress_cb is not None:
+                progress_cb(done, total, "chunk %d/%d" % (done, total))
+        audio_opt = np.concatenate([r for r in results if r is not None])
+        if rms_mix_rate != 1:
+            audio_opt = dsp.change_rms(audio, audio_opt, 16000, tgt_sr, rms_mix_rate)
+        return tgt_sr, dsp.to_int16(audio_opt)
+
+    # ------------------------------------------------------------------ models
+    @staticmethod
+    def _encode(model, audios, version):
+        """HuBERT features of every chunk: one ``encode_batch`` call when the
+        model offers it (chunk results equal per-chunk ``encode``), else
+        ``encode`` per chunk."""
+        if not audios:
+            return []
+        if hasattr(model, "encode_batch") and len(audios) > 1:
+            return [np.asarray(f, dtype=np.float32).reshape(1, -1, np.shape(f)[-1])
+                    for f in model.encode_batch([a[None, :] for a in audios], version=version)]
+        return [np.asarray(model.encode(a[None, :], version=version), dtype=np.float32) for a in audios]
+
+    @staticmethod
+    def _decode(net_g, preps):
+        """Waveforms of every chunk: ``prep_dec`` + one ``decode_batch`` when the
+        synthesizer offers them, else ``infer`` per chunk."""
+        if hasattr(net_g, "prep_dec") and hasattr(net_g, "decode_batch") and len(preps) > 1:
+            dps = [net_g.prep_dec(p["feats"], p["pitch"], p["pitchf"], p["sid_arr"]) for p in preps]
+            return net_g.decode_batch(dps)
+        return [np.asarray(net_g.infer(np.asarray(p["feats"], dtype=np.float32), p["pitch"], p["pitchf"],
+                                       p["sid_arr"], phone_gpu=None))[0, 0] for p in preps]

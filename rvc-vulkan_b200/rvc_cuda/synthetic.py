@@ -29,7 +29,7 @@ __all__ = [
     "VITS_V2_40K", "VITS_V2_48K", "vits_config_array", "make_vits_weights",
     "make_vits_inputs", "make_vits_noise", "make_hubert_weights",
     "make_hubert_input", "coarse_pitch", "make_index", "make_queries",
-    "make_rmvpe_weights", "make_rmvpe_input", "RMVPE_ENC", "RMVPE_INTER", "RMVPE_DEC",
+    "make_rmvpe_weights", "make_rmvpe_input", "RMVPE_ENC", "RMVPE_INTER", "RMVPE_DEC", "make_speech_audio",
 ]
 
 # (sr, upsample_rates, upsample_kernels) of the two measured v2 generators.
@@ -318,3 +318,35 @@ def make_rmvpe_input(T: int = 160000, seed: int = 0) -> np.ndarray:
     ph = 2 * np.pi * np.cumsum(f0) / 16000.0
     x = 0.3 * np.sin(ph) + 0.1 * np.sin(2 * ph) + 0.05 * np.sin(3 * ph) + 0.02 * rs.standard_normal(T)
     return x.astype(np.float32)
+
+
+def make_speech_audio(seconds: float = 60.0, seed: int = 0, sr: int = 16000, silence_every: float = 8.0,
+                      silence_len: float = 0.5, noise_db: float = -20.0) -> np.ndarray:
+    """Speech-like 16 kHz audio ``[T] f32``: three
+    harmonics (1, 1/2, 1/4) on an f0 random walk in 80-300 Hz (a step every
+    10 ms, linear between steps), a slow amplitude envelope, pink noise at
+    ``noise_db`` relative to the harmonic signal's RMS, and digital silences of
+    ``silence_len`` s starting every ``silence_every`` s."""
+    rs = np.random.RandomState(80_000 + seed)
+    T = int(round(seconds * sr))
+    nfr = T // 160 + 2
+    walk = np.empty(nfr)
+    f = rs.uniform(100.0, 250.0)
+    for i in range(nfr):
+        f = min(300.0, max(80.0, f + rs.standard_normal() * 4.0))
+        walk[i] = f
+    f0 = np.interp(np.arange(T) / 160.0, np.arange(nfr), walk)
+    ph = 2.0 * np.pi * np.cumsum(f0) / sr
+    env = 0.6 + 0.4 * np.sin(2.0 * np.pi * np.arange(T) / sr * 3.1 + rs.uniform(0, 2 * np.pi))
+    x = env * (0.4 * np.sin(ph) + 0.2 * np.sin(2 * ph) + 0.1 * np.sin(3 * ph))
+    spec = np.fft.rfft(rs.standard_normal(T))
+    freqs = np.arange(spec.size, dtype=np.float64)
+    freqs[0] = 1.0
+    pink = np.fft.irfft(spec / np.sqrt(freqs), n=T)
+    rms_x = np.sqrt(np.mean(x * x))
+    pink *= rms_x * 10.0 ** (noise_db / 20.0) / max(np.sqrt(np.mean(pink * pink)), 1e-12)
+    y = x + pink
+    step, ln = int(silence_every * sr), int(silence_len * sr)
+    for s in range(step, T, step):
+        y[s:s + ln] = 0.0
+    return y.astype(np.float32)

@@ -230,10 +230,89 @@ def run_ops(nn, meta):
     meta["ops"] = {"kind": "ops", "cases": cases}
 
 
+def run_dsp(meta):
+    """Pipeline signal processing through the reference's own call sites:
+    ``signal.filtfilt(_BH, _AH, .)`` (``runtime/pipeline.py:49``, ``:765``),
+    ``change_rms`` (``:164``), ``Pipeline._vc_prepare`` with given features
+    (x2 interpolation, frame alignment, protect; ``:488-614``) and whole
+    ``Pipeline.pipeline`` runs (``:697``) with the deterministic model
+    stand-ins of ``pipeline_fakes`` (split points recovered from the offsets of
+    the segments handed to ``get_f0``; int16 output)."""
+    from runtime import pipeline as rp  # noqa: PLC0415
+    sys.path.insert(0, HERE)
+    import pipeline_fakes as pf  # noqa: PLC0415
+    rec, cases = {}, {}
+    audio = syn.make_speech_audio(0.5, seed=1)
+    rec["hp_speech"] = rp.signal.filtfilt(rp._BH, rp._AH, audio)
+    edge = np.random.RandomState(91_001).standard_normal(19).astype(np.float32)
+    rec["hp_edge_x"], rec["hp_edge"] = edge, rp.signal.filtfilt(rp._BH, rp._AH, edge)
+    x64 = np.random.RandomState(91_002).standard_normal(300) * 0.3
+    rec["hp_f64_x"], rec["hp_f64"] = x64, rp.signal.filtfilt(rp._BH, rp._AH, x64)
+    cases["hp_speech"] = {"seconds": 0.5, "seed": 1, "inputs_sha256": digest([audio])}
+
+    d1 = syn.make_speech_audio(0.6, seed=2)
+    d2 = (0.8 * np.sin(np.arange(24000) * 0.03) * np.random.RandomState(91_003).uniform(0.2, 1.0, 24000)
+          ).astype(np.float32)
+    rec["rms_d2"], rec["rms_out"] = d2, rp.change_rms(d1, d2, 16000, 40000, 0.25)
+    rec["rms_small_d2"] = d2[:700].copy()
+    rec["rms_small_out"] = rp.change_rms(d1, rec["rms_small_d2"], 16000, 48000, 0.6)
+    cases["rms"] = {"seconds": 0.6, "seed": 2, "inputs_sha256": digest([d1])}
+
+    rs = np.random.RandomState(91_004)
+    feats = rs.standard_normal((1, 30, 256)).astype(np.float32)
+    pitch = rs.randint(1, 256, size=(1, 57)).astype(np.int64)
+    pitchf = rs.uniform(100, 300, size=(1, 57)).astype(np.float32)
+    pitchf[0, rs.rand(57) < 0.3] = 0.0
+    pipe = rp.Pipeline(40000, pf.config())
+    prep = pipe._vc_prepare(None, 0, np.zeros(60 * 160 + 400, np.float32), pitch, pitchf, [0.0, 0.0, 0.0], None,
+                            None, 0, 1, 0.33, feats=feats)
+    rec.update(prep_feats=feats, prep_pitch=pitch, prep_pitchf=pitchf, prep_out=prep["feats"],
+               prep_out_pitch=prep["pitch"], prep_out_pitchf=prep["pitchf"])
+
+    for name, kw in PIPE_CASES:
+        a = syn.make_speech_audio(kw["seconds"], seed=kw["seed"], silence_every=kw["silence_every"])
+        pipe = rp.Pipeline(40000, pf.config(x_query=kw["x_query"]))
+        pipe.model_rmvpe = pf.FakeRmvpe()
+        starts = []
+        orig = pipe.get_f0
+
+        def get_f0(x, *args, _orig=orig, _starts=starts):
+            _starts.append(x.__array_interface__["data"][0])
+            return _orig(x, *args)
+
+        pipe.get_f0 = get_f0
+        sr, out = pipe.pipeline(pf.FakeHubert(D=768), pf.FakeSynth(gain=kw["gain"]), 0, a, [0.0, 0.0, 0.0],
+                                kw["f0_up_key"], "rmvpe", None, 0, True, 40000, 0, kw["rms"], 2, kw["protect"],
+                                slice_length=kw["slice_length"])
+        assert sr == 40000
+        item = np.dtype(np.float64).itemsize
+        rec[name + "_split"] = np.array([(p - starts[0]) // item - pipe.t_pad for p in starts[1:]], np.int64)
+        if out.size > 200_000:  # long case: every 101st sample keeps the fixture small
+            rec[name + "_int16_every101"] = out[::101].copy()
+        else:
+            rec[name + "_int16"] = out
+        cases[name] = dict(kw, inputs_sha256=digest([a]), out_len=int(out.size))
+    np.savez_compressed(os.path.join(HERE, "dsp.npz"), **rec)
+    meta["dsp"] = {"kind": "dsp", "cases": cases, "scipy": __import__("scipy").__version__}
+
+
+# whole-pipeline cases with the stand-in models (40 kHz output)
+PIPE_CASES = [
+    ("pipe_split", {"seconds": 8.0, "seed": 3, "silence_every": 2.1, "x_query": 1, "slice_length": 2.0,
+                    "rms": 0.25, "protect": 0.33, "gain": 1.3, "f0_up_key": 2}),
+    ("pipe_voiced", {"seconds": 3.0, "seed": 5, "silence_every": 100.0, "x_query": 1, "slice_length": 1.0,
+                     "rms": 0.5, "protect": 0.2, "gain": 0.7, "f0_up_key": 0}),
+    ("pipe_whole", {"seconds": 1.2, "seed": 4, "silence_every": 8.0, "x_query": 6, "slice_length": 0,
+                    "rms": 1.0, "protect": 0.5, "gain": 1.3, "f0_up_key": -3}),
+    ("pipe_60s", {"seconds": 60.0, "seed": 0, "silence_every": 8.0, "x_query": 6, "slice_length": 0,
+                  "rms": 0.25, "protect": 0.33, "gain": 1.3, "f0_up_key": 0}),
+]
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("RVC_REFERENCE", "/root/reference"))
-    ap.add_argument("--only", choices=["vits", "hubert", "ops", "retrieval", "rmvpe", "partial"], default=None,
+    ap.add_argument("--only", choices=["vits", "hubert", "ops", "retrieval", "rmvpe", "partial", "dsp"], default=None,
                     help="regenerate one family and keep the other fixtures")
     args = ap.parse_args()
     os.environ["RVC_BACKEND"] = "numpy"
@@ -264,6 +343,8 @@ def main():
         from runtime.models import rmvpe as runtime_rmvpe  # noqa: PLC0415
         for c in RMVPE_CASES:
             run_rmvpe(runtime_rmvpe, *c, meta)
+    if args.only in (None, "dsp"):
+        run_dsp(meta)
     if args.only in (None, "retrieval"):
         from runtime import retrieval  # noqa: PLC0415
         for c in RETRIEVAL_CASES:
