@@ -649,6 +649,203 @@ def run_hubert_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def pipeline_cpu_estimate(chunk_samples, frames_total, audio_s):
+    """CPU time of the config-4 pipeline, composed from bounded samples of each
+    stage on the host cores: the oracle models (HuBERT, RMVPE, v2-40k
+    synthesizer, top-8 retrieval against the 200000 x 768 index) timed on short
+    inputs and scaled by the workload's samples / frames, plus the reference's
+    own scipy ``filtfilt`` and the oracle's split / change_rms on the full
+    signal.  Returns (seconds per workload, sample description)."""
+    from scipy import signal
+
+    from oracle import dsp as OD
+    from rvc_cuda import synthetic as syn
+    w = syn.make_vits_weights(40000, 0)
+    cfg = syn.vits_config_array(40000)
+    out_s, ts = cpu_sample(40000, 100, w, cfg, steps=1)
+    synth_s = ts[0] / 100 * frames_total
+    hs, ts = hubert_cpu_sample(48000, steps=1)
+    hub_s = ts[0] / 48000 * chunk_samples
+    rs_, ts = rmvpe_cpu_sample(48000, steps=1)
+    rmv_s = ts[0] / 48000 * chunk_samples
+    qs, tq = retrieval_cpu_sample(200000, 768, 100, steps=1)
+    ret_s = tq[0] / 100 * (frames_total // 2)
+    a = syn.make_speech_audio(audio_s, seed=0)
+    bh, ah = signal.butter(N=5, Wn=48, btype="high", fs=16000)
+    t0 = time.perf_counter()
+    hp = signal.filtfilt(bh, ah, a)
+    OD.split_points(hp, 160, 6 * 16000, 38 * 16000)
+    OD.change_rms(hp, np.zeros(int(audio_s * 40000), np.float32) + 0.1, 16000, 40000, 0.25)
+    dsp_s = time.perf_counter() - t0
+    total = synth_s + hub_s + rmv_s + ret_s + dsp_s
+    desc = (f"stage samples scaled to the workload: synth 100 frames -> {frames_total} frames ({synth_s:.1f} s), "
+            f"HuBERT 3 s -> {chunk_samples / 16000:.0f} s ({hub_s:.1f} s), RMVPE 3 s -> {chunk_samples / 16000:.0f} s "
+            f"({rmv_s:.1f} s), retrieval 100 -> {frames_total // 2} queries ({ret_s:.1f} s), filtfilt/split/"
+            f"change_rms on the full signal ({dsp_s:.2f} s)")
+    return total, desc
+
+
+def pipeline_workload(audio_s):
+    """Chunk samples (with the pipeline's 1 s pads) and synthesizer frames of a
+    conversion of ``audio_s`` seconds under the default config (x_pad 1,
+    x_query 6, x_center 38, x_max 41): chunks cut near every 38 s."""
+    n = int(audio_s * 16000)
+    cuts = list(range(38 * 16000, n, 38 * 16000)) if n + 160 > 41 * 16000 else []
+    bounds = [0] + cuts + [n]
+    samples = sum(bounds[i + 1] - bounds[i] + 2 * 16000 for i in range(len(bounds) - 1))
+    return samples, samples // 160
+
+
+def run_pipeline(args, world, rank, local):
+    """end-to-end conversion of --audio-s seconds of 16 kHz
+    speech-like audio through ``rvc_cuda.pipeline.Pipeline`` (high-pass,
+    silence split, RMVPE f0, HuBERT, top-8 retrieval against a 200000 x 768
+    index at index_rate 0.75, x2 interpolation, protect 0.33, v2-40k
+    synthesizer, change_rms 0.25, int16), one clip per rank."""
+    import types
+
+    import torch
+
+    from rvc_cuda import _lib, synthetic as syn
+    from rvc_cuda.hubert import CudaHubert
+    from rvc_cuda.pipeline import Pipeline
+    from rvc_cuda.retrieval import CudaIndex
+    from rvc_cuda.rmvpe import CudaRmvpe
+    from rvc_cuda.synth import CudaSynthesizer
+
+    torch.cuda.set_device(local)
+    os.environ.setdefault("RVC_FIXED_SEED", "1234")
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    hub = CudaHubert(syn.make_hubert_weights(0), device=local)
+    net = CudaSynthesizer(syn.make_vits_weights(40000, 0), syn.vits_config_array(40000), device=local,
+                          precision=args.precision)
+    index = CudaIndex(syn.make_index(args.index_rows, 768, 0), device=local)
+    cfg = types.SimpleNamespace(x_pad=1, x_query=6, x_center=38, x_max=41, device=f"cuda:{local}")
+    pipe = Pipeline(40000, cfg)
+    pipe.model_rmvpe = CudaRmvpe(syn.make_rmvpe_weights(0), device=local)
+    audio = syn.make_speech_audio(args.audio_s, seed=rank)
+    ctx = hub.ctx
+    stage = [0.0, 0.0, 0.0]
+    out = {}
+
+    def step():
+        sr, wav = pipe.pipeline(hub, net, 0, audio, stage, 0, "rmvpe", index, 0.75, True, 40000, 0, 0.25, 2, 0.33,
+                                slice_length=args.slice_length)
+        out["wav"] = wav
+
+    stream = torch.cuda.ExternalStream(ctx.stream(), device=local)
+
+    def timed(fn, steps):
+        barrier()
+        ctx.sync()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        t_wall = time.perf_counter()
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        ctx.sync()
+        torch.cuda.synchronize()
+        t_wall = time.perf_counter() - t_wall
+        barrier()
+        return e0.elapsed_time(e1) / 1e3, t_wall
+
+    for _ in range(args.warmup):
+        step()
+    stage[:] = [0.0, 0.0, 0.0]
+    n0 = _lib.launch_count()
+    ctx.profile(True)
+    with ClockSampler(local) as clk:
+        t, t_wall = timed(step, args.steps)
+    prof_n, prof_ms, prof_flops = ctx.profile_read()
+    ctx.profile(False)
+    launches = _lib.launch_count() - n0
+    t = max_over_ranks(t)
+    value = world * args.audio_s * args.steps / t
+    wav = out["wav"]
+    if rank == 0:
+        pb, ps, hbm, src = peaks()
+        achieved = prof_flops / (prof_ms / 1e3) / 1e12 if prof_ms > 0 else None
+        line = {
+            "metric": METRIC + ", end-to-end conversion", "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 (BF16x3 tensor-core GEMMs; float64 filtfilt / split)",
+            "data": "synthetic: seeded random-init weights, seeded speech-like audio (3 harmonics on a random-walk "
+                    "f0 80-300 Hz, pink noise -20 dB, 0.5 s silences every 8 s), one clip per rank",
+            "config": {"workload": f"config4 end-to-end pipeline, {args.audio_s:g} s at 16 kHz -> v2-40k, "
+                                   f"rmvpe f0, index {args.index_rows}x768 rate 0.75, rms_mix 0.25, protect 0.33",
+                       "audio_s": args.audio_s, "index_rows": args.index_rows, "slice_length": args.slice_length,
+                       "split": "default config (x_pad 1, x_query 6, x_center 38, x_max 41)",
+                       "l2": "working set larger than L2 (index 614 MB, GBs of activations per step)",
+                       "parallelism": f"one clip per rank x{world}, no collective"},
+            "roofline": {"bound": "tensor", "kernel": "tc_conv_kernel (implicit-GEMM conv/linear, all launches)",
+                         "achieved": achieved, "peak": ps, "unit": "TFLOP/s",
+                         "frac": (achieved / ps) if achieved else None, "traffic": None,
+                         "peak_source": f"{src} bf16 dense sustained", "launches": prof_n,
+                         "kernel_ms_per_step": prof_ms / args.steps},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": audio.nbytes * world,
+                    "d2h_bytes_per_step": wav.nbytes * world,
+                    "note": "the pipeline takes host audio and returns host int16 by contract: value is this "
+                            "end-to-end measurement (stage round trips included)"},
+            "stage_s_per_step": {"retrieval_interp": stage[0] / args.steps, "f0": stage[1] / args.steps,
+                                 "synth": stage[2] / args.steps},
+            "host_wall_s_per_step": t_wall / args.steps,
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+            "out_samples": int(wav.size),
+        }
+        if world == 1 and not args.no_cpu:
+            samples, frames = pipeline_workload(args.audio_s)
+            cpu_s, desc = pipeline_cpu_estimate(samples, frames, args.audio_s)
+            line["cpu_baseline"] = {"value": args.audio_s / cpu_s, "unit": UNIT, "cores": blas_threads(),
+                                    "kind": "port", "sample": desc}
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def run_pipeline_reference(args, world, rank):
+    if rank != 0:
+        return
+    samples, frames = pipeline_workload(args.audio_s)
+    ts, desc = [], ""
+    for _ in range(args.steps):
+        cpu_s, desc = pipeline_cpu_estimate(samples, frames, args.audio_s)
+        ts.append(cpu_s)
+    t = sum(ts)
+    value = args.audio_s * len(ts) / t
+    line = {
+        "impl": "reference", "metric": METRIC + ", end-to-end conversion", "value": value, "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t / len(ts),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": {"workload": f"config4 end-to-end pipeline, {args.audio_s:g} s, CPU stage samples",
+                   "audio_s": args.audio_s, "index_rows": 200000},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": blas_threads(), "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_ours(args, world, rank, local):
     import torch
 
@@ -813,15 +1010,22 @@ def main():
     ap.add_argument("--ref-frames", type=int, default=100)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile-out", default="", help="write the per-layer conv profile (CSV) here")
-    ap.add_argument("--workload", default="synth", choices=["synth", "hubert", "retrieval", "rmvpe"],
+    ap.add_argument("--workload", default="synth", choices=["synth", "hubert", "retrieval", "rmvpe", "pipeline"],
                     help="synth: config 3 (headline); hubert: config 1 (HuBERT-base encoder); "
-                         "retrieval: config 4's top-8 search + blend; rmvpe: config 2")
+                         "retrieval: config 4's top-8 search + blend; rmvpe: config 2; "
+                         "pipeline: config 4 end to end")
+    ap.add_argument("--slice-length", type=float, default=0.0, help="pipeline: slice_length (0 = config default)")
     ap.add_argument("--samples", type=int, default=160000, help="hubert / rmvpe: samples per chunk")
     ap.add_argument("--audio-s", type=float, default=60.0, help="retrieval: seconds of frames (50 per s)")
     ap.add_argument("--index-rows", type=int, default=200000, help="retrieval: index rows")
     args = ap.parse_args()
     world, rank, local = dist_setup()
-    if args.workload == "rmvpe":
+    if args.workload == "pipeline":
+        if args.impl == "reference":
+            run_pipeline_reference(args, world, rank)
+        else:
+            run_pipeline(args, world, rank, local)
+    elif args.workload == "rmvpe":
         if args.impl == "reference":
             run_rmvpe_reference(args, world, rank)
         else:

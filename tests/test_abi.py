@@ -113,6 +113,22 @@ def test_retrieval_patch_reference_replaces_module_functions():
     assert ret_mod._rvc_cuda_orig_search_l2() == "numpy"
 
 
+def test_dsp_patch_reference_replaces_pipeline_functions():
+    import types
+
+    from rvc_cuda import dsp
+
+    sig = types.SimpleNamespace(filtfilt=lambda b, a, x: "scipy", butter=lambda *a, **k: "butter")
+    pipe_mod = types.SimpleNamespace(signal=sig, change_rms=lambda *a: "numpy", interpolate_linear=lambda *a: "numpy")
+    dsp.patch_reference(pipe_mod)
+    assert pipe_mod.change_rms is dsp.change_rms and pipe_mod.interpolate_linear is dsp.interpolate_linear
+    assert pipe_mod.signal is not sig and pipe_mod.signal.butter is sig.butter
+    assert pipe_mod._rvc_cuda_orig_signal.filtfilt(0, 0, 0) == "scipy"
+    with pytest.raises(ValueError):  # other padding modes are not on the device path
+        pipe_mod.signal.filtfilt([1.0], [1.0], [0.0] * 10, padtype="even")
+    assert dsp.patch_reference(pipe_mod) is pipe_mod  # idempotent
+
+
 def test_rmvpe_frames_and_patch_reference():
     from rvc_cuda import rmvpe
 
