@@ -25,6 +25,8 @@ Context::~Context() {
   cudaStreamSynchronize(stream);
   for (auto& kv : allocs) cudaFree(kv.first);
   allocs.clear();
+  for (auto& kv : pool) cudaFree(kv.second);
+  pool.clear();
   for (auto& e : prof_ev) {
     cudaEventDestroy(e.a);
     cudaEventDestroy(e.b);
@@ -34,32 +36,72 @@ Context::~Context() {
   if (stream) cudaStreamDestroy(stream);
 }
 
+namespace {
+constexpr size_t kPoolMaxBytes = size_t(16) << 30;  // cached free blocks above this are returned
+size_t block_size(size_t bytes) {
+  const size_t g = bytes >= (size_t(1) << 20) ? (size_t(1) << 20) : 512;  // 1 MiB granules for large blocks
+  return (bytes + g - 1) / g * g;
+}
+}  // namespace
+
+void Context::release_pool() {
+  if (pool.empty()) return;
+  cudaStreamSynchronize(stream);
+  for (auto& kv : pool) cudaFree(kv.second);
+  pool.clear();
+  pool_bytes = 0;
+}
+
 void* Context::alloc(size_t bytes) {
   if (bytes == 0) bytes = 16;
-  if (mem_cap > 0 && mem_used + (int64_t)bytes > mem_cap)
-    throw Error{kErrOom, "device memory cap exceeded: need " + std::to_string(bytes) + " B, used " +
+  const size_t bs = block_size(bytes);
+  if (mem_cap > 0 && mem_used + (int64_t)bs > mem_cap)
+    throw Error{kErrOom, "device memory cap exceeded: need " + std::to_string(bs) + " B, used " +
                              std::to_string(mem_used) + " of " + std::to_string(mem_cap)};
   void* p = nullptr;
-  cudaError_t e = cudaMalloc(&p, bytes);
-  if (e != cudaSuccess) {
-    cudaGetLastError();
-    throw Error{kErrOom, std::string("cudaMalloc failed: ") + cudaGetErrorString(e)};
+  size_t got = bs;
+  auto it = pool.lower_bound(bs);
+  if (it != pool.end() && it->first <= bs + bs / 4) {  // reuse a cached block of about this size
+    got = it->first;
+    p = it->second;
+    pool_bytes -= got;
+    pool.erase(it);
+  } else {
+    cudaError_t e = cudaMalloc(&p, bs);
+    if (e != cudaSuccess) {  // give the cached blocks back and retry once
+      cudaGetLastError();
+      release_pool();
+      e = cudaMalloc(&p, bs);
+    }
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      throw Error{kErrOom, std::string("cudaMalloc failed: ") + cudaGetErrorString(e)};
+    }
   }
   // Zero-filled: padding rows of activation buffers must read as zeros.
   RVC_CUDA_TRY(cudaMemsetAsync(p, 0, bytes, stream));
-  allocs[p] = bytes;
-  mem_used += (int64_t)bytes;
+  allocs[p] = got;
+  mem_used += (int64_t)got;
   return p;
 }
 
 void Context::free(void* p) {
   auto it = allocs.find(p);
   if (it == allocs.end()) return;
-  // Work queued on the stream may still read the buffer.
-  cudaStreamSynchronize(stream);
-  cudaFree(p);
-  mem_used -= (int64_t)it->second;
+  const size_t bs = it->second;
+  mem_used -= (int64_t)bs;
   allocs.erase(it);
+  pool.emplace(bs, p);
+  pool_bytes += bs;
+  if (pool_bytes > kPoolMaxBytes) {  // return the largest cached blocks
+    cudaStreamSynchronize(stream);
+    while (pool_bytes > kPoolMaxBytes / 2 && !pool.empty()) {
+      auto last = std::prev(pool.end());
+      cudaFree(last->second);
+      pool_bytes -= last->first;
+      pool.erase(last);
+    }
+  }
 }
 
 void Context::prof_begin(cudaEvent_t* a, cudaEvent_t* b) {

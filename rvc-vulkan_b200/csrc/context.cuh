@@ -20,7 +20,13 @@ struct Context {
   std::mutex mu;
   int64_t mem_cap = 0;   // 0 = unlimited
   int64_t mem_used = 0;
-  std::unordered_map<void*, size_t> allocs;
+  std::unordered_map<void*, size_t> allocs;  // live blocks -> block size
+  // Freed blocks kept for reuse (by size).  All device work of a context is
+  // ordered on its one stream, so a block freed by one call can be handed to
+  // the next without waiting: the new owner's work queues after the old one's.
+  std::multimap<size_t, void*> pool;
+  size_t pool_bytes = 0;
+  void release_pool();
   // profiling: totals cover the tensor-core conv launches; other labelled
   // kernels (attention) are kept per label only
   bool prof = false;

@@ -120,6 +120,10 @@ class CudaHubert:
         check(lib.rvc_cuda_hubert_encode(self.handle, B, T, fptr(xb), version, fptr(out)))
         return out
 
+    def out_frames(self, T: int) -> int:
+        """Feature frames of a ``T``-sample input."""
+        return out_len(T)
+
     def encode(self, x: np.ndarray, version: int = 2) -> np.ndarray:
         """``HubertEncoder.encode``: ``[1,T]`` (or ``[T]``) -> ``[1,L,C]``."""
         if version not in (1, 2):

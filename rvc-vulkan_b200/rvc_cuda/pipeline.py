@@ -185,14 +185,28 @@ class Pipeline:
             step = min(self.t_center, t_max)
             opt_ts = dsp.split_points(audio, self.t_query, step, self.window)
 
+        audio_pad = np.pad(audio, (self.t_pad, self.t_pad), mode="reflect")   # :799 / :819
+        total = len(opt_ts) + 1
+        bounds, s = [], 0
+        for t in opt_ts:                                              # :840-846
+            t = t // self.window * self.window
+            bounds.append((s, t))
+            s = t
+        bounds.append((s, None))
+        blocks = []                                                   # (idx, s0, e0, chunk audio)
+        for idx, (s0, e0) in enumerate(bounds):
+            blk = audio_pad[s0:] if e0 is None else audio_pad[s0:e0 + self.t_pad2 + self.window]
+            if blk.shape[0] >= self.window * 10:
+                blocks.append((idx, s0, e0, np.asarray(blk, dtype=np.float32)))
+        noise = self._prefetch_noise(model, net_g, [b[3].shape[0] for b in blocks])
+
         t1 = time.perf_counter()
-        audio_pad_f0 = np.pad(audio, (self.t_pad, self.t_pad), mode="reflect")
-        seg_pts = [0] + [o + self.t_pad for o in opt_ts] + [audio_pad_f0.shape[0]]
+        seg_pts = [0] + [o + self.t_pad for o in opt_ts] + [audio_pad.shape[0]]
         pitch_parts, pitchf_parts = [], []
         for si in range(len(seg_pts) - 1):                            # :800-813
             ap, bp = seg_pts[si], seg_pts[si + 1]
-            b = min(bp + self.t_pad2 + self.window, audio_pad_f0.shape[0])
-            seg = audio_pad_f0[ap:b]
+            b = min(bp + self.t_pad2 + self.window, audio_pad.shape[0])
+            seg = audio_pad[ap:b]
             pi, pfi = self.get_f0(seg, seg.shape[0] // self.window, f0_up_key, f0_method)
             core_n = max(1, (bp - ap) // self.window)
             pitch_parts.append(pi[:core_n])
@@ -200,36 +214,22 @@ class Pipeline:
         pitch = np.concatenate(pitch_parts)[None, :]
         pitchf = np.concatenate(pitchf_parts).astype(np.float32)[None, :]
         times[1] += time.perf_counter() - t1
-        audio_pad = audio_pad_f0                                      # same reflect pad, :819
-
-        total = len(opt_ts) + 1
         if progress_cb is not None:
             progress_cb(0, total, "split into %d chunks" % total)
-        bounds, s = [], 0
-        for t in opt_ts:                                              # :840-846
-            t = t // self.window * self.window
-            bounds.append((s, t))
-            s = t
-        bounds.append((s, None))
 
-        blocks = []                                                   # (idx, audio, pitch, pitchf)
-        for idx, (s0, e0) in enumerate(bounds):
+        pitches = []
+        for idx, s0, e0, _ in blocks:
             if e0 is None:
-                blk = audio_pad[s0:]
-                p, pf = pitch[:, s0 // self.window:], pitchf[:, s0 // self.window:]
+                pitches.append((pitch[:, s0 // self.window:], pitchf[:, s0 // self.window:]))
             else:
-                blk = audio_pad[s0:e0 + self.t_pad2 + self.window]
-                p = pitch[:, s0 // self.window:(e0 + self.t_pad2) // self.window]
-                pf = pitchf[:, s0 // self.window:(e0 + self.t_pad2) // self.window]
-            if blk.shape[0] < self.window * 10:
-                continue
-            blocks.append((idx, np.asarray(blk, dtype=np.float32), p, pf))
+                pitches.append((pitch[:, s0 // self.window:(e0 + self.t_pad2) // self.window],
+                                pitchf[:, s0 // self.window:(e0 + self.t_pad2) // self.window]))
 
-        feats_all = self._encode(model, [b[1] for b in blocks], version)
-        preps = [self._vc_prepare(sid, b[1].shape[0], b[2], b[3], f, index, index_rate, protect, times,
-                                  retrieval_mode, brute_mix) for b, f in zip(blocks, feats_all)]
+        feats_all = self._encode(model, [b[3] for b in blocks], version)
+        preps = [self._vc_prepare(sid, b[3].shape[0], p[0], p[1], f, index, index_rate, protect, times,
+                                  retrieval_mode, brute_mix) for b, p, f in zip(blocks, pitches, feats_all)]
         t2 = time.perf_counter()
-        waves = self._decode(net_g, preps)
+        waves = self._decode(net_g, preps, noise)
         times[2] += time.perf_counter() - t2
 
         results = [None] * len(bounds)
@@ -257,11 +257,35 @@ class Pipeline:
         return [np.asarray(model.encode(a[None, :], version=version), dtype=np.float32) for a in audios]
 
     @staticmethod
-    def _decode(net_g, preps):
+    def _prefetch_noise(model, net_g, chunk_lengths):
+        """Draw every chunk's synthesizer noise on a host thread while the
+        device runs f0 and HuBERT (``RandomState`` fills release the GIL).
+        Needs the frame count before encoding: ``model.out_frames(T)``
+        (``CudaHubert``) and ``net_g.make_noise`` (``CudaSynthesizer``)."""
+        if not (hasattr(net_g, "make_noise") and hasattr(net_g, "prep_dec") and hasattr(net_g, "decode_batch")
+                and hasattr(model, "out_frames")) or not chunk_lengths:
+            return None
+        from concurrent.futures import ThreadPoolExecutor  # noqa: PLC0415
+        ex = ThreadPoolExecutor(max_workers=1, thread_name_prefix="rvc-noise")
+        jobs = []
+        for n in chunk_lengths:
+            P = 2 * int(model.out_frames(n))
+            jobs.append((P, ex.submit(net_g.make_noise, P)))
+        ex.shutdown(wait=False)
+        return jobs
+
+    @staticmethod
+    def _decode(net_g, preps, noise=None):
         """Waveforms of every chunk: ``prep_dec`` + one ``decode_batch`` when the
-        synthesizer offers them, else ``infer`` per chunk."""
-        if hasattr(net_g, "prep_dec") and hasattr(net_g, "decode_batch") and len(preps) > 1:
-            dps = [net_g.prep_dec(p["feats"], p["pitch"], p["pitchf"], p["sid_arr"]) for p in preps]
+        synthesizer offers them (with the prefetched noise where its frame count
+        matches), else ``infer`` per chunk."""
+        if hasattr(net_g, "prep_dec") and hasattr(net_g, "decode_batch") and (len(preps) > 1 or noise):
+            dps = []
+            for i, p in enumerate(preps):
+                kw = {}
+                if noise is not None and noise[i][0] == p["feats"].shape[1]:
+                    kw["noise"] = noise[i][1].result()
+                dps.append(net_g.prep_dec(p["feats"], p["pitch"], p["pitchf"], p["sid_arr"], **kw))
             return net_g.decode_batch(dps)
         return [np.asarray(net_g.infer(np.asarray(p["feats"], dtype=np.float32), p["pitch"], p["pitchf"],
                                        p["sid_arr"], phone_gpu=None))[0, 0] for p in preps]

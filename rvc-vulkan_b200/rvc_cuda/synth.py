@@ -187,9 +187,11 @@ class CudaSynthesizer:
         return out.reshape(1, 1, -1)
 
     # ---------------------------------------------------------------- batched decode
-    def prep_dec(self, phone, pitch, nsff0, sid, seed=None, skip_head=None, return_length=None, phone_gpu=None):
+    def prep_dec(self, phone, pitch, nsff0, sid, seed=None, skip_head=None, return_length=None, phone_gpu=None,
+                 noise=None):
         """``SynthesizerTrn.prep_dec`` (``runtime/models/vits.py:2478-2500``): draws the
-        chunk's noise in the reference's order and keeps the inputs for
+        chunk's noise in the reference's order (or takes ``noise = (nz, ns)``
+        drawn beforehand by ``make_noise``) and keeps the inputs for
         ``decode_batch`` (the whole model runs there, batched on the device)."""
         phone = np.asarray(phone, dtype=np.float32)
         P = phone.shape[1]
@@ -199,7 +201,7 @@ class CudaSynthesizer:
                 raise ValueError(f"skip_head/return_length out of range: P={P}, head={head}, length={length}")
         else:
             head = length = None
-        nz, ns = self.make_noise(P, seed)
+        nz, ns = self.make_noise(P, seed) if noise is None else noise
         return {"phone": phone, "pitch": np.asarray(pitch), "nsff0": np.asarray(nsff0, dtype=np.float32),
                 "sid": np.asarray(sid), "nz": nz, "ns": ns, "head": head, "length": length}
 
