@@ -254,6 +254,20 @@ int32_t rvc_cuda_index_blend(int64_t index, const float* q, int64_t F, int32_t D
                              double index_rate, const float* feats, float* out);
 int32_t rvc_cuda_index_blend_device(int64_t index, const float* q, int64_t F, int32_t D, int32_t k, int32_t mode,
                                     double index_rate, const float* feats, float* out);
+/* Inverted-file (IVF) structure of runtime/ivf_index.py:121-483: centroids
+ * [nlist,D] and the bucket of every index row, assignments [N] in [0, nlist)
+ * (IVFIndex.centroids / _assignments).  Host pointers. */
+int32_t rvc_cuda_index_set_ivf(int64_t index, const float* centroids, int32_t nlist, const int64_t* assignments);
+/* runtime/pipeline.py:_ivf_strict_search (:66-161): per query row its nprobe
+ * nearest centroids (nprobe clipped to nlist, at most 16), then the k nearest
+ * rows of the union of those buckets: scores [F,k] / inds [F,k], inf / -1
+ * past the rows the buckets hold.  Host pointers. */
+int32_t rvc_cuda_index_ivf_search(int64_t index, const float* q, int64_t F, int32_t D, int32_t k, int32_t nprobe,
+                                  float* scores, int64_t* inds);
+/* The pipeline's blend (mode 0 above) over the IVF search results
+ * (runtime/pipeline.py:523-527, :563-566).  Host pointers. */
+int32_t rvc_cuda_index_ivf_blend(int64_t index, const float* q, int64_t F, int32_t D, int32_t k, int32_t nprobe,
+                                 double index_rate, const float* feats, float* out);
 
 /* ---------------------------------------------------------------- pipeline DSP
  * The signal-processing steps of Pipeline.pipeline / _vc_prepare run on the

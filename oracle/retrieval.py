@@ -60,3 +60,72 @@ def blend(query, db, k=8):
 def mix(feats, blended, index_rate):
     """``blend * index_rate + feats * (1 - index_rate)`` (``runtime/pipeline.py:563-566``)."""
     return blended * index_rate + np.asarray(feats, dtype=F32) * (1 - index_rate)
+
+
+def ivf_buckets(assignments, nlist):
+    """Row ids per bucket, stable (``IVFIndex._rebuild_buckets``,
+    ``runtime/ivf_index.py:272-284``)."""
+    a = np.asarray(assignments, dtype=np.int64)
+    order = np.argsort(a, kind="stable")
+    counts = np.bincount(a, minlength=nlist)
+    return [b.astype(np.int64, copy=False) for b in np.split(order, np.cumsum(counts)[:-1])]
+
+
+def ivf_strict_search(centroids, vecs, buckets, query, k=8, nprobe=1):
+    """``_ivf_strict_search`` (``runtime/pipeline.py:66-161``): per query row
+    the ``nprobe`` nearest centroids (fp32 ``q2 + c2 - 2 q.c``, clamped at 0;
+    ``argmin`` for one probe, ``argpartition`` otherwise), then the k nearest
+    rows of the union of those buckets (fp32 distances), padded with inf / -1."""
+    query = np.asarray(query, dtype=F32)
+    centroids = np.asarray(centroids, dtype=F32)
+    vecs = np.asarray(vecs, dtype=F32)
+    F = query.shape[0]
+    q2 = np.einsum("fd,fd->f", query, query)
+    c2 = np.einsum("nd,nd->n", centroids, centroids)
+    dist = q2[:, None] + c2[None, :] - 2.0 * (query @ centroids.T)
+    np.maximum(dist, 0.0, out=dist)
+    nprobe = min(nprobe, centroids.shape[0])
+    scores = np.full((F, k), np.inf, dtype=F32)
+    inds = np.full((F, k), -1, dtype=np.int64)
+    if nprobe == 1:
+        top = np.argmin(dist, axis=1)
+        d2 = np.einsum("nd,nd->n", vecs, vecs)
+        for f in range(F):
+            cand = buckets[top[f]]
+            if cand.size == 0:
+                continue
+            kk = min(k, cand.size)
+            d = q2[f] + d2[cand] - 2.0 * (query[f] @ vecs[cand].T)
+            np.maximum(d, 0.0, out=d)
+            if kk >= cand.size:
+                order = np.argsort(d)
+            else:
+                p = np.argpartition(d, kk - 1)[:kk]
+                order = p[np.argsort(d[p])]
+            inds[f, :kk] = cand[order]
+            scores[f, :kk] = d[order]
+        return scores, inds
+    top = np.argpartition(dist, nprobe - 1, axis=1)[:, :nprobe]
+    for f in range(F):
+        cand = np.concatenate([buckets[b] for b in top[f] if buckets[b].size] or [np.zeros(0, np.int64)])
+        if cand.size == 0:
+            continue
+        s, ix = search_l2(query[f:f + 1], vecs[cand], k=min(k, cand.size))
+        inds[f, :ix.shape[1]] = cand[ix[0]]
+        scores[f, :s.shape[1]] = s[0]
+    return scores, inds
+
+
+def ivf_blend(vecs, scores, inds):
+    """The pipeline's IVF blend (``runtime/pipeline.py:523-527``): rows by
+    index (zero vectors for -1, ``IVFIndex.vectors_by_rows``), ``w = (1/score)^2``
+    row-normalised, weighted sum."""
+    vecs = np.asarray(vecs, dtype=F32)
+    flat = inds.reshape(-1)
+    blk = np.zeros((flat.size, vecs.shape[1]), dtype=F32)
+    ok = flat >= 0
+    blk[ok] = vecs[flat[ok]]
+    blk = blk.reshape(inds.shape + (vecs.shape[1],))
+    w = np.square(1.0 / scores)
+    w /= np.maximum(w.sum(axis=1, keepdims=True), 1e-12)
+    return np.sum(blk * w[:, :, None], axis=1)

@@ -766,6 +766,33 @@ int32_t rvc_cuda_index_blend_device(int64_t index, const float* q, int64_t F, in
   });
 }
 
+int32_t rvc_cuda_index_set_ivf(int64_t index, const float* centroids, int32_t nlist, const int64_t* assignments) {
+  return on_index(index, [&](IndexModel* m) {
+    RVC_CHECK_ARG(centroids && assignments && nlist >= 1, "index_set_ivf: bad arguments");
+    m->set_ivf(centroids, nlist, assignments);
+  });
+}
+
+int32_t rvc_cuda_index_ivf_search(int64_t index, const float* q, int64_t F, int32_t D, int32_t k, int32_t nprobe,
+                                  float* scores, int64_t* inds) {
+  return on_index(index, [&](IndexModel* m) {
+    RVC_CHECK_ARG(D == m->D, "index_ivf_search: query width does not match the index");
+    RVC_CHECK_ARG(F >= 0 && (F == 0 || (q && scores && inds)), "index_ivf_search: bad arguments");
+    m->ivf_search_host(q, F, k, nprobe, scores, inds);
+    finish(m->ctx);
+  });
+}
+
+int32_t rvc_cuda_index_ivf_blend(int64_t index, const float* q, int64_t F, int32_t D, int32_t k, int32_t nprobe,
+                                 double index_rate, const float* feats, float* out) {
+  return on_index(index, [&](IndexModel* m) {
+    RVC_CHECK_ARG(D == m->D, "index_ivf_blend: query width does not match the index");
+    RVC_CHECK_ARG(F >= 0 && (F == 0 || (q && out)), "index_ivf_blend: bad arguments");
+    m->ivf_blend_host(q, F, k, nprobe, (float)index_rate, (float)(1.0 - index_rate), feats, out);
+    finish(m->ctx);
+  });
+}
+
 // ----------------------------------------------------------------- RMVPE
 int32_t rvc_cuda_rmvpe_create(int64_t ctx, int64_t* model) {
   return on_ctx(ctx, [&](Context* c) {

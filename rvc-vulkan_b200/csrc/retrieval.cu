@@ -21,6 +21,7 @@
 
 #include <cfloat>
 #include <cmath>
+#include <vector>
 
 namespace rvc {
 
@@ -259,6 +260,86 @@ __global__ void blend_kernel(const float* __restrict__ db, int D, const float* _
 
 constexpr int kRows = 8;  // warps (query rows) per 256-thread block
 
+// IVF bucket scan: one 256-thread block per query.  The query's rows are the
+// union of its nprobe buckets; each warp takes every 8th row, forms the exact
+// distance sum((q - v)^2) in float64 and keeps its k best (distance, row) in
+// lanes 0..k-1 (ties to the lower row); the 8 lists are merged at the end.
+constexpr int kIvfWarps = 8;
+
+__device__ __forceinline__ bool before_d(double d1, int i1, double d2, int i2) {
+  if (d1 != d2) return d1 < d2;
+  return (unsigned)i1 < (unsigned)i2;  // -1 (empty) sorts last
+}
+
+__global__ void ivf_scan_kernel(const float* __restrict__ q, const float* __restrict__ db, int D,
+                                const int* __restrict__ rows, const long long* __restrict__ off,
+                                const long long* __restrict__ probe, int nprobe, int k,
+                                float* __restrict__ scores, long long* __restrict__ inds) {
+  extern __shared__ float qs[];
+  __shared__ double md[kIvfWarps][IndexModel::kMaxK];
+  __shared__ int mi[kIvfWarps][IndexModel::kMaxK];
+  const long long f = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) qs[d] = q[f * D + d];
+  __syncthreads();
+  double bd = INFINITY;
+  int bi = -1;
+  long long seen = 0;  // running row count over the probed buckets (this warp's share is every 8th)
+  for (int p = 0; p < nprobe; ++p) {
+    const long long b = probe[f * nprobe + p];
+    if (b < 0) continue;
+    const long long r0 = off[b], r1 = off[b + 1];
+    for (long long r = r0 + ((warp - seen) % kIvfWarps + kIvfWarps) % kIvfWarps; r < r1; r += kIvfWarps) {
+      const int g = rows[r];
+      const float* v = db + (long long)g * D;
+      double s = 0.0;
+      for (int d = lane; d < D; d += 32) {
+        const double t = (double)qs[d] - (double)v[d];
+        s = fma(t, t, s);
+      }
+      s = warp_sum_d(s);
+      const double wd = __shfl_sync(0xffffffffu, bd, k - 1);
+      const int wi = __shfl_sync(0xffffffffu, bi, k - 1);
+      if (before_d(s, g, wd, wi)) {
+        const bool gt = lane < k && before_d(s, g, bd, bi);  // the new entry goes before this lane's
+        const unsigned m = __ballot_sync(0xffffffffu, gt);
+        const int pos = m ? __ffs(m) - 1 : k;
+        const double ud = __shfl_up_sync(0xffffffffu, bd, 1);
+        const int ui = __shfl_up_sync(0xffffffffu, bi, 1);
+        if (lane < k && lane > pos) {
+          bd = ud;
+          bi = ui;
+        } else if (lane == pos) {
+          bd = s;
+          bi = g;
+        }
+      }
+    }
+    seen += r1 - r0;
+  }
+  if (lane < k) {
+    md[warp][lane] = bd;
+    mi[warp][lane] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int head[kIvfWarps];
+    for (int w = 0; w < kIvfWarps; ++w) head[w] = 0;
+    for (int t = 0; t < k; ++t) {
+      int bw = -1;
+      for (int w = 0; w < kIvfWarps; ++w) {
+        if (head[w] >= k) continue;
+        if (bw < 0 || before_d(md[w][head[w]], mi[w][head[w]], md[bw][head[bw]], mi[bw][head[bw]])) bw = w;
+      }
+      const double dd = md[bw][head[bw]];
+      const int ii = mi[bw][head[bw]];
+      ++head[bw];
+      scores[f * k + t] = ii >= 0 ? (float)dd : INFINITY;
+      inds[f * k + t] = ii;
+    }
+  }
+}
+
 }  // namespace
 
 IndexModel::IndexModel(Context* c, const float* db, int64_t n, int d, int prec) : ctx(c), precision(prec) {
@@ -354,6 +435,97 @@ void IndexModel::blend_device(const float* q, int64_t F, int k, int mode, float 
     note_launch();
     RVC_CUDA_TRY(cudaGetLastError());
   }
+}
+
+void IndexModel::set_ivf(const float* centroids, int nl, const int64_t* assignments) {
+  RVC_CHECK_ARG(nl >= 1 && centroids && assignments, "index_set_ivf: need nlist >= 1 centroids and assignments");
+  std::vector<int64_t> cnt((size_t)nl + 1, 0);
+  for (int64_t i = 0; i < N; ++i) {
+    RVC_CHECK_ARG(assignments[i] >= 0 && assignments[i] < nl, "index_set_ivf: assignment " +
+                                                                   std::to_string(assignments[i]) + " of row " +
+                                                                   std::to_string(i) + " outside [0, nlist)");
+    ++cnt[(size_t)assignments[i] + 1];
+  }
+  for (int b = 0; b < nl; ++b) cnt[(size_t)b + 1] += cnt[(size_t)b];
+  std::vector<int> order((size_t)N);
+  std::vector<int64_t> fill(cnt.begin(), cnt.end() - 1);
+  for (int64_t i = 0; i < N; ++i) order[(size_t)fill[(size_t)assignments[i]]++] = (int)i;  // stable, like argsort(kind="stable")
+  cent_ = std::make_unique<IndexModel>(ctx, centroids, nl, D, precision);
+  cudaStream_t st = ctx->stream;
+  bucket_rows_ = DevBuf(ctx, sizeof(int) * (size_t)N);
+  bucket_off_ = DevBuf(ctx, sizeof(int64_t) * ((size_t)nl + 1));
+  RVC_CUDA_TRY(cudaMemcpyAsync(bucket_rows_.p, order.data(), bucket_rows_.bytes, cudaMemcpyHostToDevice, st));
+  RVC_CUDA_TRY(cudaMemcpyAsync(bucket_off_.p, cnt.data(), bucket_off_.bytes, cudaMemcpyHostToDevice, st));
+  RVC_CUDA_TRY(cudaStreamSynchronize(st));
+  nlist = nl;
+}
+
+void IndexModel::ivf_search_device(const float* q, int64_t F, int k, int nprobe, float* scores, int64_t* inds) {
+  RVC_CHECK_ARG(nlist > 0, "index_ivf_search: the index has no IVF structure (set_ivf first)");
+  RVC_CHECK_ARG(k >= 1 && k <= kMaxK, "index_ivf_search: k must be in [1, 16]");
+  RVC_CHECK_ARG(nprobe >= 1, "index_ivf_search: nprobe must be >= 1");
+  RVC_CHECK_ARG(D <= 8192, "index_ivf_search: D above 8192");
+  nprobe = std::min(nprobe, nlist);
+  RVC_CHECK_ARG(nprobe <= kMaxK, "index_ivf_search: nprobe above 16 is not served");
+  if (F == 0) return;
+  if (F > probe_rows_) {
+    probe_sc_ = DevBuf();
+    probe_ix_ = DevBuf();
+    probe_sc_ = DevBuf(ctx, sizeof(float) * (size_t)F * kMaxK);
+    probe_ix_ = DevBuf(ctx, sizeof(int64_t) * (size_t)F * kMaxK);
+    probe_rows_ = F;
+  }
+  cent_->search_device(q, F, nprobe, probe_sc_.f(), probe_ix_.as<int64_t>());
+  ivf_scan_kernel<<<(unsigned)F, 32 * kIvfWarps, sizeof(float) * (size_t)D, ctx->stream>>>(
+      q, db_.f(), D, bucket_rows_.as<int>(), bucket_off_.as<long long>(), probe_ix_.as<long long>(), nprobe, k,
+      scores, (long long*)inds);
+  note_launch();
+  RVC_CUDA_TRY(cudaGetLastError());
+}
+
+void IndexModel::ivf_blend_device(const float* q, int64_t F, int k, int nprobe, float c_blend, float c_feats,
+                                  const float* feats, float* out) {
+  if (F == 0) return;
+  if (F > ivf_rows_) {
+    ivf_sc_ = DevBuf();
+    ivf_ix_ = DevBuf();
+    ivf_sc_ = DevBuf(ctx, sizeof(float) * (size_t)F * kMaxK);
+    ivf_ix_ = DevBuf(ctx, sizeof(int64_t) * (size_t)F * kMaxK);
+    ivf_rows_ = F;
+  }
+  ivf_search_device(q, F, k, nprobe, ivf_sc_.f(), ivf_ix_.as<int64_t>());
+  blend_kernel<<<(unsigned)((F + kRows - 1) / kRows), 32 * kRows, 0, ctx->stream>>>(
+      db_.f(), D, ivf_sc_.f(), ivf_ix_.as<long long>(), F, k, 0, c_blend, c_feats, feats, out);
+  note_launch();
+  RVC_CUDA_TRY(cudaGetLastError());
+}
+
+void IndexModel::ivf_search_host(const float* q, int64_t F, int k, int nprobe, float* scores, int64_t* inds) {
+  if (F <= 0) return;
+  cudaStream_t st = ctx->stream;
+  stage(h_q_, sizeof(float) * (size_t)F * D);
+  stage(h_s_, sizeof(float) * (size_t)F * k);
+  stage(h_i_, sizeof(int64_t) * (size_t)F * k);
+  RVC_CUDA_TRY(cudaMemcpyAsync(h_q_.p, q, sizeof(float) * (size_t)F * D, cudaMemcpyHostToDevice, st));
+  ivf_search_device(h_q_.f(), F, k, nprobe, h_s_.f(), h_i_.as<int64_t>());
+  RVC_CUDA_TRY(cudaMemcpyAsync(scores, h_s_.p, sizeof(float) * (size_t)F * k, cudaMemcpyDeviceToHost, st));
+  RVC_CUDA_TRY(cudaMemcpyAsync(inds, h_i_.p, sizeof(int64_t) * (size_t)F * k, cudaMemcpyDeviceToHost, st));
+}
+
+void IndexModel::ivf_blend_host(const float* q, int64_t F, int k, int nprobe, float c_blend, float c_feats,
+                                const float* feats, float* out) {
+  if (F <= 0) return;
+  cudaStream_t st = ctx->stream;
+  const size_t nb = sizeof(float) * (size_t)F * D;
+  stage(h_q_, nb);
+  stage(h_o_, nb);
+  RVC_CUDA_TRY(cudaMemcpyAsync(h_q_.p, q, nb, cudaMemcpyHostToDevice, st));
+  if (feats) {
+    stage(h_f_, nb);
+    RVC_CUDA_TRY(cudaMemcpyAsync(h_f_.p, feats, nb, cudaMemcpyHostToDevice, st));
+  }
+  ivf_blend_device(h_q_.f(), F, k, nprobe, c_blend, c_feats, feats ? h_f_.f() : nullptr, h_o_.f());
+  RVC_CUDA_TRY(cudaMemcpyAsync(out, h_o_.p, nb, cudaMemcpyDeviceToHost, st));
 }
 
 void IndexModel::stage(DevBuf& b, size_t bytes) {

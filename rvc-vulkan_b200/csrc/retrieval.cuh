@@ -4,6 +4,8 @@
 
 #include "layer.cuh"
 
+#include <memory>
+
 namespace rvc {
 
 class IndexModel {
@@ -24,8 +26,21 @@ class IndexModel {
   void search_host(const float* q, int64_t F, int k, float* scores, int64_t* inds);
   void blend_host(const float* q, int64_t F, int k, int mode, float c_blend, float c_feats, const float* feats,
                   float* out);
+  // Inverted-file structure (runtime/ivf_index.py:121-483): centroids [nlist][D]
+  // (host) and the bucket of every index row (host [N], values in [0, nlist)).
+  void set_ivf(const float* centroids, int nlist, const int64_t* assignments);
+  // runtime/pipeline.py:_ivf_strict_search (:66-161) on device pointers: per
+  // query the nprobe nearest centroids, then the k nearest rows of those
+  // buckets; scores/inds [F][k], inf / -1 where the buckets hold fewer rows.
+  void ivf_search_device(const float* q, int64_t F, int k, int nprobe, float* scores, int64_t* inds);
+  void ivf_blend_device(const float* q, int64_t F, int k, int nprobe, float c_blend, float c_feats,
+                        const float* feats, float* out);
+  void ivf_search_host(const float* q, int64_t F, int k, int nprobe, float* scores, int64_t* inds);
+  void ivf_blend_host(const float* q, int64_t F, int k, int nprobe, float c_blend, float c_feats,
+                      const float* feats, float* out);
   int64_t N = 0, Npad = 0;
   int D = 0;
+  int nlist = 0;
   Context* ctx;
   int precision;
 
@@ -36,6 +51,10 @@ class IndexModel {
   int64_t ws_rows_ = 0;
   DevBuf dot_, q2_, cand_, sc_, ix_;
   DevBuf h_q_, h_f_, h_o_, h_s_, h_i_;  // staging for the host-pointer calls
+  std::unique_ptr<IndexModel> cent_;    // brute-force index over the centroids
+  DevBuf bucket_rows_, bucket_off_;     // row ids grouped by bucket (stable), bucket offsets [nlist + 1]
+  DevBuf probe_sc_, probe_ix_, ivf_sc_, ivf_ix_;
+  int64_t probe_rows_ = 0, ivf_rows_ = 0;
   void stage(DevBuf& b, size_t bytes);
 };
 

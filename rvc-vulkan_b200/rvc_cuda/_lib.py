@@ -118,6 +118,9 @@ _SIGS = {
     "rvc_cuda_index_search_device": ([_i64, _p, _i64, _i32, _i32, _p, _p], _i32),
     "rvc_cuda_index_blend": ([_i64, _fp, _i64, _i32, _i32, _i32, _f64, _fp, _fp], _i32),
     "rvc_cuda_index_blend_device": ([_i64, _p, _i64, _i32, _i32, _i32, _f64, _p, _p], _i32),
+    "rvc_cuda_index_set_ivf": ([_i64, _fp, _i32, _ip64], _i32),
+    "rvc_cuda_index_ivf_search": ([_i64, _fp, _i64, _i32, _i32, _i32, _fp, _ip64], _i32),
+    "rvc_cuda_index_ivf_blend": ([_i64, _fp, _i64, _i32, _i32, _i32, _f64, _fp, _fp], _i32),
 }
 for _name, (_args, _ret) in _SIGS.items():
     _fn = getattr(lib, _name)

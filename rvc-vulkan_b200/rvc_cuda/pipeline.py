@@ -17,8 +17,8 @@ chunks, the frame alignment of pitch arrays (``:572-603``) and the f0
 post-processing of ``get_f0`` (``:468-482``, a few thousand values per call).
 
 Not offered here: the ``pm`` / ``fcpe`` f0 methods, output resampling
-(``resample_sr``), the IVF retrieval mode and ``brute_mix != 0``; asking for
-one raises ``NotImplementedError``.
+(``resample_sr``) and ``brute_mix != 0``; asking for one raises
+``NotImplementedError``.
 """
 
 from __future__ import annotations
@@ -106,18 +106,23 @@ class Pipeline:
     # ------------------------------------------------------------------ index
     @staticmethod
     def _resolve_index(file_index, index_rate):
-        """A ``CudaIndex`` for ``file_index`` (a ``CudaIndex``, an ``[N, D]``
-        array, or an object with ``ntotal`` / ``reconstruct_n`` such as the
-        reference's ``FeatureIndex``), or None (``runtime/pipeline.py:1227-1256``)."""
+        """The device index for ``file_index`` (``runtime/pipeline.py:1227-1256``):
+        a ``CudaIndex``, an ``[N, D]`` array, an object with ``ntotal`` /
+        ``reconstruct_n`` (the reference's ``FeatureIndex``: brute force) or an
+        ``IVFIndex`` (``vectors_by_rows``: inverted-file search), or None."""
         from . import retrieval  # noqa: PLC0415
         if index_rate == 0 or file_index is None or (isinstance(file_index, str) and file_index == ""):
             return None
         if isinstance(file_index, retrieval.CudaIndex):
             return file_index if file_index.N > 0 else None
         if isinstance(file_index, str):
-            raise NotImplementedError("index files are loaded by the caller: pass the index vectors or a CudaIndex")
+            raise NotImplementedError("index files are loaded by the caller: pass the index object or a CudaIndex")
         if getattr(file_index, "vectors_by_rows", None) is not None:
-            raise NotImplementedError("the IVF retrieval mode is not on the device path")
+            if getattr(file_index, "ntotal", 0) <= 0:
+                return None
+            if str(getattr(file_index, "metric", "L2")).upper() == "IP":
+                raise NotImplementedError("inner-product (IP) indexes are not supported by the L2 blend")
+            return retrieval._ivf_for(file_index)
         if isinstance(file_index, np.ndarray):
             vecs = file_index
         elif hasattr(file_index, "reconstruct_n") and hasattr(file_index, "ntotal"):
@@ -138,11 +143,14 @@ class Pipeline:
         feats = np.asarray(feats, dtype=np.float32)
         protecting = protect < 0.5 and pitch is not None and pitchf is not None
         feats0 = feats if protecting else None
-        if index is not None and index_rate != 0:
+        if index is not None and index_rate != 0:                   # :517-566
             if brute_mix != 0:
                 raise NotImplementedError("brute_mix != 0 is not on the device path")
-            feats = index.blend(feats[0], k=_K_SEARCH, mode="pipeline", feats=feats[0],
-                                index_rate=index_rate)[None]
+            if index.nlist and retrieval_mode != "brute":             # IVF index: strict bucket search
+                feats = index.ivf_blend(feats[0], k=_K_SEARCH, feats=feats[0], index_rate=index_rate)[None]
+            else:                                                     # brute force over every row
+                feats = index.blend(feats[0], k=_K_SEARCH, mode="pipeline", feats=feats[0],
+                                    index_rate=index_rate)[None]
         feats = dsp.interpolate_linear(feats, scale_factor=2, axis=1)
         if protecting:
             feats0 = dsp.interpolate_linear(feats0, scale_factor=2, axis=1)

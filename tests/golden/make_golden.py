@@ -185,6 +185,54 @@ def run_retrieval(retrieval, name, F, N, D, k, iseed, qseed, meta):
                   "inputs_sha256": digest([db, q])}
 
 
+# (name, N, D, nlist, F, seed, far-centroid edge case)
+IVF_CASES = [
+    ("ivf_n8000_d256", 8000, 256, 32, 120, 1, False),
+    ("ivf_n40_d16_edge", 40, 16, 8, 30, 2, True),
+]
+
+
+def run_ivf(name, N, D, nlist, F, seed, edge, meta):
+    """The reference's IVF search (``runtime/pipeline.py:_ivf_strict_search``)
+    over an ``IVFIndex`` trained by its own mini-batch k-means, for nprobe 1
+    and 3, and the pipeline's IVF blend through ``Pipeline._vc_prepare`` with
+    the ``IVFIndex`` as the index (index_rate 0.75).  Centroids and bucket
+    assignments are stored (the k-means is the reference's code)."""
+    from runtime import pipeline as rp  # noqa: PLC0415
+    from runtime.ivf_index import IVFIndex  # noqa: PLC0415
+    sys.path.insert(0, HERE)
+    import pipeline_fakes as pf  # noqa: PLC0415
+    vecs = syn.make_index(N, D, 100 + seed)
+    q = syn.make_queries(F, D, 200 + seed)
+    ivf = IVFIndex(dim=D, nlist=nlist, nprobe=1)
+    ivf.train(vecs, seed=seed)
+    if edge:  # two centroids far from every row: empty buckets; queries next to one of them
+        c = ivf.centroids.copy()
+        c[-1] = 0.0
+        c[-1, 0] = 40.0
+        c[-2] = 0.0
+        c[-2, 1] = -40.0
+        ivf.set_centroids(c)
+        q[:5] = c[-1] + 0.01 * q[:5]
+    ivf.add(vecs)
+    rec = {"centroids": ivf.centroids, "assignments": ivf._assignments.astype(np.int32)}
+    for npb in (1, 3):
+        sc, ix = rp._ivf_strict_search(ivf, q, k=8, nprobe=npb)
+        rec[f"scores_p{npb}"], rec[f"inds_p{npb}"] = sc, ix
+    feats = (q[None] * 0.5).astype(np.float32)
+    P = F
+    pitch = np.ones((1, 2 * P), np.int64) * 60
+    pitchf = np.full((1, 2 * P), 150.0, np.float32)
+    pitchf[0, ::3] = 0.0
+    pipe = rp.Pipeline(40000, pf.config())
+    prep = pipe._vc_prepare(None, 0, np.zeros(2 * P * 160 + 400, np.float32), pitch, pitchf, [0.0, 0.0, 0.0], ivf,
+                            None, 0.75, 2, 0.33, feats=feats)
+    rec["prep_feats"] = prep["feats"]
+    np.savez_compressed(os.path.join(HERE, name + ".npz"), **rec)
+    meta[name] = {"kind": "ivf", "N": N, "D": D, "nlist": int(ivf.nlist), "F": F, "seed": seed, "edge": edge,
+                  "inputs_sha256": digest([vecs, q])}
+
+
 def run_ops(nn, meta):
     """Per-op vectors from ``runtime.nn``'s numpy kernels (``_conv1d_numpy`` etc.)."""
     rs = np.random.RandomState(4242)
@@ -312,7 +360,7 @@ PIPE_CASES = [
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("RVC_REFERENCE", "/root/reference"))
-    ap.add_argument("--only", choices=["vits", "hubert", "ops", "retrieval", "rmvpe", "partial", "dsp"], default=None,
+    ap.add_argument("--only", choices=["vits", "hubert", "ops", "retrieval", "rmvpe", "partial", "dsp", "ivf"], default=None,
                     help="regenerate one family and keep the other fixtures")
     args = ap.parse_args()
     os.environ["RVC_BACKEND"] = "numpy"
@@ -345,6 +393,9 @@ def main():
             run_rmvpe(runtime_rmvpe, *c, meta)
     if args.only in (None, "dsp"):
         run_dsp(meta)
+    if args.only in (None, "ivf"):
+        for c in IVF_CASES:
+            run_ivf(*c, meta)
     if args.only in (None, "retrieval"):
         from runtime import retrieval  # noqa: PLC0415
         for c in RETRIEVAL_CASES:

@@ -106,9 +106,12 @@ def test_retrieval_patch_reference_replaces_module_functions():
     from rvc_cuda import retrieval
 
     ret_mod = types.SimpleNamespace(search_l2=lambda *a, **k: "numpy", weighted_blend=lambda *a, **k: "numpy")
-    pipe_mod = types.SimpleNamespace(search_l2=ret_mod.search_l2)
+    pipe_mod = types.SimpleNamespace(search_l2=ret_mod.search_l2, _ivf_strict_search=lambda *a, **k: "numpy")
     retrieval.patch_reference(ret_mod, pipe_mod)
     assert ret_mod.search_l2 is retrieval.search_l2 and pipe_mod.search_l2 is retrieval.search_l2
+    assert pipe_mod._ivf_strict_search is retrieval.ivf_strict_search
+    with pytest.raises(NotImplementedError):  # inner-product indexes are refused before any device work
+        retrieval.ivf_strict_search(types.SimpleNamespace(metric="IP"), np.zeros((1, 4), np.float32))
     assert ret_mod.weighted_blend is retrieval.weighted_blend
     assert ret_mod._rvc_cuda_orig_search_l2() == "numpy"
 

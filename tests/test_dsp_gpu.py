@@ -207,6 +207,8 @@ def test_device_pipeline_end_to_end_against_oracle(monkeypatch):
         change_rms=OD.change_rms, to_int16=OD.to_int16)
 
     class _OracleIndex:
+        nlist = 0  # brute force (no IVF structure)
+
         def blend(self, q, k=8, mode="pipeline", feats=None, index_rate=1.0):
             from oracle import retrieval as OR
             sc, ix = OR.search_l2(q, db, k)

@@ -124,3 +124,35 @@ def test_partial_synthesis_oracle_matches_reference(name, golden_meta):
     g = load_golden(name)
     assert wav.size == g["wave"].size == m["length"] * m["upp"]
     assert np.abs(wav.reshape(-1) - g["wave"]).max() < 1e-5
+
+
+IVF = ["ivf_n8000_d256", "ivf_n40_d16_edge"]
+
+
+@pytest.mark.parametrize("name", IVF)
+def test_ivf_oracle_matches_reference(name, golden_meta):
+    """The restated IVF strict search and blend against the reference's own
+    ``_ivf_strict_search`` / ``_vc_prepare`` on the same index structure."""
+    from oracle import dsp as OD
+    m = golden_meta[name]
+    vecs = syn.make_index(m["N"], m["D"], 100 + m["seed"])
+    q = syn.make_queries(m["F"], m["D"], 200 + m["seed"])
+    if m["edge"]:
+        g0 = load_golden(name)
+        c = g0["centroids"]
+        q[:5] = c[-1] + 0.01 * q[:5]
+    g = load_golden(name)
+    buckets = OR.ivf_buckets(g["assignments"], g["centroids"].shape[0])
+    for npb in (1, 3):
+        sc, ix = OR.ivf_strict_search(g["centroids"], vecs, buckets, q, k=8, nprobe=npb)
+        np.testing.assert_array_equal(ix, g[f"inds_p{npb}"])
+        np.testing.assert_array_equal(sc, g[f"scores_p{npb}"])
+    # the pipeline's IVF blend, mix, x2 interpolation and protect (nprobe 1)
+    feats = (q[None] * 0.5).astype(np.float32)
+    sc, ix = OR.ivf_strict_search(g["centroids"], vecs, buckets, feats[0], k=8, nprobe=1)
+    mixed = (OR.ivf_blend(vecs, sc, ix)[None] * 0.75 + feats * (1 - 0.75)).astype(np.float32)
+    f = OD.interpolate_linear(mixed, 2, axis=1)
+    f0 = OD.interpolate_linear(feats, 2, axis=1)
+    pitchf = np.full((1, 2 * m["F"]), 150.0, np.float32)
+    pitchf[0, ::3] = 0.0
+    np.testing.assert_array_equal(OD.protect_blend(f, f0, pitchf, 0.33), g["prep_feats"])

@@ -104,3 +104,65 @@ def test_dropin_search_l2_caches_one_index_per_array():
     assert ret._index_for(db) is ret._index_for(db)
     np.testing.assert_array_equal(a[1], b[1])
     np.testing.assert_array_equal(a[1], OR.search_l2(q, db, 8)[1])
+
+
+IVF = ["ivf_n8000_d256", "ivf_n40_d16_edge"]
+
+
+def _ivf_object(vecs, centroids, assignments, nprobe=1):
+    """A stand-in with the ``IVFIndex`` attributes the pipeline reads."""
+    import types
+    return types.SimpleNamespace(centroids=centroids, _vectors=vecs, _assignments=np.asarray(assignments, np.int64),
+                                 nprobe=nprobe, ntotal=vecs.shape[0], metric="L2", buckets=[],
+                                 vectors_by_rows=lambda ix: vecs[ix])
+
+
+@pytest.mark.parametrize("name", IVF)
+def test_ivf_search_matches_reference_golden(name, golden_meta):
+    m = golden_meta[name]
+    g = load_golden(name)
+    vecs = syn.make_index(m["N"], m["D"], 100 + m["seed"])
+    q = syn.make_queries(m["F"], m["D"], 200 + m["seed"])
+    if m["edge"]:
+        q[:5] = g["centroids"][-1] + 0.01 * q[:5]
+    idx = ret.CudaIndex(vecs)
+    idx.set_ivf(g["centroids"], g["assignments"])
+    for npb in (1, 3):
+        sc, ix = idx.ivf_search(q, 8, npb)
+        assert sc.shape == (m["F"], 8) and ix.dtype == np.int64
+        np.testing.assert_array_equal(ix < 0, g[f"inds_p{npb}"] < 0)
+        _check_against_oracle(ix, sc, g[f"inds_p{npb}"], g[f"scores_p{npb}"])
+    # the device pipeline's IVF blend + mix + x2 interpolation + protect vs the reference's _vc_prepare
+    from rvc_cuda.pipeline import Pipeline
+    from tests.golden import pipeline_fakes as pf
+    feats = (q[None] * 0.5).astype(np.float32)
+    pitch = np.ones((1, 2 * m["F"]), np.int64) * 60
+    pitchf = np.full((1, 2 * m["F"]), 150.0, np.float32)
+    pitchf[0, ::3] = 0.0
+    pipe = Pipeline(40000, pf.config())
+    index = pipe._resolve_index(_ivf_object(vecs, g["centroids"], g["assignments"]), 0.75)
+    assert index.nlist == g["centroids"].shape[0]
+    prep = pipe._vc_prepare(0, 2 * m["F"] * 160 + 400, pitch, pitchf, feats, index, 0.75, 0.33, [0.0, 0.0, 0.0])
+    np.testing.assert_allclose(prep["feats"], g["prep_feats"], rtol=1e-5, atol=1e-5)
+
+
+def test_ivf_larger_index_against_oracle():
+    """50000 x 768, 128 buckets (centroids = sampled rows, rows assigned to the
+    nearest in float64 as IVFIndex._assign does), 200 queries, nprobe 1 and 4."""
+    vecs = syn.make_index(50000, 768, 11)
+    rs = np.random.RandomState(5)
+    cent = vecs[rs.choice(50000, 128, replace=False)] + 0.1 * rs.standard_normal((128, 768)).astype(np.float32)
+    v64, c64 = vecs.astype(np.float64), cent.astype(np.float64)
+    d = (v64 * v64).sum(1)[:, None] + (c64 * c64).sum(1)[None] - 2.0 * v64 @ c64.T
+    asg = np.argmin(d, axis=1)
+    q = syn.make_queries(200, 768, 11)
+    q[:100] = vecs[rs.choice(50000, 100)] + 0.3 * q[:100]
+    idx = ret.CudaIndex(vecs)
+    idx.set_ivf(cent, asg)
+    buckets = OR.ivf_buckets(asg, 128)
+    for npb in (1, 4):
+        sc, ix = idx.ivf_search(q, 8, npb)
+        rsc, rix = OR.ivf_strict_search(cent, vecs, buckets, q, 8, npb)
+        assert _check_against_oracle(ix, sc, rix, rsc) <= 2
+    with pytest.raises(ValueError):
+        ret.CudaIndex(syn.make_index(100, 16, 1)).ivf_search(np.zeros((2, 16), np.float32))
