@@ -295,6 +295,21 @@ int32_t rvc_cuda_protect(int64_t ctx, const float* feats, const float* feats0, c
 /* change_rms(data1, data2, sr1, sr2, rate) (runtime/pipeline.py:164-235). */
 int32_t rvc_cuda_change_rms(int64_t ctx, const float* d1, int64_t n1, int32_t sr1, const float* d2, int64_t n2,
                             int32_t sr2, double rate, float* out);
+/* Autocorrelation f0 ("pm", runtime/dsp/f0.py:24-94): frame i centred on
+ * i * hop, win samples (odd), mean removed, skipped (0) when its peak is below
+ * 1e-7, weighted by hann [win]; f0 = sr / lag of the largest normalised
+ * autocorrelation in [lag_min, lag_max] when above threshold, else 0.
+ * x [n] float64 -> f0 [n_frames] float32.  Host pointers. */
+int32_t rvc_cuda_f0_autocorr(int64_t ctx, const double* x, int64_t n, int32_t sr, int32_t hop, int32_t win,
+                             int32_t lag_min, int32_t lag_max, const double* hann, double threshold, float* f0,
+                             int64_t n_frames);
+/* runtime.dsp.resample.resample (runtime/dsp/resample.py:129): x [n_in]
+ * (float32 when x_f32 != 0, else float64) from orig_sr to target_sr ->
+ * y [n_out] float32, n_out = max(1, round(n_in * target_sr / orig_sr));
+ * method 0 = fft (spectral Kaiser-sinc interpolation, the pipeline's), 1 =
+ * linear (np.interp), 2 = sinc (time-domain Kaiser-sinc).  Host pointers. */
+int32_t rvc_cuda_resample(int64_t ctx, const void* x, int32_t x_f32, int64_t n_in, int32_t orig_sr,
+                          int32_t target_sr, int32_t method, float* y, int64_t n_out);
 /* Peak-normalised int16 conversion (runtime/pipeline.py:1208-1213). */
 int32_t rvc_cuda_to_int16(int64_t ctx, const float* x, int64_t n, int16_t* y);
 

@@ -195,3 +195,95 @@ def to_int16(audio):
     if audio_max > 1:
         max_int16 /= audio_max
     return (audio * max_int16).astype(np.int16)
+
+
+# ---------------------------------------------------------------- pm f0
+def f0_autocorrelation(x, sr, hop=160, f0_min=50.0, f0_max=1100.0, voicing_threshold=0.6, time_step=0.01):
+    """``f0_autocorrelation`` (``runtime/dsp/f0.py:24-94``): per frame of ``win``
+    samples (45 ms, at least three periods of ``f0_min``, odd) centred on
+    ``i * hop``: mean removed, Hann window, autocorrelation through an rfft of
+    ``nfft >= 2 win`` points, the first lag of the largest normalised value in
+    ``[sr / f0_max, sr / f0_min]``; voiced above the threshold."""
+    x = np.asarray(x, dtype=np.float64)
+    if time_step is not None and time_step > 0:
+        hop = int(round(sr * time_step))
+    hop = max(1, int(hop))
+    win = int(round(sr * 0.045))
+    if f0_min > 0 and win < 3 * sr / f0_min:
+        win = int(round(3 * sr / f0_min))
+    if win % 2 == 0:
+        win += 1
+    n_frames = int(np.ceil(len(x) / hop))
+    f0 = np.zeros(n_frames, dtype=F32)
+    lag_min = max(1, int(round(sr / f0_max)))
+    lag_max = min(int(round(sr / f0_min)), win - 1)
+    nfft = 1 << int(np.ceil(np.log2(2 * win)))
+    w = np.hanning(win)
+    half = win // 2
+    for i in range(n_frames):
+        s = i * hop - half
+        e = s + win
+        if s >= 0 and e <= len(x):
+            seg = x[s:e]
+        else:
+            seg = np.pad(x[max(s, 0):min(e, len(x))], (max(0, -s), max(0, e - len(x))))
+        seg = seg - seg.mean()
+        if float(np.max(np.abs(seg))) < 1e-7:
+            continue
+        X = np.fft.rfft(seg * w, n=nfft)
+        r = np.fft.irfft(X * np.conj(X), n=nfft)[:win]
+        if r[0] <= 0.0:
+            continue
+        rn = r / r[0]
+        seg_r = rn[lag_min:lag_max + 1]
+        k = int(np.argmax(seg_r)) + lag_min
+        if seg_r[k - lag_min] > voicing_threshold:
+            f0[i] = sr / k
+    return f0
+
+
+# ---------------------------------------------------------------- resample
+def _kaiser_sinc(t, radius, beta=12.0):
+    x = t / float(radius)
+    with np.errstate(invalid="ignore", divide="ignore"):
+        kaiser = np.where(np.abs(x) <= 1.0, np.i0(beta * np.sqrt(np.maximum(0.0, 1.0 - x * x))) / np.i0(beta), 0.0)
+    return np.sinc(t) * kaiser
+
+
+def resample(x, orig_sr, target_sr, method="fft"):
+    """``resample`` (``runtime/dsp/resample.py:129-168``) for 1-D signals:
+    ``fft`` interpolates the rfft spectrum at ``p_k = k n_in sr_out / (sr_in n_out)``
+    with a 33-tap Kaiser-sinc (beta 12) over the edge-padded spectrum, zero past
+    the source Nyquist, then irfft and ``* n_out / n_in`` (:41-78); ``sinc`` is
+    the 25-tap time-domain kernel (:96-126); ``linear`` is ``np.interp`` on
+    ``np.linspace(0, n_in - 1, n_out)`` (:81-93)."""
+    x = np.asarray(x, dtype=np.float64)
+    n_in = x.shape[-1]
+    if orig_sr == target_sr:
+        return x.copy().astype(F32)
+    n_out = max(1, int(round(n_in * target_sr / orig_sr)))
+    if method == "fft":
+        X = np.fft.rfft(x, n=n_in)
+        nbi, nbo = X.shape[-1], n_out // 2 + 1
+        p = np.arange(nbo, dtype=np.float64) * (n_in * target_sr / (orig_sr * n_out))
+        ok = p <= (nbi - 1)
+        Y = np.zeros(nbo, dtype=np.complex128)
+        if ok.any():
+            radius, pad = 16, 17
+            Xp = np.pad(X, (pad, pad), mode="edge")
+            pp = p[ok] + pad
+            base = np.floor(pp)[:, None].astype(np.int64) + np.arange(-radius, radius + 1)[None, :]
+            kern = _kaiser_sinc(pp[:, None] - base.astype(np.float64), radius)
+            Y[ok] = np.sum(Xp[base] * kern, axis=-1)
+        y = np.fft.irfft(Y, n=n_out) * (n_out / n_in)
+    elif method == "sinc":
+        ratio = n_in / n_out
+        pos = np.arange(n_out, dtype=np.float64) * ratio
+        base = pos.astype(np.int64)
+        y = np.zeros(n_out, dtype=np.float64)
+        for k in range(-12, 13):
+            idx = np.clip(base + k, 0, n_in - 1)
+            y += np.take(x, idx) * _kaiser_sinc(pos - (base + k), 12)
+    else:
+        y = np.interp(np.linspace(0.0, n_in - 1, n_out), np.arange(n_in), x)
+    return y.astype(F32)

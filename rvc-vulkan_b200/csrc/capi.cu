@@ -945,6 +945,43 @@ int32_t rvc_cuda_change_rms(int64_t ctx, const float* d1, int64_t n1, int32_t sr
   });
 }
 
+int32_t rvc_cuda_f0_autocorr(int64_t ctx, const double* x, int64_t n, int32_t sr, int32_t hop, int32_t win,
+                             int32_t lag_min, int32_t lag_max, const double* hann, double threshold, float* f0,
+                             int64_t n_frames) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(x && hann && f0 && n >= 1 && sr >= 1 && n_frames >= 0, "f0_autocorr: bad arguments");
+    DevBuf dx(c, sizeof(double) * (size_t)n), dw(c, sizeof(double) * (size_t)std::max(1, win)),
+        df(c, sizeof(float) * (size_t)std::max<int64_t>(1, n_frames));
+    h2d(c, dx.p, x, sizeof(double) * n);
+    h2d(c, dw.p, hann, sizeof(double) * (size_t)win);
+    dsp_f0_autocorr(c, (const double*)dx.p, n, hop, win, lag_min, lag_max, (const double*)dw.p, (double)sr,
+                    threshold, df.f(), n_frames);
+    d2h(c, f0, df.p, sizeof(float) * (size_t)n_frames);
+    finish(c);
+  });
+}
+
+int32_t rvc_cuda_resample(int64_t ctx, const void* x, int32_t x_f32, int64_t n_in, int32_t orig_sr,
+                          int32_t target_sr, int32_t method, float* y, int64_t n_out) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(x && y && n_in >= 1 && n_out >= 1 && orig_sr > 0 && target_sr > 0, "resample: bad arguments");
+    DevBuf dx(c, sizeof(double) * (size_t)n_in), dy(c, sizeof(float) * (size_t)n_out);
+    if (x_f32) {
+      DevBuf xf(c, sizeof(float) * (size_t)n_in);
+      h2d(c, xf.p, x, sizeof(float) * n_in);
+      dsp_f32_to_f64(c, xf.f(), n_in, (double*)dx.p);
+      RVC_CUDA_TRY(cudaStreamSynchronize(c->stream));
+    } else {
+      h2d(c, dx.p, x, sizeof(double) * n_in);
+    }
+    // the fft method's bin-position factor, formed as the reference does: (n_in * sr_out) / (sr_in * n_out)
+    const double factor = (double)(n_in * (int64_t)target_sr) / (double)((int64_t)orig_sr * n_out);
+    dsp_resample(c, (const double*)dx.p, n_in, n_out, method, factor, dy.f());
+    d2h(c, y, dy.p, sizeof(float) * (size_t)n_out);
+    finish(c);
+  });
+}
+
 int32_t rvc_cuda_to_int16(int64_t ctx, const float* x, int64_t n, int16_t* y) {
   return on_ctx(ctx, [&](Context* c) {
     RVC_CHECK_ARG(x && y && n >= 1, "to_int16: bad arguments");

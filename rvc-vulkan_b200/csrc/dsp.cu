@@ -224,6 +224,120 @@ __global__ void rms_mix_kernel(const float* __restrict__ d2, long long n2, const
   }
 }
 
+// ------------------------------------------------------------------ pm f0
+// numpy's pairwise float64 sum (blocks of <= 128 with eight running sums,
+// halves rounded down to a multiple of 8 above that), iterative.
+__device__ double np_block_sum(const double* a, int n) {  // n <= 128
+  if (n < 8) {
+    double res = 0.0;
+    for (int i = 0; i < n; ++i) res += a[i];
+    return res;
+  }
+  double r[8];
+  for (int j = 0; j < 8; ++j) r[j] = a[j];
+  int i = 8;
+  for (; i < n - (n % 8); i += 8)
+    for (int j = 0; j < 8; ++j) r[j] += a[i + j];
+  double res = ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
+  for (; i < n; ++i) res += a[i];
+  return res;
+}
+
+__device__ double np_pairwise_sum(const double* a, int n) {
+  // explicit-stack form of sum(a, n) = n <= 128 ? block(a, n) : sum(a, h) + sum(a + h, n - h),
+  // h = n / 2 rounded down to a multiple of 8
+  struct Frame { int off, n, state; double left; };  // state 0: new, 1: left pending, 2: right pending
+  Frame fr[24];
+  int top = 0;
+  fr[top++] = {0, n, 0, 0.0};
+  double ret = 0.0;
+  while (top > 0) {
+    Frame& f = fr[top - 1];
+    bool done = false;
+    if (f.n <= 128) {
+      ret = np_block_sum(a + f.off, f.n);
+      done = true;
+    } else {
+      const int h = (f.n / 2) - (f.n / 2) % 8;
+      if (f.state == 0) {
+        f.state = 1;
+        fr[top++] = {f.off, h, 0, 0.0};
+      } else if (f.state == 1) {  // left finished: its sum is in ret
+        f.left = ret;
+        f.state = 2;
+        fr[top++] = {f.off + h, f.n - h, 0, 0.0};
+      } else {                    // right finished
+        ret = f.left + ret;
+        done = true;
+      }
+    }
+    if (done) --top;
+  }
+  return ret;
+}
+
+// One block per frame (runtime/dsp/f0.py:24-94): the zero-padded window of
+// `win` samples centred on i * hop, mean removed (numpy's pairwise mean),
+// skipped when its peak is below 1e-7; Hann-weighted; autocorrelation at lag 0
+// and at lag_min..lag_max (direct float64 sums); the first lag of the largest
+// normalised value, voiced above the threshold: f0 = sr / lag.
+__global__ void f0_autocorr_kernel(const double* __restrict__ x, long long n, int hop, int win, int lag_min,
+                                   int lag_max, const double* __restrict__ hann, double sr, double thr,
+                                   float* __restrict__ f0) {
+  extern __shared__ double sm[];
+  double* seg = sm;            // [win]
+  double* r = sm + win;        // [lag_max + 1]
+  __shared__ double s_mean, s_peak;
+  const long long i = blockIdx.x;
+  const long long s0 = i * hop - win / 2;
+  for (int t = threadIdx.x; t < win; t += blockDim.x) {
+    const long long p = s0 + t;
+    seg[t] = (p >= 0 && p < n) ? x[p] : 0.0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) s_mean = np_pairwise_sum(seg, win) / (double)win;
+  __syncthreads();
+  const double mean = s_mean;
+  for (int t = threadIdx.x; t < win; t += blockDim.x) seg[t] = seg[t] - mean;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double pk = 0.0;
+    for (int t = 0; t < win; ++t) pk = fmax(pk, fabs(seg[t]));
+    s_peak = pk;
+  }
+  __syncthreads();
+  if (s_peak < 1e-7) {
+    if (threadIdx.x == 0) f0[i] = 0.f;
+    return;
+  }
+  for (int t = threadIdx.x; t < win; t += blockDim.x) seg[t] = seg[t] * hann[t];
+  __syncthreads();
+  for (int lag = threadIdx.x; lag <= lag_max; lag += blockDim.x) {
+    if (lag != 0 && lag < lag_min) continue;
+    double acc = 0.0;
+    for (int t = 0; t + lag < win; ++t) acc = fma(seg[t], seg[t + lag], acc);
+    r[lag] = acc;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const double r0 = r[0];
+    float out = 0.f;
+    if (r0 > 0.0) {
+      int best = lag_min;
+      double bv = r[lag_min] / r0;
+      for (int lag = lag_min + 1; lag <= lag_max; ++lag) {
+        const double v = r[lag] / r0;
+        if (v > bv) {
+          bv = v;
+          best = lag;
+        }
+      }
+      if (bv > thr) out = (float)(sr / (double)best);
+    }
+    f0[i] = out;
+  }
+}
+
 // ------------------------------------------------------------------ int16
 __global__ void absmax_kernel(const float* __restrict__ x, long long n, unsigned int* __restrict__ out) {
   float m = 0.f;
@@ -399,6 +513,19 @@ void dsp_change_rms(Context* ctx, const float* d1, long long n1, int sr1, const 
                                                    (float)(rate - 1.0), out);
   check_launch();
   RVC_CUDA_TRY(cudaStreamSynchronize(st));
+}
+
+void dsp_f0_autocorr(Context* ctx, const double* x, long long n, int hop, int win, int lag_min, int lag_max,
+                     const double* hann, double sr, double thr, float* f0, long long n_frames) {
+  RVC_CHECK_ARG(hop >= 1 && win >= 3 && win <= 8192 && lag_min >= 1 && lag_min <= lag_max && lag_max < win,
+                "f0_autocorr: bad frame / lag parameters");
+  if (n_frames <= 0) return;
+  const size_t smem = sizeof(double) * ((size_t)win + lag_max + 1);
+  if (smem > 48 * 1024)
+    RVC_CUDA_TRY(cudaFuncSetAttribute(f0_autocorr_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  f0_autocorr_kernel<<<(unsigned)n_frames, 256, smem, ctx->stream>>>(x, n, hop, win, lag_min, lag_max, hann, sr, thr,
+                                                                       f0);
+  check_launch();
 }
 
 void dsp_to_int16(Context* ctx, const float* x, long long n, short* y) {

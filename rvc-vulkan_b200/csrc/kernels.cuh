@@ -78,6 +78,11 @@ struct Context;
 // scipy.signal.filtfilt(b, a, x) with padtype 'odd' (b, a host arrays), float64
 void dsp_filtfilt(Context* ctx, const double* b, int nb, const double* a, int na, const double* x_dev, long long n,
                   bool ext_f32, double* y_dev);
+// method 0: fft (factor = n_in sr_out / (sr_in n_out)), 1: linear, 2: sinc; y float32 [n_out]
+void dsp_resample(Context* ctx, const double* x, long long n_in, long long n_out, int method, double factor,
+                  float* y);
+void dsp_f0_autocorr(Context* ctx, const double* x, long long n, int hop, int win, int lag_min, int lag_max,
+                     const double* hann, double sr, double thr, float* f0, long long n_frames);
 void dsp_f32_to_f64(Context* ctx, const float* x, long long n, double* y);
 // first argmin of the 160-sample absolute sums around t = step, 2 step, ... (< n); -1 = empty window
 long long dsp_split_points(Context* ctx, const double* audio, long long n, int window, long long t_query,

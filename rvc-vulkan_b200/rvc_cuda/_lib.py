@@ -112,6 +112,8 @@ _SIGS = {
     "rvc_cuda_protect": ([_i64, _fp, _fp, _fp, _i64, _i32, _f32, _fp], _i32),
     "rvc_cuda_change_rms": ([_i64, _fp, _i64, _i32, _fp, _i64, _i32, _f64, _fp], _i32),
     "rvc_cuda_to_int16": ([_i64, _fp, _i64, _p], _i32),
+    "rvc_cuda_resample": ([_i64, _p, _i32, _i64, _i32, _i32, _i32, _fp, _i64], _i32),
+    "rvc_cuda_f0_autocorr": ([_i64, _p, _i64, _i32, _i32, _i32, _i32, _i32, _p, _f64, _fp, _i64], _i32),
     "rvc_cuda_index_create": ([_i64, _fp, _i64, _i32, _i32, C.POINTER(_i64)], _i32),
     "rvc_cuda_index_destroy": ([_i64], _i32),
     "rvc_cuda_index_search": ([_i64, _fp, _i64, _i32, _i32, _fp, _ip64], _i32),

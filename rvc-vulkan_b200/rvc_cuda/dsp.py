@@ -25,7 +25,7 @@ from . import _lib
 from ._lib import check, fptr, lib
 
 __all__ = ["filtfilt", "highpass", "split_points", "interpolate_linear", "protect_blend", "change_rms", "to_int16",
-           "patch_reference"]
+           "f0_autocorrelation", "resample", "patch_reference"]
 
 
 def _ctx(device: Optional[int] = None):
@@ -127,9 +127,65 @@ def to_int16(audio) -> np.ndarray:
     return y
 
 
+def f0_autocorrelation(x, sr, hop=160, f0_min=50.0, f0_max=1100.0, voicing_threshold=0.6, time_step=0.01):
+    """``runtime.dsp.f0.f0_autocorrelation`` (``runtime/dsp/f0.py:24-94``): the
+    frame / lag parameters and the Hann window are derived on the host exactly
+    as there, the per-frame analysis runs on the device."""
+    x = np.ascontiguousarray(np.asarray(x, dtype=np.float64))
+    if x.ndim != 1:
+        raise ValueError(f"f0_autocorrelation needs a 1-D signal, got {x.ndim}-D")
+    if time_step is not None and time_step > 0:
+        hop = int(round(sr * time_step))
+    hop = max(1, int(hop))
+    win = int(round(sr * 0.045))
+    if f0_min > 0 and win < 3 * sr / f0_min:
+        win = int(round(3 * sr / f0_min))
+    if win % 2 == 0:
+        win += 1
+    n_frames = int(np.ceil(len(x) / hop))
+    lag_min = max(1, int(round(sr / f0_max)))
+    lag_max = int(round(sr / f0_min))
+    if lag_max >= win:
+        lag_max = win - 1
+    if lag_min > lag_max:
+        raise ValueError("no valid lag between f0_max and f0_min inside the window")
+    f0 = np.zeros(n_frames, dtype=np.float32)
+    if n_frames and x.size:
+        w = np.ascontiguousarray(np.hanning(win))
+        check(lib.rvc_cuda_f0_autocorr(_ctx().handle, _dp(x), x.size, int(sr), hop, win, lag_min, lag_max, _dp(w),
+                                       float(voicing_threshold), fptr(f0), n_frames))
+    return f0
+
+
+_RESAMPLE_METHODS = {"fft": 0, "linear": 1, "sinc": 2}
+
+
+def resample(x, orig_sr, target_sr, method="fft"):
+    """``runtime.dsp.resample.resample`` (``runtime/dsp/resample.py:129``) for
+    1-D signals: float32 of length ``max(1, round(n * target_sr / orig_sr))``."""
+    if orig_sr <= 0 or target_sr <= 0:
+        raise ValueError("sample rates must be positive")
+    if method not in _RESAMPLE_METHODS:
+        raise ValueError(f"unsupported method: {method!r} (use 'fft', 'linear' or 'sinc')")
+    x = np.asarray(x)
+    if x.ndim != 1:
+        raise ValueError(f"the device resample takes 1-D signals, got {x.ndim}-D")
+    xx = np.ascontiguousarray(x, dtype=np.float32 if x.dtype == np.float32 else np.float64)
+    if orig_sr == target_sr:
+        return xx.astype(np.float32)
+    n_in = xx.size
+    n_out = max(1, int(round(n_in * target_sr / orig_sr)))
+    y = np.empty(n_out, np.float32)
+    if n_in == 0:
+        raise ValueError("resample of an empty signal")
+    check(lib.rvc_cuda_resample(_ctx().handle, _dp(xx), int(xx.dtype == np.float32), n_in, int(orig_sr),
+                                int(target_sr), _RESAMPLE_METHODS[method], fptr(y), n_out))
+    return y
+
+
 def patch_reference(pipeline_module=None):
-    """Route ``runtime.pipeline``'s ``change_rms``, ``interpolate_linear`` and
-    ``signal.filtfilt`` to the device versions."""
+    """Route ``runtime.pipeline``'s ``change_rms``, ``interpolate_linear``,
+    ``resample`` and ``signal.filtfilt`` to the device versions."""
     if pipeline_module is None:
         from runtime import pipeline as pipeline_module  # noqa: PLC0415
     if getattr(pipeline_module, "_rvc_cuda_patched_dsp", False):
@@ -149,5 +205,8 @@ def patch_reference(pipeline_module=None):
     pipeline_module.change_rms = change_rms
     pipeline_module._rvc_cuda_orig_interpolate_linear = pipeline_module.interpolate_linear
     pipeline_module.interpolate_linear = interpolate_linear
+    if hasattr(pipeline_module, "resample"):
+        pipeline_module._rvc_cuda_orig_resample = pipeline_module.resample
+        pipeline_module.resample = resample
     pipeline_module._rvc_cuda_patched_dsp = True
     return pipeline_module

@@ -16,9 +16,8 @@ Host-side glue that stays in numpy: the reflect padding and slicing of the
 chunks, the frame alignment of pitch arrays (``:572-603``) and the f0
 post-processing of ``get_f0`` (``:468-482``, a few thousand values per call).
 
-Not offered here: the ``pm`` / ``fcpe`` f0 methods, output resampling
-(``resample_sr``) and ``brute_mix != 0``; asking for one raises
-``NotImplementedError``.
+Not offered here: the ``fcpe`` f0 method and ``brute_mix != 0``; asking
+for one raises ``NotImplementedError``.
 """
 
 from __future__ import annotations
@@ -75,22 +74,31 @@ class Pipeline:
 
     # ------------------------------------------------------------------ f0
     def get_f0(self, x, p_len, f0_up_key, f0_method):
-        """f0 of a segment through ``self.model_rmvpe`` and the reference's
+        """f0 of a segment (``rmvpe`` through ``self.model_rmvpe``, ``pm``
+        through the device autocorrelation) and the reference's
         post-processing (``runtime/pipeline.py:408-483``): unvoiced frames
         linearly interpolated, transposed by ``f0_up_key`` semitones, then the
         mel quantisation to 1..255.  Returns ``(f0_coarse int32, f0 float32)``."""
         if f0_method not in ("pm", "rmvpe", "fcpe"):
             raise ValueError(f"Unsupported F0 method: {f0_method}")
-        if f0_method != "rmvpe":
-            raise NotImplementedError(f"f0 method {f0_method!r} is not on the device path (rmvpe is)")
-        if not hasattr(self, "model_rmvpe"):
-            raise RuntimeError("Pipeline.model_rmvpe must be set (a CudaRmvpe, or any object with "
-                               "infer_from_audio(x, thred))")
+        if f0_method == "fcpe":
+            raise NotImplementedError("f0 method 'fcpe' is not on the device path (rmvpe and pm are)")
         f0_min, f0_max = 50, 1100
         f0_mel_min = 1127 * np.log(1 + f0_min / 700)
         f0_mel_max = 1127 * np.log(1 + f0_max / 700)
-        f0 = np.asarray(self.model_rmvpe.infer_from_audio(np.asarray(x, dtype=np.float32), thred=0.03),
-                        dtype=np.float64)
+        if f0_method == "pm":                                          # :428-441
+            f0 = np.asarray(dsp.f0_autocorrelation(np.asarray(x, dtype=np.float64), self.sr, voicing_threshold=0.6,
+                                                   f0_min=f0_min, f0_max=f0_max, time_step=0.01), dtype=np.float64)
+            pad_size = (p_len - len(f0) + 1) // 2
+            right = p_len - len(f0) - pad_size
+            if pad_size > 0 or right > 0:
+                f0 = np.pad(f0, (pad_size, right), mode="constant")
+        else:
+            if not hasattr(self, "model_rmvpe"):
+                raise RuntimeError("Pipeline.model_rmvpe must be set (a CudaRmvpe, or any object with "
+                                   "infer_from_audio(x, thred))")
+            f0 = np.asarray(self.model_rmvpe.infer_from_audio(np.asarray(x, dtype=np.float32), thred=0.03),
+                            dtype=np.float64)
         uv = f0 == 0
         if uv.any():
             voiced = np.where(~uv)[0]
@@ -173,8 +181,6 @@ class Pipeline:
         Returns ``(tgt_sr, int16 audio)``."""
         if not if_f0:
             raise NotImplementedError("only f0-guided models are supported (as in the reference)")
-        if tgt_sr != resample_sr >= 16000:
-            raise NotImplementedError("output resampling is not on the device path")
         index = self._resolve_index(file_index, index_rate)
         version = _as_version(version)
         t_max = self.t_max
@@ -249,6 +255,8 @@ class Pipeline:
         audio_opt = np.concatenate([r for r in results if r is not None])
         if rms_mix_rate != 1:
             audio_opt = dsp.change_rms(audio, audio_opt, 16000, tgt_sr, rms_mix_rate)
+        if tgt_sr != resample_sr >= 16000:                             # :1204-1205
+            audio_opt = dsp.resample(audio_opt, tgt_sr, resample_sr, method="fft")
         return tgt_sr, dsp.to_int16(audio_opt)
 
     # ------------------------------------------------------------------ models

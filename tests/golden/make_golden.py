@@ -330,8 +330,8 @@ def run_dsp(meta):
 
         pipe.get_f0 = get_f0
         sr, out = pipe.pipeline(pf.FakeHubert(D=768), pf.FakeSynth(gain=kw["gain"]), 0, a, [0.0, 0.0, 0.0],
-                                kw["f0_up_key"], "rmvpe", None, 0, True, 40000, 0, kw["rms"], 2, kw["protect"],
-                                slice_length=kw["slice_length"])
+                                kw["f0_up_key"], kw.get("f0", "rmvpe"), None, 0, True, 40000,
+                                kw.get("resample_sr", 0), kw["rms"], 2, kw["protect"], slice_length=kw["slice_length"])
         assert sr == 40000
         item = np.dtype(np.float64).itemsize
         rec[name + "_split"] = np.array([(p - starts[0]) // item - pipe.t_pad for p in starts[1:]], np.int64)
@@ -340,6 +340,24 @@ def run_dsp(meta):
         else:
             rec[name + "_int16"] = out
         cases[name] = dict(kw, inputs_sha256=digest([a]), out_len=int(out.size))
+    # pm f0 (runtime/dsp/f0.py:24) and Pipeline.get_f0(..., "pm") with its padding and post-processing
+    from runtime.dsp.f0 import f0_autocorrelation  # noqa: PLC0415
+    a = syn.make_speech_audio(1.5, seed=6, silence_every=0.6, silence_len=0.2)
+    a[3000:3400] += (0.3 * np.random.RandomState(91_005).standard_normal(400)).astype(np.float32)
+    rec["pm_f0"] = f0_autocorrelation(a.astype(np.float64), 16000, voicing_threshold=0.6, f0_min=50, f0_max=1100,
+                                      time_step=0.01)
+    pipe = rp.Pipeline(40000, pf.config())
+    p_len = a.size // 160 + 3
+    rec["pm_coarse"], rec["pm_f0bak"] = pipe.get_f0(a.astype(np.float64), p_len, 4, "pm")
+    cases["pm"] = {"seconds": 1.5, "seed": 6, "p_len": p_len, "inputs_sha256": digest([a])}
+    # output resampling (runtime/dsp/resample.py:129), the three methods
+    from runtime.dsp.resample import resample  # noqa: PLC0415
+    wv = (0.6 * np.sin(np.arange(12001) * 0.05) + 0.2 * np.random.RandomState(91_006).standard_normal(12001)
+          ).astype(np.float32)
+    rec["rs_x"] = wv
+    for meth in ("fft", "linear", "sinc"):
+        rec[f"rs_{meth}_48k"] = resample(wv, 40000, 48000, method=meth)
+        rec[f"rs_{meth}_16k"] = resample(wv, 40000, 16000, method=meth)
     np.savez_compressed(os.path.join(HERE, "dsp.npz"), **rec)
     meta["dsp"] = {"kind": "dsp", "cases": cases, "scipy": __import__("scipy").__version__}
 
@@ -352,6 +370,9 @@ PIPE_CASES = [
                      "rms": 0.5, "protect": 0.2, "gain": 0.7, "f0_up_key": 0}),
     ("pipe_whole", {"seconds": 1.2, "seed": 4, "silence_every": 8.0, "x_query": 6, "slice_length": 0,
                     "rms": 1.0, "protect": 0.5, "gain": 1.3, "f0_up_key": -3}),
+    ("pipe_resample_pm", {"seconds": 1.3, "seed": 10, "silence_every": 8.0, "x_query": 6, "slice_length": 0,
+                          "rms": 0.5, "protect": 0.33, "gain": 1.3, "f0_up_key": 1, "f0": "pm",
+                          "resample_sr": 48000}),
     ("pipe_60s", {"seconds": 60.0, "seed": 0, "silence_every": 8.0, "x_query": 6, "slice_length": 0,
                   "rms": 0.25, "protect": 0.33, "gain": 1.3, "f0_up_key": 0}),
 ]

@@ -69,6 +69,8 @@ def _oracle_dsp():
         protect_blend=OD.protect_blend,
         change_rms=OD.change_rms,
         to_int16=OD.to_int16,
+        f0_autocorrelation=OD.f0_autocorrelation,
+        resample=OD.resample,
     )
 
 
@@ -92,8 +94,8 @@ def test_pipeline_orchestration_matches_reference(name, kw, gold, golden_meta, m
 
     pipe.get_f0 = get_f0
     sr, out = pipe.pipeline(pf.FakeHubert(D=768), pf.FakeSynth(gain=kw["gain"]), 0, a, [0.0, 0.0, 0.0],
-                            kw["f0_up_key"], "rmvpe", None, 0, True, 40000, 0, kw["rms"], 2, kw["protect"],
-                            slice_length=kw["slice_length"])
+                            kw["f0_up_key"], kw.get("f0", "rmvpe"), None, 0, True, 40000, kw.get("resample_sr", 0),
+                            kw["rms"], 2, kw["protect"], slice_length=kw["slice_length"])
     assert sr == 40000 and out.dtype == np.int16 and out.size == m["out_len"]
     split = [(p - starts[0]) // 8 - pipe.t_pad for p in starts[1:]]
     np.testing.assert_array_equal(split, gold[name + "_split"])
@@ -103,13 +105,38 @@ def test_pipeline_orchestration_matches_reference(name, kw, gold, golden_meta, m
         np.testing.assert_array_equal(out[::101], gold[name + "_int16_every101"])
 
 
+def _pm_audio(golden_meta):
+    m = golden_meta["dsp"]["cases"]["pm"]
+    a = syn.make_speech_audio(m["seconds"], seed=m["seed"], silence_every=0.6, silence_len=0.2)
+    a[3000:3400] += (0.3 * np.random.RandomState(91_005).standard_normal(400)).astype(np.float32)
+    assert digest([a]) == m["inputs_sha256"]
+    return a, m
+
+
+def test_pm_f0_oracle_matches_reference(gold, golden_meta, monkeypatch):
+    a, m = _pm_audio(golden_meta)
+    np.testing.assert_array_equal(OD.f0_autocorrelation(a.astype(np.float64), 16000), gold["pm_f0"])
+    # the device pipeline's get_f0("pm") host logic (padding, post-processing) with the oracle's f0
+    from rvc_cuda import pipeline as P
+    monkeypatch.setattr(P, "dsp", types.SimpleNamespace(f0_autocorrelation=OD.f0_autocorrelation))
+    coarse, f0bak = P.Pipeline(40000, pf.config()).get_f0(a.astype(np.float64), m["p_len"], 4, "pm")
+    np.testing.assert_array_equal(coarse, gold["pm_coarse"])
+    np.testing.assert_array_equal(f0bak, gold["pm_f0bak"])
+
+
+@pytest.mark.parametrize("method", ["fft", "linear", "sinc"])
+def test_resample_oracle_matches_reference(method, gold):
+    for sr, tag in ((48000, "48k"), (16000, "16k")):
+        np.testing.assert_array_equal(OD.resample(gold["rs_x"], 40000, sr, method), gold[f"rs_{method}_{tag}"])
+
+
 def test_pipeline_rejects_what_is_not_on_the_device_path():
     from rvc_cuda import pipeline as P
     pipe = P.Pipeline(40000, pf.config())
     with pytest.raises(NotImplementedError):
-        pipe.get_f0(np.zeros(1000), 6, 0, "pm")
+        pipe.get_f0(np.zeros(1000), 6, 0, "fcpe")
     with pytest.raises(ValueError):
         pipe.get_f0(np.zeros(1000), 6, 0, "crepe")
     with pytest.raises(NotImplementedError):
-        pipe.pipeline(None, None, 0, np.zeros(16000, np.float32), [0, 0, 0], 0, "rmvpe", None, 0, True, 40000,
-                      44100, 1, 2, 0.33)
+        pipe.pipeline(None, None, 0, np.zeros(16000, np.float32), [0, 0, 0], 0, "rmvpe", None, 0, False, 40000,
+                      0, 1, 2, 0.33)

@@ -112,6 +112,43 @@ def test_change_rms_matches_reference(gold, golden_meta):
                                OD.change_rms(long1, long2, 16000, 40000, 0.25), rtol=1e-5, atol=1e-7)
 
 
+def test_pm_f0_matches_reference(gold, golden_meta):
+    m = golden_meta["dsp"]["cases"]["pm"]
+    a = syn.make_speech_audio(m["seconds"], seed=m["seed"], silence_every=0.6, silence_len=0.2)
+    a[3000:3400] += (0.3 * np.random.RandomState(91_005).standard_normal(400)).astype(np.float32)
+    np.testing.assert_array_equal(dsp.f0_autocorrelation(a.astype(np.float64), 16000), gold["pm_f0"])
+    from rvc_cuda.pipeline import Pipeline
+    coarse, f0bak = Pipeline(40000, pf.config()).get_f0(a.astype(np.float64), m["p_len"], 4, "pm")
+    np.testing.assert_array_equal(coarse, gold["pm_coarse"])
+    np.testing.assert_array_equal(f0bak, gold["pm_f0bak"])
+    # other rates, hops and ranges against the oracle; a silent input is all unvoiced
+    x = syn.make_speech_audio(2.0, seed=8).astype(np.float64)
+    for kw in ({"sr": 16000, "time_step": 0.005}, {"sr": 22050, "f0_min": 80.0, "f0_max": 600.0},
+               {"sr": 16000, "voicing_threshold": 0.3}):
+        sr = kw.pop("sr")
+        np.testing.assert_array_equal(dsp.f0_autocorrelation(x, sr, **kw), OD.f0_autocorrelation(x, sr, **kw))
+    assert not dsp.f0_autocorrelation(np.zeros(4000), 16000).any()
+
+
+@pytest.mark.parametrize("method", ["fft", "linear", "sinc"])
+def test_resample_matches_reference(method, gold):
+    """fft: cuFFT double transforms and the device Kaiser-sinc spectral
+    interpolation against numpy's pocketfft path: within 1e-6 of full scale;
+    sinc: device sin / power-series I0 in the taps: 1e-6; linear: exact."""
+    for sr, tag in ((48000, "48k"), (16000, "16k")):
+        y = dsp.resample(gold["rs_x"], 40000, sr, method)
+        ref = gold[f"rs_{method}_{tag}"]
+        assert y.dtype == np.float32 and y.shape == ref.shape
+        if method == "linear":
+            np.testing.assert_array_equal(y, ref)
+        else:
+            assert np.abs(y - ref).max() <= 1e-6
+    # a long odd-length signal (a cuFFT size with a large prime factor) against the oracle
+    x = syn.make_speech_audio(7.3, seed=4)[:116_803]
+    np.testing.assert_allclose(dsp.resample(x, 16000, 44100, method), OD.resample(x, 16000, 44100, method),
+                               atol=1e-6 if method != "linear" else 0, rtol=0)
+
+
 def test_to_int16_matches_oracle():
     rs = np.random.RandomState(11)
     for peak in (0.5, 0.99, 1.0, 1.7, 40.0):
@@ -137,8 +174,8 @@ def test_device_pipeline_with_stand_ins_matches_reference(name, kw, gold, golden
 
     pipe.get_f0 = get_f0
     sr, out = pipe.pipeline(pf.FakeHubert(D=768), pf.FakeSynth(gain=kw["gain"]), 0, a, [0.0, 0.0, 0.0],
-                            kw["f0_up_key"], "rmvpe", None, 0, True, 40000, 0, kw["rms"], 2, kw["protect"],
-                            slice_length=kw["slice_length"])
+                            kw["f0_up_key"], kw.get("f0", "rmvpe"), None, 0, True, 40000, kw.get("resample_sr", 0),
+                            kw["rms"], 2, kw["protect"], slice_length=kw["slice_length"])
     assert sr == 40000 and out.size == m["out_len"]
     np.testing.assert_array_equal([(p - starts[0]) // 8 - pipe.t_pad for p in starts[1:]], gold[name + "_split"])
     ref = gold[name + "_int16"] if name + "_int16" in gold else None
