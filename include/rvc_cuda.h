@@ -229,6 +229,29 @@ int32_t rvc_cuda_rmvpe_infer_device(int64_t model, int32_t B, int64_t T, const f
 int32_t rvc_cuda_rmvpe_tap(int64_t model, const char* name, float* out, int64_t n);
 int32_t rvc_cuda_rmvpe_keep_taps(int64_t model, int32_t enable);
 
+/* ---------------------------------------------------------------- FCPE
+ * Device-resident FCPE F0 estimator (CFNaiveMelPE, conv-only); replaces
+ * FCPE.infer (runtime/models/fcpe.py:344-369) with _wav2mel (:204), the input
+ * stack (:237), the conformer conv layers (:257), _latent (:290) and the local
+ * argmax decode (:304).  precision 0 = BF16x3 tensor cores, 1 = fp32 SIMT. */
+int32_t rvc_cuda_fcpe_create(int64_t ctx, int32_t precision, int64_t* model);
+int32_t rvc_cuda_fcpe_destroy(int64_t model);
+/* Checkpoint tensors under the reference's keys (FCPE.W, cent_table included). */
+int32_t rvc_cuda_fcpe_set_weight(int64_t model, const char* key, const float* data, const int64_t* shape,
+                                 int32_t ndim);
+int32_t rvc_cuda_fcpe_finalize(int64_t model);
+/* B equal-length clips x [B,T] (host, 16 kHz) -> f0 [B,F] Hz, F = T / 160 + 1,
+ * and, when argmax is not NULL, the latent argmax [B,F].  Synchronous. */
+int32_t rvc_cuda_fcpe_infer(int64_t model, int32_t B, int64_t T, const float* x, float threshold, float* f0,
+                            int32_t* argmax);
+/* Same with device pointers, asynchronous on the context's stream. */
+int32_t rvc_cuda_fcpe_infer_device(int64_t model, int32_t B, int64_t T, const float* x, float threshold, float* f0,
+                                   int32_t* argmax);
+/* Debug taps after an infer with taps enabled: "mel" [B,F,128], "stack" and
+ * "layer0".."layer5" [B,F,512], "latent" [B,F,360]. */
+int32_t rvc_cuda_fcpe_tap(int64_t model, const char* name, float* out, int64_t n);
+int32_t rvc_cuda_fcpe_keep_taps(int64_t model, int32_t enable);
+
 /* ---------------------------------------------------------------- retrieval
  * Device-resident feature index for brute-force L2 search; replaces
  * runtime.retrieval.search_l2 (runtime/retrieval.py:35-82), weighted_blend

@@ -2,6 +2,7 @@
 // Every entry point: look up handles, take the context lock, set the device,
 // run, and turn any exception into an int32 status + thread-local message.
 #include "../../include/rvc_cuda.h"
+#include "fcpe.cuh"
 #include "hubert.cuh"
 #include "retrieval.cuh"
 #include "rmvpe.cuh"
@@ -21,6 +22,7 @@ std::unordered_map<int64_t, std::unique_ptr<SynthModel>> g_synth;
 std::unordered_map<int64_t, std::unique_ptr<HubertModel>> g_hubert;
 std::unordered_map<int64_t, std::unique_ptr<IndexModel>> g_index;
 std::unordered_map<int64_t, std::unique_ptr<RmvpeModel>> g_rmvpe;
+std::unordered_map<int64_t, std::unique_ptr<FcpeModel>> g_fcpe;
 int64_t g_next = 1;
 
 Context* get_ctx(int64_t h) {
@@ -48,6 +50,13 @@ RmvpeModel* get_rmvpe(int64_t h) {
   std::lock_guard<std::mutex> lk(g_reg_mu);
   auto it = g_rmvpe.find(h);
   if (it == g_rmvpe.end()) throw Error{kErrState, "invalid RMVPE handle " + std::to_string(h)};
+  return it->second.get();
+}
+
+FcpeModel* get_fcpe(int64_t h) {
+  std::lock_guard<std::mutex> lk(g_reg_mu);
+  auto it = g_fcpe.find(h);
+  if (it == g_fcpe.end()) throw Error{kErrState, "invalid FCPE handle " + std::to_string(h)};
   return it->second.get();
 }
 
@@ -123,6 +132,16 @@ template <typename F>
 int32_t on_index(int64_t index, F&& f) {
   return guarded([&] {
     IndexModel* m = get_index(index);
+    std::lock_guard<std::mutex> lk(m->ctx->mu);
+    DeviceGuard dg(m->ctx->device);
+    f(m);
+  });
+}
+
+template <typename F>
+int32_t on_fcpe(int64_t model, F&& f) {
+  return guarded([&] {
+    FcpeModel* m = get_fcpe(model);
     std::lock_guard<std::mutex> lk(m->ctx->mu);
     DeviceGuard dg(m->ctx->device);
     f(m);
@@ -864,6 +883,73 @@ int32_t rvc_cuda_rmvpe_tap(int64_t model, const char* name, float* out, int64_t 
 
 int32_t rvc_cuda_rmvpe_keep_taps(int64_t model, int32_t enable) {
   return on_rmvpe(model, [&](RmvpeModel* m) { m->keep_taps = enable != 0; });
+}
+
+// ----------------------------------------------------------------- FCPE
+int32_t rvc_cuda_fcpe_create(int64_t ctx, int32_t precision, int64_t* model) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(model, "fcpe_create: null output handle");
+    auto m = std::make_unique<FcpeModel>(c, precision);
+    std::lock_guard<std::mutex> lk(g_reg_mu);
+    *model = g_next++;
+    g_fcpe[*model] = std::move(m);
+  });
+}
+
+int32_t rvc_cuda_fcpe_destroy(int64_t model) {
+  return guarded([&] {
+    std::unique_ptr<FcpeModel> m;
+    {
+      std::lock_guard<std::mutex> lk(g_reg_mu);
+      auto it = g_fcpe.find(model);
+      if (it == g_fcpe.end()) throw Error{kErrState, "invalid FCPE handle " + std::to_string(model)};
+      m = std::move(it->second);
+      g_fcpe.erase(it);
+    }
+    std::lock_guard<std::mutex> lk(m->ctx->mu);
+    DeviceGuard dg(m->ctx->device);
+    m.reset();
+  });
+}
+
+int32_t rvc_cuda_fcpe_set_weight(int64_t model, const char* key, const float* data, const int64_t* shape,
+                                 int32_t ndim) {
+  return on_fcpe(model, [&](FcpeModel* m) {
+    RVC_CHECK_ARG(key && data && ndim >= 0 && ndim <= 8, "fcpe_set_weight: bad arguments");
+    std::vector<int64_t> s(shape, shape + ndim);
+    m->set_weight(key, data, s);
+  });
+}
+
+int32_t rvc_cuda_fcpe_finalize(int64_t model) {
+  return on_fcpe(model, [&](FcpeModel* m) {
+    m->finalize();
+    finish(m->ctx);
+  });
+}
+
+int32_t rvc_cuda_fcpe_infer(int64_t model, int32_t B, int64_t T, const float* x, float threshold, float* f0,
+                            int32_t* argmax) {
+  return on_fcpe(model, [&](FcpeModel* m) {
+    RVC_CHECK_ARG(B >= 1 && x && f0, "fcpe_infer: bad arguments");
+    m->infer_host(B, T, x, threshold, f0, argmax);
+    finish(m->ctx);
+  });
+}
+
+int32_t rvc_cuda_fcpe_infer_device(int64_t model, int32_t B, int64_t T, const float* x, float threshold, float* f0,
+                                   int32_t* argmax) {
+  return on_fcpe(model, [&](FcpeModel* m) { m->infer_device(B, T, x, threshold, f0, argmax); });
+}
+
+int32_t rvc_cuda_fcpe_tap(int64_t model, const char* name, float* out, int64_t n) {
+  return on_fcpe(model, [&](FcpeModel* m) {
+    if (!m->tap(name, out, n)) throw Error{kErrArg, std::string("fcpe_tap: no tap '") + name + "' of that size"};
+  });
+}
+
+int32_t rvc_cuda_fcpe_keep_taps(int64_t model, int32_t enable) {
+  return on_fcpe(model, [&](FcpeModel* m) { m->keep_taps = enable != 0; });
 }
 
 // ----------------------------------------------------------------- pipeline DSP

@@ -10,6 +10,7 @@ Drop-in for jiangchengnay/rvc-vulkan's numpy runtime:
   ``rvc_cuda.hubert.patch_reference`` for ``HubertEncoder``,
   ``rvc_cuda.retrieval.patch_reference`` for the brute-force ``search_l2``,
   ``rvc_cuda.rmvpe.patch_reference`` for ``RMVPE.infer_from_audio``,
+  ``rvc_cuda.fcpe.patch_reference`` for ``FCPE.infer``,
   ``rvc_cuda.dsp.patch_reference`` for the pipeline's ``filtfilt``,
   ``change_rms`` and ``interpolate_linear``).
 
@@ -47,10 +48,11 @@ def register(name: str = "cuda") -> None:
 def patch_reference(device=None, precision: str = "bf16x3") -> None:
     """Install the model-level CUDA paths on the reference's model classes and
     the device signal processing in ``runtime.pipeline``."""
-    from . import dsp, hubert, retrieval, rmvpe, synth  # noqa: PLC0415
+    from . import dsp, fcpe, hubert, retrieval, rmvpe, synth  # noqa: PLC0415
 
     synth.patch_reference(device=device, precision=precision)
     hubert.patch_reference(device=device, precision=precision)
     retrieval.patch_reference()
     rmvpe.patch_reference(device=device)
+    fcpe.patch_reference(device=device, precision=precision)
     dsp.patch_reference()

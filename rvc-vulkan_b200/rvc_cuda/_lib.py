@@ -97,6 +97,14 @@ _SIGS = {
     "rvc_cuda_hubert_encode_device": ([_i64, _i32, _i64, _p, _i32, _p], _i32),
     "rvc_cuda_hubert_tap": ([_i64, C.c_char_p, _fp, _i64], _i32),
     "rvc_cuda_hubert_keep_taps": ([_i64, _i32], _i32),
+    "rvc_cuda_fcpe_create": ([_i64, _i32, C.POINTER(_i64)], _i32),
+    "rvc_cuda_fcpe_destroy": ([_i64], _i32),
+    "rvc_cuda_fcpe_set_weight": ([_i64, C.c_char_p, _fp, _ip64, _i32], _i32),
+    "rvc_cuda_fcpe_finalize": ([_i64], _i32),
+    "rvc_cuda_fcpe_infer": ([_i64, _i32, _i64, _fp, _f32, _fp, C.POINTER(_i32)], _i32),
+    "rvc_cuda_fcpe_infer_device": ([_i64, _i32, _i64, _p, _f32, _p, _p], _i32),
+    "rvc_cuda_fcpe_tap": ([_i64, C.c_char_p, _fp, _i64], _i32),
+    "rvc_cuda_fcpe_keep_taps": ([_i64, _i32], _i32),
     "rvc_cuda_rmvpe_create": ([_i64, C.POINTER(_i64)], _i32),
     "rvc_cuda_rmvpe_destroy": ([_i64], _i32),
     "rvc_cuda_rmvpe_set_weight": ([_i64, C.c_char_p, _fp, _ip64, _i32], _i32),

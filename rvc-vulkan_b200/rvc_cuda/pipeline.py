@@ -7,7 +7,8 @@ same ``get_f0`` and ``pipeline(...)`` signatures and return value
 objects the reference's pipeline takes (``runtime/pipeline.py:15-25``):
 ``model.encode`` / ``encode_batch`` (``CudaHubert``), ``net_g.infer`` /
 ``prep_dec`` + ``decode_batch`` (``CudaSynthesizer``) and
-``self.model_rmvpe.infer_from_audio`` (``CudaRmvpe``).  The steps between the
+``self.model_rmvpe.infer_from_audio`` (``CudaRmvpe``) or
+``self.model_fcpe.infer`` (``CudaFcpe``).  The steps between the
 models run on the device through ``rvc_cuda.dsp``: the 48 Hz high-pass, the
 silence split, the retrieval blend (``CudaIndex``), the x2 interpolation and
 the protect blend, ``change_rms`` and the int16 conversion.
@@ -16,8 +17,7 @@ Host-side glue that stays in numpy: the reflect padding and slicing of the
 chunks, the frame alignment of pitch arrays (``:572-603``) and the f0
 post-processing of ``get_f0`` (``:468-482``, a few thousand values per call).
 
-Not offered here: the ``fcpe`` f0 method and ``brute_mix != 0``; asking
-for one raises ``NotImplementedError``.
+Not offered here: ``brute_mix != 0`` (raises ``NotImplementedError``).
 """
 
 from __future__ import annotations
@@ -74,15 +74,14 @@ class Pipeline:
 
     # ------------------------------------------------------------------ f0
     def get_f0(self, x, p_len, f0_up_key, f0_method):
-        """f0 of a segment (``rmvpe`` through ``self.model_rmvpe``, ``pm``
-        through the device autocorrelation) and the reference's
+        """f0 of a segment (``rmvpe`` through ``self.model_rmvpe``, ``fcpe``
+        through ``self.model_fcpe``, ``pm`` through the device
+        autocorrelation) and the reference's
         post-processing (``runtime/pipeline.py:408-483``): unvoiced frames
         linearly interpolated, transposed by ``f0_up_key`` semitones, then the
         mel quantisation to 1..255.  Returns ``(f0_coarse int32, f0 float32)``."""
         if f0_method not in ("pm", "rmvpe", "fcpe"):
             raise ValueError(f"Unsupported F0 method: {f0_method}")
-        if f0_method == "fcpe":
-            raise NotImplementedError("f0 method 'fcpe' is not on the device path (rmvpe and pm are)")
         f0_min, f0_max = 50, 1100
         f0_mel_min = 1127 * np.log(1 + f0_min / 700)
         f0_mel_max = 1127 * np.log(1 + f0_max / 700)
@@ -93,6 +92,12 @@ class Pipeline:
             right = p_len - len(f0) - pad_size
             if pad_size > 0 or right > 0:
                 f0 = np.pad(f0, (pad_size, right), mode="constant")
+        elif f0_method == "fcpe":                                      # :451-462
+            if not hasattr(self, "model_fcpe"):
+                raise RuntimeError("Pipeline.model_fcpe must be set (a CudaFcpe, or any object with "
+                                   "infer(x, sr, decoder_mode, threshold))")
+            f0 = np.asarray(self.model_fcpe.infer(np.asarray(x, dtype=np.float32), sr=16000,
+                                                  decoder_mode="local_argmax", threshold=0.006), dtype=np.float64)
         else:
             if not hasattr(self, "model_rmvpe"):
                 raise RuntimeError("Pipeline.model_rmvpe must be set (a CudaRmvpe, or any object with "

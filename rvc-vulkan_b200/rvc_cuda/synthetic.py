@@ -30,6 +30,7 @@ __all__ = [
     "make_vits_inputs", "make_vits_noise", "make_hubert_weights",
     "make_hubert_input", "coarse_pitch", "make_index", "make_queries",
     "make_rmvpe_weights", "make_rmvpe_input", "RMVPE_ENC", "RMVPE_INTER", "RMVPE_DEC", "make_speech_audio",
+    "make_fcpe_weights",
 ]
 
 # (sr, upsample_rates, upsample_kernels) of the two measured v2 generators.
@@ -350,3 +351,42 @@ def make_speech_audio(seconds: float = 60.0, seed: int = 0, sr: int = 16000, sil
     for s in range(step, T, step):
         y[s:s + ln] = 0.0
     return y.astype(np.float32)
+
+
+def make_fcpe_weights(seed: int = 0) -> dict:
+    """Random-init FCPE (CFNaiveMelPE, conv-only) state dict with the keys the
+    reference reads (``runtime/models/fcpe.py:237-302``): conv weights scaled by
+    1/sqrt(fan_in), norm gains near 1, the output projection's weight-norm gain
+    set to 2 so the 360 logits stay O(1) (an unsaturated sigmoid), and the
+    cent table of the bundled model (360 bins from 32.7 Hz to 1975.5 Hz)."""
+    rs = np.random.RandomState(95_000 + seed)
+
+    def n(*shape, std):
+        return (rs.standard_normal(shape) * std).astype(np.float32)
+
+    sd = {
+        "input_stack.0.weight": n(512, 128, 3, std=1.0 / math.sqrt(384)),
+        "input_stack.0.bias": n(512, std=0.1),
+        "input_stack.1.weight": (1.0 + n(512, std=0.1)).astype(np.float32),
+        "input_stack.1.bias": n(512, std=0.1),
+        "input_stack.3.weight": n(512, 512, 3, std=1.0 / math.sqrt(1536)),
+        "input_stack.3.bias": n(512, std=0.1),
+    }
+    for i in range(6):
+        p = f"net.encoder_layers.{i}.conformer.net"
+        sd[p + ".0.weight"] = (1.0 + n(512, std=0.1)).astype(np.float32)
+        sd[p + ".0.bias"] = n(512, std=0.1)
+        sd[p + ".2.weight"] = n(2048, 512, 1, std=1.0 / math.sqrt(512))
+        sd[p + ".2.bias"] = n(2048, std=0.1)
+        sd[p + ".4.conv.weight"] = n(1024, 1, 31, std=1.0 / math.sqrt(31))
+        sd[p + ".4.conv.bias"] = n(1024, std=0.1)
+        sd[p + ".6.weight"] = n(512, 1024, 1, std=0.5 / math.sqrt(1024))
+        sd[p + ".6.bias"] = n(512, std=0.1)
+    sd["norm.weight"] = (1.0 + n(512, std=0.1)).astype(np.float32)
+    sd["norm.bias"] = n(512, std=0.1)
+    sd["output_proj.weight_v"] = n(360, 512, std=1.0)
+    sd["output_proj.weight_g"] = np.full((360, 1), 2.0, np.float32)
+    sd["output_proj.bias"] = (-1.0 + n(360, std=0.1)).astype(np.float32)
+    sd["cent_table"] = np.linspace(1200.0 * np.log2(32.7 / 10.0), 1200.0 * np.log2(1975.5 / 10.0),
+                                   360).astype(np.float32)
+    return sd

@@ -233,6 +233,40 @@ def run_ivf(name, N, D, nlist, F, seed, edge, meta):
                   "inputs_sha256": digest([vecs, q])}
 
 
+# (name, T samples, weight seed, input seed)
+FCPE_CASES = [
+    ("fcpe_t24000", 24000, 0, 3),
+    ("fcpe_t3001", 3001, 0, 4),
+    ("fcpe_t400", 400, 0, 5),                 # shorter than the right pad: constant padding
+]
+
+
+def run_fcpe(name, T, wseed, iseed, meta):
+    """The reference's numpy ``FCPE`` (``runtime/models/fcpe.py:165-369``) with the
+    seeded synthetic checkpoint: log-mel, sigmoid latent, argmax and f0."""
+    from runtime.models import fcpe as rf  # noqa: PLC0415
+    sd = syn.make_fcpe_weights(wseed)
+    x = syn.make_rmvpe_input(T, iseed)
+    rf.load_pth = lambda path: {"model": sd}
+    with tempfile.TemporaryDirectory() as d:
+        open(os.path.join(d, "fcpe.pt"), "wb").close()
+        m = rf.FCPE(os.path.join(d, "fcpe.pt"))
+    mel = m._wav2mel(x)
+    lat = m._latent(mel)
+    f0 = m.infer(x)
+    # Pipeline.get_f0(..., "fcpe") with this model (runtime/pipeline.py:451-483)
+    from runtime import pipeline as rp  # noqa: PLC0415
+    sys.path.insert(0, HERE)
+    import pipeline_fakes as pf  # noqa: PLC0415
+    pipe = rp.Pipeline(40000, pf.config())
+    pipe.model_fcpe = m
+    coarse, f0bak = pipe.get_f0(x.astype(np.float64), T // 160 + 1, 3, "fcpe")
+    np.savez_compressed(os.path.join(HERE, name + ".npz"), mel=mel[0], latent=lat[0],
+                        argmax=lat[0].argmax(axis=1).astype(np.int64), f0=f0, pipe_coarse=coarse, pipe_f0bak=f0bak)
+    meta[name] = {"kind": "fcpe", "T": T, "weight_seed": wseed, "input_seed": iseed,
+                  "weights_sha256": weights_digest(sd), "inputs_sha256": digest([x])}
+
+
 def run_ops(nn, meta):
     """Per-op vectors from ``runtime.nn``'s numpy kernels (``_conv1d_numpy`` etc.)."""
     rs = np.random.RandomState(4242)
@@ -381,7 +415,7 @@ PIPE_CASES = [
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("RVC_REFERENCE", "/root/reference"))
-    ap.add_argument("--only", choices=["vits", "hubert", "ops", "retrieval", "rmvpe", "partial", "dsp", "ivf"], default=None,
+    ap.add_argument("--only", choices=["vits", "hubert", "ops", "retrieval", "rmvpe", "partial", "dsp", "ivf", "fcpe"], default=None,
                     help="regenerate one family and keep the other fixtures")
     args = ap.parse_args()
     os.environ["RVC_BACKEND"] = "numpy"
@@ -414,6 +448,9 @@ def main():
             run_rmvpe(runtime_rmvpe, *c, meta)
     if args.only in (None, "dsp"):
         run_dsp(meta)
+    if args.only in (None, "fcpe"):
+        for c in FCPE_CASES:
+            run_fcpe(*c, meta)
     if args.only in (None, "ivf"):
         for c in IVF_CASES:
             run_ivf(*c, meta)

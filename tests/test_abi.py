@@ -132,6 +132,22 @@ def test_dsp_patch_reference_replaces_pipeline_functions():
     assert dsp.patch_reference(pipe_mod) is pipe_mod  # idempotent
 
 
+def test_fcpe_patch_reference_replaces_infer():
+    import types
+
+    from rvc_cuda import fcpe
+
+    class FakeFcpe:
+        def infer(self, x, sr=16000, decoder_mode="local_argmax", threshold=0.006):
+            return "numpy"
+
+    mod = types.SimpleNamespace(FCPE=FakeFcpe)
+    cls = fcpe.patch_reference(mod)
+    assert cls is FakeFcpe and FakeFcpe.infer is not FakeFcpe._rvc_cuda_orig_infer
+    assert fcpe.patch_reference(mod) is FakeFcpe  # idempotent
+    assert fcpe.frames(16000) == 101 and fcpe.frames(159) == 1
+
+
 def test_rmvpe_frames_and_patch_reference():
     from rvc_cuda import rmvpe
 

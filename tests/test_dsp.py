@@ -133,7 +133,7 @@ def test_resample_oracle_matches_reference(method, gold):
 def test_pipeline_rejects_what_is_not_on_the_device_path():
     from rvc_cuda import pipeline as P
     pipe = P.Pipeline(40000, pf.config())
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(RuntimeError):  # no model_fcpe assigned
         pipe.get_f0(np.zeros(1000), 6, 0, "fcpe")
     with pytest.raises(ValueError):
         pipe.get_f0(np.zeros(1000), 6, 0, "crepe")

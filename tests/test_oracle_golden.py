@@ -156,3 +156,22 @@ def test_ivf_oracle_matches_reference(name, golden_meta):
     pitchf = np.full((1, 2 * m["F"]), 150.0, np.float32)
     pitchf[0, ::3] = 0.0
     np.testing.assert_array_equal(OD.protect_blend(f, f0, pitchf, 0.33), g["prep_feats"])
+
+
+FCPE = ["fcpe_t24000", "fcpe_t3001", "fcpe_t400"]
+
+
+@pytest.mark.parametrize("name", FCPE)
+def test_fcpe_oracle_matches_reference(name, golden_meta):
+    from oracle import fcpe as OF
+    m = golden_meta[name]
+    sd = syn.make_fcpe_weights(m["weight_seed"])
+    assert weights_digest(sd) == m["weights_sha256"]
+    x = syn.make_rmvpe_input(m["T"], m["input_seed"])
+    g = load_golden(name)
+    mel = OF.log_mel(x)
+    np.testing.assert_array_equal(mel, g["mel"])
+    lat = OF.latent(sd, mel)
+    assert rel_l2(lat, g["latent"]) < 1e-5
+    np.testing.assert_array_equal(lat.argmax(axis=1), g["argmax"])
+    np.testing.assert_allclose(OF.decode(lat, sd["cent_table"]), g["f0"], rtol=1e-5)
