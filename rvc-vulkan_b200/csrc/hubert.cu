@@ -293,7 +293,9 @@ void HubertModel::encode_device(int B, int64_t T, const float* x, int version, f
     {
       cudaEvent_t e0 = nullptr, e1 = nullptr;
       if (ctx->prof) ctx->prof_begin(&e0, &e1);
-      k_attention(buf("qkv"), 3 * D, 0, D, 2 * D, B, kHeads, kHeadD, (int)L, 8.f, buf("att"), D, st);
+      if (precision == 1 || !k_attention_tc(ctx, buf("qkv"), 3 * D, 0, D, 2 * D, nullptr, nullptr, B, kHeads, kHeadD,
+                                             (int)L, -1, 8.f, buf("att"), D))
+        k_attention(buf("qkv"), 3 * D, 0, D, 2 * D, B, kHeads, kHeadD, (int)L, 8.f, buf("att"), D, st);
       if (ctx->prof)
         ctx->prof_end(e0, e1, 4.0 * B * kHeads * (double)L * L * kHeadD,
                       "attn hubert B=" + std::to_string(B) + " L=" + std::to_string(L), false);

@@ -73,8 +73,15 @@ void k_taps_to_channels(const float* W, int O, int I, int K, int j0, int nt, flo
 void k_attention(const float* qkv, int qkv_ld, int q_off, int k_off, int v_off, int B, int heads, int D, int P,
                  float q_div, float* y, int y_ld, cudaStream_t st);
 
-// ---- pipeline signal processing (dsp.cu); device pointers unless noted
+// ---- tensor-core attention (tc_attn.cu)
 struct Context;
+// Same contract as k_rel_attention (window >= 0, q / q_div) / k_attention
+// (window < 0) on the tensor cores (BF16x3); false when the head size is not
+// served (D % 16 != 0 or D > 96), the caller then runs the SIMT kernel.
+bool k_attention_tc(Context* ctx, const float* qkv, int ld, int q_off, int k_off, int v_off, const float* emb_k,
+                    const float* emb_v, int B, int heads, int D, int P, int window, float q_div, float* y, int y_ld);
+
+// ---- pipeline signal processing (dsp.cu); device pointers unless noted
 // scipy.signal.filtfilt(b, a, x) with padtype 'odd' (b, a host arrays), float64
 void dsp_filtfilt(Context* ctx, const double* b, int nb, const double* a, int na, const double* x_dev, long long n,
                   bool ext_f32, double* y_dev);

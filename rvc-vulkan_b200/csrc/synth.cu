@@ -243,8 +243,12 @@ void SynthModel::enc_stage(int B, int P, const float* phone, const long long* pi
     {
       cudaEvent_t e0 = nullptr, e1 = nullptr;
       if (ctx->prof) ctx->prof_begin(&e0, &e1);
-      k_rel_attention(buf("qkv"), 3 * H, 0, H, 2 * H, W(p + ".emb_rel_k").buf.f(), W(p + ".emb_rel_v").buf.f(), B,
-                      cfg.heads, cfg.kc, P, cfg.window, buf("S"), buf("att"), H, st);
+      if (cfg.precision == 1 ||
+          !k_attention_tc(ctx, buf("qkv"), 3 * H, 0, H, 2 * H, W(p + ".emb_rel_k").buf.f(),
+                          W(p + ".emb_rel_v").buf.f(), B, cfg.heads, cfg.kc, P, cfg.window,
+                          (float)std::sqrt((double)cfg.kc), buf("att"), H))
+        k_rel_attention(buf("qkv"), 3 * H, 0, H, 2 * H, W(p + ".emb_rel_k").buf.f(), W(p + ".emb_rel_v").buf.f(), B,
+                        cfg.heads, cfg.kc, P, cfg.window, buf("S"), buf("att"), H, st);
       if (ctx->prof)
         ctx->prof_end(e0, e1, 4.0 * B * cfg.heads * (double)P * P * cfg.kc,
                       "attn enc_p B=" + std::to_string(B) + " P=" + std::to_string(P), false);

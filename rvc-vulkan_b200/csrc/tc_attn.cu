@@ -1,0 +1,519 @@
+// Tensor-core (tcgen05) scaled-dot-product attention, BF16x3, for the HuBERT
+// encoder (runtime/models/hubert.py:1315-1400: softmax(q k^T / 8) v over 12
+// heads of 64) and, with a relative-position band, the text encoder
+// (runtime/models/vits.py:993-1014).
+//
+// Pack step: q / q_div, k and v of every (chunk, head) are split into bf16
+// hi + lo planes and written in the tcgen05 K-major core-matrix layouts the
+// MMAs read, so tiles reach shared memory with plain bulk copies:
+//   Q tile [128 rows][D]           : (k/8)*128*16 + r*16 + (k%8)*2 per plane
+//   K tile [hi 128 keys | lo 128]  : (k/8)*256*16 + n*16 + (k%8)*2   (stacked N = 256)
+//   V tile [hi D rows | lo D rows] : (j/8)*2D*16 + n*16 + (j%8)*2   (keys are the K dim)
+// Main kernel, one 128-query tile per work item (persistent CTAs):
+//   warp 0  bulk-copies Q once and K / V per 128-key tile;
+//   warp 1  issues S = Qhi.[Khi|Klo] + Qlo.Khi (N = 256 and 128) into TMEM, then
+//           O_t = Phi.[Vhi|Vlo] + Plo.Vhi (N = 2D and D);
+//   warps 2-5 (one query row per thread) read S, keep the running max / sum,
+//           write P = exp(s - m) as bf16 hi / lo planes for the second MMA and
+//           fold each tile's O_t into a register accumulator (rescaled when the
+//           running max moves); band bias and band output term added on the
+//           CUDA cores when a window is given.
+// Every mbarrier wait is bounded; on a timeout the kernel records an error and
+// winds down.
+#include "context.cuh"
+#include "kernels.cuh"
+#include "tc_ptx.cuh"
+
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+
+namespace rvc {
+
+namespace {
+
+constexpr int kTQ = 128;   // queries per tile
+constexpr int kTK = 128;   // keys per tile
+constexpr int kAThreads = 192;
+constexpr uint64_t kAttnWaitNs = 2000000000ull;
+constexpr int kMaxWin = 16;
+
+__device__ __forceinline__ void split2(float v, uint16_t& hi, uint16_t& lo) {
+  const __nv_bfloat16 h = __float2bfloat16_rn(v);
+  hi = __bfloat16_as_ushort(h);
+  lo = __bfloat16_as_ushort(__float2bfloat16_rn(v - __bfloat162float(h)));
+}
+
+// q/k/v [B][P][ld] fp32 -> packed tiles.  One thread per (bh, row, 8-element chunk).
+__global__ void attn_pack_kernel(const float* __restrict__ qkv, int ld, int q_off, int k_off, int v_off, int heads,
+                                 int D, int P, int nq, int nk, float q_div, uint16_t* __restrict__ Qp,
+                                 uint16_t* __restrict__ Kp, uint16_t* __restrict__ Vp, long long total) {
+  const int dc = D / 8;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(e % dc);
+    const long long rest = e / dc;
+    const int r = (int)(rest % (nq * kTQ));  // padded row (queries and keys share the padded length)
+    const int bh = (int)(rest / (nq * kTQ));
+    const int b = bh / heads, h = bh % heads;
+    const bool ok = r < P;
+    const float* row = qkv + ((long long)b * P + (ok ? r : 0)) * ld;
+    uint16_t qh[8], ql[8], kh[8], kl[8], vh[8], vl[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int d = c * 8 + i;
+      const float q = ok ? row[q_off + h * D + d] / q_div : 0.f;
+      const float k = ok ? row[k_off + h * D + d] : 0.f;
+      const float v = ok ? row[v_off + h * D + d] : 0.f;
+      split2(q, qh[i], ql[i]);
+      split2(k, kh[i], kl[i]);
+      split2(v, vh[i], vl[i]);
+    }
+    // Q: tile qt = r / 128, plane-major
+    {
+      const int qt = r / kTQ, rr = r % kTQ;
+      uint16_t* base = Qp + ((long long)bh * nq + qt) * 2 * (kTQ * D);
+      const long long off = (long long)c * kTQ * 8 + rr * 8;
+      *reinterpret_cast<uint4*>(base + off) = *reinterpret_cast<const uint4*>(qh);
+      *reinterpret_cast<uint4*>(base + kTQ * D + off) = *reinterpret_cast<const uint4*>(ql);
+    }
+    if (r < nk * kTK) {
+      const int kt = r / kTK, rr = r % kTK;
+      uint16_t* kb = Kp + ((long long)bh * nk + kt) * (2 * kTK * D);
+      const long long off = (long long)c * (2 * kTK) * 8;
+      *reinterpret_cast<uint4*>(kb + off + rr * 8) = *reinterpret_cast<const uint4*>(kh);
+      *reinterpret_cast<uint4*>(kb + off + (kTK + rr) * 8) = *reinterpret_cast<const uint4*>(kl);
+      // V: key rr is element (rr % 8) of key chunk rr / 8; rows n = d (hi) and D + d (lo)
+      uint16_t* vb = Vp + ((long long)bh * nk + kt) * (2 * kTK * D);
+      const long long vchunk = (long long)(rr / 8) * (2 * D) * 8;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int d = c * 8 + i;
+        vb[vchunk + (long long)d * 8 + (rr % 8)] = vh[i];
+        vb[vchunk + (long long)(D + d) * 8 + (rr % 8)] = vl[i];
+      }
+    }
+  }
+}
+
+struct AttnArgs {
+  const uint16_t* Qp;
+  const uint16_t* Kp;
+  const uint16_t* Vp;
+  int heads, D, P, nq, nk;
+  float* y;
+  int y_ld;
+  // relative band (window < 0: none)
+  int window;
+  const float* rk;     // [B*heads][P][2W+1] qs . emb_k[r]
+  const float* qkv;    // fp32 source for the band scores
+  int ld, q_off, k_off;
+  float q_div;
+  const float* emb_v;  // [2W+1][D]
+  int* err;
+  int BH;              // chunks x heads
+};
+
+template <int D>
+__global__ void __launch_bounds__(kAThreads, 1) tc_attn_kernel(const __grid_constant__ AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  const uint32_t q_plane = (uint32_t)kTQ * D * 2u;      // bytes per Q plane
+  const uint32_t k_bytes = (uint32_t)2 * kTK * D * 2u;  // stacked hi|lo
+  const uint32_t v_bytes = (uint32_t)2 * kTK * D * 2u;
+  const uint32_t p_plane = (uint32_t)kTQ * kTK * 2u;
+  const uint32_t sbase = ptx::smem_u32(smem);
+  const uint32_t off_q = 0, off_k = off_q + 2 * q_plane, off_v = off_k + k_bytes, off_p = off_v + v_bytes;
+  const uint32_t off_bar = off_p + 2 * p_plane;
+  // barriers
+  const uint32_t Q_FULL = sbase + off_bar, Q_EMPTY = Q_FULL + 8, KV_FULL = Q_FULL + 16, KV_EMPTY = Q_FULL + 24;
+  const uint32_t S_FULL = Q_FULL + 32, S_EMPTY = Q_FULL + 40, P_FULL = Q_FULL + 48, PV_FULL = Q_FULL + 56;
+  const uint32_t PV_EMPTY = Q_FULL + 64;
+  uint32_t* tmem_slot = (uint32_t*)(smem + off_bar + 72);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(Q_FULL, 1);
+    ptx::mbar_init(Q_EMPTY, 1);
+    ptx::mbar_init(KV_FULL, 1);
+    ptx::mbar_init(KV_EMPTY, 1);
+    ptx::mbar_init(S_FULL, 1);
+    ptx::mbar_init(S_EMPTY, 4);
+    ptx::mbar_init(P_FULL, 4);
+    ptx::mbar_init(PV_FULL, 1);
+    ptx::mbar_init(PV_EMPTY, 4);
+    ptx::fence_mbar_init();
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(ptx::smem_u32(tmem_slot), 512);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t S_COL = 0, PV_COL = 256;  // S: 256 columns (stacked), O_t: 2D columns
+  const int total_items = a.BH * a.nq;
+
+  if (warp == 0) {
+    // ------------------------------------------------ loader
+    if (lane == 0) {
+      int qi = 0, kvi = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; it < total_items && ok; it += gridDim.x) {
+        const int bh = it / a.nq, qt = it % a.nq;
+        if (!ptx::mbar_wait(Q_EMPTY, (qi & 1) ^ 1, kAttnWaitNs)) {
+          atomicExch(a.err, 21);
+          ok = false;
+          break;
+        }
+        ++qi;
+        ptx::mbar_expect_tx(Q_FULL, 2 * q_plane);
+        ptx::bulk_g2s(sbase + off_q, a.Qp + ((long long)bh * a.nq + qt) * 2 * (kTQ * D), 2 * q_plane, Q_FULL);
+        for (int kt = 0; kt < a.nk; ++kt, ++kvi) {
+          if (!ptx::mbar_wait(KV_EMPTY, (kvi & 1) ^ 1, kAttnWaitNs)) {
+            atomicExch(a.err, 22);
+            ok = false;
+            break;
+          }
+          ptx::mbar_expect_tx(KV_FULL, k_bytes + v_bytes);
+          const long long tile = (long long)bh * a.nk + kt;
+          ptx::bulk_g2s(sbase + off_k, a.Kp + tile * (2 * kTK * D), k_bytes, KV_FULL);
+          ptx::bulk_g2s(sbase + off_v, a.Vp + tile * (2 * kTK * D), v_bytes, KV_FULL);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t id_s2 = ptx::idesc_bf16_f32(128, 2 * kTK), id_s1 = ptx::idesc_bf16_f32(128, kTK);
+      const uint32_t id_v2 = ptx::idesc_bf16_f32(128, 2 * D), id_v1 = ptx::idesc_bf16_f32(128, D);
+      const uint32_t lbo_q = (uint32_t)kTQ * 16u, lbo_k = (uint32_t)2 * kTK * 16u;
+      const uint32_t lbo_p = (uint32_t)kTQ * 16u, lbo_v = (uint32_t)2 * D * 16u;
+      int qi = 0, kvi = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; it < total_items && ok; it += gridDim.x) {
+        if (!ptx::mbar_wait(Q_FULL, qi & 1, kAttnWaitNs)) {
+          atomicExch(a.err, 23);
+          ok = false;
+          break;
+        }
+        ++qi;
+        for (int kt = 0; kt < a.nk && ok; ++kt, ++kvi) {
+          const uint32_t ph = kvi & 1;
+          if (!ptx::mbar_wait(KV_FULL, ph, kAttnWaitNs) || !ptx::mbar_wait(S_EMPTY, ph ^ 1, kAttnWaitNs)) {
+            atomicExch(a.err, 24);
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          // S = Qhi.[Khi|Klo] (N = 256) + Qlo.Khi (N = 128), K = D in steps of 16
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint64_t dqh = ptx::smem_desc(sbase + off_q + (uint32_t)kk * 2u * lbo_q, lbo_q, 128);
+            const uint64_t dql = ptx::smem_desc(sbase + off_q + q_plane + (uint32_t)kk * 2u * lbo_q, lbo_q, 128);
+            const uint64_t dk = ptx::smem_desc(sbase + off_k + (uint32_t)kk * 2u * lbo_k, lbo_k, 128);
+            ptx::mma_bf16(tmem + S_COL, dqh, dk, id_s2, kk > 0 ? 1u : 0u);
+            ptx::mma_bf16(tmem + S_COL, dql, dk, id_s1, 1u);
+          }
+          ptx::mma_commit(S_FULL);
+          if (!ptx::mbar_wait(P_FULL, ph, kAttnWaitNs) || !ptx::mbar_wait(PV_EMPTY, ph ^ 1, kAttnWaitNs)) {
+            atomicExch(a.err, 25);
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          // O_t = Phi.[Vhi|Vlo] (N = 2D) + Plo.Vhi (N = D), K = 128 keys in steps of 16
+          for (int kk = 0; kk < kTK / 16; ++kk) {
+            const uint64_t dph = ptx::smem_desc(sbase + off_p + (uint32_t)kk * 2u * lbo_p, lbo_p, 128);
+            const uint64_t dpl = ptx::smem_desc(sbase + off_p + p_plane + (uint32_t)kk * 2u * lbo_p, lbo_p, 128);
+            const uint64_t dv = ptx::smem_desc(sbase + off_v + (uint32_t)kk * 2u * lbo_v, lbo_v, 128);
+            ptx::mma_bf16(tmem + PV_COL, dph, dv, id_v2, kk > 0 ? 1u : 0u);
+            ptx::mma_bf16(tmem + PV_COL, dpl, dv, id_v1, 1u);
+          }
+          ptx::mma_commit(PV_FULL);
+          ptx::mma_commit(KV_EMPTY);
+        }
+        if (ok) ptx::mma_commit(Q_EMPTY);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------ softmax warps: one query row per thread
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const int nb = 2 * a.window + 1;
+    int kvi = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < total_items && ok; it += gridDim.x) {
+      const int bh = it / a.nq, qt = it % a.nq;
+      const int i = qt * kTQ + row;  // query index
+      float o[D];
+#pragma unroll
+      for (int d = 0; d < D; ++d) o[d] = 0.f;
+      float m = -INFINITY, l = 0.f;
+      float rk[2 * kMaxWin + 1];
+      if (a.window >= 0) {
+        const float* rr = a.rk + ((long long)bh * a.P + (i < a.P ? i : 0)) * nb;
+        for (int r = 0; r < nb; ++r) rk[r] = rr[r];
+      }
+      for (int kt = 0; kt < a.nk; ++kt, ++kvi) {
+        const uint32_t ph = kvi & 1;
+        const bool got = __all_sync(0xffffffffu, ptx::mbar_wait(S_FULL, ph, kAttnWaitNs));
+        if (!got) {
+          if (lane == 0) atomicExch(a.err, 26);
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        const int j0 = kt * kTK;
+        // pass A: row max of this tile
+        float tmax = -INFINITY;
+        for (int c = 0; c < kTK; c += 32) {
+          float s1[32];
+          ptx::tmem_ld32(tmem + lane_base + S_COL + (uint32_t)c, s1);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float s2[16];
+            ptx::tmem_ld16(tmem + lane_base + S_COL + (uint32_t)(kTK + c + 16 * h), s2);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              const int j = j0 + c + 16 * h + k;
+              float s = s1[16 * h + k] + s2[k];
+              if (a.window >= 0) {
+                const int rel = j - i;
+                if (rel >= -a.window && rel <= a.window) s = s + rk[rel + a.window];
+              }
+              if (j >= a.P) s = -INFINITY;
+              tmax = fmaxf(tmax, s);
+            }
+          }
+        }
+        const float m_new = fmaxf(m, tmax);
+        // fold the previous tile's O_t (computed with exp(s - m)) into the accumulator
+        if (kt > 0) {
+          const bool pv = __all_sync(0xffffffffu, ptx::mbar_wait(PV_FULL, ph ^ 1, kAttnWaitNs));
+          if (!pv) {
+            if (lane == 0) atomicExch(a.err, 27);
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          // O_{t-1} was formed with exp(s - m): the accumulator is at the same scale here
+#pragma unroll
+          for (int c = 0; c < D; c += 16) {
+            float u1[16], u2[16];
+            ptx::tmem_ld16(tmem + lane_base + PV_COL + (uint32_t)c, u1);
+            ptx::tmem_ld16(tmem + lane_base + PV_COL + (uint32_t)(D + c), u2);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) o[c + k] = o[c + k] + (u1[k] + u2[k]);
+          }
+          ptx::tc_fence_before();
+          if (lane == 0) ptx::mbar_arrive(PV_EMPTY);
+        }
+        // rescale the accumulator (all earlier tiles) to the new max
+        const float scale = (m == -INFINITY) ? 0.f : expf(m - m_new);
+#pragma unroll
+        for (int d = 0; d < D; ++d) o[d] *= scale;
+        l *= scale;
+        // pass B: p = exp(s - m_new) -> bf16 hi / lo planes, row sum
+        float sum = 0.f;
+        for (int c = 0; c < kTK; c += 32) {
+          float s1[32];
+          ptx::tmem_ld32(tmem + lane_base + S_COL + (uint32_t)c, s1);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float s2[16];
+            ptx::tmem_ld16(tmem + lane_base + S_COL + (uint32_t)(kTK + c + 16 * h), s2);
+            uint16_t ph16[16], pl16[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              const int j = j0 + c + 16 * h + k;
+              float s = s1[16 * h + k] + s2[k];
+              if (a.window >= 0) {
+                const int rel = j - i;
+                if (rel >= -a.window && rel <= a.window) s = s + rk[rel + a.window];
+              }
+              const float p = (j < a.P && m_new != -INFINITY) ? expf(s - m_new) : 0.f;
+              sum += p;
+              split2(p, ph16[k], pl16[k]);
+            }
+#pragma unroll
+            for (int g2 = 0; g2 < 2; ++g2) {
+              const int jc = (c + 16 * h) / 8 + g2;  // key chunk
+              const uint32_t off = (uint32_t)jc * (kTQ * 16u) + (uint32_t)row * 16u;
+              const uint4 vh = *reinterpret_cast<const uint4*>(ph16 + 8 * g2);
+              const uint4 vl = *reinterpret_cast<const uint4*>(pl16 + 8 * g2);
+              asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sbase + off_p + off), "r"(vh.x), "r"(vh.y),
+                           "r"(vh.z), "r"(vh.w)
+                           : "memory");
+              asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sbase + off_p + p_plane + off), "r"(vl.x),
+                           "r"(vl.y), "r"(vl.z), "r"(vl.w)
+                           : "memory");
+            }
+          }
+        }
+        l += sum;
+        m = m_new;
+        ptx::fence_proxy_async_smem();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          ptx::mbar_arrive(S_EMPTY);
+          ptx::mbar_arrive(P_FULL);
+        }
+      }
+      if (!ok) break;
+      // the last tile's O_t
+      {
+        const uint32_t ph = (kvi - 1) & 1;
+        const bool pv = __all_sync(0xffffffffu, ptx::mbar_wait(PV_FULL, ph, kAttnWaitNs));
+        if (!pv) {
+          if (lane == 0) atomicExch(a.err, 28);
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D; c += 16) {
+          float u1[16], u2[16];
+          ptx::tmem_ld16(tmem + lane_base + PV_COL + (uint32_t)c, u1);
+          ptx::tmem_ld16(tmem + lane_base + PV_COL + (uint32_t)(D + c), u2);
+#pragma unroll
+          for (int k = 0; k < 16; ++k) o[c + k] = o[c + k] + (u1[k] + u2[k]);
+        }
+        ptx::tc_fence_before();
+        if (lane == 0) ptx::mbar_arrive(PV_EMPTY);
+      }
+      if (i < a.P) {
+        const int b = bh / a.heads, h = bh % a.heads;
+        float* yr = a.y + ((long long)b * a.P + i) * a.y_ld + h * D;
+        if (a.window >= 0) {
+          // band term: p(i, i + r - W) from the final max / sum, times emb_v[r]
+          const float* qr = a.qkv + ((long long)b * a.P + i) * a.ld + a.q_off + h * D;
+          float pb[2 * kMaxWin + 1];
+          for (int r = 0; r < nb; ++r) {
+            const int j = i + r - a.window;
+            float p = 0.f;
+            if (j >= 0 && j < a.P) {
+              const float* kr = a.qkv + ((long long)b * a.P + j) * a.ld + a.k_off + h * D;
+              float sc = 0.f;
+              for (int d = 0; d < D; ++d) sc = fmaf(qr[d] / a.q_div, kr[d], sc);
+              p = expf(sc + rk[r] - m) / l;
+            }
+            pb[r] = p;
+          }
+#pragma unroll
+          for (int d = 0; d < D; ++d) {
+            float band = 0.f;
+            for (int r = 0; r < nb; ++r) band = fmaf(pb[r], a.emb_v[(long long)r * D + d], band);
+            yr[d] = o[d] / l + band;
+          }
+        } else {
+#pragma unroll
+          for (int d = 0; d < D; ++d) yr[d] = o[d] / l;
+        }
+      }
+    }
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  if (warp == 1) ptx::tmem_dealloc(tmem, 512);
+}
+
+// qs . emb_k[r] for every query row: rk[bh][i][r]
+__global__ void attn_rel_k_kernel(const float* __restrict__ qkv, int ld, int q_off, int heads, int D, int P, int W,
+                                  float q_div, const float* __restrict__ emb_k, float* __restrict__ rk,
+                                  long long total) {
+  const int nb = 2 * W + 1;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int r = (int)(e % nb);
+    const long long rest = e / nb;
+    const int i = (int)(rest % P);
+    const int bh = (int)(rest / P);
+    const int b = bh / heads, h = bh % heads;
+    const float* q = qkv + ((long long)b * P + i) * ld + q_off + h * D;
+    float s = 0.f;
+    for (int d = 0; d < D; ++d) s = fmaf(q[d] / q_div, emb_k[(long long)r * D + d], s);
+    rk[e] = s;
+  }
+}
+
+}  // namespace
+
+// Returns false when the shape is not served (the caller then runs the SIMT kernel).
+bool k_attention_tc(Context* ctx, const float* qkv, int ld, int q_off, int k_off, int v_off, const float* emb_k,
+                    const float* emb_v, int B, int heads, int D, int P, int window, float q_div, float* y, int y_ld) {
+  if (B * P == 0) return true;
+  if ((D != 64 && D != 96) || window > kMaxWin) return false;
+  cudaStream_t st = ctx->stream;
+  const int nq = (P + kTQ - 1) / kTQ, nk = (P + kTK - 1) / kTK;
+  const int BH = B * heads;
+  const size_t tile_elems = (size_t)2 * kTQ * D;  // one Q tile (2 planes) == one K or V tile
+  DevBuf Qp(ctx, sizeof(uint16_t) * tile_elems * BH * nq), Kp(ctx, sizeof(uint16_t) * tile_elems * BH * nk),
+      Vp(ctx, sizeof(uint16_t) * tile_elems * BH * nk), err(ctx, sizeof(int));
+  const long long total = (long long)BH * nq * kTQ * (D / 8);
+  attn_pack_kernel<<<(int)std::min<long long>((total + 255) / 256, 148ll * 32), 256, 0, st>>>(
+      qkv, ld, q_off, k_off, v_off, heads, D, P, nq, nk, q_div, Qp.as<uint16_t>(), Kp.as<uint16_t>(),
+      Vp.as<uint16_t>(), total);
+  note_launch();
+  RVC_CUDA_TRY(cudaGetLastError());
+  DevBuf rk;
+  if (window >= 0) {
+    const long long n = (long long)BH * P * (2 * window + 1);
+    rk = DevBuf(ctx, sizeof(float) * (size_t)n);
+    attn_rel_k_kernel<<<(int)std::min<long long>((n + 255) / 256, 148ll * 32), 256, 0, st>>>(
+        qkv, ld, q_off, heads, D, P, window, q_div, emb_k, rk.f(), n);
+    note_launch();
+    RVC_CUDA_TRY(cudaGetLastError());
+  }
+  AttnArgs a;
+  a.Qp = Qp.as<uint16_t>();
+  a.Kp = Kp.as<uint16_t>();
+  a.Vp = Vp.as<uint16_t>();
+  a.heads = heads;
+  a.D = D;
+  a.P = P;
+  a.nq = nq;
+  a.nk = nk;
+  a.y = y;
+  a.y_ld = y_ld;
+  a.window = window;
+  a.rk = rk.f();
+  a.qkv = qkv;
+  a.ld = ld;
+  a.q_off = q_off;
+  a.k_off = k_off;
+  a.q_div = q_div;
+  a.emb_v = emb_v;
+  a.err = err.as<int>();
+  a.BH = BH;
+  const size_t smem = 1024 + (size_t)2 * kTQ * D * 2 + (size_t)2 * kTK * D * 2 * 2 + (size_t)2 * kTQ * kTK * 2 + 128;
+  static std::atomic<uint64_t> attr_done{0};
+  int dev = 0;
+  RVC_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 64 && !(attr_done.load() & (1ull << dev))) {
+    RVC_CUDA_TRY(cudaFuncSetAttribute(tc_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    RVC_CUDA_TRY(cudaFuncSetAttribute(tc_attn_kernel<96>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    attr_done.fetch_or(1ull << dev);
+  }
+  const int items = BH * nq;
+  if (D == 64)
+    tc_attn_kernel<64><<<std::min(items, 148), kAThreads, smem, st>>>(a);
+  else
+    tc_attn_kernel<96><<<std::min(items, 148), kAThreads, smem, st>>>(a);
+  note_launch();
+  RVC_CUDA_TRY(cudaGetLastError());
+  int h_err = 0;
+  RVC_CUDA_TRY(cudaMemcpyAsync(&h_err, err.p, sizeof(int), cudaMemcpyDeviceToHost, st));
+  RVC_CUDA_TRY(cudaStreamSynchronize(st));
+  if (h_err != 0) throw Error{kErrTimeout, "attention: a bounded wait gave up (code " + std::to_string(h_err) + ")"};
+  return true;
+}
+
+}  // namespace rvc
