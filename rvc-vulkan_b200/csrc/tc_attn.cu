@@ -108,9 +108,7 @@ struct AttnArgs {
   // relative band (window < 0: none)
   int window;
   const float* rk;     // [B*heads][P][2W+1] qs . emb_k[r]
-  const float* qkv;    // fp32 source for the band scores
-  int ld, q_off, k_off;
-  float q_div;
+  const float* sb;     // [B*heads][P][2W+1] band logits qs . k[i + r - W] + rk (-inf outside)
   const float* emb_v;  // [2W+1][D]
   int* err;
   int BH;              // chunks x heads
@@ -391,31 +389,24 @@ __global__ void __launch_bounds__(kAThreads, 1) tc_attn_kernel(const __grid_cons
       if (i < a.P) {
         const int b = bh / a.heads, h = bh % a.heads;
         float* yr = a.y + ((long long)b * a.P + i) * a.y_ld + h * D;
+        const float inv_l = 1.f / l;
         if (a.window >= 0) {
           // band term: p(i, i + r - W) from the final max / sum, times emb_v[r]
-          const float* qr = a.qkv + ((long long)b * a.P + i) * a.ld + a.q_off + h * D;
+          const float* sbr = a.sb + ((long long)bh * a.P + i) * nb;
           float pb[2 * kMaxWin + 1];
-          for (int r = 0; r < nb; ++r) {
-            const int j = i + r - a.window;
-            float p = 0.f;
-            if (j >= 0 && j < a.P) {
-              const float* kr = a.qkv + ((long long)b * a.P + j) * a.ld + a.k_off + h * D;
-              float sc = 0.f;
-              for (int d = 0; d < D; ++d) sc = fmaf(qr[d] / a.q_div, kr[d], sc);
-              p = expf(sc + rk[r] - m) / l;
-            }
-            pb[r] = p;
-          }
+          for (int r = 0; r < nb; ++r) pb[r] = expf(sbr[r] - m) * inv_l;
 #pragma unroll
           for (int d = 0; d < D; ++d) {
             float band = 0.f;
             for (int r = 0; r < nb; ++r) band = fmaf(pb[r], a.emb_v[(long long)r * D + d], band);
-            yr[d] = o[d] / l + band;
+            o[d] = o[d] * inv_l + band;
           }
         } else {
 #pragma unroll
-          for (int d = 0; d < D; ++d) yr[d] = o[d] / l;
+          for (int d = 0; d < D; ++d) o[d] = o[d] * inv_l;
         }
+#pragma unroll
+        for (int d = 0; d < D; d += 4) *reinterpret_cast<float4*>(yr + d) = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
       }
     }
   }
@@ -425,22 +416,43 @@ __global__ void __launch_bounds__(kAThreads, 1) tc_attn_kernel(const __grid_cons
   if (warp == 1) ptx::tmem_dealloc(tmem, 512);
 }
 
-// qs . emb_k[r] for every query row: rk[bh][i][r]
-__global__ void attn_rel_k_kernel(const float* __restrict__ qkv, int ld, int q_off, int heads, int D, int P, int W,
-                                  float q_div, const float* __restrict__ emb_k, float* __restrict__ rk,
-                                  long long total) {
+// One warp per (chunk x head, query row): rk[r] = qs . emb_k[r] (added to the
+// band of S) and sb[r] = qs . k[i + r - W] + rk[r] (the band logits the output
+// term uses), r < 2W + 1, lanes over the head dimension.
+__global__ void attn_band_kernel(const float* __restrict__ qkv, int ld, int q_off, int k_off, int heads, int D,
+                                 int P, int W, float q_div, const float* __restrict__ emb_k, float* __restrict__ rk,
+                                 float* __restrict__ sb, long long rows) {
+  const long long wr = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (wr >= rows) return;
+  const int i = (int)(wr % P);
+  const int bh = (int)(wr / P);
+  const int b = bh / heads, h = bh % heads;
+  const float* q = qkv + ((long long)b * P + i) * ld + q_off + h * D;
   const int nb = 2 * W + 1;
-  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
-       e += (long long)gridDim.x * blockDim.x) {
-    const int r = (int)(e % nb);
-    const long long rest = e / nb;
-    const int i = (int)(rest % P);
-    const int bh = (int)(rest / P);
-    const int b = bh / heads, h = bh % heads;
-    const float* q = qkv + ((long long)b * P + i) * ld + q_off + h * D;
-    float s = 0.f;
-    for (int d = 0; d < D; ++d) s = fmaf(q[d] / q_div, emb_k[(long long)r * D + d], s);
-    rk[e] = s;
+  float qs[4];
+#pragma unroll
+  for (int t = 0; t < 4; ++t) qs[t] = lane + 32 * t < D ? q[lane + 32 * t] / q_div : 0.f;
+  for (int r = 0; r < nb; ++r) {
+    const int j = i + r - W;
+    float se = 0.f, sk = 0.f;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int d = lane + 32 * t;
+      if (d < D) {
+        se = fmaf(qs[t], emb_k[(long long)r * D + d], se);
+        if (j >= 0 && j < P) sk = fmaf(qs[t], qkv[((long long)b * P + j) * ld + k_off + h * D + d], sk);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      se += __shfl_xor_sync(0xffffffffu, se, o);
+      sk += __shfl_xor_sync(0xffffffffu, sk, o);
+    }
+    if (lane == 0) {
+      rk[wr * nb + r] = se;
+      sb[wr * nb + r] = (j >= 0 && j < P) ? sk + se : -INFINITY;
+    }
   }
 }
 
@@ -456,19 +468,20 @@ bool k_attention_tc(Context* ctx, const float* qkv, int ld, int q_off, int k_off
   const int BH = B * heads;
   const size_t tile_elems = (size_t)2 * kTQ * D;  // one Q tile (2 planes) == one K or V tile
   DevBuf Qp(ctx, sizeof(uint16_t) * tile_elems * BH * nq), Kp(ctx, sizeof(uint16_t) * tile_elems * BH * nk),
-      Vp(ctx, sizeof(uint16_t) * tile_elems * BH * nk), err(ctx, sizeof(int));
+      Vp(ctx, sizeof(uint16_t) * tile_elems * BH * nk);
   const long long total = (long long)BH * nq * kTQ * (D / 8);
   attn_pack_kernel<<<(int)std::min<long long>((total + 255) / 256, 148ll * 32), 256, 0, st>>>(
       qkv, ld, q_off, k_off, v_off, heads, D, P, nq, nk, q_div, Qp.as<uint16_t>(), Kp.as<uint16_t>(),
       Vp.as<uint16_t>(), total);
   note_launch();
   RVC_CUDA_TRY(cudaGetLastError());
-  DevBuf rk;
+  DevBuf rk, sb;
   if (window >= 0) {
-    const long long n = (long long)BH * P * (2 * window + 1);
+    const long long rows = (long long)BH * P, n = rows * (2 * window + 1);
     rk = DevBuf(ctx, sizeof(float) * (size_t)n);
-    attn_rel_k_kernel<<<(int)std::min<long long>((n + 255) / 256, 148ll * 32), 256, 0, st>>>(
-        qkv, ld, q_off, heads, D, P, window, q_div, emb_k, rk.f(), n);
+    sb = DevBuf(ctx, sizeof(float) * (size_t)n);
+    attn_band_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(qkv, ld, q_off, k_off, heads, D, P, window, q_div,
+                                                                 emb_k, rk.f(), sb.f(), rows);
     note_launch();
     RVC_CUDA_TRY(cudaGetLastError());
   }
@@ -485,13 +498,9 @@ bool k_attention_tc(Context* ctx, const float* qkv, int ld, int q_off, int k_off
   a.y_ld = y_ld;
   a.window = window;
   a.rk = rk.f();
-  a.qkv = qkv;
-  a.ld = ld;
-  a.q_off = q_off;
-  a.k_off = k_off;
-  a.q_div = q_div;
+  a.sb = sb.f();
   a.emb_v = emb_v;
-  a.err = err.as<int>();
+  a.err = ctx->d_err;  // reported by the context's bounded sync
   a.BH = BH;
   const size_t smem = 1024 + (size_t)2 * kTQ * D * 2 + (size_t)2 * kTK * D * 2 * 2 + (size_t)2 * kTQ * kTK * 2 + 128;
   static std::atomic<uint64_t> attr_done{0};
@@ -509,11 +518,7 @@ bool k_attention_tc(Context* ctx, const float* qkv, int ld, int q_off, int k_off
     tc_attn_kernel<96><<<std::min(items, 148), kAThreads, smem, st>>>(a);
   note_launch();
   RVC_CUDA_TRY(cudaGetLastError());
-  int h_err = 0;
-  RVC_CUDA_TRY(cudaMemcpyAsync(&h_err, err.p, sizeof(int), cudaMemcpyDeviceToHost, st));
-  RVC_CUDA_TRY(cudaStreamSynchronize(st));
-  if (h_err != 0) throw Error{kErrTimeout, "attention: a bounded wait gave up (code " + std::to_string(h_err) + ")"};
-  return true;
+  return true;  // the packed tiles are released to the stream-ordered cache: later work queues behind this kernel
 }
 
 }  // namespace rvc
