@@ -63,6 +63,8 @@ int32_t rvc_cuda_alloc(int64_t ctx, int64_t bytes, void** dptr);
 int32_t rvc_cuda_free(int64_t ctx, void* dptr);
 int32_t rvc_cuda_h2d(int64_t ctx, void* dst, const void* src, int64_t bytes);
 int32_t rvc_cuda_d2h(int64_t ctx, void* dst, const void* src, int64_t bytes);
+/* Device-to-device copy, asynchronous on the context's stream. */
+int32_t rvc_cuda_d2d(int64_t ctx, void* dst, const void* src, int64_t bytes);
 /* Per-kernel timing of the tensor-core convolutions: enable, then read the
  * accumulated launch count, device milliseconds and algorithmic FLOPs. */
 int32_t rvc_cuda_profile(int64_t ctx, int32_t enable);
@@ -287,6 +289,9 @@ int32_t rvc_cuda_index_set_ivf(int64_t index, const float* centroids, int32_t nl
  * past the rows the buckets hold.  Host pointers. */
 int32_t rvc_cuda_index_ivf_search(int64_t index, const float* q, int64_t F, int32_t D, int32_t k, int32_t nprobe,
                                   float* scores, int64_t* inds);
+/* Same as rvc_cuda_index_ivf_blend with device pointers, asynchronous. */
+int32_t rvc_cuda_index_ivf_blend_device(int64_t index, const float* q, int64_t F, int32_t D, int32_t k,
+                                        int32_t nprobe, double index_rate, const float* feats, float* out);
 /* The pipeline's blend (mode 0 above) over the IVF search results
  * (runtime/pipeline.py:523-527, :563-566).  Host pointers. */
 int32_t rvc_cuda_index_ivf_blend(int64_t index, const float* q, int64_t F, int32_t D, int32_t k, int32_t nprobe,
@@ -326,6 +331,16 @@ int32_t rvc_cuda_change_rms(int64_t ctx, const float* d1, int64_t n1, int32_t sr
 int32_t rvc_cuda_f0_autocorr(int64_t ctx, const double* x, int64_t n, int32_t sr, int32_t hop, int32_t win,
                              int32_t lag_min, int32_t lag_max, const double* hann, double threshold, float* f0,
                              int64_t n_frames);
+/* Device-pointer forms of interp_linear, protect, change_rms and to_int16
+ * (same arguments), asynchronous on the context's stream: the device pipeline
+ * keeps a conversion's features and waveform in HBM between the steps. */
+int32_t rvc_cuda_interp_linear_device(int64_t ctx, const float* x, int64_t L, int32_t D, double scale, float* y,
+                                      int64_t Lo);
+int32_t rvc_cuda_protect_device(int64_t ctx, const float* feats, const float* feats0, const float* pitchf, int64_t P,
+                                int32_t D, float protect, float* out);
+int32_t rvc_cuda_change_rms_device(int64_t ctx, const float* d1, int64_t n1, int32_t sr1, const float* d2, int64_t n2,
+                                   int32_t sr2, double rate, float* out);
+int32_t rvc_cuda_to_int16_device(int64_t ctx, const float* x, int64_t n, int16_t* y);
 /* runtime.dsp.resample.resample (runtime/dsp/resample.py:129): x [n_in]
  * (float32 when x_f32 != 0, else float64) from orig_sr to target_sr ->
  * y [n_out] float32, n_out = max(1, round(n_in * target_sr / orig_sr));

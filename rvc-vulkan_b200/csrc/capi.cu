@@ -273,6 +273,13 @@ int32_t rvc_cuda_d2h(int64_t ctx, void* dst, const void* src, int64_t bytes) {
   });
 }
 
+int32_t rvc_cuda_d2d(int64_t ctx, void* dst, const void* src, int64_t bytes) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(dst && src && bytes >= 0, "d2d: bad arguments");
+    if (bytes) RVC_CUDA_TRY(cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDeviceToDevice, c->stream));
+  });
+}
+
 int32_t rvc_cuda_profile(int64_t ctx, int32_t enable) {
   return on_ctx(ctx, [&](Context* c) {
     c->prof_collect();
@@ -802,6 +809,14 @@ int32_t rvc_cuda_index_ivf_search(int64_t index, const float* q, int64_t F, int3
   });
 }
 
+int32_t rvc_cuda_index_ivf_blend_device(int64_t index, const float* q, int64_t F, int32_t D, int32_t k,
+                                        int32_t nprobe, double index_rate, const float* feats, float* out) {
+  return on_index(index, [&](IndexModel* m) {
+    RVC_CHECK_ARG(D == m->D, "index_ivf_blend: query width does not match the index");
+    m->ivf_blend_device(q, F, k, nprobe, (float)index_rate, (float)(1.0 - index_rate), feats, out);
+  });
+}
+
 int32_t rvc_cuda_index_ivf_blend(int64_t index, const float* q, int64_t F, int32_t D, int32_t k, int32_t nprobe,
                                  double index_rate, const float* feats, float* out) {
   return on_index(index, [&](IndexModel* m) {
@@ -1044,6 +1059,38 @@ int32_t rvc_cuda_f0_autocorr(int64_t ctx, const double* x, int64_t n, int32_t sr
                     threshold, df.f(), n_frames);
     d2h(c, f0, df.p, sizeof(float) * (size_t)n_frames);
     finish(c);
+  });
+}
+
+int32_t rvc_cuda_interp_linear_device(int64_t ctx, const float* x, int64_t L, int32_t D, double scale, float* y,
+                                      int64_t Lo) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(x && y && L >= 1 && D >= 1 && scale > 0.0 && Lo == (int64_t)((double)L * scale),
+                  "interp_linear: bad arguments (Lo must be int(L * scale))");
+    dsp_interp_time(c, x, L, D, scale, y, Lo);
+  });
+}
+
+int32_t rvc_cuda_protect_device(int64_t ctx, const float* feats, const float* feats0, const float* pitchf, int64_t P,
+                                int32_t D, float protect, float* out) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(feats && feats0 && pitchf && out && P >= 0 && D >= 1, "protect: bad arguments");
+    if (P) dsp_protect(c, feats, feats0, pitchf, P, D, protect, out);
+  });
+}
+
+int32_t rvc_cuda_change_rms_device(int64_t ctx, const float* d1, int64_t n1, int32_t sr1, const float* d2, int64_t n2,
+                                   int32_t sr2, double rate, float* out) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(d1 && d2 && out && n1 >= 0 && n2 >= 0, "change_rms: bad arguments");
+    dsp_change_rms(c, d1, n1, sr1, d2, n2, sr2, rate, out);
+  });
+}
+
+int32_t rvc_cuda_to_int16_device(int64_t ctx, const float* x, int64_t n, int16_t* y) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(x && y && n >= 0, "to_int16: bad arguments");
+    if (n) dsp_to_int16(c, x, n, (short*)y);
   });
 }
 

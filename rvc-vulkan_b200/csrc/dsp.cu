@@ -511,8 +511,7 @@ void dsp_change_rms(Context* ctx, const float* d1, long long n1, int sr1, const 
   // np.power(r, 1.0 - rate) with a float32 base: the exponent is rounded to float32
   rms_mix_kernel<<<grid_for(n2, 256), 256, 0, st>>>(d2, n2, r1.f(), L1, r2.f(), L2, (float)(1.0 - rate),
                                                    (float)(rate - 1.0), out);
-  check_launch();
-  RVC_CUDA_TRY(cudaStreamSynchronize(st));
+  check_launch();  // r1 / r2 go back to the stream-ordered cache: later work queues behind this
 }
 
 void dsp_f0_autocorr(Context* ctx, const double* x, long long n, int hop, int win, int lag_min, int lag_max,
@@ -536,7 +535,6 @@ void dsp_to_int16(Context* ctx, const float* x, long long n, short* y) {
   check_launch();
   to_int16_kernel<<<grid_for(n, 256), 256, 0, st>>>(x, n, (const unsigned int*)am.p, y);
   check_launch();
-  RVC_CUDA_TRY(cudaStreamSynchronize(st));
 }
 
 }  // namespace rvc

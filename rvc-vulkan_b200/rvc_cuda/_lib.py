@@ -120,6 +120,12 @@ _SIGS = {
     "rvc_cuda_protect": ([_i64, _fp, _fp, _fp, _i64, _i32, _f32, _fp], _i32),
     "rvc_cuda_change_rms": ([_i64, _fp, _i64, _i32, _fp, _i64, _i32, _f64, _fp], _i32),
     "rvc_cuda_to_int16": ([_i64, _fp, _i64, _p], _i32),
+    "rvc_cuda_interp_linear_device": ([_i64, _p, _i64, _i32, _f64, _p, _i64], _i32),
+    "rvc_cuda_protect_device": ([_i64, _p, _p, _p, _i64, _i32, _f32, _p], _i32),
+    "rvc_cuda_change_rms_device": ([_i64, _p, _i64, _i32, _p, _i64, _i32, _f64, _p], _i32),
+    "rvc_cuda_to_int16_device": ([_i64, _p, _i64, _p], _i32),
+    "rvc_cuda_index_ivf_blend_device": ([_i64, _p, _i64, _i32, _i32, _i32, _f64, _p, _p], _i32),
+    "rvc_cuda_d2d": ([_i64, _p, _p, _i64], _i32),
     "rvc_cuda_resample": ([_i64, _p, _i32, _i64, _i32, _i32, _i32, _fp, _i64], _i32),
     "rvc_cuda_f0_autocorr": ([_i64, _p, _i64, _i32, _i32, _i32, _i32, _i32, _p, _f64, _fp, _i64], _i32),
     "rvc_cuda_index_create": ([_i64, _fp, _i64, _i32, _i32, C.POINTER(_i64)], _i32),
@@ -216,6 +222,10 @@ class Context:
 
     def d2h(self, arr: np.ndarray, dptr: int):
         check(lib.rvc_cuda_d2h(self.handle, arr.ctypes.data_as(_p), _p(dptr), arr.nbytes))
+
+    def d2d(self, dst: int, src: int, nbytes: int):
+        """Device-to-device copy, asynchronous on this context's stream."""
+        check(lib.rvc_cuda_d2d(self.handle, _p(dst), _p(src), int(nbytes)))
 
     def profile(self, enable: bool):
         check(lib.rvc_cuda_profile(self.handle, 1 if enable else 0))

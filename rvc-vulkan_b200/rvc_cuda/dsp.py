@@ -183,6 +183,27 @@ def resample(x, orig_sr, target_sr, method="fft"):
     return y
 
 
+# ---- device-pointer forms (asynchronous on the context's stream), used by the
+# device-resident conversion in rvc_cuda.pipeline
+def interpolate_device(ctx, d_x: int, L: int, D: int, scale: float, d_y: int, Lo: int):
+    check(lib.rvc_cuda_interp_linear_device(ctx.handle, C.c_void_p(d_x), int(L), int(D), float(scale),
+                                            C.c_void_p(d_y), int(Lo)))
+
+
+def protect_device(ctx, d_feats: int, d_feats0: int, d_pitchf: int, P: int, D: int, protect: float, d_out: int):
+    check(lib.rvc_cuda_protect_device(ctx.handle, C.c_void_p(d_feats), C.c_void_p(d_feats0), C.c_void_p(d_pitchf),
+                                      int(P), int(D), float(protect), C.c_void_p(d_out)))
+
+
+def change_rms_device(ctx, d1: int, n1: int, sr1: int, d2: int, n2: int, sr2: int, rate: float, d_out: int):
+    check(lib.rvc_cuda_change_rms_device(ctx.handle, C.c_void_p(d1), int(n1), int(sr1), C.c_void_p(d2), int(n2),
+                                         int(sr2), float(rate), C.c_void_p(d_out)))
+
+
+def to_int16_device(ctx, d_x: int, n: int, d_y: int):
+    check(lib.rvc_cuda_to_int16_device(ctx.handle, C.c_void_p(d_x), int(n), C.c_void_p(d_y)))
+
+
 def patch_reference(pipeline_module=None):
     """Route ``runtime.pipeline``'s ``change_rms``, ``interpolate_linear``,
     ``resample`` and ``signal.filtfilt`` to the device versions."""

@@ -120,6 +120,12 @@ class CudaHubert:
         check(lib.rvc_cuda_hubert_encode(self.handle, B, T, fptr(xb), version, fptr(out)))
         return out
 
+    def encode_device(self, d_x: int, B: int, T: int, version: int, d_out: int):
+        """Device pointers (from this model's context): ``x [B,T]`` -> ``out [B,L,768|256]``,
+        asynchronous on the context's stream."""
+        check(lib.rvc_cuda_hubert_encode_device(self.handle, int(B), int(T), C.c_void_p(d_x), int(version),
+                                                C.c_void_p(d_out)))
+
     def out_frames(self, T: int) -> int:
         """Feature frames of a ``T``-sample input."""
         return out_len(T)

@@ -244,6 +244,11 @@ class Pipeline:
                 pitches.append((pitch[:, s0 // self.window:(e0 + self.t_pad2) // self.window],
                                 pitchf[:, s0 // self.window:(e0 + self.t_pad2) // self.window]))
 
+        ctx = self._device_chain(model, net_g, index)
+        if ctx is not None:
+            return tgt_sr, self._convert_on_device(ctx, model, net_g, index, audio, blocks, pitches, noise, sid, version,
+                                                   index_rate, protect, tgt_sr, resample_sr, rms_mix_rate, times,
+                                                   retrieval_mode, brute_mix, progress_cb, total)
         feats_all = self._encode(model, [b[3] for b in blocks], version)
         preps = [self._vc_prepare(sid, b[3].shape[0], p[0], p[1], f, index, index_rate, protect, times,
                                   retrieval_mode, brute_mix) for b, p, f in zip(blocks, pitches, feats_all)]
@@ -263,6 +268,110 @@ class Pipeline:
         if tgt_sr != resample_sr >= 16000:                             # :1204-1205
             audio_opt = dsp.resample(audio_opt, tgt_sr, resample_sr, method="fft")
         return tgt_sr, dsp.to_int16(audio_opt)
+
+    # ------------------------------------------------------------------ device-resident path
+    @staticmethod
+    def _device_chain(model, net_g, index):
+        """The context every stage shares when the models are this library's
+        (``CudaHubert``, ``CudaSynthesizer``, ``CudaIndex`` on one device), else None."""
+        from .hubert import CudaHubert  # noqa: PLC0415
+        from .synth import CudaSynthesizer  # noqa: PLC0415
+        if not (isinstance(model, CudaHubert) and isinstance(net_g, CudaSynthesizer)) or model.ctx is not net_g.ctx:
+            return None
+        if index is not None and getattr(index, "ctx", None) is not model.ctx:
+            return None
+        return model.ctx
+
+    def _convert_on_device(self, ctx, model, net_g, index, audio, blocks, pitches, noise, sid, version, index_rate,
+                           protect, tgt_sr, resample_sr, rms_mix_rate, times, retrieval_mode, brute_mix, progress_cb,
+                           total):
+        """The chunk loop with the features and waveforms resident in HBM: per
+        chunk the audio goes up, HuBERT, the retrieval blend, the x2
+        interpolation, the protect blend and the synthesizer run on device
+        buffers, and the trimmed waveform is copied into one output buffer;
+        then change_rms and the int16 conversion on the device, one copy down.
+        The same kernels as the host-buffer path, so the same result."""
+        if index is not None and index_rate != 0 and brute_mix != 0:
+            raise NotImplementedError("brute_mix != 0 is not on the device path")
+        D = 256 if version == 1 else 768
+        upp, H = net_g.upp, net_g.hidden
+        bufs = []
+
+        def alloc(nbytes):
+            p = ctx.alloc(max(16, int(nbytes)))
+            bufs.append(p)
+            return p
+
+        try:
+            plan, n_out = [], 0
+            for (idx, s0, e0, blk), (p, pf) in zip(blocks, pitches):
+                L = int(model.out_frames(blk.shape[0]))
+                P = 2 * L
+                keep = max(0, P * upp - 2 * self.t_pad_tgt)
+                plan.append((blk, p, pf, L, P, keep))
+                n_out += keep
+            d_out = alloc(4 * n_out)
+            off = 0
+            for done, (blk, p, pf, L, P, keep) in enumerate(plan, 1):
+                t0 = time.perf_counter()
+                T = blk.shape[0]
+                d_x = alloc(4 * T)
+                ctx.h2d(d_x, blk)
+                d_f = alloc(4 * L * D)
+                model.encode_device(d_x, 1, T, version, d_f)
+                d_m = d_f
+                if index is not None and index_rate != 0:                 # :517-566
+                    d_m = alloc(4 * L * D)
+                    index.blend_device(d_f, L, d_f, index_rate, d_m, k=_K_SEARCH,
+                                       ivf=bool(index.nlist) and retrieval_mode != "brute")
+                d_ph = alloc(4 * P * D)
+                dsp.interpolate_device(ctx, d_m, L, D, 2, d_ph, P)
+                pitch, pitchf = _align(p, P), _align(pf, P)                # :582-603
+                pitchf32 = np.ascontiguousarray(pitchf[0], dtype=np.float32)
+                d_pf = alloc(4 * P)
+                ctx.h2d(d_pf, pitchf32)
+                if protect < 0.5:                                          # :594-608
+                    d_f0 = alloc(4 * P * D)
+                    dsp.interpolate_device(ctx, d_f, L, D, 2, d_f0, P)
+                    dsp.protect_device(ctx, d_ph, d_f0, d_pf, P, D, protect, d_ph)
+                t1 = time.perf_counter()
+                times[0] += t1 - t0
+                if noise is not None and noise[done - 1][0] == P:
+                    nz, ns = noise[done - 1][1].result()
+                else:
+                    nz, ns = net_g.make_noise(P)
+                d_p, d_sid = alloc(8 * P), alloc(8)
+                d_nz, d_ns, d_w = alloc(4 * H * P), alloc(4 * P * upp), alloc(4 * P * upp)
+                ctx.h2d(d_p, np.ascontiguousarray(pitch[0], dtype=np.int64))
+                ctx.h2d(d_sid, np.asarray([sid], dtype=np.int64))
+                ctx.h2d(d_nz, np.ascontiguousarray(nz, dtype=np.float32))
+                ctx.h2d(d_ns, np.ascontiguousarray(ns, dtype=np.float32))
+                net_g.infer_device(1, P, d_ph, d_p, d_pf, d_sid, d_nz, d_ns, d_w)
+                if keep:                                                   # [t_pad_tgt : -t_pad_tgt]
+                    ctx.d2d(d_out + 4 * off, d_w + 4 * self.t_pad_tgt, 4 * keep)
+                off += keep
+                times[2] += time.perf_counter() - t1
+                if progress_cb is not None:
+                    progress_cb(done, total, "chunk %d/%d" % (done, total))
+            if rms_mix_rate != 1 and n_out:
+                a32 = np.ascontiguousarray(audio, dtype=np.float32)
+                d_a = alloc(4 * a32.size)
+                ctx.h2d(d_a, a32)
+                dsp.change_rms_device(ctx, d_a, a32.size, 16000, d_out, n_out, tgt_sr, rms_mix_rate, d_out)
+            if tgt_sr != resample_sr >= 16000:
+                host = np.empty(n_out, np.float32)
+                if n_out:
+                    ctx.d2h(host, d_out)
+                return dsp.to_int16(dsp.resample(host, tgt_sr, resample_sr, method="fft"))
+            out = np.empty(n_out, np.int16)
+            if n_out:
+                d_i = alloc(2 * n_out)
+                dsp.to_int16_device(ctx, d_out, n_out, d_i)
+                ctx.d2h(out, d_i)
+            return out
+        finally:
+            for b in bufs:
+                ctx.free(b)
 
     # ------------------------------------------------------------------ models
     @staticmethod

@@ -119,6 +119,21 @@ class CudaIndex:
                                                fptr(f) if f is not None else None, fptr(out)))
         return out
 
+    def blend_device(self, d_q: int, F: int, d_feats: int, index_rate: float, d_out: int, k: int = 8,
+                     ivf: Optional[bool] = None, nprobe: Optional[int] = None):
+        """The pipeline's blend + mix on device pointers (this index's context):
+        ``q [F,D]``, ``feats [F,D]`` -> ``out [F,D]``; IVF search when the index
+        has the structure (or ``ivf``), else brute force.  Asynchronous."""
+        use_ivf = bool(self.nlist) if ivf is None else ivf
+        if use_ivf:
+            check(lib.rvc_cuda_index_ivf_blend_device(self.handle, C.c_void_p(d_q), int(F), self.D, int(k),
+                                                      self._nprobe(nprobe), float(index_rate), C.c_void_p(d_feats),
+                                                      C.c_void_p(d_out)))
+        else:
+            check(lib.rvc_cuda_index_blend_device(self.handle, C.c_void_p(d_q), int(F), self.D, int(k),
+                                                  BLEND_MODES["pipeline"], float(index_rate), C.c_void_p(d_feats),
+                                                  C.c_void_p(d_out)))
+
     def close(self):
         if getattr(self, "handle", 0):
             lib.rvc_cuda_index_destroy(self.handle)

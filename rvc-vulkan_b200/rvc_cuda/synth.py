@@ -148,6 +148,14 @@ class CudaSynthesizer:
                                        fptr(nz), fptr(ns), fptr(out)))
         return out
 
+    def infer_device(self, B: int, P: int, d_phone: int, d_pitch: int, d_nsff0: int, d_sid: int, d_nz: int,
+                     d_ns: int, d_wave: int):
+        """Device pointers (from this model's context): phone [B,P,D] f32, pitch [B,P] i64,
+        nsff0 [B,P] f32, sid [B] i64, nz [B,h,P] f32, ns [B,P*upp] f32 -> wave [B,P*upp] f32;
+        asynchronous on the context's stream."""
+        check(lib.rvc_cuda_synth_infer_device(self.handle, int(B), int(P), *[C.c_void_p(v) for v in (
+            d_phone, d_pitch, d_nsff0, d_sid, d_nz, d_ns, d_wave)]))
+
     def infer_controlled(self, phone, pitch, nsff0, sid, nz, ns, phone_gpu=None, _defer: bool = False):
         """Same contract as ``SynthesizerTrn.infer_controlled``: ``[1,1,upp*P]``."""
         phone = np.asarray(phone, dtype=np.float32)

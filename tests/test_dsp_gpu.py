@@ -262,3 +262,47 @@ def test_device_pipeline_end_to_end_against_oracle(monkeypatch):
                             file_index=db, **kw)
     assert out.shape == ref.shape and out.dtype == np.int16
     assert np.abs(out.astype(np.int32) - ref.astype(np.int32)).max() <= 33
+
+
+class _Proxy:
+    """Forwards every attribute; not an instance of the library's model classes,
+    so the pipeline takes its host-buffer path."""
+
+    def __init__(self, m):
+        self._m = m
+
+    def __getattr__(self, k):
+        return getattr(self._m, k)
+
+
+@pytest.mark.parametrize("ivf", [False, True])
+def test_device_resident_chain_equals_host_buffer_path(monkeypatch, ivf):
+    """The HBM-resident chunk chain runs the same kernels as the host-buffer
+    path: identical int16 output (2 chunks, retrieval brute force / IVF,
+    protect, change_rms)."""
+    from rvc_cuda import pipeline as P
+    from rvc_cuda.hubert import CudaHubert
+    from rvc_cuda.retrieval import CudaIndex
+    from rvc_cuda.rmvpe import CudaRmvpe
+    from rvc_cuda.synth import CudaSynthesizer
+    monkeypatch.setenv("RVC_FIXED_SEED", "77")
+    a = syn.make_speech_audio(2.2, seed=12, silence_every=1.0)
+    hub = CudaHubert(syn.make_hubert_weights(0))
+    net = CudaSynthesizer(syn.make_vits_weights(40000, 0), syn.vits_config_array(40000))
+    db = syn.make_index(4000, 768, 3)
+    index = CudaIndex(db)
+    if ivf:
+        rs = np.random.RandomState(1)
+        cent = db[rs.choice(4000, 16, replace=False)]
+        d = ((db[:, None, :] - cent[None]) ** 2).sum(-1)
+        index.set_ivf(cent, d.argmin(1))
+    pipe = P.Pipeline(40000, pf.config(x_query=1))
+    pipe.model_rmvpe = CudaRmvpe(syn.make_rmvpe_weights(0))
+    kw = dict(f0_up_key=0, f0_method="rmvpe", index_rate=0.75, if_f0=True, tgt_sr=40000, resample_sr=0,
+              rms_mix_rate=0.25, version=2, protect=0.33, slice_length=1.0)
+    assert pipe._device_chain(hub, net, index) is hub.ctx
+    _, dev = pipe.pipeline(hub, net, 0, a, [0.0, 0.0, 0.0], file_index=index, **kw)
+    assert pipe._device_chain(_Proxy(hub), net, index) is None
+    _, host = pipe.pipeline(_Proxy(hub), _Proxy(net), 0, a, [0.0, 0.0, 0.0], file_index=index, **kw)
+    assert dev.shape == host.shape and dev.size > 40000
+    np.testing.assert_array_equal(dev, host)
