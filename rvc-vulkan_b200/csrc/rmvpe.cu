@@ -21,6 +21,7 @@
 #include <cooperative_groups.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdio>
 
@@ -360,6 +361,81 @@ __global__ void __launch_bounds__(256) conv2d_rb_kernel(const C2Args a) {
         a.part[(((long long)sp * a.B + b) * M + m) * a.C_out + co] = acc[i][j];
       else
         c2_store(a, b, m, co, acc[i][j]);
+    }
+  }
+}
+
+// Direct 3x3 stride-1 conv over a shared-memory halo tile: per block of CK
+// input channels the (TH+2) x (TW+2) input pixels of a TH x TW output tile are
+// loaded once and serve all nine taps (the implicit-GEMM kernels re-read them
+// per tap).  Each thread owns 4 consecutive pixels of a row x TNC channels;
+// input channels go in blocks of kDirCK (8 for the narrow levels, 16 for the
+// wide ones, measured).
+// Accumulation order per output: channel block, tap, channel.
+template <int BN, int TNC, int TPX, int kDirCK>
+__global__ void __launch_bounds__(256) conv3x3_direct_kernel(const C2Args a, int TW) {
+  constexpr int TMP = 4;
+  static_assert((TPX / TMP) * (BN / TNC) == 256, "256 threads");
+  __shared__ __align__(16) float wts[9][kDirCK][BN];
+  extern __shared__ float halo[];  // [(TH + 2) * (TW + 2)][kDirCK + 1]
+  const int TH = TPX / TW;
+  const int HW = TW + 2;
+  const int tid = threadIdx.x;
+  const int tilesW = (a.OW + TW - 1) / TW;
+  const int h0 = (blockIdx.x / tilesW) * TH, w0 = (blockIdx.x % tilesW) * TW;
+  const int n0 = blockIdx.y * BN, b = blockIdx.z;
+  const float* xb = a.x + (long long)b * a.x_bs;
+  const int tn = tid % (BN / TNC), tg = tid / (BN / TNC);
+  const int p0 = tg * TMP, pr = p0 / TW, pc = p0 % TW;  // first pixel of this thread (tile coordinates)
+  float acc[TMP][TNC];
+#pragma unroll
+  for (int i = 0; i < TMP; ++i)
+#pragma unroll
+    for (int j = 0; j < TNC; ++j) acc[i][j] = 0.f;
+  const int npx = (TH + 2) * HW;
+  for (int c0 = 0; c0 < a.C_in; c0 += kDirCK) {
+    // halo: pixel-major, kDirCK channels (+1 pad) per pixel
+    for (int e = tid; e < npx * kDirCK; e += 256) {
+      const int px = e / kDirCK, c = e % kDirCK;
+      const int ih = h0 - 1 + px / HW, iw = w0 - 1 + px % HW;
+      const bool ok = ih >= 0 && ih < a.H && iw >= 0 && iw < a.W && c0 + c < a.C_in;
+      halo[px * (kDirCK + 1) + c] = ok ? __ldg(xb + ((long long)ih * a.W + iw) * a.ldi + c0 + c) : 0.f;
+    }
+    for (int e = tid; e < 9 * kDirCK * BN; e += 256) {
+      const int n = e % BN, c = (e / BN) % kDirCK, tap = e / (BN * kDirCK);
+      const bool ok = c0 + c < a.C_in && n0 + n < a.C_out;
+      wts[tap][c][n] = ok ? __ldg(a.w + ((long long)tap * a.C_in + c0 + c) * a.C_out + n0 + n) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int tap = 0; tap < 9; ++tap) {
+      const int dy = tap / 3, dx = tap % 3;
+#pragma unroll
+      for (int c = 0; c < kDirCK; ++c) {
+        float av[TMP], wv[TNC];
+#pragma unroll
+        for (int i = 0; i < TMP; ++i) av[i] = halo[((pr + dy) * HW + pc + i + dx) * (kDirCK + 1) + c];
+#pragma unroll
+        for (int j = 0; j < TNC; j += 4) {
+          const float4 v = *reinterpret_cast<const float4*>(&wts[tap][c][tn * TNC + j]);
+          wv[j] = v.x; wv[j + 1] = v.y; wv[j + 2] = v.z; wv[j + 3] = v.w;
+        }
+#pragma unroll
+        for (int i = 0; i < TMP; ++i)
+#pragma unroll
+          for (int j = 0; j < TNC; ++j) acc[i][j] = fmaf(av[i], wv[j], acc[i][j]);
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < TMP; ++i) {
+    const int oh = h0 + pr, ow = w0 + pc + i;
+    if (oh >= a.OH || ow >= a.OW || pr >= TH) continue;
+#pragma unroll
+    for (int j = 0; j < TNC; ++j) {
+      const int co = n0 + tn * TNC + j;
+      if (co < a.C_out) c2_store(a, b, oh * a.OW + ow, co, acc[i][j]);
     }
   }
 }
@@ -805,6 +881,48 @@ void RmvpeModel::conv(const Conv2dW& L, int B, const float* x, long long x_bs, i
   a.res = res; a.res_bs = res_bs; a.ldr = ldr;
   a.B = B;
   const long long M = (long long)a.OH * a.OW;
+  if (!L.transposed && L.taps == 9 && a.OW >= 4) {
+    // direct kernel: BN 64 (8 channels per thread) or 16 / 32 (4 per thread)
+    const int BNd = L.C_out <= 16 ? 16 : (L.C_out <= 32 ? 32 : 64);
+    const int TPX = BNd == 16 ? 256 : 128;
+    const int TW = std::min(32, a.OW);
+    const int TH = TPX / TW;
+    const long long blocks = (long long)((a.OH + TH - 1) / TH) * ((a.OW + TW - 1) / TW) * ((L.C_out + BNd - 1) / BNd) * B;
+    if (blocks >= 148) {
+      a.splits = 1;
+      dim3 g((unsigned)(((a.OH + TH - 1) / TH) * ((a.OW + TW - 1) / TW)), (unsigned)((L.C_out + BNd - 1) / BNd),
+             (unsigned)B);
+      const int ck = BNd == 64 ? 16 : 8;
+      const size_t hs = sizeof(float) * (size_t)(TH + 2) * (TW + 2) * (ck + 1);
+      static std::atomic<uint64_t> attr_done{0};  // the attribute is per device
+      if (ctx->device < 64 && !(attr_done.load() & (1ull << ctx->device))) {
+        RVC_CUDA_TRY(cudaFuncSetAttribute(conv3x3_direct_kernel<16, 4, 256, 8>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+        RVC_CUDA_TRY(cudaFuncSetAttribute(conv3x3_direct_kernel<32, 4, 128, 8>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+        RVC_CUDA_TRY(cudaFuncSetAttribute(conv3x3_direct_kernel<64, 8, 128, 16>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+        attr_done.fetch_or(1ull << ctx->device);
+      }
+      cudaEvent_t e0 = nullptr, e1 = nullptr;
+      if (ctx->prof) ctx->prof_begin(&e0, &e1);
+      if (BNd == 16)
+        conv3x3_direct_kernel<16, 4, 256, 8><<<g, 256, hs, ctx->stream>>>(a, TW);
+      else if (BNd == 32)
+        conv3x3_direct_kernel<32, 4, 128, 8><<<g, 256, hs, ctx->stream>>>(a, TW);
+      else
+        conv3x3_direct_kernel<64, 8, 128, 16><<<g, 256, hs, ctx->stream>>>(a, TW);
+      note_launch();
+      RVC_CUDA_TRY(cudaGetLastError());
+      if (ctx->prof) {
+        char lab[160];
+        snprintf(lab, sizeof(lab), "rmvpe conv Cin=%d Cout=%d taps=9 %dx%d B=%d direct", L.C_in, L.C_out, a.OH, a.OW,
+                 B);
+        ctx->prof_end(e0, e1, 2.0 * B * M * L.C_out * L.C_in * 9.0, lab, false);
+      }
+      return;
+    }
+  }
   // narrow stride-1 convs (<= 32 output channels, the tall full-resolution
   // levels): register-blocked 8 x 4 tiles; the rest (measured faster there:
   // fewer registers, more resident blocks) the 4 x 4 kernel
