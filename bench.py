@@ -740,7 +740,7 @@ def run_pipeline(args, world, rank, local):
     index = CudaIndex(syn.make_index(args.index_rows, 768, 0), device=local)
     cfg = types.SimpleNamespace(x_pad=1, x_query=6, x_center=38, x_max=41, device=f"cuda:{local}")
     pipe = Pipeline(40000, cfg)
-    pipe.model_rmvpe = CudaRmvpe(syn.make_rmvpe_weights(0), device=local)
+    pipe.model_rmvpe = CudaRmvpe(syn.make_rmvpe_weights(0), device=local, own_stream=True)
     audio = syn.make_speech_audio(args.audio_s, seed=rank)
     ctx = hub.ctx
     stage = [0.0, 0.0, 0.0]

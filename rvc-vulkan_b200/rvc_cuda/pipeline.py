@@ -219,34 +219,30 @@ class Pipeline:
                 blocks.append((idx, s0, e0, np.asarray(blk, dtype=np.float32)))
         noise = self._prefetch_noise(model, net_g, [b[3].shape[0] for b in blocks])
 
-        t1 = time.perf_counter()
-        seg_pts = [0] + [o + self.t_pad for o in opt_ts] + [audio_pad.shape[0]]
-        pitch_parts, pitchf_parts = [], []
-        for si in range(len(seg_pts) - 1):                            # :800-813
-            ap, bp = seg_pts[si], seg_pts[si + 1]
-            b = min(bp + self.t_pad2 + self.window, audio_pad.shape[0])
-            seg = audio_pad[ap:b]
-            pi, pfi = self.get_f0(seg, seg.shape[0] // self.window, f0_up_key, f0_method)
-            core_n = max(1, (bp - ap) // self.window)
-            pitch_parts.append(pi[:core_n])
-            pitchf_parts.append(pfi[:core_n])
-        pitch = np.concatenate(pitch_parts)[None, :]
-        pitchf = np.concatenate(pitchf_parts).astype(np.float32)[None, :]
-        times[1] += time.perf_counter() - t1
+        ctx = self._device_chain(model, net_g, index)
+        f0_model = getattr(self, "model_fcpe" if f0_method == "fcpe" else "model_rmvpe", None)
+        f0_ctx = getattr(f0_model, "ctx", None)
+        if ctx is not None and f0_method != "pm" and f0_ctx is not None and f0_ctx is not ctx:
+            # the f0 model has its own stream: extract f0 on a host thread while the
+            # device chain runs HuBERT, retrieval and interpolation
+            from concurrent.futures import ThreadPoolExecutor  # noqa: PLC0415
+            ex = ThreadPoolExecutor(max_workers=1, thread_name_prefix="rvc-f0")
+            fut = ex.submit(self._f0_all, audio_pad, opt_ts, f0_up_key, f0_method, times)
+            ex.shutdown(wait=False)
+            if progress_cb is not None:
+                progress_cb(0, total, "split into %d chunks" % total)
+            return tgt_sr, self._convert_on_device(ctx, model, net_g, index, audio, blocks,
+                                                   lambda: self._chunk_pitches(blocks, *fut.result()), noise, sid,
+                                                   version, index_rate, protect, tgt_sr, resample_sr, rms_mix_rate,
+                                                   times, retrieval_mode, brute_mix, progress_cb, total)
+        pitch, pitchf = self._f0_all(audio_pad, opt_ts, f0_up_key, f0_method, times)
         if progress_cb is not None:
             progress_cb(0, total, "split into %d chunks" % total)
+        pitches = self._chunk_pitches(blocks, pitch, pitchf)
 
-        pitches = []
-        for idx, s0, e0, _ in blocks:
-            if e0 is None:
-                pitches.append((pitch[:, s0 // self.window:], pitchf[:, s0 // self.window:]))
-            else:
-                pitches.append((pitch[:, s0 // self.window:(e0 + self.t_pad2) // self.window],
-                                pitchf[:, s0 // self.window:(e0 + self.t_pad2) // self.window]))
-
-        ctx = self._device_chain(model, net_g, index)
         if ctx is not None:
-            return tgt_sr, self._convert_on_device(ctx, model, net_g, index, audio, blocks, pitches, noise, sid, version,
+            return tgt_sr, self._convert_on_device(ctx, model, net_g, index, audio, blocks, lambda: pitches, noise, sid,
+                                                   version,
                                                    index_rate, protect, tgt_sr, resample_sr, rms_mix_rate, times,
                                                    retrieval_mode, brute_mix, progress_cb, total)
         feats_all = self._encode(model, [b[3] for b in blocks], version)
@@ -269,6 +265,35 @@ class Pipeline:
             audio_opt = dsp.resample(audio_opt, tgt_sr, resample_sr, method="fft")
         return tgt_sr, dsp.to_int16(audio_opt)
 
+    def _f0_all(self, audio_pad, opt_ts, f0_up_key, f0_method, times):
+        """f0 of every split segment, concatenated (``runtime/pipeline.py:795-816``)."""
+        t1 = time.perf_counter()
+        seg_pts = [0] + [o + self.t_pad for o in opt_ts] + [audio_pad.shape[0]]
+        pitch_parts, pitchf_parts = [], []
+        for si in range(len(seg_pts) - 1):
+            ap, bp = seg_pts[si], seg_pts[si + 1]
+            b = min(bp + self.t_pad2 + self.window, audio_pad.shape[0])
+            seg = audio_pad[ap:b]
+            pi, pfi = self.get_f0(seg, seg.shape[0] // self.window, f0_up_key, f0_method)
+            core_n = max(1, (bp - ap) // self.window)
+            pitch_parts.append(pi[:core_n])
+            pitchf_parts.append(pfi[:core_n])
+        pitch = np.concatenate(pitch_parts)[None, :]
+        pitchf = np.concatenate(pitchf_parts).astype(np.float32)[None, :]
+        times[1] += time.perf_counter() - t1
+        return pitch, pitchf
+
+    def _chunk_pitches(self, blocks, pitch, pitchf):
+        """Each chunk's slice of the frame-level pitch (``runtime/pipeline.py:903-916``)."""
+        out = []
+        for idx, s0, e0, _ in blocks:
+            if e0 is None:
+                out.append((pitch[:, s0 // self.window:], pitchf[:, s0 // self.window:]))
+            else:
+                out.append((pitch[:, s0 // self.window:(e0 + self.t_pad2) // self.window],
+                            pitchf[:, s0 // self.window:(e0 + self.t_pad2) // self.window]))
+        return out
+
     # ------------------------------------------------------------------ device-resident path
     @staticmethod
     def _device_chain(model, net_g, index):
@@ -282,15 +307,17 @@ class Pipeline:
             return None
         return model.ctx
 
-    def _convert_on_device(self, ctx, model, net_g, index, audio, blocks, pitches, noise, sid, version, index_rate,
-                           protect, tgt_sr, resample_sr, rms_mix_rate, times, retrieval_mode, brute_mix, progress_cb,
-                           total):
-        """The chunk loop with the features and waveforms resident in HBM: per
-        chunk the audio goes up, HuBERT, the retrieval blend, the x2
-        interpolation, the protect blend and the synthesizer run on device
-        buffers, and the trimmed waveform is copied into one output buffer;
-        then change_rms and the int16 conversion on the device, one copy down.
-        The same kernels as the host-buffer path, so the same result."""
+    def _convert_on_device(self, ctx, model, net_g, index, audio, blocks, pitches_fn, noise, sid, version,
+                           index_rate, protect, tgt_sr, resample_sr, rms_mix_rate, times, retrieval_mode, brute_mix,
+                           progress_cb, total):
+        """The chunk loop with the features and waveforms resident in HBM.  Phase
+        A (no f0 needed): per chunk the audio goes up, HuBERT, the retrieval blend
+        and the x2 interpolations run on device buffers.  Then the chunks' pitch
+        (``pitches_fn``, which may wait for f0 extracted concurrently on another
+        stream); phase B: protect blend, synthesizer, the trimmed waveform into
+        one output buffer.  Finally change_rms and the int16 conversion on the
+        device, one copy down.  The same kernels as the host-buffer path, so the
+        same result."""
         if index is not None and index_rate != 0 and brute_mix != 0:
             raise NotImplementedError("brute_mix != 0 is not on the device path")
         D = 256 if version == 1 else 768
@@ -304,15 +331,15 @@ class Pipeline:
 
         try:
             plan, n_out = [], 0
-            for (idx, s0, e0, blk), (p, pf) in zip(blocks, pitches):
+            for (idx, s0, e0, blk) in blocks:
                 L = int(model.out_frames(blk.shape[0]))
                 P = 2 * L
                 keep = max(0, P * upp - 2 * self.t_pad_tgt)
-                plan.append((blk, p, pf, L, P, keep))
+                plan.append([blk, L, P, keep, 0, 0])
                 n_out += keep
             d_out = alloc(4 * n_out)
-            off = 0
-            for done, (blk, p, pf, L, P, keep) in enumerate(plan, 1):
+            for item in plan:                                              # phase A
+                blk, L, P = item[0], item[1], item[2]
                 t0 = time.perf_counter()
                 T = blk.shape[0]
                 d_x = alloc(4 * T)
@@ -326,16 +353,22 @@ class Pipeline:
                                        ivf=bool(index.nlist) and retrieval_mode != "brute")
                 d_ph = alloc(4 * P * D)
                 dsp.interpolate_device(ctx, d_m, L, D, 2, d_ph, P)
-                pitch, pitchf = _align(p, P), _align(pf, P)                # :582-603
-                pitchf32 = np.ascontiguousarray(pitchf[0], dtype=np.float32)
-                d_pf = alloc(4 * P)
-                ctx.h2d(d_pf, pitchf32)
-                if protect < 0.5:                                          # :594-608
+                d_f0 = 0
+                if protect < 0.5:
                     d_f0 = alloc(4 * P * D)
                     dsp.interpolate_device(ctx, d_f, L, D, 2, d_f0, P)
-                    dsp.protect_device(ctx, d_ph, d_f0, d_pf, P, D, protect, d_ph)
+                item[4], item[5] = d_ph, d_f0
+                times[0] += time.perf_counter() - t0
+            pitches = pitches_fn()
+            off = 0
+            for done, (item, (p, pf)) in enumerate(zip(plan, pitches), 1):  # phase B
+                blk, L, P, keep, d_ph, d_f0 = item
                 t1 = time.perf_counter()
-                times[0] += t1 - t0
+                pitch, pitchf = _align(p, P), _align(pf, P)                # :582-603
+                d_pf = alloc(4 * P)
+                ctx.h2d(d_pf, np.ascontiguousarray(pitchf[0], dtype=np.float32))
+                if protect < 0.5:                                          # :594-608
+                    dsp.protect_device(ctx, d_ph, d_f0, d_pf, P, D, protect, d_ph)
                 if noise is not None and noise[done - 1][0] == P:
                     nz, ns = noise[done - 1][1].result()
                 else:

@@ -16,6 +16,7 @@ runs on the device unchanged.
 from __future__ import annotations
 
 import ctypes as C
+import os
 from typing import Optional
 
 import numpy as np
@@ -36,8 +37,15 @@ def frames(T: int) -> int:
 class CudaRmvpe:
     """Device-resident RMVPE on one GPU (one library context)."""
 
-    def __init__(self, weights: dict, device: Optional[int] = None):
-        self.ctx = _lib.get_context(device)
+    def __init__(self, weights: dict, device: Optional[int] = None, own_stream: bool = False):
+        """``own_stream``: a private library context (stream and workspace) on the
+        device, so f0 extraction can run concurrently with work on the shared
+        context (the device pipeline overlaps it with HuBERT)."""
+        if own_stream:
+            dev = device if device is not None else int(os.environ.get("RVC_CUDA_DEVICE", "0"))
+            self.ctx = _lib.Context(dev)
+        else:
+            self.ctx = _lib.get_context(device)
         h = C.c_int64(0)
         check(lib.rvc_cuda_rmvpe_create(self.ctx.handle, C.byref(h)))
         self.handle = int(h.value)

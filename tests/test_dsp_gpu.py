@@ -297,7 +297,7 @@ def test_device_resident_chain_equals_host_buffer_path(monkeypatch, ivf):
         d = ((db[:, None, :] - cent[None]) ** 2).sum(-1)
         index.set_ivf(cent, d.argmin(1))
     pipe = P.Pipeline(40000, pf.config(x_query=1))
-    pipe.model_rmvpe = CudaRmvpe(syn.make_rmvpe_weights(0))
+    pipe.model_rmvpe = CudaRmvpe(syn.make_rmvpe_weights(0), own_stream=True)  # f0 concurrently on its own stream
     kw = dict(f0_up_key=0, f0_method="rmvpe", index_rate=0.75, if_f0=True, tgt_sr=40000, resample_sr=0,
               rms_mix_rate=0.25, version=2, protect=0.33, slice_length=1.0)
     assert pipe._device_chain(hub, net, index) is hub.ctx
