@@ -365,77 +365,124 @@ __global__ void __launch_bounds__(256) conv2d_rb_kernel(const C2Args a) {
   }
 }
 
+// 4-byte global -> shared copy without a register round trip; n = 0 copies
+// nothing and writes zero (the source must still be a valid address).
+__device__ __forceinline__ void cp_async4(float* dst, const float* src, int n) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(d), "l"(src), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
 // Direct 3x3 stride-1 conv over a shared-memory halo tile: per block of CK
 // input channels the (TH+2) x (TW+2) input pixels of a TH x TW output tile are
 // loaded once and serve all nine taps (the implicit-GEMM kernels re-read them
-// per tap).  Each thread owns 4 consecutive pixels of a row x TNC channels;
-// input channels go in blocks of kDirCK (8 for the narrow levels, 16 for the
-// wide ones, measured).
-// Accumulation order per output: channel block, tap, channel.
-template <int BN, int TNC, int TPX, int kDirCK>
-__global__ void __launch_bounds__(256) conv3x3_direct_kernel(const C2Args a, int TW) {
-  constexpr int TMP = 4;
-  static_assert((TPX / TMP) * (BN / TNC) == 256, "256 threads");
-  __shared__ __align__(16) float wts[9][kDirCK][BN];
-  extern __shared__ float halo[];  // [(TH + 2) * (TW + 2)][kDirCK + 1]
+// per tap).  Each thread owns TMP consecutive pixels of one output row x TNC
+// channels (in quads NT x 4 apart, so a warp's float4 weight loads are
+// contiguous); per input channel and kernel row it reads the TMP + 2 halo
+// values of that row into registers once and applies the three kernel columns
+// from there.  Halo and weights are double-buffered: cp.async fills channel
+// block cb + 1 while block cb is summed.  Optional split over the channel
+// blocks (blockIdx.z = clip x split): partial sums go to a.part and
+// conv2d_reduce_kernel adds them in split order.
+// Accumulation order per output: channel block, channel, kernel row, column.
+template <int BN, int TNC, int TMP, int CK>
+__global__ void __launch_bounds__(256, 2) conv3x3_direct_kernel(const C2Args a, int TW) {
+  constexpr int NT = BN / TNC;         // threads across the channel block
+  constexpr int TPX = 256 / NT * TMP;  // pixels per tile
+  constexpr int WST = 9 * CK * BN;     // one weight stage [9][CK][BN]
+  extern __shared__ __align__(16) float dsm[];
   const int TH = TPX / TW;
   const int HW = TW + 2;
+  const int npx = (TH + 2) * HW;
+  const int HST = (npx * (CK + 1) + 3) & ~3;  // one halo stage [(TH+2)(TW+2)][CK+1], 16-byte multiple
+  float* wts = dsm;                           // [2][WST]
+  float* halo = dsm + 2 * WST;                // [2][HST]
   const int tid = threadIdx.x;
   const int tilesW = (a.OW + TW - 1) / TW;
   const int h0 = (blockIdx.x / tilesW) * TH, w0 = (blockIdx.x % tilesW) * TW;
-  const int n0 = blockIdx.y * BN, b = blockIdx.z;
+  const int n0 = blockIdx.y * BN;
+  const int b = blockIdx.z / a.splits, sp = blockIdx.z - b * a.splits;
+  const int ncb = (a.C_in + CK - 1) / CK;
+  const int cb0 = (int)((long long)ncb * sp / a.splits), cb1 = (int)((long long)ncb * (sp + 1) / a.splits);
   const float* xb = a.x + (long long)b * a.x_bs;
-  const int tn = tid % (BN / TNC), tg = tid / (BN / TNC);
+  const int tn = tid % NT, tg = tid / NT;
   const int p0 = tg * TMP, pr = p0 / TW, pc = p0 % TW;  // first pixel of this thread (tile coordinates)
+  auto issue = [&](int cb, int st) {
+    const int c0 = cb * CK;
+    float* hs = halo + st * HST;
+    for (int e = tid; e < npx * CK; e += 256) {
+      const int px = e / CK, c = e % CK;
+      const int ih = h0 - 1 + px / HW, iw = w0 - 1 + px % HW;
+      const bool ok = ih >= 0 && ih < a.H && iw >= 0 && iw < a.W && c0 + c < a.C_in;
+      cp_async4(hs + px * (CK + 1) + c, ok ? xb + ((long long)ih * a.W + iw) * a.ldi + c0 + c : xb, ok ? 4 : 0);
+    }
+    float* ws = wts + st * WST;
+    for (int e = tid; e < WST; e += 256) {
+      const int n = e % BN, c = (e / BN) % CK, tap = e / (BN * CK);
+      const bool ok = c0 + c < a.C_in && n0 + n < a.C_out;
+      cp_async4(ws + e, ok ? a.w + ((long long)tap * a.C_in + c0 + c) * a.C_out + n0 + n : a.w, ok ? 4 : 0);
+    }
+    cp_async_commit();
+  };
   float acc[TMP][TNC];
 #pragma unroll
   for (int i = 0; i < TMP; ++i)
 #pragma unroll
     for (int j = 0; j < TNC; ++j) acc[i][j] = 0.f;
-  const int npx = (TH + 2) * HW;
-  for (int c0 = 0; c0 < a.C_in; c0 += kDirCK) {
-    // halo: pixel-major, kDirCK channels (+1 pad) per pixel
-    for (int e = tid; e < npx * kDirCK; e += 256) {
-      const int px = e / kDirCK, c = e % kDirCK;
-      const int ih = h0 - 1 + px / HW, iw = w0 - 1 + px % HW;
-      const bool ok = ih >= 0 && ih < a.H && iw >= 0 && iw < a.W && c0 + c < a.C_in;
-      halo[px * (kDirCK + 1) + c] = ok ? __ldg(xb + ((long long)ih * a.W + iw) * a.ldi + c0 + c) : 0.f;
-    }
-    for (int e = tid; e < 9 * kDirCK * BN; e += 256) {
-      const int n = e % BN, c = (e / BN) % kDirCK, tap = e / (BN * kDirCK);
-      const bool ok = c0 + c < a.C_in && n0 + n < a.C_out;
-      wts[tap][c][n] = ok ? __ldg(a.w + ((long long)tap * a.C_in + c0 + c) * a.C_out + n0 + n) : 0.f;
+  if (cb0 < cb1) issue(cb0, 0);
+  for (int cb = cb0; cb < cb1; ++cb) {
+    const int st = (cb - cb0) & 1;
+    if (cb + 1 < cb1) {
+      issue(cb + 1, st ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
     __syncthreads();
+    const float* hs = halo + st * HST;
+    const float* ws = wts + st * WST;
+#pragma unroll 2
+    for (int c = 0; c < CK; ++c) {
 #pragma unroll
-    for (int tap = 0; tap < 9; ++tap) {
-      const int dy = tap / 3, dx = tap % 3;
+      for (int dy = 0; dy < 3; ++dy) {
+        float r[TMP + 2];
+        const float* hp = hs + ((pr + dy) * HW + pc) * (CK + 1) + c;
 #pragma unroll
-      for (int c = 0; c < kDirCK; ++c) {
-        float av[TMP], wv[TNC];
+        for (int k = 0; k < TMP + 2; ++k) r[k] = hp[k * (CK + 1)];
 #pragma unroll
-        for (int i = 0; i < TMP; ++i) av[i] = halo[((pr + dy) * HW + pc + i + dx) * (kDirCK + 1) + c];
+        for (int dx = 0; dx < 3; ++dx) {
+          float wv[TNC];
 #pragma unroll
-        for (int j = 0; j < TNC; j += 4) {
-          const float4 v = *reinterpret_cast<const float4*>(&wts[tap][c][tn * TNC + j]);
-          wv[j] = v.x; wv[j + 1] = v.y; wv[j + 2] = v.z; wv[j + 3] = v.w;
+          for (int q = 0; q < TNC / 4; ++q) {
+            const float4 v = *reinterpret_cast<const float4*>(ws + ((dy * 3 + dx) * CK + c) * BN + q * NT * 4 + tn * 4);
+            wv[4 * q] = v.x; wv[4 * q + 1] = v.y; wv[4 * q + 2] = v.z; wv[4 * q + 3] = v.w;
+          }
+#pragma unroll
+          for (int i = 0; i < TMP; ++i)
+#pragma unroll
+            for (int j = 0; j < TNC; ++j) acc[i][j] = fmaf(r[i + dx], wv[j], acc[i][j]);
         }
-#pragma unroll
-        for (int i = 0; i < TMP; ++i)
-#pragma unroll
-          for (int j = 0; j < TNC; ++j) acc[i][j] = fmaf(av[i], wv[j], acc[i][j]);
       }
     }
-    __syncthreads();
+    __syncthreads();  // stage st is refilled by the next iteration's issue
   }
+  const int oh = h0 + pr;
+  if (oh >= a.OH) return;
+  const long long M = (long long)a.OH * a.OW;
 #pragma unroll
   for (int i = 0; i < TMP; ++i) {
-    const int oh = h0 + pr, ow = w0 + pc + i;
-    if (oh >= a.OH || ow >= a.OW || pr >= TH) continue;
+    const int ow = w0 + pc + i;
+    if (ow >= a.OW) continue;
 #pragma unroll
     for (int j = 0; j < TNC; ++j) {
-      const int co = n0 + tn * TNC + j;
-      if (co < a.C_out) c2_store(a, b, oh * a.OW + ow, co, acc[i][j]);
+      const int co = n0 + (j / 4) * (NT * 4) + tn * 4 + (j % 4);
+      if (co >= a.C_out) continue;
+      if (a.splits > 1)
+        a.part[(((long long)sp * a.B + b) * M + (long long)oh * a.OW + ow) * a.C_out + co] = acc[i][j];
+      else
+        c2_store(a, b, oh * a.OW + ow, co, acc[i][j]);
     }
   }
 }
@@ -843,7 +890,9 @@ void RmvpeModel::ensure_ws(int B, int64_t T) {
   add("sal", Fp * 360);
   add("f0", F);
   ws_.emplace("amax", DevBuf(ctx, sizeof(int32_t) * (size_t)B * F));
-  ws_.emplace("part", DevBuf(ctx, sizeof(float) * (size_t)(4 * 148 + 64) * kTileElems));
+  // split partials: the direct conv splits while the batch's tiles x splits <
+  // 2 x 148, so the partials hold < 4 x 148 tiles x 256 pixels x 64 channels
+  ws_.emplace("part", DevBuf(ctx, sizeof(float) * (size_t)4 * 148 * 256 * 64));
   ws_B = B;
   ws_T = T;
 }
@@ -881,47 +930,64 @@ void RmvpeModel::conv(const Conv2dW& L, int B, const float* x, long long x_bs, i
   a.res = res; a.res_bs = res_bs; a.ldr = ldr;
   a.B = B;
   const long long M = (long long)a.OH * a.OW;
-  if (!L.transposed && L.taps == 9 && a.OW >= 4) {
-    // direct kernel: BN 64 (8 channels per thread) or 16 / 32 (4 per thread)
-    const int BNd = L.C_out <= 16 ? 16 : (L.C_out <= 32 ? 32 : 64);
-    const int TPX = BNd == 16 ? 256 : 128;
-    const int TW = std::min(32, a.OW);
+  // direct kernel: <BN, TNC, TMP, CK> by output channels and row width (a
+  // thread's TMP pixels lie in one row, so rows narrower than TMP go below)
+  static const int kBN[4] = {16, 32, 64, 64}, kTNC[4] = {4, 4, 8, 8}, kTMP[4] = {8, 8, 8, 4}, kCK[4] = {8, 8, 8, 8};
+  const int v = L.C_out <= 16 ? 0 : (L.C_out <= 32 ? 1 : (a.OW >= 8 ? 2 : 3));
+  if (!L.transposed && L.taps == 9 && a.OW >= kTMP[v]) {
+    const int BNd = kBN[v], TMP = kTMP[v], CK = kCK[v];
+    const int TPX = 256 / (BNd / kTNC[v]) * TMP;
+    const int TW = std::min(32, a.OW) / TMP * TMP;
     const int TH = TPX / TW;
-    const long long blocks = (long long)((a.OH + TH - 1) / TH) * ((a.OW + TW - 1) / TW) * ((L.C_out + BNd - 1) / BNd) * B;
-    if (blocks >= 148) {
-      a.splits = 1;
-      dim3 g((unsigned)(((a.OH + TH - 1) / TH) * ((a.OW + TW - 1) / TW)), (unsigned)((L.C_out + BNd - 1) / BNd),
-             (unsigned)B);
-      const int ck = BNd == 64 ? 16 : 8;
-      const size_t hs = sizeof(float) * (size_t)(TH + 2) * (TW + 2) * (ck + 1);
-      static std::atomic<uint64_t> attr_done{0};  // the attribute is per device
-      if (ctx->device < 64 && !(attr_done.load() & (1ull << ctx->device))) {
-        RVC_CUDA_TRY(cudaFuncSetAttribute(conv3x3_direct_kernel<16, 4, 256, 8>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
-        RVC_CUDA_TRY(cudaFuncSetAttribute(conv3x3_direct_kernel<32, 4, 128, 8>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
-        RVC_CUDA_TRY(cudaFuncSetAttribute(conv3x3_direct_kernel<64, 8, 128, 16>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
-        attr_done.fetch_or(1ull << ctx->device);
-      }
-      cudaEvent_t e0 = nullptr, e1 = nullptr;
-      if (ctx->prof) ctx->prof_begin(&e0, &e1);
-      if (BNd == 16)
-        conv3x3_direct_kernel<16, 4, 256, 8><<<g, 256, hs, ctx->stream>>>(a, TW);
-      else if (BNd == 32)
-        conv3x3_direct_kernel<32, 4, 128, 8><<<g, 256, hs, ctx->stream>>>(a, TW);
-      else
-        conv3x3_direct_kernel<64, 8, 128, 16><<<g, 256, hs, ctx->stream>>>(a, TW);
+    const int ncb = (L.C_in + CK - 1) / CK;
+    const long long tiles = (long long)((a.OH + TH - 1) / TH) * ((a.OW + TW - 1) / TW) * ((L.C_out + BNd - 1) / BNd);
+    // split the channel blocks when the batch's tiles fill less than two waves
+    // (sums then differ from the unsplit order by fp32 rounding only)
+    int splits = 1;
+    while (tiles * B * splits < 2 * 148 && ncb / (splits * 2) >= 2 && splits < 16) splits *= 2;
+    if (splits > 1 && (size_t)splits * B * M * L.C_out * sizeof(float) > ws_.at("part").bytes) splits = 1;
+    a.splits = splits;
+    a.part = ws_.at("part").f();
+    dim3 g((unsigned)(((a.OH + TH - 1) / TH) * ((a.OW + TW - 1) / TW)), (unsigned)((L.C_out + BNd - 1) / BNd),
+           (unsigned)(B * splits));
+    // dynamic shared memory: two stages of weights [9][CK][BN] and halo
+    const size_t hs = sizeof(float) * 2 * ((size_t)9 * CK * BNd + (((size_t)(TH + 2) * (TW + 2) * (CK + 1) + 3) & ~(size_t)3));
+    static std::atomic<uint64_t> attr_done{0};  // the attribute is per device
+    if (ctx->device < 64 && !(attr_done.load() & (1ull << ctx->device))) {
+      RVC_CUDA_TRY(cudaFuncSetAttribute(conv3x3_direct_kernel<16, 4, 8, 8>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+      RVC_CUDA_TRY(cudaFuncSetAttribute(conv3x3_direct_kernel<32, 4, 8, 8>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+      RVC_CUDA_TRY(cudaFuncSetAttribute(conv3x3_direct_kernel<64, 8, 8, 8>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+      RVC_CUDA_TRY(cudaFuncSetAttribute(conv3x3_direct_kernel<64, 8, 4, 8>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+      attr_done.fetch_or(1ull << ctx->device);
+    }
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (ctx->prof) ctx->prof_begin(&e0, &e1);
+    if (v == 0)
+      conv3x3_direct_kernel<16, 4, 8, 8><<<g, 256, hs, ctx->stream>>>(a, TW);
+    else if (v == 1)
+      conv3x3_direct_kernel<32, 4, 8, 8><<<g, 256, hs, ctx->stream>>>(a, TW);
+    else if (v == 2)
+      conv3x3_direct_kernel<64, 8, 8, 8><<<g, 256, hs, ctx->stream>>>(a, TW);
+    else
+      conv3x3_direct_kernel<64, 8, 4, 8><<<g, 256, hs, ctx->stream>>>(a, TW);
+    note_launch();
+    RVC_CUDA_TRY(cudaGetLastError());
+    if (splits > 1) {
+      conv2d_reduce_kernel<<<grid_for(B * M * L.C_out, 256), 256, 0, ctx->stream>>>(a);
       note_launch();
       RVC_CUDA_TRY(cudaGetLastError());
-      if (ctx->prof) {
-        char lab[160];
-        snprintf(lab, sizeof(lab), "rmvpe conv Cin=%d Cout=%d taps=9 %dx%d B=%d direct", L.C_in, L.C_out, a.OH, a.OW,
-                 B);
-        ctx->prof_end(e0, e1, 2.0 * B * M * L.C_out * L.C_in * 9.0, lab, false);
-      }
-      return;
     }
+    if (ctx->prof) {
+      char lab[160];
+      snprintf(lab, sizeof(lab), "rmvpe conv Cin=%d Cout=%d taps=9 %dx%d B=%d direct split=%d", L.C_in, L.C_out,
+               a.OH, a.OW, B, splits);
+      ctx->prof_end(e0, e1, 2.0 * B * M * L.C_out * L.C_in * 9.0, lab, false);
+    }
+    return;
   }
   // narrow stride-1 convs (<= 32 output channels, the tall full-resolution
   // levels): register-blocked 8 x 4 tiles; the rest (measured faster there:
