@@ -487,6 +487,145 @@ __global__ void __launch_bounds__(256, 2) conv3x3_direct_kernel(const C2Args a, 
   }
 }
 
+// Direct 3x3 stride-2 transposed conv, split by output parity: output
+// (2i + ph, 2j + pw) takes kernel row 1 from input row i when ph = 0, rows 0
+// and 2 from input rows i + 1 and i when ph = 1 (columns likewise), so each
+// output sums 1, 2, 2 or 4 taps instead of masking nine.  Each thread owns one
+// output row x TMP input columns (2 TMP output columns) x TNC channels; pixel
+// groups are ordered by row parity so a warp's branch is uniform.  The
+// reference computes rows / columns < 2H - 1 / 2W - 1 only and zero-fills the
+// output-padding row and column (runtime/models/rmvpe.py:378-384): those sums
+// are zeroed before the epilogue.  Same double-buffered halo / weights and
+// channel-block split as conv3x3_direct_kernel.
+// Accumulation order per output: channel block, channel, kernel row, column.
+template <int BN, int TNC, int TMP, int CK>
+__global__ void __launch_bounds__(256, 2) convT3x3_direct_kernel(const C2Args a, int TW) {
+  constexpr int NT = BN / TNC;
+  constexpr int G = 256 / NT;  // pixel groups per tile
+  constexpr int WST = 9 * CK * BN;
+  extern __shared__ __align__(16) float dsm[];
+  const int gpr = TW / TMP;  // groups per output row
+  const int OHt = G / gpr;   // output rows per tile (even)
+  const int IR = OHt / 2 + 1, IW = TW + 1;
+  const int npx = IR * IW;
+  const int HST = (npx * (CK + 1) + 3) & ~3;
+  float* wts = dsm;
+  float* halo = dsm + 2 * WST;
+  const int tid = threadIdx.x;
+  const int tilesW = (a.W + TW - 1) / TW;
+  const int oh0 = (blockIdx.x / tilesW) * OHt, w0 = (blockIdx.x % tilesW) * TW;  // w0: input column
+  const int i0 = oh0 / 2;
+  const int n0 = blockIdx.y * BN;
+  const int b = blockIdx.z / a.splits, sp = blockIdx.z - b * a.splits;
+  const int ncb = (a.C_in + CK - 1) / CK;
+  const int cb0 = (int)((long long)ncb * sp / a.splits), cb1 = (int)((long long)ncb * (sp + 1) / a.splits);
+  const float* xb = a.x + (long long)b * a.x_bs;
+  const int tn = tid % NT, g = tid / NT;
+  const int ph = g / (G / 2), rem = g % (G / 2);
+  const int rr = rem / gpr, pc = (rem % gpr) * TMP;
+  const int oh = oh0 + 2 * rr + ph;  // input row i0 + rr is local halo row rr
+  auto issue = [&](int cb, int st) {
+    const int c0 = cb * CK;
+    float* hs = halo + st * HST;
+    for (int e = tid; e < npx * CK; e += 256) {
+      const int px = e / CK, c = e % CK;
+      const int ih = i0 + px / IW, iw = w0 + px % IW;
+      const bool ok = ih < a.H && iw < a.W && c0 + c < a.C_in;
+      cp_async4(hs + px * (CK + 1) + c, ok ? xb + ((long long)ih * a.W + iw) * a.ldi + c0 + c : xb, ok ? 4 : 0);
+    }
+    float* ws = wts + st * WST;
+    for (int e = tid; e < WST; e += 256) {
+      const int n = e % BN, c = (e / BN) % CK, tap = e / (BN * CK);
+      const bool ok = c0 + c < a.C_in && n0 + n < a.C_out;
+      cp_async4(ws + e, ok ? a.w + ((long long)tap * a.C_in + c0 + c) * a.C_out + n0 + n : a.w, ok ? 4 : 0);
+    }
+    cp_async_commit();
+  };
+  float acc[TMP][2][TNC];
+#pragma unroll
+  for (int i = 0; i < TMP; ++i)
+#pragma unroll
+    for (int p = 0; p < 2; ++p)
+#pragma unroll
+      for (int j = 0; j < TNC; ++j) acc[i][p][j] = 0.f;
+  if (cb0 < cb1) issue(cb0, 0);
+  for (int cb = cb0; cb < cb1; ++cb) {
+    const int st = (cb - cb0) & 1;
+    if (cb + 1 < cb1) {
+      issue(cb + 1, st ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const float* hs = halo + st * HST;
+    const float* ws = wts + st * WST;
+#pragma unroll 2
+    for (int c = 0; c < CK; ++c) {
+      // kernel row ky read from local input row lr: column taps kx = 1 (even
+      // outputs, column j), then kx = 0 (column j + 1) and kx = 2 (column j)
+      auto krow = [&](int ky, int lr) {
+        float r[TMP + 1];
+        const float* hp = hs + (lr * IW + pc) * (CK + 1) + c;
+#pragma unroll
+        for (int k = 0; k < TMP + 1; ++k) r[k] = hp[k * (CK + 1)];
+        float wv[TNC];
+        auto wload = [&](int kx) {
+#pragma unroll
+          for (int q = 0; q < TNC / 4; ++q) {
+            const float4 v = *reinterpret_cast<const float4*>(ws + ((ky * 3 + kx) * CK + c) * BN + q * NT * 4 + tn * 4);
+            wv[4 * q] = v.x; wv[4 * q + 1] = v.y; wv[4 * q + 2] = v.z; wv[4 * q + 3] = v.w;
+          }
+        };
+        wload(1);
+#pragma unroll
+        for (int t = 0; t < TMP; ++t)
+#pragma unroll
+          for (int j = 0; j < TNC; ++j) acc[t][0][j] = fmaf(r[t], wv[j], acc[t][0][j]);
+        wload(0);
+#pragma unroll
+        for (int t = 0; t < TMP; ++t)
+#pragma unroll
+          for (int j = 0; j < TNC; ++j) acc[t][1][j] = fmaf(r[t + 1], wv[j], acc[t][1][j]);
+        wload(2);
+#pragma unroll
+        for (int t = 0; t < TMP; ++t)
+#pragma unroll
+          for (int j = 0; j < TNC; ++j) acc[t][1][j] = fmaf(r[t], wv[j], acc[t][1][j]);
+      };
+      if (ph == 0) {
+        krow(1, rr);
+      } else {
+        krow(0, rr + 1);
+        krow(2, rr);
+      }
+    }
+    __syncthreads();  // stage st is refilled by the next iteration's issue
+  }
+  if (oh >= a.OH) return;
+  const bool zrow = oh == 2 * a.H - 1;
+  const long long M = (long long)a.OH * a.OW;
+#pragma unroll
+  for (int t = 0; t < TMP; ++t) {
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      const int ow = 2 * (w0 + pc + t) + p;
+      if (ow >= a.OW) continue;
+      const bool zero = zrow || ow == 2 * a.W - 1;
+#pragma unroll
+      for (int j = 0; j < TNC; ++j) {
+        const int co = n0 + (j / 4) * (NT * 4) + tn * 4 + (j % 4);
+        if (co >= a.C_out) continue;
+        const float v = zero ? 0.f : acc[t][p][j];
+        if (a.splits > 1)
+          a.part[(((long long)sp * a.B + b) * M + (long long)oh * a.OW + ow) * a.C_out + co] = v;
+        else
+          c2_store(a, b, oh * a.OW + ow, co, v);
+      }
+    }
+  }
+}
+
 // Split-K: partial sums added in split order, then the epilogue.
 __global__ void conv2d_reduce_kernel(const C2Args a) {
   const long long M = (long long)a.OH * a.OW, per = M * a.C_out, n = per * a.B;
@@ -554,16 +693,24 @@ __global__ void __cluster_dims__(kGruCta, 1, 1) __launch_bounds__(kGruThreads)
   const int gu = tid % kGruUnits, gb = tid / kGruUnits;  // gate threads: unit, sequence
   const bool gate = gb < nb;
   const int j = rank * kGruUnits + gu;
+  // the input gates of step s + 1 are loaded during step s, so the recurrence
+  // does not wait on a global load
+  float nx[3] = {0.f, 0.f, 0.f};
+  auto fetch = [&](int s2) {
+    if (gate && s2 < T) {
+      const int t2 = dir == 0 ? s2 : T - 1 - s2;
+      const float* g = gx + ((long long)(b0 + gb) * T + t2) * 1536 + dir * 768;
+      nx[0] = g[j];
+      nx[1] = g[256 + j];
+      nx[2] = g[512 + j];
+    }
+  };
+  fetch(0);
   for (int s = 0; s < T; ++s) {
     const int tt = dir == 0 ? s : T - 1 - s;
     const int cur = s & 1, nxt = cur ^ 1;
-    float gxr = 0.f, gxz = 0.f, gxn = 0.f;
-    if (gate) {
-      const float* g = gx + ((long long)(b0 + gb) * T + tt) * 1536 + dir * 768;
-      gxr = g[j];
-      gxz = g[256 + j];
-      gxn = g[512 + j];
-    }
+    const float gxr = nx[0], gxz = nx[1], gxn = nx[2];
+    fetch(s + 1);
     for (int bb = 0; bb < nb; ++bb) {
       float hv[8];
 #pragma unroll
@@ -986,6 +1133,58 @@ void RmvpeModel::conv(const Conv2dW& L, int B, const float* x, long long x_bs, i
       snprintf(lab, sizeof(lab), "rmvpe conv Cin=%d Cout=%d taps=9 %dx%d B=%d direct split=%d", L.C_in, L.C_out,
                a.OH, a.OW, B, splits);
       ctx->prof_end(e0, e1, 2.0 * B * M * L.C_out * L.C_in * 9.0, lab, false);
+    }
+    return;
+  }
+  if (L.transposed && L.taps == 9 && Wd >= 4) {
+    // parity-split direct transposed conv: <BN, TNC, TMP = 4, CK = 8>
+    const int vt = L.C_out <= 16 ? 0 : (L.C_out <= 32 ? 1 : 2);
+    static const int kTBN[3] = {16, 32, 64}, kTTNC[3] = {4, 4, 8};
+    const int BNd = kTBN[vt], TMP = 4, CK = 8;
+    const int G = 256 / (BNd / kTTNC[vt]);
+    const int TW = std::min(32, Wd) / TMP * TMP;
+    const int OHt = G / (TW / TMP);
+    const int ncb = (L.C_in + CK - 1) / CK;
+    const long long tiles = (long long)((a.OH + OHt - 1) / OHt) * ((Wd + TW - 1) / TW) * ((L.C_out + BNd - 1) / BNd);
+    int splits = 1;
+    while (tiles * B * splits < 2 * 148 && ncb / (splits * 2) >= 2 && splits < 16) splits *= 2;
+    if (splits > 1 && (size_t)splits * B * M * L.C_out * sizeof(float) > ws_.at("part").bytes) splits = 1;
+    a.splits = splits;
+    a.part = ws_.at("part").f();
+    dim3 g((unsigned)(((a.OH + OHt - 1) / OHt) * ((Wd + TW - 1) / TW)), (unsigned)((L.C_out + BNd - 1) / BNd),
+           (unsigned)(B * splits));
+    const size_t hs =
+        sizeof(float) * 2 * ((size_t)9 * CK * BNd + (((size_t)(OHt / 2 + 1) * (TW + 1) * (CK + 1) + 3) & ~(size_t)3));
+    static std::atomic<uint64_t> attr_done{0};  // the attribute is per device
+    if (ctx->device < 64 && !(attr_done.load() & (1ull << ctx->device))) {
+      RVC_CUDA_TRY(cudaFuncSetAttribute(convT3x3_direct_kernel<16, 4, 4, 8>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+      RVC_CUDA_TRY(cudaFuncSetAttribute(convT3x3_direct_kernel<32, 4, 4, 8>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+      RVC_CUDA_TRY(cudaFuncSetAttribute(convT3x3_direct_kernel<64, 8, 4, 8>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024));
+      attr_done.fetch_or(1ull << ctx->device);
+    }
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (ctx->prof) ctx->prof_begin(&e0, &e1);
+    if (vt == 0)
+      convT3x3_direct_kernel<16, 4, 4, 8><<<g, 256, hs, ctx->stream>>>(a, TW);
+    else if (vt == 1)
+      convT3x3_direct_kernel<32, 4, 4, 8><<<g, 256, hs, ctx->stream>>>(a, TW);
+    else
+      convT3x3_direct_kernel<64, 8, 4, 8><<<g, 256, hs, ctx->stream>>>(a, TW);
+    note_launch();
+    RVC_CUDA_TRY(cudaGetLastError());
+    if (splits > 1) {
+      conv2d_reduce_kernel<<<grid_for(B * M * L.C_out, 256), 256, 0, ctx->stream>>>(a);
+      note_launch();
+      RVC_CUDA_TRY(cudaGetLastError());
+    }
+    if (ctx->prof) {
+      char lab[160];
+      snprintf(lab, sizeof(lab), "rmvpe convT Cin=%d Cout=%d taps=9 %dx%d B=%d direct split=%d", L.C_in, L.C_out,
+               a.OH, a.OW, B, splits);
+      ctx->prof_end(e0, e1, 2.0 * B * M * L.C_out * L.C_in * 2.25, lab, false);
     }
     return;
   }
