@@ -219,12 +219,22 @@ int32_t rvc_cuda_destroy(int64_t ctx) {
       std::lock_guard<std::mutex> lk(g_reg_mu);
       auto it = g_ctx.find(ctx);
       if (it == g_ctx.end()) throw Error{kErrState, "invalid context handle " + std::to_string(ctx)};
-      for (auto s = g_synth.begin(); s != g_synth.end();) {
-        if (s->second->ctx == it->second.get())
-          s = g_synth.erase(s);
-        else
-          ++s;
-      }
+      // every model bound to this context goes first: their buffers and plans
+      // are released through it
+      const Context* cp = it->second.get();
+      auto drop = [cp](auto& reg) {
+        for (auto s = reg.begin(); s != reg.end();) {
+          if (s->second->ctx == cp)
+            s = reg.erase(s);
+          else
+            ++s;
+        }
+      };
+      drop(g_synth);
+      drop(g_hubert);
+      drop(g_index);
+      drop(g_rmvpe);
+      drop(g_fcpe);
       c = std::move(it->second);
       g_ctx.erase(it);
     }

@@ -19,6 +19,7 @@
 #include "rmvpe.cuh"
 
 #include <cooperative_groups.h>
+#include <cufft.h>
 
 #include <algorithm>
 #include <atomic>
@@ -57,33 +58,28 @@ __device__ __forceinline__ float np_sum_small(const float* a, int n) {
 }
 
 // ------------------------------------------------------------------ front end
-// |rfft(frame * hann)| in float64, cast to float32: mag[b][t][k], k < 513.
-// Frames come from the reflect-padded signal (pad 512 each side).
-__global__ void __launch_bounds__(256) stft_mag_kernel(const float* __restrict__ x, long long T, int F,
-                                                        const double* __restrict__ window,
-                                                        const double* __restrict__ tw, float* __restrict__ mag) {
-  __shared__ double xs[1024];
-  __shared__ double cs[1024], sn[1024];
-  const int t = blockIdx.x, b = blockIdx.y;
-  const float* xb = x + (long long)b * T;
-  for (int n = threadIdx.x; n < 1024; n += blockDim.x) {
+// |rfft(frame * hann)| in float64, cast to float32: the windowed frames of the
+// reflect-padded signal (pad 512 each side) go to frames[b][t][1024] (double),
+// a batched cuFFT D2Z gives spec[b][t][513], then mag[b][t][k].
+__global__ void stft_frames_kernel(const float* __restrict__ x, long long T, int F, const double* __restrict__ window,
+                                   double* __restrict__ frames, int B) {
+  const long long n_all = (long long)B * F * 1024;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n_all;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int n = (int)(e & 1023);
+    const long long bt = e >> 10;
+    const int b = (int)(bt / F), t = (int)(bt - (long long)b * F);
     long long p = (long long)t * 160 + n - 512;
     if (p < 0) p = -p;
     if (p >= T) p = 2 * (T - 1) - p;
-    xs[n] = (double)xb[p] * window[n];
-    cs[n] = tw[n];
-    sn[n] = tw[1024 + n];
+    frames[e] = (double)x[(long long)b * T + p] * window[n];
   }
-  __syncthreads();
-  for (int k = threadIdx.x; k < 513; k += blockDim.x) {
-    double re = 0.0, im = 0.0;
-    int idx = 0;
-    for (int n = 0; n < 1024; ++n) {
-      re = fma(xs[n], cs[idx], re);
-      im = fma(xs[n], sn[idx], im);
-      idx = (idx + k) & 1023;
-    }
-    mag[((long long)b * F + t) * 513 + k] = (float)sqrt(re * re + im * im);
+}
+
+__global__ void stft_mag_kernel(const double2* __restrict__ spec, long long n, float* __restrict__ mag) {
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
+    const double2 v = spec[e];
+    mag[e] = (float)sqrt(v.x * v.x + v.y * v.y);
   }
 }
 
@@ -795,6 +791,11 @@ int grid_for(long long n, int block) {
 // ================================================================== model
 RmvpeModel::RmvpeModel(Context* c) : ctx(c) {}
 
+RmvpeModel::~RmvpeModel() {
+  if (!fft_plans_.empty()) cudaStreamSynchronize(ctx->stream);  // no transform still in flight
+  for (auto& kv : fft_plans_) cufftDestroy((cufftHandle)kv.second);
+}
+
 void RmvpeModel::set_weight(const std::string& key, const float* host, const std::vector<int64_t>& shape) {
   RmvpeTensor t;
   t.shape = shape;
@@ -993,20 +994,16 @@ void RmvpeModel::finalize() {
       }
       for (int k = 0; k < nb; ++k) basis[(size_t)i * nb + k] = (float)(s > 0 ? tri[k] / s : tri[k]);
     }
-    std::vector<double> win(kNFFT), tw(2 * kNFFT);
+    std::vector<double> win(kNFFT);
     const double pi = 3.14159265358979323846;
     for (int k = 0; k < kNFFT; ++k) {
       const double n = 1.0 - kNFFT + 2.0 * k;  // numpy.hanning: 0.5 + 0.5 cos(pi n / (M - 1))
       win[k] = 0.5 + 0.5 * std::cos(pi * n / (kNFFT - 1));
-      tw[k] = std::cos(2.0 * pi * k / kNFFT);
-      tw[kNFFT + k] = -std::sin(2.0 * pi * k / kNFFT);
     }
     mel_basis_ = DevBuf(ctx, sizeof(float) * basis.size());
     window_ = DevBuf(ctx, sizeof(double) * win.size());
-    twiddle_ = DevBuf(ctx, sizeof(double) * tw.size());
     RVC_CUDA_TRY(cudaMemcpy(mel_basis_.p, basis.data(), mel_basis_.bytes, cudaMemcpyHostToDevice));
     RVC_CUDA_TRY(cudaMemcpy(window_.p, win.data(), window_.bytes, cudaMemcpyHostToDevice));
-    RVC_CUDA_TRY(cudaMemcpy(twiddle_.p, tw.data(), twiddle_.bytes, cudaMemcpyHostToDevice));
   }
   RVC_CUDA_TRY(cudaStreamSynchronize(st));
   finalized_ = true;
@@ -1037,6 +1034,8 @@ void RmvpeModel::ensure_ws(int B, int64_t T) {
   add("sal", Fp * 360);
   add("f0", F);
   ws_.emplace("amax", DevBuf(ctx, sizeof(int32_t) * (size_t)B * F));
+  ws_.emplace("frames", DevBuf(ctx, sizeof(double) * (size_t)B * F * kNFFT));
+  ws_.emplace("spec", DevBuf(ctx, 2 * sizeof(double) * (size_t)B * F * kBins));
   // split partials: the direct conv splits while the batch's tiles x splits <
   // 2 x 148, so the partials hold < 4 x 148 tiles x 256 pixels x 64 channels
   ws_.emplace("part", DevBuf(ctx, sizeof(float) * (size_t)4 * 148 * 256 * 64));
@@ -1270,9 +1269,29 @@ void RmvpeModel::infer_device(int B, int64_t T, const float* x, float thred, flo
   const int F = (int)frames(T), Fp = 32 * ((F - 1) / 32 + 1);
   const long long bs_big = (long long)(ws_.at("A").bytes / sizeof(float) / ws_B);
   // ---------------- front end
-  stft_mag_kernel<<<dim3(F, B), 256, 0, st>>>(x, T, F, (const double*)window_.p, (const double*)twiddle_.p,
-                                              buf("mag"));
-  note_launch();
+  {
+    const long long nfr = (long long)B * F;
+    auto it = fft_plans_.find(nfr);
+    if (it == fft_plans_.end()) {
+      cufftHandle h = 0;
+      int n = kNFFT;
+      if (cufftPlanMany(&h, 1, &n, nullptr, 1, kNFFT, nullptr, 1, kBins, CUFFT_D2Z, (int)nfr) != CUFFT_SUCCESS)
+        throw Error{kErrCuda, "rmvpe: cuFFT plan failed"};
+      it = fft_plans_.emplace(nfr, (int)h).first;
+    }
+    const cufftHandle h = (cufftHandle)it->second;
+    double* fr = reinterpret_cast<double*>(ws_.at("frames").p);
+    stft_frames_kernel<<<(unsigned)std::min<long long>((nfr * 1024 + 255) / 256, 148ll * 16), 256, 0, st>>>(
+        x, T, F, (const double*)window_.p, fr, B);
+    note_launch();
+    RVC_CUDA_TRY(cudaGetLastError());
+    if (cufftSetStream(h, st) != CUFFT_SUCCESS ||
+        cufftExecD2Z(h, (cufftDoubleReal*)fr, (cufftDoubleComplex*)ws_.at("spec").p) != CUFFT_SUCCESS)
+      throw Error{kErrCuda, "rmvpe: cuFFT transform failed"};
+    stft_mag_kernel<<<(unsigned)std::min<long long>((nfr * kBins + 255) / 256, 148ll * 16), 256, 0, st>>>(
+        (const double2*)ws_.at("spec").p, nfr * kBins, buf("mag"));
+    note_launch();
+  }
   mel_log_kernel<<<dim3(Fp, B), 128, 0, st>>>(buf("mag"), mel_basis_.f(), F, Fp, in_scale_.f(), in_shift_.f(),
                                               buf("mel"), buf("x0"));
   note_launch();

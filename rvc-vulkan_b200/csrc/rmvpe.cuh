@@ -34,6 +34,9 @@ class RmvpeModel {
   static constexpr int kNFFT = 1024, kHop = 160, kBins = 513, kMels = 128, kHidden = 256, kClasses = 360;
 
   explicit RmvpeModel(Context* ctx);
+  ~RmvpeModel();
+  RmvpeModel(const RmvpeModel&) = delete;
+  RmvpeModel& operator=(const RmvpeModel&) = delete;
   void set_weight(const std::string& key, const float* host, const std::vector<int64_t>& shape);
   void finalize();
   static int64_t frames(int64_t T) { return 1 + T / kHop; }
@@ -62,7 +65,8 @@ class RmvpeModel {
   std::unordered_map<std::string, RmvpeTensor> raw_;
   std::map<std::string, Conv2dW> convs_;  // by checkpoint prefix
   DevBuf in_scale_, in_shift_;            // unet.encoder.bn
-  DevBuf mel_basis_, window_, twiddle_;   // front end tables
+  DevBuf mel_basis_, window_;             // front end tables
+  std::map<long long, int> fft_plans_;    // cuFFT D2Z plans (n = 1024) by frame count
   DevBuf w_hh_, b_hh_;                    // GRU recurrent weights [2][768][256], biases [2][768]
   int ws_B = 0;
   int64_t ws_T = 0;
