@@ -17,6 +17,8 @@
 // the STFT and the GroupNorm statistics).
 #include "fcpe.cuh"
 
+#include <cufft.h>
+
 #include <algorithm>
 #include <cmath>
 
@@ -25,14 +27,17 @@ namespace rvc {
 namespace {
 
 // |rfft(frame * window)|: mag[b][t][k] = sqrt(re^2 + im^2 + 1e-9), k < 513.
-__global__ void __launch_bounds__(256) fcpe_stft_kernel(const float* __restrict__ x, long long T, int nf,
-                                                         bool reflect, const double* __restrict__ window,
-                                                         const double* __restrict__ tw, float* __restrict__ mag) {
-  __shared__ double xs[1024];
-  __shared__ double cs[1024], sn[1024];
-  const int t = blockIdx.x, b = blockIdx.y;
-  const float* xb = x + (long long)b * T;
-  for (int n = threadIdx.x; n < 1024; n += blockDim.x) {
+// The windowed frames (offset -432, reflect or zero padding) go to
+// frames[b][t][1024] (double), a batched cuFFT D2Z gives spec[b][t][513].
+__global__ void fcpe_frames_kernel(const float* __restrict__ x, long long T, int nf, bool reflect,
+                                   const double* __restrict__ window, double* __restrict__ frames, int B) {
+  const long long n_all = (long long)B * nf * 1024;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n_all;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int n = (int)(e & 1023);
+    const long long bt = e >> 10;
+    const int b = (int)(bt / nf), t = (int)(bt - (long long)b * nf);
+    const float* xb = x + (long long)b * T;
     long long p = (long long)t * 160 + n - 432;
     double v;
     if (reflect) {
@@ -42,20 +47,14 @@ __global__ void __launch_bounds__(256) fcpe_stft_kernel(const float* __restrict_
     } else {
       v = (p >= 0 && p < T) ? (double)xb[p] : 0.0;
     }
-    xs[n] = v * window[n];
-    cs[n] = tw[n];
-    sn[n] = tw[1024 + n];
+    frames[e] = v * window[n];
   }
-  __syncthreads();
-  for (int k = threadIdx.x; k < 513; k += blockDim.x) {
-    double re = 0.0, im = 0.0;
-    int idx = 0;
-    for (int n = 0; n < 1024; ++n) {
-      re = fma(xs[n], cs[idx], re);
-      im = fma(xs[n], sn[idx], im);
-      idx = (idx + k) & 1023;
-    }
-    mag[((long long)b * nf + t) * 513 + k] = (float)sqrt(__dadd_rn(__dadd_rn(__dmul_rn(re, re), __dmul_rn(im, im)), 1e-9));
+}
+
+__global__ void fcpe_mag_kernel(const double2* __restrict__ spec, long long n, float* __restrict__ mag) {
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
+    const double2 v = spec[e];
+    mag[e] = (float)sqrt(__dadd_rn(__dadd_rn(__dmul_rn(v.x, v.x), __dmul_rn(v.y, v.y)), 1e-9));
   }
 }
 
@@ -240,6 +239,11 @@ FcpeModel::FcpeModel(Context* c, int prec) : ctx(c), precision(prec) {
   RVC_CHECK_ARG(prec == 0 || prec == 1, "fcpe: precision must be 0 (tensor cores) or 1 (fp32 SIMT)");
 }
 
+FcpeModel::~FcpeModel() {
+  if (!fft_plans_.empty()) cudaStreamSynchronize(ctx->stream);  // no transform still in flight
+  for (auto& kv : fft_plans_) cufftDestroy((cufftHandle)kv.second);
+}
+
 void FcpeModel::set_weight(const std::string& key, const float* host, const std::vector<int64_t>& shape) {
   Tensor t;
   t.shape = shape;
@@ -300,16 +304,12 @@ void FcpeModel::finalize() {
   k_fold_weight_norm(W("output_proj.weight_v").buf.f(), W("output_proj.weight_g").buf.f(), wproj_.f(), kOut, kH, st);
   proj_ = ConvLayer();
   proj_.build(ctx, LayerKind::kConv, wproj_.f(), W("output_proj.bias").buf.f(), kOut, kH, 1, tc);
-  // front-end tables: periodic Hann (torch.hann_window), DFT twiddles, Slaney
+  // front-end tables: periodic Hann (torch.hann_window), Slaney
   // mel filters with area normalisation (runtime/dsp/mel.py:118-146)
   {
     const double pi = 3.14159265358979323846;
-    std::vector<double> win(kNFFT), tw(2 * kNFFT);
-    for (int k = 0; k < kNFFT; ++k) {
-      win[k] = 0.5 - 0.5 * std::cos(2.0 * pi * k / kNFFT);
-      tw[k] = std::cos(2.0 * pi * k / kNFFT);
-      tw[kNFFT + k] = -std::sin(2.0 * pi * k / kNFFT);
-    }
+    std::vector<double> win(kNFFT);
+    for (int k = 0; k < kNFFT; ++k) win[k] = 0.5 - 0.5 * std::cos(2.0 * pi * k / kNFFT);
     const double f_sp = 200.0 / 3.0, min_log_hz = 1000.0, min_log_mel = min_log_hz / f_sp;
     const double logstep = std::log(6.4) / 27.0;
     auto hz_to_mel = [&](double f) { return f >= min_log_hz ? min_log_mel + std::log(f / min_log_hz) / logstep : f / f_sp; };
@@ -329,10 +329,8 @@ void FcpeModel::finalize() {
       }
     }
     window_ = DevBuf(ctx, sizeof(double) * win.size());
-    twiddle_ = DevBuf(ctx, sizeof(double) * tw.size());
     basis_ = DevBuf(ctx, sizeof(float) * basis.size());
     RVC_CUDA_TRY(cudaMemcpyAsync(window_.p, win.data(), window_.bytes, cudaMemcpyHostToDevice, st));
-    RVC_CUDA_TRY(cudaMemcpyAsync(twiddle_.p, tw.data(), twiddle_.bytes, cudaMemcpyHostToDevice, st));
     RVC_CUDA_TRY(cudaMemcpyAsync(basis_.p, basis.data(), basis_.bytes, cudaMemcpyHostToDevice, st));
   }
   RVC_CUDA_TRY(cudaStreamSynchronize(st));
@@ -362,6 +360,9 @@ void FcpeModel::ensure_ws(int B, int64_t T) {
   add("f0", F);
   add("am", F);
   add("gn", 2 * kGroups * ((F + kGnRows - 1) / kGnRows) * 2 + 2 * kGroups);  // doubles in float units
+  // STFT frames (nf <= F) as doubles and their D2Z spectra
+  ws_.emplace("frames", DevBuf(ctx, sizeof(double) * (size_t)B * F * kNFFT));
+  ws_.emplace("spec", DevBuf(ctx, 2 * sizeof(double) * (size_t)B * F * kBins));
   ws_B = B;
   ws_T = T;
 }
@@ -393,9 +394,29 @@ void FcpeModel::infer_device(int B, int64_t T, const float* x, float threshold, 
   const bool reflect = pr < T;
   const int nf = (int)(1 + (T + pl + pr - kNFFT) / kHop);
   // ---------------- front end
-  fcpe_stft_kernel<<<dim3(nf, B), 256, 0, st>>>(x, T, nf, reflect, (const double*)window_.p,
-                                                (const double*)twiddle_.p, buf("mag"));
-  note_launch();
+  {
+    const long long nfr = (long long)B * nf;
+    auto it = fft_plans_.find(nfr);
+    if (it == fft_plans_.end()) {
+      cufftHandle h = 0;
+      int n = kNFFT;
+      if (cufftPlanMany(&h, 1, &n, nullptr, 1, kNFFT, nullptr, 1, kBins, CUFFT_D2Z, (int)nfr) != CUFFT_SUCCESS)
+        throw Error{kErrCuda, "fcpe: cuFFT plan failed"};
+      it = fft_plans_.emplace(nfr, (int)h).first;
+    }
+    const cufftHandle h = (cufftHandle)it->second;
+    double* fr = reinterpret_cast<double*>(ws_.at("frames").p);
+    fcpe_frames_kernel<<<(unsigned)std::min<long long>((nfr * 1024 + 255) / 256, 148ll * 16), 256, 0, st>>>(
+        x, T, nf, reflect, (const double*)window_.p, fr, B);
+    note_launch();
+    RVC_CUDA_TRY(cudaGetLastError());
+    if (cufftSetStream(h, st) != CUFFT_SUCCESS ||
+        cufftExecD2Z(h, (cufftDoubleReal*)fr, (cufftDoubleComplex*)ws_.at("spec").p) != CUFFT_SUCCESS)
+      throw Error{kErrCuda, "fcpe: cuFFT transform failed"};
+    fcpe_mag_kernel<<<(unsigned)std::min<long long>((nfr * kBins + 255) / 256, 148ll * 16), 256, 0, st>>>(
+        (const double2*)ws_.at("spec").p, nfr * kBins, buf("mag"));
+    note_launch();
+  }
   fcpe_mel_kernel<<<dim3(F, B), 128, 0, st>>>(buf("mag"), basis_.f(), nf, F, buf("mel"));
   note_launch();
   RVC_CUDA_TRY(cudaGetLastError());

@@ -17,6 +17,9 @@ class FcpeModel {
   static constexpr int kDWK = 31, kLayers = 6, kOut = 360, kGroups = 4;
 
   FcpeModel(Context* ctx, int precision);
+  ~FcpeModel();
+  FcpeModel(const FcpeModel&) = delete;
+  FcpeModel& operator=(const FcpeModel&) = delete;
   // Checkpoint tensors under the reference's keys (FCPE.W), incl. cent_table.
   void set_weight(const std::string& key, const float* host, const std::vector<int64_t>& shape);
   void finalize();
@@ -47,7 +50,8 @@ class FcpeModel {
   bool finalized_ = false;
   std::unordered_map<std::string, Tensor> raw_;
   ConvLayer in0_, in3_, up_[kLayers], down_[kLayers], proj_;
-  DevBuf window_, twiddle_, basis_, wproj_;
+  DevBuf window_, basis_, wproj_;
+  std::map<long long, int> fft_plans_;  // cuFFT D2Z plans (n = 1024) by frame count
   int ws_B = 0;
   int64_t ws_T = 0;
   std::map<std::string, DevBuf> ws_;
