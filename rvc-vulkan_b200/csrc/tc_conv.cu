@@ -906,10 +906,31 @@ static TcPlan tc_plan(const ConvArgs& a) {
     g.smem_bytes = total(stages);
     return true;
   };
-  bool found = false;
-  for (int i = 0; i < ncand && !found; ++i) found = try_cand(cands[i], cands[i].min_stages);
-  for (int i = 0; i < ncand && !found; ++i) found = try_cand(cands[i], 2);
-  RVC_CHECK_ARG(found, "tc_conv: tile does not fit in shared memory");
+  // Best-first, except that a plan whose tiles leave SMs idle (one long
+  // sequence: few row tiles) gives way to the fitting candidate with fewer
+  // 128-row subtiles per tile and so more tiles; a row's K order is the same
+  // for every msub.
+  const int sms = g_num_sms > 0 ? g_num_sms : 148;
+  auto tiles_for = [&](int msub) {
+    return (long long)a.B * a.nslices * (a.C_out / a.bn) * cdiv(maxrows, msub * kTM);
+  };
+  int pick = -1, pick_need = 0;
+  long long pick_tiles = -1;
+  for (int pass = 0; pass < 2 && (pick < 0 || pick_tiles < sms); ++pass) {
+    for (int i = 0; i < ncand; ++i) {
+      const int need = pass == 0 ? cands[i].min_stages : 2;
+      if (!try_cand(cands[i], need)) continue;
+      const long long t = tiles_for(cands[i].msub);
+      if (t > pick_tiles) {
+        pick = i;
+        pick_need = need;
+        pick_tiles = t;
+      }
+      if (t >= sms) break;
+    }
+  }
+  RVC_CHECK_ARG(pick >= 0, "tc_conv: tile does not fit in shared memory");
+  try_cand(cands[pick], pick_need);
   g.tiles_m = cdiv(maxrows, g.msub * kTM);
   g.ntiles = a.C_out / a.bn;
   g.total_tiles = a.B * a.nslices * g.ntiles * g.tiles_m;
@@ -922,6 +943,11 @@ void launch_tc_conv(const ConvArgs& a, cudaStream_t st) {
                 "tc_conv: channel tiling");
   RVC_CHECK_ARG(a.x_ld % 4 == 0 && a.x_bs % 4 == 0 && ((uintptr_t)a.x & 15) == 0,
                 "tc_conv: input rows must be 16-byte aligned");
+  if (g_num_sms == 0) {
+    int d = 0;
+    RVC_CUDA_TRY(cudaGetDevice(&d));
+    RVC_CUDA_TRY(cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, d));
+  }
   TcPlan g = tc_plan(a);
   if (g.total_tiles == 0) return;
   TcMaps maps;

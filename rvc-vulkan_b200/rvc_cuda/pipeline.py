@@ -22,6 +22,7 @@ Not offered here: ``brute_mix != 0`` (raises ``NotImplementedError``).
 
 from __future__ import annotations
 
+import os
 import time
 from typing import Optional
 
@@ -429,7 +430,10 @@ class Pipeline:
                 and hasattr(model, "out_frames")) or not chunk_lengths:
             return None
         from concurrent.futures import ThreadPoolExecutor  # noqa: PLC0415
-        ex = ThreadPoolExecutor(max_workers=1, thread_name_prefix="rvc-noise")
+        # each chunk draws from its own RandomState(seed), so the chunks are
+        # independent: one thread per chunk (up to the host's cores)
+        workers = max(1, min(len(chunk_lengths), os.cpu_count() or 1, 8))
+        ex = ThreadPoolExecutor(max_workers=workers, thread_name_prefix="rvc-noise")
         jobs = []
         for n in chunk_lengths:
             P = 2 * int(model.out_frames(n))
