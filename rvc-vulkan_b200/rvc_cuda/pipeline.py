@@ -83,9 +83,11 @@ class Pipeline:
         mel quantisation to 1..255.  Returns ``(f0_coarse int32, f0 float32)``."""
         if f0_method not in ("pm", "rmvpe", "fcpe"):
             raise ValueError(f"Unsupported F0 method: {f0_method}")
+        return self._f0_post(self._f0_raw(x, p_len, f0_method), f0_up_key)
+
+    def _f0_raw(self, x, p_len, f0_method):
+        """The f0 estimator's Hz curve of a segment (``runtime/pipeline.py:428-462``)."""
         f0_min, f0_max = 50, 1100
-        f0_mel_min = 1127 * np.log(1 + f0_min / 700)
-        f0_mel_max = 1127 * np.log(1 + f0_max / 700)
         if f0_method == "pm":                                          # :428-441
             f0 = np.asarray(dsp.f0_autocorrelation(np.asarray(x, dtype=np.float64), self.sr, voicing_threshold=0.6,
                                                    f0_min=f0_min, f0_max=f0_max, time_step=0.01), dtype=np.float64)
@@ -105,6 +107,16 @@ class Pipeline:
                                    "infer_from_audio(x, thred))")
             f0 = np.asarray(self.model_rmvpe.infer_from_audio(np.asarray(x, dtype=np.float32), thred=0.03),
                             dtype=np.float64)
+        return f0
+
+    @staticmethod
+    def _f0_post(f0, f0_up_key):
+        """Unvoiced frames interpolated, transposition, mel quantisation to
+        1..255 (``runtime/pipeline.py:468-482``)."""
+        f0_min, f0_max = 50, 1100
+        f0_mel_min = 1127 * np.log(1 + f0_min / 700)
+        f0_mel_max = 1127 * np.log(1 + f0_max / 700)
+        f0 = np.array(f0, dtype=np.float64)
         uv = f0 == 0
         if uv.any():
             voiced = np.where(~uv)[0]
@@ -270,13 +282,21 @@ class Pipeline:
         """f0 of every split segment, concatenated (``runtime/pipeline.py:795-816``)."""
         t1 = time.perf_counter()
         seg_pts = [0] + [o + self.t_pad for o in opt_ts] + [audio_pad.shape[0]]
-        pitch_parts, pitchf_parts = [], []
+        segs, cores = [], []
         for si in range(len(seg_pts) - 1):
             ap, bp = seg_pts[si], seg_pts[si + 1]
             b = min(bp + self.t_pad2 + self.window, audio_pad.shape[0])
-            seg = audio_pad[ap:b]
-            pi, pfi = self.get_f0(seg, seg.shape[0] // self.window, f0_up_key, f0_method)
-            core_n = max(1, (bp - ap) // self.window)
+            segs.append(audio_pad[ap:b])
+            cores.append(max(1, (bp - ap) // self.window))
+        model = getattr(self, "model_rmvpe", None)
+        if f0_method == "rmvpe" and len(segs) > 1 and hasattr(model, "infer_many"):
+            # the segments are independent calls: run them concurrently
+            raws = model.infer_many([np.asarray(g, dtype=np.float32) for g in segs], thred=0.03)
+            outs = [self._f0_post(r, f0_up_key) for r in raws]
+        else:
+            outs = [self.get_f0(g, g.shape[0] // self.window, f0_up_key, f0_method) for g in segs]
+        pitch_parts, pitchf_parts = [], []
+        for (pi, pfi), core_n in zip(outs, cores):
             pitch_parts.append(pi[:core_n])
             pitchf_parts.append(pfi[:core_n])
         pitch = np.concatenate(pitch_parts)[None, :]

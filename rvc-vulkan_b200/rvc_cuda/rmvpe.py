@@ -46,6 +46,8 @@ class CudaRmvpe:
             self.ctx = _lib.Context(dev)
         else:
             self.ctx = _lib.get_context(device)
+        self._weights = weights  # sibling lanes of infer_many are built from the same dict
+        self._lanes = []
         h = C.c_int64(0)
         check(lib.rvc_cuda_rmvpe_create(self.ctx.handle, C.byref(h)))
         self.handle = int(h.value)
@@ -95,6 +97,23 @@ class CudaRmvpe:
         if x.ndim != 1:
             raise ValueError(f"infer_from_audio needs 1-D audio, got {x.ndim}-D")
         return self.infer_batch(x[None, :], thred)[0]
+
+    def infer_many(self, xs, thred: float = 0.03):
+        """f0 of several 1-D clips of any lengths, run concurrently: clip ``i``
+        on lane ``i`` (this model, then sibling models with their own context
+        and stream, built on first use), one host thread per lane.  Each result
+        equals ``infer_from_audio`` of that clip (each clip is its own batch of
+        one, as in the reference's per-segment calls)."""
+        xs = [np.asarray(x, dtype=np.float32) for x in xs]
+        if len(xs) <= 1:
+            return [self.infer_from_audio(x, thred) for x in xs]
+        while len(self._lanes) < len(xs) - 1:
+            self._lanes.append(CudaRmvpe(self._weights, device=self.ctx.device, own_stream=True))
+        lanes = [self] + self._lanes[:len(xs) - 1]
+        from concurrent.futures import ThreadPoolExecutor  # noqa: PLC0415
+        with ThreadPoolExecutor(max_workers=len(xs), thread_name_prefix="rvc-rmvpe") as ex:
+            futs = [ex.submit(m.infer_from_audio, x, thred) for m, x in zip(lanes, xs)]
+            return [f.result() for f in futs]
 
     # ---------------------------------------------------------------- debug
     def keep_taps(self, on: bool = True):
