@@ -38,6 +38,12 @@ struct Context {
   int64_t prof_launches = 0;
   double prof_ms = 0.0, prof_flops = 0.0;
 
+  int sms = 0;
+  int num_sms() {
+    if (sms == 0 && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) sms = 148;
+    return sms;
+  }
+
   explicit Context(int dev);
   ~Context();
   void* alloc(size_t bytes);  // zero-filled

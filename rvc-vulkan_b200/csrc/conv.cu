@@ -118,32 +118,70 @@ size_t tc_packed_elems(int taps, int C_in, int C_out, int bn, int cb) {
   return (size_t)taps * C_in * C_out * 2;
 }
 
+// Offsets of element (tap, ci, co)'s hi and lo halves in the packed layout for
+// column tiles of bn and K blocks of cb: blocks (tap, column tile, K block) of
+// 2 cb bn values; inside, 8-channel chunks of bn columns x 8, hi and lo either
+// stacked per chunk (bn <= 64) or as two planes.
+__device__ __forceinline__ void tc_pack_offsets(int tap, int ci, int co, int C_in, int C_out, int bn, int cb,
+                                                long long& hi, long long& lo) {
+  const int ntiles = C_out / bn, nblk = C_in / cb;
+  const int nt = co / bn, n = co % bn;
+  const int kb = ci / cb, cc = ci % cb;
+  const int chunk = cc >> 3, e = cc & 7;
+  const long long blk = ((long long)(tap * ntiles + nt) * nblk + kb) * (2LL * cb * bn);
+  if (tc_stacked(bn)) {
+    hi = blk + ((long long)chunk * 2 * bn + n) * 8 + e;
+    lo = hi + (long long)bn * 8;
+  } else {
+    hi = blk + ((long long)chunk * bn + n) * 8 + e;
+    lo = hi + (long long)cb * bn;
+  }
+}
+
 __global__ void tc_pack_kernel(const float* __restrict__ w, uint16_t* __restrict__ wpk, int taps, int C_in,
                                int C_out, int bn, int cb) {
   const long long total = (long long)taps * C_in * C_out;
-  const int ntiles = C_out / bn, nblk = C_in / cb;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
        i += (long long)gridDim.x * blockDim.x) {
     const int co = (int)(i % C_out);
     const long long r = i / C_out;
     const int ci = (int)(r % C_in);
     const int tap = (int)(r / C_in);
-    const int nt = co / bn, n = co % bn;
-    const int kb = ci / cb, cc = ci % cb;
-    const int chunk = cc >> 3, e = cc & 7;
-    const long long blk = ((long long)(tap * ntiles + nt) * nblk + kb) * (2LL * cb * bn);
+    long long oh, ol;
+    tc_pack_offsets(tap, ci, co, C_in, C_out, bn, cb, oh, ol);
     __nv_bfloat16 hi, lo;
     split_bf16(w[i], hi, lo);
-    if (tc_stacked(bn)) {
-      const long long off = ((long long)chunk * 2 * bn + n) * 8 + e;
-      wpk[blk + off] = __bfloat16_as_ushort(hi);
-      wpk[blk + off + (long long)bn * 8] = __bfloat16_as_ushort(lo);
-    } else {
-      const long long off = ((long long)chunk * bn + n) * 8 + e;
-      wpk[blk + off] = __bfloat16_as_ushort(hi);
-      wpk[blk + (long long)cb * bn + off] = __bfloat16_as_ushort(lo);
-    }
+    wpk[oh] = __bfloat16_as_ushort(hi);
+    wpk[ol] = __bfloat16_as_ushort(lo);
   }
+}
+
+// The same hi / lo values moved from the layout for column tiles of bn_a to
+// the one for bn_b (K blocks of cb in both).
+__global__ void tc_repack_kernel(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst, int taps, int C_in,
+                                 int C_out, int bn_a, int bn_b, int cb) {
+  const long long total = (long long)taps * C_in * C_out;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int co = (int)(i % C_out);
+    const long long r = i / C_out;
+    const int ci = (int)(r % C_in);
+    const int tap = (int)(r / C_in);
+    long long ah, al, bh, bl;
+    tc_pack_offsets(tap, ci, co, C_in, C_out, bn_a, cb, ah, al);
+    tc_pack_offsets(tap, ci, co, C_in, C_out, bn_b, cb, bh, bl);
+    dst[bh] = src[ah];
+    dst[bl] = src[al];
+  }
+}
+
+void launch_tc_repack(const uint16_t* src, uint16_t* dst, int taps, int C_in, int C_out, int bn_a, int bn_b, int cb,
+                      cudaStream_t st) {
+  long long total = (long long)taps * C_in * C_out;
+  int grid = (int)std::min<long long>(cdiv<long long>(total, 256), 148 * 16);
+  tc_repack_kernel<<<grid, 256, 0, st>>>(src, dst, taps, C_in, C_out, bn_a, bn_b, cb);
+  note_launch();
+  RVC_CUDA_TRY(cudaGetLastError());
 }
 
 void launch_tc_pack(const float* w, uint16_t* wpk, int taps, int C_in, int C_out, int bn, int cb,

@@ -89,6 +89,9 @@ void launch_simt_conv(const ConvArgs& a, cudaStream_t st);
 void launch_tc_conv(const ConvArgs& a, cudaStream_t st);
 // Pack fp32 [taps][C_in][C_out] into the tcgen05 operand layout (conv.cu).
 size_t tc_packed_elems(int taps, int C_in, int C_out, int bn, int cb);
+// Packed weights for column tiles of bn_a -> the layout for bn_b (same values).
+void launch_tc_repack(const uint16_t* src, uint16_t* dst, int taps, int C_in, int C_out, int bn_a, int bn_b, int cb,
+                      cudaStream_t st);
 void launch_tc_pack(const float* w, uint16_t* wpk, int taps, int C_in, int C_out, int bn, int cb,
                     cudaStream_t st);
 bool tc_shape_ok(int C_in, int C_out);

@@ -126,13 +126,42 @@ void ConvLayer::run(Context* ctx, const ConvIO& io, bool force_simt) const {
   const bool use_tc = tc && !force_simt && !any_empty && (io.x_ld % 4 == 0) && (io.x_bs % 4 == 0);
   RVC_CHECK_ARG(use_tc || Wg.p, "conv: fp32 weights were released; only the tensor-core path can run this layer");
   if (use_tc) {
+    // Few row tiles even at one 128-row subtile per tile: narrower column
+    // tiles (the same weights repacked once) put more SMs to work.  Each
+    // output's K order is unchanged.
+    {
+      int maxrows = 0;
+      for (int s = 0; s < a.nslices; ++s) maxrows = std::max(maxrows, a.sl[s].rows);
+      const long long row_tiles = (long long)io.B * a.nslices * cdiv(maxrows, 128);
+      const int sms = ctx->num_sms();
+      // only widths that keep the MMA efficient and the epilogue in whole
+      // 32-column steps (narrower tiles measured slower)
+      if (2 * row_tiles * (C_out / bn) < sms) {
+        int want = 0;
+        for (int c : {128, 64})
+          if (c < bn && C_out % c == 0) {
+            want = c;
+            break;
+          }
+        if (want) {
+          if (bn_n != want) {
+            wpk_n = DevBuf(ctx, sizeof(uint16_t) * tc_packed_elems(taps_total, C_in, C_out, want, cb));
+            launch_tc_repack(wpk.as<uint16_t>(), wpk_n.as<uint16_t>(), taps_total, C_in, C_out, bn, want, cb,
+                             ctx->stream);
+            bn_n = want;
+          }
+          a.wpk = wpk_n.as<uint16_t>();
+          a.bn = bn_n;
+        }
+      }
+    }
     cudaEvent_t e0 = nullptr, e1 = nullptr;
     if (ctx->prof) ctx->prof_begin(&e0, &e1);
     launch_tc_conv(a, ctx->stream);
     if (ctx->prof) {
       char lab[160];
       snprintf(lab, sizeof(lab), "%s Cin=%d Cout=%d K=%d dil=%d up=%d g=%d T=%d B=%d bn=%d cb=%d",
-               kind == LayerKind::kConv ? "conv" : "convT", C_in, C_out, K, dil, up, groups, io.T_in, io.B, bn, cb);
+               kind == LayerKind::kConv ? "conv" : "convT", C_in, C_out, K, dil, up, groups, io.T_in, io.B, a.bn, cb);
       ctx->prof_end(e0, e1, flops(io.B, io.T_in), lab);
     }
   } else {

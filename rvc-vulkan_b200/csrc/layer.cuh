@@ -39,6 +39,10 @@ struct ConvLayer {
   DevBuf Wg, wpk, bias;
   bool tc = false;
   int bn = 0, cb = 0;
+  // narrower column tiles for launches whose row tiles leave SMs idle (one
+  // short sequence), packed from wpk on first use
+  mutable DevBuf wpk_n;
+  mutable int bn_n = 0;
 
   // W: conv [O,I,K] (I = input channels per group) or convT [I,O,K], device
   // fp32 (already weight-norm folded).

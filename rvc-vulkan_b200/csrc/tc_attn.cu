@@ -112,6 +112,11 @@ struct AttnArgs {
   const float* emb_v;  // [2W+1][D]
   int* err;
   int BH;              // chunks x heads
+  // key split: item = (query tile, key range); with nsplit > 1 each item
+  // writes its unnormalised O and (row max, row sum) for attn_combine_kernel
+  int nsplit;
+  float* po;           // [BH][nsplit][P][D]
+  float* pml;          // [BH][nsplit][P][2]
 };
 
 template <int D>
@@ -153,7 +158,7 @@ __global__ void __launch_bounds__(kAThreads, 1) tc_attn_kernel(const __grid_cons
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const uint32_t S_COL = 0, PV_COL = 256;  // S: 256 columns (stacked), O_t: 2D columns
-  const int total_items = a.BH * a.nq;
+  const int total_items = a.BH * a.nq * a.nsplit;
 
   if (warp == 0) {
     // ------------------------------------------------ loader
@@ -161,7 +166,9 @@ __global__ void __launch_bounds__(kAThreads, 1) tc_attn_kernel(const __grid_cons
       int qi = 0, kvi = 0;
       bool ok = true;
       for (int it = blockIdx.x; it < total_items && ok; it += gridDim.x) {
-        const int bh = it / a.nq, qt = it % a.nq;
+        const int sp = it % a.nsplit, bq = it / a.nsplit;
+        const int bh = bq / a.nq, qt = bq % a.nq;
+        const int kt0 = a.nk * sp / a.nsplit, kt1 = a.nk * (sp + 1) / a.nsplit;
         if (!ptx::mbar_wait(Q_EMPTY, (qi & 1) ^ 1, kAttnWaitNs)) {
           atomicExch(a.err, 21);
           ok = false;
@@ -170,7 +177,7 @@ __global__ void __launch_bounds__(kAThreads, 1) tc_attn_kernel(const __grid_cons
         ++qi;
         ptx::mbar_expect_tx(Q_FULL, 2 * q_plane);
         ptx::bulk_g2s(sbase + off_q, a.Qp + ((long long)bh * a.nq + qt) * 2 * (kTQ * D), 2 * q_plane, Q_FULL);
-        for (int kt = 0; kt < a.nk; ++kt, ++kvi) {
+        for (int kt = kt0; kt < kt1; ++kt, ++kvi) {
           if (!ptx::mbar_wait(KV_EMPTY, (kvi & 1) ^ 1, kAttnWaitNs)) {
             atomicExch(a.err, 22);
             ok = false;
@@ -194,13 +201,15 @@ __global__ void __launch_bounds__(kAThreads, 1) tc_attn_kernel(const __grid_cons
       int qi = 0, kvi = 0;
       bool ok = true;
       for (int it = blockIdx.x; it < total_items && ok; it += gridDim.x) {
+        const int sp = it % a.nsplit;
+        const int kt0 = a.nk * sp / a.nsplit, kt1 = a.nk * (sp + 1) / a.nsplit;
         if (!ptx::mbar_wait(Q_FULL, qi & 1, kAttnWaitNs)) {
           atomicExch(a.err, 23);
           ok = false;
           break;
         }
         ++qi;
-        for (int kt = 0; kt < a.nk && ok; ++kt, ++kvi) {
+        for (int kt = kt0; kt < kt1 && ok; ++kt, ++kvi) {
           const uint32_t ph = kvi & 1;
           if (!ptx::mbar_wait(KV_FULL, ph, kAttnWaitNs) || !ptx::mbar_wait(S_EMPTY, ph ^ 1, kAttnWaitNs)) {
             atomicExch(a.err, 24);
@@ -247,7 +256,9 @@ __global__ void __launch_bounds__(kAThreads, 1) tc_attn_kernel(const __grid_cons
     int kvi = 0;
     bool ok = true;
     for (int it = blockIdx.x; it < total_items && ok; it += gridDim.x) {
-      const int bh = it / a.nq, qt = it % a.nq;
+      const int sp = it % a.nsplit, bq = it / a.nsplit;
+      const int bh = bq / a.nq, qt = bq % a.nq;
+      const int kt0 = a.nk * sp / a.nsplit, kt1 = a.nk * (sp + 1) / a.nsplit;
       const int i = qt * kTQ + row;  // query index
       float o[D];
 #pragma unroll
@@ -258,7 +269,7 @@ __global__ void __launch_bounds__(kAThreads, 1) tc_attn_kernel(const __grid_cons
         const float* rr = a.rk + ((long long)bh * a.P + (i < a.P ? i : 0)) * nb;
         for (int r = 0; r < nb; ++r) rk[r] = rr[r];
       }
-      for (int kt = 0; kt < a.nk; ++kt, ++kvi) {
+      for (int kt = kt0; kt < kt1; ++kt, ++kvi) {
         const uint32_t ph = kvi & 1;
         const bool got = __all_sync(0xffffffffu, ptx::mbar_wait(S_FULL, ph, kAttnWaitNs));
         if (!got) {
@@ -292,7 +303,7 @@ __global__ void __launch_bounds__(kAThreads, 1) tc_attn_kernel(const __grid_cons
         }
         const float m_new = fmaxf(m, tmax);
         // fold the previous tile's O_t (computed with exp(s - m)) into the accumulator
-        if (kt > 0) {
+        if (kt > kt0) {
           const bool pv = __all_sync(0xffffffffu, ptx::mbar_wait(PV_FULL, ph ^ 1, kAttnWaitNs));
           if (!pv) {
             if (lane == 0) atomicExch(a.err, 27);
@@ -386,7 +397,15 @@ __global__ void __launch_bounds__(kAThreads, 1) tc_attn_kernel(const __grid_cons
         ptx::tc_fence_before();
         if (lane == 0) ptx::mbar_arrive(PV_EMPTY);
       }
-      if (i < a.P) {
+      if (i < a.P && a.nsplit > 1) {
+        // partial result of this key range: unnormalised O, row max and sum
+        const long long pr = ((long long)bh * a.nsplit + sp) * a.P + i;
+        float* po = a.po + pr * D;
+#pragma unroll
+        for (int d = 0; d < D; d += 4) *reinterpret_cast<float4*>(po + d) = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
+        a.pml[2 * pr] = m;
+        a.pml[2 * pr + 1] = l;
+      } else if (i < a.P) {
         const int b = bh / a.heads, h = bh % a.heads;
         float* yr = a.y + ((long long)b * a.P + i) * a.y_ld + h * D;
         const float inv_l = 1.f / l;
@@ -414,6 +433,52 @@ __global__ void __launch_bounds__(kAThreads, 1) tc_attn_kernel(const __grid_cons
   __syncthreads();
   ptx::tc_fence_after();
   if (warp == 1) ptx::tmem_dealloc(tmem, 512);
+}
+
+// Merge of the key ranges of one (chunk x head, query row), one warp, lanes
+// over the head dimension: M = max m_s, L = sum exp(m_s - M) l_s, O = sum
+// exp(m_s - M) O_s; then y = O / L plus the band term p(i, i + r - W) emb_v[r]
+// with p from the final M and L, as in the one-range epilogue.
+__global__ void attn_combine_kernel(const float* __restrict__ po, const float* __restrict__ pml, int nsplit, int P,
+                                    int heads, int D, int W, const float* __restrict__ sb,
+                                    const float* __restrict__ emb_v, float* __restrict__ y, int y_ld,
+                                    long long rows) {
+  const long long wr = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (wr >= rows) return;
+  const int i = (int)(wr % P);
+  const int bh = (int)(wr / P);
+  const int b = bh / heads, h = bh % heads;
+  float M = -INFINITY;
+  for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, pml[2 * (((long long)bh * nsplit + sp) * P + i)]);
+  float L = 0.f, o[3] = {0.f, 0.f, 0.f};
+  for (int sp = 0; sp < nsplit; ++sp) {
+    const long long pr = ((long long)bh * nsplit + sp) * P + i;
+    const float ms = pml[2 * pr];
+    const float f = ms == -INFINITY ? 0.f : expf(ms - M);
+    L += f * pml[2 * pr + 1];
+#pragma unroll
+    for (int t = 0; t < 3; ++t) {
+      const int d = lane + 32 * t;
+      if (d < D) o[t] = fmaf(f, po[pr * D + d], o[t]);
+    }
+  }
+  const float inv_l = 1.f / L;
+  float* yr = y + ((long long)b * P + i) * y_ld + h * D;
+  const int nb = 2 * W + 1;
+#pragma unroll
+  for (int t = 0; t < 3; ++t) {
+    const int d = lane + 32 * t;
+    if (d >= D) continue;
+    float v = o[t] * inv_l;
+    if (W >= 0) {
+      const float* sbr = sb + ((long long)bh * P + i) * nb;
+      float band = 0.f;
+      for (int r = 0; r < nb; ++r) band = fmaf(expf(sbr[r] - M) * inv_l, emb_v[(long long)r * D + d], band);
+      v = v + band;
+    }
+    yr[d] = v;
+  }
 }
 
 // One warp per (chunk x head, query row): rk[r] = qs . emb_k[r] (added to the
@@ -511,13 +576,33 @@ bool k_attention_tc(Context* ctx, const float* qkv, int ld, int q_off, int k_off
     RVC_CUDA_TRY(cudaFuncSetAttribute(tc_attn_kernel<96>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
     attr_done.fetch_or(1ull << dev);
   }
-  const int items = BH * nq;
+  // few (query tile) items for the SMs (one short sequence, few heads): split
+  // the keys so about one item per SM runs, then merge the ranges
+  const int sms = ctx->num_sms();
+  int nsplit = 1;
+  if (BH * nq < sms) nsplit = std::min(nk, (sms + BH * nq - 1) / (BH * nq));
+  a.nsplit = nsplit;
+  DevBuf po, pml;
+  if (nsplit > 1) {
+    po = DevBuf(ctx, sizeof(float) * (size_t)BH * nsplit * P * D);
+    pml = DevBuf(ctx, sizeof(float) * (size_t)BH * nsplit * P * 2);
+  }
+  a.po = po.p ? po.f() : nullptr;
+  a.pml = pml.p ? pml.f() : nullptr;
+  const int items = BH * nq * nsplit;
   if (D == 64)
-    tc_attn_kernel<64><<<std::min(items, 148), kAThreads, smem, st>>>(a);
+    tc_attn_kernel<64><<<std::min(items, sms), kAThreads, smem, st>>>(a);
   else
-    tc_attn_kernel<96><<<std::min(items, 148), kAThreads, smem, st>>>(a);
+    tc_attn_kernel<96><<<std::min(items, sms), kAThreads, smem, st>>>(a);
   note_launch();
   RVC_CUDA_TRY(cudaGetLastError());
+  if (nsplit > 1) {
+    const long long rows = (long long)BH * P;
+    attn_combine_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(po.f(), pml.f(), nsplit, P, heads, D, window,
+                                                                     sb.p ? sb.f() : nullptr, emb_v, y, y_ld, rows);
+    note_launch();
+    RVC_CUDA_TRY(cudaGetLastError());
+  }
   return true;  // the packed tiles are released to the stream-ordered cache: later work queues behind this kernel
 }
 

@@ -155,7 +155,9 @@ def test_partial_equals_slice_of_full_interior():
 def test_prep_dec_decode_batch_ragged_and_partial():
     """The pipeline's batched decode (prep_dec + decode_batch): equal-length
     chunks share a call, other lengths and partial preps run on their own; each
-    result equals the single-chunk path with the same noise."""
+    result equals the single-chunk path with the same noise up to fp32
+    rounding (the kernel plans follow the batch: column-tile widths and
+    attention key splits differ between a batch of two and one chunk)."""
     w, m = model(40000, 0)
     ins = [syn.make_vits_inputs(P, 30 + i) for i, P in enumerate((48, 48, 33))]
     preps = [m.prep_dec(*x, seed=100 + i) for i, x in enumerate(ins)]
@@ -164,7 +166,7 @@ def test_prep_dec_decode_batch_ragged_and_partial():
     assert [wv.shape[-1] for wv in waves] == [48 * m.upp, 48 * m.upp, 33 * m.upp, 12 * m.upp]
     for x, p, wv in zip(ins, preps[:3], waves[:3]):
         ref = m.infer_controlled(x[0], x[1], x[2], x[3], p["nz"], p["ns"])
-        assert np.abs(wv - ref).max() <= 1e-6
+        assert np.abs(wv - ref).max() <= 1e-4
     pp = preps[3]
     ref = m.infer_partial(*ins[2], pp["nz"], pp["ns"], 10, 12)
-    assert np.abs(waves[3] - ref).max() <= 1e-6
+    assert np.abs(waves[3] - ref).max() <= 1e-4
