@@ -65,6 +65,14 @@ int32_t rvc_cuda_h2d(int64_t ctx, void* dst, const void* src, int64_t bytes);
 int32_t rvc_cuda_d2h(int64_t ctx, void* dst, const void* src, int64_t bytes);
 /* Device-to-device copy, asynchronous on the context's stream. */
 int32_t rvc_cuda_d2d(int64_t ctx, void* dst, const void* src, int64_t bytes);
+/* Host-to-device copy enqueued on the context's stream without waiting for it
+ * (rvc_cuda_h2d waits for the stream).  From page-locked memory
+ * (rvc_cuda_host_alloc) the copy runs in stream order after the call returns,
+ * so the source must stay unchanged until the next rvc_cuda_sync / rvc_cuda_d2h. */
+int32_t rvc_cuda_h2d_async(int64_t ctx, void* dst, const void* src, int64_t bytes);
+/* Page-locked host memory (cudaHostAlloc, portable) for rvc_cuda_h2d_async. */
+int32_t rvc_cuda_host_alloc(int64_t bytes, void** ptr);
+int32_t rvc_cuda_host_free(void* ptr);
 /* Per-kernel timing of the tensor-core convolutions: enable, then read the
  * accumulated launch count, device milliseconds and algorithmic FLOPs. */
 int32_t rvc_cuda_profile(int64_t ctx, int32_t enable);

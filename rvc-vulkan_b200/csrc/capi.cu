@@ -290,6 +290,27 @@ int32_t rvc_cuda_d2d(int64_t ctx, void* dst, const void* src, int64_t bytes) {
   });
 }
 
+int32_t rvc_cuda_h2d_async(int64_t ctx, void* dst, const void* src, int64_t bytes) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(dst && src && bytes >= 0, "h2d_async: bad arguments");
+    h2d(c, dst, src, (size_t)bytes);
+  });
+}
+
+int32_t rvc_cuda_host_alloc(int64_t bytes, void** ptr) {
+  return guarded([&] {
+    RVC_CHECK_ARG(ptr && bytes > 0, "host_alloc: bad arguments");
+    *ptr = nullptr;
+    RVC_CUDA_TRY(cudaHostAlloc(ptr, (size_t)bytes, cudaHostAllocPortable));
+  });
+}
+
+int32_t rvc_cuda_host_free(void* ptr) {
+  return guarded([&] {
+    if (ptr) RVC_CUDA_TRY(cudaFreeHost(ptr));
+  });
+}
+
 int32_t rvc_cuda_profile(int64_t ctx, int32_t enable) {
   return on_ctx(ctx, [&](Context* c) {
     c->prof_collect();

@@ -66,7 +66,33 @@ __global__ void iir_warm_kernel(const IirCoef f, const double* __restrict__ x, l
 #pragma unroll
     for (int i = 0; i < N - 1; ++i) z[i] = __dmul_rn(f.zi[i], x0);
   }
+  // 8 samples per step through 16-byte loads / stores (t is a multiple of 8
+  // here: L and warm are), the recursion itself unchanged
+  for (; t + 8 <= s; t += 8) {
+    double xv[8];
+#pragma unroll
+    for (int k = 0; k < 8; k += 2) {
+      const double2 v = *reinterpret_cast<const double2*>(x + t + k);
+      xv[k] = v.x;
+      xv[k + 1] = v.y;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) df2t<N>(f, xv[k], z);
+  }
   for (; t < s; ++t) df2t<N>(f, x[t], z);
+  for (; t + 8 <= e; t += 8) {
+    double xv[8], yv[8];
+#pragma unroll
+    for (int k = 0; k < 8; k += 2) {
+      const double2 v = *reinterpret_cast<const double2*>(x + t + k);
+      xv[k] = v.x;
+      xv[k + 1] = v.y;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) yv[k] = df2t<N>(f, xv[k], z);
+#pragma unroll
+    for (int k = 0; k < 8; k += 2) *reinterpret_cast<double2*>(y + t + k) = make_double2(yv[k], yv[k + 1]);
+  }
   for (; t < e; ++t) y[t] = df2t<N>(f, x[t], z);
 }
 
@@ -431,11 +457,12 @@ static void iir_run(Context* ctx, const IirPlan& p, const double* x, long long n
                     double* y) {
   const long long L = p.warm < 0 ? n : kIirBlock, warm = p.warm < 0 ? 0 : p.warm;
   const long long threads = (n + L - 1) / L;
-  const unsigned grid = (unsigned)((threads + 127) / 128);
+  // one warp per block: the sequential threads spread over as many SMs as possible
+  const unsigned grid = (unsigned)((threads + 31) / 32);
   cudaStream_t st = ctx->stream;
   switch (p.f.n) {
 #define RVC_IIR_CASE(N) \
-  case N: iir_warm_kernel<N><<<grid, 128, 0, st>>>(p.f, x, n, scale_src, L, warm, y); break;
+  case N: iir_warm_kernel<N><<<grid, 32, 0, st>>>(p.f, x, n, scale_src, L, warm, y); break;
     RVC_IIR_CASE(2) RVC_IIR_CASE(3) RVC_IIR_CASE(4) RVC_IIR_CASE(5) RVC_IIR_CASE(6) RVC_IIR_CASE(7) RVC_IIR_CASE(8)
 #undef RVC_IIR_CASE
     default: RVC_CHECK_ARG(false, "filtfilt: filters of 2..8 taps supported");

@@ -16,7 +16,7 @@ import threading
 
 import numpy as np
 
-__all__ = ["lib", "check", "Context", "get_context", "device_count", "RvcCudaError"]
+__all__ = ["lib", "check", "Context", "get_context", "device_count", "RvcCudaError", "PinnedBuffer"]
 
 RVC_E_ARG = -1
 RVC_E_TIMEOUT = -3
@@ -126,6 +126,9 @@ _SIGS = {
     "rvc_cuda_to_int16_device": ([_i64, _p, _i64, _p], _i32),
     "rvc_cuda_index_ivf_blend_device": ([_i64, _p, _i64, _i32, _i32, _i32, _f64, _p, _p], _i32),
     "rvc_cuda_d2d": ([_i64, _p, _p, _i64], _i32),
+    "rvc_cuda_h2d_async": ([_i64, _p, _p, _i64], _i32),
+    "rvc_cuda_host_alloc": ([_i64, C.POINTER(_p)], _i32),
+    "rvc_cuda_host_free": ([_p], _i32),
     "rvc_cuda_resample": ([_i64, _p, _i32, _i64, _i32, _i32, _i32, _fp, _i64], _i32),
     "rvc_cuda_f0_autocorr": ([_i64, _p, _i64, _i32, _i32, _i32, _i32, _i32, _p, _f64, _fp, _i64], _i32),
     "rvc_cuda_index_create": ([_i64, _fp, _i64, _i32, _i32, C.POINTER(_i64)], _i32),
@@ -223,6 +226,14 @@ class Context:
     def d2h(self, arr: np.ndarray, dptr: int):
         check(lib.rvc_cuda_d2h(self.handle, arr.ctypes.data_as(_p), _p(dptr), arr.nbytes))
 
+    def h2d_async(self, dptr: int, arr: np.ndarray):
+        """Host-to-device copy enqueued without waiting for the stream.  ``arr``
+        (page-locked, from ``PinnedBuffer``, for a copy that overlaps) must stay
+        unchanged and alive until the next ``sync`` / ``d2h`` of this context."""
+        if not (arr.flags.c_contiguous):
+            raise ValueError("h2d_async needs a contiguous source")
+        check(lib.rvc_cuda_h2d_async(self.handle, _p(dptr), arr.ctypes.data_as(_p), arr.nbytes))
+
     def d2d(self, dst: int, src: int, nbytes: int):
         """Device-to-device copy, asynchronous on this context's stream."""
         check(lib.rvc_cuda_d2d(self.handle, _p(dst), _p(src), int(nbytes)))
@@ -263,3 +274,32 @@ def get_context(device: int | None = None) -> Context:
             c = Context(device)
             _contexts[device] = c
         return c
+
+
+class PinnedBuffer:
+    """Page-locked host memory (``rvc_cuda_host_alloc``) with numpy views."""
+
+    def __init__(self, nbytes: int):
+        p = _p()
+        check(lib.rvc_cuda_host_alloc(int(max(16, nbytes)), C.byref(p)))
+        self.ptr = int(p.value)
+        self.nbytes = int(max(16, nbytes))
+
+    def view(self, dtype, count: int, offset: int = 0) -> np.ndarray:
+        """``count`` elements of ``dtype`` starting ``offset`` bytes in."""
+        dt = np.dtype(dtype)
+        if offset < 0 or offset + count * dt.itemsize > self.nbytes:
+            raise ValueError("pinned view out of range")
+        buf = (C.c_char * (count * dt.itemsize)).from_address(self.ptr + offset)
+        return np.frombuffer(buf, dtype=dt, count=count)
+
+    def close(self):
+        if getattr(self, "ptr", 0):
+            lib.rvc_cuda_host_free(_p(self.ptr))
+            self.ptr = 0
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001
+            pass

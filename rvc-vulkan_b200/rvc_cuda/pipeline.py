@@ -350,21 +350,44 @@ class Pipeline:
             bufs.append(p)
             return p
 
+        def al(n):
+            return (int(n) + 255) // 256 * 256
+
         try:
-            plan, n_out = [], 0
+            plan, n_out, need = [], 0, 0
             for (idx, s0, e0, blk) in blocks:
                 L = int(model.out_frames(blk.shape[0]))
                 P = 2 * L
                 keep = max(0, P * upp - 2 * self.t_pad_tgt)
                 plan.append([blk, L, P, keep, 0, 0])
                 n_out += keep
+                need += al(4 * blk.shape[0]) + al(4 * P) + al(8 * P) + al(8)
+            mix = rms_mix_rate != 1 and n_out > 0
+            if mix:
+                need += al(4 * np.asarray(audio).size)
+            # uploads go through a page-locked staging buffer and are enqueued
+            # without waiting for the stream (the final download waits for all)
+            stage_buf, stage_off = self._pinned("stage", need), [0]
+
+            def up(dptr, arr, dtype):
+                a = np.ascontiguousarray(arr, dtype=dtype).reshape(-1)
+                v = stage_buf.view(dtype, a.size, stage_off[0])
+                v[...] = a
+                stage_off[0] += al(a.nbytes)
+                ctx.h2d_async(dptr, v)
+
             d_out = alloc(4 * n_out)
+            d_a = 0
+            if mix:                                                        # change_rms input, up early
+                n_a = np.asarray(audio).size
+                d_a = alloc(4 * n_a)
+                up(d_a, audio, np.float32)
             for item in plan:                                              # phase A
                 blk, L, P = item[0], item[1], item[2]
                 t0 = time.perf_counter()
                 T = blk.shape[0]
                 d_x = alloc(4 * T)
-                ctx.h2d(d_x, blk)
+                up(d_x, blk, np.float32)
                 d_f = alloc(4 * L * D)
                 model.encode_device(d_x, 1, T, version, d_f)
                 d_m = d_f
@@ -387,7 +410,7 @@ class Pipeline:
                 t1 = time.perf_counter()
                 pitch, pitchf = _align(p, P), _align(pf, P)                # :582-603
                 d_pf = alloc(4 * P)
-                ctx.h2d(d_pf, np.ascontiguousarray(pitchf[0], dtype=np.float32))
+                up(d_pf, pitchf[0], np.float32)
                 if protect < 0.5:                                          # :594-608
                     dsp.protect_device(ctx, d_ph, d_f0, d_pf, P, D, protect, d_ph)
                 if noise is not None and noise[done - 1][0] == P:
@@ -396,10 +419,14 @@ class Pipeline:
                     nz, ns = net_g.make_noise(P)
                 d_p, d_sid = alloc(8 * P), alloc(8)
                 d_nz, d_ns, d_w = alloc(4 * H * P), alloc(4 * P * upp), alloc(4 * P * upp)
-                ctx.h2d(d_p, np.ascontiguousarray(pitch[0], dtype=np.int64))
-                ctx.h2d(d_sid, np.asarray([sid], dtype=np.int64))
-                ctx.h2d(d_nz, np.ascontiguousarray(nz, dtype=np.float32))
-                ctx.h2d(d_ns, np.ascontiguousarray(ns, dtype=np.float32))
+                up(d_p, pitch[0], np.int64)
+                up(d_sid, [sid], np.int64)
+                for d, z in ((d_nz, nz), (d_ns, ns)):
+                    z = np.asarray(z)
+                    if z.dtype == np.float32 and z.flags.c_contiguous:
+                        ctx.h2d_async(d, z)  # page-locked noise from the prefetch, or staged by the driver
+                    else:
+                        ctx.h2d(d, np.ascontiguousarray(z, dtype=np.float32))
                 net_g.infer_device(1, P, d_ph, d_p, d_pf, d_sid, d_nz, d_ns, d_w)
                 if keep:                                                   # [t_pad_tgt : -t_pad_tgt]
                     ctx.d2d(d_out + 4 * off, d_w + 4 * self.t_pad_tgt, 4 * keep)
@@ -407,11 +434,8 @@ class Pipeline:
                 times[2] += time.perf_counter() - t1
                 if progress_cb is not None:
                     progress_cb(done, total, "chunk %d/%d" % (done, total))
-            if rms_mix_rate != 1 and n_out:
-                a32 = np.ascontiguousarray(audio, dtype=np.float32)
-                d_a = alloc(4 * a32.size)
-                ctx.h2d(d_a, a32)
-                dsp.change_rms_device(ctx, d_a, a32.size, 16000, d_out, n_out, tgt_sr, rms_mix_rate, d_out)
+            if mix:
+                dsp.change_rms_device(ctx, d_a, n_a, 16000, d_out, n_out, tgt_sr, rms_mix_rate, d_out)
             if tgt_sr != resample_sr >= 16000:
                 host = np.empty(n_out, np.float32)
                 if n_out:
@@ -440,24 +464,47 @@ class Pipeline:
                     for f in model.encode_batch([a[None, :] for a in audios], version=version)]
         return [np.asarray(model.encode(a[None, :], version=version), dtype=np.float32) for a in audios]
 
-    @staticmethod
-    def _prefetch_noise(model, net_g, chunk_lengths):
-        """Draw every chunk's synthesizer noise on a host thread while the
-        device runs f0 and HuBERT (``RandomState`` fills release the GIL).
-        Needs the frame count before encoding: ``model.out_frames(T)``
-        (``CudaHubert``) and ``net_g.make_noise`` (``CudaSynthesizer``)."""
+    def _pinned(self, name, nbytes):
+        """A page-locked host buffer of at least ``nbytes``, kept for reuse
+        across calls (a call's asynchronous uploads from it end with the
+        call's final device-to-host copy)."""
+        from ._lib import PinnedBuffer  # noqa: PLC0415
+        cache = self.__dict__.setdefault("_pin", {})
+        buf = cache.get(name)
+        if buf is None or buf.nbytes < nbytes:
+            if buf is not None:
+                buf.close()
+            buf = cache[name] = PinnedBuffer(int(nbytes * 1.25) + 4096)
+        return buf
+
+    def _prefetch_noise(self, model, net_g, chunk_lengths):
+        """Draw every chunk's synthesizer noise on host threads while the
+        device runs f0 and HuBERT (``RandomState`` fills release the GIL),
+        into page-locked buffers when the synthesizer is this library's, so
+        the uploads overlap device work.  Needs the frame count before
+        encoding: ``model.out_frames(T)`` (``CudaHubert``) and
+        ``net_g.make_noise`` (``CudaSynthesizer``)."""
         if not (hasattr(net_g, "make_noise") and hasattr(net_g, "prep_dec") and hasattr(net_g, "decode_batch")
                 and hasattr(model, "out_frames")) or not chunk_lengths:
             return None
         from concurrent.futures import ThreadPoolExecutor  # noqa: PLC0415
+
+        from .synth import CudaSynthesizer  # noqa: PLC0415
+        pin = isinstance(net_g, CudaSynthesizer)
         # each chunk draws from its own RandomState(seed), so the chunks are
         # independent: one thread per chunk (up to the host's cores)
         workers = max(1, min(len(chunk_lengths), os.cpu_count() or 1, 8))
         ex = ThreadPoolExecutor(max_workers=workers, thread_name_prefix="rvc-noise")
         jobs = []
-        for n in chunk_lengths:
+        for i, n in enumerate(chunk_lengths):
             P = 2 * int(model.out_frames(n))
-            jobs.append((P, ex.submit(net_g.make_noise, P)))
+            if pin:
+                nh, nn = net_g.hidden * P, P * net_g.upp
+                buf = self._pinned(f"noise{i}", 4 * (nh + nn))
+                out = (buf.view(np.float32, nh, 0), buf.view(np.float32, nn, 4 * nh))
+                jobs.append((P, ex.submit(net_g.make_noise, P, None, out)))
+            else:
+                jobs.append((P, ex.submit(net_g.make_noise, P)))
         ex.shutdown(wait=False)
         return jobs
 

@@ -120,16 +120,24 @@ class CudaSynthesizer:
             pass
 
     # ---------------------------------------------------------------- noise
-    def make_noise(self, P: int, seed=None):
+    def make_noise(self, P: int, seed=None, out=None):
         """``nz [1,h,P]`` then ``ns [1,P*upp,1]`` in the order of
         ``SynthesizerTrn._make_noise`` (``runtime/models/vits.py:2337-2350``),
-        honouring ``RVC_FIXED_SEED``."""
+        honouring ``RVC_FIXED_SEED``.  ``out``: two float32 arrays of
+        ``h*P`` and ``P*upp`` elements (e.g. page-locked views) the draws are
+        cast into; they are returned reshaped."""
         fixed = os.environ.get("RVC_FIXED_SEED", "").strip()
         if seed is None and fixed:
             seed = int(fixed)
         rng = np.random.RandomState(seed) if seed is not None else np.random.RandomState()
-        nz = rng.standard_normal((1, self.hidden, P)).astype(np.float32)
-        ns = rng.standard_normal((1, P * self.upp, 1)).astype(np.float32)
+        if out is None:
+            nz = rng.standard_normal((1, self.hidden, P)).astype(np.float32)
+            ns = rng.standard_normal((1, P * self.upp, 1)).astype(np.float32)
+            return nz, ns
+        nz = out[0].reshape(1, self.hidden, P)
+        ns = out[1].reshape(1, P * self.upp, 1)
+        np.copyto(nz, rng.standard_normal((1, self.hidden, P)), casting="same_kind")
+        np.copyto(ns, rng.standard_normal((1, P * self.upp, 1)), casting="same_kind")
         return nz, ns
 
     # ---------------------------------------------------------------- infer
