@@ -576,11 +576,24 @@ bool k_attention_tc(Context* ctx, const float* qkv, int ld, int q_off, int k_off
     RVC_CUDA_TRY(cudaFuncSetAttribute(tc_attn_kernel<96>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
     attr_done.fetch_or(1ull << dev);
   }
-  // few (query tile) items for the SMs (one short sequence, few heads): split
-  // the keys so about one item per SM runs, then merge the ranges
+  // Split the keys when the (query tile) items fill the SMs' waves poorly (one
+  // sequence, few heads): the split count maximises items / (waves x SMs),
+  // at least 2 key tiles per split and a charge of 0.05 per extra split for the
+  // partial results and the merge.
   const int sms = ctx->num_sms();
   int nsplit = 1;
-  if (BH * nq < sms) nsplit = std::min(nk, (sms + BH * nq - 1) / (BH * nq));
+  {
+    const long long base = (long long)BH * nq;
+    double best = -1.0;
+    for (int ns = 1; ns <= std::max(1, nk / 2); ++ns) {
+      const long long it = base * ns, waves = (it + sms - 1) / sms;
+      const double score = (double)it / (double)(waves * sms) - 0.05 * (ns - 1);
+      if (score > best + 1e-9) {
+        best = score;
+        nsplit = ns;
+      }
+    }
+  }
   a.nsplit = nsplit;
   DevBuf po, pml;
   if (nsplit > 1) {
