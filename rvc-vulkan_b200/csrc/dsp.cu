@@ -66,34 +66,38 @@ __global__ void iir_warm_kernel(const IirCoef f, const double* __restrict__ x, l
 #pragma unroll
     for (int i = 0; i < N - 1; ++i) z[i] = __dmul_rn(f.zi[i], x0);
   }
-  // 8 samples per step through 16-byte loads / stores (t is a multiple of 8
-  // here: L and warm are), the recursion itself unchanged
-  for (; t + 8 <= s; t += 8) {
-    double xv[8];
+  // 16-sample chunks through 16-byte loads / stores, the next chunk loaded
+  // while this one runs (each thread streams its own segment, so the loads
+  // would otherwise stall the recursion); the recursion itself unchanged.
+  // t and s are multiples of 16 here (L and warm are), so a chunk lies wholly
+  // in the warm-up or wholly in the output range.
+  const long long e16 = t + (e - t) / 16 * 16;
+  double cur[16], nxt[16];
+  auto load16 = [&](long long tt, double (&v)[16]) {
 #pragma unroll
-    for (int k = 0; k < 8; k += 2) {
-      const double2 v = *reinterpret_cast<const double2*>(x + t + k);
-      xv[k] = v.x;
-      xv[k + 1] = v.y;
+    for (int k = 0; k < 16; k += 2) {
+      const double2 w = *reinterpret_cast<const double2*>(x + tt + k);
+      v[k] = w.x;
+      v[k + 1] = w.y;
+    }
+  };
+  if (t < e16) load16(t, cur);
+  for (; t < e16; t += 16) {
+    if (t + 16 < e16) load16(t + 16, nxt);
+    double yv[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) yv[k] = df2t<N>(f, cur[k], z);
+    if (t >= s) {
+#pragma unroll
+      for (int k = 0; k < 16; k += 2) *reinterpret_cast<double2*>(y + t + k) = make_double2(yv[k], yv[k + 1]);
     }
 #pragma unroll
-    for (int k = 0; k < 8; ++k) df2t<N>(f, xv[k], z);
+    for (int k = 0; k < 16; ++k) cur[k] = nxt[k];
   }
-  for (; t < s; ++t) df2t<N>(f, x[t], z);
-  for (; t + 8 <= e; t += 8) {
-    double xv[8], yv[8];
-#pragma unroll
-    for (int k = 0; k < 8; k += 2) {
-      const double2 v = *reinterpret_cast<const double2*>(x + t + k);
-      xv[k] = v.x;
-      xv[k + 1] = v.y;
-    }
-#pragma unroll
-    for (int k = 0; k < 8; ++k) yv[k] = df2t<N>(f, xv[k], z);
-#pragma unroll
-    for (int k = 0; k < 8; k += 2) *reinterpret_cast<double2*>(y + t + k) = make_double2(yv[k], yv[k + 1]);
+  for (; t < e; ++t) {
+    const double yy = df2t<N>(f, x[t], z);
+    if (t >= s) y[t] = yy;
   }
-  for (; t < e; ++t) y[t] = df2t<N>(f, x[t], z);
 }
 
 // odd extension: [2 x0 - x[pl..1], x, 2 x_last - x[n-2 .. n-1-pl]]; for a
