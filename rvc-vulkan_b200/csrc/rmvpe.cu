@@ -9,13 +9,15 @@
 // Layout: channels-last images [B][H = frames][W = mel bins][C], fp32.  The
 // argmax over 360 salience bins must reproduce the reference's, so the whole
 // network runs in fp32 on the CUDA cores (no reduced-precision tensor-core
-// split): every conv is an fp32 implicit GEMM (64 pixels x 64 channels per
-// block, split over K when a layer has few pixels), BatchNorm + ReLU +
-// residual in its epilogue, in the reference's operation order.  The STFT is
-// a float64 DFT (the reference transforms in float64).  The BiGRU runs as one
-// 8-CTA thread-block cluster per direction: each CTA keeps 96 rows of the
-// recurrent matrix in shared memory and broadcasts its 32 new hidden units to
-// the other CTAs' shared memory every step.
+// split): 3x3 convs in a direct kernel over shared-memory halo tiles (row
+// segments in registers, cp.async double buffering, channel-block splits for
+// small grids), the stride-2 transposed convs split by output parity, 1x1
+// convs and linears as an fp32 implicit GEMM; BatchNorm + ReLU + residual in
+// every epilogue, in the reference's operation order.  The STFT is a batched
+// cuFFT D2Z in float64 (the reference transforms in float64).  The BiGRU runs
+// as one 8-CTA thread-block cluster per (direction, pair of clips): each CTA
+// keeps 96 rows of the recurrent matrix in registers and broadcasts its 32 new
+// hidden units to the other CTAs' shared memory every step.
 #include "rmvpe.cuh"
 
 #include <cooperative_groups.h>
@@ -967,9 +969,8 @@ void RmvpeModel::finalize() {
     RVC_CUDA_TRY(cudaStreamSynchronize(st));  // t4 is freed on return
     convs_["fc"] = std::move(fc);
   }
-  // front-end tables: HTK mel filters (rows normalised to sum 1), numpy's
-  // symmetric Hann window, DFT twiddles (runtime/dsp/mel.py:97-122,
-  // runtime/dsp/fft.py:16-56)
+  // front-end tables: HTK mel filters (rows normalised to sum 1) and numpy's
+  // symmetric Hann window (runtime/dsp/mel.py:97-122, runtime/dsp/fft.py:16-56)
   {
     const int nb = kBins;
     std::vector<double> fftf(nb);
