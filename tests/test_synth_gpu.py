@@ -105,6 +105,23 @@ def test_synth_long_chunk_properties():
     assert 0.05 < a.std() < 0.8
 
 
+def test_enc_p_long_sequence_key_split():
+    """The text encoder on one 10 s chunk (P = 1000: 8 query tiles x 2 heads,
+    so the tensor-core attention splits the keys and merges the ranges)
+    against the oracle's text encoder, layer by layer."""
+    w, m = model(40000, 0)
+    P = 1000
+    phone, pitch, nsff0, sid = syn.make_vits_inputs(P, 9)
+    nz, ns = syn.make_vits_noise(P, m.upp, 99)
+    m.keep_taps(True)
+    m.infer_controlled(phone, pitch, nsff0, sid, nz, ns)
+    taps = {}
+    OV.text_encoder(w, OV.VitsShape(w, syn.vits_config_array(40000)), phone, pitch, taps)
+    for k in ("enc.embed", "enc.l0", "enc.l3", "enc.l5"):
+        err = rel_l2(m.tap(k, (P, m.hidden)), taps[k])
+        assert err <= LAYER_TOL, (k, err)
+
+
 def test_seeded_infer_matches_infer_controlled():
     w, m = model(40000, 0)
     phone, pitch, nsff0, sid = syn.make_vits_inputs(16, 3)
