@@ -105,6 +105,36 @@ def test_pipeline_orchestration_matches_reference(name, kw, gold, golden_meta, m
         np.testing.assert_array_equal(out[::101], gold[name + "_int16_every101"])
 
 
+def test_pipeline_concurrent_f0_segments_match_reference(gold, golden_meta, monkeypatch):
+    """With an f0 model offering ``infer_many`` (the device RMVPE's concurrent
+    segments) the pipeline's segment slicing and f0 post-processing still give
+    the reference's split points and int16 output, bit for bit."""
+    from rvc_cuda import pipeline as P
+    name, kw = next(c for c in PIPE_CASES if c[0] == "pipe_split")
+    monkeypatch.setattr(P, "dsp", _oracle_dsp())
+    m = golden_meta["dsp"]["cases"][name]
+    a = syn.make_speech_audio(kw["seconds"], seed=kw["seed"], silence_every=kw["silence_every"])
+
+    class ManyRmvpe(pf.FakeRmvpe):
+        calls = []
+
+        def infer_many(self, xs, thred=0.03):
+            self.calls.append(len(xs))
+            return [self.infer_from_audio(x, thred) for x in xs]
+
+    pipe = P.Pipeline(40000, pf.config(x_query=kw["x_query"]))
+    pipe.model_rmvpe = ManyRmvpe()
+    sr, out = pipe.pipeline(pf.FakeHubert(D=768), pf.FakeSynth(gain=kw["gain"]), 0, a, [0.0, 0.0, 0.0],
+                            kw["f0_up_key"], "rmvpe", None, 0, True, 40000, 0, kw["rms"], 2, kw["protect"],
+                            slice_length=kw["slice_length"])
+    assert ManyRmvpe.calls and ManyRmvpe.calls[0] > 1
+    assert out.size == m["out_len"]
+    if name + "_int16" in gold:
+        np.testing.assert_array_equal(out, gold[name + "_int16"])
+    else:
+        np.testing.assert_array_equal(out[::101], gold[name + "_int16_every101"])
+
+
 def _pm_audio(golden_meta):
     m = golden_meta["dsp"]["cases"]["pm"]
     a = syn.make_speech_audio(m["seconds"], seed=m["seed"], silence_every=0.6, silence_len=0.2)
