@@ -402,51 +402,72 @@ void k_wn_update(float* h, float* skip, const float* rs, long long rows, int H, 
 
 // k_sine_source, k_conv_post_tanh live in dec_kernels.cu.
 
-// NSF noise conv (runtime/models/vits.py:1616-1636 noise_convs): a tile of 32
-// output rows x 64 channels per CTA, the source window and the weights staged
-// in shared memory (weights transposed to [k][co] for conflict-free reads).
-constexpr int kNzRows = 32, kNzCols = 64, kNzMaxK = 128;
+// NSF noise conv (runtime/models/vits.py:1616-1636 noise_convs): a tile of
+// ROWS output rows x COLS channels per CTA (COLS = 32 for 32-channel stages so
+// no thread idles, else 64), each thread 4 consecutive rows x 4 channels with
+// one 16-byte store per row; the source window and the weights staged in
+// shared memory (weights transposed to [k][co] for conflict-free reads).  Per
+// output: sum over k in order, then the bias.
+constexpr int kNzMaxK = 128, kNzRpt = 4;
+template <int COLS>
 __global__ void __launch_bounds__(256) noise_conv_kernel(const float* __restrict__ har, long long har_bs, int har_len,
                                                          const float* __restrict__ w, const float* __restrict__ bias,
                                                          int C, int nk, int str, int pad, int T_out,
                                                          float* __restrict__ y, long long y_bs) {
+  constexpr int TX = COLS / 4, TY = 256 / TX, ROWS = TY * kNzRpt;
   extern __shared__ float sm[];
-  const int span = (kNzRows - 1) * str + nk;
-  float* hs = sm;                       // [span]
-  float* ws = sm + ((span + 3) & ~3);   // [nk][kNzCols], 16-byte aligned for float4 reads
+  const int span = (ROWS - 1) * str + nk;
+  float* hs = sm;                      // [span]
+  float* ws = sm + ((span + 3) & ~3);  // [nk][COLS], 16-byte aligned for float4 reads
   const int b = blockIdx.z;
-  const int t0 = blockIdx.x * kNzRows, c0 = blockIdx.y * kNzCols;
+  const int t0 = blockIdx.x * ROWS, c0 = blockIdx.y * COLS;
   const float* hb = har + (long long)b * har_bs;
   const int base = t0 * str - pad;
   for (int i = threadIdx.x; i < span; i += blockDim.x) {
-    int idx = base + i;
+    const int idx = base + i;
     hs[i] = (idx >= 0 && idx < har_len) ? hb[idx] : 0.f;
   }
-  for (int i = threadIdx.x; i < nk * kNzCols; i += blockDim.x) {
-    int k = i / kNzCols, c = i % kNzCols;
+  for (int i = threadIdx.x; i < nk * COLS; i += blockDim.x) {
+    const int k = i / COLS, c = i % COLS;
     ws[i] = (c0 + c < C) ? w[(long long)(c0 + c) * nk + k] : 0.f;
   }
   __syncthreads();
-  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // 2 rows x 4 cols per thread
-  float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  const int tx = threadIdx.x % TX, ty = threadIdx.x / TX;
+  float acc[kNzRpt][4];
+#pragma unroll
+  for (int r = 0; r < kNzRpt; ++r)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[r][j] = 0.f;
   for (int k = 0; k < nk; ++k) {
-    const float h0 = hs[(ty * 2) * str + k], h1 = hs[(ty * 2 + 1) * str + k];
-    const float4 wv = *reinterpret_cast<const float4*>(ws + k * kNzCols + tx * 4);
+    const float4 wv = *reinterpret_cast<const float4*>(ws + k * COLS + tx * 4);
     const float wa[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      acc[0][j] = fmaf(h0, wa[j], acc[0][j]);
-      acc[1][j] = fmaf(h1, wa[j], acc[1][j]);
+    for (int r = 0; r < kNzRpt; ++r) {
+      const float h = hs[(ty * kNzRpt + r) * str + k];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[r][j] = fmaf(h, wa[j], acc[r][j]);
     }
   }
+  const int c = c0 + tx * 4;
+  float bv[4] = {0.f, 0.f, 0.f, 0.f};
+  if (bias) {
 #pragma unroll
-  for (int i = 0; i < 2; ++i) {
-    const int t = t0 + ty * 2 + i;
+    for (int j = 0; j < 4; ++j) bv[j] = c + j < C ? bias[c + j] : 0.f;
+  }
+#pragma unroll
+  for (int r = 0; r < kNzRpt; ++r) {
+    const int t = t0 + ty * kNzRpt + r;
     if (t >= T_out) continue;
+    float* yr = y + (long long)b * y_bs + (long long)t * C;
+    float o[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int c = c0 + tx * 4 + j;
-      if (c < C) y[(long long)b * y_bs + (long long)t * C + c] = bias ? acc[i][j] + bias[c] : acc[i][j];
+    for (int j = 0; j < 4; ++j) o[j] = bias ? acc[r][j] + bv[j] : acc[r][j];
+    if (c + 3 < C && (C & 3) == 0) {
+      *reinterpret_cast<float4*>(yr + c) = make_float4(o[0], o[1], o[2], o[3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (c + j < C) yr[c + j] = o[j];
     }
   }
 }
@@ -454,18 +475,25 @@ void k_noise_conv(const float* har, long long har_bs, int har_len, const float* 
                   int str, int pad, int B, int T_out, float* y, long long y_bs, cudaStream_t st) {
   if (B * T_out == 0) return;
   RVC_CHECK_ARG(nk <= kNzMaxK * 4, "noise_conv: kernel too long");
-  const int span = (kNzRows - 1) * str + nk;
-  size_t smem = sizeof(float) * ((size_t)((span + 3) & ~3) + (size_t)nk * kNzCols);
+  const bool narrow = C <= 32;
+  const int cols = narrow ? 32 : 64, rows = (256 / (cols / 4)) * kNzRpt;
+  const int span = (rows - 1) * str + nk;
+  size_t smem = sizeof(float) * ((size_t)((span + 3) & ~3) + (size_t)nk * cols);
   RVC_CHECK_ARG(smem <= 200 * 1024, "noise_conv: tile does not fit in shared memory");
+  RVC_CHECK_ARG(((uintptr_t)y & 15) == 0 && y_bs % 4 == 0, "noise_conv: output must be 16-byte aligned");
   static std::atomic<uint64_t> attr_done{0};
   int dev = 0;
   RVC_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 64 && !(attr_done.load() & (1ull << dev))) {
-    RVC_CUDA_TRY(cudaFuncSetAttribute(noise_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    RVC_CUDA_TRY(cudaFuncSetAttribute(noise_conv_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    RVC_CUDA_TRY(cudaFuncSetAttribute(noise_conv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     attr_done.fetch_or(1ull << dev);
   }
-  dim3 g(cdiv(T_out, kNzRows), cdiv(C, kNzCols), B);
-  noise_conv_kernel<<<g, 256, smem, st>>>(har, har_bs, har_len, w, bias, C, nk, str, pad, T_out, y, y_bs);
+  dim3 g(cdiv(T_out, rows), cdiv(C, cols), B);
+  if (narrow)
+    noise_conv_kernel<32><<<g, 256, smem, st>>>(har, har_bs, har_len, w, bias, C, nk, str, pad, T_out, y, y_bs);
+  else
+    noise_conv_kernel<64><<<g, 256, smem, st>>>(har, har_bs, har_len, w, bias, C, nk, str, pad, T_out, y, y_bs);
   RVC_LAUNCH_CHECK();
 }
 
