@@ -85,24 +85,19 @@ __global__ void stft_mag_kernel(const double2* __restrict__ spec, long long n, f
   }
 }
 
-// log(clip(basis @ mag, 1e-5)) per (frame, mel bin); frames >= F are the
-// zero padding to a multiple of 32 (mel2hidden, :861-867).  Writes the raw
-// log-mel [B][Fp][128] and the encoder's input BatchNorm of it.
-__global__ void mel_log_kernel(const float* __restrict__ mag, const float* __restrict__ basis, int F, int Fp,
-                               const float* __restrict__ s_in, const float* __restrict__ t_in,
-                               float* __restrict__ mel, float* __restrict__ x0) {
-  const int t = blockIdx.x, b = blockIdx.y, m = threadIdx.x;
-  float v = 0.f;
-  if (t < F) {
-    const float* mr = mag + ((long long)b * F + t) * 513;
-    const float* br = basis + (long long)m * 513;
-    float s = 0.f;
-    for (int k = 0; k < 513; ++k) s = fmaf(br[k], mr[k], s);
-    v = logf(fmaxf(s, 1e-5f));
+// After the mel projection s = basis @ mag (the fp32 implicit GEMM, frames < F):
+// log(clip(s, 1e-5)) per (frame, mel bin); frames >= F are the zero padding to
+// a multiple of 32 (mel2hidden, :861-867).  Writes the raw log-mel [B][Fp][128]
+// in place and the encoder's input BatchNorm of it.
+__global__ void mel_finish_kernel(float* __restrict__ mel, int F, int Fp, int B, const float* __restrict__ s_in,
+                                  const float* __restrict__ t_in, float* __restrict__ x0) {
+  const long long n = (long long)B * Fp * 128;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < n; e += (long long)gridDim.x * blockDim.x) {
+    const int t = (int)((e / 128) % Fp);
+    const float v = t < F ? logf(fmaxf(mel[e], 1e-5f)) : 0.f;
+    mel[e] = v;
+    x0[e] = __fadd_rn(__fmul_rn(v, s_in[0]), t_in[0]);
   }
-  const long long o = ((long long)b * Fp + t) * 128 + m;
-  mel[o] = v;
-  x0[o] = __fadd_rn(__fmul_rn(v, s_in[0]), t_in[0]);
 }
 
 // ------------------------------------------------------------------ conv
@@ -1001,9 +996,13 @@ void RmvpeModel::finalize() {
       const double n = 1.0 - kNFFT + 2.0 * k;  // numpy.hanning: 0.5 + 0.5 cos(pi n / (M - 1))
       win[k] = 0.5 + 0.5 * std::cos(pi * n / (kNFFT - 1));
     }
-    mel_basis_ = DevBuf(ctx, sizeof(float) * basis.size());
+    // the projection runs as a 1x1 conv: weights [1][513 bins][128 mels]
+    std::vector<float> basis_t(basis.size());
+    for (int m = 0; m < kMels; ++m)
+      for (int k = 0; k < nb; ++k) basis_t[(size_t)k * kMels + m] = basis[(size_t)m * nb + k];
+    mel_basis_ = DevBuf(ctx, sizeof(float) * basis_t.size());
     window_ = DevBuf(ctx, sizeof(double) * win.size());
-    RVC_CUDA_TRY(cudaMemcpy(mel_basis_.p, basis.data(), mel_basis_.bytes, cudaMemcpyHostToDevice));
+    RVC_CUDA_TRY(cudaMemcpy(mel_basis_.p, basis_t.data(), mel_basis_.bytes, cudaMemcpyHostToDevice));
     RVC_CUDA_TRY(cudaMemcpy(window_.p, win.data(), window_.bytes, cudaMemcpyHostToDevice));
   }
   RVC_CUDA_TRY(cudaStreamSynchronize(st));
@@ -1293,10 +1292,26 @@ void RmvpeModel::infer_device(int B, int64_t T, const float* x, float thred, flo
         (const double2*)ws_.at("spec").p, nfr * kBins, buf("mag"));
     note_launch();
   }
-  mel_log_kernel<<<dim3(Fp, B), 128, 0, st>>>(buf("mag"), mel_basis_.f(), F, Fp, in_scale_.f(), in_shift_.f(),
-                                              buf("mel"), buf("x0"));
-  note_launch();
-  RVC_CUDA_TRY(cudaGetLastError());
+  {
+    // mel projection s[t][m] = sum_k basis[m][k] mag[t][k] as an unsplit fp32
+    // 1x1 implicit GEMM: each sum runs over k in ascending order from 0, one
+    // fmaf per bin, as a per-(frame, mel) loop would
+    C2Args a{};
+    a.x = buf("mag"); a.x_bs = (long long)F * kBins; a.H = F; a.W = 1; a.ldi = kBins;
+    a.C_in = kBins; a.C_out = kMels; a.taps = 1; a.transposed = 0;
+    a.w = mel_basis_.f();
+    a.OH = F; a.OW = 1;
+    a.y = buf("mel"); a.y_bs = (long long)Fp * kMels; a.oh_s = kMels; a.ow_s = kMels; a.oc_s = 1;
+    a.B = B; a.splits = 1; a.kit = (kBins + kBK - 1) / kBK;
+    conv2d_kernel<64, 64><<<dim3((unsigned)((F + 63) / 64), (unsigned)(kMels / 64), (unsigned)B), 256, 0, st>>>(a);
+    note_launch();
+    RVC_CUDA_TRY(cudaGetLastError());
+    const long long n = (long long)B * Fp * kMels;
+    mel_finish_kernel<<<(unsigned)std::min<long long>((n + 255) / 256, 148ll * 16), 256, 0, st>>>(
+        buf("mel"), F, Fp, B, in_scale_.f(), in_shift_.f(), buf("x0"));
+    note_launch();
+    RVC_CUDA_TRY(cudaGetLastError());
+  }
   save_tap("mel", buf("mel"), (long long)B * Fp * 128);
   // ---------------- encoder
   float *A = buf("A"), *Bb = buf("Bb"), *Tt = buf("Tt"), *P = buf("P");
