@@ -11,60 +11,58 @@
 #include <cstring>
 #include <memory>
 #include <unordered_map>
+#include <vector>
 
 using namespace rvc;
 
 namespace {
 
 std::mutex g_reg_mu;
-std::unordered_map<int64_t, std::unique_ptr<Context>> g_ctx;
-std::unordered_map<int64_t, std::unique_ptr<SynthModel>> g_synth;
-std::unordered_map<int64_t, std::unique_ptr<HubertModel>> g_hubert;
-std::unordered_map<int64_t, std::unique_ptr<IndexModel>> g_index;
-std::unordered_map<int64_t, std::unique_ptr<RmvpeModel>> g_rmvpe;
-std::unordered_map<int64_t, std::unique_ptr<FcpeModel>> g_fcpe;
+// Registries hold shared ownership: a call in flight keeps its model (and the
+// model keeps its context) alive, so a concurrent destroy only drops the
+// registry's reference and the object goes away when the last call is done.
+std::unordered_map<int64_t, std::shared_ptr<Context>> g_ctx;
+std::unordered_map<int64_t, std::shared_ptr<SynthModel>> g_synth;
+std::unordered_map<int64_t, std::shared_ptr<HubertModel>> g_hubert;
+std::unordered_map<int64_t, std::shared_ptr<IndexModel>> g_index;
+std::unordered_map<int64_t, std::shared_ptr<RmvpeModel>> g_rmvpe;
+std::unordered_map<int64_t, std::shared_ptr<FcpeModel>> g_fcpe;
 int64_t g_next = 1;
 
-Context* get_ctx(int64_t h) {
+template <typename T>
+std::shared_ptr<T> lookup(std::unordered_map<int64_t, std::shared_ptr<T>>& reg, int64_t h, const char* what) {
   std::lock_guard<std::mutex> lk(g_reg_mu);
-  auto it = g_ctx.find(h);
-  if (it == g_ctx.end()) throw Error{kErrState, "invalid context handle " + std::to_string(h)};
-  return it->second.get();
+  auto it = reg.find(h);
+  if (it == reg.end()) throw Error{kErrState, std::string("invalid ") + what + " handle " + std::to_string(h)};
+  return it->second;
 }
 
-SynthModel* get_synth(int64_t h) {
-  std::lock_guard<std::mutex> lk(g_reg_mu);
-  auto it = g_synth.find(h);
-  if (it == g_synth.end()) throw Error{kErrState, "invalid synthesizer handle " + std::to_string(h)};
-  return it->second.get();
+std::shared_ptr<Context> get_ctx(int64_t h) { return lookup(g_ctx, h, "context"); }
+
+// Shared ownership of a new model: the deleter keeps the model's context alive
+// and frees the model's device buffers under the context lock, on its device.
+// The last reference is never dropped by a thread holding that lock (callers
+// release the lock before their reference).
+template <typename T>
+std::shared_ptr<T> own_model(Context* c, std::unique_ptr<T> m) {
+  std::shared_ptr<Context> cref = c->shared_from_this();
+  return std::shared_ptr<T>(m.release(), [cref](T* p) {
+    std::lock_guard<std::mutex> lk(cref->mu);
+    DeviceGuard dg(cref->device);
+    delete p;
+  });
 }
 
-HubertModel* get_hubert(int64_t h) {
+// Removes a model from its registry; the caller drops the returned reference
+// outside every lock.
+template <typename T>
+std::shared_ptr<T> take(std::unordered_map<int64_t, std::shared_ptr<T>>& reg, int64_t h, const char* what) {
   std::lock_guard<std::mutex> lk(g_reg_mu);
-  auto it = g_hubert.find(h);
-  if (it == g_hubert.end()) throw Error{kErrState, "invalid HuBERT handle " + std::to_string(h)};
-  return it->second.get();
-}
-
-RmvpeModel* get_rmvpe(int64_t h) {
-  std::lock_guard<std::mutex> lk(g_reg_mu);
-  auto it = g_rmvpe.find(h);
-  if (it == g_rmvpe.end()) throw Error{kErrState, "invalid RMVPE handle " + std::to_string(h)};
-  return it->second.get();
-}
-
-FcpeModel* get_fcpe(int64_t h) {
-  std::lock_guard<std::mutex> lk(g_reg_mu);
-  auto it = g_fcpe.find(h);
-  if (it == g_fcpe.end()) throw Error{kErrState, "invalid FCPE handle " + std::to_string(h)};
-  return it->second.get();
-}
-
-IndexModel* get_index(int64_t h) {
-  std::lock_guard<std::mutex> lk(g_reg_mu);
-  auto it = g_index.find(h);
-  if (it == g_index.end()) throw Error{kErrState, "invalid index handle " + std::to_string(h)};
-  return it->second.get();
+  auto it = reg.find(h);
+  if (it == reg.end()) throw Error{kErrState, std::string("invalid ") + what + " handle " + std::to_string(h)};
+  std::shared_ptr<T> m = std::move(it->second);
+  reg.erase(it);
+  return m;
 }
 
 template <typename F>
@@ -88,10 +86,10 @@ int32_t guarded(F&& f) {
 template <typename F>
 int32_t on_ctx(int64_t h, F&& f) {
   return guarded([&] {
-    Context* c = get_ctx(h);
+    std::shared_ptr<Context> c = get_ctx(h);
     std::lock_guard<std::mutex> lk(c->mu);
     DeviceGuard dg(c->device);
-    f(c);
+    f(c.get());
   });
 }
 
@@ -111,57 +109,57 @@ void d2h(Context* c, void* h, const void* d, size_t n) {
 template <typename F>
 int32_t on_synth(int64_t model, F&& f) {
   return guarded([&] {
-    SynthModel* m = get_synth(model);
+    std::shared_ptr<SynthModel> m = lookup(g_synth, model, "synthesizer");
     std::lock_guard<std::mutex> lk(m->ctx->mu);
     DeviceGuard dg(m->ctx->device);
-    f(m);
+    f(m.get());
   });
 }
 
 template <typename F>
 int32_t on_hubert(int64_t model, F&& f) {
   return guarded([&] {
-    HubertModel* m = get_hubert(model);
+    std::shared_ptr<HubertModel> m = lookup(g_hubert, model, "HuBERT");
     std::lock_guard<std::mutex> lk(m->ctx->mu);
     DeviceGuard dg(m->ctx->device);
-    f(m);
+    f(m.get());
   });
 }
 
 template <typename F>
 int32_t on_index(int64_t index, F&& f) {
   return guarded([&] {
-    IndexModel* m = get_index(index);
+    std::shared_ptr<IndexModel> m = lookup(g_index, index, "index");
     std::lock_guard<std::mutex> lk(m->ctx->mu);
     DeviceGuard dg(m->ctx->device);
-    f(m);
+    f(m.get());
   });
 }
 
 template <typename F>
 int32_t on_fcpe(int64_t model, F&& f) {
   return guarded([&] {
-    FcpeModel* m = get_fcpe(model);
+    std::shared_ptr<FcpeModel> m = lookup(g_fcpe, model, "FCPE");
     std::lock_guard<std::mutex> lk(m->ctx->mu);
     DeviceGuard dg(m->ctx->device);
-    f(m);
+    f(m.get());
   });
 }
 
 template <typename F>
 int32_t on_rmvpe(int64_t model, F&& f) {
   return guarded([&] {
-    RmvpeModel* m = get_rmvpe(model);
+    std::shared_ptr<RmvpeModel> m = lookup(g_rmvpe, model, "RMVPE");
     std::lock_guard<std::mutex> lk(m->ctx->mu);
     DeviceGuard dg(m->ctx->device);
-    f(m);
+    f(m.get());
   });
 }
 
 }  // namespace
 
 // Handle lookup for entry points defined in other translation units.
-rvc::Context* rvc_capi_context(int64_t h) { return get_ctx(h); }
+std::shared_ptr<rvc::Context> rvc_capi_context(int64_t h) { return get_ctx(h); }
 
 extern "C" {
 
@@ -205,7 +203,7 @@ int32_t rvc_cuda_create(int32_t device, int64_t* ctx) {
     RVC_CUDA_TRY(cudaGetDeviceProperties(&prop, device));
     if (prop.major != 10)
       throw Error{kErrArg, std::string("librvc_cuda is built for sm_100a (B200); device is ") + prop.name};
-    auto c = std::make_unique<Context>(device);
+    auto c = std::make_shared<Context>(device);
     std::lock_guard<std::mutex> lk(g_reg_mu);
     *ctx = g_next++;
     g_ctx[*ctx] = std::move(c);
@@ -214,20 +212,22 @@ int32_t rvc_cuda_create(int32_t device, int64_t* ctx) {
 
 int32_t rvc_cuda_destroy(int64_t ctx) {
   return guarded([&] {
-    std::unique_ptr<Context> c;
+    std::shared_ptr<Context> c;
+    std::vector<std::shared_ptr<void>> bound;
     {
       std::lock_guard<std::mutex> lk(g_reg_mu);
       auto it = g_ctx.find(ctx);
       if (it == g_ctx.end()) throw Error{kErrState, "invalid context handle " + std::to_string(ctx)};
-      // every model bound to this context goes first: their buffers and plans
-      // are released through it
+      // every model bound to this context leaves the registry first
       const Context* cp = it->second.get();
-      auto drop = [cp](auto& reg) {
+      auto drop = [cp, &bound](auto& reg) {
         for (auto s = reg.begin(); s != reg.end();) {
-          if (s->second->ctx == cp)
+          if (s->second->ctx == cp) {
+            bound.push_back(std::move(s->second));
             s = reg.erase(s);
-          else
+          } else {
             ++s;
+          }
         }
       };
       drop(g_synth);
@@ -238,7 +238,10 @@ int32_t rvc_cuda_destroy(int64_t ctx) {
       c = std::move(it->second);
       g_ctx.erase(it);
     }
-    std::lock_guard<std::mutex> lk(c->mu);
+    // models first (each deleter waits for the context lock, i.e. for calls in
+    // flight on it), then the context once no call holds it any more
+    bound.clear();
+    { std::lock_guard<std::mutex> lk(c->mu); }
     c.reset();
   });
 }
@@ -540,7 +543,7 @@ int32_t rvc_cuda_rel_attention(int64_t ctx, const float* q, const float* k, cons
     DevBuf dq(c, sizeof(float) * n), dk(c, sizeof(float) * n), dv(c, sizeof(float) * n);
     DevBuf qkv(c, sizeof(float) * 3 * n), ek(c, sizeof(float) * (2 * window + 1) * kc),
         ev(c, sizeof(float) * (2 * window + 1) * kc);
-    DevBuf S(c, sizeof(float) * (size_t)B * heads * P * P), yt(c, sizeof(float) * n), yo(c, sizeof(float) * n);
+    DevBuf yt(c, sizeof(float) * n), yo(c, sizeof(float) * n);
     h2d(c, dq.p, q, dq.bytes);
     h2d(c, dk.p, k, dk.bytes);
     h2d(c, dv.p, v, dv.bytes);
@@ -552,7 +555,7 @@ int32_t rvc_cuda_rel_attention(int64_t ctx, const float* q, const float* k, cons
       k_nct_to_ntc(dk.f() + (size_t)bb * H * P, qkv.f() + (size_t)bb * P * 3 * H + H, 1, H, P, 3 * H, c->stream);
       k_nct_to_ntc(dv.f() + (size_t)bb * H * P, qkv.f() + (size_t)bb * P * 3 * H + 2 * H, 1, H, P, 3 * H, c->stream);
     }
-    k_rel_attention(qkv.f(), 3 * H, 0, H, 2 * H, ek.f(), ev.f(), B, heads, kc, P, window, S.f(), yt.f(), H,
+    k_rel_attention(qkv.f(), 3 * H, 0, H, 2 * H, ek.f(), ev.f(), B, heads, kc, P, window, nullptr, yt.f(), H,
                     c->stream);
     k_ntc_to_nct(yt.f(), H, yo.f(), B, H, P, c->stream);
     d2h(c, y, yo.p, yo.bytes);
@@ -590,23 +593,14 @@ int32_t rvc_cuda_synth_create(int64_t ctx, const int32_t* cfg, int32_t ncfg, int
     auto m = std::make_unique<SynthModel>(c, s);
     std::lock_guard<std::mutex> lk(g_reg_mu);
     *model = g_next++;
-    g_synth[*model] = std::move(m);
+    g_synth[*model] = own_model(c, std::move(m));
   });
 }
 
 int32_t rvc_cuda_synth_destroy(int64_t model) {
   return guarded([&] {
-    std::unique_ptr<SynthModel> m;
-    {
-      std::lock_guard<std::mutex> lk(g_reg_mu);
-      auto it = g_synth.find(model);
-      if (it == g_synth.end()) throw Error{kErrState, "invalid synthesizer handle " + std::to_string(model)};
-      m = std::move(it->second);
-      g_synth.erase(it);
-    }
-    std::lock_guard<std::mutex> lk(m->ctx->mu);
-    DeviceGuard dg(m->ctx->device);
-    m.reset();
+    std::shared_ptr<SynthModel> m = take(g_synth, model, "synthesizer");
+    m.reset();  // freed now, or when the last call in flight returns
   });
 }
 
@@ -691,23 +685,14 @@ int32_t rvc_cuda_hubert_create(int64_t ctx, int32_t precision, int64_t* model) {
     auto m = std::make_unique<HubertModel>(c, precision);
     std::lock_guard<std::mutex> lk(g_reg_mu);
     *model = g_next++;
-    g_hubert[*model] = std::move(m);
+    g_hubert[*model] = own_model(c, std::move(m));
   });
 }
 
 int32_t rvc_cuda_hubert_destroy(int64_t model) {
   return guarded([&] {
-    std::unique_ptr<HubertModel> m;
-    {
-      std::lock_guard<std::mutex> lk(g_reg_mu);
-      auto it = g_hubert.find(model);
-      if (it == g_hubert.end()) throw Error{kErrState, "invalid HuBERT handle " + std::to_string(model)};
-      m = std::move(it->second);
-      g_hubert.erase(it);
-    }
-    std::lock_guard<std::mutex> lk(m->ctx->mu);
-    DeviceGuard dg(m->ctx->device);
-    m.reset();
+    std::shared_ptr<HubertModel> m = take(g_hubert, model, "HuBERT");
+    m.reset();  // freed now, or when the last call in flight returns
   });
 }
 
@@ -765,23 +750,14 @@ int32_t rvc_cuda_index_create(int64_t ctx, const float* db, int64_t N, int32_t D
     auto m = std::make_unique<IndexModel>(c, db, N, D, precision);
     std::lock_guard<std::mutex> lk(g_reg_mu);
     *index = g_next++;
-    g_index[*index] = std::move(m);
+    g_index[*index] = own_model(c, std::move(m));
   });
 }
 
 int32_t rvc_cuda_index_destroy(int64_t index) {
   return guarded([&] {
-    std::unique_ptr<IndexModel> m;
-    {
-      std::lock_guard<std::mutex> lk(g_reg_mu);
-      auto it = g_index.find(index);
-      if (it == g_index.end()) throw Error{kErrState, "invalid index handle " + std::to_string(index)};
-      m = std::move(it->second);
-      g_index.erase(it);
-    }
-    std::lock_guard<std::mutex> lk(m->ctx->mu);
-    DeviceGuard dg(m->ctx->device);
-    m.reset();
+    std::shared_ptr<IndexModel> m = take(g_index, index, "index");
+    m.reset();  // freed now, or when the last call in flight returns
   });
 }
 
@@ -864,23 +840,14 @@ int32_t rvc_cuda_rmvpe_create(int64_t ctx, int64_t* model) {
     auto m = std::make_unique<RmvpeModel>(c);
     std::lock_guard<std::mutex> lk(g_reg_mu);
     *model = g_next++;
-    g_rmvpe[*model] = std::move(m);
+    g_rmvpe[*model] = own_model(c, std::move(m));
   });
 }
 
 int32_t rvc_cuda_rmvpe_destroy(int64_t model) {
   return guarded([&] {
-    std::unique_ptr<RmvpeModel> m;
-    {
-      std::lock_guard<std::mutex> lk(g_reg_mu);
-      auto it = g_rmvpe.find(model);
-      if (it == g_rmvpe.end()) throw Error{kErrState, "invalid RMVPE handle " + std::to_string(model)};
-      m = std::move(it->second);
-      g_rmvpe.erase(it);
-    }
-    std::lock_guard<std::mutex> lk(m->ctx->mu);
-    DeviceGuard dg(m->ctx->device);
-    m.reset();
+    std::shared_ptr<RmvpeModel> m = take(g_rmvpe, model, "RMVPE");
+    m.reset();  // freed now, or when the last call in flight returns
   });
 }
 
@@ -938,23 +905,14 @@ int32_t rvc_cuda_fcpe_create(int64_t ctx, int32_t precision, int64_t* model) {
     auto m = std::make_unique<FcpeModel>(c, precision);
     std::lock_guard<std::mutex> lk(g_reg_mu);
     *model = g_next++;
-    g_fcpe[*model] = std::move(m);
+    g_fcpe[*model] = own_model(c, std::move(m));
   });
 }
 
 int32_t rvc_cuda_fcpe_destroy(int64_t model) {
   return guarded([&] {
-    std::unique_ptr<FcpeModel> m;
-    {
-      std::lock_guard<std::mutex> lk(g_reg_mu);
-      auto it = g_fcpe.find(model);
-      if (it == g_fcpe.end()) throw Error{kErrState, "invalid FCPE handle " + std::to_string(model)};
-      m = std::move(it->second);
-      g_fcpe.erase(it);
-    }
-    std::lock_guard<std::mutex> lk(m->ctx->mu);
-    DeviceGuard dg(m->ctx->device);
-    m.reset();
+    std::shared_ptr<FcpeModel> m = take(g_fcpe, model, "FCPE");
+    m.reset();  // freed now, or when the last call in flight returns
   });
 }
 

@@ -5,6 +5,7 @@
 #include "common.cuh"
 
 #include <map>
+#include <memory>
 #include <mutex>
 #include <string>
 #include <unordered_map>
@@ -13,7 +14,7 @@
 
 namespace rvc {
 
-struct Context {
+struct Context : std::enable_shared_from_this<Context> {
   int device = 0;
   cudaStream_t stream = nullptr;
   int* d_err = nullptr;

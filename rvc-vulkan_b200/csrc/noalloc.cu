@@ -60,17 +60,18 @@ static float* noalloc_scratch(int device) {
 using namespace rvc;
 
 // Declared in the registry of capi.cu; looked up the same way.
-Context* rvc_capi_context(int64_t h);
+std::shared_ptr<Context> rvc_capi_context(int64_t h);
 
 extern "C" int32_t rvc_cuda_rel_attention_noalloc(int64_t ctx, const float* q, const float* k, const float* v,
                                                   const float* emb_k, const float* emb_v, int32_t B, int32_t heads,
                                                   int32_t kc, int32_t P, int32_t window, float* y) {
   try {
-    Context* c = rvc_capi_context(ctx);
+    std::shared_ptr<Context> c = rvc_capi_context(ctx);
     std::lock_guard<std::mutex> lk(c->mu);
     DeviceGuard dg(c->device);
     RVC_CHECK_ARG(B >= 0 && heads > 0 && kc > 0 && P >= 0 && window >= 0, "rel_attention_noalloc: bad shape");
     RVC_CHECK_ARG(q && k && v && emb_k && emb_v && y, "rel_attention_noalloc: null device pointer");
+    RVC_CHECK_ARG(kc <= 128 && window <= 16, "rel_attention_noalloc: head dim <= 128 and window <= 16 supported");
     if ((long long)B * P == 0) return kOk;
     const long long H = (long long)heads * kc;
     const long long need = 4LL * B * H * P;

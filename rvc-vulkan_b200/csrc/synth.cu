@@ -181,7 +181,6 @@ void SynthModel::ensure_ws(int B, int P) {
   for (const char* n : {"ex", "att", "ao", "y2", "z", "zf", "h", "acts", "skip"}) add(n, (long long)P * H);
   add("qkv", (long long)P * 3 * H);
   add("y1", (long long)P * F);
-  add("S", (long long)cfg.heads * P * P);
   add("stats", (long long)P * 2 * H);
   add("xin", (long long)P * 2 * H);
   add("rs", (long long)P * 2 * H);
@@ -248,7 +247,7 @@ void SynthModel::enc_stage(int B, int P, const float* phone, const long long* pi
                           W(p + ".emb_rel_v").buf.f(), B, cfg.heads, cfg.kc, P, cfg.window,
                           (float)std::sqrt((double)cfg.kc), buf("att"), H))
         k_rel_attention(buf("qkv"), 3 * H, 0, H, 2 * H, W(p + ".emb_rel_k").buf.f(), W(p + ".emb_rel_v").buf.f(), B,
-                        cfg.heads, cfg.kc, P, cfg.window, buf("S"), buf("att"), H, st);
+                        cfg.heads, cfg.kc, P, cfg.window, nullptr, buf("att"), H, st);
       if (ctx->prof)
         ctx->prof_end(e0, e1, 4.0 * B * cfg.heads * (double)P * P * cfg.kc,
                       "attn enc_p B=" + std::to_string(B) + " P=" + std::to_string(P), false);

@@ -33,3 +33,11 @@ def rel_l2(a, b):
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def pytest_collection_modifyitems(config, items):
+    """A GPU run needs the CUDA library: when any selected test is marked
+    ``gpu``, loading librvc_cuda.so is checked once up front, so a missing or
+    broken build fails the run loudly instead of skipping its tests."""
+    if any(it.get_closest_marker("gpu") for it in items):
+        from rvc_cuda import _lib  # noqa: F401,PLC0415  (raises ImportError when the library is missing)

@@ -414,10 +414,18 @@ PIPE_CASES = [
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("RVC_REFERENCE", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("RVC_REFERENCE", ""),
+                    help="checkout of the reference (default: $RVC_REFERENCE, else the oracle/_ref copy)")
     ap.add_argument("--only", choices=["vits", "hubert", "ops", "retrieval", "rmvpe", "partial", "dsp", "ivf", "fcpe"], default=None,
                     help="regenerate one family and keep the other fixtures")
     args = ap.parse_args()
+    if not args.ref:
+        sys.path.insert(0, ROOT)
+        from oracle import reference as oref  # noqa: PLC0415
+
+        args.ref = oref.root() or ""
+    if not args.ref:
+        ap.error("no reference: pass --ref <checkout> or set RVC_REFERENCE (or run make -C oracle ref)")
     os.environ["RVC_BACKEND"] = "numpy"
     sys.path.insert(0, args.ref)
     from runtime import nn  # noqa: PLC0415

@@ -28,7 +28,7 @@ from tests.golden.make_golden import PIPE_CASES
 
 pytestmark = pytest.mark.gpu
 
-dsp = pytest.importorskip("rvc_cuda.dsp")
+from rvc_cuda import dsp  # noqa: E402
 signal = pytest.importorskip("scipy.signal")
 BH, AH = signal.butter(N=5, Wn=48, btype="high", fs=16000)
 

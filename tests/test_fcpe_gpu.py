@@ -15,7 +15,7 @@ from tests.conftest import load_golden, rel_l2
 
 pytestmark = pytest.mark.gpu
 
-fc = pytest.importorskip("rvc_cuda.fcpe")
+from rvc_cuda import fcpe as fc  # noqa: E402
 
 GOLD = ["fcpe_t24000", "fcpe_t3001", "fcpe_t400"]
 _models = {}

@@ -14,7 +14,7 @@ from tests.conftest import load_golden, rel_l2
 
 pytestmark = pytest.mark.gpu
 
-hub = pytest.importorskip("rvc_cuda.hubert")
+from rvc_cuda import hubert as hub  # noqa: E402
 
 TOL = 1e-3
 _models = {}

@@ -14,7 +14,7 @@ from oracle import vits as OV
 
 pytestmark = pytest.mark.gpu
 
-ops = pytest.importorskip("rvc_cuda.ops")
+from rvc_cuda import ops  # noqa: E402
 
 RS = np.random.RandomState(7)
 

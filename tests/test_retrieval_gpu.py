@@ -17,7 +17,7 @@ from tests.conftest import load_golden
 
 pytestmark = pytest.mark.gpu
 
-ret = pytest.importorskip("rvc_cuda.retrieval")
+from rvc_cuda import retrieval as ret  # noqa: E402
 
 GOLD = ["ret_f200_n20000", "ret_f64_n3000_d256", "ret_f37_n5", "ret_f9_n1000_d60"]
 

@@ -16,7 +16,7 @@ from tests.conftest import load_golden, rel_l2
 
 pytestmark = pytest.mark.gpu
 
-rm = pytest.importorskip("rvc_cuda.rmvpe")
+from rvc_cuda import rmvpe as rm  # noqa: E402
 
 _models = {}
 

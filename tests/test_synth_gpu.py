@@ -14,7 +14,7 @@ from tests.conftest import load_golden, rel_l2
 
 pytestmark = pytest.mark.gpu
 
-synth = pytest.importorskip("rvc_cuda.synth")
+from rvc_cuda import synth  # noqa: E402
 
 WAVE_TOL = 1e-3
 LAYER_TOL = 1e-3

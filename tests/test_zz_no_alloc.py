@@ -14,7 +14,7 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-ops = pytest.importorskip("rvc_cuda.ops")
+from rvc_cuda import ops  # noqa: E402  (a missing library fails the module, it does not skip it)
 
 
 def _noalloc(ctx, q, k, v, ek, ev, heads, window):
@@ -63,3 +63,27 @@ def test_noalloc_rejects_sizes_beyond_the_fixed_scratch():
                                                   C.c_void_p(16))
     assert rc == _lib.RVC_E_ARG
     assert "scratch" in _lib.last_error()
+
+
+def test_noalloc_rejects_unsupported_head_dim_before_queueing_work():
+    """A head dimension above 128 (or a window above 16) is refused with the
+    same argument error before any kernel is queued on the shared array: the
+    library's launch counter does not move.  The buffers are real and sized
+    for the call, so nothing could read outside them either way."""
+    from rvc_cuda import _lib
+
+    ctx = _lib.get_context()
+    B, heads, kc, P, window = 1, 1, 129, 8, 10
+    n = B * heads * kc * P
+    bufs = [ctx.alloc(4 * n) for _ in range(3)] + [ctx.alloc(4 * (2 * window + 1) * kc) for _ in range(2)]
+    dy = ctx.alloc(4 * n)
+    try:
+        before = _lib.launch_count()
+        rc = _lib.lib.rvc_cuda_rel_attention_noalloc(ctx.handle, *[C.c_void_p(p) for p in bufs], B, heads, kc, P,
+                                                      window, C.c_void_p(dy))
+        assert rc == _lib.RVC_E_ARG
+        assert "head dim" in _lib.last_error()
+        assert _lib.launch_count() == before
+    finally:
+        for p in bufs + [dy]:
+            ctx.free(p)
