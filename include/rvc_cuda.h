@@ -58,6 +58,11 @@ int32_t rvc_cuda_stream(int64_t ctx, void** stream);
 /* Caps the bytes the context may hold on the device (0 = no cap); a request
  * over the cap fails with RVC_E_OOM (host-side fault injection for tests). */
 int32_t rvc_cuda_set_mem_cap(int64_t ctx, int64_t bytes);
+/* Gives the context's cached free device blocks back to the driver; blocks in
+ * use are untouched.  Counterpart of VulkanContext.clear_pool
+ * (runtime/vulkan_ops.py:618-633), which VC.vc_single calls after every
+ * conversion (runtime/vc.py:532-534). */
+int32_t rvc_cuda_release_pool(int64_t ctx);
 /* Device buffers owned by the context (for device-resident inputs). */
 int32_t rvc_cuda_alloc(int64_t ctx, int64_t bytes, void** dptr);
 int32_t rvc_cuda_free(int64_t ctx, void* dptr);
@@ -180,7 +185,9 @@ int32_t rvc_cuda_synth_infer_partial(int64_t model, int32_t P, int32_t skip_head
 /* Debug taps: copies the named intermediate of the last infer (e.g.
  * "enc.l5", "flow.z", "dec.s2.out") into out (n floats); RVC_E_ARG if unknown. */
 int32_t rvc_cuda_synth_tap(int64_t model, const char* name, float* out, int64_t n);
-/* Enables recording of debug taps (off by default: taps cost a copy). */
+/* Enables recording of debug taps (off by default: taps cost a copy).
+ * enable: 0 off, 1 every chunk of the call (chunk-major), 2 + c only chunk c
+ * of a batched call (the taps then hold that chunk's data alone). */
 int32_t rvc_cuda_synth_keep_taps(int64_t model, int32_t enable);
 
 /* ---------------------------------------------------------------- HuBERT

@@ -261,6 +261,10 @@ int32_t rvc_cuda_set_mem_cap(int64_t ctx, int64_t bytes) {
   return on_ctx(ctx, [&](Context* c) { c->mem_cap = bytes; });
 }
 
+int32_t rvc_cuda_release_pool(int64_t ctx) {
+  return on_ctx(ctx, [&](Context* c) { c->release_pool(); });
+}
+
 int32_t rvc_cuda_alloc(int64_t ctx, int64_t bytes, void** dptr) {
   return on_ctx(ctx, [&](Context* c) {
     RVC_CHECK_ARG(bytes >= 0, "alloc: negative size");
@@ -676,7 +680,10 @@ int32_t rvc_cuda_synth_tap(int64_t model, const char* name, float* out, int64_t 
 }
 
 int32_t rvc_cuda_synth_keep_taps(int64_t model, int32_t enable) {
-  return on_synth(model, [&](SynthModel* m) { m->keep_taps = enable != 0; });
+  return on_synth(model, [&](SynthModel* m) {
+    RVC_CHECK_ARG(enable >= 0, "synth_keep_taps: enable must be >= 0");
+    m->keep_taps = enable;
+  });
 }
 
 // ----------------------------------------------------------------- HuBERT

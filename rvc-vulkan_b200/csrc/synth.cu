@@ -191,10 +191,17 @@ void SynthModel::ensure_ws(int B, int P) {
   ws_P = P;
 }
 
-void SynthModel::save_tap(const std::string& name, const float* d, int64_t n) {
+void SynthModel::save_tap(const std::string& name, const float* d, int64_t per_chunk, int B) {
   if (!keep_taps) return;
+  int64_t off = 0, n = per_chunk * B;
+  if (keep_taps >= 2) {
+    const int c = keep_taps - 2;
+    if (c >= B) return;
+    off = per_chunk * c;
+    n = per_chunk;
+  }
   std::vector<float> h((size_t)n);
-  RVC_CUDA_TRY(cudaMemcpyAsync(h.data(), d, sizeof(float) * n, cudaMemcpyDeviceToHost, ctx->stream));
+  RVC_CUDA_TRY(cudaMemcpyAsync(h.data(), d + off, sizeof(float) * n, cudaMemcpyDeviceToHost, ctx->stream));
   RVC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
   taps_[name] = std::move(h);
 }
@@ -235,7 +242,7 @@ void SynthModel::enc_stage(int B, int P, const float* phone, const long long* pi
   run_conv(emb_phone_, io_rows(phone, cfg.phone_dim, P, ex, H, B, (long long)P * cfg.phone_dim, PH));
   k_enc_embed_finish(ex, pitch, W("enc_p.emb_pitch.weight").buf.f(), (long long)B * P, H,
                      (float)std::sqrt((double)H), st);
-  save_tap("enc.embed", ex, (long long)B * PH);
+  save_tap("enc.embed", ex, PH, B);
   for (int i = 0; i < cfg.layers; ++i) {
     const std::string p = "enc_p.encoder.attn_layers." + std::to_string(i);
     run_conv(qkv_[i], io_rows(ex, H, P, buf("qkv"), 3 * H, B, PH, 3 * PH));
@@ -253,7 +260,7 @@ void SynthModel::enc_stage(int B, int P, const float* phone, const long long* pi
                       "attn enc_p B=" + std::to_string(B) + " P=" + std::to_string(P), false);
     }
     run_conv(o_[i], io_rows(buf("att"), H, P, buf("ao"), H, B, PH, PH));
-    save_tap("enc.l" + std::to_string(i) + ".attn", buf("ao"), (long long)B * PH);
+    save_tap("enc.l" + std::to_string(i) + ".attn", buf("ao"), PH, B);
     const std::string nl = "enc_p.encoder.norm_layers_";
     k_layernorm(ex, H, buf("ao"), H, (long long)B * P, H, W(nl + "1." + std::to_string(i) + ".gamma").buf.f(),
                 W(nl + "1." + std::to_string(i) + ".beta").buf.f(), 1e-5f, ex, H, st);
@@ -263,11 +270,11 @@ void SynthModel::enc_stage(int B, int P, const float* phone, const long long* pi
     run_conv(ffn2_[i], io_rows(buf("y1"), F, P, buf("y2"), H, B, (long long)P * F, PH));
     k_layernorm(ex, H, buf("y2"), H, (long long)B * P, H, W(nl + "2." + std::to_string(i) + ".gamma").buf.f(),
                 W(nl + "2." + std::to_string(i) + ".beta").buf.f(), 1e-5f, ex, H, st);
-    save_tap("enc.l" + std::to_string(i), ex, (long long)B * PH);
+    save_tap("enc.l" + std::to_string(i), ex, PH, B);
   }
   run_conv(proj_, io_rows(ex, H, P, buf("stats"), 2 * H, B, PH, 2 * PH));
   k_zp(buf("stats"), nz, B, P, H, buf("z"), st);
-  save_tap("enc.zp", buf("z"), (long long)B * PH);
+  save_tap("enc.zp", buf("z"), PH, B);
 
 }
 
@@ -319,7 +326,7 @@ void SynthModel::dec_stage(int B, int P, const float* z, long long z_bs, const f
     a.bias2 = buf("dcond");
     a.bias2_bs = cfg.up0;
     run_conv(conv_pre_, a);
-    save_tap("dec.pre", xo, (long long)B * dmax);
+    save_tap("dec.pre", xo, dmax, B);
   }
   int Lc = P;
   for (int i = 0; i < cfg.n_ups; ++i) {
@@ -338,7 +345,7 @@ void SynthModel::dec_stage(int B, int P, const float* z, long long z_bs, const f
       a.res_bs = dmax;
       a.res_ld = C;
       run_conv(ups_[i], a);
-      save_tap("dec.s" + std::to_string(i) + ".ups", x0, (long long)B * dmax);
+      save_tap("dec.s" + std::to_string(i) + ".ups", x0, dmax, B);
     }
     for (int j = 0; j < 3; ++j) {
       for (int m = 0; m < 3; ++m) {
@@ -368,12 +375,12 @@ void SynthModel::dec_stage(int B, int P, const float* z, long long z_bs, const f
         run_conv(rb2_[i][j][m], c);
       }
     }
-    save_tap("dec.s" + std::to_string(i) + ".out", xo, (long long)B * dmax);
+    save_tap("dec.s" + std::to_string(i) + ".out", xo, dmax, B);
     Lc = Ln;
   }
   const int Cl = cfg.up0 >> cfg.n_ups;
   k_conv_post_tanh(xo, dmax, B, Lc, Cl, W("dec.conv_post.weight").buf.f(), 7, 3, 0.01f, wave, st);
-  save_tap("dec.wave", wave, (long long)B * N);
+  save_tap("dec.wave", wave, N, B);
 }
 
 void SynthModel::infer_device(int B, int P, const float* phone, const long long* pitch, const float* nsff0,
@@ -387,9 +394,9 @@ void SynthModel::infer_device(int B, int P, const float* phone, const long long*
   taps_.clear();
   enc_stage(B, P, phone, pitch, sid, nz);
   float* z = flow_stage(B, P, buf("z"), buf("zf"));
-  save_tap("flow.z", z, (long long)B * PH);
+  save_tap("flow.z", z, PH, B);
   k_sine_source(nsff0, ns, B, P, upp, cfg.sr, lin_w_, lin_b_, buf("phase"), buf("har"), st);
-  save_tap("dec.har", buf("har"), (long long)B * N);
+  save_tap("dec.har", buf("har"), N, B);
   dec_stage(B, P, z, PH, buf("har"), N, (int)N, wave);
 }
 

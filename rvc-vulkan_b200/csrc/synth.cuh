@@ -49,7 +49,7 @@ class SynthModel {
                             const float* nsff0, const long long* sid, const float* nz, const float* ns,
                             float* wave);
   bool tap(const std::string& name, float* host, int64_t n);
-  bool keep_taps = false;
+  int keep_taps = 0;  // 0 off, 1 every chunk, 2 + c chunk c only
   Context* ctx;
   SynthConfig cfg;
 
@@ -57,7 +57,8 @@ class SynthModel {
   const RawTensor& W(const std::string& key) const;
   DevBuf fold(const std::string& base);  // weight_v/weight_g -> folded
   void ensure_ws(int B, int P);
-  void save_tap(const std::string& name, const float* d, int64_t n);
+  // records B chunks of `per_chunk` floats each (chunk stride per_chunk) from d
+  void save_tap(const std::string& name, const float* d, int64_t per_chunk, int B);
   void run_conv(const ConvLayer& L, const ConvIO& io);
   void enc_stage(int B, int P, const float* phone, const long long* pitch, const long long* sid, const float* nz);
   float* flow_stage(int B, int P, float* z, float* zf);

@@ -12,7 +12,9 @@ Drop-in for jiangchengnay/rvc-vulkan's numpy runtime:
   ``rvc_cuda.rmvpe.patch_reference`` for ``RMVPE.infer_from_audio``,
   ``rvc_cuda.fcpe.patch_reference`` for ``FCPE.infer``,
   ``rvc_cuda.dsp.patch_reference`` for the pipeline's ``filtfilt``,
-  ``change_rms`` and ``interpolate_linear``).
+  ``change_rms`` and ``interpolate_linear``) and makes ``VC.vc_single``'s
+  closing pool release work without the Vulkan engine library
+  (``patch_vc_pool_release``).
 
 Importing this package does not touch the GPU; the shared library is loaded
 on first use of ``rvc_cuda.ops`` / ``rvc_cuda.synth`` and raises if missing.
@@ -20,7 +22,7 @@ on first use of ``rvc_cuda.ops`` / ``rvc_cuda.synth`` and raises if missing.
 
 from __future__ import annotations
 
-__all__ = ["register", "patch_reference", "probe"]
+__all__ = ["register", "patch_reference", "patch_vc_pool_release", "probe"]
 
 
 def probe() -> bool:
@@ -56,3 +58,43 @@ def patch_reference(device=None, precision: str = "bf16x3") -> None:
     rmvpe.patch_reference(device=device)
     fcpe.patch_reference(device=device, precision=precision)
     dsp.patch_reference()
+    patch_vc_pool_release()
+
+
+class _DevicePool:
+    """What ``VC.vc_single`` gets from ``vulkan_ops.get_context()`` when the
+    Vulkan engine is absent: its one call, ``clear_pool()``, returns the cached
+    free device blocks of every rvc_cuda context to the driver, as
+    ``VulkanContext.clear_pool`` does for the engine's output pool
+    (``runtime/vulkan_ops.py:618-633``)."""
+
+    def clear_pool(self) -> None:
+        from . import _lib  # noqa: PLC0415
+
+        _lib.release_pools()
+
+
+def patch_vc_pool_release() -> None:
+    """``VC.vc_single`` ends every conversion, in a ``finally``, with
+    ``vulkan_ops.get_context().clear_pool()`` (``runtime/vc.py:532-534``);
+    ``get_context`` raises when ``rvc_core.dll`` is missing
+    (``runtime/vulkan_ops.py:3935-3945``), which would turn every finished
+    conversion into an exception.  ``get_context`` is wrapped: the Vulkan
+    context when the engine loads, otherwise ``_DevicePool``.  Pure Python;
+    ``runtime/vc.py`` itself is unchanged."""
+    from runtime import vulkan_ops  # noqa: PLC0415
+
+    orig = vulkan_ops.get_context
+    if getattr(orig, "_rvc_cuda_pool", False):
+        return
+    pool = _DevicePool()
+
+    def get_context():
+        try:
+            return orig()
+        except Exception:  # noqa: BLE001 - no Vulkan engine: the device pool is rvc_cuda's
+            return pool
+
+    get_context._rvc_cuda_pool = True
+    get_context.__wrapped__ = orig
+    vulkan_ops.get_context = get_context

@@ -13,6 +13,7 @@ from __future__ import annotations
 import ctypes as C
 import os
 import threading
+import weakref
 
 import numpy as np
 
@@ -60,6 +61,7 @@ _SIGS = {
     "rvc_cuda_sync": ([_i64, _i32], _i32),
     "rvc_cuda_stream": ([_i64, C.POINTER(_p)], _i32),
     "rvc_cuda_set_mem_cap": ([_i64, _i64], _i32),
+    "rvc_cuda_release_pool": ([_i64], _i32),
     "rvc_cuda_alloc": ([_i64, _i64, C.POINTER(_p)], _i32),
     "rvc_cuda_free": ([_i64, _p], _i32),
     "rvc_cuda_h2d": ([_i64, _p, _p, _i64], _i32),
@@ -194,6 +196,7 @@ class Context:
         check(lib.rvc_cuda_create(int(device), C.byref(h)))
         self.handle = int(h.value)
         self.device = int(device)
+        _live.add(self)
 
     def close(self):
         if getattr(self, "handle", 0):
@@ -210,6 +213,10 @@ class Context:
 
     def set_mem_cap(self, nbytes: int):
         check(lib.rvc_cuda_set_mem_cap(self.handle, int(nbytes)))
+
+    def release_pool(self):
+        """Return this context's cached free device blocks to the driver."""
+        check(lib.rvc_cuda_release_pool(self.handle))
 
     def alloc(self, nbytes: int) -> int:
         p = _p()
@@ -262,6 +269,15 @@ class Context:
 
 _ctx_lock = threading.Lock()
 _contexts: dict = {}
+_live: "weakref.WeakSet[Context]" = weakref.WeakSet()
+
+
+def release_pools() -> None:
+    """Return the cached free device blocks of every open context of this
+    process (models' own contexts included) to the driver."""
+    for c in list(_live):
+        if getattr(c, "handle", 0):
+            c.release_pool()
 
 
 def get_context(device: int | None = None) -> Context:

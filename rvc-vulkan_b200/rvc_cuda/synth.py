@@ -246,8 +246,11 @@ class CudaSynthesizer:
         return out
 
     # ---------------------------------------------------------------- debug
-    def keep_taps(self, on: bool = True):
-        check(lib.rvc_cuda_synth_keep_taps(self.handle, 1 if on else 0))
+    def keep_taps(self, on: bool = True, chunk: Optional[int] = None):
+        """Record per-layer intermediates of the next calls: of every chunk
+        (chunk-major), or with ``chunk`` of that chunk of a batched call only."""
+        mode = 0 if not on else (1 if chunk is None else 2 + int(chunk))
+        check(lib.rvc_cuda_synth_keep_taps(self.handle, mode))
 
     def tap(self, name: str, shape) -> np.ndarray:
         out = np.empty(int(np.prod(shape)), np.float32)

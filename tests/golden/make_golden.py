@@ -412,11 +412,29 @@ PIPE_CASES = [
 ]
 
 
+def run_refruns(ref, meta):
+    """The reference's own ``SynthesizerTrn``, ``Pipeline.pipeline`` and
+    ``VC.vc_single`` on seeded weights (``reference_runs.py --backend numpy``,
+    in a child process: the operator backend is chosen once per process)."""
+    import subprocess  # noqa: PLC0415
+
+    out = os.path.join(HERE, "refruns.npz")
+    env = dict(os.environ, RVC_REFERENCE=ref)
+    subprocess.run([sys.executable, os.path.join(HERE, "reference_runs.py"), "--backend", "numpy", "--out", out],
+                   check=True, env=env)
+    sys.path.insert(0, HERE)
+    import reference_runs as rr  # noqa: PLC0415
+
+    meta["refruns"] = {"kind": "reference_runs", "seed": rr.SEED, "clip_s": rr.CLIP_S, "clip_seed": rr.CLIP_SEED,
+                       "index_n": rr.INDEX_N, "index_seed": rr.INDEX_SEED, "pipeline": rr.PIPE_KW}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("RVC_REFERENCE", ""),
                     help="checkout of the reference (default: $RVC_REFERENCE, else the oracle/_ref copy)")
-    ap.add_argument("--only", choices=["vits", "hubert", "ops", "retrieval", "rmvpe", "partial", "dsp", "ivf", "fcpe"], default=None,
+    ap.add_argument("--only", choices=["vits", "hubert", "ops", "retrieval", "rmvpe", "partial", "dsp", "ivf", "fcpe",
+                                       "refruns"], default=None,
                     help="regenerate one family and keep the other fixtures")
     args = ap.parse_args()
     if not args.ref:
@@ -466,6 +484,8 @@ def main():
         from runtime import retrieval  # noqa: PLC0415
         for c in RETRIEVAL_CASES:
             run_retrieval(retrieval, *c, meta)
+    if args.only in (None, "refruns"):
+        run_refruns(args.ref, meta)
     with open(os.path.join(HERE, "golden.json"), "w") as f:
         json.dump(meta, f, indent=1, sort_keys=True)
     print("wrote", sorted(k for k in meta if k not in ("numpy", "numba", "blas")))

@@ -189,3 +189,32 @@ def test_synth_patch_reference_replaces_full_and_partial_paths():
     assert FakeSynth._infer_partial is not FakeSynth._rvc_cuda_orig_infer_partial
     assert FakeSynth.decode_batch is not FakeSynth._rvc_cuda_orig_decode_batch
     assert FakeSynth.prep_dec is not FakeSynth._rvc_cuda_orig_prep_dec
+
+
+def test_vc_pool_release_shim_on_the_reference_module():
+    """``VC.vc_single`` ends with ``vulkan_ops.get_context().clear_pool()``
+    (``runtime/vc.py:532-534``), which raises without the Vulkan engine.  After
+    ``patch_vc_pool_release()`` the reference's own ``get_context`` (from the
+    ``oracle/_ref`` copy, in a child process) yields rvc_cuda's pool release,
+    and installing twice keeps one wrapper.  No GPU is touched: with no open
+    context the release has nothing to do."""
+    import subprocess
+    import sys
+
+    from oracle import reference as oref
+
+    if not oref.available():
+        pytest.skip("reference runtime copy not built (make -C oracle ref)")
+    code = (
+        "import sys; sys.path[:0] = [%r, %r]\n"
+        "from oracle import reference as r; r.activate('numpy')\n"
+        "from runtime import vulkan_ops as v\n"
+        "try:\n    v.get_context(); raised = False\nexcept RuntimeError:\n    raised = True\n"
+        "import rvc_cuda; rvc_cuda.patch_vc_pool_release(); rvc_cuda.patch_vc_pool_release()\n"
+        "c = v.get_context(); c.clear_pool()\n"
+        "print(raised, type(c).__name__, v.get_context.__wrapped__.__module__)\n"
+    ) % (ROOT, os.path.join(ROOT, "rvc-vulkan_b200"))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300,
+                       env=dict(os.environ, RVC_BACKEND="numpy"))
+    assert r.returncode == 0, r.stderr[-3000:]
+    assert r.stdout.split()[-3:] == ["True", "_DevicePool", "runtime.vulkan_ops"], r.stdout

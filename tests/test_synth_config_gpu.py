@@ -1,0 +1,106 @@
+"""Synthesizer parity at the configurations bench.py measures.
+
+* v2-40k, one 10 s chunk (P = 1000 frames, B = 1).
+* BASELINE config 3 as one timed step runs it: v2-48k, P = 1000, one library
+  call of B = 32 chunks (bench.py's default ``--group``).  Every kernel plan of
+  the synthesizer is a function of (B, P, layer) only: the tensor-core conv's
+  row-subtile count (``tc_plan``), the narrow column tiles of short launches
+  (``ConvLayer::run``) and the attention key split all come from those sizes,
+  so this call runs exactly the launches bench.py times.  The batch's first
+  and last chunks are compared, each through per-chunk taps.
+
+Each chunk is compared with ``oracle.vits.synth`` (the restatement of
+``SynthesizerTrn.infer_controlled``, ``runtime/models/vits.py:2551-2598``) on
+the same seeded weights, inputs and noise: waveform max-abs <= 1e-3 and
+per-layer relative L2 <= 1e-3.  The oracle runs in
+spawned worker processes while the device work proceeds.
+"""
+
+import numpy as np
+import pytest
+
+from rvc_cuda import synth  # noqa: E402  (a missing library fails the module)
+from rvc_cuda import synthetic as syn
+from tests import oracle_jobs as OJ
+from tests.conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+WAVE_TOL = 1e-3
+LAYER_TOL = 1e-3
+P = 1000
+GROUP = 32  # bench.py --group default: one call per 32 chunks
+TAPS = ["enc.embed", "enc.l0", "enc.l5", "enc.zp", "flow.z", "dec.har", "dec.pre"] + \
+       [f"dec.s{i}.{k}" for i in range(4) for k in ("ups", "out")]
+# (name, sr, weight seed, input seed, noise seed, chunk index in the call, call size)
+CASES = [("config0", 40000, 0, 9, 99, 0, 1),
+         ("config3_first", 48000, 0, 1000, 5000, 0, GROUP),
+         ("config3_last", 48000, 0, 1000 + GROUP - 1, 5000 + GROUP - 1, GROUP - 1, GROUP)]
+
+
+@pytest.fixture(scope="module")
+def oracle_runs():
+    ex = OJ.pool(len(CASES))
+    thr = OJ.threads_per_worker(len(CASES))
+    futs = {name: ex.submit(OJ.synth_chunk, sr, P, ws, i, n, TAPS, thr) for name, sr, ws, i, n, _, _ in CASES}
+    yield futs
+    ex.shutdown(wait=False, cancel_futures=True)
+
+
+def _tap_shapes(m, sr):
+    H = m.hidden
+    shp = {"enc.embed": (P, H), "enc.l0": (P, H), "enc.l5": (P, H), "enc.zp": (P, H), "flow.z": (P, H),
+           "dec.har": (P * m.upp,), "dec.pre": (P, 512)}
+    L = P
+    for i, r in enumerate(m.arch["rates"]):
+        L *= r
+        shp[f"dec.s{i}.ups"] = (L, 512 >> (i + 1))
+        shp[f"dec.s{i}.out"] = (L, 512 >> (i + 1))
+    return shp
+
+
+def _batch_inputs(B, iseed0, nseed0, upp):
+    ins = [syn.make_vits_inputs(P, iseed0 + j) for j in range(B)]
+    noise = [syn.make_vits_noise(P, upp, nseed0 + j) for j in range(B)]
+    return (np.concatenate([x[0] for x in ins]), np.concatenate([x[1] for x in ins]),
+            np.concatenate([x[2] for x in ins]), np.concatenate([x[3] for x in ins]),
+            np.concatenate([n[0] for n in noise]), np.stack([n[1].reshape(-1) for n in noise]))
+
+
+def _check(name, wav, taps_dev, oracle_runs):
+    ref_wav, ref_taps = oracle_runs[name].result(timeout=1500)
+    bad = {k: rel_l2(taps_dev[k], ref_taps[k]) for k in TAPS}
+    assert all(v <= LAYER_TOL for v in bad.values()), (name, bad)
+    err = float(np.abs(wav.reshape(-1) - ref_wav).max())
+    assert err <= WAVE_TOL, (name, err)
+
+
+def test_config0_one_10s_chunk_v2_40k(oracle_runs):
+    _, sr, ws, iseed, nseed, _, _ = CASES[0]
+    m = synth.CudaSynthesizer(syn.make_vits_weights(sr, ws), syn.vits_config_array(sr))
+    phone, pitch, nsff0, sid = syn.make_vits_inputs(P, iseed)
+    nz, ns = syn.make_vits_noise(P, m.upp, nseed)
+    m.keep_taps(True)
+    wav = m.infer_controlled(phone, pitch, nsff0, sid, nz, ns)
+    assert wav.shape == (1, 1, 400000)
+    taps = {k: m.tap(k, s) for k, s in _tap_shapes(m, sr).items()}
+    m.close()
+    _check("config0", wav, taps, oracle_runs)
+
+
+def test_config3_batch_of_32_as_bench_runs_it(oracle_runs):
+    sr = 48000
+    m = synth.CudaSynthesizer(syn.make_vits_weights(sr, 0), syn.vits_config_array(sr))
+    args = _batch_inputs(GROUP, 1000, 5000, m.upp)
+    shapes = _tap_shapes(m, sr)
+    waves, taps = [], []
+    for chunk in (0, GROUP - 1):
+        m.keep_taps(True, chunk=chunk)
+        waves.append(m.infer_batch(*args))
+        taps.append({k: m.tap(k, s) for k, s in shapes.items()})
+    m.keep_taps(False)
+    m.close()
+    assert waves[0].shape == (GROUP, 480000)
+    np.testing.assert_array_equal(waves[0], waves[1])  # same call twice: deterministic
+    _check("config3_first", waves[0][0], taps[0], oracle_runs)
+    _check("config3_last", waves[0][GROUP - 1], taps[1], oracle_runs)
