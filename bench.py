@@ -1018,7 +1018,8 @@ def run_ours(args, world, rank, local):
     upp, H, D = m.upp, m.hidden, m.arch["phone_dim"]
     assert args.chunks % world == 0, "chunks must split evenly across ranks"
     n_local = args.chunks // world
-    ids = list(range(rank * n_local, (rank + 1) * n_local))
+    from rvc_cuda.multi import shard
+    ids = shard(args.chunks, world, rank)  # contiguous chunk range of this rank
     n_unique = min(args.unique, n_local)
     ins, noise = make_inputs(n_unique, P, upp)
 

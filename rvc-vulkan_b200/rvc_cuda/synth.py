@@ -267,7 +267,10 @@ def patch_reference(vits_module=None, device: Optional[int] = None, precision: s
     The class methods are replaced, not the loader, because ``runtime/vc.py``
     imports the loaders by name.  A device model is built once per
     ``SynthesizerTrn`` instance and cached on it; ``vc.get_vc`` builds a new
-    instance on model switch, which drops the old cache with it.
+    instance on model switch, which drops the old cache with it.  When
+    ``RVC_CUDA_DEVICES`` names several GPUs (and no ``device`` is given) the
+    device model is a ``rvc_cuda.multi.SynthPool`` over them: the pipeline's
+    batched decode then spreads its chunks over the devices.
     """
     if vits_module is None:
         from runtime.models import vits as vits_module  # noqa: PLC0415
@@ -275,26 +278,24 @@ def patch_reference(vits_module=None, device: Optional[int] = None, precision: s
     if getattr(cls, "_rvc_cuda_patched", False):
         return cls
 
-    def infer_controlled(self, phone, pitch, nsff0, sid, nz, ns, phone_gpu=None, _defer=False):
-        m = self.__dict__.get("_rvc_cuda_model")
-        if m is None:
-            m = CudaSynthesizer.from_reference(self, device=device, precision=precision)
-            self.__dict__["_rvc_cuda_model"] = m
-        return m.infer_controlled(phone, pitch, nsff0, sid, nz, ns, _defer=_defer)
-
-    def _infer_partial(self, phone, pitch, nsff0, sid, nz, ns, head, length, phone_gpu=None):
-        m = self.__dict__.get("_rvc_cuda_model")
-        if m is None:
-            m = CudaSynthesizer.from_reference(self, device=device, precision=precision)
-            self.__dict__["_rvc_cuda_model"] = m
-        return m.infer_partial(phone, pitch, nsff0, sid, nz, ns, int(head), int(length))
-
     def _model(self):
         m = self.__dict__.get("_rvc_cuda_model")
         if m is None:
-            m = CudaSynthesizer.from_reference(self, device=device, precision=precision)
+            from .multi import SynthPool, devices_from_env  # noqa: PLC0415
+
+            devs = devices_from_env() if device is None else [device]
+            if len(devs) > 1:
+                m = SynthPool.from_reference(self, devices=devs, precision=precision)
+            else:
+                m = CudaSynthesizer.from_reference(self, device=devs[0], precision=precision)
             self.__dict__["_rvc_cuda_model"] = m
         return m
+
+    def infer_controlled(self, phone, pitch, nsff0, sid, nz, ns, phone_gpu=None, _defer=False):
+        return _model(self).infer_controlled(phone, pitch, nsff0, sid, nz, ns, _defer=_defer)
+
+    def _infer_partial(self, phone, pitch, nsff0, sid, nz, ns, head, length, phone_gpu=None):
+        return _model(self).infer_partial(phone, pitch, nsff0, sid, nz, ns, int(head), int(length))
 
     def prep_dec(self, phone, pitch, nsff0, sid, seed=None, skip_head=None, return_length=None, phone_gpu=None):
         return _model(self).prep_dec(phone, pitch, nsff0, sid, seed, skip_head, return_length)

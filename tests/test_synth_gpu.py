@@ -187,3 +187,25 @@ def test_prep_dec_decode_batch_ragged_and_partial():
     pp = preps[3]
     ref = m.infer_partial(*ins[2], pp["nz"], pp["ns"], 10, 12)
     assert np.abs(waves[3] - ref).max() <= 1e-4
+
+
+def test_synth_pool_matches_one_device():
+    """``rvc_cuda.multi.SynthPool`` (the multi-GPU entry of the pipeline and of
+    ``patch_reference`` under ``RVC_CUDA_DEVICES``): chunks spread over the
+    devices (two GPUs when present, else two models on GPU 0) come back in
+    order, equal to one device's ``decode_batch`` up to fp32 rounding (the
+    batch sizes per call differ, and with them the kernel plans)."""
+    from rvc_cuda import _lib
+    from rvc_cuda.multi import SynthPool
+
+    w, m = model(40000, 0)
+    devs = [0, 1] if _lib.device_count() >= 2 else [0, 0]
+    pool = SynthPool(w, syn.vits_config_array(40000), devices=devs)
+    ins = [syn.make_vits_inputs(P, 60 + i) for i, P in enumerate((48, 20, 48, 33, 48))]
+    preps = [m.prep_dec(*x, seed=300 + i) for i, x in enumerate(ins)]
+    got = pool.decode_batch(preps)
+    ref = m.decode_batch(preps)
+    assert [g.shape for g in got] == [r.shape for r in ref]
+    for g, r in zip(got, ref):
+        assert np.abs(g - r).max() <= 1e-4
+    pool.close()
