@@ -1140,6 +1140,54 @@ def run_ours(args, world, rank, local):
         dist.destroy_process_group()
 
 
+def run_layer(args):
+    """Single-GPU layer cases for timing and ncu captures (one process, no JSON
+    line): ``--layer conv`` runs ``rvc_cuda.ops.conv1d`` on [1,C,T] ("same"
+    padding, dilation --dil), ``synth`` ``CudaSynthesizer.infer_batch`` on
+    --batch seeded chunks of --frames frames, ``hubert`` ``CudaHubert.encode_equal``
+    on --batch chunks of --samples samples; each --reps times, printing the wall
+    time of the last."""
+    from rvc_cuda import synthetic as syn
+    rs = np.random.RandomState(0)
+    if args.layer == "conv":
+        from rvc_cuda import ops
+        C, K, T, d = args.C, args.K, args.T, args.dil
+        x = rs.standard_normal((1, C, T)).astype(np.float32)
+        w = (rs.standard_normal((C, C, K)) / np.sqrt(C * K)).astype(np.float32)
+        b = rs.standard_normal(C).astype(np.float32)
+        for _ in range(args.reps):
+            t0 = time.perf_counter()
+            y = ops.conv1d(x, w, b, 1, (K - 1) * d // 2, d)
+            dt = time.perf_counter() - t0
+        print(f"conv C={C} K={K} dil={d} T={T}: {dt * 1e3:.2f} ms (host API, incl. copies) "
+              f"mean|y|={np.abs(y).mean():.4f}")
+    elif args.layer == "synth":
+        from rvc_cuda.synth import CudaSynthesizer
+        m = CudaSynthesizer(syn.make_vits_weights(args.sr, 0), syn.vits_config_array(args.sr))
+        B, P = args.batch, args.frames
+        ins = [syn.make_vits_inputs(P, i) for i in range(B)]
+        noise = [syn.make_vits_noise(P, m.upp, 50 + i) for i in range(B)]
+        a = (np.concatenate([i[0] for i in ins]), np.concatenate([i[1] for i in ins]),
+             np.concatenate([i[2] for i in ins]), np.concatenate([i[3] for i in ins]),
+             np.concatenate([n[0] for n in noise]), np.stack([n[1].reshape(-1) for n in noise]))
+        for _ in range(args.reps):
+            t0 = time.perf_counter()
+            out = m.infer_batch(*a)
+            dt = time.perf_counter() - t0
+        print(f"synth sr={args.sr} B={B} P={P}: {dt * 1e3:.2f} ms, {B * P * m.upp / args.sr / dt:.1f}x realtime, "
+              f"std={out.std():.4f}")
+    else:
+        from rvc_cuda.hubert import CudaHubert
+        m = CudaHubert(syn.make_hubert_weights(0))
+        x = np.concatenate([syn.make_hubert_input(args.samples, i) for i in range(args.batch)], axis=0)
+        for _ in range(args.reps):
+            t0 = time.perf_counter()
+            y = m.encode_equal(x)
+            dt = time.perf_counter() - t0
+        print(f"hubert B={args.batch} T={args.samples}: {dt * 1e3:.2f} ms, "
+              f"{args.batch * args.samples / 16000 / dt:.1f}x realtime, std={y.std():.4f}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1158,17 +1206,27 @@ def main():
     ap.add_argument("--no-config0", action="store_true", help="skip the v2-40k config-0 figure")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--profile-out", default="", help="write the per-layer conv profile (CSV) here")
-    ap.add_argument("--workload", default="synth", choices=["synth", "hubert", "retrieval", "rmvpe", "pipeline"],
+    ap.add_argument("--layer", default="conv", choices=["conv", "synth", "hubert"], help="--workload layer: the case")
+    ap.add_argument("--C", type=int, default=32, help="layer conv: channels")
+    ap.add_argument("--K", type=int, default=3, help="layer conv: kernel size")
+    ap.add_argument("--T", type=int, default=1920000, help="layer conv: time steps")
+    ap.add_argument("--dil", type=int, default=1, help="layer conv: dilation")
+    ap.add_argument("--batch", type=int, default=2, help="layer synth / hubert: chunks per call")
+    ap.add_argument("--reps", type=int, default=2, help="layer: repetitions")
+    ap.add_argument("--workload", default="synth",
+                    choices=["synth", "hubert", "retrieval", "rmvpe", "pipeline", "layer"],
                     help="synth: config 3 (headline); hubert: config 1 (HuBERT-base encoder); "
                          "retrieval: config 4's top-8 search + blend; rmvpe: config 2; "
-                         "pipeline: config 4 end to end")
+                         "pipeline: config 4 end to end; layer: one layer case for timing / ncu (--layer)")
     ap.add_argument("--slice-length", type=float, default=0.0, help="pipeline: slice_length (0 = config default)")
     ap.add_argument("--samples", type=int, default=160000, help="hubert / rmvpe: samples per chunk")
     ap.add_argument("--audio-s", type=float, default=60.0, help="retrieval: seconds of frames (50 per s)")
     ap.add_argument("--index-rows", type=int, default=200000, help="retrieval: index rows")
     args = ap.parse_args()
     world, rank, local = dist_setup()
-    if args.workload == "pipeline":
+    if args.workload == "layer":
+        run_layer(args)
+    elif args.workload == "pipeline":
         if args.impl == "reference":
             run_pipeline_reference(args, world, rank)
         else:

@@ -206,7 +206,8 @@ def to_int16_device(ctx, d_x: int, n: int, d_y: int):
 
 def patch_reference(pipeline_module=None):
     """Route ``runtime.pipeline``'s ``change_rms``, ``interpolate_linear``,
-    ``resample`` and ``signal.filtfilt`` to the device versions."""
+    ``resample``, ``signal.filtfilt`` and the pm f0 (``f0_autocorrelation``,
+    imported there by name, ``runtime/pipeline.py:40``) to the device versions."""
     if pipeline_module is None:
         from runtime import pipeline as pipeline_module  # noqa: PLC0415
     if getattr(pipeline_module, "_rvc_cuda_patched_dsp", False):
@@ -229,5 +230,8 @@ def patch_reference(pipeline_module=None):
     if hasattr(pipeline_module, "resample"):
         pipeline_module._rvc_cuda_orig_resample = pipeline_module.resample
         pipeline_module.resample = resample
+    if hasattr(pipeline_module, "f0_autocorrelation"):
+        pipeline_module._rvc_cuda_orig_f0_autocorrelation = pipeline_module.f0_autocorrelation
+        pipeline_module.f0_autocorrelation = f0_autocorrelation
     pipeline_module._rvc_cuda_patched_dsp = True
     return pipeline_module

@@ -425,8 +425,34 @@ def run_refruns(ref, meta):
     sys.path.insert(0, HERE)
     import reference_runs as rr  # noqa: PLC0415
 
+    runs = np.load(out)
+    for case in ("pipeline", "vc"):
+        gap, coarse = runs[case + "_margins"]
+        if not (gap >= rr.MIN_RET_GAP and coarse >= rr.MIN_COARSE_MARGIN):
+            raise SystemExit(f"refruns: the {case} case has a decision margin below the bar "
+                             f"(retrieval gap {gap}, coarse {coarse}); change its inputs")
     meta["refruns"] = {"kind": "reference_runs", "seed": rr.SEED, "clip_s": rr.CLIP_S, "clip_seed": rr.CLIP_SEED,
                        "index_n": rr.INDEX_N, "index_seed": rr.INDEX_SEED, "pipeline": rr.PIPE_KW}
+
+
+def run_config4(ref, meta):
+    """The reference's ``Pipeline.pipeline`` on config 4's 60 s clip with its
+    own numpy models (``reference_runs.py --cases config4``, ~10 minutes)."""
+    import subprocess  # noqa: PLC0415
+
+    out = os.path.join(HERE, "config4.npz")
+    env = dict(os.environ, RVC_REFERENCE=ref)
+    subprocess.run([sys.executable, os.path.join(HERE, "reference_runs.py"), "--backend", "numpy", "--out", out,
+                    "--cases", "config4"], check=True, env=env)
+    sys.path.insert(0, HERE)
+    import reference_runs as rr  # noqa: PLC0415
+
+    gap, coarse = np.load(out)["config4_margins"]
+    if not (gap >= rr.MIN_RET_GAP and coarse >= rr.MIN_COARSE_MARGIN):
+        raise SystemExit(f"config4: a decision margin is below the bar (retrieval gap {gap}, coarse {coarse})")
+    meta["config4"] = {"kind": "reference_runs", "seconds": rr.C4_SECONDS, "seed": rr.C4_SEED,
+                       "stride": rr.C4_STRIDE, "index_n": rr.INDEX_N, "index_seed": rr.INDEX_SEED,
+                       "fixed_seed": rr.SEED, "pipeline": rr.config4_kwargs()}
 
 
 def main():
@@ -434,7 +460,7 @@ def main():
     ap.add_argument("--ref", default=os.environ.get("RVC_REFERENCE", ""),
                     help="checkout of the reference (default: $RVC_REFERENCE, else the oracle/_ref copy)")
     ap.add_argument("--only", choices=["vits", "hubert", "ops", "retrieval", "rmvpe", "partial", "dsp", "ivf", "fcpe",
-                                       "refruns"], default=None,
+                                       "refruns", "config4"], default=None,
                     help="regenerate one family and keep the other fixtures")
     args = ap.parse_args()
     if not args.ref:
@@ -486,6 +512,8 @@ def main():
             run_retrieval(retrieval, *c, meta)
     if args.only in (None, "refruns"):
         run_refruns(args.ref, meta)
+    if args.only in (None, "config4"):
+        run_config4(args.ref, meta)
     with open(os.path.join(HERE, "golden.json"), "w") as f:
         json.dump(meta, f, indent=1, sort_keys=True)
     print("wrote", sorted(k for k in meta if k not in ("numpy", "numba", "blas")))

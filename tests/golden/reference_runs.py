@@ -25,7 +25,9 @@ Cases:
 * ``pipeline``: ``Pipeline.pipeline`` (``runtime/pipeline.py:697``) with the
   reference's HubertEncoder, RMVPE and SynthesizerTrn and a FeatureIndex.
 * ``vc``: ``VC.get_vc`` + ``VC.vc_single`` (``runtime/vc.py:332``, ``:440``) on a
-  WAV file, through to the int16 output.
+  WAV file, through to the int16 output (pm f0).
+* ``config4``: ``Pipeline.pipeline`` on BASELINE config 4's 60 s clip (numpy
+  only: the fixture for the device pipeline's 60 s test).
 """
 
 from __future__ import annotations
@@ -48,8 +50,13 @@ from rvc_cuda import synthetic as syn  # noqa: E402
 
 SEED = 1234               # RVC_FIXED_SEED: the synthesizer noise of every chunk
 CLIP_S, CLIP_SEED = 2.5, 21
-INDEX_N, INDEX_SEED = 2000, 5
-PIPE_KW = dict(f0_up_key=1, f0_method="rmvpe", index_rate=0.75, if_f0=1, tgt_sr=40000, resample_sr=0,
+# 8 index rows: k = 8 takes them all (runtime/retrieval.py:35-82 with N <= k),
+# so the blend weights are continuous in the features and no top-k decision
+# is left to a float near-tie; top-k selection at scale has its own tests.
+INDEX_N, INDEX_SEED = 8, 5
+# f0_up_key 5: every coarse-pitch decision of this clip is >= 0.027 bins from
+# a rounding point (the random-init RMVPE gives a few distinct f0 values)
+PIPE_KW = dict(f0_up_key=5, f0_method="rmvpe", index_rate=0.75, if_f0=1, tgt_sr=40000, resample_sr=0,
                rms_mix_rate=0.25, version="v2", protect=0.33)
 
 
@@ -122,6 +129,54 @@ def _index():
     return idx
 
 
+# The pipeline makes two discrete decisions on float data: the top-8 set of
+# each retrieval query (runtime/pipeline.py:547) and the coarse pitch bin,
+# rint of a mel-scaled f0 (:477-482).  Float paths that agree to ~1e-5 can
+# still land on opposite sides of a decision whose margin is that small, and
+# a changed neighbour or pitch bin reaches every frame of the chunk through
+# the text encoder's attention.  The runs record each decision's smallest
+# margin, computed in float64 from their own inputs, and the test inputs are
+# chosen so that every margin is far above the float paths' differences.
+MIN_RET_GAP = 0.1        # squared-distance gap between the 8th and 9th neighbour
+MIN_COARSE_MARGIN = 1e-3  # distance of the scaled mel f0 from a rounding point, in bins
+
+
+def _record_margins():
+    """Wraps ``runtime.pipeline.search_l2`` and ``Pipeline.get_f0``; returns a
+    function that removes the wrappers and gives (retrieval gap, coarse margin)."""
+    from runtime import pipeline as rp  # noqa: PLC0415
+
+    st = {"gap": np.inf, "coarse": np.inf}
+    orig_search, orig_f0 = rp.search_l2, rp.Pipeline.get_f0
+
+    def search_l2(q, vecs, k=8):
+        r = orig_search(q, vecs, k=k)
+        q64, v64 = np.asarray(q, np.float64), np.asarray(vecs, np.float64)
+        if v64.shape[0] > k:
+            d = (q64 * q64).sum(1)[:, None] + (v64 * v64).sum(1)[None, :] - 2.0 * (q64 @ v64.T)
+            part = np.sort(np.partition(d, k, axis=1)[:, :k + 1], axis=1)
+            st["gap"] = min(st["gap"], float((part[:, k] - part[:, k - 1]).min()))
+        return r
+
+    def get_f0(self, x, p_len, f0_up_key, f0_method, *a, **kw):
+        coarse, f0bak = orig_f0(self, x, p_len, f0_up_key, f0_method, *a, **kw)
+        mel = 1127.0 * np.log(1.0 + np.asarray(f0bak, np.float64) / 700.0)
+        lo, hi = 1127.0 * np.log(1.0 + 50.0 / 700.0), 1127.0 * np.log(1.0 + 1100.0 / 700.0)
+        m = (mel[mel > 0] - lo) * 254.0 / (hi - lo) + 1.0
+        m = m[(m > 1.0) & (m < 255.0)]
+        if m.size:
+            st["coarse"] = min(st["coarse"], float(np.abs(m - np.floor(m) - 0.5).min()))
+        return coarse, f0bak
+
+    rp.search_l2, rp.Pipeline.get_f0 = search_l2, get_f0
+
+    def done():
+        rp.search_l2, rp.Pipeline.get_f0 = orig_search, orig_f0
+        return st["gap"], st["coarse"]
+
+    return done
+
+
 def _case_pipeline(out):
     from oracle import reference as oref  # noqa: PLC0415
     from runtime.native_config import Config  # noqa: PLC0415
@@ -131,9 +186,13 @@ def _case_pipeline(out):
     audio = syn.make_speech_audio(CLIP_S, seed=CLIP_SEED, silence_every=1.2)
     pipe = Pipeline(40000, Config())
     pipe.model_rmvpe = oref.rmvpe(syn.make_rmvpe_weights(0))
-    sr, y = pipe.pipeline(hub, net, 0, audio, [0.0, 0.0, 0.0], PIPE_KW["f0_up_key"], PIPE_KW["f0_method"], _index(),
-                          PIPE_KW["index_rate"], PIPE_KW["if_f0"], PIPE_KW["tgt_sr"], PIPE_KW["resample_sr"],
-                          PIPE_KW["rms_mix_rate"], PIPE_KW["version"], PIPE_KW["protect"])
+    done = _record_margins()
+    try:
+        sr, y = pipe.pipeline(hub, net, 0, audio, [0.0, 0.0, 0.0], PIPE_KW["f0_up_key"], PIPE_KW["f0_method"],
+                              _index(), PIPE_KW["index_rate"], PIPE_KW["if_f0"], PIPE_KW["tgt_sr"],
+                              PIPE_KW["resample_sr"], PIPE_KW["rms_mix_rate"], PIPE_KW["version"], PIPE_KW["protect"])
+    finally:
+        out["pipeline_margins"] = np.array(done(), np.float64)
     out["pipeline_sr"] = np.array(sr)
     out["pipeline_int16"] = np.asarray(y)
 
@@ -202,19 +261,60 @@ def _case_vc(out):
         info = v.get_vc(os.path.join(d, "model.pth"))
         if not info["success"]:
             raise RuntimeError(info.get("traceback") or info["error"])
-        msg, (sr, y) = v.vc_single(0, wav_path, 0, "rmvpe", idx_path, 0.75, 0, 0.25, 0.33)
+        done = _record_margins()
+        try:
+            msg, (sr, y) = v.vc_single(0, wav_path, 0, "pm", idx_path, 0.75, 0, 0.25, 0.33)
+        finally:
+            out["vc_margins"] = np.array(done(), np.float64)
     out["vc_sr"] = np.array(sr)
     out["vc_int16"] = np.asarray(y)
 
 
-CASES = {"ops": _case_ops, "synth": _case_synth, "pipeline": _case_pipeline, "vc": _case_vc}
+# BASELINE config 4 at its full 60 s: the speech-like clip, RMVPE f0, HuBERT,
+# retrieval at index_rate 0.75, protect 0.33, v2-40k synthesizer, rms mix
+# 0.25, default split (two chunks near 38 s).  The index has 8 rows (no top-k
+# near-ties, see INDEX_N) and f0_up_key 9 keeps every coarse-pitch decision of
+# this clip >= 0.04 bins from a rounding point.
+C4_SECONDS, C4_SEED, C4_KEY, C4_STRIDE = 60.0, 0, 9, 11
+
+
+def config4_kwargs():
+    return dict(f0_up_key=C4_KEY, f0_method="rmvpe", index_rate=0.75, if_f0=1, tgt_sr=40000, resample_sr=0,
+                rms_mix_rate=0.25, version="v2", protect=0.33)
+
+
+def _case_config4(out):
+    from oracle import reference as oref  # noqa: PLC0415
+    from runtime.native_config import Config  # noqa: PLC0415
+    from runtime.pipeline import Pipeline  # noqa: PLC0415
+
+    hub, net = _models()
+    audio = syn.make_speech_audio(C4_SECONDS, seed=C4_SEED)
+    pipe = Pipeline(40000, Config())
+    pipe.model_rmvpe = oref.rmvpe(syn.make_rmvpe_weights(0))
+    kw = config4_kwargs()
+    done = _record_margins()
+    try:
+        sr, y = pipe.pipeline(hub, net, 0, audio, [0.0, 0.0, 0.0], kw["f0_up_key"], kw["f0_method"], _index(),
+                              kw["index_rate"], kw["if_f0"], kw["tgt_sr"], kw["resample_sr"], kw["rms_mix_rate"],
+                              kw["version"], kw["protect"])
+    finally:
+        out["config4_margins"] = np.array(done(), np.float64)
+    y = np.asarray(y)
+    out["config4_len"] = np.array(y.size)
+    out["config4_int16_every"] = y[::C4_STRIDE].copy()
+
+
+CASES = {"ops": _case_ops, "synth": _case_synth, "pipeline": _case_pipeline, "vc": _case_vc,
+         "config4": _case_config4}
+FIXTURE_CASES = "ops,synth,pipeline,vc"
 
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--backend", choices=["numpy", "cuda"], required=True)
     ap.add_argument("--out", required=True)
-    ap.add_argument("--cases", default=",".join(CASES))
+    ap.add_argument("--cases", default=FIXTURE_CASES)
     args = ap.parse_args(argv)
     os.environ["RVC_BACKEND"] = args.backend
     os.environ["RVC_FIXED_SEED"] = str(SEED)

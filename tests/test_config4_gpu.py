@@ -1,0 +1,54 @@
+"""BASELINE config 4 at its full length: 60 s through the device pipeline.
+
+``rvc_cuda.pipeline.Pipeline`` (the path ``bench.py --workload pipeline``
+times: high-pass, silence split at the default x_center = 38 s into two
+chunks, RMVPE f0, HuBERT, retrieval blend at index_rate 0.75, x2
+interpolation, protect 0.33, v2-40k synthesizer, change_rms 0.25, int16) on
+config 4's 60 s speech-like clip, with its HuBERT, RMVPE, synthesizer and
+index on the device and the chunk chain resident in HBM, against the
+reference's own ``Pipeline.pipeline`` with its numpy models on the same
+seeded weights, clip and noise (``tests/golden/config4.npz``, made by
+``make_golden.py --only config4``; every 11th output sample is stored).
+
+Bar: same output length, int16 within 33 LSB (1e-3 of full scale).  The
+index has 8 rows, so k = 8 takes them all and no top-k choice rests on a
+float near-tie, and f0_up_key 9 keeps every coarse-pitch decision of this
+clip >= 0.04 bins from a rounding point: a neighbour or pitch bin that flips
+on a tie would reach every frame of its chunk through the text encoder's
+attention.  Top-8 selection against the full 200000 x 768 index is tested on
+config 4's 3000 queries in ``test_retrieval_gpu.py``.
+"""
+
+import numpy as np
+import pytest
+
+from rvc_cuda import pipeline as P  # noqa: E402  (a missing library fails the module)
+from rvc_cuda import synthetic as syn
+from tests.conftest import load_golden
+from tests.golden import pipeline_fakes as pf
+from tests.golden import reference_runs as rr
+
+pytestmark = pytest.mark.gpu
+
+
+def test_config4_60s_device_pipeline_matches_reference(monkeypatch):
+    from rvc_cuda.hubert import CudaHubert
+    from rvc_cuda.retrieval import CudaIndex
+    from rvc_cuda.rmvpe import CudaRmvpe
+    from rvc_cuda.synth import CudaSynthesizer
+
+    monkeypatch.setenv("RVC_FIXED_SEED", str(rr.SEED))
+    gold = load_golden("config4")
+    audio = syn.make_speech_audio(rr.C4_SECONDS, seed=rr.C4_SEED)
+    hub = CudaHubert(syn.make_hubert_weights(0))
+    net = CudaSynthesizer(syn.make_vits_weights(40000, 0), syn.vits_config_array(40000))
+    index = CudaIndex(syn.make_index(rr.INDEX_N, 768, rr.INDEX_SEED))
+    pipe = P.Pipeline(40000, pf.config())
+    pipe.model_rmvpe = CudaRmvpe(syn.make_rmvpe_weights(0), own_stream=True)
+    assert pipe._device_chain(hub, net, index) is hub.ctx  # the HBM-resident chain bench.py times
+    sr, out = pipe.pipeline(hub, net, 0, audio, [0.0, 0.0, 0.0], file_index=index, **rr.config4_kwargs())
+    assert sr == 40000 and out.dtype == np.int16
+    assert out.size == int(gold["config4_len"])
+    got = out[::rr.C4_STRIDE].astype(np.int32)
+    err = np.abs(got - gold["config4_int16_every"].astype(np.int32))
+    assert err.max() <= 33, (int(err.max()), float((err > 33).mean()))

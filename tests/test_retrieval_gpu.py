@@ -52,20 +52,33 @@ def _check_against_oracle(ix, sc, rix, rsc, tie_tol=1e-3):
 
 
 def test_config4_index_size_against_oracle():
-    """BASELINE config 4 index (200000 x 768 ~N(0,1)), 256 queries."""
+    """BASELINE config 4's retrieval: 3000 queries (60 s of 50 Hz frames)
+    against the 200000 x 768 ~N(0,1) index, top-8 + blend at index_rate 0.75.
+    Indices equal the oracle's except where the oracle's own fp32 distances
+    make a near-tie (the oracle's 9th neighbour is taken too, so a swap across
+    the 8th / 9th boundary is recognised); the blend of every row without such
+    a swap matches (rel 1e-5), and swapped rows stay a small minority."""
     db = syn.make_index(200000, 768, 7)
-    q = syn.make_queries(256, 768, 7)
+    q = syn.make_queries(3000, 768, 7)
     idx = ret.CudaIndex(db)
     sc, ix = idx.search(q, 8)
-    rsc, rix = OR.search_l2(q, db, 8)
-    ndiff = _check_against_oracle(ix, sc, rix, rsc)
-    assert ndiff <= 2
-    feats = syn.make_queries(256, 768, 8)
+    rsc9, rix9 = OR.search_l2(q, db, 9)
+    rsc, rix = rsc9[:, :8], rix9[:, :8]
+    swapped = np.zeros(len(q), bool)
+    for r in np.flatnonzero((ix != rix).any(axis=1)):
+        swapped[r] = True
+        row = dict(zip(rix9[r].tolist(), rsc9[r].tolist()))
+        for j in np.flatnonzero(ix[r] != rix[r]):
+            a, b = int(ix[r, j]), int(rix[r, j])
+            assert a in row, f"row {r}: index {a} is not among the oracle's 9 nearest"
+            assert abs(row[a] - row[b]) <= 1e-3, f"row {r} pos {j}: {a} vs {b} is not a near-tie"
+    keep = ~swapped
+    np.testing.assert_allclose(sc[keep], rsc[keep], rtol=1e-6, atol=1e-3)
+    assert swapped.sum() <= len(q) // 100, int(swapped.sum())
+    feats = syn.make_queries(3000, 768, 8)
     got = idx.blend(q, 8, feats=feats, index_rate=0.75)
-    blended = OR.blend(q, db, 8)
-    ref = OR.mix(feats, blended, 0.75)
-    if ndiff == 0:
-        np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-5)
+    ref = OR.mix(feats, OR.blend(q, db, 8), 0.75)
+    np.testing.assert_allclose(got[keep], ref[keep], rtol=1e-5, atol=1e-5)
 
 
 def test_k_range_simt_path_and_ties():
