@@ -100,5 +100,15 @@ bool tc_shape_ok(int C_in, int C_out);
 __host__ __device__ __forceinline__ bool tc_stacked(int bn) { return bn <= 64; }
 int tc_pick_bn(int C_out);
 int tc_pick_cb(int C_in);
+// Time-rows-as-N tensor-core conv (tcn_conv.cu): one slice, stride 1, dilated
+// taps, C_in % 32 == 0, C_out == 32, 64 or a multiple of 128.
+bool tcn_shape_ok(const ConvArgs& a);
+// tcn_shape_ok and a pipeline plan that fits in shared memory
+bool tcn_fits(const ConvArgs& a);
+size_t tcn_packed_elems(int taps, int C_in, int C_out);
+void launch_tcn_pack(const float* w, uint16_t* out, int taps, int C_in, int C_out, cudaStream_t st);
+void launch_tcn_conv(const ConvArgs& a, cudaStream_t st);
+// True unless RVC_CUDA_TCN=0 (read once): the time-as-N kernel is used where it applies.
+bool tcn_enabled();
 
 }  // namespace rvc

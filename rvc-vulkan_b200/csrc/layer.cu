@@ -77,6 +77,14 @@ void ConvLayer::build(Context* ctx, LayerKind k, const float* W, const float* b,
     wpk = DevBuf(ctx, sizeof(uint16_t) * tc_packed_elems(taps_total, C_in, C_out, bn, cb));
     launch_tc_pack(Wg.f(), wpk.as<uint16_t>(), taps_total, C_in, C_out, bn, cb, st);
   }
+  // square convs of the generator (ResBlocks: C_in == C_out) also get the
+  // operand stages of the time-rows-as-N kernel
+  tn = tc && k == LayerKind::kConv && groups == 1 && dil >= 1 && C_in == C_out && C_in % 32 == 0 &&
+       (C_out == 32 || C_out == 64 || C_out % 128 == 0);
+  if (tn) {
+    wpk_t = DevBuf(ctx, sizeof(uint16_t) * tcn_packed_elems(taps_total, C_in, C_out));
+    launch_tcn_pack(Wg.f(), wpk_t.as<uint16_t>(), taps_total, C_in, C_out, st);
+  }
   RVC_CUDA_TRY(cudaStreamSynchronize(st));  // `taps` is freed on return
 }
 
@@ -125,6 +133,29 @@ void ConvLayer::run(Context* ctx, const ConvIO& io, bool force_simt) const {
   for (int s = 0; s < a.nslices; ++s) any_empty |= a.sl[s].ntaps == 0;
   const bool use_tc = tc && !force_simt && !any_empty && (io.x_ld % 4 == 0) && (io.x_bs % 4 == 0);
   RVC_CHECK_ARG(use_tc || Wg.p, "conv: fp32 weights were released; only the tensor-core path can run this layer");
+  // Time rows as the MMA's N (tcn_conv.cu) where it measured faster than the
+  // time-rows-as-M kernel (B200, the v2-48k generator at 32 chunks per call):
+  // C >= 128 always (K = 11: 4.3 -> 2.9 ms per launch); C = 64 for K >= 7
+  // (K = 11: 3.8 -> 3.1 ms; K = 3: 1.5 -> 2.5 ms); C = 32 only for K >= 11
+  // without residual / accumulator inputs (3.4 -> 2.7 ms).  At least one wave
+  // of 256-row tiles.
+  const bool tn_pick = C_out >= 128 || (C_out == 64 && K >= 7) || (C_out == 32 && K >= 11 && !io.res && !io.accin);
+  if (use_tc && tn && tn_pick && tcn_enabled() && ((uintptr_t)io.x & 15) == 0 && tcn_fits(a)) {
+    const long long tiles = (long long)io.B * cdiv(a.sl[0].rows, 256) * (C_out <= 64 ? 1 : C_out / 128);
+    if (tiles >= ctx->num_sms()) {
+      a.wpk = wpk_t.as<uint16_t>();
+      cudaEvent_t e0 = nullptr, e1 = nullptr;
+      if (ctx->prof) ctx->prof_begin(&e0, &e1);
+      launch_tcn_conv(a, ctx->stream);
+      if (ctx->prof) {
+        char lab[160];
+        snprintf(lab, sizeof(lab), "tcn conv Cin=%d Cout=%d K=%d dil=%d T=%d B=%d", C_in, C_out, K, dil, io.T_in,
+                 io.B);
+        ctx->prof_end(e0, e1, flops(io.B, io.T_in), lab);
+      }
+      return;
+    }
+  }
   if (use_tc) {
     // Few row tiles even at one 128-row subtile per tile: narrower column
     // tiles (the same weights repacked once) put more SMs to work.  Each

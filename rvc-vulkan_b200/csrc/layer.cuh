@@ -43,6 +43,9 @@ struct ConvLayer {
   // short sequence), packed from wpk on first use
   mutable DevBuf wpk_n;
   mutable int bn_n = 0;
+  // operand stages of the time-rows-as-N kernel (tcn_conv.cu), for convs it takes
+  DevBuf wpk_t;
+  bool tn = false;
 
   // W: conv [O,I,K] (I = input channels per group) or convT [I,O,K], device
   // fp32 (already weight-norm folded).

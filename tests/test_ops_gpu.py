@@ -42,6 +42,27 @@ def test_conv1d(case):
     np.testing.assert_allclose(y, ref, rtol=2e-4, atol=2e-4)
 
 
+# Long square convs: these take the time-rows-as-N kernel (tcn_conv.cu; at
+# least one wave of 256-row tiles): C = 32 (tap pairs stacked with the split),
+# 64 (stacked hi/lo weight rows), 128 and 256 (hi and lo planes, two channel
+# tiles), odd and even tap counts, dilations, ragged last tiles.
+CONV_TCN = [(1, 64, 40000, 3, 1, 1), (1, 64, 40001, 11, 25, 5), (1, 128, 40000, 7, 9, 3),
+            (2, 256, 19000, 3, 1, 1), (1, 128, 38000, 11, 5, 1),
+            (1, 32, 40000, 3, 1, 1), (1, 32, 40003, 11, 25, 5), (2, 32, 20000, 7, 9, 3), (1, 32, 39000, 11, 5, 1)]
+
+
+@pytest.mark.parametrize("case", CONV_TCN)
+def test_conv1d_time_as_n_kernel(case):
+    import torch
+    B, C, T, K, p, d = case
+    x, w, b = rnd(B, C, T), rnd(C, C, K, scale=1.0 / np.sqrt(C * K)), rnd(C)
+    y = ops.conv1d(x, w, b, 1, p, d)
+    ref = torch.nn.functional.conv1d(torch.from_numpy(x).double(), torch.from_numpy(w).double(),
+                                     torch.from_numpy(b).double(), padding=p, dilation=d).numpy()
+    assert y.shape == ref.shape
+    np.testing.assert_allclose(y, ref, rtol=2e-4, atol=2e-4)
+
+
 CONVT = [(1, 512, 20, 256, 16, 10, 3), (2, 64, 33, 32, 4, 2, 1), (1, 256, 17, 128, 20, 10, 5),
          (1, 512, 9, 256, 24, 12, 6), (1, 6, 11, 4, 16, 10, 3)]
 
