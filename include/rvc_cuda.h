@@ -110,6 +110,16 @@ int32_t rvc_cuda_matmul(int64_t ctx, const float* a, const float* b, int32_t M, 
  * backend.layer_norm (runtime/backend.py:286) / rvc_layernorm (ffi.zig:575). */
 int32_t rvc_cuda_layer_norm(int64_t ctx, const float* x, int64_t rows, int32_t C, const float* gamma,
                             const float* beta, float eps, float* y);
+/* 2-D convolution x[B,C,H,W] * w[O,C,KH,KW] (+ b[O] when not NULL), stride
+ * (sh, sw), symmetric zero padding (ph, pw) -> y[B,O,Ho,Wo], fp32.  Replaces
+ * backend.conv2d (runtime/backend.py:254) / the engine's conv2d. */
+int32_t rvc_cuda_conv2d(int64_t ctx, const float* x, int32_t B, int32_t C, int32_t H, int32_t W, const float* w,
+                        int32_t O, int32_t KH, int32_t KW, const float* b, int32_t sh, int32_t sw, int32_t ph,
+                        int32_t pw, float* y);
+/* Row RMSNorm over the last axis: y = x / sqrt(mean(x^2) + eps) * gamma.
+ * Replaces backend.rmsnorm (runtime/backend.py:309). */
+int32_t rvc_cuda_rmsnorm(int64_t ctx, const float* x, int64_t rows, int32_t C, const float* gamma, float eps,
+                         float* y);
 /* Row softmax over the last axis.  Replaces backend.softmax (runtime/backend.py:298) / rvc_softmax (ffi.zig:604). */
 int32_t rvc_cuda_softmax(int64_t ctx, const float* x, int64_t rows, int32_t C, float* y);
 /* Elementwise: op 0 add(a,b), 1 mul(a,b), 2 relu(a), 3 leaky_relu(a, alpha),
@@ -261,6 +271,11 @@ int32_t rvc_cuda_fcpe_finalize(int64_t model);
  * and, when argmax is not NULL, the latent argmax [B,F].  Synchronous. */
 int32_t rvc_cuda_fcpe_infer(int64_t model, int32_t B, int64_t T, const float* x, float threshold, float* f0,
                             int32_t* argmax);
+/* FCPE.infer with its decoder_mode (runtime/models/fcpe.py:304-342, :344-369):
+ * 0 = "local_argmax" (what rvc_cuda_fcpe_infer runs), 1 = "argmax" (the
+ * latent-weighted mean of the cents over all 360 bins).  Host buffers. */
+int32_t rvc_cuda_fcpe_infer_mode(int64_t model, int32_t B, int64_t T, const float* x, float threshold,
+                                 int32_t decoder_mode, float* f0, int32_t* argmax);
 /* Same with device pointers, asynchronous on the context's stream. */
 int32_t rvc_cuda_fcpe_infer_device(int64_t model, int32_t B, int64_t T, const float* x, float threshold, float* f0,
                                    int32_t* argmax);

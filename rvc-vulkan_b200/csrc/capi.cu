@@ -474,6 +474,44 @@ int32_t rvc_cuda_layer_norm(int64_t ctx, const float* x, int64_t rows, int32_t C
   });
 }
 
+int32_t rvc_cuda_conv2d(int64_t ctx, const float* x, int32_t B, int32_t C, int32_t H, int32_t W, const float* w,
+                        int32_t O, int32_t KH, int32_t KW, const float* b, int32_t sh, int32_t sw, int32_t ph,
+                        int32_t pw, float* y) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(B >= 0 && C > 0 && H > 0 && W > 0 && O > 0 && KH > 0 && KW > 0 && sh > 0 && sw > 0 && ph >= 0 &&
+                      pw >= 0,
+                  "conv2d: bad shape");
+    const int Ho = (H + 2 * ph - KH) / sh + 1, Wo = (W + 2 * pw - KW) / sw + 1;
+    RVC_CHECK_ARG(H + 2 * ph >= KH && W + 2 * pw >= KW && Ho > 0 && Wo > 0, "conv2d: kernel larger than the input");
+    if (B == 0) return;
+    DevBuf dx(c, sizeof(float) * (size_t)B * C * H * W), dw(c, sizeof(float) * (size_t)O * C * KH * KW), db,
+        dy(c, sizeof(float) * (size_t)B * O * Ho * Wo);
+    h2d(c, dx.p, x, dx.bytes);
+    h2d(c, dw.p, w, dw.bytes);
+    if (b) {
+      db = DevBuf(c, sizeof(float) * O);
+      h2d(c, db.p, b, db.bytes);
+    }
+    k_conv2d(dx.f(), B, C, H, W, dw.f(), O, KH, KW, b ? db.f() : nullptr, sh, sw, ph, pw, dy.f(), c->stream);
+    d2h(c, y, dy.p, dy.bytes);
+    finish(c);
+  });
+}
+
+int32_t rvc_cuda_rmsnorm(int64_t ctx, const float* x, int64_t rows, int32_t C, const float* gamma, float eps,
+                         float* y) {
+  return on_ctx(ctx, [&](Context* c) {
+    RVC_CHECK_ARG(rows >= 0 && C > 0, "rmsnorm: bad shape");
+    if (rows == 0) return;
+    DevBuf dx(c, sizeof(float) * (size_t)rows * C), dg(c, sizeof(float) * C);
+    h2d(c, dx.p, x, dx.bytes);
+    h2d(c, dg.p, gamma, dg.bytes);
+    k_rmsnorm(dx.f(), rows, C, dg.f(), eps, dx.f(), c->stream);
+    d2h(c, y, dx.p, dx.bytes);
+    finish(c);
+  });
+}
+
 int32_t rvc_cuda_softmax(int64_t ctx, const float* x, int64_t rows, int32_t C, float* y) {
   return on_ctx(ctx, [&](Context* c) {
     RVC_CHECK_ARG(rows >= 0 && C > 0, "softmax: bad shape");
@@ -935,6 +973,15 @@ int32_t rvc_cuda_fcpe_set_weight(int64_t model, const char* key, const float* da
 int32_t rvc_cuda_fcpe_finalize(int64_t model) {
   return on_fcpe(model, [&](FcpeModel* m) {
     m->finalize();
+    finish(m->ctx);
+  });
+}
+
+int32_t rvc_cuda_fcpe_infer_mode(int64_t model, int32_t B, int64_t T, const float* x, float threshold,
+                                 int32_t decoder_mode, float* f0, int32_t* argmax) {
+  return on_fcpe(model, [&](FcpeModel* m) {
+    RVC_CHECK_ARG(B >= 1 && x && f0, "fcpe_infer_mode: bad arguments");
+    m->infer_host(B, T, x, threshold, f0, argmax, decoder_mode);
     finish(m->ctx);
   });
 }

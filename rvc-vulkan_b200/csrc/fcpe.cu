@@ -185,12 +185,35 @@ __device__ __forceinline__ float np_sum9(const float* a) {
   return __fadd_rn(s, a[8]);
 }
 
-// One warp per frame: latent = sigmoid(logits); local argmax decode
-// (runtime/models/fcpe.py:304-342): f0 = 10 * 2^(decoded / 1200), 0 when the
-// peak is <= threshold.
+// numpy's float32 pairwise sum of n <= 128 values (n >= 8): eight running
+// values over the blocks of eight, folded ((0+1)+(2+3))+((4+5)+(6+7)), then
+// the remainder in order
+__device__ float np_sum_block(const float* a, int n) {
+  float r[8];
+  for (int j = 0; j < 8; ++j) r[j] = a[j];
+  int i = 8;
+  for (; i < n - (n % 8); i += 8)
+    for (int j = 0; j < 8; ++j) r[j] = __fadd_rn(r[j], a[i + j]);
+  float s = __fadd_rn(__fadd_rn(__fadd_rn(r[0], r[1]), __fadd_rn(r[2], r[3])),
+                      __fadd_rn(__fadd_rn(r[4], r[5]), __fadd_rn(r[6], r[7])));
+  for (; i < n; ++i) s = __fadd_rn(s, a[i]);
+  return s;
+}
+// ... of the 360 bins: numpy halves n > 128 at a multiple of 8:
+// 360 -> 176 + 184, 176 -> 88 + 88, 184 -> 88 + 96
+__device__ float np_sum360(const float* a) {
+  return __fadd_rn(__fadd_rn(np_sum_block(a, 88), np_sum_block(a + 88, 88)),
+                   __fadd_rn(np_sum_block(a + 176, 88), np_sum_block(a + 264, 96)));
+}
+
+// One warp per frame: latent = sigmoid(logits); decode (runtime/models/fcpe.py:
+// 304-342): local argmax (mode 0: the cents-weighted mean of the 9 bins around
+// the peak) or argmax (mode 1: over all 360 bins); f0 = 10 * 2^(decoded /
+// 1200), 0 when the peak is <= threshold.  `wsum` holds 360 floats per frame
+// for mode 1 (cents x latent).
 __global__ void fcpe_decode_kernel(const float* __restrict__ logit, long long rows, const float* __restrict__ cents,
-                                   float threshold, float* __restrict__ lat, float* __restrict__ f0,
-                                   int32_t* __restrict__ argmax) {
+                                   float threshold, int mode, float* __restrict__ lat, float* __restrict__ wsum,
+                                   float* __restrict__ f0, int32_t* __restrict__ argmax) {
   const long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (r >= rows) return;
@@ -214,6 +237,16 @@ __global__ void fcpe_decode_kernel(const float* __restrict__ logit, long long ro
       bv = ov;
       bi = oi;
     }
+  }
+  if (mode == 1) {
+    float* cw = wsum + r * 360;
+    for (int k = lane; k < 360; k += 32) cw[k] = __fmul_rn(cents[k], lo[k]);
+    __syncwarp();
+    if (lane != 0) return;
+    const float dec = __fdiv_rn(np_sum360(cw), np_sum360(lo));
+    f0[r] = bv <= threshold ? 0.f : __fmul_rn(10.f, powf(2.f, __fdiv_rn(dec, 1200.f)));
+    if (argmax) argmax[r] = bi;
+    return;
   }
   __syncwarp();
   if (lane != 0) return;
@@ -357,6 +390,7 @@ void FcpeModel::ensure_ws(int B, int64_t T) {
   add("s", F * kDW);
   add("logit", F * kOut);
   add("lat", F * kOut);
+  add("wsum", F * kOut);
   add("f0", F);
   add("am", F);
   add("gn", 2 * kGroups * ((F + kGnRows - 1) / kGnRows) * 2 + 2 * kGroups);  // doubles in float units
@@ -382,7 +416,9 @@ bool FcpeModel::tap(const std::string& name, float* host, int64_t n) {
   return true;
 }
 
-void FcpeModel::infer_device(int B, int64_t T, const float* x, float threshold, float* f0, int32_t* argmax) {
+void FcpeModel::infer_device(int B, int64_t T, const float* x, float threshold, float* f0, int32_t* argmax,
+                             int decoder_mode) {
+  RVC_CHECK_ARG(decoder_mode == 0 || decoder_mode == 1, "fcpe: decoder_mode must be 0 (local_argmax) or 1 (argmax)");
   if (!finalized_) throw Error{kErrState, "fcpe: finalize() not called after the last weight upload"};
   RVC_CHECK_ARG(B >= 1 && T >= 1, "fcpe: need B >= 1 clips of T >= 1 samples");
   RVC_CHECK_ARG(T <= (1ll << 30), "fcpe: input too long");
@@ -480,19 +516,22 @@ void FcpeModel::infer_device(int B, int64_t T, const float* x, float threshold, 
               st);
   run_conv(proj_, gemm_io(buf("xn"), kH, buf("logit"), kOut));
   fcpe_decode_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(buf("logit"), rows, W("cent_table").buf.f(),
-                                                                  threshold, buf("lat"), f0, argmax);
+                                                                  threshold, decoder_mode, buf("lat"),
+                                                                  decoder_mode == 1 ? buf("wsum") : nullptr, f0,
+                                                                  argmax);
   note_launch();
   RVC_CUDA_TRY(cudaGetLastError());
   save_tap("latent", buf("lat"), rows * kOut);
 }
 
-void FcpeModel::infer_host(int B, int64_t T, const float* x, float threshold, float* f0, int32_t* argmax) {
+void FcpeModel::infer_host(int B, int64_t T, const float* x, float threshold, float* f0, int32_t* argmax,
+                           int decoder_mode) {
   RVC_CHECK_ARG(B >= 1 && T >= 1, "fcpe: need B >= 1 clips of T >= 1 samples");
   ensure_ws(B, T);
   cudaStream_t st = ctx->stream;
   const int64_t F = frames(T);
   RVC_CUDA_TRY(cudaMemcpyAsync(buf("x_in"), x, sizeof(float) * (size_t)B * T, cudaMemcpyHostToDevice, st));
-  infer_device(B, T, buf("x_in"), threshold, buf("f0"), argmax ? (int32_t*)buf("am") : nullptr);
+  infer_device(B, T, buf("x_in"), threshold, buf("f0"), argmax ? (int32_t*)buf("am") : nullptr, decoder_mode);
   RVC_CUDA_TRY(cudaMemcpyAsync(f0, buf("f0"), sizeof(float) * (size_t)B * F, cudaMemcpyDeviceToHost, st));
   if (argmax)
     RVC_CUDA_TRY(cudaMemcpyAsync(argmax, buf("am"), sizeof(int32_t) * (size_t)B * F, cudaMemcpyDeviceToHost, st));

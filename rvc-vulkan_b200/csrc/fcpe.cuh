@@ -26,8 +26,11 @@ class FcpeModel {
   static int64_t frames(int64_t T) { return T / kHop + 1; }
   // Device pointers, asynchronous on ctx->stream: x [B][T] -> f0 [B][F] Hz and,
   // when argmax != nullptr, the latent argmax [B][F].
-  void infer_device(int B, int64_t T, const float* x, float threshold, float* f0, int32_t* argmax);
-  void infer_host(int B, int64_t T, const float* x, float threshold, float* f0, int32_t* argmax);
+  // decoder_mode: 0 local_argmax (the pipeline's), 1 argmax (runtime/models/fcpe.py:304-333)
+  void infer_device(int B, int64_t T, const float* x, float threshold, float* f0, int32_t* argmax,
+                    int decoder_mode = 0);
+  void infer_host(int B, int64_t T, const float* x, float threshold, float* f0, int32_t* argmax,
+                  int decoder_mode = 0);
   bool tap(const std::string& name, float* host, int64_t n);
   bool keep_taps = false;
   Context* ctx;

@@ -101,4 +101,9 @@ void dsp_change_rms(Context* ctx, const float* d1, long long n1, int sr1, const 
                     double rate, float* out);
 void dsp_to_int16(Context* ctx, const float* x, long long n, short* y);
 
+// Tier-1 2-D convolution (torch conv2d semantics, zero padding) and RMSNorm (ops2d.cu).
+void k_conv2d(const float* x, int B, int C, int H, int W, const float* w, int O, int KH, int KW, const float* bias,
+              int sh, int sw, int ph, int pw, float* y, cudaStream_t st);
+void k_rmsnorm(const float* x, long long rows, int C, const float* g, float eps, float* y, cudaStream_t st);
+
 }  // namespace rvc

@@ -74,6 +74,9 @@ _SIGS = {
                                    _i32], _i32),
     "rvc_cuda_matmul": ([_i64, _fp, _fp, _i32, _i32, _i32, _fp], _i32),
     "rvc_cuda_layer_norm": ([_i64, _fp, _i64, _i32, _fp, _fp, _f32, _fp], _i32),
+    "rvc_cuda_conv2d": ([_i64, _fp, _i32, _i32, _i32, _i32, _fp, _i32, _i32, _i32, _fp, _i32, _i32, _i32, _i32,
+                         _fp], _i32),
+    "rvc_cuda_rmsnorm": ([_i64, _fp, _i64, _i32, _fp, _f32, _fp], _i32),
     "rvc_cuda_softmax": ([_i64, _fp, _i64, _i32, _fp], _i32),
     "rvc_cuda_elementwise": ([_i64, _i32, _fp, _fp, _i64, _f32, _fp], _i32),
     "rvc_cuda_embedding": ([_i64, _ip64, _i64, _fp, _i32, _i32, _fp], _i32),
@@ -104,6 +107,7 @@ _SIGS = {
     "rvc_cuda_fcpe_set_weight": ([_i64, C.c_char_p, _fp, _ip64, _i32], _i32),
     "rvc_cuda_fcpe_finalize": ([_i64], _i32),
     "rvc_cuda_fcpe_infer": ([_i64, _i32, _i64, _fp, _f32, _fp, C.POINTER(_i32)], _i32),
+    "rvc_cuda_fcpe_infer_mode": ([_i64, _i32, _i64, _fp, _f32, _i32, _fp, C.POINTER(_i32)], _i32),
     "rvc_cuda_fcpe_infer_device": ([_i64, _i32, _i64, _p, _f32, _p, _p], _i32),
     "rvc_cuda_fcpe_tap": ([_i64, C.c_char_p, _fp, _i64], _i32),
     "rvc_cuda_fcpe_keep_taps": ([_i64, _i32], _i32),

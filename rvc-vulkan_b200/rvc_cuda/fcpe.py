@@ -2,9 +2,10 @@
 
 ``CudaFcpe`` keeps the contract of ``FCPE.infer`` (``runtime/models/fcpe.py:344``):
 ``[T]`` float32 16 kHz audio -> ``[F]`` float32 f0 in Hz, ``F = T // 160 + 1``,
-``decoder_mode="local_argmax"``.  The whole model (log-mel front end, input
-stack, six conv-only conformer layers, weight-normalised projection, sigmoid,
-local argmax decode) runs in one library call per batch of equal-length clips;
+``decoder_mode`` "local_argmax" (the pipeline's) or "argmax".  The whole model
+(log-mel front end, input stack, six conv-only conformer layers,
+weight-normalised projection, sigmoid, decode) runs in one library call per
+batch of equal-length clips;
 the convolutions and linears on tensor cores (BF16x3, fp32 accumulate).
 Weights are the reference's checkpoint dict (``FCPE.W``) under its own keys.
 
@@ -31,6 +32,9 @@ PRECISIONS = {"bf16x3": 0, "simt": 1}
 def frames(T: int) -> int:
     """Frames for ``T`` samples (hop 160)."""
     return int(T) // 160 + 1
+
+
+DECODER_MODES = {"local_argmax": 0, "argmax": 1}
 
 
 class CudaFcpe:
@@ -66,9 +70,13 @@ class CudaFcpe:
         except Exception:  # noqa: BLE001
             pass
 
-    def infer_batch(self, xb, threshold: float = 0.006, return_argmax: bool = False):
+    def infer_batch(self, xb, threshold: float = 0.006, return_argmax: bool = False,
+                    decoder_mode: str = "local_argmax"):
         """``xb [B,T]`` equal-length clips -> ``f0 [B,F]`` (and the latent argmax
-        ``[B,F]`` int32 when ``return_argmax``)."""
+        ``[B,F]`` int32 when ``return_argmax``); ``decoder_mode`` as in
+        ``FCPE._decode`` (``runtime/models/fcpe.py:304-342``)."""
+        if decoder_mode not in DECODER_MODES:
+            raise ValueError(f"Unknown FCPE decoder mode: {decoder_mode}")
         xb = np.ascontiguousarray(np.asarray(xb, dtype=np.float32))
         if xb.ndim != 2 or xb.shape[1] < 1:
             raise ValueError(f"batch input must be [B, T] with T >= 1, got {xb.shape}")
@@ -76,8 +84,9 @@ class CudaFcpe:
         F = frames(T)
         f0 = np.empty((B, F), np.float32)
         am = np.empty((B, F), np.int32)
-        check(lib.rvc_cuda_fcpe_infer(self.handle, B, T, fptr(xb), float(threshold), fptr(f0),
-                                      am.ctypes.data_as(C.POINTER(C.c_int32))))
+        check(lib.rvc_cuda_fcpe_infer_mode(self.handle, B, T, fptr(xb), float(threshold),
+                                           DECODER_MODES[decoder_mode], fptr(f0),
+                                           am.ctypes.data_as(C.POINTER(C.c_int32))))
         return (f0, am) if return_argmax else f0
 
     def infer(self, x, sr: int = 16000, decoder_mode: str = "local_argmax", threshold: float = 0.006) -> np.ndarray:
@@ -87,9 +96,7 @@ class CudaFcpe:
             raise ValueError(f"infer needs 1-D audio, got {x.ndim}-D")
         if sr != 16000:
             raise NotImplementedError(f"FCPE is defined at sr=16000, got sr={sr}; resample to 16 kHz first")
-        if decoder_mode != "local_argmax":
-            raise NotImplementedError("only decoder_mode='local_argmax' (the pipeline's) is on the device path")
-        return self.infer_batch(x[None, :], threshold)[0]
+        return self.infer_batch(x[None, :], threshold, decoder_mode=decoder_mode)[0]
 
     # ---------------------------------------------------------------- debug
     def keep_taps(self, on: bool = True):

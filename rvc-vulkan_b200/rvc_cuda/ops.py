@@ -205,6 +205,51 @@ def layer_norm(x, gamma, beta, eps=1e-5, buf_gamma=None, buf_beta=None):
     return out
 
 
+def rmsnorm(x, gamma, eps=1e-5, buf_gamma=None):
+    """RMSNorm over the last axis: ``x / sqrt(mean(x^2) + eps) * gamma``
+    (``runtime/backend.py:309-316``)."""
+    x = _f32(x)
+    C = x.shape[-1]
+    out = np.empty(x.shape, np.float32)
+    rows = x.size // C if C else 0
+    if rows:
+        check(lib.rvc_cuda_rmsnorm(_ctx(), fptr(x), rows, C, fptr(_f32(gamma)), float(eps), fptr(out)))
+    return out
+
+
+def _pair(v, name):
+    if isinstance(v, (tuple, list)):
+        if len(v) != 2:
+            raise ValueError(f"conv2d: {name} must be an int or a pair, got {v!r}")
+        return int(v[0]), int(v[1])
+    return int(v), int(v)
+
+
+def conv2d(x, w, b=None, stride=1, padding=0, buf_w=None, buf_b=None):
+    """2-D convolution with ``torch.nn.functional.conv2d`` semantics (symmetric
+    zero padding), ``runtime/backend.py:254-260`` / ``runtime/nn.py:259-290``:
+    ``x [B,C,H,W]``, ``w [O,C,KH,KW]``, ``b [O]`` or None -> ``[B,O,Ho,Wo]``.
+    Shape errors raise ``ValueError`` (the caller then takes its numpy path)."""
+    x, w = _f32(x), _f32(w)
+    if x.ndim != 4 or w.ndim != 4 or x.shape[1] != w.shape[1]:
+        raise ValueError(f"conv2d: x {x.shape} and w {w.shape} do not match [B,C,H,W] / [O,C,KH,KW]")
+    sh, sw = _pair(stride, "stride")
+    ph, pw = _pair(padding, "padding")
+    B, C, H, W = x.shape
+    O, _, KH, KW = w.shape
+    if sh < 1 or sw < 1 or ph < 0 or pw < 0 or H + 2 * ph < KH or W + 2 * pw < KW:
+        raise ValueError("conv2d: bad stride / padding for these shapes")
+    Ho, Wo = (H + 2 * ph - KH) // sh + 1, (W + 2 * pw - KW) // sw + 1
+    bb = None if b is None else _f32(b).reshape(-1)
+    if bb is not None and bb.size != O:
+        raise ValueError(f"conv2d: bias of {bb.size} values for {O} output channels")
+    out = np.empty((B, O, Ho, Wo), np.float32)
+    if B:
+        check(lib.rvc_cuda_conv2d(_ctx(), fptr(x), B, C, H, W, fptr(w), O, KH, KW,
+                                  fptr(bb) if bb is not None else None, sh, sw, ph, pw, fptr(out)))
+    return out
+
+
 def softmax(x):
     """Row softmax over the last axis (``runtime/backend.py:298-306``)."""
     x = _f32(x)

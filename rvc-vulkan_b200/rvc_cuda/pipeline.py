@@ -17,7 +17,9 @@ Host-side glue that stays in numpy: the reflect padding and slicing of the
 chunks, the frame alignment of pitch arrays (``:572-603``) and the f0
 post-processing of ``get_f0`` (``:468-482``, a few thousand values per call).
 
-Not offered here: ``brute_mix != 0`` (raises ``NotImplementedError``).
+``brute_mix != 0`` (a blend of the IVF and brute-force retrievals) runs on the
+host-buffer path: both blends come from the device index and are mixed in
+float32 in the reference's order.
 """
 
 from __future__ import annotations
@@ -169,9 +171,9 @@ class Pipeline:
         feats = np.asarray(feats, dtype=np.float32)
         protecting = protect < 0.5 and pitch is not None and pitchf is not None
         feats0 = feats if protecting else None
-        if index is not None and index_rate != 0:                   # :517-566
-            if brute_mix != 0:
-                raise NotImplementedError("brute_mix != 0 is not on the device path")
+        if index is not None and index_rate != 0 and brute_mix != 0:  # :521-566, the two-path blend
+            feats = self._mixed_blend(index, feats, index_rate, retrieval_mode, float(brute_mix))
+        elif index is not None and index_rate != 0:                 # :517-566
             if index.nlist and retrieval_mode != "brute":             # IVF index: strict bucket search
                 feats = index.ivf_blend(feats[0], k=_K_SEARCH, feats=feats[0], index_rate=index_rate)[None]
             else:                                                     # brute force over every row
@@ -190,6 +192,24 @@ class Pipeline:
             feats = dsp.protect_blend(feats, feats0, pitchf, protect)
         times[0] += t1 - t0
         return {"feats": feats, "pitch": pitch, "pitchf": pitchf, "sid_arr": np.asarray([sid], dtype=np.int64)}
+
+    @staticmethod
+    def _mixed_blend(index, feats, index_rate, retrieval_mode, brute_mix):
+        """``brute_mix != 0`` (``runtime/pipeline.py:521-566``): the IVF blend (the
+        strict bucket search; the brute-force blend again when the index has no
+        IVF structure) and the brute-force blend over every row, both on the
+        device; mixed as ``(1 - m) * main + m * other`` (main = IVF, or the
+        brute force under ``retrieval_mode="brute"``), then
+        ``blend * index_rate + feats * (1 - index_rate)``, in float32 as there."""
+        q = feats[0]
+        brute = index.blend(q, k=_K_SEARCH, mode="pipeline")
+        ivf = index.ivf_blend(q, k=_K_SEARCH) if index.nlist else brute
+        m = float(brute_mix)  # Python scalars against float32 arrays, as there
+        if retrieval_mode == "brute":
+            blend = (1.0 - m) * brute + m * ivf
+        else:
+            blend = (1.0 - m) * ivf + m * brute
+        return (blend[None, :, :] * float(index_rate) + feats * (1 - float(index_rate))).astype(np.float32)
 
     # ------------------------------------------------------------------ whole
     def pipeline(self, model, net_g, sid, audio, times, f0_up_key, f0_method, file_index, index_rate, if_f0,
@@ -232,7 +252,8 @@ class Pipeline:
                 blocks.append((idx, s0, e0, np.asarray(blk, dtype=np.float32)))
         noise = self._prefetch_noise(model, net_g, [b[3].shape[0] for b in blocks])
 
-        ctx = self._device_chain(model, net_g, index)
+        # the two-path retrieval mix (brute_mix) runs on the host-buffer path
+        ctx = None if (brute_mix and index is not None and index_rate != 0) else self._device_chain(model, net_g, index)
         f0_model = getattr(self, "model_fcpe" if f0_method == "fcpe" else "model_rmvpe", None)
         f0_ctx = getattr(f0_model, "ctx", None)
         if ctx is not None and f0_method != "pm" and f0_ctx is not None and f0_ctx is not ctx:

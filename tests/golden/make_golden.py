@@ -228,6 +228,11 @@ def run_ivf(name, N, D, nlist, F, seed, edge, meta):
     prep = pipe._vc_prepare(None, 0, np.zeros(2 * P * 160 + 400, np.float32), pitch, pitchf, [0.0, 0.0, 0.0], ivf,
                             None, 0.75, 2, 0.33, feats=feats)
     rec["prep_feats"] = prep["feats"]
+    # the two-path retrieval mix (brute_mix, runtime/pipeline.py:521-566)
+    for tag, mode, bm in (("bm_ivf", "ivf", 0.3), ("bm_brute", "brute", 0.4)):
+        prep = pipe._vc_prepare(None, 0, np.zeros(2 * P * 160 + 400, np.float32), pitch, pitchf, [0.0, 0.0, 0.0],
+                                ivf, None, 0.75, 2, 0.33, feats=feats, retrieval_mode=mode, brute_mix=bm)
+        rec[f"prep_{tag}"] = prep["feats"][:, ::7]  # every 7th frame keeps the fixture small
     np.savez_compressed(os.path.join(HERE, name + ".npz"), **rec)
     meta[name] = {"kind": "ivf", "N": N, "D": D, "nlist": int(ivf.nlist), "F": F, "seed": seed, "edge": edge,
                   "inputs_sha256": digest([vecs, q])}
@@ -254,6 +259,7 @@ def run_fcpe(name, T, wseed, iseed, meta):
     mel = m._wav2mel(x)
     lat = m._latent(mel)
     f0 = m.infer(x)
+    f0_argmax = m.infer(x, decoder_mode="argmax")
     # Pipeline.get_f0(..., "fcpe") with this model (runtime/pipeline.py:451-483)
     from runtime import pipeline as rp  # noqa: PLC0415
     sys.path.insert(0, HERE)
@@ -262,7 +268,8 @@ def run_fcpe(name, T, wseed, iseed, meta):
     pipe.model_fcpe = m
     coarse, f0bak = pipe.get_f0(x.astype(np.float64), T // 160 + 1, 3, "fcpe")
     np.savez_compressed(os.path.join(HERE, name + ".npz"), mel=mel[0], latent=lat[0],
-                        argmax=lat[0].argmax(axis=1).astype(np.int64), f0=f0, pipe_coarse=coarse, pipe_f0bak=f0bak)
+                        argmax=lat[0].argmax(axis=1).astype(np.int64), f0=f0, f0_argmax=f0_argmax,
+                        pipe_coarse=coarse, pipe_f0bak=f0bak)
     meta[name] = {"kind": "fcpe", "T": T, "weight_seed": wseed, "input_seed": iseed,
                   "weights_sha256": weights_digest(sd), "inputs_sha256": digest([x])}
 

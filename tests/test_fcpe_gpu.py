@@ -47,6 +47,22 @@ def test_fcpe_matches_reference_golden(name, golden_meta):
     model.keep_taps(False)
 
 
+@pytest.mark.parametrize("name", ["fcpe_t24000", "fcpe_t3001"])
+def test_fcpe_argmax_decoder_matches_reference_golden(name, golden_meta):
+    """``decoder_mode="argmax"`` (``runtime/models/fcpe.py:318-322``): the
+    latent-weighted mean of the cents over all 360 bins, summed in numpy's
+    pairwise order; f0 within float32 rounding of the latent (rel 1e-4)."""
+    m = golden_meta[name]
+    x = syn.make_rmvpe_input(m["T"], m["input_seed"])
+    g = load_golden(name)
+    f0 = _model().infer(x, decoder_mode="argmax")
+    assert f0.shape == g["f0_argmax"].shape
+    np.testing.assert_array_equal(f0 == 0, g["f0_argmax"] == 0)
+    np.testing.assert_allclose(f0, g["f0_argmax"], rtol=1e-4, atol=1e-3)
+    with pytest.raises(ValueError):
+        _model().infer(x, decoder_mode="median")
+
+
 def test_fcpe_layers_against_oracle_and_simt():
     sd = syn.make_fcpe_weights(0)
     x = syn.make_rmvpe_input(16000, 9)

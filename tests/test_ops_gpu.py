@@ -136,3 +136,34 @@ def test_im2col():
     oL = (20 + 4 - 5) // 2 + 1
     ref = np.stack([xp[:, :, t * 2:t * 2 + 5].reshape(2, -1) for t in range(oL)], axis=1)
     np.testing.assert_array_equal(cols, ref)
+
+
+CONV2D = [  # B, C, H, W, O, KH, KW, stride, padding
+    (1, 16, 64, 32, 16, 3, 3, 1, 1), (2, 3, 17, 9, 5, 3, 3, (2, 1), (1, 0)), (1, 64, 16, 8, 32, 1, 1, 1, 0),
+    (1, 4, 11, 13, 6, 5, 3, 2, 2),
+]
+
+
+@pytest.mark.parametrize("case", CONV2D)
+def test_conv2d(case):
+    """Tier-1 conv2d (``runtime/backend.py:254``) against torch conv2d in float64."""
+    import torch
+    B, C, H, W, Oc, KH, KW, st, pd = case
+    x, w, b = rnd(B, C, H, W), rnd(Oc, C, KH, KW, scale=1.0 / np.sqrt(C * KH * KW)), rnd(Oc)
+    y = ops.conv2d(x, w, b, st, pd)
+    ref = torch.nn.functional.conv2d(torch.from_numpy(x).double(), torch.from_numpy(w).double(),
+                                     torch.from_numpy(b).double(), stride=st, padding=pd).numpy()
+    assert y.shape == ref.shape
+    np.testing.assert_allclose(y, ref, rtol=1e-5, atol=1e-5)
+    with pytest.raises(ValueError):
+        ops.conv2d(x, w[:, :1], b, st, pd)
+
+
+def test_rmsnorm():
+    """Tier-1 rmsnorm (``runtime/backend.py:309-316``) against the reference formula."""
+    x = rnd(7, 33, 192, scale=3.0)
+    g = rnd(192)
+    y = ops.rmsnorm(x, g, 1e-5)
+    x64 = x.astype(np.float64)
+    ref = x64 / np.sqrt((x64 * x64).mean(-1, keepdims=True) + 1e-5) * g
+    np.testing.assert_allclose(y, ref, rtol=1e-5, atol=1e-5)

@@ -157,6 +157,11 @@ def test_ivf_search_matches_reference_golden(name, golden_meta):
     assert index.nlist == g["centroids"].shape[0]
     prep = pipe._vc_prepare(0, 2 * m["F"] * 160 + 400, pitch, pitchf, feats, index, 0.75, 0.33, [0.0, 0.0, 0.0])
     np.testing.assert_allclose(prep["feats"], g["prep_feats"], rtol=1e-5, atol=1e-5)
+    # brute_mix: the IVF and brute-force blends mixed (runtime/pipeline.py:521-566)
+    for tag, mode, bm in (("bm_ivf", "ivf", 0.3), ("bm_brute", "brute", 0.4)):
+        prep = pipe._vc_prepare(0, 2 * m["F"] * 160 + 400, pitch, pitchf, feats, index, 0.75, 0.33,
+                                [0.0, 0.0, 0.0], retrieval_mode=mode, brute_mix=bm)
+        np.testing.assert_allclose(prep["feats"][:, ::7], g[f"prep_{tag}"], rtol=1e-5, atol=1e-5)
 
 
 def test_ivf_larger_index_against_oracle():
