@@ -984,6 +984,17 @@ def config0_figure(args, local, timed, max_over_ranks, world):
             "steps": args.steps, "warmup": args.warmup}
 
 
+# DRAM bytes of the tensor-core conv launches for one v2-48k chunk of 1000 frames, from an ncu
+# capture of a 4-chunk call (36.33 GB over its 135 conv launches); traffic grows with rows.
+SYNTH_DRAM_BYTES_48K_PER_1000_FRAMES = 9.0825e9
+
+
+def synth_traffic(sr, P, chunks):
+    if sr != 48000:
+        return None
+    return SYNTH_DRAM_BYTES_48K_PER_1000_FRAMES * chunks * P / 1000.0
+
+
 def run_ours(args, world, rank, local):
     import torch
 
@@ -1116,9 +1127,15 @@ def run_ours(args, world, rank, local):
                        "chunks": args.chunks, "frames": P, "sr": sr, "group": G, "precision": args.precision,
                        "l2": "inputs larger than L2 (GBs per step)",
                        "parallelism": f"chunk-sharded x{world}, no collective"},
-            "roofline": {"bound": "tensor", "kernel": "tc_conv_kernel (implicit-GEMM conv, all launches)",
+            "roofline": {"bound": "tensor",
+                         "kernel": "tc_conv_kernel + tcn_conv_kernel (implicit-GEMM convs, all launches)",
                          "achieved": achieved, "peak": ps, "unit": "TFLOP/s",
-                         "frac": (achieved / ps) if achieved else None, "traffic": None,
+                         "frac": (achieved / ps) if achieved else None,
+                         "traffic": synth_traffic(sr, P, n_local),
+                         "traffic_note": "DRAM bytes of this rank's conv launches per step: an ncu capture of one "
+                                         "4-chunk v2-48k call (dram__bytes_read.sum + dram__bytes_write.sum over its "
+                                         "135 conv launches) scaled by chunks x frames; a lower bound, as the small "
+                                         "call keeps its early-stage tensors in L2",
                          "peak_source": f"{src} bf16 dense sustained",
                          "note": "achieved = useful fp32 GEMM FLOPs / kernel time; BF16x3 runs 3 bf16 MMAs per "
                                  "useful MAC, so frac <= 1/3 by construction",

@@ -34,6 +34,16 @@ def frames(T: int) -> int:
     return int(F.value)
 
 
+def max_lanes() -> int:
+    """Concurrent f0 lanes of ``CudaRmvpe.infer_many`` (``RVC_CUDA_RMVPE_LANES``,
+    default 4): each extra lane holds its own weight copy (~180 MB) and
+    workspace, so the count is fixed rather than following the input."""
+    n = int(os.environ.get("RVC_CUDA_RMVPE_LANES", "4"))
+    if n < 1:
+        raise ValueError(f"RVC_CUDA_RMVPE_LANES must be >= 1, got {n}")
+    return n
+
+
 class CudaRmvpe:
     """Device-resident RMVPE on one GPU (one library context)."""
 
@@ -65,6 +75,9 @@ class CudaRmvpe:
         return cls(model.W, device=device)
 
     def close(self):
+        for m in getattr(self, "_lanes", ()):
+            m.close()
+        self._lanes = []
         if getattr(self, "handle", 0):
             lib.rvc_cuda_rmvpe_destroy(self.handle)
             self.handle = 0
@@ -99,21 +112,31 @@ class CudaRmvpe:
         return self.infer_batch(x[None, :], thred)[0]
 
     def infer_many(self, xs, thred: float = 0.03):
-        """f0 of several 1-D clips of any lengths, run concurrently: clip ``i``
-        on lane ``i`` (this model, then sibling models with their own context
-        and stream, built on first use), one host thread per lane.  Each result
-        equals ``infer_from_audio`` of that clip (each clip is its own batch of
-        one, as in the reference's per-segment calls)."""
+        """f0 of several 1-D clips of any lengths, run concurrently on at most
+        ``max_lanes()`` lanes (this model, then sibling models with their own
+        context, stream and weight copy, built on first use and kept): clip
+        ``i`` runs on lane ``i % lanes``, each lane's clips in order on one host
+        thread.  Each result equals ``infer_from_audio`` of that clip (each clip
+        is its own batch of one, as in the reference's per-segment calls), so
+        the lane count changes the timing only."""
         xs = [np.asarray(x, dtype=np.float32) for x in xs]
-        if len(xs) <= 1:
+        n = min(len(xs), max_lanes())
+        if n <= 1:
             return [self.infer_from_audio(x, thred) for x in xs]
-        while len(self._lanes) < len(xs) - 1:
+        while len(self._lanes) < n - 1:
             self._lanes.append(CudaRmvpe(self._weights, device=self.ctx.device, own_stream=True))
-        lanes = [self] + self._lanes[:len(xs) - 1]
+        lanes = [self] + self._lanes[:n - 1]
+
+        def run_lane(j):
+            return [(i, lanes[j].infer_from_audio(xs[i], thred)) for i in range(j, len(xs), n)]
+
         from concurrent.futures import ThreadPoolExecutor  # noqa: PLC0415
-        with ThreadPoolExecutor(max_workers=len(xs), thread_name_prefix="rvc-rmvpe") as ex:
-            futs = [ex.submit(m.infer_from_audio, x, thred) for m, x in zip(lanes, xs)]
-            return [f.result() for f in futs]
+        out = [None] * len(xs)
+        with ThreadPoolExecutor(max_workers=n, thread_name_prefix="rvc-rmvpe") as ex:
+            for f in [ex.submit(run_lane, j) for j in range(n)]:
+                for i, r in f.result():
+                    out[i] = r
+        return out
 
     # ---------------------------------------------------------------- debug
     def keep_taps(self, on: bool = True):

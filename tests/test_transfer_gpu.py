@@ -48,3 +48,18 @@ def test_rmvpe_infer_many_equals_per_segment():
     for x, f in zip(xs, many):
         np.testing.assert_array_equal(f, m.infer_from_audio(x))
     assert [f.shape[0] for f in m.infer_many(xs[:1])] == [101]
+
+
+def test_rmvpe_infer_many_lane_cap(monkeypatch):
+    """More segments than lanes: the lanes stay at the cap and every segment
+    still equals its own ``infer_from_audio``."""
+    from rvc_cuda.rmvpe import CudaRmvpe
+
+    monkeypatch.setenv("RVC_CUDA_RMVPE_LANES", "2")
+    m = CudaRmvpe(syn.make_rmvpe_weights(0), own_stream=True)
+    xs = [syn.make_rmvpe_input(T, s) for T, s in ((8000, 1), (9000, 2), (7000, 3), (12000, 4), (6000, 5))]
+    many = m.infer_many(xs)
+    assert len(m._lanes) == 1
+    for x, f in zip(xs, many):
+        np.testing.assert_array_equal(f, m.infer_from_audio(x))
+    m.close()
