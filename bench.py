@@ -1157,6 +1157,11 @@ def run_ours(args, world, rank, local):
         dist.destroy_process_group()
 
 
+def _lib_ctx():
+    from rvc_cuda import _lib
+    return _lib.get_context()
+
+
 def run_layer(args):
     """Single-GPU layer cases for timing and ncu captures (one process, no JSON
     line): ``--layer conv`` runs ``rvc_cuda.ops.conv1d`` on [1,C,T] ("same"
@@ -1176,7 +1181,13 @@ def run_layer(args):
             t0 = time.perf_counter()
             y = ops.conv1d(x, w, b, 1, (K - 1) * d // 2, d)
             dt = time.perf_counter() - t0
-        print(f"conv C={C} K={K} dil={d} T={T}: {dt * 1e3:.2f} ms (host API, incl. copies) "
+        ctx = _lib_ctx()
+        ctx.profile(True)  # one more call with CUDA events around the conv kernel
+        ops.conv1d(x, w, b, 1, (K - 1) * d // 2, d)
+        n, ms, fl = ctx.profile_read()
+        ctx.profile(False)
+        print(f"conv C={C} K={K} dil={d} T={T}: {dt * 1e3:.2f} ms (host API, incl. copies); kernel "
+              f"{ms * 1e3:.1f} us over {n} launch(es), {fl / (ms / 1e3) / 1e12 if ms else 0:.1f} TFLOP/s useful; "
               f"mean|y|={np.abs(y).mean():.4f}")
     elif args.layer == "synth":
         from rvc_cuda.synth import CudaSynthesizer

@@ -67,6 +67,19 @@ struct ConvArgs {
   int* err;        // device error flag (bounded waits)
 };
 
+// v / d for a divisor d used across many values, with rd = __frcp_rn(d): the
+// quotient q = RN(v * rd) corrected once by its remainder, RN(q + RN(v - q*d) * rd)
+// (division by a constant known in advance: Markstein's correction step, as in
+// Brisebarre, Muller and Raina, IEEE Trans. Computers 2004).  Checked on the
+// host against IEEE v / d over every mantissa of 9 binades, both signs, for
+// d = 2, 3, 5, 7: identical (so for every normal v and these d); 3 instructions
+// instead of a full division per value.
+__device__ __forceinline__ float div_by(float v, float d, float rd) {
+  const float q = __fmul_rn(v, rd);
+  const float r = __fmaf_rn(-q, d, v);
+  return __fmaf_rn(r, rd, q);
+}
+
 // Epilogue for one output element (physical row `prow`, channel `c` in [0, C_out)
 // of slice s).  `acc` is the raw dot product.
 __device__ __forceinline__ void conv_epilogue(const ConvArgs& a, int b, int prow, int cg, float acc) {
@@ -108,7 +121,9 @@ bool tcn_fits(const ConvArgs& a);
 size_t tcn_packed_elems(int taps, int C_in, int C_out);
 void launch_tcn_pack(const float* w, uint16_t* out, int taps, int C_in, int C_out, cudaStream_t st);
 void launch_tcn_conv(const ConvArgs& a, cudaStream_t st);
-// True unless RVC_CUDA_TCN=0 (read once): the time-as-N kernel is used where it applies.
-bool tcn_enabled();
+// RVC_CUDA_TCN (read once): 0 = never use the time-as-N kernel, 2 = use it for
+// every conv it can run (for timing both kernels), otherwise (default, 1) where
+// ConvLayer::run's routing picks it.
+int tcn_enabled();
 
 }  // namespace rvc

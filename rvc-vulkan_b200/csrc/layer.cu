@@ -134,13 +134,18 @@ void ConvLayer::run(Context* ctx, const ConvIO& io, bool force_simt) const {
   const bool use_tc = tc && !force_simt && !any_empty && (io.x_ld % 4 == 0) && (io.x_bs % 4 == 0);
   RVC_CHECK_ARG(use_tc || Wg.p, "conv: fp32 weights were released; only the tensor-core path can run this layer");
   // Time rows as the MMA's N (tcn_conv.cu) where it measured faster than the
-  // time-rows-as-M kernel (B200, the v2-48k generator at 32 chunks per call):
-  // C >= 128 always (K = 11: 4.3 -> 2.9 ms per launch); C = 64 for K >= 7
-  // (K = 11: 3.8 -> 3.1 ms; K = 3: 1.5 -> 2.5 ms); C = 32 only for K >= 11
-  // without residual / accumulator inputs (3.4 -> 2.7 ms).  At least one wave
-  // of 256-row tiles.
-  const bool tn_pick = C_out >= 128 || (C_out == 64 && K >= 7) || (C_out == 32 && K >= 11 && !io.res && !io.accin);
-  if (use_tc && tn && tn_pick && tcn_enabled() && ((uintptr_t)io.x & 15) == 0 && tcn_fits(a)) {
+  // time-rows-as-M kernel (B200, both kernels on the same inputs in one
+  // process, the v2-48k generator's ResBlock convs at 4 chunks per call):
+  // C >= 128 always (0.54-0.87 of the time); C = 64 for K >= 7 (0.64-0.87) and
+  // for K = 3 without residual / accumulator inputs (0.64); C = 32 for K >= 7
+  // without them (0.71-0.73).  With a residual input at C = 64, K = 3 and at
+  // C = 32 for every K it is no faster (0.96-2.2x).  At least one wave of
+  // 256-row tiles.
+  const int tcn_mode = tcn_enabled();
+  const bool plain_out = !io.res && !io.accin;
+  const bool tn_pick = tcn_mode == 2 || C_out >= 128 || (C_out == 64 && (K >= 7 || plain_out)) ||
+                       (C_out == 32 && K >= 7 && plain_out);
+  if (use_tc && tn && tn_pick && tcn_mode != 0 && ((uintptr_t)io.x & 15) == 0 && tcn_fits(a)) {
     const long long tiles = (long long)io.B * cdiv(a.sl[0].rows, 256) * (C_out <= 64 ? 1 : C_out / 128);
     if (tiles >= ctx->num_sms()) {
       a.wpk = wpk_t.as<uint16_t>();

@@ -643,8 +643,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           if (a.out_div != 0.f) {
+            const float dv = a.out_div, rd = __frcp_rn(dv);
 #pragma unroll
-            for (int k = 0; k < 32; ++k) v[k] = v[k] / a.out_div;
+            for (int k = 0; k < 32; ++k) v[k] = div_by(v[k], dv, rd);
           }
           act_row(v, a.out_act, a.out_slope);
 #pragma unroll

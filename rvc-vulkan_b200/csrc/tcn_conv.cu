@@ -58,6 +58,7 @@ constexpr uint64_t kWaitNs = 2000000000ull;
 
 struct TnPlan {
   int mode, co_tiles, tiles_t, total_tiles;
+  int resident;  // every weight stage in its own slot, loaded once per CTA
   int nst, st_shift, ts;  // weight stages per k block (taps), their row shift, output rows per tile
   int arows_pad, nbox, box_rows, nstg, stages, nslot;
   uint32_t x_plane, stg_bytes, w_stage;
@@ -90,19 +91,33 @@ __device__ __forceinline__ TileT tile_of(int tile, int co_tiles, int tiles_t) {
   return c;
 }
 
+// Terms of the prologue / epilogue a launch uses, as compile-time flags of
+// tcn_conv_kernel.  The ResBlock convs need a handful of combinations; with
+// only those terms unrolled the epilogue warps run about twice as fast as
+// with every optional term behind a run-time branch (the unrolled code of the
+// unused terms cost instruction fetch and branch stalls).  Any other
+// combination runs the kFGeneric instantiation, which reads the terms from
+// ConvArgs at run time.  Both compute the same operations in the same order.
+constexpr int kFBias = 1, kFRes = 2, kFResSub = 4, kFAcc = 8, kFDiv = 16, kFOutLeaky = 32, kFOutRelu = 64,
+              kFInLeaky = 128, kFGeneric = 256;
+
 // Epilogue of N rows of this lane's output channel: v[i] = the accumulated
 // sum of row r0 + i of the current chunk (r0 may differ between lanes); bias,
 // then the residual and accumulator values from the chunk's TMA boxes (32 rows
 // x BW channels of fp32, box column bc = this lane's channel; BW = 32 boxes
 // are 128B-swizzled: row r, column c at r*128 + ((c/4) ^ (r%8))*16 + (c%4)*4;
 // BW = 16 boxes are plain: r*64 + c*4), divide, activation; rows below nval
-// are stored at y + i*y_ld.  Each optional term is one uniform branch over
-// the N values and the activation is chosen once, so the unrolled code stays
-// small.
-template <int N, int BW>
+// are stored at y + i*y_ld.
+template <int N, int BW, int F>
 __device__ __forceinline__ void tn_finish(const ConvArgs& a, float (&v)[N], float bsum, uint32_t resp,
                                           int r0, int bc, float* y, int nval) {
-  if (a.bias || a.bias2) {
+  constexpr bool gen = (F & kFGeneric) != 0;
+  const bool t_bias = gen ? (a.bias || a.bias2) : (F & kFBias) != 0;
+  const bool t_res = gen ? a.res != nullptr : (F & kFRes) != 0;
+  const bool t_sub = gen ? a.res_sub != 0 : (F & kFResSub) != 0;
+  const bool t_acc = gen ? a.accin != nullptr : (F & kFAcc) != 0;
+  const bool t_div = gen ? a.out_div != 0.f : (F & kFDiv) != 0;
+  if (t_bias) {
 #pragma unroll
     for (int i = 0; i < N; ++i) v[i] += bsum;
   }
@@ -112,8 +127,8 @@ __device__ __forceinline__ void tn_finish(const ConvArgs& a, float (&v)[N], floa
                     : (uint32_t)(r * 64 + bc * 4);
   };
   constexpr uint32_t kBox = 32u * BW * 4u;
-  if (a.res) {
-    if (a.res_sub) {
+  if (t_res) {
+    if (t_sub) {
 #pragma unroll
       for (int i = 0; i < N; ++i) {
         float r;
@@ -129,8 +144,8 @@ __device__ __forceinline__ void tn_finish(const ConvArgs& a, float (&v)[N], floa
       }
     }
   }
-  if (a.accin) {
-    const uint32_t accp = resp + (a.res ? kBox : 0u);
+  if (t_acc) {
+    const uint32_t accp = resp + (t_res ? kBox : 0u);
 #pragma unroll
     for (int i = 0; i < N; ++i) {
       float qv;
@@ -138,20 +153,30 @@ __device__ __forceinline__ void tn_finish(const ConvArgs& a, float (&v)[N], floa
       v[i] = qv + v[i];
     }
   }
-  if (a.out_div != 0.f) {
+  if (t_div) {
+    const float dv = a.out_div, rd = __frcp_rn(dv);
 #pragma unroll
-    for (int i = 0; i < N; ++i) v[i] = v[i] / a.out_div;
+    for (int i = 0; i < N; ++i) v[i] = div_by(v[i], dv, rd);
   }
-  if (a.out_act == kActLeaky && a.out_slope >= 0.f && a.out_slope <= 1.f) {
+  if constexpr (gen) {
+    if (a.out_act == kActLeaky && a.out_slope >= 0.f && a.out_slope <= 1.f) {
+      const float sl = a.out_slope;
+#pragma unroll
+      for (int i = 0; i < N; ++i) v[i] = fmaxf(v[i], sl * v[i]);
+    } else if (a.out_act == kActRelu) {
+#pragma unroll
+      for (int i = 0; i < N; ++i) v[i] = fmaxf(v[i], 0.f);
+    } else if (a.out_act != kActNone) {
+#pragma unroll
+      for (int i = 0; i < N; ++i) v[i] = act_apply(v[i], a.out_act, a.out_slope);
+    }
+  } else if constexpr ((F & kFOutLeaky) != 0) {
     const float sl = a.out_slope;
 #pragma unroll
     for (int i = 0; i < N; ++i) v[i] = fmaxf(v[i], sl * v[i]);
-  } else if (a.out_act == kActRelu) {
+  } else if constexpr ((F & kFOutRelu) != 0) {
 #pragma unroll
     for (int i = 0; i < N; ++i) v[i] = fmaxf(v[i], 0.f);
-  } else if (a.out_act != kActNone) {  // not on the generator's path
-#pragma unroll
-    for (int i = 0; i < N; ++i) v[i] = act_apply(v[i], a.out_act, a.out_slope);
   }
   if (nval >= N) {
 #pragma unroll
@@ -163,6 +188,7 @@ __device__ __forceinline__ void tn_finish(const ConvArgs& a, float (&v)[N], floa
   }
 }
 
+template <int F>
 __global__ void __launch_bounds__(kThreads, 1)
     tcn_conv_kernel(const __grid_constant__ ConvArgs a, const __grid_constant__ TnMaps maps, TnPlan g) {
   extern __shared__ uint8_t smem_raw[];
@@ -215,7 +241,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int ks = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < g.total_tiles && ok; tile += gridDim.x) {
+      // resident weights: the first tile's pass loads every stage once
+      const int tile_end = g.resident ? min(g.total_tiles, (int)blockIdx.x + 1) : g.total_tiles;
+      for (int tile = blockIdx.x; tile < tile_end && ok; tile += gridDim.x) {
         const TileT c = tile_of(tile, g.co_tiles, g.tiles_t);
         for (int kb = 0; kb < nblk && ok; ++kb)
           for (int j = 0; j < g.nst; ++j, ++ks) {
@@ -261,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ptx::tc_fence_after();
           for (int j = 0; j < g.nst; ++j, ++ks) {
             const int st = ks % g.stages, round = ks / g.stages;
-            if (!ptx::mbar_wait(W_FULL + 8 * st, round & 1, kWaitNs)) {
+            if (!ptx::mbar_wait(W_FULL + 8 * st, g.resident ? 0 : (round & 1), kWaitNs)) {
               ok = false;
               atomicExch(a.err, 24);
               break;
@@ -287,7 +315,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
             first = false;
-            ptx::mma_commit(W_EMPTY + 8 * st);
+            if (!g.resident) ptx::mma_commit(W_EMPTY + 8 * st);
           }
           if (ok) ptx::mma_commit(X_EMPTY + 8 * buf);
         }
@@ -331,6 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool leaky_max = a.in_act == kActLeaky && a.in_slope >= 0.f && a.in_slope <= 1.f;
     const bool plain = a.in_act == kActNone || leaky_max;
     const float sl = leaky_max ? a.in_slope : 1.f;
+    constexpr bool gen = (F & kFGeneric) != 0;
     int ab = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < g.total_tiles && ok; tile += gridDim.x) {
@@ -352,16 +381,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 4
         for (int i = 0; i < niter; ++i) {
           float4 v = ptx::lds128(s_addr);
-          if (plain) {
+          if constexpr (gen) {
+            if (plain) {
+              v.x = fmaxf(v.x, sl * v.x);
+              v.y = fmaxf(v.y, sl * v.y);
+              v.z = fmaxf(v.z, sl * v.z);
+              v.w = fmaxf(v.w, sl * v.w);
+            } else {
+              v.x = act_apply(v.x, a.in_act, a.in_slope);
+              v.y = act_apply(v.y, a.in_act, a.in_slope);
+              v.z = act_apply(v.z, a.in_act, a.in_slope);
+              v.w = act_apply(v.w, a.in_act, a.in_slope);
+            }
+          } else if constexpr ((F & kFInLeaky) != 0) {
             v.x = fmaxf(v.x, sl * v.x);
             v.y = fmaxf(v.y, sl * v.y);
             v.z = fmaxf(v.z, sl * v.z);
             v.w = fmaxf(v.w, sl * v.w);
-          } else {
-            v.x = act_apply(v.x, a.in_act, a.in_slope);
-            v.y = act_apply(v.y, a.in_act, a.in_slope);
-            v.z = act_apply(v.z, a.in_act, a.in_slope);
-            v.w = act_apply(v.w, a.in_act, a.in_slope);
           }
           uint32_t h01, l01, h23, l23;
           split_pair(v.x, v.y, h01, l01);
@@ -385,7 +421,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // residual / accumulator boxes (32 rows x 32 channels, mode 2: x 16) are
     // loaded by the warp itself with TMA, a few chunks ahead, into its slots.
     const int wq = warp & 3;
-    const bool wlead = lane == 0;
     const bool m2 = g.mode == 2;
     const int nq2 = a.C_out / 16;            // mode 2: lane quarters holding channels
     const bool active = !m2 || wq < nq2;     // mode 2, 32 channels: quarters 2-3 are zero rows
@@ -396,8 +431,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool has_in = (a.res || a.accin) && active;
     const uint32_t box_bytes = 32u * (uint32_t)bw * 4u;
     const uint32_t slot_bytes = box_bytes * ((a.res ? 1u : 0u) + (a.accin ? 1u : 0u));
+    // input slots exist for the warps that hold channels (wq < 2 for 32 channels)
     auto slot_res = [&](int sl) { return sbase + g.off_epi + (uint32_t)(wq * g.nslot + sl) * slot_bytes; };
     auto epi_bar = [&](int sl) { return EPI + 8u * (uint32_t)(wq * g.nslot + sl); };
+    const bool loader = lane == 0;  // issues this warp's input boxes
     const int pdist = g.nslot - 1;  // input boxes are loaded this many chunks ahead
     const int bc = m2 ? (lane & 15) : lane;  // this lane's column of the boxes
     float bias_r0 = 0.f, bias_r1 = 0.f;      // this lane's channel: constant but for the channel tile
@@ -408,10 +445,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     int issued = 0;
     auto issue = [&](int f) {  // input boxes of chunk step f (lane 0)
       if (!has_in || f >= total_steps) return;
-      issued = f + 1;
       const int sl = f % g.nslot;
       const TileT c = tile_of(blockIdx.x + (f >> 3) * gridDim.x, g.co_tiles, g.tiles_t);
       const int row0 = c.tt * g.ts + 32 * (f & 7), col0 = col_of(c.ct);
+      issued = f + 1;
       // the slot was last read (generic proxy) at step f - nslot, finished by now
       ptx::fence_proxy_async_smem();
       ptx::mbar_expect_tx(epi_bar(sl), slot_bytes);
@@ -422,7 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (a.accin) ptx::tma_load_3d(dst, &maps.acc, col0, row0, c.b, epi_bar(sl));
     };
-    if (wlead)
+    if (loader)
       for (int f = 0; f < pdist; ++f) issue(f);
     int e = 0;  // this warp's next step
     bool ok = true;
@@ -444,7 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // chunk ch's results: the TMEM load of the next chunk is already in flight
       auto process = [&](int ch, const uint32_t (&r)[32]) {
         if (!ok || !active) return;
-        if (wlead) issue(e + pdist);
+        if (loader) issue(e + pdist);
         if (has_in) {
           const int sl = e % g.nslot;
           if (!__all_sync(0xffffffffu, ptx::mbar_wait(epi_bar(sl), (e / g.nslot) & 1, kWaitNs))) {
@@ -459,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
           const int row0 = t_tile + 32 * ch;
-          tn_finish<32, 32>(a, v, bsum, resp, 0, bc, ybase + (long long)row0 * a.y_ld, min(32, t_end - row0));
+          tn_finish<32, 32, F>(a, v, bsum, resp, 0, bc, ybase + (long long)row0 * a.y_ld, min(32, t_end - row0));
         } else {
           // lane l < 16: hi part of channel l, rows 0-31; lane l + 16: its lo
           // part.  Lane l finishes rows 0-15 and lane l + 16 rows 16-31, each
@@ -474,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const int r0 = hi ? 0 : 16;
           const int row0 = t_tile + 32 * ch + r0;
-          tn_finish<16, 16>(a, w, bsum, resp, r0, bc, ybase + (long long)row0 * a.y_ld, min(16, t_end - row0));
+          tn_finish<16, 16, F>(a, w, bsum, resp, r0, bc, ybase + (long long)row0 * a.y_ld, min(16, t_end - row0));
         }
       };
       uint32_t ra[32], rb[32];
@@ -498,7 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       ++it;
     }
-    if (wlead) {
+    if (loader) {
       // no TMA load left in flight into this warp's slots
       for (int f = (issued > g.nslot ? issued - g.nslot : 0); f < issued; ++f)
         ptx::mbar_wait(epi_bar(f % g.nslot), (f / g.nslot) & 1, kWaitNs);
@@ -584,17 +621,29 @@ bool tn_plan(const ConvArgs& a, int sms, TnPlan* out) {
   g.w_stage = (uint32_t)(g.mode == 1 ? 2 : 1) * kCB * kMT * 2u;
   const uint32_t limit = 227u * 1024u;
   const uint32_t slot_bytes = (g.mode == 1 ? 4096u : 2048u) * ((a.res ? 1u : 0u) + (a.accin ? 1u : 0u));
-  // preference: deep input prefetch in the epilogue (4 slots per warp), 2
-  // activation staging buffers, then as many weight stages as fit
+  // epilogue warps holding channels (mode 2 with 32 channels: lane quarters 0-1)
+  const uint32_t nact = (g.mode == 2 && a.C_out == 32) ? 2u : 4u;
+  // Preference: resident weights (a CTA reads its weights from L2 once
+  // instead of once per tile; streaming them was the MMA warp's main wait)
+  // with deep residual / accumulator prefetch in the epilogue (its box waits
+  // were the next cost), then a ring of weight stages, then shallower
+  // prefetch; two activation staging buffers where they fit.
   struct Cand {
-    int nslot, nstg, min_stages;
+    int resident, nslot, nstg, min_stages;
   };
-  const Cand cands[] = {{4, 2, 4}, {4, 1, 4}, {3, 1, 4}, {3, 1, 3}, {2, 1, 3}, {2, 1, 2}};
+  const Cand cands[] = {{1, 8, 2, 0}, {1, 8, 1, 0}, {1, 6, 1, 0}, {1, 4, 2, 0}, {1, 4, 1, 0},
+                        {0, 8, 1, 4}, {0, 6, 1, 4}, {0, 4, 2, 4}, {0, 4, 1, 4}, {1, 3, 1, 0},
+                        {1, 2, 1, 0}, {0, 3, 1, 4}, {0, 3, 1, 3}, {0, 2, 1, 3}, {0, 2, 1, 2}};
+  const int all_stages = g.nst * (a.C_in / kCB);  // one channel tile's stages (resident: co_tiles == 1)
   for (Cand cd : cands) {
-    if (slot_bytes == 0) cd.nslot = 1;  // no input boxes: the slot count only sizes the barriers
+    if (cd.resident && g.co_tiles != 1) continue;
+    if (slot_bytes == 0) {  // no input boxes: the slot count only sizes the barriers
+      if (cd.nslot > 4) continue;
+      cd.nslot = 1;
+    }
     uint32_t off = 0;
     const uint32_t off_epi = off;  // 1024-aligned: 128B-swizzled boxes
-    off += 4u * (uint32_t)cd.nslot * slot_bytes;
+    off += nact * (uint32_t)cd.nslot * slot_bytes;
     off = (off + 1023u) & ~1023u;
     const uint32_t off_x = off;
     off += 4u * g.x_plane;
@@ -606,9 +655,11 @@ bool tn_plan(const ConvArgs& a, int sms, TnPlan* out) {
     auto total = [&](int st) {
       return 1024u + off_w + (uint32_t)st * g.w_stage + 104u + 16u * st + 32u * cd.nslot + 16u;
     };
-    int stages = 8;
-    while (stages > cd.min_stages && total(stages) > limit) --stages;
+    int stages = cd.resident ? all_stages : 8;
+    if (!cd.resident)
+      while (stages > cd.min_stages && total(stages) > limit) --stages;
     if (total(stages) > limit) continue;
+    g.resident = cd.resident;
     g.nslot = cd.nslot;
     g.nstg = cd.nstg;
     g.stages = stages;
@@ -627,12 +678,14 @@ bool tn_plan(const ConvArgs& a, int sms, TnPlan* out) {
 
 }  // namespace
 
-bool tcn_enabled() {
-  static const bool on = [] {
+int tcn_enabled() {
+  static const int mode = [] {
     const char* e = getenv("RVC_CUDA_TCN");
-    return !(e && e[0] == '0');
+    if (e && e[0] == '0') return 0;
+    if (e && e[0] == '2') return 2;
+    return 1;
   }();
-  return on;
+  return mode;
 }
 
 bool tcn_shape_ok(const ConvArgs& a) {
@@ -669,6 +722,38 @@ void launch_tcn_pack(const float* w, uint16_t* out, int taps, int C_in, int C_ou
   RVC_CUDA_TRY(cudaGetLastError());
 }
 
+namespace {
+
+// The compile-time flags of a launch (kFGeneric when its terms are not one
+// of the instantiated combinations).
+int tn_flags(const ConvArgs& a) {
+  int f = 0;
+  if (a.bias || a.bias2) f |= kFBias;
+  if (a.res) f |= kFRes | (a.res_sub ? kFResSub : 0);
+  if (a.accin) f |= kFAcc;
+  if (a.out_div != 0.f) f |= kFDiv;
+  if (a.out_act == kActLeaky && a.out_slope >= 0.f && a.out_slope <= 1.f) f |= kFOutLeaky;
+  else if (a.out_act == kActRelu) f |= kFOutRelu;
+  else if (a.out_act != kActNone) return kFGeneric;
+  if (a.in_act == kActLeaky && a.in_slope >= 0.f && a.in_slope <= 1.f) f |= kFInLeaky;
+  else if (a.in_act != kActNone) return kFGeneric;
+  return f;
+}
+
+template <int F>
+void tn_launch(const ConvArgs& a, const TnMaps& maps, const TnPlan& g, int grid, int dev, cudaStream_t st) {
+  static std::atomic<uint64_t> attr_done{0};  // per instantiation, one bit per device
+  if (dev < 64 && !(attr_done.load() & (1ull << dev))) {
+    RVC_CUDA_TRY(cudaFuncSetAttribute(tcn_conv_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    attr_done.fetch_or(1ull << dev);
+  }
+  tcn_conv_kernel<F><<<grid, kThreads, g.smem_bytes, st>>>(a, maps, g);
+  note_launch();
+  RVC_CUDA_TRY(cudaGetLastError());
+}
+
+}  // namespace
+
 void launch_tcn_conv(const ConvArgs& a, cudaStream_t st) {
   RVC_CHECK_ARG(tcn_shape_ok(a), "tcn_conv: unsupported conv shape");
   RVC_CHECK_ARG(a.x_ld % 4 == 0 && a.x_bs % 4 == 0 && ((uintptr_t)a.x & 15) == 0 && ((uintptr_t)a.wpk & 15) == 0,
@@ -699,15 +784,15 @@ void launch_tcn_conv(const ConvArgs& a, cudaStream_t st) {
   const int bw = g.mode == 1 ? 32 : 16;  // epilogue box: 32 rows x bw channels (32: 128B-swizzled)
   if (a.res) encode(&maps.res, a.res, width, rows, a.B, a.res_ld, a.res_bs, bw, 32, bw == 32);
   if (a.accin) encode(&maps.acc, a.accin, width, rows, a.B, a.acc_ld, a.acc_bs, bw, 32, bw == 32);
-  static std::atomic<uint64_t> attr_done{0};
-  if (dev < 64 && !(attr_done.load() & (1ull << dev))) {
-    RVC_CUDA_TRY(cudaFuncSetAttribute(tcn_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-    attr_done.fetch_or(1ull << dev);
-  }
   const int grid = std::min(g.total_tiles, sms);
-  tcn_conv_kernel<<<grid, kThreads, g.smem_bytes, st>>>(a, maps, g);
-  note_launch();
-  RVC_CUDA_TRY(cudaGetLastError());
+  switch (tn_flags(a)) {
+    case kFBias: tn_launch<kFBias>(a, maps, g, grid, dev, st); break;
+    case kFBias | kFInLeaky | kFOutLeaky: tn_launch<kFBias | kFInLeaky | kFOutLeaky>(a, maps, g, grid, dev, st); break;
+    case kFBias | kFRes: tn_launch<kFBias | kFRes>(a, maps, g, grid, dev, st); break;
+    case kFBias | kFRes | kFAcc: tn_launch<kFBias | kFRes | kFAcc>(a, maps, g, grid, dev, st); break;
+    case kFBias | kFRes | kFAcc | kFDiv: tn_launch<kFBias | kFRes | kFAcc | kFDiv>(a, maps, g, grid, dev, st); break;
+    default: tn_launch<kFGeneric>(a, maps, g, grid, dev, st); break;
+  }
 }
 
 }  // namespace rvc
