@@ -136,15 +136,12 @@ void ConvLayer::run(Context* ctx, const ConvIO& io, bool force_simt) const {
   // Time rows as the MMA's N (tcn_conv.cu) where it measured faster than the
   // time-rows-as-M kernel (B200, both kernels on the same inputs in one
   // process, the v2-48k generator's ResBlock convs at 4 chunks per call):
-  // C >= 128 always (0.54-0.87 of the time); C = 64 for K >= 7 (0.64-0.87) and
-  // for K = 3 without residual / accumulator inputs (0.64); C = 32 for K >= 7
-  // without them (0.71-0.73).  With a residual input at C = 64, K = 3 and at
-  // C = 32 for every K it is no faster (0.96-2.2x).  At least one wave of
-  // 256-row tiles.
+  // C >= 128 always (0.54-0.87 of the time); C = 32 and 64 for K >= 7
+  // (0.64-0.89) and for K = 3 without residual / accumulator inputs
+  // (0.61-0.64).  At K = 3 with a residual input it is slower (1.1-1.4x).  At
+  // least one wave of 256-row tiles.
   const int tcn_mode = tcn_enabled();
-  const bool plain_out = !io.res && !io.accin;
-  const bool tn_pick = tcn_mode == 2 || C_out >= 128 || (C_out == 64 && (K >= 7 || plain_out)) ||
-                       (C_out == 32 && K >= 7 && plain_out);
+  const bool tn_pick = tcn_mode == 2 || C_out >= 128 || K >= 7 || (!io.res && !io.accin);
   if (use_tc && tn && tn_pick && tcn_mode != 0 && ((uintptr_t)io.x & 15) == 0 && tcn_fits(a)) {
     const long long tiles = (long long)io.B * cdiv(a.sl[0].rows, 256) * (C_out <= 64 ? 1 : C_out / 128);
     if (tiles >= ctx->num_sms()) {

@@ -16,11 +16,15 @@
 //     of channels 16q .. 16q + 15, so two MMAs D += A.Xh + A.Xl leave the
 //     hi and lo products of one channel 16 lanes apart in the same warp; one
 //     shuffle adds them (the extra Wl.Xl term is below fp32 rounding).  With
-//     32 channels the upper two quarters are zero rows.
+//     32 channels the upper two quarters repeat the lower two (free in the
+//     MMA, which is M = 128 either way), so all four epilogue warps have
+//     channels: warps 7-8 finish a tile's time rows 0-127, warps 9-10 rows
+//     128-255.
 //
 // Warp roles (11 warps, one CTA per SM, persistent over tiles):
 //   warp 0      weight producer: cp.async.bulk of one (tap, channel block)
-//               stage of packed weights into a ring
+//               stage of packed weights into a ring, or every stage once
+//               (resident weights) when they fit
 //   warp 1      TMEM owner (2 x 256 columns) + single-thread MMA issuer
 //   warp 2      activation loader: TMA of the fp32 halo tile [rows][cb]
 //               (out-of-range rows zero-filled = conv padding)
@@ -422,13 +426,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     // loaded by the warp itself with TMA, a few chunks ahead, into its slots.
     const int wq = warp & 3;
     const bool m2 = g.mode == 2;
-    const int nq2 = a.C_out / 16;            // mode 2: lane quarters holding channels
-    const bool active = !m2 || wq < nq2;     // mode 2, 32 channels: quarters 2-3 are zero rows
+    // mode 2 with 32 channels: quarters 2-3 hold copies of quarters 0-1, so
+    // warps 7-8 finish chunks 0-3 and warps 9-10 chunks 4-7 of every tile
+    const bool split = m2 && a.C_out == 32;
+    const int nch = split ? 4 : 8;            // chunks of a tile this warp finishes
+    const int c0 = split ? (wq >> 1) * 4 : 0;  // its first chunk
     const int bw = m2 ? 16 : 32;             // box width (channels)
-    auto col_of = [&](int ct) { return S.co_off + (m2 ? wq * 16 : ct * kMT + wq * 32); };
+    auto col_of = [&](int ct) { return S.co_off + (m2 ? (split ? (wq & 1) : wq) * 16 : ct * kMT + wq * 32); };
     const int ntile_cta = (g.total_tiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
-    const int total_steps = ntile_cta * 8;  // one step per chunk
-    const bool has_in = (a.res || a.accin) && active;
+    const int total_steps = ntile_cta * nch;  // one step per chunk
+    const bool has_in = a.res || a.accin;
     const uint32_t box_bytes = 32u * (uint32_t)bw * 4u;
     const uint32_t slot_bytes = box_bytes * ((a.res ? 1u : 0u) + (a.accin ? 1u : 0u));
     // input slots exist for the warps that hold channels (wq < 2 for 32 channels)
@@ -438,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int pdist = g.nslot - 1;  // input boxes are loaded this many chunks ahead
     const int bc = m2 ? (lane & 15) : lane;  // this lane's column of the boxes
     float bias_r0 = 0.f, bias_r1 = 0.f;      // this lane's channel: constant but for the channel tile
-    if (a.bias && active) {
+    if (a.bias) {
       bias_r0 = __ldg(a.bias + col_of(0) + bc);
       if (g.co_tiles > 1) bias_r1 = __ldg(a.bias + col_of(1) + bc);
     }
@@ -446,8 +453,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto issue = [&](int f) {  // input boxes of chunk step f (lane 0)
       if (!has_in || f >= total_steps) return;
       const int sl = f % g.nslot;
-      const TileT c = tile_of(blockIdx.x + (f >> 3) * gridDim.x, g.co_tiles, g.tiles_t);
-      const int row0 = c.tt * g.ts + 32 * (f & 7), col0 = col_of(c.ct);
+      const TileT c = tile_of(blockIdx.x + (f / nch) * gridDim.x, g.co_tiles, g.tiles_t);
+      const int row0 = c.tt * g.ts + 32 * (c0 + f % nch), col0 = col_of(c.ct);
       issued = f + 1;
       // the slot was last read (generic proxy) at step f - nslot, finished by now
       ptx::fence_proxy_async_smem();
@@ -476,11 +483,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int t_tile = c.tt * g.ts, t_end = min(S.rows, t_tile + g.ts);
       const int co = col_of(c.ct) + bc;
       const float br = (c.ct & 1) ? bias_r1 : bias_r0;
-      const float bsum = a.bias2 && active ? br + __ldg(a.bias2 + (long long)c.b * a.bias2_bs + co) : br;
+      const float bsum = a.bias2 ? br + __ldg(a.bias2 + (long long)c.b * a.bias2_bs + co) : br;
       float* ybase = a.y + (long long)c.b * a.y_bs + co;
       // chunk ch's results: the TMEM load of the next chunk is already in flight
       auto process = [&](int ch, const uint32_t (&r)[32]) {
-        if (!ok || !active) return;
+        if (!ok) return;
         if (loader) issue(e + pdist);
         if (has_in) {
           const int sl = e % g.nslot;
@@ -515,15 +522,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       uint32_t ra[32], rb[32];
-      ptx::tmem_ld32_async(dt, ra);
+      const int c_end = c0 + nch;
+      ptx::tmem_ld32_async(dt + (uint32_t)(c0 * 32), ra);
       ptx::tmem_wait_ld(ra);
 #pragma unroll 1
-      for (int ch = 0; ch < kNT / 32; ch += 2) {
+      for (int ch = c0; ch < c_end; ch += 2) {
         ptx::tmem_ld32_async(dt + (uint32_t)((ch + 1) * 32), rb);
         process(ch, ra);
         ++e;
         ptx::tmem_wait_ld(rb);
-        if (ch + 2 < kNT / 32) {
+        if (ch + 2 < c_end) {
           ptx::tmem_ld32_async(dt + (uint32_t)((ch + 2) * 32), ra);
         } else {  // every column of this accumulator set is in registers
           ptx::tc_fence_before();
@@ -531,7 +539,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         process(ch + 1, rb);
         ++e;
-        if (ch + 2 < kNT / 32) ptx::tmem_wait_ld(ra);
+        if (ch + 2 < c_end) ptx::tmem_wait_ld(ra);
       }
       ++it;
     }
@@ -576,7 +584,9 @@ __global__ void tcn_pack_kernel(const float* __restrict__ w, uint16_t* __restric
       co = ct * kMT + m;
       lo = hl == 1;
     } else {
-      co = (m >> 5) * 16 + (m & 15);
+      // 32 channels: lane quarters 2-3 repeat quarters 0-1 (the epilogue then
+      // splits each tile's columns over all four warps)
+      co = (C_out == 32 ? ((m >> 5) & 1) : (m >> 5)) * 16 + (m & 15);
       lo = (m & 16) != 0;
     }
     const float x = co < C_out ? w[((long long)tap * C_in + ci) * C_out + co] : 0.f;
@@ -621,8 +631,7 @@ bool tn_plan(const ConvArgs& a, int sms, TnPlan* out) {
   g.w_stage = (uint32_t)(g.mode == 1 ? 2 : 1) * kCB * kMT * 2u;
   const uint32_t limit = 227u * 1024u;
   const uint32_t slot_bytes = (g.mode == 1 ? 4096u : 2048u) * ((a.res ? 1u : 0u) + (a.accin ? 1u : 0u));
-  // epilogue warps holding channels (mode 2 with 32 channels: lane quarters 0-1)
-  const uint32_t nact = (g.mode == 2 && a.C_out == 32) ? 2u : 4u;
+  const uint32_t nact = 4u;  // epilogue warps with input slots
   // Preference: resident weights (a CTA reads its weights from L2 once
   // instead of once per tile; streaming them was the MMA warp's main wait)
   // with deep residual / accumulator prefetch in the epilogue (its box waits
