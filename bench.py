@@ -204,7 +204,7 @@ def hubert_cpu_sample(T, steps=1):
         if "hubert" not in _REF_MODELS:
             _REF_MODELS["hubert"] = ref.hubert(syn.make_hubert_weights(0))
         enc = _REF_MODELS["hubert"]
-        fn = lambda: enc.encode(x[None, :], version=2)  # noqa: E731
+        fn = lambda: enc.encode(x, version=2)  # noqa: E731
     else:
         from oracle import hubert as OH
         sd = OH.prepare(syn.make_hubert_weights(0))
@@ -728,9 +728,10 @@ def run_hubert_reference(args, world, rank):
 
 def pipeline_cpu_estimate(chunk_samples, frames_total, audio_s):
     """CPU time of the config-4 pipeline, composed from bounded samples of each
-    stage on the host cores: the oracle models (HuBERT, RMVPE, v2-40k
-    synthesizer, top-8 retrieval against the 200000 x 768 index) timed on short
-    inputs and scaled by the workload's samples / frames, plus the reference's
+    stage on the host cores: the reference's models where its runtime is
+    available, else the oracle port (HuBERT, RMVPE, v2-40k synthesizer, top-8
+    retrieval against the 200000 x 768 index), timed on short inputs and scaled
+    by the workload's samples / frames, plus the reference's
     own scipy ``filtfilt`` and the oracle's split / change_rms on the full
     signal.  Returns (seconds per workload, sample description)."""
     from scipy import signal
@@ -985,8 +986,9 @@ def config0_figure(args, local, timed, max_over_ranks, world):
 
 
 # DRAM bytes of the tensor-core conv launches for one v2-48k chunk of 1000 frames, from an ncu
-# capture of a 4-chunk call (36.33 GB over its 135 conv launches); traffic grows with rows.
-SYNTH_DRAM_BYTES_48K_PER_1000_FRAMES = 9.0825e9
+# capture of the GeneratorNSF convs of an 8-chunk call (75.6 GB) plus enc_p / flow / conv_pre
+# (76 MB per chunk, 4-chunk capture); traffic grows with rows.
+SYNTH_DRAM_BYTES_48K_PER_1000_FRAMES = 9.53e9
 
 
 def synth_traffic(sr, P, chunks):
@@ -1132,9 +1134,9 @@ def run_ours(args, world, rank, local):
                          "achieved": achieved, "peak": ps, "unit": "TFLOP/s",
                          "frac": (achieved / ps) if achieved else None,
                          "traffic": synth_traffic(sr, P, n_local),
-                         "traffic_note": "DRAM bytes of this rank's conv launches per step: an ncu capture of one "
-                                         "4-chunk v2-48k call (dram__bytes_read.sum + dram__bytes_write.sum over its "
-                                         "135 conv launches) scaled by chunks x frames; a lower bound, as the small "
+                         "traffic_note": "DRAM bytes of this rank's conv launches per step: ncu captures of "
+                                         "8- and 4-chunk v2-48k calls (dram__bytes_read.sum + dram__bytes_write.sum over the "
+                                         "conv launches) scaled by chunks x frames; a lower bound, as the smaller "
                                          "call keeps its early-stage tensors in L2",
                          "peak_source": f"{src} bf16 dense sustained",
                          "note": "achieved = useful fp32 GEMM FLOPs / kernel time; BF16x3 runs 3 bf16 MMAs per "
