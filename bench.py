@@ -1067,9 +1067,9 @@ def run_ours(args, world, rank, local):
                                                             _lib._p(d_wave + s * (h_wave.nbytes // n_local))))
 
     def step_e2e():
-        for s, g in groups:
-            h_wave[s:s + g] = m.infer_batch(h_phone[s:s + g], h_pitch[s:s + g], h_f0[s:s + g], h_sid[s:s + g],
-                                            h_nz[s:s + g], h_ns[s:s + g])
+        # the public call a user makes for many chunks: groups of G synthesized
+        # with each group's host<->device copies overlapping the next group
+        h_wave[:] = m.infer_batch(h_phone, h_pitch, h_f0, h_sid, h_nz, h_ns, group=G)
 
     stream = torch.cuda.ExternalStream(ctx.stream(), device=local)
 

@@ -180,6 +180,14 @@ int32_t rvc_cuda_synth_finalize(int64_t model);
 int32_t rvc_cuda_synth_infer(int64_t model, int32_t B, int32_t P, const float* phone, const int64_t* pitch,
                              const float* nsff0, const int64_t* sid, const float* nz, const float* ns,
                              float* wave);
+/* rvc_cuda_synth_infer over B chunks in groups of G chunks (each group's
+ * result equals rvc_cuda_synth_infer of those chunks): a group's inputs are
+ * copied up and its waveforms down on two copy streams while the neighbouring
+ * groups compute, so the host<->device traffic overlaps the synthesis.  The
+ * batched-decode loop of decode_batch (vits.py:1847-1878) over many chunks. */
+int32_t rvc_cuda_synth_infer_grouped(int64_t model, int32_t B, int32_t G, int32_t P, const float* phone,
+                                     const int64_t* pitch, const float* nsff0, const int64_t* sid, const float* nz,
+                                     const float* ns, float* wave);
 /* Same with device pointers (allocated by rvc_cuda_alloc); asynchronous on
  * the context stream (call rvc_cuda_sync before reading `wave`). */
 int32_t rvc_cuda_synth_infer_device(int64_t model, int32_t B, int32_t P, const float* phone,

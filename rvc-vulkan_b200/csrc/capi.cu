@@ -676,6 +676,20 @@ int32_t rvc_cuda_synth_infer(int64_t model, int32_t B, int32_t P, const float* p
   });
 }
 
+int32_t rvc_cuda_synth_infer_grouped(int64_t model, int32_t B, int32_t G, int32_t P, const float* phone,
+                                     const int64_t* pitch, const float* nsff0, const int64_t* sid, const float* nz,
+                                     const float* ns, float* wave) {
+  return on_synth(model, [&](SynthModel* m) {
+    RVC_CHECK_ARG(B >= 1 && G >= 1 && P >= 1, "synth_infer_grouped: B, G and P must be positive");
+    for (int64_t i = 0; i < (int64_t)B * P; ++i)
+      RVC_CHECK_ARG(pitch[i] >= -256 && pitch[i] < 256, "synth_infer_grouped: pitch id out of [0,256)");
+    for (int i = 0; i < B; ++i)
+      RVC_CHECK_ARG(sid[i] >= -m->cfg.n_spk && sid[i] < m->cfg.n_spk, "synth_infer_grouped: speaker id out of range");
+    m->infer_host_grouped(B, G, P, phone, (const long long*)pitch, nsff0, (const long long*)sid, nz, ns, wave);
+    finish(m->ctx);
+  });
+}
+
 int32_t rvc_cuda_synth_infer_device(int64_t model, int32_t B, int32_t P, const float* phone, const int64_t* pitch,
                                     const float* nsff0, const int64_t* sid, const float* nz, const float* ns,
                                     float* wave) {

@@ -455,4 +455,93 @@ void SynthModel::infer_host(int B, int P, const float* phone, const long long* p
   RVC_CUDA_TRY(cudaMemcpyAsync(wave, buf("out_wave"), sizeof(float) * (size_t)B * P * upp, cudaMemcpyDeviceToHost, st));
 }
 
+SynthModel::~SynthModel() {
+  // every grouped call returns with its copies finished; nothing is in flight
+  for (cudaEvent_t& e : ev_)
+    if (e) cudaEventDestroy(e);
+  if (up_st_) cudaStreamDestroy(up_st_);
+  if (down_st_) cudaStreamDestroy(down_st_);
+}
+
+void SynthModel::infer_host_grouped(int B, int G, int P, const float* phone, const long long* pitch,
+                                    const float* nsff0, const long long* sid, const float* nz, const float* ns,
+                                    float* wave) {
+  RVC_CHECK_ARG(B >= 1 && G >= 1 && P >= 1, "synth: B, G and P must be positive");
+  if (G >= B) {
+    infer_host(B, P, phone, pitch, nsff0, sid, nz, ns, wave);
+    return;
+  }
+  if (!finalized_) throw Error{kErrState, "synth: finalize() not called after the last weight upload"};
+  ensure_ws(G, P);
+  const int H = cfg.hidden, upp = cfg.upp();
+  if (!up_st_) {
+    RVC_CUDA_TRY(cudaStreamCreateWithFlags(&up_st_, cudaStreamNonBlocking));
+    RVC_CUDA_TRY(cudaStreamCreateWithFlags(&down_st_, cudaStreamNonBlocking));
+    for (cudaEvent_t& e : ev_) RVC_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  }
+  cudaEvent_t* ev_up = ev_;
+  cudaEvent_t* ev_done = ev_ + 2;
+  cudaEvent_t* ev_down = ev_ + 4;
+  // bytes per chunk of the six inputs and of the waveform
+  const size_t per[6] = {sizeof(float) * (size_t)P * cfg.phone_dim, sizeof(long long) * (size_t)P,
+                         sizeof(float) * (size_t)P, sizeof(long long), sizeof(float) * (size_t)H * P,
+                         sizeof(float) * (size_t)P * upp};
+  const size_t per_out = sizeof(float) * (size_t)P * upp;
+  const uint8_t* src[6] = {(const uint8_t*)phone, (const uint8_t*)pitch, (const uint8_t*)nsff0,
+                           (const uint8_t*)sid,   (const uint8_t*)nz,    (const uint8_t*)ns};
+  if (G > g_G_ || P > g_P_) {  // no copy is in flight between calls
+    g_G_ = std::max(G, g_G_);
+    g_P_ = std::max(P, g_P_);
+    const size_t per_max[6] = {sizeof(float) * (size_t)g_P_ * cfg.phone_dim, sizeof(long long) * (size_t)g_P_,
+                               sizeof(float) * (size_t)g_P_, sizeof(long long), sizeof(float) * (size_t)H * g_P_,
+                               sizeof(float) * (size_t)g_P_ * upp};
+    for (int b = 0; b < 2; ++b) {
+      for (int i = 0; i < 6; ++i) gin_[b][i] = DevBuf(ctx, per_max[i] * (size_t)g_G_);
+      gout_[b] = DevBuf(ctx, sizeof(float) * (size_t)g_P_ * upp * (size_t)g_G_);
+    }
+    // the new buffers are zero-filled on ctx->stream: copies on the other
+    // streams start after that
+    RVC_CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  }
+  const int ng = cdiv(B, G);
+  auto count = [&](int g) { return std::min(G, B - g * G); };
+  auto up = [&](int g) {  // group g's inputs, once group g - 2 has been computed from the same buffers
+    const int b = g & 1, nb = count(g);
+    if (g >= 2) RVC_CUDA_TRY(cudaStreamWaitEvent(up_st_, ev_done[b], 0));
+    for (int i = 0; i < 6; ++i)
+      RVC_CUDA_TRY(cudaMemcpyAsync(gin_[b][i].p, src[i] + (size_t)g * G * per[i], (size_t)nb * per[i],
+                                   cudaMemcpyHostToDevice, up_st_));
+    RVC_CUDA_TRY(cudaEventRecord(ev_up[b], up_st_));
+  };
+  auto compute = [&](int g) {  // after its inputs arrived and group g - 2's waveforms left
+    const int b = g & 1, nb = count(g);
+    RVC_CUDA_TRY(cudaStreamWaitEvent(ctx->stream, ev_up[b], 0));
+    if (g >= 2) RVC_CUDA_TRY(cudaStreamWaitEvent(ctx->stream, ev_down[b], 0));
+    infer_device(nb, P, gin_[b][0].f(), gin_[b][1].as<long long>(), gin_[b][2].f(), gin_[b][3].as<long long>(),
+                 gin_[b][4].f(), gin_[b][5].f(), gout_[b].f());
+    RVC_CUDA_TRY(cudaEventRecord(ev_done[b], ctx->stream));
+  };
+  auto down = [&](int g) {
+    const int b = g & 1, nb = count(g);
+    RVC_CUDA_TRY(cudaStreamWaitEvent(down_st_, ev_done[b], 0));
+    RVC_CUDA_TRY(cudaMemcpyAsync(wave + (size_t)g * G * P * upp, gout_[b].p, (size_t)nb * per_out,
+                                 cudaMemcpyDeviceToHost, down_st_));
+    RVC_CUDA_TRY(cudaEventRecord(ev_down[b], down_st_));
+  };
+  // group g + 1 is queued before group g's download, so a download from
+  // pageable memory (which returns only when done) leaves the next group
+  // already queued on the device
+  up(0);
+  compute(0);
+  for (int g = 0; g < ng; ++g) {
+    if (g + 1 < ng) {
+      up(g + 1);
+      compute(g + 1);
+    }
+    down(g);
+  }
+  RVC_CUDA_TRY(cudaStreamSynchronize(up_st_));
+  RVC_CUDA_TRY(cudaStreamSynchronize(down_st_));
+}
+
 }  // namespace rvc

@@ -44,6 +44,14 @@ class SynthModel {
                     const long long* sid, const float* nz, const float* ns, float* wave);
   void infer_host(int B, int P, const float* phone, const long long* pitch, const float* nsff0,
                   const long long* sid, const float* nz, const float* ns, float* wave);
+  // Host buffers, B chunks in groups of G (each group exactly as infer_host
+  // of those chunks): a group's inputs go up on one copy stream and its
+  // waveforms come down on another while the neighbouring groups compute on
+  // ctx->stream (double-buffered device inputs and outputs, ordered by
+  // events).  Returns with every copy finished.
+  void infer_host_grouped(int B, int G, int P, const float* phone, const long long* pitch, const float* nsff0,
+                          const long long* sid, const float* nz, const float* ns, float* wave);
+  ~SynthModel();
   // Partial synthesis of one chunk: wave [length * upp] for frames [head, head + length).
   void infer_partial_device(int P, int head, int length, const float* phone, const long long* pitch,
                             const float* nsff0, const long long* sid, const float* nz, const float* ns,
@@ -75,6 +83,12 @@ class SynthModel {
   ConvLayer conv_pre_, ups_[8], rb1_[8][3][3], rb2_[8][3][3];
   int noise_k_[8] = {0}, noise_s_[8] = {0};
   float lin_w_ = 0.f, lin_b_ = 0.f;  // dec.m_source.l_linear (1x1)
+  // grouped host path: copy streams, events (inputs up [2], group computed
+  // [2], waveforms down [2]) and the double-buffered group inputs / outputs
+  cudaStream_t up_st_ = nullptr, down_st_ = nullptr;
+  cudaEvent_t ev_[6] = {};
+  DevBuf gin_[2][6], gout_[2];
+  int g_G_ = 0, g_P_ = 0;
   // workspace
   int ws_B = 0, ws_P = 0;
   std::map<std::string, DevBuf> ws_;

@@ -89,6 +89,7 @@ _SIGS = {
     "rvc_cuda_synth_set_weight": ([_i64, C.c_char_p, _fp, _ip64, _i32], _i32),
     "rvc_cuda_synth_finalize": ([_i64], _i32),
     "rvc_cuda_synth_infer": ([_i64, _i32, _i32, _fp, _ip64, _fp, _ip64, _fp, _fp, _fp], _i32),
+    "rvc_cuda_synth_infer_grouped": ([_i64, _i32, _i32, _i32, _fp, _ip64, _fp, _ip64, _fp, _fp, _fp], _i32),
     "rvc_cuda_synth_infer_device": ([_i64, _i32, _i32, _p, _p, _p, _p, _p, _p, _p], _i32),
     "rvc_cuda_synth_infer_partial": ([_i64, _i32, _i32, _i32, _fp, _ip64, _fp, _ip64, _fp, _fp, _fp], _i32),
     "rvc_cuda_synth_tap": ([_i64, C.c_char_p, _fp, _i64], _i32),

@@ -141,9 +141,12 @@ class CudaSynthesizer:
         return nz, ns
 
     # ---------------------------------------------------------------- infer
-    def infer_batch(self, phone, pitch, nsff0, sid, nz, ns) -> np.ndarray:
+    def infer_batch(self, phone, pitch, nsff0, sid, nz, ns, group: Optional[int] = None) -> np.ndarray:
         """B equal-length chunks: ``phone [B,P,D]``, ``pitch [B,P]``, ``nsff0 [B,P]``,
-        ``sid [B]``, ``nz [B,h,P]``, ``ns [B,P*upp]`` -> ``[B, P*upp]``."""
+        ``sid [B]``, ``nz [B,h,P]``, ``ns [B,P*upp]`` -> ``[B, P*upp]``.
+        ``group``: synthesize in groups of that many chunks with the copies of
+        one group overlapping the synthesis of the next (each group's result is
+        that of ``infer_batch`` on those chunks)."""
         phone = np.ascontiguousarray(phone, dtype=np.float32)
         B, P, D = phone.shape
         pitch = np.ascontiguousarray(np.asarray(pitch).reshape(B, P), dtype=np.int64)
@@ -152,6 +155,10 @@ class CudaSynthesizer:
         nz = np.ascontiguousarray(np.asarray(nz, dtype=np.float32).reshape(B, self.hidden, P))
         ns = np.ascontiguousarray(np.asarray(ns, dtype=np.float32).reshape(B, P * self.upp))
         out = np.empty((B, P * self.upp), np.float32)
+        if group is not None and 0 < int(group) < B:
+            check(lib.rvc_cuda_synth_infer_grouped(self.handle, B, int(group), P, fptr(phone), iptr(pitch),
+                                                   fptr(nsff0), iptr(sid), fptr(nz), fptr(ns), fptr(out)))
+            return out
         check(lib.rvc_cuda_synth_infer(self.handle, B, P, fptr(phone), iptr(pitch), fptr(nsff0), iptr(sid),
                                        fptr(nz), fptr(ns), fptr(out)))
         return out

@@ -92,6 +92,25 @@ def test_synth_batch_equals_single():
         np.testing.assert_allclose(batch[i], one, rtol=0, atol=1e-6)
 
 
+def test_grouped_infer_equals_per_group_calls():
+    """``infer_batch(..., group=G)`` (copies of one group overlapping the next
+    group's synthesis on separate streams) gives exactly the per-group
+    ``infer_batch`` results, the short last group included, twice in a row
+    (the double buffers are reused)."""
+    w, m = model(48000, 0)
+    P, B, G = 40, 5, 2
+    ins = [syn.make_vits_inputs(P, 300 + i) for i in range(B)]
+    noise = [syn.make_vits_noise(P, m.upp, 400 + i) for i in range(B)]
+    args = (np.concatenate([i[0] for i in ins]), np.concatenate([i[1] for i in ins]),
+            np.concatenate([i[2] for i in ins]), np.concatenate([i[3] for i in ins]),
+            np.concatenate([n[0] for n in noise]), np.stack([n[1].reshape(-1) for n in noise]))
+    ref = np.concatenate([m.infer_batch(*[a[s:s + G] for a in args]) for s in range(0, B, G)])
+    for _ in range(2):
+        got = m.infer_batch(*args, group=G)
+        np.testing.assert_array_equal(got, ref)
+    assert np.array_equal(m.infer_batch(*args, group=B), m.infer_batch(*args))
+
+
 def test_synth_long_chunk_properties():
     """Full 10 s chunk (P=1000): output shape, finite, bounded, deterministic."""
     w, m = model(40000, 0)
