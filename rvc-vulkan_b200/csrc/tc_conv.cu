@@ -64,8 +64,34 @@ struct TcPlan {
 
 // Direct epilogue for N (16 or 32) consecutive output channels of one row;
 // every global load of the step is issued before any is used.
-template <int N>
+// Terms of the prologue / epilogue a launch uses, as compile-time flags of
+// tc_conv_kernel: the models' layers use a handful of combinations, and with
+// only those terms compiled the epilogue warps skip the instruction fetch and
+// branches of the unused ones (the activation switch alone was unrolled 32x).
+// kTGeneric reads the terms from ConvArgs at run time.  Same operations in
+// the same order either way.
+constexpr int kTBias = 1, kTBias2 = 2, kTRes = 4, kTResSub = 8, kTAcc = 16, kTDiv = 32, kTLeaky = 64, kTRelu = 128,
+              kTGelu = 256, kTGeneric = 512;
+
+// the output activation of one value (act_apply's formulas)
+template <int F>
+__device__ __forceinline__ float act_val(float x, const ConvArgs& a) {
+  if constexpr ((F & kTGeneric) != 0) return act_apply(x, a.out_act, a.out_slope);
+  else if constexpr ((F & kTLeaky) != 0) return act_apply(x, kActLeaky, a.out_slope);
+  else if constexpr ((F & kTRelu) != 0) return act_apply(x, kActRelu, 0.f);
+  else if constexpr ((F & kTGelu) != 0) return gelu_as(x);
+  else return x;
+}
+
+template <int N, int F>
 __device__ __forceinline__ void epi_direct(const ConvArgs& a, int b, int prow, int cg0, float (&v)[N], int vec) {
+  constexpr bool gen = (F & kTGeneric) != 0;
+  const bool t_bias = gen ? a.bias != nullptr : (F & kTBias) != 0;
+  const bool t_bias2 = gen ? a.bias2 != nullptr : (F & kTBias2) != 0;
+  const bool t_res = gen ? a.res != nullptr : (F & kTRes) != 0;
+  const bool t_sub = gen ? a.res_sub != 0 : (F & kTResSub) != 0;
+  const bool t_acc = gen ? a.accin != nullptr : (F & kTAcc) != 0;
+  const bool t_div = gen ? a.out_div != 0.f : (F & kTDiv) != 0;
   if (!vec) {
 #pragma unroll
     for (int i = 0; i < N; ++i) conv_epilogue(a, b, prow, cg0 + i, v[i]);
@@ -73,13 +99,13 @@ __device__ __forceinline__ void epi_direct(const ConvArgs& a, int b, int prow, i
   }
   constexpr int Q = N / 4;
   float4 rb[Q], ra[Q];
-  if (a.res) {
+  if (t_res) {
     const float4* p =
         reinterpret_cast<const float4*>(a.res + (long long)b * a.res_bs + (long long)prow * a.res_ld + cg0);
 #pragma unroll
     for (int q = 0; q < Q; ++q) rb[q] = p[q];
   }
-  if (a.accin) {
+  if (t_acc) {
     const float4* p =
         reinterpret_cast<const float4*>(a.accin + (long long)b * a.acc_bs + (long long)prow * a.acc_ld + cg0);
 #pragma unroll
@@ -89,19 +115,19 @@ __device__ __forceinline__ void epi_direct(const ConvArgs& a, int b, int prow, i
 #pragma unroll
   for (int q = 0; q < Q; ++q) {
     float x[4] = {v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]};
-    const float4 bi = a.bias ? __ldg(reinterpret_cast<const float4*>(a.bias + cg0) + q) : make_float4(0, 0, 0, 0);
-    const float4 b2 = a.bias2 ? __ldg(reinterpret_cast<const float4*>(a.bias2 + (long long)b * a.bias2_bs + cg0) + q)
+    const float4 bi = t_bias ? __ldg(reinterpret_cast<const float4*>(a.bias + cg0) + q) : make_float4(0, 0, 0, 0);
+    const float4 b2 = t_bias2 ? __ldg(reinterpret_cast<const float4*>(a.bias2 + (long long)b * a.bias2_bs + cg0) + q)
                               : make_float4(0, 0, 0, 0);
     const float bb[4] = {bi.x, bi.y, bi.z, bi.w}, b22[4] = {b2.x, b2.y, b2.z, b2.w};
     const float rr[4] = {rb[q].x, rb[q].y, rb[q].z, rb[q].w}, aa[4] = {ra[q].x, ra[q].y, ra[q].z, ra[q].w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       float t = x[e];
-      if (a.bias) t += bb[e];
-      if (a.bias2) t += b22[e];
-      if (a.res) t = a.res_sub ? (rr[e] - t) : (t + rr[e]);
-      if (a.accin) t = aa[e] + t;
-      if (a.out_div != 0.f) t = t / a.out_div;
+      if (t_bias) t += bb[e];
+      if (t_bias2) t += b22[e];
+      if (t_res) t = t_sub ? (rr[e] - t) : (t + rr[e]);
+      if (t_acc) t = aa[e] + t;
+      if (t_div) t = t / a.out_div;
       out[4 * q + e] = t;
     }
   }
@@ -114,9 +140,8 @@ __device__ __forceinline__ void epi_direct(const ConvArgs& a, int b, int prow, i
   float4* p = reinterpret_cast<float4*>(a.y + o);
 #pragma unroll
   for (int q = 0; q < Q; ++q)
-    p[q] = make_float4(act_apply(out[4 * q], a.out_act, a.out_slope), act_apply(out[4 * q + 1], a.out_act, a.out_slope),
-                       act_apply(out[4 * q + 2], a.out_act, a.out_slope),
-                       act_apply(out[4 * q + 3], a.out_act, a.out_slope));
+    p[q] = make_float4(act_val<F>(out[4 * q], a), act_val<F>(out[4 * q + 1], a), act_val<F>(out[4 * q + 2], a),
+                       act_val<F>(out[4 * q + 3], a));
 }
 
 // Issues the BF16x3 MMAs of one weight stage: for each 16-wide k step and each
@@ -243,8 +268,33 @@ __device__ __forceinline__ void act_row(float (&x)[32], int act, float slope) {
   }
 }
 
+template <int F>
+__device__ __forceinline__ void act_row_t(float (&x)[32], const ConvArgs& a) {
+  if constexpr ((F & kTGeneric) != 0) {
+    act_row(x, a.out_act, a.out_slope);
+  } else if constexpr ((F & kTLeaky) != 0) {  // slope in [0, 1] (tc_flags)
+    const float sl = a.out_slope;
+#pragma unroll
+    for (int k = 0; k < 32; ++k) x[k] = fmaxf(x[k], sl * x[k]);
+  } else if constexpr ((F & kTRelu) != 0) {
+#pragma unroll
+    for (int k = 0; k < 32; ++k) x[k] = act_apply(x[k], kActRelu, 0.f);
+  } else if constexpr ((F & kTGelu) != 0) {
+#pragma unroll
+    for (int k = 0; k < 32; ++k) x[k] = gelu_as(x[k]);
+  }
+}
+
+template <int F>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_conv_kernel(const __grid_constant__ ConvArgs a, const __grid_constant__ TcMaps maps, TcPlan g) {
+  constexpr bool gen = (F & kTGeneric) != 0;
+  const bool t_bias = gen ? a.bias != nullptr : (F & kTBias) != 0;
+  const bool t_bias2 = gen ? a.bias2 != nullptr : (F & kTBias2) != 0;
+  const bool t_res = gen ? a.res != nullptr : (F & kTRes) != 0;
+  const bool t_sub = gen ? a.res_sub != 0 : (F & kTResSub) != 0;
+  const bool t_acc = gen ? a.accin != nullptr : (F & kTAcc) != 0;
+  const bool t_div = gen ? a.out_div != 0.f : (F & kTDiv) != 0;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   const int BN = a.bn, CB = a.cb;
@@ -488,11 +538,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = tp; e < total; e += 128) {
             const int r = e / c4n, c4 = e - r * c4n;
             float4 v = ptx::lds128(src + (uint32_t)e * 16u);
-            if (a.in_act) {
-              v.x = act_apply(v.x, a.in_act, a.in_slope);
-              v.y = act_apply(v.y, a.in_act, a.in_slope);
-              v.z = act_apply(v.z, a.in_act, a.in_slope);
-              v.w = act_apply(v.w, a.in_act, a.in_slope);
+            if constexpr (gen) {
+              if (a.in_act) {
+                v.x = act_apply(v.x, a.in_act, a.in_slope);
+                v.y = act_apply(v.y, a.in_act, a.in_slope);
+                v.z = act_apply(v.z, a.in_act, a.in_slope);
+                v.w = act_apply(v.w, a.in_act, a.in_slope);
+              }
+            } else if (a.in_act) {  // leaky with slope in [0, 1] (tc_flags)
+              v.x = act_apply(v.x, kActLeaky, a.in_slope);
+              v.y = act_apply(v.y, kActLeaky, a.in_slope);
+              v.z = act_apply(v.z, kActLeaky, a.in_slope);
+              v.w = act_apply(v.w, kActLeaky, a.in_slope);
             }
             uint32_t h01, l01, h23, l23;
             split_pair(v.x, v.y, h01, l01);
@@ -539,16 +596,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         // this warp's previous store from the slot (step f - nslot) has finished
         // reading it; the nslot - pdist - 1 newer stores may still be in flight
         ptx::bulk_wait_read(g.nslot - pdist - 1);
-        const uint32_t bytes = (a.res ? kWarpSlotBytes : 0u) + (a.accin ? kWarpSlotBytes : 0u);
+        const uint32_t bytes = (t_res ? kWarpSlotBytes : 0u) + (t_acc ? kWarpSlotBytes : 0u);
         ptx::mbar_expect_tx(epi_bar(sl), bytes);
         if (g.ephase) {  // transposed-conv phase p: rows q*up + p through the 4-D view
-          if (a.res)
+          if (t_res)
             ptx::tma_load_4d(sbase + slot_main(sl) + wslot, &maps.res, col0, S.out_r0, row0, c.b, epi_bar(sl));
-          if (a.accin)
+          if (t_acc)
             ptx::tma_load_4d(sbase + slot_aux(sl) + wslot, &maps.acc, col0, S.out_r0, row0, c.b, epi_bar(sl));
         } else {
-          if (a.res) ptx::tma_load_3d(sbase + slot_main(sl) + wslot, &maps.res, col0, row0, c.b, epi_bar(sl));
-          if (a.accin) ptx::tma_load_3d(sbase + slot_aux(sl) + wslot, &maps.acc, col0, row0, c.b, epi_bar(sl));
+          if (t_res) ptx::tma_load_3d(sbase + slot_main(sl) + wslot, &maps.res, col0, row0, c.b, epi_bar(sl));
+          if (t_acc) ptx::tma_load_3d(sbase + slot_aux(sl) + wslot, &maps.acc, col0, row0, c.b, epi_bar(sl));
         }
       };
       if (g.off_bias) {  // stage the bias vector once per CTA
@@ -603,7 +660,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t mainp = sbase + slot_main(sl) + wslot + (uint32_t)lane * 128u;
           const uint32_t auxp = sbase + slot_aux(sl) + wslot + (uint32_t)lane * 128u;
           // each optional term is one uniform branch per 32 values
-          if (a.bias) {
+          if (t_bias) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
               const float4 t = g.off_bias ? ptx::lds128(sbase + g.off_bias + (uint32_t)(col0 + 4 * j) * 4u)
@@ -611,15 +668,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
             }
           }
-          if (a.bias2) {
+          if (t_bias2) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
               const float4 t = __ldg(reinterpret_cast<const float4*>(a.bias2 + (long long)c.b * a.bias2_bs + col0) + j);
               v[4 * j] += t.x; v[4 * j + 1] += t.y; v[4 * j + 2] += t.z; v[4 * j + 3] += t.w;
             }
           }
-          if (a.res) {
-            if (a.res_sub) {
+          if (t_res) {
+            if (t_sub) {
 #pragma unroll
               for (int j = 0; j < 8; ++j) {
                 const float4 t = ptx::lds128(mainp + (uint32_t)((j ^ (lane & 7)) << 4));
@@ -634,7 +691,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           }
-          if (a.accin) {
+          if (t_acc) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
               const float4 t = ptx::lds128(auxp + (uint32_t)((j ^ (lane & 7)) << 4));
@@ -642,12 +699,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               v[4 * j + 2] = t.z + v[4 * j + 2]; v[4 * j + 3] = t.w + v[4 * j + 3];
             }
           }
-          if (a.out_div != 0.f) {
+          if (t_div) {
             const float dv = a.out_div, rd = __frcp_rn(dv);
 #pragma unroll
             for (int k = 0; k < 32; ++k) v[k] = div_by(v[k], dv, rd);
           }
-          act_row(v, a.out_act, a.out_slope);
+          act_row_t<F>(v, a);
 #pragma unroll
           for (int j = 0; j < 8; ++j)
             ptx::sts128(mainp + (uint32_t)((j ^ (lane & 7)) << 4),
@@ -706,7 +763,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int k = 0; k < 16; ++k) v[16 * h + k] += w2[k];
               }
             }
-            if (valid) epi_direct<32>(a, c.b, prow, S.co_off + c.nt * BN + col, v, g.vec);
+            if (valid) epi_direct<32, F>(a, c.b, prow, S.co_off + c.nt * BN + col, v, g.vec);
           }
           if (col < BN) {
             float v[16];
@@ -717,7 +774,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int k = 0; k < 16; ++k) v[k] += w2[k];
             }
-            if (valid) epi_direct<16>(a, c.b, prow, S.co_off + c.nt * BN + col, v, g.vec);
+            if (valid) epi_direct<16, F>(a, c.b, prow, S.co_off + c.nt * BN + col, v, g.vec);
           }
         }
         ptx::tc_fence_before();
@@ -745,6 +802,43 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   });
   if (!fn) throw Error{kErrCuda, "cuTensorMapEncodeTiled is not available from the driver"};
   return fn;
+}
+
+// The compile-time flags of a launch (kTGeneric when its terms are not
+// expressible: a pre-activation copy, a prologue activation other than
+// leaky / none, an activation other than leaky / relu / gelu).
+static int tc_flags(const ConvArgs& a) {
+  if (a.y_raw) return kTGeneric;
+  if (a.in_act != kActNone && !(a.in_act == kActLeaky && a.in_slope >= 0.f && a.in_slope <= 1.f)) return kTGeneric;
+  int f = 0;
+  if (a.bias) f |= kTBias;
+  if (a.bias2) f |= kTBias2;
+  if (a.res) f |= kTRes | (a.res_sub ? kTResSub : 0);
+  if (a.accin) f |= kTAcc;
+  if (a.out_div != 0.f) f |= kTDiv;
+  switch (a.out_act) {
+    case kActNone: break;
+    case kActLeaky:
+      if (!(a.out_slope >= 0.f && a.out_slope <= 1.f)) return kTGeneric;
+      f |= kTLeaky;
+      break;
+    case kActRelu: f |= kTRelu; break;
+    case kActGelu: f |= kTGelu; break;
+    default: return kTGeneric;
+  }
+  return f;
+}
+
+template <int F>
+static void tc_launch(const ConvArgs& a, const TcMaps& maps, const TcPlan& g, int grid, int dev, cudaStream_t st) {
+  static std::atomic<uint64_t> attr_done{0};  // per instantiation, one bit per device
+  if (dev < 64 && !(attr_done.load() & (1ull << dev))) {
+    RVC_CUDA_TRY(cudaFuncSetAttribute(tc_conv_kernel<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
+    attr_done.fetch_or(1ull << dev);
+  }
+  tc_conv_kernel<F><<<grid, kThreads, g.smem_bytes, st>>>(a, maps, g);
+  note_launch();
+  RVC_CUDA_TRY(cudaGetLastError());
 }
 
 // fp32 3-D map [B][rows][width] with row stride `ld` and batch stride `bs` (elements).
@@ -970,16 +1064,23 @@ void launch_tc_conv(const ConvArgs& a, cudaStream_t st) {
   }
   int dev = 0;
   RVC_CUDA_TRY(cudaGetDevice(&dev));
-  static std::atomic<uint64_t> attr_done{0};  // the attribute is per device
-  if (dev < 64 && !(attr_done.load() & (1ull << dev))) {
-    RVC_CUDA_TRY(cudaFuncSetAttribute(tc_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024));
-    attr_done.fetch_or(1ull << dev);
-  }
   if (g_num_sms == 0) RVC_CUDA_TRY(cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev));
   const int grid = std::min(g.total_tiles, g_num_sms);
-  tc_conv_kernel<<<grid, kThreads, g.smem_bytes, st>>>(a, maps, g);
-  note_launch();
-  RVC_CUDA_TRY(cudaGetLastError());
+  switch (tc_flags(a)) {  // the combinations the models' layers use
+    case 0: tc_launch<0>(a, maps, g, grid, dev, st); break;
+    case kTBias: tc_launch<kTBias>(a, maps, g, grid, dev, st); break;
+    case kTBias | kTRes: tc_launch<kTBias | kTRes>(a, maps, g, grid, dev, st); break;
+    case kTBias | kTGelu: tc_launch<kTBias | kTGelu>(a, maps, g, grid, dev, st); break;
+    case kTGelu: tc_launch<kTGelu>(a, maps, g, grid, dev, st); break;
+    case kTAcc | kTGelu: tc_launch<kTAcc | kTGelu>(a, maps, g, grid, dev, st); break;
+    case kTBias | kTRelu: tc_launch<kTBias | kTRelu>(a, maps, g, grid, dev, st); break;
+    case kTBias | kTBias2: tc_launch<kTBias | kTBias2>(a, maps, g, grid, dev, st); break;
+    case kTBias | kTRes | kTResSub: tc_launch<kTBias | kTRes | kTResSub>(a, maps, g, grid, dev, st); break;
+    case kTBias | kTLeaky: tc_launch<kTBias | kTLeaky>(a, maps, g, grid, dev, st); break;
+    case kTBias | kTRes | kTAcc: tc_launch<kTBias | kTRes | kTAcc>(a, maps, g, grid, dev, st); break;
+    case kTBias | kTRes | kTAcc | kTDiv: tc_launch<kTBias | kTRes | kTAcc | kTDiv>(a, maps, g, grid, dev, st); break;
+    default: tc_launch<kTGeneric>(a, maps, g, grid, dev, st); break;
+  }
 }
 
 }  // namespace rvc
