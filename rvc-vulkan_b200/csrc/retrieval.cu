@@ -10,10 +10,13 @@
 //      kernel with K = 1; the index is its resident "weight", packed once) into
 //      a [rows][Npad] fp32 block (Npad = N rounded up to 256, pad rows have
 //      ||d||^2 = +inf so they never win);
-//   2. a warp per query scans its row, forms the reference's fp32 distance and
-//      keeps the k + 8 smallest (value, index) in registers, then merges lanes;
-//   3. a warp per query re-ranks those candidates with the exact distance
-//      sum((q - d)^2) in float64 and writes the k best, ties to the lower index.
+//   2. a warp per (query, column slice) scans its slice of the row, forms the
+//      reference's fp32 distance and keeps the k + 8 smallest (value, index)
+//      in registers, then merges lanes (slices keep the GPU full when a block
+//      has few rows);
+//   3. a warp per query takes the k + 8 smallest of its slices' lists and
+//      re-ranks them with the exact distance sum((q - d)^2) in float64, writing
+//      the k best, ties to the lower index.
 // Step 3 makes the order independent of the GEMM's rounding: the result
 // matches the reference wherever the reference's own fp32 rounding does not
 // reorder two candidates.
@@ -66,67 +69,162 @@ __device__ __forceinline__ bool before(float d1, int i1, int l1, float d2, int i
   return l1 < l2;
 }
 
+constexpr int kTopkSlices = 16;  // column slices of one query row (candidate lists merged by the re-rank)
+constexpr int kSliceCols = 512;  // slice granularity: one warp step (32 lanes x 4 float4 loads)
+
+// Candidate scan, one warp per (query row, column slice [s*slice, (s+1)*slice)):
+// the reference's fp32 distance (q2 + d2) - 2 q.d clamped at 0, the KC
+// smallest (value, index) of the slice in (value, index) order, written to
+// cv / ci [row][slice][KC] (inf / -1 where the slice has fewer entries).
+// Splitting a row into slices keeps enough warps (and loads in flight) on the
+// GPU when a query block has few rows; the union of the slices' exact lists
+// holds the row's exact list, which the re-rank selects.
+//
+// The warp keeps ONE sorted list, lane j < KC holding the j-th smallest.  An
+// element is a candidate only if its distance is <= the list's last value (a
+// warp-uniform threshold), so after the list fills almost every element costs
+// one compare and a ballot; candidates are inserted one at a time by the whole
+// warp (compare, ballot, shift up by one lane).  The threshold before the list
+// fills is the KC-th smallest of the first step's 32 lane minima (real
+// elements, so at least KC elements of the slice are at or below it).  Ties
+// are exact: the insertion compares (value, index).  The distance block is
+// streamed once (evict-first loads, the next step's loads issued before this
+// step's values are used); d2 is shared by the block's 8 rows through L1.
 template <int KC>
-__global__ void topk_approx_kernel(const float* __restrict__ dot, long long ld, const float* __restrict__ q2,
-                                   const float* __restrict__ d2, long long rows, long long npad,
-                                   int* __restrict__ cand) {
+__global__ void __launch_bounds__(256) topk_slice_kernel(const float* __restrict__ dot, long long ld,
+                                                          const float* __restrict__ q2, const float* __restrict__ d2,
+                                                          long long rows, long long npad, long long slice,
+                                                          float* __restrict__ cv, int* __restrict__ ci) {
+  static_assert(KC <= 32, "one list entry per lane");
   const long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (r >= rows) return;
-  float dl[KC];
-  int il[KC];
-#pragma unroll
-  for (int j = 0; j < KC; ++j) {
-    dl[j] = INFINITY;
-    il[j] = -1;
-  }
+  const long long c_begin = (long long)blockIdx.y * slice;
+  const long long c_end = min(npad, c_begin + slice);
+  float lv = INFINITY;  // this lane's list entry (lane < KC)
+  int li = -1;
+  float tau = INFINITY;  // candidates: dist <= tau (warp-uniform)
   const float qq = q2[r];
   const float* row = dot + r * ld;
-  auto offer = [&](float dist, int col) {
-    if (dist < dl[KC - 1]) {
-      float cd = dist;
-      int ci = col;
-#pragma unroll
-      for (int j = 0; j < KC; ++j) {
-        if (cd < dl[j]) {  // strict: an equal value stays behind the earlier index
-          const float td = dl[j];
-          const int ti = il[j];
-          dl[j] = cd;
-          il[j] = ci;
-          cd = td;
-          ci = ti;
-        }
-      }
+  auto insert = [&](float d, int c) {  // warp-wide; d, c uniform
+    const bool gt = lane < KC && before(d, c, 0, lv, li, 0);
+    const unsigned gm = __ballot_sync(0xffffffffu, gt);
+    if (gm == 0) return;  // not better than the KC-th entry
+    const int pos = __ffs(gm) - 1;
+    const float uv = __shfl_up_sync(0xffffffffu, lv, 1);
+    const int ui = __shfl_up_sync(0xffffffffu, li, 1);
+    if (lane == pos) {
+      lv = d;
+      li = c;
+    } else if (lane > pos && lane < KC) {
+      lv = uv;
+      li = ui;
     }
+    tau = fminf(tau, __shfl_sync(0xffffffffu, lv, KC - 1));
   };
-  // four 16-byte loads in flight per lane (2 KB per warp) before any is used
-  for (long long base = 4ll * lane; base < npad; base += 512) {
-    float4 v[4], n2[4];
+  // one warp step: lane columns base + 128 u + (0..3), u = 0..3
+  auto load = [&](long long base, float4 (&v)[4], float4 (&n2)[4]) {
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const long long c0 = base + 128ll * u;
-      if (c0 < npad) {
-        v[u] = *reinterpret_cast<const float4*>(row + c0);
-        n2[u] = *reinterpret_cast<const float4*>(d2 + c0);
+      if (c0 < c_end) {
+        v[u] = __ldcs(reinterpret_cast<const float4*>(row + c0));
+        n2[u] = __ldg(reinterpret_cast<const float4*>(d2 + c0));
       } else {
         v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        n2[u] = make_float4(INFINITY, INFINITY, INFINITY, INFINITY);
+        n2[u] = make_float4(INFINITY, INFINITY, INFINITY, INFINITY);  // inf: never a candidate
       }
     }
+  };
+  auto dist_of = [&](float x, float nn) { return fmaxf((qq + nn) - 2.f * x, 0.f); };  // the reference's fp32 order
+  auto process = [&](long long base, const float4 (&v)[4], const float4 (&n2)[4]) {
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const float x[4] = {v[u].x, v[u].y, v[u].z, v[u].w}, nn[4] = {n2[u].x, n2[u].y, n2[u].z, n2[u].w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float dist = fmaxf((qq + nn[e]) - 2.f * x[e], 0.f);  // the reference's fp32 order
-        offer(dist, (int)(base + 128ll * u + e));
+        const float dist = dist_of(x[e], nn[e]);
+        unsigned m = __ballot_sync(0xffffffffu, dist <= tau && dist < INFINITY);
+        while (m) {  // warp-uniform
+          const int l = __ffs(m) - 1;
+          m &= m - 1;
+          const float d = __shfl_sync(0xffffffffu, dist, l);
+          const int c = __shfl_sync(0xffffffffu, (int)(base + 128ll * u + e), l);
+          if (d <= tau) insert(d, c);
+        }
       }
     }
+  };
+  float4 va[4], na[4], vb[4], nb[4];
+  long long base = c_begin + 4ll * lane;
+  load(base, va, na);
+  {
+    // threshold before the list fills: the KC-th smallest lane minimum of the first step
+    float mn = INFINITY;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      mn = fminf(mn, fminf(fminf(dist_of(va[u].x, na[u].x), dist_of(va[u].y, na[u].y)),
+                           fminf(dist_of(va[u].z, na[u].z), dist_of(va[u].w, na[u].w))));
+    }
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {  // bitonic sort of the 32 lane minima, ascending
+#pragma unroll
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        const float o = __shfl_xor_sync(0xffffffffu, mn, j);
+        const bool asc = (lane & k) == 0, lower = (lane & j) == 0;
+        mn = (asc == lower) ? fminf(mn, o) : fmaxf(mn, o);
+      }
+    }
+    tau = __shfl_sync(0xffffffffu, mn, KC - 1);
   }
-  int* out = cand + r * KC;
+  for (; base < c_end; base += 2 * kSliceCols) {
+    load(base + kSliceCols, vb, nb);
+    process(base, va, na);
+    load(base + 2 * kSliceCols, va, na);
+    process(base + kSliceCols, vb, nb);
+  }
+  if (lane < KC) {
+    const long long o0 = (r * gridDim.y + blockIdx.y) * KC;
+    cv[o0 + lane] = lv;
+    ci[o0 + lane] = li;
+  }
+}
+
+// Re-rank, one warp per query row: the KC smallest (value, index) of the
+// row's nsl slice lists (the row's exact candidate list), then the exact
+// float64 distance sum((q - d)^2) of each and the k best, ties to the lower
+// index.
+template <int KC>
+__global__ void rerank_kernel(const float* __restrict__ q, const float* __restrict__ db, int D,
+                              const float* __restrict__ cv, const int* __restrict__ cidx, int nsl, long long rows,
+                              int k, float* __restrict__ scores, long long* __restrict__ inds) {
+  const long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const float* qr = q + r * D;
+  constexpr int kPer = kTopkSlices * KC / 32;  // slice-list entries per lane
+  const int total = nsl * KC;
+  float mv[kPer];
+  int mi[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int e = lane + 32 * j;
+    mv[j] = e < total ? cv[r * total + e] : INFINITY;
+    mi[j] = e < total ? cidx[r * total + e] : -1;
+  }
+  int ci[KC];
+#pragma unroll
   for (int t = 0; t < KC; ++t) {
-    float bd = dl[0];
-    int bi = il[0], bl = lane;
+    float bd = mv[0];
+    int bi = mi[0], bj = 0;
+#pragma unroll
+    for (int j = 1; j < kPer; ++j)
+      if (before(mv[j], mi[j], 0, bd, bi, 0)) {
+        bd = mv[j];
+        bi = mi[j];
+        bj = j;
+      }
+    int bl = lane;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       const float od = __shfl_xor_sync(0xffffffffu, bd, o);
@@ -140,30 +238,17 @@ __global__ void topk_approx_kernel(const float* __restrict__ dot, long long ld, 
     }
     if (lane == bl) {
 #pragma unroll
-      for (int j = 0; j < KC - 1; ++j) {
-        dl[j] = dl[j + 1];
-        il[j] = il[j + 1];
-      }
-      dl[KC - 1] = INFINITY;
-      il[KC - 1] = -1;
+      for (int j = 0; j < kPer; ++j)
+        if (j == bj) {
+          mv[j] = INFINITY;
+          mi[j] = -1;
+        }
     }
-    if (lane == 0) out[t] = bi;
+    ci[t] = bi;
   }
-}
-
-template <int KC>
-__global__ void rerank_kernel(const float* __restrict__ q, const float* __restrict__ db, int D,
-                              const int* __restrict__ cand, long long rows, int k, float* __restrict__ scores,
-                              long long* __restrict__ inds) {
-  const long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (r >= rows) return;
-  const float* qr = q + r * D;
   double dd[KC];
-  int ci[KC];
 #pragma unroll
   for (int j = 0; j < KC; ++j) {
-    ci[j] = cand[r * KC + j];
     double s = 0.0;
     if (ci[j] >= 0) {
       const float* dr = db + (long long)ci[j] * D;
@@ -371,7 +456,8 @@ void IndexModel::ensure_ws(int64_t rows) {
   dot_ = DevBuf();
   dot_ = DevBuf(ctx, sizeof(float) * (size_t)rows * Npad);
   q2_ = DevBuf(ctx, sizeof(float) * (size_t)rows);
-  cand_ = DevBuf(ctx, sizeof(int) * (size_t)rows * (kMaxK + kExtra));
+  cand_v_ = DevBuf(ctx, sizeof(float) * (size_t)rows * kTopkSlices * (kMaxK + kExtra));
+  cand_i_ = DevBuf(ctx, sizeof(int) * (size_t)rows * kTopkSlices * (kMaxK + kExtra));
   sc_ = DevBuf(ctx, sizeof(float) * (size_t)rows * kMaxK);
   ix_ = DevBuf(ctx, sizeof(long long) * (size_t)rows * kMaxK);
   ws_rows_ = rows;
@@ -399,17 +485,26 @@ void IndexModel::search_device(const float* q, int64_t F, int k, float* scores, 
     io.y = dot_.f(); io.y_ld = (int)Npad; io.y_bs = rows * Npad;
     io.B = 1;
     gemm_.run(ctx, io, precision == 1);
+    // column slices per row: about 32 scanning warps per SM however few rows the block has
+    const long long want = (long long)ctx->num_sms() * 32;
+    long long nsl = std::min<long long>(kTopkSlices, std::max<long long>(1, cdiv<long long>(want, rows)));
+    nsl = std::max<long long>(1, std::min<long long>(nsl, Npad / kSliceCols));
+    const long long slice = cdiv<long long>(cdiv<long long>(Npad, nsl), kSliceCols) * kSliceCols;
+    nsl = cdiv<long long>(Npad, slice);  // no empty slice
+    const dim3 sgrid((unsigned)((rows + kRows - 1) / kRows), (unsigned)nsl);
     const unsigned grid = (unsigned)((rows + kRows - 1) / kRows);
     if (KC == 16) {
-      topk_approx_kernel<16><<<grid, 32 * kRows, 0, st>>>(dot_.f(), Npad, q2_.f(), d2_.f(), rows, Npad, cand_.as<int>());
+      topk_slice_kernel<16><<<sgrid, 32 * kRows, 0, st>>>(dot_.f(), Npad, q2_.f(), d2_.f(), rows, Npad, slice,
+                                                          cand_v_.f(), cand_i_.as<int>());
       note_launch();
-      rerank_kernel<16><<<grid, 32 * kRows, 0, st>>>(qb, db_.f(), D, cand_.as<int>(), rows, kk, scores + r0 * kk,
-                                                     (long long*)inds + r0 * kk);
+      rerank_kernel<16><<<grid, 32 * kRows, 0, st>>>(qb, db_.f(), D, cand_v_.f(), cand_i_.as<int>(), (int)nsl, rows,
+                                                     kk, scores + r0 * kk, (long long*)inds + r0 * kk);
     } else {
-      topk_approx_kernel<24><<<grid, 32 * kRows, 0, st>>>(dot_.f(), Npad, q2_.f(), d2_.f(), rows, Npad, cand_.as<int>());
+      topk_slice_kernel<24><<<sgrid, 32 * kRows, 0, st>>>(dot_.f(), Npad, q2_.f(), d2_.f(), rows, Npad, slice,
+                                                          cand_v_.f(), cand_i_.as<int>());
       note_launch();
-      rerank_kernel<24><<<grid, 32 * kRows, 0, st>>>(qb, db_.f(), D, cand_.as<int>(), rows, kk, scores + r0 * kk,
-                                                     (long long*)inds + r0 * kk);
+      rerank_kernel<24><<<grid, 32 * kRows, 0, st>>>(qb, db_.f(), D, cand_v_.f(), cand_i_.as<int>(), (int)nsl, rows,
+                                                     kk, scores + r0 * kk, (long long*)inds + r0 * kk);
     }
     note_launch();
     RVC_CUDA_TRY(cudaGetLastError());

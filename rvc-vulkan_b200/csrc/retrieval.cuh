@@ -49,7 +49,7 @@ class IndexModel {
   DevBuf db_, d2_;
   ConvLayer gemm_;
   int64_t ws_rows_ = 0;
-  DevBuf dot_, q2_, cand_, sc_, ix_;
+  DevBuf dot_, q2_, cand_v_, cand_i_, sc_, ix_;
   DevBuf h_q_, h_f_, h_o_, h_s_, h_i_;  // staging for the host-pointer calls
   std::unique_ptr<IndexModel> cent_;    // brute-force index over the centroids
   DevBuf bucket_rows_, bucket_off_;     // row ids grouped by bucket (stable), bucket offsets [nlist + 1]

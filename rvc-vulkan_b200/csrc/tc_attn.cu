@@ -10,14 +10,17 @@
 //   K tile [hi 128 keys | lo 128]  : (k/8)*256*16 + n*16 + (k%8)*2   (stacked N = 256)
 //   V tile [hi D rows | lo D rows] : (j/8)*2D*16 + n*16 + (j%8)*2   (keys are the K dim)
 // Main kernel, one 128-query tile per work item (persistent CTAs):
-//   warp 0  bulk-copies Q once and K / V per 128-key tile;
-//   warp 1  issues S = Qhi.[Khi|Klo] + Qlo.Khi (N = 256 and 128) into TMEM, then
-//           O_t = Phi.[Vhi|Vlo] + Plo.Vhi (N = 2D and D);
-//   warps 2-5 (one query row per thread) read S, keep the running max / sum,
-//           write P = exp(s - m) as bf16 hi / lo planes for the second MMA and
-//           fold each tile's O_t into a register accumulator (rescaled when the
-//           running max moves); band bias and band output term added on the
-//           CUDA cores when a window is given.
+//   warp 0  bulk-copies Q once per item and K per 128-key tile; warp 10 V;
+//   warp 1  issues S = Qhi.Khi + Qhi.Klo + Qlo.Khi (three N = 128 MMAs into one
+//           of two TMEM buffers), then O_t = Phi.[Vhi|Vlo] + Plo.Vhi (N = 2D
+//           and D), in the order S_0, S_1, PV_0, S_2, PV_1, ... so the next
+//           tile's S is on the tensor pipe while the softmax warps work;
+//   warps 2-9 (one query row per thread, two warps per row: each half of the
+//           tile's keys and of the head dimensions) read S, keep the running
+//           max / sum, write P = exp(s - m) as bf16 hi / lo planes for the
+//           second MMA and fold each tile's O_t into a register accumulator
+//           (rescaled when the running max moves); band bias and band output
+//           term added on the CUDA cores when a window is given.
 // Every mbarrier wait is bounded; on a timeout the kernel records an error and
 // winds down.
 #include "context.cuh"
@@ -36,7 +39,7 @@ namespace {
 
 constexpr int kTQ = 128;   // queries per tile
 constexpr int kTK = 128;   // keys per tile
-constexpr int kAThreads = 192;
+constexpr int kAThreads = 352;
 constexpr uint64_t kAttnWaitNs = 2000000000ull;
 constexpr int kMaxWin = 16;
 
@@ -129,24 +132,30 @@ __global__ void __launch_bounds__(kAThreads, 1) tc_attn_kernel(const __grid_cons
   const uint32_t p_plane = (uint32_t)kTQ * kTK * 2u;
   const uint32_t sbase = ptx::smem_u32(smem);
   const uint32_t off_q = 0, off_k = off_q + 2 * q_plane, off_v = off_k + k_bytes, off_p = off_v + v_bytes;
-  const uint32_t off_bar = off_p + 2 * p_plane;
-  // barriers
-  const uint32_t Q_FULL = sbase + off_bar, Q_EMPTY = Q_FULL + 8, KV_FULL = Q_FULL + 16, KV_EMPTY = Q_FULL + 24;
-  const uint32_t S_FULL = Q_FULL + 32, S_EMPTY = Q_FULL + 40, P_FULL = Q_FULL + 48, PV_FULL = Q_FULL + 56;
-  const uint32_t PV_EMPTY = Q_FULL + 64;
-  uint32_t* tmem_slot = (uint32_t*)(smem + off_bar + 72);
+  const uint32_t off_bar = off_p + 2 * p_plane, off_red = off_bar + 128;  // red: softmax pair exchange, 3 KB
+  // barriers; tiles are counted over the whole CTA (g), S alternates between two TMEM buffers
+  const uint32_t Q_FULL = sbase + off_bar, Q_EMPTY = Q_FULL + 8, K_FULL = Q_FULL + 16, K_EMPTY = Q_FULL + 24;
+  const uint32_t V_FULL = Q_FULL + 32, V_EMPTY = Q_FULL + 40, S_FULL = Q_FULL + 48 /* [2] */,
+                 S_EMPTY = Q_FULL + 64 /* [2] */, P_FULL = Q_FULL + 80, PV_FULL = Q_FULL + 88,
+                 PV_EMPTY = Q_FULL + 96, DRAIN = Q_FULL + 104;
+  uint32_t* tmem_slot = (uint32_t*)(smem + off_bar + 112);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     ptx::mbar_init(Q_FULL, 1);
     ptx::mbar_init(Q_EMPTY, 1);
-    ptx::mbar_init(KV_FULL, 1);
-    ptx::mbar_init(KV_EMPTY, 1);
-    ptx::mbar_init(S_FULL, 1);
-    ptx::mbar_init(S_EMPTY, 4);
-    ptx::mbar_init(P_FULL, 4);
+    ptx::mbar_init(K_FULL, 1);
+    ptx::mbar_init(K_EMPTY, 1);
+    ptx::mbar_init(V_FULL, 1);
+    ptx::mbar_init(V_EMPTY, 1);
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(S_FULL + 8 * b, 1);
+      ptx::mbar_init(S_EMPTY + 8 * b, 8);
+    }
+    ptx::mbar_init(P_FULL, 8);
     ptx::mbar_init(PV_FULL, 1);
-    ptx::mbar_init(PV_EMPTY, 4);
+    ptx::mbar_init(PV_EMPTY, 8);
+    ptx::mbar_init(DRAIN, 1);
     ptx::fence_mbar_init();
   }
   if (warp == 1) {
@@ -157,13 +166,14 @@ __global__ void __launch_bounds__(kAThreads, 1) tc_attn_kernel(const __grid_cons
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t S_COL = 0, PV_COL = 256;  // S: 256 columns (stacked), O_t: 2D columns
+  // S of tile g: columns (g & 1) * 128 .. + 127; O_t: 2D columns from 256
+  const uint32_t PV_COL = 256;
   const int total_items = a.BH * a.nq * a.nsplit;
 
   if (warp == 0) {
-    // ------------------------------------------------ loader
+    // ------------------------------------------------ Q and K loader
     if (lane == 0) {
-      int qi = 0, kvi = 0;
+      int qi = 0, g = 0;
       bool ok = true;
       for (int it = blockIdx.x; it < total_items && ok; it += gridDim.x) {
         const int sp = it % a.nsplit, bq = it / a.nsplit;
@@ -177,29 +187,75 @@ __global__ void __launch_bounds__(kAThreads, 1) tc_attn_kernel(const __grid_cons
         ++qi;
         ptx::mbar_expect_tx(Q_FULL, 2 * q_plane);
         ptx::bulk_g2s(sbase + off_q, a.Qp + ((long long)bh * a.nq + qt) * 2 * (kTQ * D), 2 * q_plane, Q_FULL);
-        for (int kt = kt0; kt < kt1; ++kt, ++kvi) {
-          if (!ptx::mbar_wait(KV_EMPTY, (kvi & 1) ^ 1, kAttnWaitNs)) {
+        for (int kt = kt0; kt < kt1; ++kt, ++g) {
+          // the K tile is free once the previous tile's S MMAs have read it
+          if (!ptx::mbar_wait(K_EMPTY, (g & 1) ^ 1, kAttnWaitNs)) {
             atomicExch(a.err, 22);
             ok = false;
             break;
           }
-          ptx::mbar_expect_tx(KV_FULL, k_bytes + v_bytes);
-          const long long tile = (long long)bh * a.nk + kt;
-          ptx::bulk_g2s(sbase + off_k, a.Kp + tile * (2 * kTK * D), k_bytes, KV_FULL);
-          ptx::bulk_g2s(sbase + off_v, a.Vp + tile * (2 * kTK * D), v_bytes, KV_FULL);
+          ptx::mbar_expect_tx(K_FULL, k_bytes);
+          ptx::bulk_g2s(sbase + off_k, a.Kp + ((long long)bh * a.nk + kt) * (2 * kTK * D), k_bytes, K_FULL);
         }
       }
+      // no copy left in flight
+      if (qi > 0) ptx::mbar_wait(Q_FULL, (qi - 1) & 1, kAttnWaitNs);
+      if (g > 0) ptx::mbar_wait(K_FULL, (g - 1) & 1, kAttnWaitNs);
+    }
+    __syncwarp();
+  } else if (warp == 10) {
+    // ------------------------------------------------ V loader
+    if (lane == 0) {
+      int g = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; it < total_items && ok; it += gridDim.x) {
+        const int sp = it % a.nsplit, bq = it / a.nsplit;
+        const int bh = bq / a.nq;
+        const int kt0 = a.nk * sp / a.nsplit, kt1 = a.nk * (sp + 1) / a.nsplit;
+        for (int kt = kt0; kt < kt1; ++kt, ++g) {
+          // free once the previous tile's P.V MMAs have read it
+          if (!ptx::mbar_wait(V_EMPTY, (g & 1) ^ 1, kAttnWaitNs)) {
+            atomicExch(a.err, 29);
+            ok = false;
+            break;
+          }
+          ptx::mbar_expect_tx(V_FULL, v_bytes);
+          ptx::bulk_g2s(sbase + off_v, a.Vp + ((long long)bh * a.nk + kt) * (2 * kTK * D), v_bytes, V_FULL);
+        }
+      }
+      if (g > 0) ptx::mbar_wait(V_FULL, (g - 1) & 1, kAttnWaitNs);
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------ MMA issuer
+    // Order: S_0, S_1, PV_0, S_2, PV_1, ...: the next tile's S is computed while
+    // the softmax warps work on this one (S double-buffered in TMEM).
     if (lane == 0) {
-      const uint32_t id_s2 = ptx::idesc_bf16_f32(128, 2 * kTK), id_s1 = ptx::idesc_bf16_f32(128, kTK);
+      const uint32_t id_s = ptx::idesc_bf16_f32(128, kTK);
       const uint32_t id_v2 = ptx::idesc_bf16_f32(128, 2 * D), id_v1 = ptx::idesc_bf16_f32(128, D);
       const uint32_t lbo_q = (uint32_t)kTQ * 16u, lbo_k = (uint32_t)2 * kTK * 16u;
       const uint32_t lbo_p = (uint32_t)kTQ * 16u, lbo_v = (uint32_t)2 * D * 16u;
-      int qi = 0, kvi = 0;
+      int qi = 0, g = 0;
       bool ok = true;
+      // O_h = Phi.[Vhi|Vlo] (N = 2D) + Plo.Vhi (N = D), K = 128 keys in steps of 16
+      auto issue_pv = [&](int h) {
+        if (!ptx::mbar_wait(P_FULL, h & 1, kAttnWaitNs) || !ptx::mbar_wait(V_FULL, h & 1, kAttnWaitNs) ||
+            !ptx::mbar_wait(PV_EMPTY, (h & 1) ^ 1, kAttnWaitNs)) {
+          atomicExch(a.err, 25);
+          ok = false;
+          return;
+        }
+        ptx::tc_fence_after();
+        for (int kk = 0; kk < kTK / 16; ++kk) {
+          const uint64_t dph = ptx::smem_desc(sbase + off_p + (uint32_t)kk * 2u * lbo_p, lbo_p, 128);
+          const uint64_t dpl = ptx::smem_desc(sbase + off_p + p_plane + (uint32_t)kk * 2u * lbo_p, lbo_p, 128);
+          const uint64_t dv = ptx::smem_desc(sbase + off_v + (uint32_t)kk * 2u * lbo_v, lbo_v, 128);
+          ptx::mma_bf16(tmem + PV_COL, dph, dv, id_v2, kk > 0 ? 1u : 0u);
+          ptx::mma_bf16(tmem + PV_COL, dpl, dv, id_v1, 1u);
+        }
+        ptx::mma_commit(PV_FULL);
+        ptx::mma_commit(V_EMPTY);
+      };
       for (int it = blockIdx.x; it < total_items && ok; it += gridDim.x) {
         const int sp = it % a.nsplit;
         const int kt0 = a.nk * sp / a.nsplit, kt1 = a.nk * (sp + 1) / a.nsplit;
@@ -209,60 +265,65 @@ __global__ void __launch_bounds__(kAThreads, 1) tc_attn_kernel(const __grid_cons
           break;
         }
         ++qi;
-        for (int kt = kt0; kt < kt1 && ok; ++kt, ++kvi) {
-          const uint32_t ph = kvi & 1;
-          if (!ptx::mbar_wait(KV_FULL, ph, kAttnWaitNs) || !ptx::mbar_wait(S_EMPTY, ph ^ 1, kAttnWaitNs)) {
+        for (int kt = kt0; kt < kt1 && ok; ++kt, ++g) {
+          const int b = g & 1;
+          if (!ptx::mbar_wait(K_FULL, g & 1, kAttnWaitNs) ||
+              !ptx::mbar_wait(S_EMPTY + 8 * b, ((g >> 1) & 1) ^ 1, kAttnWaitNs)) {
             atomicExch(a.err, 24);
             ok = false;
             break;
           }
           ptx::tc_fence_after();
-          // S = Qhi.[Khi|Klo] (N = 256) + Qlo.Khi (N = 128), K = D in steps of 16
+          // S = Qhi.Khi + Qhi.Klo + Qlo.Khi (N = 128 each; K tile rows 0-127 hi, 128-255 lo)
+          const uint32_t s_col = tmem + (uint32_t)(b * kTK);
           for (int kk = 0; kk < D / 16; ++kk) {
             const uint64_t dqh = ptx::smem_desc(sbase + off_q + (uint32_t)kk * 2u * lbo_q, lbo_q, 128);
             const uint64_t dql = ptx::smem_desc(sbase + off_q + q_plane + (uint32_t)kk * 2u * lbo_q, lbo_q, 128);
-            const uint64_t dk = ptx::smem_desc(sbase + off_k + (uint32_t)kk * 2u * lbo_k, lbo_k, 128);
-            ptx::mma_bf16(tmem + S_COL, dqh, dk, id_s2, kk > 0 ? 1u : 0u);
-            ptx::mma_bf16(tmem + S_COL, dql, dk, id_s1, 1u);
+            const uint64_t dkh = ptx::smem_desc(sbase + off_k + (uint32_t)kk * 2u * lbo_k, lbo_k, 128);
+            const uint64_t dkl = ptx::smem_desc(sbase + off_k + kTK * 16u + (uint32_t)kk * 2u * lbo_k, lbo_k, 128);
+            ptx::mma_bf16(s_col, dqh, dkh, id_s, kk > 0 ? 1u : 0u);
+            ptx::mma_bf16(s_col, dqh, dkl, id_s, 1u);
+            ptx::mma_bf16(s_col, dql, dkh, id_s, 1u);
           }
-          ptx::mma_commit(S_FULL);
-          if (!ptx::mbar_wait(P_FULL, ph, kAttnWaitNs) || !ptx::mbar_wait(PV_EMPTY, ph ^ 1, kAttnWaitNs)) {
-            atomicExch(a.err, 25);
-            ok = false;
-            break;
-          }
-          ptx::tc_fence_after();
-          // O_t = Phi.[Vhi|Vlo] (N = 2D) + Plo.Vhi (N = D), K = 128 keys in steps of 16
-          for (int kk = 0; kk < kTK / 16; ++kk) {
-            const uint64_t dph = ptx::smem_desc(sbase + off_p + (uint32_t)kk * 2u * lbo_p, lbo_p, 128);
-            const uint64_t dpl = ptx::smem_desc(sbase + off_p + p_plane + (uint32_t)kk * 2u * lbo_p, lbo_p, 128);
-            const uint64_t dv = ptx::smem_desc(sbase + off_v + (uint32_t)kk * 2u * lbo_v, lbo_v, 128);
-            ptx::mma_bf16(tmem + PV_COL, dph, dv, id_v2, kk > 0 ? 1u : 0u);
-            ptx::mma_bf16(tmem + PV_COL, dpl, dv, id_v1, 1u);
-          }
-          ptx::mma_commit(PV_FULL);
-          ptx::mma_commit(KV_EMPTY);
+          ptx::mma_commit(S_FULL + 8 * b);
+          ptx::mma_commit(K_EMPTY);
+          if (kt + 1 == kt1) ptx::mma_commit(Q_EMPTY);
+          if (g > 0) issue_pv(g - 1);
         }
-        if (ok) ptx::mma_commit(Q_EMPTY);
       }
+      if (ok && g > 0) issue_pv(g - 1);
+      ptx::mma_commit(DRAIN);
+      ptx::mbar_wait(DRAIN, 0, kAttnWaitNs);  // every MMA done before TMEM is freed
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------ softmax warps: one query row per thread
+    // ------------------------------------------------ softmax warps 2-9
+    // Two warps per TMEM lane quarter: warp w reads lanes 32 (w % 4) .. +31
+    // (one query row per thread); half hf = (w - 2) / 4 takes key columns
+    // [64 hf, 64 hf + 64) of every tile and head dimensions [hf D/2, (hf+1) D/2)
+    // of O.  The pair exchanges its row maxima through shared memory (named
+    // barrier 1 + quarter, 64 threads) once per tile and its row sums once per
+    // item; everything else is per half.
+    constexpr int DH = D / 2;
+    constexpr int CH = kTK / 2;
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int hf = (warp - 2) >> 2;
     const int row = quarter * 32 + lane;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const uint32_t pair_bar = 1u + (uint32_t)quarter;
+    float* red_m = reinterpret_cast<float*>(smem + off_red);  // [tile parity][half][128 rows]
+    float* red_l = red_m + 2 * 2 * kTQ;                       // [half][128 rows]
     const int nb = 2 * a.window + 1;
-    int kvi = 0;
+    int kvi = 0;  // tiles seen by this CTA (g)
     bool ok = true;
     for (int it = blockIdx.x; it < total_items && ok; it += gridDim.x) {
       const int sp = it % a.nsplit, bq = it / a.nsplit;
       const int bh = bq / a.nq, qt = bq % a.nq;
       const int kt0 = a.nk * sp / a.nsplit, kt1 = a.nk * (sp + 1) / a.nsplit;
       const int i = qt * kTQ + row;  // query index
-      float o[D];
+      float o[DH];
 #pragma unroll
-      for (int d = 0; d < D; ++d) o[d] = 0.f;
+      for (int d = 0; d < DH; ++d) o[d] = 0.f;
       float m = -INFINITY, l = 0.f;
       float rk[2 * kMaxWin + 1];
       if (a.window >= 0) {
@@ -270,53 +331,55 @@ __global__ void __launch_bounds__(kAThreads, 1) tc_attn_kernel(const __grid_cons
         for (int r = 0; r < nb; ++r) rk[r] = rr[r];
       }
       for (int kt = kt0; kt < kt1; ++kt, ++kvi) {
-        const uint32_t ph = kvi & 1;
-        const bool got = __all_sync(0xffffffffu, ptx::mbar_wait(S_FULL, ph, kAttnWaitNs));
+        const int b = kvi & 1;
+        const bool got = __all_sync(0xffffffffu, ptx::mbar_wait(S_FULL + 8 * b, (kvi >> 1) & 1, kAttnWaitNs));
         if (!got) {
           if (lane == 0) atomicExch(a.err, 26);
           ok = false;
-          break;
         }
+        // The pair takes every named barrier together: an error in either half
+        // (a bounded wait that ran out) ends both here, never between barriers.
+        ok = ptx::named_bar_and(pair_bar, 64, ok);
+        if (!ok) break;
         ptx::tc_fence_after();
-        const int j0 = kt * kTK;
-        // pass A: row max of this tile
+        const uint32_t s_col = tmem + lane_base + (uint32_t)(b * kTK + hf * CH);
+        const int j0 = kt * kTK + hf * CH;
+        // pass A: row max of this half tile, then of the tile through the pair
         float tmax = -INFINITY;
-        for (int c = 0; c < kTK; c += 32) {
+#pragma unroll 1
+        for (int c = 0; c < CH; c += 32) {
           float s1[32];
-          ptx::tmem_ld32(tmem + lane_base + S_COL + (uint32_t)c, s1);
+          ptx::tmem_ld32(s_col + (uint32_t)c, s1);
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            float s2[16];
-            ptx::tmem_ld16(tmem + lane_base + S_COL + (uint32_t)(kTK + c + 16 * h), s2);
-#pragma unroll
-            for (int k = 0; k < 16; ++k) {
-              const int j = j0 + c + 16 * h + k;
-              float s = s1[16 * h + k] + s2[k];
-              if (a.window >= 0) {
-                const int rel = j - i;
-                if (rel >= -a.window && rel <= a.window) s = s + rk[rel + a.window];
-              }
-              if (j >= a.P) s = -INFINITY;
-              tmax = fmaxf(tmax, s);
+          for (int k = 0; k < 32; ++k) {
+            const int j = j0 + c + k;
+            float s = s1[k];
+            if (a.window >= 0) {
+              const int rel = j - i;
+              if (rel >= -a.window && rel <= a.window) s = s + rk[rel + a.window];
             }
+            if (j >= a.P) s = -INFINITY;
+            tmax = fmaxf(tmax, s);
           }
         }
+        red_m[(b * 2 + hf) * kTQ + row] = tmax;
+        ptx::named_bar(pair_bar, 64);
+        tmax = fmaxf(tmax, red_m[(b * 2 + (hf ^ 1)) * kTQ + row]);
         const float m_new = fmaxf(m, tmax);
-        // fold the previous tile's O_t (computed with exp(s - m)) into the accumulator
+        // fold the previous tile's O_t (computed with exp(s - m)) into this half's dimensions
         if (kt > kt0) {
-          const bool pv = __all_sync(0xffffffffu, ptx::mbar_wait(PV_FULL, ph ^ 1, kAttnWaitNs));
+          const bool pv = __all_sync(0xffffffffu, ptx::mbar_wait(PV_FULL, (kvi - 1) & 1, kAttnWaitNs));
           if (!pv) {
             if (lane == 0) atomicExch(a.err, 27);
             ok = false;
-            break;
+            continue;  // to the next tile's pair barrier, which ends the item for both halves
           }
           ptx::tc_fence_after();
-          // O_{t-1} was formed with exp(s - m): the accumulator is at the same scale here
 #pragma unroll
-          for (int c = 0; c < D; c += 16) {
+          for (int c = 0; c < DH; c += 16) {
             float u1[16], u2[16];
-            ptx::tmem_ld16(tmem + lane_base + PV_COL + (uint32_t)c, u1);
-            ptx::tmem_ld16(tmem + lane_base + PV_COL + (uint32_t)(D + c), u2);
+            ptx::tmem_ld16(tmem + lane_base + PV_COL + (uint32_t)(hf * DH + c), u1);
+            ptx::tmem_ld16(tmem + lane_base + PV_COL + (uint32_t)(D + hf * DH + c), u2);
 #pragma unroll
             for (int k = 0; k < 16; ++k) o[c + k] = o[c + k] + (u1[k] + u2[k]);
           }
@@ -326,22 +389,23 @@ __global__ void __launch_bounds__(kAThreads, 1) tc_attn_kernel(const __grid_cons
         // rescale the accumulator (all earlier tiles) to the new max
         const float scale = (m == -INFINITY) ? 0.f : expf(m - m_new);
 #pragma unroll
-        for (int d = 0; d < D; ++d) o[d] *= scale;
+        for (int d = 0; d < DH; ++d) o[d] *= scale;
         l *= scale;
-        // pass B: p = exp(s - m_new) -> bf16 hi / lo planes, row sum
+        // pass B: p = exp(s - m_new) -> bf16 hi / lo planes, this half's row sum.
+        // The P planes are free: the previous tile's P.V MMAs finished (folded
+        // above, or at the end of the previous item).
         float sum = 0.f;
-        for (int c = 0; c < kTK; c += 32) {
+#pragma unroll 1
+        for (int c = 0; c < CH; c += 32) {
           float s1[32];
-          ptx::tmem_ld32(tmem + lane_base + S_COL + (uint32_t)c, s1);
+          ptx::tmem_ld32(s_col + (uint32_t)c, s1);
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            float s2[16];
-            ptx::tmem_ld16(tmem + lane_base + S_COL + (uint32_t)(kTK + c + 16 * h), s2);
             uint16_t ph16[16], pl16[16];
 #pragma unroll
             for (int k = 0; k < 16; ++k) {
               const int j = j0 + c + 16 * h + k;
-              float s = s1[16 * h + k] + s2[k];
+              float s = s1[16 * h + k];
               if (a.window >= 0) {
                 const int rel = j - i;
                 if (rel >= -a.window && rel <= a.window) s = s + rk[rel + a.window];
@@ -352,7 +416,7 @@ __global__ void __launch_bounds__(kAThreads, 1) tc_attn_kernel(const __grid_cons
             }
 #pragma unroll
             for (int g2 = 0; g2 < 2; ++g2) {
-              const int jc = (c + 16 * h) / 8 + g2;  // key chunk
+              const int jc = (hf * CH + c + 16 * h) / 8 + g2;  // key chunk
               const uint32_t off = (uint32_t)jc * (kTQ * 16u) + (uint32_t)row * 16u;
               const uint4 vh = *reinterpret_cast<const uint4*>(ph16 + 8 * g2);
               const uint4 vl = *reinterpret_cast<const uint4*>(pl16 + 8 * g2);
@@ -371,43 +435,50 @@ __global__ void __launch_bounds__(kAThreads, 1) tc_attn_kernel(const __grid_cons
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          ptx::mbar_arrive(S_EMPTY);
+          ptx::mbar_arrive(S_EMPTY + 8 * b);
           ptx::mbar_arrive(P_FULL);
         }
       }
-      if (!ok) break;
-      // the last tile's O_t
-      {
+      // the last tile's O_t (an error in the tile loop skips it; the pair
+      // barrier below then ends the item for both halves)
+      if (ok) {
         const uint32_t ph = (kvi - 1) & 1;
         const bool pv = __all_sync(0xffffffffu, ptx::mbar_wait(PV_FULL, ph, kAttnWaitNs));
         if (!pv) {
           if (lane == 0) atomicExch(a.err, 28);
           ok = false;
-          break;
-        }
-        ptx::tc_fence_after();
+        } else {
+          ptx::tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < D; c += 16) {
-          float u1[16], u2[16];
-          ptx::tmem_ld16(tmem + lane_base + PV_COL + (uint32_t)c, u1);
-          ptx::tmem_ld16(tmem + lane_base + PV_COL + (uint32_t)(D + c), u2);
+          for (int c = 0; c < DH; c += 16) {
+            float u1[16], u2[16];
+            ptx::tmem_ld16(tmem + lane_base + PV_COL + (uint32_t)(hf * DH + c), u1);
+            ptx::tmem_ld16(tmem + lane_base + PV_COL + (uint32_t)(D + hf * DH + c), u2);
 #pragma unroll
-          for (int k = 0; k < 16; ++k) o[c + k] = o[c + k] + (u1[k] + u2[k]);
+            for (int k = 0; k < 16; ++k) o[c + k] = o[c + k] + (u1[k] + u2[k]);
+          }
+          ptx::tc_fence_before();
+          if (lane == 0) ptx::mbar_arrive(PV_EMPTY);
         }
-        ptx::tc_fence_before();
-        if (lane == 0) ptx::mbar_arrive(PV_EMPTY);
       }
+      // the row sum: this half's plus the partner's (same max, same rescaling)
+      red_l[hf * kTQ + row] = l;
+      ok = ptx::named_bar_and(pair_bar, 64, ok);
+      if (!ok) break;
+      l = red_l[row] + red_l[kTQ + row];
       if (i < a.P && a.nsplit > 1) {
         // partial result of this key range: unnormalised O, row max and sum
         const long long pr = ((long long)bh * a.nsplit + sp) * a.P + i;
-        float* po = a.po + pr * D;
+        float* po = a.po + pr * D + hf * DH;
 #pragma unroll
-        for (int d = 0; d < D; d += 4) *reinterpret_cast<float4*>(po + d) = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
-        a.pml[2 * pr] = m;
-        a.pml[2 * pr + 1] = l;
+        for (int d = 0; d < DH; d += 4) *reinterpret_cast<float4*>(po + d) = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
+        if (hf == 0) {
+          a.pml[2 * pr] = m;
+          a.pml[2 * pr + 1] = l;
+        }
       } else if (i < a.P) {
         const int b = bh / a.heads, h = bh % a.heads;
-        float* yr = a.y + ((long long)b * a.P + i) * a.y_ld + h * D;
+        float* yr = a.y + ((long long)b * a.P + i) * a.y_ld + h * D + hf * DH;
         const float inv_l = 1.f / l;
         if (a.window >= 0) {
           // band term: p(i, i + r - W) from the final max / sum, times emb_v[r]
@@ -415,17 +486,17 @@ __global__ void __launch_bounds__(kAThreads, 1) tc_attn_kernel(const __grid_cons
           float pb[2 * kMaxWin + 1];
           for (int r = 0; r < nb; ++r) pb[r] = expf(sbr[r] - m) * inv_l;
 #pragma unroll
-          for (int d = 0; d < D; ++d) {
+          for (int d = 0; d < DH; ++d) {
             float band = 0.f;
-            for (int r = 0; r < nb; ++r) band = fmaf(pb[r], a.emb_v[(long long)r * D + d], band);
+            for (int r = 0; r < nb; ++r) band = fmaf(pb[r], a.emb_v[(long long)r * D + hf * DH + d], band);
             o[d] = o[d] * inv_l + band;
           }
         } else {
 #pragma unroll
-          for (int d = 0; d < D; ++d) o[d] = o[d] * inv_l;
+          for (int d = 0; d < DH; ++d) o[d] = o[d] * inv_l;
         }
 #pragma unroll
-        for (int d = 0; d < D; d += 4) *reinterpret_cast<float4*>(yr + d) = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
+        for (int d = 0; d < DH; d += 4) *reinterpret_cast<float4*>(yr + d) = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
       }
     }
   }
@@ -567,7 +638,7 @@ bool k_attention_tc(Context* ctx, const float* qkv, int ld, int q_off, int k_off
   a.emb_v = emb_v;
   a.err = ctx->d_err;  // reported by the context's bounded sync
   a.BH = BH;
-  const size_t smem = 1024 + (size_t)2 * kTQ * D * 2 + (size_t)2 * kTK * D * 2 * 2 + (size_t)2 * kTQ * kTK * 2 + 128;
+  const size_t smem = 1024 + (size_t)2 * kTQ * D * 2 + (size_t)2 * kTK * D * 2 * 2 + (size_t)2 * kTQ * kTK * 2 + 128 + 3 * kTQ * sizeof(float) * 2;
   static std::atomic<uint64_t> attr_done{0};
   int dev = 0;
   RVC_CUDA_TRY(cudaGetDevice(&dev));
