@@ -463,6 +463,22 @@ void IndexModel::ensure_ws(int64_t rows) {
   ws_rows_ = rows;
 }
 
+namespace {
+// Resident 256-thread blocks of topk_slice_kernel<KC> per SM (registers bound it).
+int topk_blocks_per_sm(int KC) {
+  static int n16 = 0, n24 = 0;
+  int& n = KC == 16 ? n16 : n24;
+  if (n == 0) {
+    int b = 0;
+    const cudaError_t e = KC == 16
+                              ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, topk_slice_kernel<16>, 32 * kRows, 0)
+                              : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, topk_slice_kernel<24>, 32 * kRows, 0);
+    n = (e == cudaSuccess && b > 0) ? b : 1;
+  }
+  return n;
+}
+}  // namespace
+
 void IndexModel::search_device(const float* q, int64_t F, int k, float* scores, int64_t* inds) {
   RVC_CHECK_ARG(k >= 1 && k <= kMaxK, "index_search: k must be in [1, 16]");
   RVC_CHECK_ARG(F >= 0, "index_search: negative query count");
@@ -485,12 +501,27 @@ void IndexModel::search_device(const float* q, int64_t F, int k, float* scores, 
     io.y = dot_.f(); io.y_ld = (int)Npad; io.y_bs = rows * Npad;
     io.B = 1;
     gemm_.run(ctx, io, precision == 1);
-    // column slices per row: about 32 scanning warps per SM however few rows the block has
-    const long long want = (long long)ctx->num_sms() * 32;
-    long long nsl = std::min<long long>(kTopkSlices, std::max<long long>(1, cdiv<long long>(want, rows)));
-    nsl = std::max<long long>(1, std::min<long long>(nsl, Npad / kSliceCols));
-    const long long slice = cdiv<long long>(cdiv<long long>(Npad, nsl), kSliceCols) * kSliceCols;
-    nsl = cdiv<long long>(Npad, slice);  // no empty slice
+    // column slices per row: the count whose blocks fill the resident block
+    // slots' waves best (the scan is bound by HBM: a half-empty last wave is
+    // lost bandwidth), fewer slices on a tie
+    const long long rb = cdiv<long long>(rows, kRows);
+    const long long slots = (long long)ctx->num_sms() * topk_blocks_per_sm(KC);
+    long long nsl = 1, slice = Npad;
+    {
+      double best = -1.0;
+      const long long max_sl = std::max<long long>(1, std::min<long long>(kTopkSlices, Npad / kSliceCols));
+      for (long long ns = 1; ns <= max_sl; ++ns) {
+        const long long sl = cdiv<long long>(cdiv<long long>(Npad, ns), kSliceCols) * kSliceCols;
+        const long long n_eff = cdiv<long long>(Npad, sl);  // no empty slice
+        const long long blocks = rb * n_eff, waves = cdiv<long long>(blocks, slots);
+        const double score = (double)blocks / (double)(waves * slots) - 0.01 * (double)n_eff;
+        if (score > best + 1e-9) {
+          best = score;
+          nsl = n_eff;
+          slice = sl;
+        }
+      }
+    }
     const dim3 sgrid((unsigned)((rows + kRows - 1) / kRows), (unsigned)nsl);
     const unsigned grid = (unsigned)((rows + kRows - 1) / kRows);
     if (KC == 16) {
