@@ -91,7 +91,7 @@ constexpr int kSliceCols = 512;  // slice granularity: one warp step (32 lanes x
 // streamed once (evict-first loads, the next step's loads issued before this
 // step's values are used); d2 is shared by the block's 8 rows through L1.
 template <int KC>
-__global__ void __launch_bounds__(256) topk_slice_kernel(const float* __restrict__ dot, long long ld,
+__global__ void __launch_bounds__(256, 3) topk_slice_kernel(const float* __restrict__ dot, long long ld,
                                                           const float* __restrict__ q2, const float* __restrict__ d2,
                                                           long long rows, long long npad, long long slice,
                                                           float* __restrict__ cv, int* __restrict__ ci) {
@@ -141,9 +141,15 @@ __global__ void __launch_bounds__(256) topk_slice_kernel(const float* __restrict
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const float x[4] = {v[u].x, v[u].y, v[u].z, v[u].w}, nn[4] = {n2[u].x, n2[u].y, n2[u].z, n2[u].w};
+      float dd[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) dd[e] = dist_of(x[e], nn[e]);
+      // one ballot per four elements: most groups hold no candidate
+      const float m4 = fminf(fminf(dd[0], dd[1]), fminf(dd[2], dd[3]));
+      if (!__any_sync(0xffffffffu, m4 <= tau && m4 < INFINITY)) continue;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const float dist = dist_of(x[e], nn[e]);
+        const float dist = dd[e];
         unsigned m = __ballot_sync(0xffffffffu, dist <= tau && dist < INFINITY);
         while (m) {  // warp-uniform
           const int l = __ffs(m) - 1;
