@@ -358,6 +358,21 @@ __global__ void __launch_bounds__(256) conv2d_rb_kernel(const C2Args a) {
   }
 }
 
+// Packed fp32 pairs for the sm_100 fma.rn.f32x2 instruction: two independent
+// fused multiply-adds, round to nearest, in one instruction; each half's
+// result is the one fmaf gives.
+__device__ __forceinline__ unsigned long long pack2(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(unsigned long long v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ void fma2(unsigned long long& c, unsigned long long a, unsigned long long b) {
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(c) : "l"(a), "l"(b));
+}
+
 // 4-byte global -> shared copy without a register round trip; n = 0 copies
 // nothing and writes zero (the source must still be a valid address).
 __device__ __forceinline__ void cp_async4(float* dst, const float* src, int n) {
@@ -419,11 +434,12 @@ __global__ void __launch_bounds__(256, 2) conv3x3_direct_kernel(const C2Args a, 
     }
     cp_async_commit();
   };
-  float acc[TMP][TNC];
+  // channel pairs (j, j + 1) packed for fma.rn.f32x2 (zero bits = (0.f, 0.f))
+  unsigned long long acc2[TMP][TNC / 2];
 #pragma unroll
   for (int i = 0; i < TMP; ++i)
 #pragma unroll
-    for (int j = 0; j < TNC; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < TNC / 2; ++j) acc2[i][j] = 0ull;
   if (cb0 < cb1) issue(cb0, 0);
   for (int cb = cb0; cb < cb1; ++cb) {
     const int st = (cb - cb0) & 1;
@@ -446,16 +462,20 @@ __global__ void __launch_bounds__(256, 2) conv3x3_direct_kernel(const C2Args a, 
         for (int k = 0; k < TMP + 2; ++k) r[k] = hp[k * (CK + 1)];
 #pragma unroll
         for (int dx = 0; dx < 3; ++dx) {
-          float wv[TNC];
+          unsigned long long wv2[TNC / 2];
 #pragma unroll
           for (int q = 0; q < TNC / 4; ++q) {
             const float4 v = *reinterpret_cast<const float4*>(ws + ((dy * 3 + dx) * CK + c) * BN + q * NT * 4 + tn * 4);
-            wv[4 * q] = v.x; wv[4 * q + 1] = v.y; wv[4 * q + 2] = v.z; wv[4 * q + 3] = v.w;
+            wv2[2 * q] = pack2(v.x, v.y);
+            wv2[2 * q + 1] = pack2(v.z, v.w);
           }
+          // two channels per packed FMA: acc += r * w per output, as fmaf in the same order
 #pragma unroll
-          for (int i = 0; i < TMP; ++i)
+          for (int i = 0; i < TMP; ++i) {
+            const unsigned long long x2 = pack2(r[i + dx], r[i + dx]);
 #pragma unroll
-            for (int j = 0; j < TNC; ++j) acc[i][j] = fmaf(r[i + dx], wv[j], acc[i][j]);
+            for (int j = 0; j < TNC / 2; ++j) fma2(acc2[i][j], x2, wv2[j]);
+          }
         }
       }
     }
@@ -464,6 +484,11 @@ __global__ void __launch_bounds__(256, 2) conv3x3_direct_kernel(const C2Args a, 
   const int oh = h0 + pr;
   if (oh >= a.OH) return;
   const long long M = (long long)a.OH * a.OW;
+  float acc[TMP][TNC];
+#pragma unroll
+  for (int i = 0; i < TMP; ++i)
+#pragma unroll
+    for (int j = 0; j < TNC / 2; ++j) unpack2(acc2[i][j], acc[i][2 * j], acc[i][2 * j + 1]);
 #pragma unroll
   for (int i = 0; i < TMP; ++i) {
     const int ow = w0 + pc + i;
