@@ -285,7 +285,57 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         ptx::tc_fence_after();
       }
-      for (int tile = blockIdx.x; tile < g.total_tiles && ok; tile += gridDim.x) {
+      // Resident weights: every descriptor is a per-CTA base plus multiples of
+      // fixed strides (start address >> 4 in the low bits, all offsets
+      // multiples of 16 B inside shared memory), so the loop below advances
+      // them by additions and issues the MMAs of a tap back to back.
+      const uint64_t d_x0 = ptx::smem_desc(x_plane(0, 0), LBO_X, 128);
+      const uint64_t s_lo = (uint64_t)(g.x_plane >> 4), s_buf = (uint64_t)((2u * g.x_plane) >> 4);
+      const uint64_t s_tap = (uint64_t)g.st_shift, s_kx = (uint64_t)((2u * LBO_X) >> 4);
+      const uint64_t d_w0 = ptx::smem_desc(w_slot(0), 2048, 128), s_w = (uint64_t)(g.w_stage >> 4);
+      const uint64_t s_ka = 4096u >> 4, s_wl = W_PLANE >> 4;
+      for (int tile = blockIdx.x; tile < g.total_tiles && ok && g.resident; tile += gridDim.x) {
+        const int set = it & 1;
+        if (!ptx::mbar_wait(ACC_EMPTY + 8 * set, ((it >> 1) & 1) ^ 1, kWaitNs)) {
+          ok = false;
+          atomicExch(a.err, 22);
+          break;
+        }
+        ptx::tc_fence_after();
+        const uint32_t dtm = tmem + (uint32_t)(set * kNT);
+        uint64_t aw = d_w0;  // stage kb * nst + j
+        for (int kb = 0; kb < nblk; ++kb, ++ab) {
+          const int buf = ab & 1;
+          if (!ptx::mbar_wait(X_FULL + 8 * buf, (ab >> 1) & 1, kWaitNs)) {
+            ok = false;
+            atomicExch(a.err, 23);
+            break;
+          }
+          ptx::tc_fence_after();
+          uint64_t bh = d_x0 + (uint64_t)buf * s_buf;
+          if (g.mode == 1) {
+            for (int j = 0; j < g.nst; ++j, bh += s_tap, aw += s_w) {
+              ptx::mma_bf16(dtm, aw, bh, idesc, (kb | j) ? 1u : 0u);
+              ptx::mma_bf16(dtm, aw, bh + s_lo, idesc, 1u);
+              ptx::mma_bf16(dtm, aw + s_wl, bh, idesc, 1u);
+              ptx::mma_bf16(dtm, aw + s_ka, bh + s_kx, idesc, 1u);
+              ptx::mma_bf16(dtm, aw + s_ka, bh + s_lo + s_kx, idesc, 1u);
+              ptx::mma_bf16(dtm, aw + s_wl + s_ka, bh + s_kx, idesc, 1u);
+            }
+          } else {
+            for (int j = 0; j < g.nst; ++j, bh += s_tap, aw += s_w) {
+              ptx::mma_bf16(dtm, aw, bh, idesc, (kb | j) ? 1u : 0u);
+              ptx::mma_bf16(dtm, aw, bh + s_lo, idesc, 1u);
+              ptx::mma_bf16(dtm, aw + s_ka, bh + s_kx, idesc, 1u);
+              ptx::mma_bf16(dtm, aw + s_ka, bh + s_lo + s_kx, idesc, 1u);
+            }
+          }
+          ptx::mma_commit(X_EMPTY + 8 * buf);
+        }
+        if (ok) ptx::mma_commit(ACC_FULL + 8 * set);
+        ++it;
+      }
+      for (int tile = blockIdx.x; tile < g.total_tiles && ok && !g.resident; tile += gridDim.x) {
         const int set = it & 1;
         if (!ptx::mbar_wait(ACC_EMPTY + 8 * set, ((it >> 1) & 1) ^ 1, kWaitNs)) {
           ok = false;
