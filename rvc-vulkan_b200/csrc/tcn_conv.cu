@@ -271,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t idesc = ptx::idesc_bf16_f32(kMT, kNT);
       const uint32_t W_PLANE = (uint32_t)kCB * kMT * 2u;  // one hi or lo weight plane (mode 1)
-      int ks = 0, ab = 0, it = 0;
+      int ab = 0, it = 0;
       bool ok = true;
       if (g.resident) {
         // every weight stage lands once: wait for all of them here, so the
@@ -335,6 +335,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) ptx::mma_commit(ACC_FULL + 8 * set);
         ++it;
       }
+      // Streamed weights: stage st = ks % stages of the ring, phase round =
+      // ks / stages, both advanced by counting; descriptors by additions.
+      int st = 0, round = 0;
+      uint64_t aw = d_w0;  // descriptor of stage st
       for (int tile = blockIdx.x; tile < g.total_tiles && ok && !g.resident; tile += gridDim.x) {
         const int set = it & 1;
         if (!ptx::mbar_wait(ACC_EMPTY + 8 * set, ((it >> 1) & 1) ^ 1, kWaitNs)) {
@@ -344,7 +348,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         ptx::tc_fence_after();
         const uint32_t dtm = tmem + (uint32_t)(set * kNT);
-        bool first = true;
         for (int kb = 0; kb < nblk && ok; ++kb, ++ab) {
           const int buf = ab & 1;
           if (!ptx::mbar_wait(X_FULL + 8 * buf, (ab >> 1) & 1, kWaitNs)) {
@@ -353,37 +356,36 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           ptx::tc_fence_after();
-          for (int j = 0; j < g.nst; ++j, ++ks) {
-            const int st = ks % g.stages, round = ks / g.stages;
-            if (!g.resident) {
-              if (!ptx::mbar_wait(W_FULL + 8 * st, round & 1, kWaitNs)) {
-                ok = false;
-                atomicExch(a.err, 24);
-                break;
-              }
-              ptx::tc_fence_after();
+          uint64_t bh = d_x0 + (uint64_t)buf * s_buf;
+          for (int j = 0; j < g.nst; ++j, bh += s_tap) {
+            if (!ptx::mbar_wait(W_FULL + 8 * st, round & 1, kWaitNs)) {
+              ok = false;
+              atomicExch(a.err, 24);
+              break;
             }
-            const uint32_t rowoff = (uint32_t)(j * g.st_shift) * 16u;
-            const uint64_t bxh = ptx::smem_desc(x_plane(buf, 0) + rowoff, LBO_X, 128);
-            const uint64_t bxl = ptx::smem_desc(x_plane(buf, 1) + rowoff, LBO_X, 128);
-            const uint64_t awh = ptx::smem_desc(w_slot(st), 2048, 128);
-#pragma unroll
-            for (int kk = 0; kk < kCB / 16; ++kk) {
-              // k step kk: weights +kk*4096 B (2 cores x 128 rows x 16 B), activations +2 K-cores
-              const uint64_t ka = (uint64_t)((uint32_t)kk * 4096u >> 4);
-              const uint64_t kx = (uint64_t)((2u * (uint32_t)kk * LBO_X) >> 4);
-              if (g.mode == 1) {
-                const uint64_t awl = awh + (uint64_t)(W_PLANE >> 4);
-                ptx::mma_bf16(dtm, awh + ka, bxh + kx, idesc, (first && kk == 0) ? 0u : 1u);
-                ptx::mma_bf16(dtm, awh + ka, bxl + kx, idesc, 1u);
-                ptx::mma_bf16(dtm, awl + ka, bxh + kx, idesc, 1u);
-              } else {
-                ptx::mma_bf16(dtm, awh + ka, bxh + kx, idesc, (first && kk == 0) ? 0u : 1u);
-                ptx::mma_bf16(dtm, awh + ka, bxl + kx, idesc, 1u);
-              }
+            ptx::tc_fence_after();
+            const uint32_t acc0 = (kb | j) ? 1u : 0u;
+            if (g.mode == 1) {
+              ptx::mma_bf16(dtm, aw, bh, idesc, acc0);
+              ptx::mma_bf16(dtm, aw, bh + s_lo, idesc, 1u);
+              ptx::mma_bf16(dtm, aw + s_wl, bh, idesc, 1u);
+              ptx::mma_bf16(dtm, aw + s_ka, bh + s_kx, idesc, 1u);
+              ptx::mma_bf16(dtm, aw + s_ka, bh + s_lo + s_kx, idesc, 1u);
+              ptx::mma_bf16(dtm, aw + s_wl + s_ka, bh + s_kx, idesc, 1u);
+            } else {
+              ptx::mma_bf16(dtm, aw, bh, idesc, acc0);
+              ptx::mma_bf16(dtm, aw, bh + s_lo, idesc, 1u);
+              ptx::mma_bf16(dtm, aw + s_ka, bh + s_kx, idesc, 1u);
+              ptx::mma_bf16(dtm, aw + s_ka, bh + s_lo + s_kx, idesc, 1u);
             }
-            first = false;
-            if (!g.resident) ptx::mma_commit(W_EMPTY + 8 * st);
+            ptx::mma_commit(W_EMPTY + 8 * st);
+            if (++st == g.stages) {
+              st = 0;
+              ++round;
+              aw = d_w0;
+            } else {
+              aw += s_w;
+            }
           }
           if (ok) ptx::mma_commit(X_EMPTY + 8 * buf);
         }
