@@ -390,7 +390,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       const uint32_t idesc = ptx::idesc_bf16_f32(kTM, BN);
       const uint32_t idesc2 = ptx::idesc_bf16_f32(kTM, 2 * BN);
-      int ks = 0, ab = 0, it = 0;
+      int ab = 0, it = 0;
+      int st = 0, round = 0;  // weight ring stage and phase, counted (no per-tap division)
+      // descriptor bases: start address >> 4 in the low bits and every offset
+      // below a multiple of 16 B inside shared memory, so offsets are added
+      const uint64_t d_a0 = ptx::smem_desc(a_plane(0, 0), LBO_A, 128), s_aplane = (uint64_t)(g.a_plane >> 4);
+      const uint64_t d_b0 = ptx::smem_desc(b_plane(0, 0), LBO_B, 128), s_bplane = (uint64_t)(g.b_plane >> 4);
+      const uint64_t d_w0 = ptx::smem_desc(sbase + g.off_w, LBO_B, 128);
       bool ok = true;
       if (g.w_res && !ptx::mbar_wait(W_FULL, 0, kWaitNs)) {
         ok = false;
@@ -418,12 +424,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             atomicExch(a.err, 3);
             break;
           }
-          for (int j = 0; j < S.ntaps; ++j, ++ks) {
-            const int st = ks % g.stages, round = ks / g.stages;
-            uint32_t bhi, blo;
+          const uint64_t da_buf = d_a0 + (uint64_t)(2 * buf) * s_aplane;
+          for (int j = 0; j < S.ntaps; ++j) {
+            uint64_t dbh0;
             if (g.w_res) {
-              bhi = sbase + g.off_w + (uint32_t)((S.wtap0 + j) * nblk + kb) * 2u * g.b_plane;
-              blo = bhi + g.b_plane;
+              dbh0 = d_w0 + (uint64_t)((S.wtap0 + j) * nblk + kb) * 2u * s_bplane;
             } else {
               if (!ptx::mbar_wait(B_FULL + 8 * st, round & 1, kWaitNs)) {
                 ok = false;
@@ -431,21 +436,23 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
               }
               ptx::tc_fence_after();
-              bhi = b_plane(st, 0);
-              blo = b_plane(st, 1);
+              dbh0 = d_b0 + (uint64_t)(2 * st) * s_bplane;
             }
-            const uint32_t rowoff = (uint32_t)(j * S.tap_step + shift);
-            const uint64_t dah0 = ptx::smem_desc(a_plane(buf, 0) + rowoff * 16u, LBO_A, 128);
-            const uint64_t dal0 = ptx::smem_desc(a_plane(buf, 1) + rowoff * 16u, LBO_A, 128);
-            const uint64_t dbh0 = ptx::smem_desc(bhi, LBO_B, 128);
+            const uint64_t dah0 = da_buf + (uint64_t)(uint32_t)(j * S.tap_step + shift);
+            const uint64_t dal0 = dah0 + s_aplane;
             if (STK) {
               issue_stacked_any(g.msub, CB / 16, dbase, dah0, dal0, dbh0, LBO_A, LBO_B, BN, idesc2, idesc, first);
             } else {
-              const uint64_t dbl0 = ptx::smem_desc(blo, LBO_B, 128);
-              issue_any(g.msub, CB / 16, dbase, dah0, dal0, dbh0, dbl0, LBO_A, LBO_B, BN, idesc, first);
+              issue_any(g.msub, CB / 16, dbase, dah0, dal0, dbh0, dbh0 + s_bplane, LBO_A, LBO_B, BN, idesc, first);
             }
             first = false;
-            if (!g.w_res) ptx::mma_commit(B_EMPTY + 8 * st);
+            if (!g.w_res) {
+              ptx::mma_commit(B_EMPTY + 8 * st);
+              if (++st == g.stages) {
+                st = 0;
+                ++round;
+              }
+            }
           }
           if (ok) ptx::mma_commit(A_EMPTY + 8 * buf);
         }
