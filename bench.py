@@ -1241,7 +1241,7 @@ def main():
     ap.add_argument("--unique", type=int, default=16)
     ap.add_argument("--precision", default="bf16x3", choices=["bf16x3", "simt"])
     ap.add_argument("--ref-frames", type=int, default=1000,
-                    help="frames of the CPU sample chunk (default: the config's own 1000-frame chunk; about 16 s "
+                    help="frames of the CPU sample chunk (default: the config's own 1000-frame chunk; about 14 s "
                          "per chunk for the reference's numpy code on 16 host threads)")
     ap.add_argument("--no-config0", action="store_true", help="skip the v2-40k config-0 figure")
     ap.add_argument("--no-cpu", action="store_true")

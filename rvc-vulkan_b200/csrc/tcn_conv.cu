@@ -335,8 +335,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (ok) ptx::mma_commit(ACC_FULL + 8 * set);
         ++it;
       }
-      // Streamed weights: stage st = ks % stages of the ring, phase round =
-      // ks / stages, both advanced by counting; descriptors by additions.
+      // Streamed weights: the ring stage st and its phase round are counted
+      // per tap (the producer fills the stages in the same order); the
+      // descriptors advance by additions as above.
       int st = 0, round = 0;
       uint64_t aw = d_w0;  // descriptor of stage st
       for (int tile = blockIdx.x; tile < g.total_tiles && ok && !g.resident; tile += gridDim.x) {
